@@ -1,0 +1,22 @@
+"""laya_b200 — the Laya decision engine's hot path on B200 (sm_100a), behind a C ABI.
+
+The compute lives in `liblaya_b200.so` (CUDA kernels + the C ABI of include/laya_b200.h).  This package is the
+host-side mirror of the reference's interfaces for that path, over ctypes:
+
+  * `DecisionModel`      — DecisionModel / ModernBertEncoder inference (Laya/Models/DecisionModel.cs,
+                           Laya/Models/ModernBertEncoder.cs): construct from named weights, `forward(items)`.
+  * `PackedMatrixQ8_0`   — the ILinear Q8_0 projection (Base/Numerics/PackedMatrixQ8_0.cs): `multiply(...)`.
+  * `Q8_0`               — the quantizers on device buffers.
+
+There is no CPU fallback: importing works anywhere, but every call needs the built library and a B200; a missing
+library raises `LayaLibraryMissing`.
+"""
+from .api import (Context, DecisionModel, DecisionOutput, BatchItem, ModelDesc, PackedMatrixQ8_0, Q8_0,
+                  LayaError, LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
+                  LayaNotFoundError, LayaDeviceTimeout, LayaLibraryMissing, lib, library_path, base_desc,
+                  PRECISION_F32, PRECISION_Q8_0)
+
+__all__ = ["Context", "DecisionModel", "DecisionOutput", "BatchItem", "ModelDesc", "PackedMatrixQ8_0", "Q8_0",
+           "LayaError", "LayaArgumentError", "LayaOutOfRangeError", "LayaNotSupportedError", "LayaCudaError",
+           "LayaNotFoundError", "LayaDeviceTimeout", "LayaLibraryMissing", "lib", "library_path", "base_desc",
+           "PRECISION_F32", "PRECISION_Q8_0"]

@@ -1,0 +1,383 @@
+"""ctypes bindings of include/laya_b200.h and the host-side mirror of the reference's interfaces."""
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_NAME = "liblaya_b200.so"
+
+PRECISION_F32 = 0
+PRECISION_Q8_0 = 1
+F32, BF16, F16, I8, I32 = 0, 1, 2, 3, 4
+
+
+# --------------------------------------------------------------------------------------------------- errors
+class LayaError(RuntimeError):
+    code = -1
+
+
+class LayaArgumentError(LayaError, ValueError):      # ArgumentException
+    code = 1
+
+
+class LayaOutOfRangeError(LayaArgumentError, IndexError):   # ArgumentOutOfRangeException
+    code = 2
+
+
+class LayaNotSupportedError(LayaError, NotImplementedError):   # PlatformNotSupportedException
+    code = 3
+
+
+class LayaCudaError(LayaError):
+    code = 4
+
+
+class LayaNotFoundError(LayaError, KeyError):
+    code = 5
+
+
+class LayaDeviceTimeout(LayaError):
+    code = 6
+
+
+class LayaLibraryMissing(LayaError):
+    pass
+
+
+_ERRORS = {c.code: c for c in (LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
+                               LayaNotFoundError, LayaDeviceTimeout)}
+
+
+# --------------------------------------------------------------------------------------------------- library
+class ModelDesc(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int), ("intermediate", ctypes.c_int), ("layers", ctypes.c_int),
+                ("heads", ctypes.c_int), ("vocab", ctypes.c_int), ("local_attention", ctypes.c_int),
+                ("global_every", ctypes.c_int), ("layer_kinds", ctypes.POINTER(ctypes.c_int)),
+                ("theta_global", ctypes.c_double), ("theta_local", ctypes.c_double), ("norm_eps", ctypes.c_float),
+                ("head_layers", ctypes.c_int), ("n_act", ctypes.c_int), ("act_hidden", ctypes.c_int),
+                ("precision", ctypes.c_int), ("max_tokens", ctypes.c_int), ("max_items", ctypes.c_int),
+                ("max_markers", ctypes.c_int)]
+
+
+def library_path():
+    return os.path.join(HERE, _LIB_NAME)
+
+
+_lib = None
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIGS = {
+    "laya_last_error": (ctypes.c_char_p, []),
+    "laya_version": (ctypes.c_char_p, []),
+    "laya_ctx_create": (_I, [ctypes.POINTER(ModelDesc), _I, ctypes.POINTER(_P)]),
+    "laya_ctx_destroy": (_I, [_P]),
+    "laya_ctx_set_stream": (_I, [_P, _P]),
+    "laya_ctx_synchronize": (_I, [_P]),
+    "laya_ctx_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_ctx_set_profiling": (_I, [_P, _I]),
+    "laya_ctx_profile": (_I, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                              ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_upload_tensor": (_I, [_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P]),
+    "laya_upload_q8_0": (_I, [_P, ctypes.c_char_p, _P, _P, _I, _I]),
+    "laya_download_tensor": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
+    "laya_q8_0_linear": (_I, [_P, ctypes.c_char_p, _P, _I, _I, _P, _P, _I]),
+    "laya_q8_0_linear_device": (_I, [_P, ctypes.c_char_p, _P, _I, _I, _P, _P, _I]),
+    "laya_q8_0_quantize_activations_device": (_I, [_P, _P, _I, _I, _I, _P, _P, _I]),
+    "laya_q8_0_quantize_weights_device": (_I, [_P, _P, _I, _I, _P, _P, _I]),
+    "laya_q8_0_gemm_device": (_I, [_P, _P, _P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I]),
+    "laya_q8_0_gemm_fused_device": (_I, [_P, _I, _P, _P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _I]),
+    "laya_pack_q8_0": (_I, [_P, ctypes.c_char_p, _I, _P, _I, _I]),
+    "laya_decision_forward": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "laya_decision_forward_device": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P]),
+    "laya_encoder_forward": (_I, [_P, _P, _P, _I, _P]),
+    "laya_record_enable": (_I, [_P, _I]),
+    "laya_record_get": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
+    "laya_encoder_layer": (_I, [_P, _I, _P, _P, _I]),
+}
+
+
+def lib():
+    """The loaded liblaya_b200.so (raises LayaLibraryMissing if it was not built)."""
+    global _lib
+    if _lib is None:
+        path = library_path()
+        if not os.path.exists(path):
+            raise LayaLibraryMissing(f"{path} is missing: build it with `python -m laya_b200.build`")
+        L = ctypes.CDLL(path)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc):
+    if rc != 0:
+        msg = lib().laya_last_error().decode("utf-8", "replace")
+        raise _ERRORS.get(rc, LayaError)(msg)
+
+
+def _np_ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def base_desc(**kw) -> ModelDesc:
+    """ModernBERT-base geometry (22 layers, h 768, 12×64, I 1152, vocab 50368) with a Laya decision head."""
+    d = dict(hidden=768, intermediate=1152, layers=22, heads=12, vocab=50368, local_attention=128, global_every=3,
+             theta_global=160000.0, theta_local=10000.0, norm_eps=1e-5, head_layers=2, n_act=2, act_hidden=256,
+             precision=PRECISION_Q8_0, max_tokens=32768, max_items=256, max_markers=4096)
+    d.update(kw)
+    kinds = d.pop("layer_kinds", None)
+    desc = ModelDesc(**d)
+    if kinds is not None:
+        arr = (ctypes.c_int * len(kinds))(*kinds)
+        desc.layer_kinds = ctypes.cast(arr, ctypes.POINTER(ctypes.c_int))
+        desc._kinds_keepalive = arr
+    return desc
+
+
+# --------------------------------------------------------------------------------------------------- context
+class Context:
+    """A device context (laya_ctx): weights by name, workspaces, stream."""
+
+    def __init__(self, desc: ModelDesc, device: int = 0):
+        self.desc = desc
+        h = ctypes.c_void_p()
+        check(lib().laya_ctx_create(ctypes.byref(desc), device, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_handle: Optional[int]):
+        check(lib().laya_ctx_set_stream(self.handle, stream_handle))
+
+    def synchronize(self):
+        check(lib().laya_ctx_synchronize(self.handle))
+
+    def launches(self) -> int:
+        n = ctypes.c_longlong()
+        check(lib().laya_ctx_launches(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def set_profiling(self, enabled: bool):
+        check(lib().laya_ctx_set_profiling(self.handle, 1 if enabled else 0))
+
+    def profile(self) -> Tuple[float, float, int]:
+        ms, ops, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_longlong()
+        check(lib().laya_ctx_profile(self.handle, ctypes.byref(ms), ctypes.byref(ops), ctypes.byref(n)))
+        return ms.value, ops.value, n.value
+
+    def upload(self, name: str, array: np.ndarray):
+        a = np.ascontiguousarray(array)
+        if a.dtype == np.float32:
+            dt = F32
+        elif a.dtype == np.float16:
+            dt = F16
+        else:
+            a = a.astype(np.float32)
+            dt = F32
+        shape = (ctypes.c_int64 * a.ndim)(*a.shape)
+        check(lib().laya_upload_tensor(self.handle, name.encode(), dt, shape, a.ndim, _np_ptr(a)))
+
+    def upload_bf16_bits(self, name: str, bits: np.ndarray):
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        shape = (ctypes.c_int64 * a.ndim)(*a.shape)
+        check(lib().laya_upload_tensor(self.handle, name.encode(), BF16, shape, a.ndim, _np_ptr(a)))
+
+    def upload_q8_0(self, name: str, q: np.ndarray, d_fp16: np.ndarray):
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        d = np.ascontiguousarray(d_fp16, dtype=np.float16).view(np.uint16)
+        N, K = q.shape
+        check(lib().laya_upload_q8_0(self.handle, name.encode(), _np_ptr(q), _np_ptr(d), N, K))
+
+    def download(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(shape, np.float32)
+        check(lib().laya_download_tensor(self.handle, name.encode(), _np_ptr(out), out.size))
+        return out
+
+    def record(self, enabled: bool):
+        check(lib().laya_record_enable(self.handle, 1 if enabled else 0))
+
+    def recorded(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(shape, np.float32)
+        check(lib().laya_record_get(self.handle, name.encode(), _np_ptr(out), out.size))
+        return out
+
+
+# --------------------------------------------------------------------------------------------------- ILinear
+class PackedMatrixQ8_0:
+    """A Q8_0 projection (PackedMatrixQ8_0, Base/Numerics/PackedMatrixQ8_0.cs:108-246) living in a Context.
+
+    Construct from a PyTorch-layout [out, in] fp32 weight (quantized on the device by ggml's weight quantizer,
+    PackedMatrixQ8_0.cs:168-173) or from Q8_0 codes + fp16 scales.  `multiply` is ILinear.Multiply.
+    """
+
+    def __init__(self, ctx: Context, name: str, weight: Optional[np.ndarray] = None,
+                 q: Optional[np.ndarray] = None, d_fp16: Optional[np.ndarray] = None):
+        self.ctx, self.name = ctx, name
+        if weight is not None:
+            w = np.ascontiguousarray(weight)
+            if w.dtype == np.uint16:          # raw bf16 bit patterns, as the bf16 constructor takes them
+                dt = BF16
+            else:
+                w = _f32(w)
+                dt = F32
+            self.out_features, self.in_features = w.shape
+            check(lib().laya_pack_q8_0(ctx.handle, name.encode(), dt, _np_ptr(w), w.shape[0], w.shape[1]))
+        else:
+            ctx.upload_q8_0(name, q, d_fp16)
+            self.out_features, self.in_features = q.shape
+
+    def multiply(self, input: np.ndarray, rows: int, input_stride: Optional[int] = None,
+                 bias: Optional[np.ndarray] = None, output: Optional[np.ndarray] = None,
+                 output_stride: Optional[int] = None) -> np.ndarray:
+        input_stride = self.in_features if input_stride is None else input_stride
+        output_stride = self.out_features if output_stride is None else output_stride
+        x = _f32(input).reshape(-1)
+        if rows > 0 and x.size < (rows - 1) * input_stride + self.in_features:
+            raise LayaArgumentError("input is too small")
+        if output is None:
+            output = np.zeros(max(rows, 1) * output_stride, np.float32)
+        if rows > 0 and output.size < (rows - 1) * output_stride + self.out_features:
+            raise LayaArgumentError("output is too small")
+        b = None if bias is None or len(bias) == 0 else _f32(bias)
+        if b is not None and b.size < self.out_features:
+            raise LayaArgumentError("bias is too small")
+        check(lib().laya_q8_0_linear(self.ctx.handle, self.name.encode(), _np_ptr(x), rows, input_stride,
+                                     _np_ptr(b), output.ctypes.data_as(ctypes.c_void_p), output_stride))
+        return output
+
+    def dequantize(self) -> np.ndarray:
+        """Every column's q·d (PackedMatrixQ8_0.Dequantize, PackedMatrixQ8_0.cs:209-218), as [out, in]."""
+        return self.ctx.download(self.name, (self.out_features, self.in_features))
+
+
+class Q8_0:
+    """The two ggml quantizers on device buffers (Q8_0, Base/Numerics/PackedMatrixQ8_0.cs:15-72).
+
+    Pointers are device addresses (ints), e.g. torch tensors' data_ptr().
+    """
+    BlockSize = 32
+
+    @staticmethod
+    def quantize_activations(ctx: Context, x_ptr: int, rows: int, stride: int, features: int, q_ptr: int,
+                             d_ptr: int, ldd: int):
+        check(lib().laya_q8_0_quantize_activations_device(ctx.handle, x_ptr, rows, stride, features, q_ptr, d_ptr,
+                                                          ldd))
+
+    @staticmethod
+    def quantize_weights(ctx: Context, w_ptr: int, n: int, k: int, q_ptr: int, d_ptr: int, ldd: int):
+        check(lib().laya_q8_0_quantize_weights_device(ctx.handle, w_ptr, n, k, q_ptr, d_ptr, ldd))
+
+    @staticmethod
+    def gemm(ctx: Context, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n, k, bias_ptr, out_ptr, ldo):
+        check(lib().laya_q8_0_gemm_device(ctx.handle, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n, k, bias_ptr,
+                                          out_ptr, ldo))
+
+    STORE, RESIDUAL, GEGLU, RELU = 0, 1, 2, 3
+
+    @staticmethod
+    def gemm_fused(ctx: Context, epilogue, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n, k, bias_ptr, out_ptr, ldo,
+                   qout_ptr, qscale_ptr, ldqs):
+        check(lib().laya_q8_0_gemm_fused_device(ctx.handle, epilogue, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n,
+                                                k, bias_ptr, out_ptr, ldo, qout_ptr, qscale_ptr, ldqs))
+
+
+# --------------------------------------------------------------------------------------------------- model
+@dataclass
+class BatchItem:
+    """DecisionModel.BatchItem (Laya/Models/DecisionModel.cs:107)."""
+    token_ids: Sequence[int]
+    marker_positions: Sequence[int]
+    type: int
+
+
+@dataclass
+class DecisionOutput:
+    """DecisionOutput (Laya/Models/DecisionModel.cs:10)."""
+    option_logits: np.ndarray
+    action_probabilities: np.ndarray
+
+
+class DecisionModel:
+    """The decision model's batched inference forward on the device (DecisionModel + ModernBertEncoder).
+
+    `weights` maps safetensors names to arrays; `q8` maps projection names to (codes int8 [N, K], scales fp16
+    [N, K/32]) for checkpoints already in Q8_0.  Projections given as floats are quantized on the device.
+    """
+
+    def __init__(self, desc: ModelDesc, weights: Dict[str, np.ndarray], q8: Optional[Dict] = None, device: int = 0):
+        self.desc = desc
+        self.ctx = Context(desc, device)
+        for name, arr in weights.items():
+            if q8 and name in q8:
+                continue
+            if name == "temperature":
+                continue
+            self.ctx.upload(name, arr)
+        for name, (q, d) in (q8 or {}).items():
+            self.ctx.upload_q8_0(name, q, d)
+
+    @staticmethod
+    def pack(items: List[BatchItem]):
+        ids = _i32(np.concatenate([np.asarray(it.token_ids, np.int64) for it in items])) if items else _i32([])
+        seg_len = _i32([len(it.token_ids) for it in items])
+        qtype = _i32([it.type for it in items])
+        counts = _i32([len(it.marker_positions) for it in items])
+        markers = _i32(np.concatenate([np.asarray(it.marker_positions, np.int64) for it in items])
+                       if items and counts.sum() else np.zeros(1))
+        return ids, seg_len, qtype, counts, markers
+
+    def forward(self, items: List[BatchItem]) -> List[DecisionOutput]:
+        """DecisionModel.Forward (Laya/Models/DecisionModel.cs:128-169)."""
+        if not items:
+            return []
+        ids, seg_len, qtype, counts, markers = self.pack(items)
+        logits = np.zeros(max(1, int(counts.sum())), np.float32)
+        act = np.zeros(len(items) * self.desc.n_act, np.float32)
+        check(lib().laya_decision_forward(self.ctx.handle, _np_ptr(ids), _np_ptr(seg_len), _np_ptr(qtype),
+                                          len(items), _np_ptr(counts), _np_ptr(markers), _np_ptr(logits),
+                                          _np_ptr(act)))
+        out, m = [], 0
+        for i, it in enumerate(items):
+            k = len(it.marker_positions)
+            out.append(DecisionOutput(logits[m:m + k].copy(), act[i * self.desc.n_act:(i + 1) * self.desc.n_act].copy()))
+            m += k
+        return out
+
+    def encoder_forward(self, token_ids: Sequence[np.ndarray]) -> np.ndarray:
+        """ModernBertEncoder.Forward over concatenated segments: final hidden states [T, hidden]."""
+        ids = _i32(np.concatenate([np.asarray(t, np.int64) for t in token_ids]))
+        seg_len = _i32([len(t) for t in token_ids])
+        out = np.zeros((ids.size, self.desc.hidden), np.float32)
+        check(lib().laya_encoder_forward(self.ctx.handle, _np_ptr(ids), _np_ptr(seg_len), len(seg_len),
+                                         _np_ptr(out)))
+        return out
+
+    def encoder_layer(self, layer: int, hidden: np.ndarray, seg_len: Sequence[int]) -> np.ndarray:
+        """Runs one encoder layer on given hidden states (teacher forcing for per-layer parity)."""
+        h = _f32(hidden).copy()
+        sl = _i32(seg_len)
+        check(lib().laya_encoder_layer(self.ctx.handle, layer, _np_ptr(h), _np_ptr(sl), len(sl)))
+        return h

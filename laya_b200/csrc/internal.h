@@ -1,0 +1,75 @@
+// internal.h — host-side declarations shared by the laya_b200 translation units (not part of the C ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace laya {
+
+// Thread-local error message behind laya_last_error().
+void set_error(const std::string& msg);
+const char* last_error();
+
+// Status codes (mirrors include/laya_b200.h).
+enum Status : int {
+    OK = 0,
+    ERR_ARGUMENT = 1,
+    ERR_OUT_OF_RANGE = 2,
+    ERR_NOT_SUPPORTED = 3,
+    ERR_CUDA = 4,
+    ERR_NOT_FOUND = 5,
+    ERR_DEVICE_TIMEOUT = 6,
+    ERR_COMM = 7,
+};
+
+int cuda_fail(cudaError_t e, const char* what);
+#define LAYA_CUDA(call)                                      \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return ::laya::cuda_fail(e_, #call); \
+    } while (0)
+
+// 2-D tensor map over a row-major [rows, cols] matrix of `elem_bytes`-byte elements, tile box
+// [box_rows, box_cols], 128-byte swizzle; out-of-range elements read as zero.
+int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols);
+
+// Launch accounting: every kernel launched by the library bumps this counter (per host thread).
+void count_launch(int n = 1);
+long long launches();
+
+// ------------------------------------------------------------------------------------------------ Q8_0
+namespace q8 {
+enum Epi : int {
+    EPI_STORE = 0,     // out = acc (fp32)
+    EPI_RESID = 1,     // out += acc (fp32 residual stream, in place)
+    EPI_GEGLU_Q8 = 2,  // columns come as [32 input | 32 gate] groups: gelu(u)*g, quantized to Q8_0
+    EPI_RELU_Q8 = 3,   // relu(acc), quantized to Q8_0
+};
+
+struct GemmArgs {
+    int M, N, K;                 // out[M, N] = X[M, K] · W[N, K]ᵀ (+ bias), K a multiple of 32
+    const int8_t* qx;            // [M, K] activation codes
+    const float* dx; int ldx;    // [K/32, ldx] activation block scales, ldx >= roundup(M, 128)
+    const int8_t* qw;            // [N, K] weight codes
+    const float* dw; int ldw;    // [K/32, ldw] weight block scales, ldw >= roundup(N, 128), zero padded
+    const float* bias;           // [N] or null
+    int epi;
+    float* out; int ldo;         // EPI_STORE / EPI_RESID
+    int8_t* qout; int ldqo;      // Q8 epilogues: codes [M, ldqo]
+    float* qsc; int ldqs;        // Q8 epilogues: block scales [Nout/32, ldqs]
+    int* err;                    // device error word
+};
+int gemm(const GemmArgs& a, cudaStream_t stream);
+
+// Activation quantizer (Q8_0.QuantizeActivations): x [rows, stride] fp32 -> q [rows, K], d [K/32, ldd].
+int quantize_activations(const float* x, int rows, int stride, int K, int8_t* q, float* d, int ldd,
+                         cudaStream_t stream);
+// Weight quantizer (Q8_0.QuantizeWeightBlock over every block): w [N, K] fp32 -> q [N, K], d [K/32, ldd] and
+// optionally the fp16-rounded scales row-major [N, K/32] (d_rows).
+int quantize_weights(const float* w, int N, int K, int8_t* q, float* d, int ldd, cudaStream_t stream);
+}  // namespace q8
+
+}  // namespace laya

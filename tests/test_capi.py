@@ -1,0 +1,61 @@
+"""The C ABI library on any machine: it loads, exports every declared entry point, and fails loudly without a GPU."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        names += re.findall(r"^\s*(?:int|const char\s*\*)\s+(laya_\w+)\s*\(", open(h).read(), re.M)
+    return names
+
+
+def test_header_declares_the_boundary():
+    names = declared()
+    for n in ["laya_ctx_create", "laya_upload_tensor", "laya_upload_q8_0", "laya_q8_0_linear", "laya_decision_forward",
+              "laya_last_error"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    import laya_b200
+    L = laya_b200.lib()
+    missing = [n for n in declared() if not hasattr(L, n)]
+    assert not missing, missing
+    assert L.laya_version().startswith(b"laya_b200")
+
+
+def test_no_cpu_fallback_without_a_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("this machine has a GPU")
+    import laya_b200
+    with pytest.raises(laya_b200.LayaError):
+        laya_b200.Context(laya_b200.base_desc(max_tokens=128, max_items=4, max_markers=16))
+
+
+def test_model_desc_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of laya_model_desc has the C compiler's size and field offsets."""
+    import subprocess
+    import laya_b200
+    fields = [f for f, _ in laya_b200.ModelDesc._fields_]
+    src = tmp_path / "desc.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "laya_b200.h"\nint main(void){printf("%zu", sizeof(laya_model_desc));'
+                   + "".join(f'printf(" %zu", offsetof(laya_model_desc, {f}));' for f in fields) + "return 0;}\n")
+    exe = tmp_path / "desc"
+    subprocess.check_call(["gcc", "-I" + os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    out = [int(v) for v in subprocess.check_output([str(exe)]).split()]
+    assert out[0] == ctypes.sizeof(laya_b200.ModelDesc)
+    assert out[1:] == [getattr(laya_b200.ModelDesc, f).offset for f in fields]
+
+
+def test_invalid_geometry_is_an_argument_error():
+    import laya_b200
+    with pytest.raises(laya_b200.LayaArgumentError):
+        laya_b200.Context(laya_b200.base_desc(heads=7))
