@@ -85,8 +85,10 @@ const char* laya_version(void);
 int laya_ctx_create(const laya_model_desc* desc, int device, laya_ctx** out);
 int laya_ctx_destroy(laya_ctx* ctx);
 
-/* Makes every later launch of this context go to `stream` (a cudaStream_t); NULL restores the context's own. */
+/* Makes every later launch of this context go to `stream` (a cudaStream_t); NULL selects CUDA's legacy default
+ * stream.  A new context launches on a non-blocking stream of its own; laya_ctx_get_stream returns the current one. */
 int laya_ctx_set_stream(laya_ctx* ctx, void* stream);
+int laya_ctx_get_stream(laya_ctx* ctx, void** stream);
 
 /* Blocks until the context's stream is idle, then reports any device-side error (a timed-out wait inside
  * a kernel returns LAYA_ERR_DEVICE_TIMEOUT). */
@@ -130,24 +132,26 @@ int laya_q8_0_linear_device(laya_ctx* ctx, const char* weight, const float* x, i
                             const float* bias, float* y, int output_stride);
 
 /*
- * The Q8_0 primitives on caller-owned device buffers, in the layouts the kernels use.
+ * The Q8_0 primitives on caller-owned device buffers, in the layouts the kernels use.  On the device a Q8_0 code is
+ * held as an IEEE fp16 value equal to the integer code (-127..127; the reference stores q+128 as bytes): the
+ * tensor-core product multiplies these exactly.  Block scales are fp32 holding the stored fp16 value.
  *   laya_q8_0_quantize_activations_device: Q8_0.QuantizeActivations (PackedMatrixQ8_0.cs:35-71); x [rows, stride] ->
- *       q [rows, K] int8 codes (the reference stores q+128), d [K/32, ldd] block scales as stored (fp16-rounded).
+ *       q [rows, K] codes, d [K/32, ldd] block scales as stored (fp16-rounded).
  *   laya_q8_0_quantize_weights_device: Q8_0.QuantizeWeightBlock over every block (PackedMatrixQ8_0.cs:20-28);
  *       w [N, K] -> q [N, K], d [K/32, ldd].
  *   laya_q8_0_gemm_device: the product of already-quantized operands (the kernels of PackedMatrixQ8_0.cs:248-557);
- *       out[M, N] (row stride ldo) = bias + Σ_b fma(Σ_b, dw·dx); ldx >= M rounded up to 128, ldw >= N rounded up to
- *       128 with zero padding.
+ *       out[M, N] (row stride ldo) = bias + Σ_b fma(Σ_b, dw·dx); ldx >= M rounded up to 128, ldw >= N, both multiples
+ *       of 4; every buffer 16-byte aligned.
  */
 /* The PackedMatrixQ8_0 constructors (PackedMatrixQ8_0.cs:146-173): a PyTorch [N, K] weight given as fp32 (LAYA_F32),
  * bf16 bits (LAYA_BF16) or fp16 bits (LAYA_F16), quantized on the device with ggml's weight quantizer and kept under
  * `name` for laya_q8_0_linear.  K not a multiple of 32 -> LAYA_ERR_ARGUMENT, as the reference throws. */
 int laya_pack_q8_0(laya_ctx* ctx, const char* name, int dtype, const void* host, int N, int K);
 
-int laya_q8_0_quantize_activations_device(laya_ctx* ctx, const float* x, int rows, int stride, int K, int8_t* q,
+int laya_q8_0_quantize_activations_device(laya_ctx* ctx, const float* x, int rows, int stride, int K, uint16_t* q,
                                           float* d, int ldd);
-int laya_q8_0_quantize_weights_device(laya_ctx* ctx, const float* w, int N, int K, int8_t* q, float* d, int ldd);
-int laya_q8_0_gemm_device(laya_ctx* ctx, const int8_t* qx, const float* dx, int ldx, int M, const int8_t* qw,
+int laya_q8_0_quantize_weights_device(laya_ctx* ctx, const float* w, int N, int K, uint16_t* q, float* d, int ldd);
+int laya_q8_0_gemm_device(laya_ctx* ctx, const uint16_t* qx, const float* dx, int ldx, int M, const uint16_t* qw,
                           const float* dw, int ldw, int N, int K, const float* bias, float* out, int ldo);
 
 /*
@@ -159,11 +163,11 @@ int laya_q8_0_gemm_device(laya_ctx* ctx, const int8_t* qx, const float* dx, int 
  *      and qout/qscale = Q8_0(gelu(u) · g) of the N/2 activations  (ModernBertEncoder.GeGlu, ModernBertEncoder.cs:204-214,
  *      then the next projection's activation quantizer)
  *   3  qout/qscale = Q8_0(relu(product))                  (DecisionModel.cs:300-304)
- * qout is [M, N or N/2] int8 codes, qscale [columns/32, ldqs] block scales.
+ * qout is [M, N or N/2] codes, qscale [columns/32, ldqs] block scales.
  */
-int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const int8_t* qx, const float* dx, int ldx, int M,
-                                const int8_t* qw, const float* dw, int ldw, int N, int K, const float* bias, float* out,
-                                int ldo, int8_t* qout, float* qscale, int ldqs);
+int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const uint16_t* qx, const float* dx, int ldx, int M,
+                                const uint16_t* qw, const float* dw, int ldw, int N, int K, const float* bias, float* out,
+                                int ldo, uint16_t* qout, float* qscale, int ldqs);
 
 /*
  * The batched decision forward (DecisionModel.Forward, Laya/Models/DecisionModel.cs:128-169, with ModernBertEncoder.Forward,

@@ -75,6 +75,7 @@ _SIGS = {
     "laya_ctx_create": (_I, [ctypes.POINTER(ModelDesc), _I, ctypes.POINTER(_P)]),
     "laya_ctx_destroy": (_I, [_P]),
     "laya_ctx_set_stream": (_I, [_P, _P]),
+    "laya_ctx_get_stream": (_I, [_P, ctypes.POINTER(_P)]),
     "laya_ctx_synchronize": (_I, [_P]),
     "laya_ctx_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
     "laya_ctx_set_profiling": (_I, [_P, _I]),
@@ -170,7 +171,13 @@ class Context:
             pass
 
     def set_stream(self, stream_handle: Optional[int]):
-        check(lib().laya_ctx_set_stream(self.handle, stream_handle))
+        """Launch on this cudaStream_t from now on (0 / None: CUDA's legacy default stream, torch's default)."""
+        check(lib().laya_ctx_set_stream(self.handle, stream_handle or None))
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        check(lib().laya_ctx_get_stream(self.handle, ctypes.byref(s)))
+        return s.value or 0
 
     def synchronize(self):
         check(lib().laya_ctx_synchronize(self.handle))
@@ -274,9 +281,10 @@ class PackedMatrixQ8_0:
 
 
 class Q8_0:
-    """The two ggml quantizers on device buffers (Q8_0, Base/Numerics/PackedMatrixQ8_0.cs:15-72).
+    """The two ggml quantizers and the product on device buffers (Q8_0, Base/Numerics/PackedMatrixQ8_0.cs:15-72).
 
-    Pointers are device addresses (ints), e.g. torch tensors' data_ptr().
+    Pointers are device addresses (ints), e.g. torch tensors' data_ptr().  Codes are fp16 values equal to the integer
+    codes (-127..127); block scales are fp32 [blocks, stride].
     """
     BlockSize = 32
 

@@ -246,13 +246,12 @@ __global__ void __launch_bounds__(128) attention_kernel(Args a) {
             const float id = m != 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
             if (qp < L) {
                 const size_t tok = static_cast<size_t>(seg0 + qp);
-                int8_t* qrow = a.q + tok * a.hidden + head * HD + blk * 32;
+                __half* qrow = a.q + tok * a.hidden + head * HD + blk * 32;
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                     const int c0 = __float2int_rn(__fmul_rn(v[2 * jj], id));
                     const int c1 = __float2int_rn(__fmul_rn(v[2 * jj + 1], id));
-                    const uint16_t pk = static_cast<uint16_t>((c0 & 0xFF) | ((c1 & 0xFF) << 8));
-                    *reinterpret_cast<uint16_t*>(qrow + 8 * jj + 2 * t4) = pk;
+                    *reinterpret_cast<__half2*>(qrow + 8 * jj + 2 * t4) = __halves2half2(__int2half_rn(c0), __int2half_rn(c1));
                 }
                 if (t4 == 0) a.d[static_cast<size_t>(head * (HD / 32) + blk) * a.ldd + tok] = round_fp16(__fdiv_rn(m, 127.0f));
             }

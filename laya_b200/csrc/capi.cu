@@ -52,7 +52,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols) {
+                 uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) { set_error("cuTensorMapEncodeTiled unavailable"); return ERR_CUDA; }
     cuuint64_t dims[2] = {cols, rows};
@@ -61,7 +61,8 @@ int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, i
     cuuint32_t estr[2] = {1, 1};
     (void)elem_bytes;
     CUresult r = fn(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         char buf[160];
         snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu tile map", static_cast<int>(r),
@@ -86,7 +87,7 @@ struct DevBuf {
 };
 
 struct QWeight {
-    int8_t* q = nullptr;   // [N, K]
+    q8::code_t* q = nullptr;   // [N, K] fp16-held codes
     float* d = nullptr;    // [K/32, ldw]
     int N = 0, K = 0, ldw = 0;
     bool geglu = false;    // rows stored in [32 input | 32 gate] groups
@@ -125,7 +126,7 @@ struct laya_ctx {
     int T_cap = 0, ldx = 0, maxk = 0, max_qtiles = 0;
     float* h = nullptr;
     float* qkv = nullptr;
-    int8_t *qa0 = nullptr, *qa1 = nullptr;
+    q8::code_t *qa0 = nullptr, *qa1 = nullptr;
     float *da0 = nullptr, *da1 = nullptr;
     int32_t *ids = nullptr, *seg_len = nullptr, *qtype = nullptr, *mk_count = nullptr, *markers = nullptr;
     int32_t *seg_start = nullptr, *mk_start = nullptr, *qt_start = nullptr, *qt_item = nullptr, *qt_q0 = nullptr,
@@ -243,8 +244,8 @@ int collect_profile(laya_ctx* c) {
 }
 
 // Projection y[M, N] = Q8(x) · W with a given epilogue.  x codes/scales live in (q, d) with stride ldx.
-int q8_proj(laya_ctx* c, const std::string& name, const int8_t* qx, const float* dx, int M, const float* bias, int epi,
-            float* out, int ldo, int8_t* qout, float* qsc) {
+int q8_proj(laya_ctx* c, const std::string& name, const q8::code_t* qx, const float* dx, int M, const float* bias,
+            int epi, float* out, int ldo, q8::code_t* qout, float* qsc) {
     auto it = c->q8.find(name);
     if (it == c->q8.end()) { set_error("missing Q8_0 projection " + name); return ERR_NOT_FOUND; }
     const QWeight& w = it->second;
@@ -495,7 +496,7 @@ int store_q8(laya_ctx* c, const std::string& name, const int8_t* q_host, const f
     if (w.geglu && (N % 64 != 0 || (N / 2) % 32 != 0)) { set_error("Wi needs 2·I rows with I a multiple of 32"); return ERR_ARGUMENT; }
     auto old = c->q8.find(name);
     if (old != c->q8.end()) { cudaFree(old->second.q); cudaFree(old->second.d); c->q8.erase(old); }
-    LAYA_CUDA(cudaMalloc(&w.q, static_cast<size_t>(N) * K));
+    LAYA_CUDA(cudaMalloc(&w.q, sizeof(q8::code_t) * static_cast<size_t>(N) * K));
     LAYA_CUDA(cudaMalloc(&w.d, sizeof(float) * static_cast<size_t>(K / 32) * w.ldw));
     LAYA_CUDA(cudaMemsetAsync(w.d, 0, sizeof(float) * static_cast<size_t>(K / 32) * w.ldw, c->stream));
     const int I = N / 2;
@@ -524,9 +525,14 @@ int store_q8(laya_ctx* c, const std::string& name, const int8_t* q_host, const f
             memcpy(&qp[static_cast<size_t>(p) * K], q_host + static_cast<size_t>(r) * K, K);
             for (int b = 0; b < K / 32; ++b) dt[static_cast<size_t>(b) * w.ldw + p] = d_rows_host[static_cast<size_t>(r) * (K / 32) + b];
         }
-        LAYA_CUDA(cudaMemcpyAsync(w.q, qp.data(), qp.size(), cudaMemcpyHostToDevice, c->stream));
+        int8_t* q8tmp = nullptr;
+        LAYA_CUDA(cudaMalloc(&q8tmp, qp.size()));
+        LAYA_CUDA(cudaMemcpyAsync(q8tmp, qp.data(), qp.size(), cudaMemcpyHostToDevice, c->stream));
+        int rc = q8::widen_codes(q8tmp, w.q, qp.size(), c->stream);
         LAYA_CUDA(cudaMemcpyAsync(w.d, dt.data(), sizeof(float) * dt.size(), cudaMemcpyHostToDevice, c->stream));
         LAYA_CUDA(cudaStreamSynchronize(c->stream));
+        cudaFree(q8tmp);
+        if (rc) return rc;
     }
     c->q8[name] = w;
     return OK;
@@ -645,7 +651,13 @@ int laya_ctx_destroy(laya_ctx* c) {
 
 int laya_ctx_set_stream(laya_ctx* c, void* stream) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
-    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own;
+    c->stream = static_cast<cudaStream_t>(stream);   // NULL: CUDA's legacy default stream
+    return OK;
+}
+
+int laya_ctx_get_stream(laya_ctx* c, void** stream) {
+    if (!c || !stream) { set_error("null argument"); return ERR_ARGUMENT; }
+    *stream = static_cast<void*>(c->stream);
     return OK;
 }
 
@@ -764,41 +776,42 @@ int laya_download_tensor(laya_ctx* c, const char* name, float* host, int64_t cou
     if (jt == c->q8.end()) { set_error("no tensor named " + n); return ERR_NOT_FOUND; }
     const QWeight& w = jt->second;
     if (count < static_cast<int64_t>(w.N) * w.K) { set_error("host buffer too small"); return ERR_ARGUMENT; }
-    std::vector<int8_t> q(static_cast<size_t>(w.N) * w.K);
+    std::vector<uint16_t> q(static_cast<size_t>(w.N) * w.K);
     std::vector<float> d(static_cast<size_t>(w.K / 32) * w.ldw);
-    LAYA_CUDA(cudaMemcpy(q.data(), w.q, q.size(), cudaMemcpyDeviceToHost));
+    LAYA_CUDA(cudaMemcpy(q.data(), w.q, sizeof(uint16_t) * q.size(), cudaMemcpyDeviceToHost));
     LAYA_CUDA(cudaMemcpy(d.data(), w.d, sizeof(float) * d.size(), cudaMemcpyDeviceToHost));
     for (int p = 0; p < w.N; ++p) {
         const int r = w.geglu ? geglu_src_row(p, w.N / 2) : p;
         for (int k = 0; k < w.K; ++k)
-            host[static_cast<size_t>(r) * w.K + k] = static_cast<float>(q[static_cast<size_t>(p) * w.K + k]) * d[static_cast<size_t>(k / 32) * w.ldw + p];
+            host[static_cast<size_t>(r) * w.K + k] = half_bits_to_float(q[static_cast<size_t>(p) * w.K + k]) * d[static_cast<size_t>(k / 32) * w.ldw + p];
     }
     return OK;
 }
 
 // ------------------------------------------------------------------------------------------------ Q8_0 entry points
-int laya_q8_0_quantize_activations_device(laya_ctx* c, const float* x, int rows, int stride, int K, int8_t* q, float* d,
-                                          int ldd) {
+int laya_q8_0_quantize_activations_device(laya_ctx* c, const float* x, int rows, int stride, int K, uint16_t* q,
+                                          float* d, int ldd) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
     if (rows < 0 || ldd < rows) { set_error("scale stride below the row count"); return ERR_ARGUMENT; }
     DeviceGuard g(c->device);
-    return q8::quantize_activations(x, rows, stride, K, q, d, ldd, c->stream);
+    return q8::quantize_activations(x, rows, stride, K, reinterpret_cast<q8::code_t*>(q), d, ldd, c->stream);
 }
 
-int laya_q8_0_quantize_weights_device(laya_ctx* c, const float* w, int N, int K, int8_t* q, float* d, int ldd) {
+int laya_q8_0_quantize_weights_device(laya_ctx* c, const float* w, int N, int K, uint16_t* q, float* d, int ldd) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
     if (N < 0 || ldd < N) { set_error("scale stride below the column count"); return ERR_ARGUMENT; }
     DeviceGuard g(c->device);
-    return q8::quantize_weights(w, N, K, q, d, ldd, c->stream);
+    return q8::quantize_weights(w, N, K, reinterpret_cast<q8::code_t*>(q), d, ldd, c->stream);
 }
 
-int laya_q8_0_gemm_device(laya_ctx* c, const int8_t* qx, const float* dx, int ldx, int M, const int8_t* qw, const float* dw,
-                          int ldw, int N, int K, const float* bias, float* out, int ldo) {
+int laya_q8_0_gemm_device(laya_ctx* c, const uint16_t* qx, const float* dx, int ldx, int M, const uint16_t* qw,
+                          const float* dw, int ldw, int N, int K, const float* bias, float* out, int ldo) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
     if (M < 0 || N < 0 || ldo < N) { set_error("output stride below the column count"); return ERR_ARGUMENT; }
     DeviceGuard g(c->device);
     q8::GemmArgs a{};
-    a.M = M; a.N = N; a.K = K; a.qx = qx; a.dx = dx; a.ldx = ldx; a.qw = qw; a.dw = dw; a.ldw = ldw;
+    a.M = M; a.N = N; a.K = K; a.dx = dx; a.ldx = ldx; a.dw = dw; a.ldw = ldw;
+    a.qx = reinterpret_cast<const q8::code_t*>(qx); a.qw = reinterpret_cast<const q8::code_t*>(qw);
     a.bias = bias; a.epi = q8::EPI_STORE; a.out = out; a.ldo = ldo; a.err = c->err;
     return gemm_profiled(c, a);
 }
@@ -820,9 +833,9 @@ int laya_pack_q8_0(laya_ctx* c, const char* name, int dtype, const void* host, i
     return store_q8(c, name, nullptr, nullptr, N, K, true, src);
 }
 
-int laya_q8_0_gemm_fused_device(laya_ctx* c, int epilogue, const int8_t* qx, const float* dx, int ldx, int M,
-                                const int8_t* qw, const float* dw, int ldw, int N, int K, const float* bias, float* out,
-                                int ldo, int8_t* qout, float* qscale, int ldqs) {
+int laya_q8_0_gemm_fused_device(laya_ctx* c, int epilogue, const uint16_t* qx, const float* dx, int ldx, int M,
+                                const uint16_t* qw, const float* dw, int ldw, int N, int K, const float* bias, float* out,
+                                int ldo, uint16_t* qout, float* qscale, int ldqs) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
     if (epilogue < 0 || epilogue > 3) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
     if ((epilogue <= 1 && (!out || ldo < N)) || (epilogue >= 2 && (!qout || !qscale || ldqs < M))) {
@@ -830,8 +843,9 @@ int laya_q8_0_gemm_fused_device(laya_ctx* c, int epilogue, const int8_t* qx, con
     }
     DeviceGuard g(c->device);
     q8::GemmArgs a{};
-    a.M = M; a.N = N; a.K = K; a.qx = qx; a.dx = dx; a.ldx = ldx; a.qw = qw; a.dw = dw; a.ldw = ldw;
-    a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.qout = qout;
+    a.M = M; a.N = N; a.K = K; a.dx = dx; a.ldx = ldx; a.dw = dw; a.ldw = ldw;
+    a.qx = reinterpret_cast<const q8::code_t*>(qx); a.qw = reinterpret_cast<const q8::code_t*>(qw);
+    a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.qout = reinterpret_cast<q8::code_t*>(qout);
     a.ldqo = epilogue == q8::EPI_GEGLU_Q8 ? N / 2 : N;
     a.qsc = qscale; a.ldqs = ldqs; a.err = c->err;
     return gemm_profiled(c, a);
@@ -869,12 +883,12 @@ static int q8_linear_impl(laya_ctx* c, const char* weight, const float* x, int r
         dxin = dx_; dyout = dy_; dbias = bias ? db_ : nullptr;
     }
     // activation codes [rows, K] and scales [K/32, ldx]: the workspace holds K <= maxk; wider inputs get their own
-    int8_t* qa = c->qa1;
+    q8::code_t* qa = c->qa1;
     float* da = c->da1;
-    int8_t* qa_tmp = nullptr;
+    q8::code_t* qa_tmp = nullptr;
     float* da_tmp = nullptr;
     if (w.K > c->maxk) {
-        LAYA_CUDA(cudaMalloc(&qa_tmp, static_cast<size_t>(c->ldx) * w.K));
+        LAYA_CUDA(cudaMalloc(&qa_tmp, sizeof(q8::code_t) * static_cast<size_t>(c->ldx) * w.K));
         LAYA_CUDA(cudaMalloc(&da_tmp, sizeof(float) * static_cast<size_t>(w.K / 32) * c->ldx));
         LAYA_CUDA(cudaMemsetAsync(da_tmp, 0, sizeof(float) * static_cast<size_t>(w.K / 32) * c->ldx, c->stream));
         qa = qa_tmp;

@@ -157,6 +157,31 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t dfmt, uint32_t afmt, 
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ------------------------------------------------------------------------------------------------ packed fp32
+// sm_100 two-wide fp32 arithmetic on 64-bit register pairs (lo, hi); each lane is one IEEE op with round-to-nearest,
+// identical to the scalar __fmul_rn / __fsub_rn / __fmaf_rn, in half the issue slots.
+DEVI uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+DEVI void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+DEVI uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+DEVI uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+DEVI uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // ------------------------------------------------------------------------------------------------ numerics
 // Exact int32 → fp32 for |s| < 2^22: place s in the mantissa of 1.5·2^23 and subtract it back.
 DEVI float i2f_exact(int32_t s) { return __fsub_rn(__int_as_float(s + 0x4B400000), 12582912.0f); }

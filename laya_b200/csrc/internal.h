@@ -1,6 +1,7 @@
 // internal.h — host-side declarations shared by the laya_b200 translation units (not part of the C ABI).
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -31,10 +32,10 @@ int cuda_fail(cudaError_t e, const char* what);
         if (e_ != cudaSuccess) return ::laya::cuda_fail(e_, #call); \
     } while (0)
 
-// 2-D tensor map over a row-major [rows, cols] matrix of `elem_bytes`-byte elements, tile box
-// [box_rows, box_cols], 128-byte swizzle; out-of-range elements read as zero.
+// 2-D tensor map over a row-major [rows, cols] matrix, tile box [box_rows, box_cols]; out-of-range elements read
+// as zero.  swizzle128: 128-byte swizzle (MMA operand tiles) or none (plain tiles such as block scales).
 int make_tmap_2d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols);
+                 uint64_t cols, uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols, bool swizzle128 = true);
 
 // Launch accounting: every kernel launched by the library bumps this counter (per host thread).
 void count_launch(int n = 1);
@@ -49,27 +50,32 @@ enum Epi : int {
     EPI_RELU_Q8 = 3,   // relu(acc), quantized to Q8_0
 };
 
+// Q8_0 codes live on the device as fp16 values that are exactly the integers -127..127 ("fp16-held codes"), the
+// operand form of the kind::f16 tensor-core product; block scales are fp32 (the stored fp16 value, widened).
+using code_t = __half;
+
 struct GemmArgs {
     int M, N, K;                 // out[M, N] = X[M, K] · W[N, K]ᵀ (+ bias), K a multiple of 32
-    const int8_t* qx;            // [M, K] activation codes
-    const float* dx; int ldx;    // [K/32, ldx] activation block scales, ldx >= roundup(M, 128)
-    const int8_t* qw;            // [N, K] weight codes
-    const float* dw; int ldw;    // [K/32, ldw] weight block scales, ldw >= roundup(N, 128), zero padded
+    const code_t* qx;            // [M, K] activation codes
+    const float* dx; int ldx;    // [K/32, ldx] activation block scales, ldx >= roundup(M, 128), multiple of 4
+    const code_t* qw;            // [N, K] weight codes
+    const float* dw; int ldw;    // [K/32, ldw] weight block scales, ldw >= N, multiple of 4
     const float* bias;           // [N] or null
     int epi;
     float* out; int ldo;         // EPI_STORE / EPI_RESID
-    int8_t* qout; int ldqo;      // Q8 epilogues: codes [M, ldqo]
+    code_t* qout; int ldqo;      // Q8 epilogues: codes [M, ldqo]
     float* qsc; int ldqs;        // Q8 epilogues: block scales [Nout/32, ldqs]
     int* err;                    // device error word
 };
 int gemm(const GemmArgs& a, cudaStream_t stream);
 
 // Activation quantizer (Q8_0.QuantizeActivations): x [rows, stride] fp32 -> q [rows, K], d [K/32, ldd].
-int quantize_activations(const float* x, int rows, int stride, int K, int8_t* q, float* d, int ldd,
+int quantize_activations(const float* x, int rows, int stride, int K, code_t* q, float* d, int ldd,
                          cudaStream_t stream);
-// Weight quantizer (Q8_0.QuantizeWeightBlock over every block): w [N, K] fp32 -> q [N, K], d [K/32, ldd] and
-// optionally the fp16-rounded scales row-major [N, K/32] (d_rows).
-int quantize_weights(const float* w, int N, int K, int8_t* q, float* d, int ldd, cudaStream_t stream);
+// Weight quantizer (Q8_0.QuantizeWeightBlock over every block): w [N, K] fp32 -> q [N, K], d [K/32, ldd].
+int quantize_weights(const float* w, int N, int K, code_t* q, float* d, int ldd, cudaStream_t stream);
+// int8 codes -> fp16-held codes (n values).
+int widen_codes(const int8_t* src, code_t* dst, size_t n, cudaStream_t stream);
 }  // namespace q8
 
 }  // namespace laya

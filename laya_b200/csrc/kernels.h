@@ -1,5 +1,6 @@
 // kernels.h — argument blocks and launchers of the laya_b200 kernels (internal to the library).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -20,7 +21,7 @@ struct LnArgs {
     const float* temb;         // final LN: type embedding [3, n]
     const int32_t* tok_item;   // final LN: question of each token
     const int32_t* qtype;      // final LN: type of each question
-    int8_t* q; float* d; int ldd;   // Q8_0 output: codes [rows, n], scales [n/32, ldd]
+    __half* q; float* d; int ldd;   // Q8_0 output: fp16-held codes [rows, n], scales [n/32, ldd]
     int* err;
 };
 int ln_q8(const LnArgs& a, cudaStream_t s);
@@ -36,7 +37,7 @@ struct Args {
     int window;                       // < 0: global
     float scale;                      // 1/sqrt(head_dim), applied to every dot product
     const float* cosv; const float* sinv;   // [positions, head_dim/2] or null (no rotary)
-    int8_t* q; float* d; int ldd;     // context codes [T, hidden], scales [hidden/32, ldd]
+    __half* q; float* d; int ldd;     // context codes (fp16-held) [T, hidden], scales [hidden/32, ldd]
 };
 }  // namespace attn
 int attention(const attn::Args& a, int max_qtiles, cudaStream_t stream);

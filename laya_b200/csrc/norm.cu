@@ -80,9 +80,9 @@ __global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
             const float amax = octet_max(m);
             const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
             if (active) {
-                int8_t* qrow = a.q + static_cast<size_t>(r) * n + blk * 32 + l;
+                __half* qrow = a.q + static_cast<size_t>(r) * n + blk * 32 + l;
 #pragma unroll
-                for (int t = 0; t < 4; ++t) qrow[8 * t] = static_cast<int8_t>(__float2int_rn(__fmul_rn(v[4 * blk + t], id)));
+                for (int t = 0; t < 4; ++t) qrow[8 * t] = __int2half_rn(__float2int_rn(__fmul_rn(v[4 * blk + t], id)));
                 if (l == 0) a.d[static_cast<size_t>(blk) * a.ldd + r] = round_fp16(__fdiv_rn(amax, 127.0f));
             }
         }

@@ -5,23 +5,27 @@
 //
 // Definition being computed (PackedMatrixQ8_0Tests.cs:145-182):
 //     out[r, c] = bias[c];  for b in 0 .. K/32-1:  out[r, c] = fma((float)Σ_b, d_w[c, b] · d_x[r, b], out[r, c])
-// with Σ_b = Σ_{k in block b} q_x[r, k] · q_w[c, k] an exact int32.
+// with Σ_b = Σ_{k in block b} q_x[r, k] · q_w[c, k] an exact integer.
 //
-// One Q8_0 block (32 int8 along K) is exactly one tcgen05.mma.kind::i8 instruction (K = 32).  Every block's
-// product goes to its own TMEM accumulator (the instruction overwrites, it never accumulates), so the exact
-// int32 block sums Σ_b land in TMEM one block at a time.  Epilogue warps drain them with tcgen05.ld and apply
-// the reference's rescale in the reference's order, keeping the fp32 accumulators in registers; the result
-// is therefore bit-identical to the definition above.
+// Codes are held as fp16 values (the integers -127..127 are exact in fp16).  Every product of two codes is an
+// integer below 2^14 and every partial sum of a 32-term block stays an integer below 2^19, so the kind::f16
+// tensor-core product with fp32 accumulation computes each block's Σ_b exactly — and delivers it already as the
+// fp32 value (float)Σ_b the rescale needs.  Each block is its own accumulator: two K=16 MMAs (the first
+// overwriting, the second accumulating) into the TMEM buffer of that block.  Epilogue warps drain the buffers
+// with tcgen05.ld and apply the reference's rescale in the reference's order (one fp32 multiply d_w·d_x and one
+// fma per output per block), keeping the fp32 accumulators in registers: the result is bit-identical to the
+// definition.  The rescale — 2 fp32 ops per output per block on the CUDA cores — is the throughput bound; the
+// tensor pipe is nearly idle, which is why the exact-integer fp16 form (no int→fp32 conversion in the epilogue)
+// is used rather than kind::i8.
 //
 // CTA layout (one CTA per SM; 128 × BN output tile):
-//   warp 0      TMA producer: A (activation codes, 128 rows × 128 B) and B (weight codes, BN rows × 128 B)
-//               per stage, 128-byte swizzle, STAGES-deep ring.
-//   warp 1      TMEM allocator + MMA issuer (one thread): 4 MMAs per stage, one per Q8_0 block, each into
-//               TMEM buffer (block mod NBUF), committed to that buffer's "full" barrier.
+//   warp 0      TMA producer: A (activation codes, 128 rows × 64) and B (weight codes, BN rows × 64) per stage
+//               with 128-byte swizzle, STAGES-deep ring; and per stage the two blocks' scales (d_x for the tile's
+//               rows, d_w for its columns) into a separate SST-slot ring released by the epilogue.
+//   warp 1      TMEM allocator + MMA issuer (one thread).
 //   warps 2..   EPI_WARPS epilogue warps.  tcgen05.ld restricts warp w to TMEM lanes 32·(w mod 4)…+31, so the
 //               warps split as 4 lane quarters × (EPI_WARPS/4) column groups; a thread owns one output row
 //               and CPT consecutive columns.
-// The per-block rescale (cvt + mul + fma per output per block) is the throughput bound, not the MMA.
 #include "common.cuh"
 #include "internal.h"
 
@@ -29,75 +33,94 @@ namespace laya {
 namespace q8 {
 
 constexpr int BM = 128;        // tile rows (tokens)
-constexpr int BK = 128;        // K bytes per stage = 4 Q8_0 blocks
+constexpr int BKB = 128;       // K bytes per stage (one 128-byte swizzle row)
+constexpr int BK = BKB / 2;    // K codes per stage = 2 Q8_0 blocks
 constexpr int BPS = BK / 32;   // blocks per stage
+constexpr int SST = 8;         // slots of the block-scale ring
 
 template <int BN, int EPI_WARPS, int STAGES>
 struct Cfg {
-    static constexpr int A_BYTES = BM * BK;
-    static constexpr int B_BYTES = BN * BK;
+    static constexpr int A_BYTES = BM * BKB;
+    static constexpr int B_BYTES = BN * BKB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int NBUF = (512 / BN) < 4 ? (512 / BN) : 4;
+    static constexpr int SC_FLOATS = BPS * (BM + BN);          // one scale slot: dx [2][128], dw [2][BN]
+    static constexpr int SC_BYTES = SC_FLOATS * 4;
+    static constexpr int NBUF = (512 / BN) < 8 ? (512 / BN) : 8;   // TMEM accumulators (one per in-flight block)
     static constexpr int GROUPS = EPI_WARPS / 4;
     static constexpr int CPT = BN / GROUPS;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
-    static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * NBUF) + 16;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+    static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * SST + 2 * NBUF) + 16;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SST * SC_BYTES + BAR_BYTES;
     static_assert(CPT % 32 == 0, "each epilogue thread owns whole 32-column TMEM loads");
     static_assert(EPI_WARPS % 4 == 0, "epilogue warps come in lane-quarter sets");
+    static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte alignment of 128-byte swizzling");
 };
 
 struct KParams {
     int M, N, K;
-    const float* dx; int ldx;
-    const float* dw; int ldw;
     const float* bias;
     float* out; int ldo;
-    int8_t* qout; int ldqo;
+    code_t* qout; int ldqo;
     float* qsc; int ldqs;
     int* err;
 };
 
 // Quantizes 32 consecutive fp32 values held by one thread to Q8_0 (Q8_0.QuantizeActivations,
 // PackedMatrixQ8_0.cs:50-71): d = amax/127 stored fp16, id = 127/amax, q = round-half-even(x · id).
-DEVI void quantize_block32_store(const float* v, int8_t* qdst, float* ddst) {
+DEVI void quantize_block32_store(const float* v, code_t* qdst, float* ddst) {
     float amax = 0.0f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    uint32_t packed[8];
+    uint4* q4 = reinterpret_cast<uint4*>(qdst);
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-        uint32_t word = 0;
+    for (int w = 0; w < 4; ++w) {
+        uint32_t word[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            int qi = __float2int_rn(__fmul_rn(v[w * 4 + t], id));
-            word |= (static_cast<uint32_t>(qi) & 0xFFu) << (8 * t);
+            const __half2 h2 = __halves2half2(__int2half_rn(__float2int_rn(__fmul_rn(v[w * 8 + 2 * t], id))),
+                                              __int2half_rn(__float2int_rn(__fmul_rn(v[w * 8 + 2 * t + 1], id))));
+            word[t] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        packed[w] = word;
+        q4[w] = make_uint4(word[0], word[1], word[2], word[3]);
     }
-    uint4* q4 = reinterpret_cast<uint4*>(qdst);
-    q4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    q4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     *ddst = round_fp16(d);
+}
+
+// One block's rescale for 32 columns whose exact block sums arrive as fp32 bits in s[]:
+// acc[j] = fma((float)Σ, d_w[j] · d_x, acc[j]).
+DEVI void rescale32(float* acc, const uint32_t (&s)[32], const float* dw, float dx) {
+    const float4* w4 = reinterpret_cast<const float4*>(dw);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 w = w4[q];
+        acc[4 * q + 0] = __fmaf_rn(__uint_as_float(s[4 * q + 0]), __fmul_rn(w.x, dx), acc[4 * q + 0]);
+        acc[4 * q + 1] = __fmaf_rn(__uint_as_float(s[4 * q + 1]), __fmul_rn(w.y, dx), acc[4 * q + 1]);
+        acc[4 * q + 2] = __fmaf_rn(__uint_as_float(s[4 * q + 2]), __fmul_rn(w.z, dx), acc[4 * q + 2]);
+        acc[4 * q + 3] = __fmaf_rn(__uint_as_float(s[4 * q + 3]), __fmul_rn(w.w, dx), acc[4 * q + 3]);
+    }
 }
 
 template <int BN, int EPI_WARPS, int STAGES, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
-    q8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, KParams p) {
+    q8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDW, KParams p) {
     using C = Cfg<BN, EPI_WARPS, STAGES>;
     constexpr int NBUF = C::NBUF;
     constexpr int CPT = C::CPT;
-    constexpr uint32_t IDESC = make_idesc(/*D s32*/ 2, /*A s8*/ 1, /*B s8*/ 1, BM, BN);
+    constexpr uint32_t IDESC = make_idesc(/*D f32*/ 1, /*A f16*/ 0, /*B f16*/ 0, BM, BN);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    float* sSc = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);   // [SST][dx 4×128 | dw 4×BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + SST * C::SC_BYTES);
     uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
+    uint64_t* sfull = empty + STAGES;
+    uint64_t* sempty = sfull + SST;
+    uint64_t* tfull = sempty + SST;
     uint64_t* tempty = tfull + NBUF;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + NBUF);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -109,28 +132,38 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+        for (int s = 0; s < SST; ++s) { mbar_init(sfull + s, 1); mbar_init(sempty + s, EPI_WARPS); }
         for (int b = 0; b < NBUF; ++b) { mbar_init(tfull + b, 1); mbar_init(tempty + b, EPI_WARPS); }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-    if (warp == 0 && lane == 0) { prefetch_tmap(&tmA); prefetch_tmap(&tmB); }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmDX); prefetch_tmap(&tmDW);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
+        // ---- producer: operand tiles and, per stage, the 4 blocks' scales for this tile's rows and columns
         if (lane == 0) {
             for (int it = 0; it < iters; ++it) {
-                const int s = it % STAGES;
+                const int s = it % STAGES, ss = it % SST;
                 if (!mbar_wait(empty + s, ((it / STAGES) & 1) ^ 1, abort_flag, p.err)) break;
                 mbar_arrive_expect_tx(full + s, C::STAGE_BYTES);
-                tma_load_2d(sA + s * C::A_BYTES, &tmA, full + s, it * BK, m0);
+                tma_load_2d(sA + s * C::A_BYTES, &tmA, full + s, it * BK, m0);   // x in codes (2 bytes each)
                 tma_load_2d(sB + s * C::B_BYTES, &tmB, full + s, it * BK, n0);
+                if (!mbar_wait(sempty + ss, ((it / SST) & 1) ^ 1, abort_flag, p.err)) break;
+                mbar_arrive_expect_tx(sfull + ss, C::SC_BYTES);
+                float* slot = sSc + ss * C::SC_FLOATS;
+                tma_load_2d(slot, &tmDX, sfull + ss, m0, it * BPS);
+                tma_load_2d(slot + BPS * BM, &tmDW, sfull + ss, n0, it * BPS);
             }
         }
     } else if (warp == 1) {
+        // ---- MMA issuer: per Q8_0 block two K=16 kind::f16 instructions into that block's own TMEM buffer
         if (lane == 0) {
             for (int b = 0; b < nblk; ++b) {
                 const int it = b / BPS, j = b % BPS, s = it % STAGES;
@@ -141,15 +174,18 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
                 const int buf = b % NBUF;
                 if (!mbar_wait(tempty + buf, ((b / NBUF) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();
-                const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_BYTES + j * 32));
-                const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_BYTES + j * 32));
-                mma_i8(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, 0u);
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {   // 16 codes = 32 bytes per instruction
+                    const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_BYTES + j * 64 + kk * 32));
+                    const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_BYTES + j * 64 + kk * 32));
+                    mma_f16(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, kk);
+                }
                 mma_commit(tfull + buf);
                 if (j == BPS - 1 || b == nblk - 1) mma_commit(empty + s);
             }
         }
     } else {
-        // ------------------------------------------------------------------ epilogue warps
+        // ---- epilogue warps: drain each block's int32 sums and apply the rescale in the reference's order
         const int e = warp - 2;
         const int quarter = warp & 3;
         const int grp = e >> 2;
@@ -165,32 +201,33 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
             acc[j] = (p.bias != nullptr && c < p.N) ? __ldg(p.bias + c) : 0.0f;
         }
         const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(col0);
-        const float* dxp = p.dx + grow;
         bool ok = true;
-        float dxr = __ldg(dxp);
         for (int b = 0; b < nblk; ++b) {
+            const int it = b / BPS, j = b % BPS, ss = it % SST;
+            if (j == 0 && !mbar_wait(sfull + ss, (it / SST) & 1, abort_flag, p.err)) { ok = false; break; }
             const int buf = b % NBUF;
-            const float dx_next = (b + 1 < nblk) ? __ldg(dxp + static_cast<size_t>(b + 1) * p.ldx) : 0.0f;
-            const float4* dwp = reinterpret_cast<const float4*>(p.dw + static_cast<size_t>(b) * p.ldw + gcol0);
             if (!mbar_wait(tfull + buf, (b / NBUF) & 1, abort_flag, p.err)) { ok = false; break; }
             tc_fence_after();
-            uint32_t s[CPT / 32][32];
+            const float* slot = sSc + ss * C::SC_FLOATS;
+            const float dxr = slot[j * BM + row];
+            const float* dw = slot + BPS * BM + j * BN + col0;
+            // one 32-column chunk in registers at a time; the TMEM buffer is released after its last load
 #pragma unroll
-            for (int c = 0; c < CPT / 32; ++c) tmem_ld32(tbase + static_cast<uint32_t>(buf * BN + c * 32), s[c]);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty + buf);
-#pragma unroll
-            for (int j4 = 0; j4 < CPT / 4; ++j4) {
-                const float4 w = __ldg(dwp + j4);
-                const int j = j4 * 4;
-                acc[j + 0] = __fmaf_rn(i2f_exact(static_cast<int32_t>(s[(j + 0) / 32][(j + 0) % 32])), __fmul_rn(w.x, dxr), acc[j + 0]);
-                acc[j + 1] = __fmaf_rn(i2f_exact(static_cast<int32_t>(s[(j + 1) / 32][(j + 1) % 32])), __fmul_rn(w.y, dxr), acc[j + 1]);
-                acc[j + 2] = __fmaf_rn(i2f_exact(static_cast<int32_t>(s[(j + 2) / 32][(j + 2) % 32])), __fmul_rn(w.z, dxr), acc[j + 2]);
-                acc[j + 3] = __fmaf_rn(i2f_exact(static_cast<int32_t>(s[(j + 3) / 32][(j + 3) % 32])), __fmul_rn(w.w, dxr), acc[j + 3]);
+            for (int c = 0; c < CPT / 32; ++c) {
+                uint32_t s[32];
+                tmem_ld32(tbase + static_cast<uint32_t>(buf * BN + c * 32), s);
+                tmem_ld_wait();
+                if (c == CPT / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty + buf);
+                }
+                rescale32(acc + c * 32, s, dw + c * 32, dxr);
             }
-            dxr = dx_next;
+            if (j == BPS - 1 || b == nblk - 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sempty + ss);
+            }
         }
 
         if (ok && grow < p.M) {
@@ -263,20 +300,25 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
 template <int BN, int EPI_WARPS, int STAGES, int EPI>
 static int launch(const GemmArgs& a, cudaStream_t stream) {
     using C = Cfg<BN, EPI_WARPS, STAGES>;
-    CUtensorMap tA, tB;
-    int rc = make_tmap_2d(&tA, a.qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.M, a.K, a.K, BM, BK);
-    if (rc) return rc;
-    rc = make_tmap_2d(&tB, a.qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.N, a.K, a.K, BN, BK);
+    CUtensorMap tA, tB, tDX, tDW;
+    int rc = make_tmap_2d(&tA, a.qx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.K) * 2, BM, BK);
+    if (!rc) rc = make_tmap_2d(&tB, a.qw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.K) * 2, BN, BK);
+    if (!rc) rc = make_tmap_2d(&tDX, a.dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.K / 32, a.ldx,
+                               static_cast<uint64_t>(a.ldx) * 4, BPS, BM, false);
+    if (!rc) rc = make_tmap_2d(&tDW, a.dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.K / 32, a.ldw,
+                               static_cast<uint64_t>(a.ldw) * 4, BPS, BN, false);
     if (rc) return rc;
     auto kern = q8_gemm_kernel<BN, EPI_WARPS, STAGES, EPI>;
-    static bool attr_set = false;   // per instantiation
-    if (!attr_set) {
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    static uint64_t attr_set = 0;   // per instantiation, one bit per device
+    if (dev < 64 && !(attr_set & (1ull << dev))) {
         LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_set = true;
+        attr_set |= 1ull << dev;
     }
-    KParams p{a.M, a.N, a.K, a.dx, a.ldx, a.dw, a.ldw, a.bias, a.out, a.ldo, a.qout, a.ldqo, a.qsc, a.ldqs, a.err};
+    KParams p{a.M, a.N, a.K, a.bias, a.out, a.ldo, a.qout, a.ldqo, a.qsc, a.ldqs, a.err};
     dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-    kern<<<grid, C::THREADS, C::SMEM, stream>>>(tA, tB, p);
+    kern<<<grid, C::THREADS, C::SMEM, stream>>>(tA, tB, tDX, tDW, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -285,13 +327,15 @@ static int launch(const GemmArgs& a, cudaStream_t stream) {
 int gemm(const GemmArgs& a, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return OK;
     if (a.K <= 0 || a.K % 32 != 0) { set_error("Q8_0 needs a multiple of 32 inputs"); return ERR_ARGUMENT; }
-    if (a.ldx < ((a.M + BM - 1) / BM) * BM) { set_error("activation scale stride below the padded row count"); return ERR_ARGUMENT; }
-    if (a.ldw < ((a.N + 127) / 128) * 128) { set_error("weight scale stride below the padded column count"); return ERR_ARGUMENT; }
-    if ((reinterpret_cast<uintptr_t>(a.qx) & 15) || (reinterpret_cast<uintptr_t>(a.qw) & 15)) {
-        set_error("Q8_0 operands must be 16-byte aligned"); return ERR_ARGUMENT;
+    if (a.ldx < ((a.M + BM - 1) / BM) * BM || a.ldx % 4) {
+        set_error("activation scale stride must cover the rows rounded up to 128 and be a multiple of 4"); return ERR_ARGUMENT;
     }
-    if ((reinterpret_cast<uintptr_t>(a.dw) & 15) || (a.ldw & 3)) { set_error("weight scales must be 16-byte aligned rows"); return ERR_ARGUMENT; }
-    constexpr int BN = 128, EW = 8, ST = 4;
+    if (a.ldw < a.N || a.ldw % 4) { set_error("weight scale stride must cover N and be a multiple of 4"); return ERR_ARGUMENT; }
+    if ((reinterpret_cast<uintptr_t>(a.qx) & 15) || (reinterpret_cast<uintptr_t>(a.qw) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.dx) & 15) || (reinterpret_cast<uintptr_t>(a.dw) & 15)) {
+        set_error("Q8_0 operands and scales must be 16-byte aligned"); return ERR_ARGUMENT;
+    }
+    constexpr int BN = 192, EW = 12, ST = 4;
     switch (a.epi) {
         case EPI_STORE: return launch<BN, EW, ST, EPI_STORE>(a, stream);
         case EPI_RESID: return launch<BN, EW, ST, EPI_RESID>(a, stream);
@@ -310,7 +354,7 @@ int gemm(const GemmArgs& a, cudaStream_t stream) {
 
 // One warp per 32-value block; lane j owns value j.
 __global__ void quantize_activations_kernel(const float* __restrict__ x, int rows, int stride, int K,
-                                            int8_t* __restrict__ q, float* __restrict__ d, int ldd) {
+                                            code_t* __restrict__ q, float* __restrict__ d, int ldd) {
     const int nb = K / 32;
     const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -319,12 +363,12 @@ __global__ void quantize_activations_kernel(const float* __restrict__ x, int row
     const float v = x[static_cast<size_t>(r) * stride + b * 32 + lane];
     const float amax = warp_max(fabsf(v));
     const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    q[static_cast<size_t>(r) * K + b * 32 + lane] = static_cast<int8_t>(__float2int_rn(__fmul_rn(v, id)));
+    q[static_cast<size_t>(r) * K + b * 32 + lane] = __int2half_rn(__float2int_rn(__fmul_rn(v, id)));
     if (lane == 0) d[static_cast<size_t>(b) * ldd + r] = round_fp16(__fdiv_rn(amax, 127.0f));
 }
 
 // Q8_0.QuantizeWeightBlock (PackedMatrixQ8_0.cs:20-28): d = amax/127, id = 1/d, q = round half away.
-__global__ void quantize_weights_kernel(const float* __restrict__ w, int N, int K, int8_t* __restrict__ q,
+__global__ void quantize_weights_kernel(const float* __restrict__ w, int N, int K, code_t* __restrict__ q,
                                         float* __restrict__ d, int ldd) {
     const int nb = K / 32;
     const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -335,11 +379,11 @@ __global__ void quantize_weights_kernel(const float* __restrict__ w, int N, int 
     const float amax = warp_max(fabsf(v));
     const float dd = __fdiv_rn(amax, 127.0f);
     const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-    q[static_cast<size_t>(c) * K + b * 32 + lane] = static_cast<int8_t>(roundf(__fmul_rn(v, id)));
+    q[static_cast<size_t>(c) * K + b * 32 + lane] = __int2half_rn(static_cast<int>(roundf(__fmul_rn(v, id))));
     if (lane == 0) d[static_cast<size_t>(b) * ldd + c] = round_fp16(dd);
 }
 
-int quantize_activations(const float* x, int rows, int stride, int K, int8_t* q, float* d, int ldd,
+int quantize_activations(const float* x, int rows, int stride, int K, code_t* q, float* d, int ldd,
                          cudaStream_t stream) {
     if (rows <= 0) return OK;
     if (K % 32 || stride < K) { set_error("activation rows must hold whole 32-value blocks"); return ERR_ARGUMENT; }
@@ -352,13 +396,26 @@ int quantize_activations(const float* x, int rows, int stride, int K, int8_t* q,
     return OK;
 }
 
-int quantize_weights(const float* w, int N, int K, int8_t* q, float* d, int ldd, cudaStream_t stream) {
+int quantize_weights(const float* w, int N, int K, code_t* q, float* d, int ldd, cudaStream_t stream) {
     if (N <= 0) return OK;
     if (K % 32) { set_error("Q8_0 needs a multiple of 32 inputs"); return ERR_ARGUMENT; }
     const long long warps = static_cast<long long>(N) * (K / 32);
     const int threads = 256;
     const long long blocks = (warps * 32 + threads - 1) / threads;
     quantize_weights_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(w, N, K, q, d, ldd);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+__global__ void widen_codes_kernel(const int8_t* __restrict__ src, code_t* __restrict__ dst, size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __int2half_rn(src[i]);
+}
+
+int widen_codes(const int8_t* src, code_t* dst, size_t n, cudaStream_t stream) {
+    if (n == 0) return OK;
+    widen_codes_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(src, dst, n);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
