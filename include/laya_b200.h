@@ -170,6 +170,27 @@ int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const uint16_t* qx,
                                 int ldo, uint16_t* qout, float* qscale, int ldqs);
 
 /*
+ * laya_q8_0_linear_noalloc — the Q8_0 projection y = Q8_0(x) · W (+ bias) without any device allocation.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc — hosts whose device memory
+ * is owned by their own pool under a fixed budget, and plugins inside another process that may neither grow its
+ * device footprint nor take the implicit device synchronisation of cudaMalloc/cudaFree on a latency-critical path.
+ *   x [rows, input_stride] fp32 and y [rows, output_stride] fp32 are device buffers of the caller; weight_codes
+ *   [N, K] and weight_scales [K/32, ldw] are a projection in the device layout of laya_q8_0_quantize_weights_device
+ *   (16-byte aligned, ldw >= N and a multiple of 4); bias [N] or NULL.  Enqueued on `stream` (NULL: the legacy default
+ *   stream); the call returns without synchronising.
+ * The scratch (activation codes, their scales, a status word) is one static device array of LAYA_NOALLOC_SCRATCH_BYTES
+ * that every GPU loading the library holds until the process exits; a call needs about rows·K·2 + rows·K/8 bytes of it,
+ * and larger calls fail with LAYA_ERR_ARGUMENT before anything runs.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.
+ * Every call shares the array: calls that overlap on the GPU (different streams, devices excepted) race and must be
+ * serialised by the caller.
+ */
+#define LAYA_NOALLOC_SCRATCH_BYTES (8u << 20)
+int laya_q8_0_linear_noalloc(const float* x, int rows, int input_stride, const uint16_t* weight_codes,
+                             const float* weight_scales, int ldw, int N, int K, const float* bias, float* y,
+                             int output_stride, void* stream);
+
+/*
  * The batched decision forward (DecisionModel.Forward, Laya/Models/DecisionModel.cs:128-169, with ModernBertEncoder.Forward,
  * ModernBertEncoder.cs:123-188): questions concatenated, not padded.
  *   ids [Σ seg_len]          token ids of every question back to back
