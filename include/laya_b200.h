@@ -174,7 +174,8 @@ int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const uint16_t* qx,
  * No counterpart in the reference: it exists for callers that cannot call cudaMalloc — hosts whose device memory
  * is owned by their own pool under a fixed budget, and plugins inside another process that may neither grow its
  * device footprint nor take the implicit device synchronisation of cudaMalloc/cudaFree on a latency-critical path.
- *   x [rows, input_stride] fp32 and y [rows, output_stride] fp32 are device buffers of the caller; weight_codes
+ *   x [rows, input_stride] fp32 and y [rows, output_stride] fp32 are device buffers of the caller (y 16-byte aligned,
+ *   output_stride a multiple of 4); weight_codes
  *   [N, K] and weight_scales [K/32, ldw] are a projection in the device layout of laya_q8_0_quantize_weights_device
  *   (16-byte aligned, ldw >= N and a multiple of 4); bias [N] or NULL.  Enqueued on `stream` (NULL: the legacy default
  *   stream); the call returns without synchronising.

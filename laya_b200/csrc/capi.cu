@@ -398,6 +398,7 @@ int forward_staged(laya_ctx* c, int n_items, int T, int n_markers, float* logits
     RC(need_f32(c, "scorer.3.weight", &sa.w2));
     RC(need_f32(c, "scorer.3.bias", &sa.b2));
     sa.logits = logits_out;
+    sa.hid = c->qkv;   // [n_markers, hidden] scratch: the QKV buffer is free after the head layers
     RC(scorer(sa, c->stream));
     if (act_out) {
         ActArgs aa{};
@@ -869,14 +870,14 @@ static int q8_linear_impl(laya_ctx* c, const char* weight, const float* x, int r
     const size_t yout = (static_cast<size_t>(rows) - 1) * output_stride + w.N;
     if (host) {
         // stage through the qkv workspace: [x | y | bias]
-        const size_t need = xin + yout + w.N;
+        const size_t need = xin + yout + w.N + 8;
         if (need > static_cast<size_t>(c->T_cap) * 3 * c->d.hidden) {
             LAYA_CUDA(cudaMalloc(&tmp, need * sizeof(float)));
         }
         float* base = tmp ? tmp : c->qkv;
         float* dx_ = base;
-        float* dy_ = base + xin;
-        float* db_ = dy_ + yout;
+        float* dy_ = base + (xin + 3) / 4 * 4;           // 16-byte aligned
+        float* db_ = dy_ + (yout + 3) / 4 * 4;
         LAYA_CUDA(cudaMemcpyAsync(dx_, x, xin * sizeof(float), cudaMemcpyHostToDevice, c->stream));
         if (bias) LAYA_CUDA(cudaMemcpyAsync(db_, bias, w.N * sizeof(float), cudaMemcpyHostToDevice, c->stream));
         if (output_stride != w.N) LAYA_CUDA(cudaMemcpyAsync(dy_, y, yout * sizeof(float), cudaMemcpyHostToDevice, c->stream));
@@ -894,24 +895,40 @@ static int q8_linear_impl(laya_ctx* c, const char* weight, const float* x, int r
         qa = qa_tmp;
         da = da_tmp;
     }
+    // The product stores whole 16-byte-aligned rows with the TMA; an output whose base or row stride does not allow
+    // that (the reference accepts any stride) gets an aligned buffer and a strided copy.
+    float* gout = dyout;
+    int gld = output_stride;
+    float* out_tmp = nullptr;
+    if ((reinterpret_cast<uintptr_t>(dyout) & 15) || (output_stride & 3)) {
+        gld = (w.N + 3) / 4 * 4;
+        LAYA_CUDA(cudaMalloc(&out_tmp, sizeof(float) * static_cast<size_t>(rows) * gld));
+        gout = out_tmp;
+    }
     int rc = q8::quantize_activations(dxin, rows, input_stride, w.K, qa, da, c->ldx, c->stream);
     if (rc == OK) {
         q8::GemmArgs a{};
         a.M = rows; a.N = w.N; a.K = w.K; a.qx = qa; a.dx = da; a.ldx = c->ldx;
-        a.qw = w.q; a.dw = w.d; a.ldw = w.ldw; a.bias = dbias; a.epi = q8::EPI_STORE; a.out = dyout; a.ldo = output_stride;
+        a.qw = w.q; a.dw = w.d; a.ldw = w.ldw; a.bias = dbias; a.epi = q8::EPI_STORE; a.out = gout; a.ldo = gld;
         a.err = c->err;
         if (w.geglu) { set_error("Wi is stored in GeGLU row order; use the forward"); rc = ERR_NOT_SUPPORTED; }
         else rc = gemm_profiled(c, a);
+    }
+    if (rc == OK && out_tmp) {
+        cudaError_t e = cudaMemcpy2DAsync(dyout, sizeof(float) * output_stride, out_tmp, sizeof(float) * gld,
+                                          sizeof(float) * w.N, rows, cudaMemcpyDeviceToDevice, c->stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "strided output copy");
     }
     if (rc == OK && host) {
         cudaError_t e = cudaMemcpyAsync(y, dyout, yout * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
         if (e != cudaSuccess) rc = cuda_fail(e, "copy result");
         if (rc == OK) rc = check_device_error(c);
     }
-    if (tmp || qa_tmp) {
+    if (tmp || qa_tmp || out_tmp) {
         cudaStreamSynchronize(c->stream);
         if (tmp) cudaFree(tmp);
         if (qa_tmp) { cudaFree(qa_tmp); cudaFree(da_tmp); }
+        if (out_tmp) cudaFree(out_tmp);
     }
     return rc;
 }

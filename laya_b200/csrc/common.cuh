@@ -88,6 +88,24 @@ DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, i
         : "memory");
 }
 
+// Bulk tensor stores from this CTA's shared memory (no multicast), tracked by bulk groups of the issuing thread.
+DEVI void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+// Element-wise fp32 add of the smem tile into global memory (dst += src), performed by the TMA unit.
+DEVI void tma_reduce_add_2d(const CUtensorMap* map, int x, int y, const void* src) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+DEVI void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+DEVI void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+DEVI void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 DEVI void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

@@ -145,13 +145,29 @@ int plan(const PlanArgs& a, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------------------------------------------------ scorer
-constexpr int SC_MK = 8;   // markers per CTA
+// SimdOps.Dot's 16 accumulation chains (element i goes to chain i mod 16) by a half-warp, one chain per lane with
+// coalesced loads, combined in the reference's order: octet sums of s0 (lanes 0-7) and s1 (lanes 8-15), then s0 + s1.
+// n must be a multiple of 16 (the scorer's hidden size).  Every lane of the half-warp returns the dot.
+DEVI float halfwarp_ref_dot(const float* a, const float* b, int n, int l16) {
+    float acc = 0.0f;
+    for (int i = l16; i < n; i += 16) acc = __fmaf_rn(a[i], b[i], acc);
+    // hsum8 of the octet: (a0+a4, a1+a5, a2+a6, a3+a7) then pairwise, as octet_hsum in norm.cu
+    float t = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+    float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+    float v = __fadd_rn(u, __shfl_xor_sync(0xffffffffu, u, 2));
+    const float other = __shfl_xor_sync(0xffffffffu, v, 8);   // the other octet's sum
+    return l16 < 8 ? __fadd_rn(v, other) : __fadd_rn(other, v);
+}
 
-__global__ void __launch_bounds__(256) scorer_kernel(ScorerArgs a) {
+constexpr int SC_MK = 8;     // markers per CTA
+constexpr int SC_OUT = 128;  // Linear1 outputs per CTA
+
+// grid (marker groups, output chunks): LayerNorm of the CTA's marker rows, then SC_OUT outputs of
+// GELU(Linear1) for each of them, each weight row read once per CTA.
+__global__ void __launch_bounds__(256) scorer_hidden_kernel(ScorerArgs a) {
     extern __shared__ float sm[];
     const int H = a.hidden;
-    float* xs = sm;                   // [SC_MK][H] normalised marker rows
-    float* hid = sm + SC_MK * H;      // [SC_MK][H] GELU(Linear1)
+    float* xs = sm;   // [SC_MK][H]
     const int m0 = blockIdx.x * SC_MK;
     const int nm = min(SC_MK, a.n_markers - m0);
     if (threadIdx.x < nm) {
@@ -159,12 +175,26 @@ __global__ void __launch_bounds__(256) scorer_kernel(ScorerArgs a) {
         ref_layer_norm(row, H, a.ln_w, a.ln_b, 1e-5f, xs + threadIdx.x * H);
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < H; j += blockDim.x) {
-        const float* wj = a.w1 + static_cast<size_t>(j) * H;
-        for (int m = 0; m < nm; ++m) hid[m * H + j] = ref_gelu(__fadd_rn(ref_dot(xs + m * H, wj, H), a.b1[j]));
+    const int warp = threadIdx.x >> 5, half = (threadIdx.x >> 4) & 1, l16 = threadIdx.x & 15;
+    const int j0 = blockIdx.y * SC_OUT, jend = min(H, j0 + SC_OUT);
+    // warp-uniform trip count (the shuffles need all 32 lanes): the second half-warp repeats row jj past the end
+    for (int jj = j0 + 2 * warp; jj < jend; jj += 16) {
+        const int j = jj + half;
+        const bool valid = j < jend;
+        const float* wj = a.w1 + static_cast<size_t>(valid ? j : jj) * H;
+        for (int m = 0; m < nm; ++m) {
+            const float d = halfwarp_ref_dot(xs + m * H, wj, H, l16);
+            if (valid && l16 == 0) a.hid[static_cast<size_t>(m0 + m) * H + j] = ref_gelu(__fadd_rn(d, a.b1[j]));
+        }
     }
-    __syncthreads();
-    if (threadIdx.x < nm) a.logits[m0 + threadIdx.x] = __fadd_rn(ref_dot(hid + threadIdx.x * H, a.w2, H), a.b2[0]);
+}
+
+// logit = Dot(hidden, w2) + b2: one half-warp per marker.
+__global__ void __launch_bounds__(256) scorer_logit_kernel(ScorerArgs a) {
+    const int hw = (blockIdx.x * blockDim.x + threadIdx.x) >> 4, l16 = threadIdx.x & 15;
+    const int m = hw < a.n_markers ? hw : a.n_markers - 1;
+    const float d = halfwarp_ref_dot(a.hid + static_cast<size_t>(m) * a.hidden, a.w2, a.hidden, l16);
+    if (hw < a.n_markers && l16 == 0) a.logits[m] = __fadd_rn(d, a.b2[0]);
 }
 
 // SimdOps.Softmax (SimdOps.cs:275-291) by one thread.
@@ -222,9 +252,15 @@ __global__ void __launch_bounds__(256) act_kernel(ActArgs a) {
 
 int scorer(const ScorerArgs& a, cudaStream_t stream) {
     if (a.n_markers <= 0) return OK;
-    const size_t smem = sizeof(float) * 2 * SC_MK * a.hidden;
-    if (smem > 48 * 1024) LAYA_CUDA(cudaFuncSetAttribute(scorer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    scorer_kernel<<<(a.n_markers + SC_MK - 1) / SC_MK, 256, smem, stream>>>(a);
+    if (a.hidden % 16) { set_error("scorer hidden size must be a multiple of 16"); return ERR_NOT_SUPPORTED; }
+    const size_t smem = sizeof(float) * SC_MK * a.hidden;
+    if (smem > 48 * 1024)
+        LAYA_CUDA(cudaFuncSetAttribute(scorer_hidden_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    dim3 grid((a.n_markers + SC_MK - 1) / SC_MK, (a.hidden + SC_OUT - 1) / SC_OUT);
+    scorer_hidden_kernel<<<grid, 256, smem, stream>>>(a);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    scorer_logit_kernel<<<(a.n_markers * 16 + 255) / 256, 256, 0, stream>>>(a);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;

@@ -58,6 +58,7 @@ struct ScorerArgs {
     const float* h; const int32_t* marker_row;
     const float* ln_w; const float* ln_b;
     const float* w1; const float* b1; const float* w2; const float* b2;
+    float* hid;        // [n_markers, hidden] workspace: GELU(Linear1) of each marker row
     float* logits;
 };
 int scorer(const ScorerArgs& a, cudaStream_t stream);

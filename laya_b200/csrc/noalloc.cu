@@ -47,6 +47,9 @@ extern "C" int laya_q8_0_linear_noalloc(const float* x, int rows, int input_stri
     if ((reinterpret_cast<uintptr_t>(weight_codes) & 15) || (reinterpret_cast<uintptr_t>(weight_scales) & 15)) {
         set_error("weight codes and scales must be 16-byte aligned"); return ERR_ARGUMENT;
     }
+    if ((reinterpret_cast<uintptr_t>(y) & 15) || (output_stride & 3)) {
+        set_error("y must be 16-byte aligned with output_stride a multiple of 4"); return ERR_ARGUMENT;
+    }
     const size_t ldx = (static_cast<size_t>(rows) + 127) / 128 * 128;
     const size_t code_bytes = align256(static_cast<size_t>(rows) * K * sizeof(q8::code_t));
     const size_t scale_bytes = static_cast<size_t>(K / 32) * ldx * sizeof(float);

@@ -36,7 +36,7 @@ constexpr int BM = 128;        // tile rows (tokens)
 constexpr int BKB = 128;       // K bytes per stage (one 128-byte swizzle row)
 constexpr int BK = BKB / 2;    // K codes per stage = 2 Q8_0 blocks
 constexpr int BPS = BK / 32;   // blocks per stage
-constexpr int SST = 8;         // slots of the block-scale ring
+constexpr int SST = 4;         // slots of the block-scale ring
 
 template <int BN, int EPI_WARPS, int STAGES>
 struct Cfg {
@@ -49,8 +49,10 @@ struct Cfg {
     static constexpr int GROUPS = EPI_WARPS / 4;
     static constexpr int CPT = BN / GROUPS;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int STAGE_OUT_BYTES = 4096;               // per epilogue warp: 32 rows x 128 B of output
     static constexpr int BAR_BYTES = 8 * (2 * STAGES + 2 * SST + 2 * NBUF) + 16;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SST * SC_BYTES + BAR_BYTES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT_BYTES + SST * SC_BYTES + BAR_BYTES;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
     static_assert(CPT % 32 == 0, "each epilogue thread owns whole 32-column TMEM loads");
     static_assert(EPI_WARPS % 4 == 0, "epilogue warps come in lane-quarter sets");
     static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte alignment of 128-byte swizzling");
@@ -105,7 +107,8 @@ DEVI void rescale32(float* acc, const uint32_t (&s)[32], const float* dw, float 
 template <int BN, int EPI_WARPS, int STAGES, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
     q8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDW, KParams p) {
+                   const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDW,
+                   const __grid_constant__ CUtensorMap tmOut, KParams p) {
     using C = Cfg<BN, EPI_WARPS, STAGES>;
     constexpr int NBUF = C::NBUF;
     constexpr int CPT = C::CPT;
@@ -115,8 +118,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    float* sSc = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);   // [SST][dx 4×128 | dw 4×BN]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + SST * C::SC_BYTES);
+    uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;                          // [EPI_WARPS][4 KB] output staging
+    float* sSc = reinterpret_cast<float*>(sOut + EPI_WARPS * C::STAGE_OUT_BYTES);   // [SST][dx BPS×128 | dw BPS×BN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sSc) + SST * C::SC_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* sfull = empty + STAGES;
     uint64_t* sempty = sfull + SST;
@@ -126,9 +130,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = warp_id(), lane = lane_id();
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nblk = p.K / 32;
     const int iters = (nblk + BPS - 1) / BPS;
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_n * ((p.M + BM - 1) / BM);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -139,152 +144,169 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
     }
     if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmDX); prefetch_tmap(&tmDW);
+        prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmDX); prefetch_tmap(&tmDW); prefetch_tmap(&tmOut);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Persistent: every role walks the same tile sequence (N fastest, so concurrent CTAs share activation rows in
+    // L2); the stage ring, scale ring and TMEM buffers run on across tiles, so one tile's stores overlap the next
+    // tile's loads and MMAs.  stage_base / block_base count stages and blocks issued by this CTA so far.
     if (warp == 0) {
-        // ---- producer: operand tiles and, per stage, the 4 blocks' scales for this tile's rows and columns
+        // ---- producer: operand tiles and, per stage, the blocks' scales for this tile's rows and columns
         if (lane == 0) {
-            for (int it = 0; it < iters; ++it) {
-                const int s = it % STAGES, ss = it % SST;
-                if (!mbar_wait(empty + s, ((it / STAGES) & 1) ^ 1, abort_flag, p.err)) break;
-                mbar_arrive_expect_tx(full + s, C::STAGE_BYTES);
-                tma_load_2d(sA + s * C::A_BYTES, &tmA, full + s, it * BK, m0);   // x in codes (2 bytes each)
-                tma_load_2d(sB + s * C::B_BYTES, &tmB, full + s, it * BK, n0);
-                if (!mbar_wait(sempty + ss, ((it / SST) & 1) ^ 1, abort_flag, p.err)) break;
-                mbar_arrive_expect_tx(sfull + ss, C::SC_BYTES);
-                float* slot = sSc + ss * C::SC_FLOATS;
-                tma_load_2d(slot, &tmDX, sfull + ss, m0, it * BPS);
-                tma_load_2d(slot + BPS * BM, &tmDW, sfull + ss, n0, it * BPS);
+            uint32_t g = 0;   // global stage counter
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+                for (int it = 0; it < iters; ++it, ++g) {
+                    const int s = g % STAGES, ss = g % SST;
+                    if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full + s, C::STAGE_BYTES);
+                    tma_load_2d(sA + s * C::A_BYTES, &tmA, full + s, it * BK, m0);   // x counts codes
+                    tma_load_2d(sB + s * C::B_BYTES, &tmB, full + s, it * BK, n0);
+                    if (!mbar_wait(sempty + ss, ((g / SST) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(sfull + ss, C::SC_BYTES);
+                    float* slot = sSc + ss * C::SC_FLOATS;
+                    tma_load_2d(slot, &tmDX, sfull + ss, m0, it * BPS);
+                    tma_load_2d(slot + BPS * BM, &tmDW, sfull + ss, n0, it * BPS);
+                }
             }
         }
     } else if (warp == 1) {
         // ---- MMA issuer: per Q8_0 block two K=16 kind::f16 instructions into that block's own TMEM buffer
         if (lane == 0) {
-            for (int b = 0; b < nblk; ++b) {
-                const int it = b / BPS, j = b % BPS, s = it % STAGES;
-                if (j == 0) {
-                    if (!mbar_wait(full + s, (it / STAGES) & 1, abort_flag, p.err)) break;
+            uint32_t stage_base = 0, block_base = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                for (int b = 0; b < nblk; ++b) {
+                    const int j = b % BPS;
+                    const uint32_t g = stage_base + b / BPS, gb = block_base + b;
+                    const int s = g % STAGES, buf = gb % NBUF;
+                    if (j == 0) {
+                        if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
+                    }
+                    if (!mbar_wait(tempty + buf, ((gb / NBUF) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                }
-                const int buf = b % NBUF;
-                if (!mbar_wait(tempty + buf, ((b / NBUF) & 1) ^ 1, abort_flag, p.err)) break;
-                tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {   // 16 codes = 32 bytes per instruction
-                    const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_BYTES + j * 64 + kk * 32));
-                    const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_BYTES + j * 64 + kk * 32));
-                    mma_f16(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, kk);
+                    for (int kk = 0; kk < 2; ++kk) {   // 16 codes = 32 bytes per instruction
+                        const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * C::A_BYTES + j * 64 + kk * 32));
+                        const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * C::B_BYTES + j * 64 + kk * 32));
+                        mma_f16(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, kk);
+                    }
+                    mma_commit(tfull + buf);
+                    if (j == BPS - 1 || b == nblk - 1) mma_commit(empty + s);
                 }
-                mma_commit(tfull + buf);
-                if (j == BPS - 1 || b == nblk - 1) mma_commit(empty + s);
+                stage_base += iters;
+                block_base += nblk;
             }
         }
     } else {
-        // ---- epilogue warps: drain each block's int32 sums and apply the rescale in the reference's order
+        // ---- epilogue warps: drain each block's exact sums and apply the rescale in the reference's order
         const int e = warp - 2;
         const int quarter = warp & 3;
         const int grp = e >> 2;
         const int row = quarter * 32 + lane;
-        const int grow = m0 + row;
         const int col0 = grp * CPT;
-        const int gcol0 = n0 + col0;
-
-        float acc[CPT];
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) {
-            const int c = gcol0 + j;
-            acc[j] = (p.bias != nullptr && c < p.N) ? __ldg(p.bias + c) : 0.0f;
-        }
         const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(col0);
+        uint32_t stage_base = 0, block_base = 0;
         bool ok = true;
-        for (int b = 0; b < nblk; ++b) {
-            const int it = b / BPS, j = b % BPS, ss = it % SST;
-            if (j == 0 && !mbar_wait(sfull + ss, (it / SST) & 1, abort_flag, p.err)) { ok = false; break; }
-            const int buf = b % NBUF;
-            if (!mbar_wait(tfull + buf, (b / NBUF) & 1, abort_flag, p.err)) { ok = false; break; }
-            tc_fence_after();
-            const float* slot = sSc + ss * C::SC_FLOATS;
-            const float dxr = slot[j * BM + row];
-            const float* dw = slot + BPS * BM + j * BN + col0;
-            // one 32-column chunk in registers at a time; the TMEM buffer is released after its last load
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+            const int grow = m0 + row;
+            const int gcol0 = n0 + col0;
+            float acc[CPT];
 #pragma unroll
-            for (int c = 0; c < CPT / 32; ++c) {
-                uint32_t s[32];
-                tmem_ld32(tbase + static_cast<uint32_t>(buf * BN + c * 32), s);
-                tmem_ld_wait();
-                if (c == CPT / 32 - 1) {
-                    tc_fence_before();
+            for (int j = 0; j < CPT; ++j) {
+                const int c = gcol0 + j;
+                acc[j] = (p.bias != nullptr && c < p.N) ? __ldg(p.bias + c) : 0.0f;
+            }
+            for (int b = 0; b < nblk; ++b) {
+                const int j = b % BPS;
+                const uint32_t g = stage_base + b / BPS, gb = block_base + b;
+                const int ss = g % SST, buf = gb % NBUF;
+                if (j == 0 && !mbar_wait(sfull + ss, (g / SST) & 1, abort_flag, p.err)) { ok = false; break; }
+                if (!mbar_wait(tfull + buf, (gb / NBUF) & 1, abort_flag, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const float* slot = sSc + ss * C::SC_FLOATS;
+                const float dxr = slot[j * BM + row];
+                const float* dw = slot + BPS * BM + j * BN + col0;
+                // one 32-column chunk in registers at a time; the TMEM buffer is released after its last load
+#pragma unroll
+                for (int c = 0; c < CPT / 32; ++c) {
+                    uint32_t sv[32];
+                    tmem_ld32(tbase + static_cast<uint32_t>(buf * BN + c * 32), sv);
+                    tmem_ld_wait();
+                    if (c == CPT / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty + buf);
+                    }
+                    rescale32(acc + c * 32, sv, dw + c * 32, dxr);
+                }
+                if (j == BPS - 1 || b == nblk - 1) {
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty + buf);
+                    if (lane == 0) mbar_arrive(sempty + ss);
                 }
-                rescale32(acc + c * 32, s, dw + c * 32, dxr);
             }
-            if (j == BPS - 1 || b == nblk - 1) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(sempty + ss);
-            }
-        }
-
-        if (ok && grow < p.M) {
+            stage_base += iters;
+            block_base += nblk;
+            if (!ok) break;
+            // Outputs leave through a per-warp 4 KB staging tile and TMA bulk stores: one store moves the warp's
+            // 32 rows x 128 B, and the TMA clips rows >= M and columns >= N.
+            uint8_t* stage = sOut + e * C::STAGE_OUT_BYTES;
             if constexpr (EPI == EPI_STORE || EPI == EPI_RESID) {
-                float* o = p.out + static_cast<size_t>(grow) * p.ldo + gcol0;
-                const bool vec = (gcol0 + CPT <= p.N) && ((p.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
-                if (vec) {
 #pragma unroll
-                    for (int j4 = 0; j4 < CPT / 4; ++j4) {
-                        float4 v = make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]);
-                        float4* dst = reinterpret_cast<float4*>(o) + j4;
-                        if constexpr (EPI == EPI_RESID) {
-                            const float4 h = *dst;
-                            v.x = __fadd_rn(h.x, v.x); v.y = __fadd_rn(h.y, v.y);
-                            v.z = __fadd_rn(h.z, v.z); v.w = __fadd_rn(h.w, v.w);
-                        }
-                        *dst = v;
-                    }
-                } else {
+                for (int c = 0; c < CPT / 32; ++c) {
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                    // 128-byte swizzle: 16-byte chunk q of row r sits at chunk q ^ (r mod 8)
 #pragma unroll
-                    for (int j = 0; j < CPT; ++j) {
-                        if (gcol0 + j < p.N) {
-                            if constexpr (EPI == EPI_RESID) o[j] = __fadd_rn(o[j], acc[j]);
-                            else o[j] = acc[j];
-                        }
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                            make_float4(acc[c * 32 + 4 * q], acc[c * 32 + 4 * q + 1], acc[c * 32 + 4 * q + 2], acc[c * 32 + 4 * q + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (EPI == EPI_RESID) tma_reduce_add_2d(&tmOut, gcol0 + c * 32, m0 + quarter * 32, stage);
+                        else tma_store_2d(&tmOut, gcol0 + c * 32, m0 + quarter * 32, stage);
+                        bulk_commit();
                     }
                 }
-            } else if constexpr (EPI == EPI_GEGLU_Q8) {
-                // Column groups of 64: [32 GELU inputs | their 32 gates] -> 32 activations = one Q8_0 block of
-                // the next product's input (ModernBertEncoder.GeGlu, ModernBertEncoder.cs:204-214).
+            } else if constexpr (EPI == EPI_GEGLU_Q8 || EPI == EPI_RELU_Q8) {
+                // 32 activations per thread and group -> one Q8_0 block of the next product's input:
+                // GeGLU groups of 64 columns are [32 GELU inputs | their 32 gates] (ModernBertEncoder.GeGlu,
+                // ModernBertEncoder.cs:204-214); ReLU groups are 32 columns (DecisionModel.cs:300).
+                constexpr int GW = EPI == EPI_GEGLU_Q8 ? 64 : 32;
 #pragma unroll
-                for (int g = 0; g < CPT / 64; ++g) {
-                    const int pcol = gcol0 + g * 64;
-                    if (pcol < p.N) {
-                        const int blk = pcol / 64;
-                        float act[32];
+                for (int g = 0; g < CPT / GW; ++g) {
+                    const int pcol = gcol0 + g * GW;
+                    const int blk = pcol / GW;           // output block index (32 codes)
+                    float act[32];
+                    if constexpr (EPI == EPI_GEGLU_Q8) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) act[j] = __fmul_rn(ref_gelu(acc[g * 64 + j]), acc[g * 64 + 32 + j]);
-                        quantize_block32_store(act, p.qout + static_cast<size_t>(grow) * p.ldqo + blk * 32,
-                                               p.qsc + static_cast<size_t>(blk) * p.ldqs + grow);
-                    }
-                }
-            } else if constexpr (EPI == EPI_RELU_Q8) {
-                // nn.TransformerEncoderLayer's ReLU feed-forward (DecisionModel.cs:300), quantized for linear2.
-#pragma unroll
-                for (int g = 0; g < CPT / 32; ++g) {
-                    const int c = gcol0 + g * 32;
-                    if (c < p.N) {
-                        float act[32];
+                    } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) act[j] = fmaxf(acc[g * 32 + j], 0.0f);
-                        quantize_block32_store(act, p.qout + static_cast<size_t>(grow) * p.ldqo + c,
-                                               p.qsc + static_cast<size_t>(c / 32) * p.ldqs + grow);
+                    }
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                    float d;
+                    quantize_block32_store(act, reinterpret_cast<code_t*>(stage + lane * 64), &d);   // 64 B per row
+                    if (pcol < p.N && grow < p.M) p.qsc[static_cast<size_t>(blk) * p.ldqs + grow] = d;
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (pcol < p.N) { tma_store_2d(&tmOut, blk * 32, m0 + quarter * 32, stage); bulk_commit(); }
                     }
                 }
             }
         }
+        if (lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -300,13 +322,20 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
 template <int BN, int EPI_WARPS, int STAGES, int EPI>
 static int launch(const GemmArgs& a, cudaStream_t stream) {
     using C = Cfg<BN, EPI_WARPS, STAGES>;
-    CUtensorMap tA, tB, tDX, tDW;
+    CUtensorMap tA, tB, tDX, tDW, tO;
     int rc = make_tmap_2d(&tA, a.qx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.K) * 2, BM, BK);
     if (!rc) rc = make_tmap_2d(&tB, a.qw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.K) * 2, BN, BK);
     if (!rc) rc = make_tmap_2d(&tDX, a.dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.K / 32, a.ldx,
                                static_cast<uint64_t>(a.ldx) * 4, BPS, BM, false);
     if (!rc) rc = make_tmap_2d(&tDW, a.dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.K / 32, a.ldw,
                                static_cast<uint64_t>(a.ldw) * 4, BPS, BN, false);
+    if (!rc) {
+        if (EPI == EPI_STORE || EPI == EPI_RESID)
+            rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
+        else   // codes [M, ldqo] fp16-held, 32 codes (64 B) per row per store, no swizzle
+            rc = make_tmap_2d(&tO, a.qout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.M, EPI == EPI_GEGLU_Q8 ? a.N / 2 : a.N,
+                              static_cast<uint64_t>(a.ldqo) * 2, 32, 32, false);
+    }
     if (rc) return rc;
     auto kern = q8_gemm_kernel<BN, EPI_WARPS, STAGES, EPI>;
     int dev = 0;
@@ -317,8 +346,11 @@ static int launch(const GemmArgs& a, cudaStream_t stream) {
         attr_set |= 1ull << dev;
     }
     KParams p{a.M, a.N, a.K, a.bias, a.out, a.ldo, a.qout, a.ldqo, a.qsc, a.ldqs, a.err};
-    dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-    kern<<<grid, C::THREADS, C::SMEM, stream>>>(tA, tB, tDX, tDW, p);
+    static int sms[64] = {0};
+    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
+    const int ctas = tiles < (dev < 64 ? sms[dev] : 148) ? tiles : (dev < 64 ? sms[dev] : 148);
+    kern<<<ctas, C::THREADS, C::SMEM, stream>>>(tA, tB, tDX, tDW, tO, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -334,6 +366,12 @@ int gemm(const GemmArgs& a, cudaStream_t stream) {
     if ((reinterpret_cast<uintptr_t>(a.qx) & 15) || (reinterpret_cast<uintptr_t>(a.qw) & 15) ||
         (reinterpret_cast<uintptr_t>(a.dx) & 15) || (reinterpret_cast<uintptr_t>(a.dw) & 15)) {
         set_error("Q8_0 operands and scales must be 16-byte aligned"); return ERR_ARGUMENT;
+    }
+    if ((a.epi == EPI_STORE || a.epi == EPI_RESID) && ((reinterpret_cast<uintptr_t>(a.out) & 15) || (a.ldo & 3))) {
+        set_error("product output must be 16-byte aligned with a row stride that is a multiple of 4"); return ERR_ARGUMENT;
+    }
+    if ((a.epi == EPI_GEGLU_Q8 || a.epi == EPI_RELU_Q8) && ((reinterpret_cast<uintptr_t>(a.qout) & 15) || (a.ldqo & 7))) {
+        set_error("code output must be 16-byte aligned with a row stride that is a multiple of 8"); return ERR_ARGUMENT;
     }
     constexpr int BN = 192, EW = 12, ST = 4;
     switch (a.epi) {
