@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "train.h"
 
 namespace laya {
 
@@ -940,6 +941,19 @@ int laya_q8_0_linear(laya_ctx* c, const char* weight, const float* x, int rows, 
 int laya_q8_0_linear_device(laya_ctx* c, const char* weight, const float* x, int rows, int input_stride,
                             const float* bias, float* y, int output_stride) {
     return q8_linear_impl(c, weight, x, rows, input_stride, bias, y, output_stride, false);
+}
+
+int laya_gemm_bf16_device(laya_ctx* c, int M, int N, int K, const uint16_t* A, int lda, int a_mn, const uint16_t* B,
+                          int ldb, int b_mn, const float* bias, int epilogue, void* out, int ldo) {
+    if (!c) { set_error("null context"); return ERR_ARGUMENT; }
+    if (epilogue < 0 || epilogue > 2) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    bf::Args a{};
+    a.M = M; a.N = N; a.K = K;
+    a.A = reinterpret_cast<const __nv_bfloat16*>(A); a.lda = lda; a.a_mn = a_mn != 0;
+    a.B = reinterpret_cast<const __nv_bfloat16*>(B); a.ldb = ldb; a.b_mn = b_mn != 0;
+    a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.err = c->err;
+    return bf::gemm(a, c->stream);
 }
 
 // ------------------------------------------------------------------------------------------------ forward

@@ -1,0 +1,313 @@
+// gemm_bf16.cu — the bf16 tensor-core products of the training step (sm_100a tcgen05, fp32 accumulation in TMEM).
+//
+// Replaces the fp32 panel GEMM of the reference's training path (PackedMatrix.Multiply, Base/Numerics/PackedMatrix.cs:
+// 121-305) as used by Ops.Linear / Ops.LinearBackward (Laya.Training/Ops.cs:22-69):
+//     forward   y  = x · Wᵀ (+ b)          A = x  [T, K] K-major,        B = W  [N, K] K-major
+//     input     dx = dy · W                 A = dy [T, N] K-major,        B = W  [N, K] read MN-major (K contiguous)
+//     weight    dW += dyᵀ · x               A = dy [T, N] read MN-major,  B = x  [T, K] read MN-major
+// Operand majorness is a bit of the tcgen05 instruction descriptor plus the shared-memory descriptor layout, so no
+// operand is ever transposed in memory (the reference transposes dy and repacks x for every dW, Ops.cs:43-62).
+//
+// CTA layout: persistent, one CTA per SM, tiles of 128 × BN walked N-fastest.
+//   warp 0      TMA producer, STAGES-deep ring of A and B tiles (64 codes of K per stage = one 128-byte swizzle row).
+//   warp 1      TMEM allocator and MMA issuer: 4 × (M=128, N=BN, K=16) per stage into one of two TMEM accumulators,
+//               so the epilogue of one tile overlaps the MMAs of the next.
+//   warps 2-9   epilogue: 4 lane quarters × 2 column halves; each drains 32-column chunks with tcgen05.ld, adds the
+//               bias, converts, stages 32 rows × 128 B in shared memory and writes them with one TMA store (or TMA
+//               reduce-add for accumulating outputs: residual streams and parameter gradients).
+#include "common.cuh"
+#include "internal.h"
+#include "train.h"
+
+namespace laya {
+namespace bf {
+
+constexpr int BM = 128;
+constexpr int BK = 64;           // bf16 per 128-byte row
+constexpr int EPI_WARPS = 8;
+
+template <int BN, int STAGES>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGE_OUT = 4096;
+    static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT + BAR_BYTES;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(2 * BN <= 512, "two TMEM accumulators");
+};
+
+// MN-major operand, 128-byte swizzle: 64-element MN atoms of BK rows each (LBO apart), 8-row K groups 1024 B apart.
+DEVI uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+struct KParams {
+    int M, N, K;
+    const float* bias;
+    int* err;
+};
+
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
+__global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmOut, KParams p) {
+    using C = Cfg<BN, STAGES>;
+    constexpr uint32_t IDESC = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, BM, BN) |
+                               (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * C::STAGE_OUT);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = warp_id(), lane = lane_id();
+    const int iters = (p.K + BK - 1) / BK;
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_n * ((p.M + BM - 1) / BM);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(tfull + b, 1); mbar_init(tempty + b, EPI_WARPS); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmOut); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+                for (int kb = 0; kb < iters; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full + s, C::STAGE_BYTES);
+                    uint8_t* a = sA + s * C::A_BYTES;
+                    uint8_t* b = sB + s * C::B_BYTES;
+                    if constexpr (A_MN) {
+#pragma unroll
+                        for (int j = 0; j < BM / 64; ++j) tma_load_2d(a + j * (BK * 128), &tmA, full + s, m0 + 64 * j, kb * BK);
+                    } else {
+                        tma_load_2d(a, &tmA, full + s, kb * BK, m0);
+                    }
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * (BK * 128), &tmB, full + s, n0 + 64 * j, kb * BK);
+                    } else {
+                        tma_load_2d(b, &tmB, full + s, kb * BK, n0);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t g = 0, ti = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ti) {
+                const int buf = ti & 1;
+                if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+                tc_fence_after();
+                for (int kb = 0; kb < iters; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(sA + s * C::A_BYTES), b = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = A_MN ? smem_desc_mn_sw128(a + kk * 2048, BK * 128) : smem_desc_sw128(a + kk * 32);
+                        const uint64_t bd = B_MN ? smem_desc_mn_sw128(b + kk * 2048, BK * 128) : smem_desc_sw128(b + kk * 32);
+                        mma_f16(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(empty + s);
+                }
+                mma_commit(tfull + buf);
+            }
+        }
+    } else {
+        const int e = warp - 2;
+        const int quarter = warp & 3;
+        const int half = e >> 2;
+        constexpr int COLS = BN / 2;
+        uint8_t* stage = sOut + e * C::STAGE_OUT;
+        uint32_t ti = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+            const int buf = ti & 1;
+            const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+            if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
+            const int gc0 = n0 + half * COLS;
+            const int gr0 = m0 + quarter * 32;
+            if constexpr (EPI == EPI_BF16) {
+                // 64 columns per chunk: 64 bf16 = one 128-byte swizzled row per lane
+#pragma unroll 1
+                for (int c = 0; c < COLS / 64; ++c) {
+                    uint32_t v0[32], v1[32];
+                    tmem_ld32(tbase + c * 64, v0);
+                    tmem_ld32(tbase + c * 64 + 32, v1);
+                    tmem_ld_wait();
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int j = q * 8 + 2 * t;
+                            float lo = __uint_as_float(j < 32 ? v0[j] : v1[j - 32]);
+                            float hi = __uint_as_float(j + 1 < 32 ? v0[j + 1] : v1[j + 1 - 32]);
+                            if (p.bias) {
+                                const int col = gc0 + c * 64 + j;
+                                lo += col < p.N ? __ldg(p.bias + col) : 0.0f;
+                                hi += col + 1 < p.N ? __ldg(p.bias + col + 1) : 0.0f;
+                            }
+                            __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+                            w[t] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        *reinterpret_cast<uint4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) { tma_store_2d(&tmOut, gc0 + c * 64, gr0, stage); bulk_commit(); }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < COLS / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + c * 32, v);
+                    tmem_ld_wait();
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float4 f;
+                        float* fp = &f.x;
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int j = q * 4 + t;
+                            float x = __uint_as_float(v[j]);
+                            if (p.bias) {
+                                const int col = gc0 + c * 32 + j;
+                                x += col < p.N ? __ldg(p.bias + col) : 0.0f;
+                            }
+                            fp[t] = x;
+                        }
+                        *reinterpret_cast<float4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = f;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (EPI == EPI_F32_ADD) tma_reduce_add_2d(&tmOut, gc0 + c * 32, gr0, stage);
+                        else tma_store_2d(&tmOut, gc0 + c * 32, gr0, stage);
+                        bulk_commit();
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + buf);
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
+static int launch(const Args& a, cudaStream_t stream) {
+    using C = Cfg<BN, STAGES>;
+    CUtensorMap tA, tB, tO;
+    int rc;
+    if (A_MN) rc = make_tmap_2d(&tA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
+    else rc = make_tmap_2d(&tA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
+    if (!rc) {
+        if (B_MN) rc = make_tmap_2d(&tB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, static_cast<uint64_t>(a.ldb) * 2, BK, 64);
+        else rc = make_tmap_2d(&tB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, BN, BK);
+    }
+    if (!rc) {
+        if (EPI == EPI_BF16)
+            rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
+        else
+            rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
+    }
+    if (rc) return rc;
+    auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    static uint64_t attr_set = 0;
+    static int sms[64] = {0};
+    if (dev < 64 && !(attr_set & (1ull << dev))) {
+        LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        attr_set |= 1ull << dev;
+    }
+    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
+    const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    KParams p{a.M, a.N, a.K, a.bias, a.err};
+    kern<<<tiles < nsm ? tiles : nsm, C::THREADS, C::SMEM, stream>>>(tA, tB, tO, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+template <int BN, int STAGES, int EPI>
+static int dispatch_major(const Args& a, cudaStream_t s) {
+    if (!a.a_mn && !a.b_mn) return launch<BN, STAGES, 0, 0, EPI>(a, s);
+    if (!a.a_mn && a.b_mn) return launch<BN, STAGES, 0, 1, EPI>(a, s);
+    if (a.a_mn && a.b_mn) return launch<BN, STAGES, 1, 1, EPI>(a, s);
+    return launch<BN, STAGES, 1, 0, EPI>(a, s);
+}
+
+int gemm(const Args& a, cudaStream_t stream) {
+    if (a.M <= 0 || a.N <= 0) return OK;
+    if (a.K <= 0) { set_error("bf16 product needs K > 0"); return ERR_ARGUMENT; }
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.out);
+    if ((al & 15) || (a.lda & 7) || (a.ldb & 7) || (a.epi == EPI_BF16 ? (a.ldo & 7) : (a.ldo & 3))) {
+        set_error("bf16 product operands need 16-byte aligned bases and row strides");
+        return ERR_ARGUMENT;
+    }
+    if (a.N <= 128) {
+        switch (a.epi) {
+            case EPI_BF16: return dispatch_major<128, 4, EPI_BF16>(a, stream);
+            case EPI_F32: return dispatch_major<128, 4, EPI_F32>(a, stream);
+            case EPI_F32_ADD: return dispatch_major<128, 4, EPI_F32_ADD>(a, stream);
+        }
+    } else {
+        switch (a.epi) {
+            case EPI_BF16: return dispatch_major<256, 3, EPI_BF16>(a, stream);
+            case EPI_F32: return dispatch_major<256, 3, EPI_F32>(a, stream);
+            case EPI_F32_ADD: return dispatch_major<256, 3, EPI_F32_ADD>(a, stream);
+        }
+    }
+    set_error("unknown bf16 product epilogue");
+    return ERR_ARGUMENT;
+}
+
+}  // namespace bf
+}  // namespace laya

@@ -1,0 +1,54 @@
+"""The bf16 tensor-core product of the training step against torch (fp32 products of the same bf16 values).
+
+The three layouts the training step uses: y = x·Wᵀ (both K-major), dx = dy·W (W read N-contiguous),
+dW += dyᵀ·x (both read with the output index contiguous); epilogues bf16, fp32 and fp32 accumulate, with bias.
+"""
+import numpy as np
+import pytest
+
+from conftest import max_rel
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1000, 2304, 768), (304, 768, 1152), (72, 96, 128), (136, 200, 72), (4096, 1152, 768)]
+LAYOUTS = [(0, 0), (0, 1), (1, 1)]
+
+
+@pytest.fixture(scope="module")
+def ctx(cuda):
+    import laya_b200
+    c = laya_b200.Context(laya_b200.base_desc(max_tokens=256, max_items=4, max_markers=16))
+    c.set_stream(cuda.cuda.current_stream().cuda_stream)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_product_matches_torch(ctx, cuda, M, N, K, a_mn, b_mn, epi):
+    torch = cuda
+    import laya_b200
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K + 13 * a_mn + 5 * b_mn + epi)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=g)
+    As = A.t().contiguous() if a_mn else A
+    Bs = B.t().contiguous() if b_mn else B
+    lda = M if a_mn else K
+    ldb = N if b_mn else K
+    want = A.float() @ B.float().t() + bias
+    if epi == 0:
+        out = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
+    else:
+        out = torch.zeros(M, N, dtype=torch.float32, device="cuda")
+        if epi == 2:
+            base = torch.randn(M, N, device="cuda", generator=g)
+            out.copy_(base)
+            want = want + base
+    laya_b200.api.check(laya_b200.lib().laya_gemm_bf16_device(
+        ctx.handle, M, N, K, As.data_ptr(), lda, a_mn, Bs.data_ptr(), ldb, b_mn, bias.data_ptr(), epi, out.data_ptr(), N))
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    err = max_rel(out.float().cpu().numpy(), want.cpu().numpy())
+    assert err < (8e-3 if epi == 0 else 2e-5), f"max rel {err:.2e}"
