@@ -7,6 +7,8 @@ host-side mirror of the reference's interfaces for that path, over ctypes:
                            Laya/Models/ModernBertEncoder.cs): construct from named weights, `forward(items)`.
   * `PackedMatrixQ8_0`   — the ILinear Q8_0 projection (Base/Numerics/PackedMatrixQ8_0.cs): `multiply(...)`.
   * `Q8_0`               — the quantizers on device buffers.
+  * `Trainer`, `Batch`   — the fine-tuning step of include/laya_train.h (Laya.Training/TrainableDecisionModel.cs,
+                           RlcdObjective.cs, AdamW.cs): forward, objective, backward, clip + AdamW, NCCL buckets.
 
 There is no CPU fallback: importing works anywhere, but every call needs the built library and a B200; a missing
 library raises `LayaLibraryMissing`.
@@ -14,9 +16,10 @@ library raises `LayaLibraryMissing`.
 from .api import (Context, DecisionModel, DecisionOutput, BatchItem, ModelDesc, PackedMatrixQ8_0, Q8_0,
                   LayaError, LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
                   LayaNotFoundError, LayaDeviceTimeout, LayaLibraryMissing, lib, library_path, base_desc,
-                  PRECISION_F32, PRECISION_Q8_0)
+                  PRECISION_F32, PRECISION_Q8_0, Trainer, Batch, TrainingItem, TrainDesc, RlcdDesc, train_desc)
 
 __all__ = ["Context", "DecisionModel", "DecisionOutput", "BatchItem", "ModelDesc", "PackedMatrixQ8_0", "Q8_0",
            "LayaError", "LayaArgumentError", "LayaOutOfRangeError", "LayaNotSupportedError", "LayaCudaError",
            "LayaNotFoundError", "LayaDeviceTimeout", "LayaLibraryMissing", "lib", "library_path", "base_desc",
-           "PRECISION_F32", "PRECISION_Q8_0"]
+           "PRECISION_F32", "PRECISION_Q8_0", "Trainer", "Batch", "TrainingItem", "TrainDesc", "RlcdDesc",
+           "train_desc"]

@@ -99,6 +99,31 @@ _SIGS = {
     "laya_record_enable": (_I, [_P, _I]),
     "laya_record_get": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
     "laya_encoder_layer": (_I, [_P, _I, _P, _P, _I]),
+    # include/laya_train.h
+    "laya_trainer_create": (_I, [ctypes.POINTER(ModelDesc), _P, _I, ctypes.POINTER(_P)]),
+    "laya_trainer_destroy": (_I, [_P]),
+    "laya_trainer_set_stream": (_I, [_P, _P]),
+    "laya_trainer_get_stream": (_I, [_P, ctypes.POINTER(_P)]),
+    "laya_trainer_synchronize": (_I, [_P]),
+    "laya_trainer_upload": (_I, [_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P]),
+    "laya_trainer_download": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
+    "laya_trainer_download_grad": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
+    "laya_trainer_param_count": (_I, [_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+    "laya_trainer_param_info": (_I, [_P, _I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_int64),
+                                     ctypes.POINTER(ctypes.c_int64)]),
+    "laya_batch_create": (_I, [_P, ctypes.POINTER(_P)]),
+    "laya_batch_destroy": (_I, [_P]),
+    "laya_batch_set": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I]),
+    "laya_batch_shape": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "laya_train_forward": (_I, [_P, _P, _I, ctypes.c_uint64, _P]),
+    "laya_train_objective": (_I, [_P, _P, _P, _P, _P]),
+    "laya_train_backward": (_I, [_P, _P, _P]),
+    "laya_train_set_lr": (_I, [_P, _P, _I]),
+    "laya_train_clip_and_step": (_I, [_P, ctypes.c_double, _P]),
+    "laya_train_zero_grads": (_I, [_P]),
+    "laya_train_steps": (_I, [_P, ctypes.POINTER(ctypes.c_int64)]),
+    "laya_comm_unique_id": (_I, [_P]),
+    "laya_train_comm_init": (_I, [_P, _P, _I, _I]),
 }
 
 
@@ -391,3 +416,220 @@ class DecisionModel:
         sl = _i32(seg_len)
         check(lib().laya_encoder_layer(self.ctx.handle, layer, _np_ptr(h), _np_ptr(sl), len(sl)))
         return h
+
+
+# --------------------------------------------------------------------------------------------------- training
+class TrainDesc(ctypes.Structure):
+    """laya_train_desc (include/laya_train.h): TrainerOptions + AdamW settings (Trainer.cs:16-58)."""
+    _fields_ = [("trainable_encoder_layers", ctypes.c_int), ("head_dropout", ctypes.c_float),
+                ("beta1", ctypes.c_double), ("beta2", ctypes.c_double), ("eps", ctypes.c_double),
+                ("weight_decay", ctypes.c_double), ("encoder_lr", ctypes.c_double), ("head_lr", ctypes.c_double),
+                ("max_segment", ctypes.c_int), ("grad_accumulation", ctypes.c_int)]
+
+
+class RlcdDesc(ctypes.Structure):
+    """laya_rlcd_desc: RlcdObjective settings (RlcdObjective.cs:31-35) + sigma and gradient scale."""
+    _fields_ = [("groups", ctypes.c_int), ("sigma", ctypes.c_double), ("scale", ctypes.c_double),
+                ("spherical_weight", ctypes.c_double), ("rps_weight", ctypes.c_double),
+                ("cross_entropy_weight", ctypes.c_double)]
+
+
+def train_desc(**kw) -> TrainDesc:
+    """Trainer defaults (TrainerOptions: encoder 2.5e-5, head 1e-4, wd 0.01, dropout 0.1; AdamW 0.9/0.999/1e-8)."""
+    d = dict(trainable_encoder_layers=-1, head_dropout=0.1, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
+             encoder_lr=2.5e-5, head_lr=1e-4, max_segment=0, grad_accumulation=1)
+    d.update(kw)
+    return TrainDesc(**d)
+
+
+@dataclass
+class TrainingItem:
+    """TrainingItem (Laya.Training): token ids, option marker positions, question type, soft target per option."""
+    token_ids: np.ndarray
+    marker_positions: np.ndarray
+    question_type: int
+    target: Optional[np.ndarray] = None
+
+    @property
+    def options(self) -> int:
+        return len(self.marker_positions)
+
+
+class Batch:
+    """A batch resident on the device (laya_batch)."""
+
+    def __init__(self, trainer: "Trainer"):
+        self.trainer = trainer
+        h = ctypes.c_void_p()
+        check(lib().laya_batch_create(trainer.handle, ctypes.byref(h)))
+        self.handle = h
+
+    def set(self, items: List[TrainingItem], draws: Optional[np.ndarray] = None):
+        """draws: standard normals [groups, options] in item order (RlcdObjective's supplied-draws overload)."""
+        ids = _i32(np.concatenate([np.asarray(it.token_ids, np.int64) for it in items]))
+        seg_len = _i32([len(it.token_ids) for it in items])
+        qtype = _i32([it.question_type for it in items])
+        counts = _i32([it.options for it in items])
+        markers = _i32(np.concatenate([np.asarray(it.marker_positions, np.int64) for it in items]))
+        tg = [np.zeros(it.options, np.float32) if it.target is None else np.asarray(it.target, np.float32)
+              for it in items]
+        targets = _f32(np.concatenate(tg))
+        groups = 0
+        dr = None
+        if draws is not None:
+            dr = np.ascontiguousarray(draws, dtype=np.float64)
+            groups = dr.shape[0]
+            if dr.shape[1] != int(counts.sum()):
+                raise LayaArgumentError("draws must be [groups, options]")
+        check(lib().laya_batch_set(self.trainer.handle, self.handle, _np_ptr(ids), _np_ptr(seg_len), _np_ptr(qtype),
+                                   len(items), _np_ptr(counts), _np_ptr(markers), _np_ptr(targets), _np_ptr(dr),
+                                   groups))
+        self.counts = counts
+        self._keep = (ids, seg_len, qtype, counts, markers, targets, dr)   # pinned staging copies them; keep anyway
+        return self
+
+    def shape(self):
+        t, n, m = _I(), _I(), _I()
+        check(lib().laya_batch_shape(self.handle, ctypes.byref(t), ctypes.byref(n), ctypes.byref(m)))
+        return t.value, n.value, m.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_batch_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Trainer:
+    """The fine-tuning step on the device (laya_trainer): TrainableDecisionModel + RlcdObjective + AdamW."""
+
+    def __init__(self, desc: ModelDesc, tdesc: Optional[TrainDesc] = None, device: int = 0):
+        self.desc = desc
+        self.tdesc = tdesc or train_desc()
+        h = ctypes.c_void_p()
+        check(lib().laya_trainer_create(ctypes.byref(desc), ctypes.byref(self.tdesc), device, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_trainer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # parameters
+    def names(self) -> List[Tuple[str, int, int]]:
+        out = []
+        i = 0
+        while True:
+            nm, r, c = ctypes.c_char_p(), ctypes.c_int64(), ctypes.c_int64()
+            rc = lib().laya_trainer_param_info(self.handle, i, ctypes.byref(nm), ctypes.byref(r), ctypes.byref(c))
+            if rc != 0:
+                break
+            out.append((nm.value.decode(), r.value, c.value))
+            i += 1
+        return out
+
+    def upload(self, name: str, array: np.ndarray, dtype: int = F32):
+        a = np.ascontiguousarray(array, dtype=np.float32 if dtype == F32 else np.uint16)
+        shape = (ctypes.c_int64 * max(1, a.ndim))(*a.shape)
+        check(lib().laya_trainer_upload(self.handle, name.encode(), dtype, shape, a.ndim, _np_ptr(a)))
+
+    def load(self, weights: Dict[str, np.ndarray]):
+        for k, v in weights.items():
+            self.upload(k, v)
+
+    def download(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(shape, np.float32)
+        check(lib().laya_trainer_download(self.handle, name.encode(), _np_ptr(out), out.size))
+        return out
+
+    def gradient(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(shape, np.float32)
+        check(lib().laya_trainer_download_grad(self.handle, name.encode(), _np_ptr(out), out.size))
+        return out
+
+    def param_count(self) -> Tuple[int, int]:
+        a, b = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().laya_trainer_param_count(self.handle, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+
+    def batch(self, items: List[TrainingItem], draws: Optional[np.ndarray] = None) -> Batch:
+        return Batch(self).set(items, draws)
+
+    # the step
+    def forward(self, batch: Batch, training: bool = False, seed: int = 0, fetch: bool = True):
+        """TrainableDecisionModel.Forward: option logits per item (device-resident tape kept for backward)."""
+        _, _, m = batch.shape()
+        logits = np.zeros(max(1, m), np.float32) if fetch else None
+        check(lib().laya_train_forward(self.handle, batch.handle, int(training), ctypes.c_uint64(seed & (2**64 - 1)),
+                                       _np_ptr(logits)))
+        if not fetch:
+            return None
+        out, o = [], 0
+        for k in batch.counts:
+            out.append(logits[o:o + k].copy())
+            o += k
+        return out
+
+    def objective(self, batch: Batch, sigma: float, groups: int = 4, scale: float = 1.0, spherical_weight=0.75,
+                  rps_weight=1.0, cross_entropy_weight=1.0, fetch: bool = True):
+        """RlcdObjective.Compute with the batch's draws: ((loss, policy, cross-entropy, mean reward), dlogits per item)."""
+        o = RlcdDesc(groups, sigma, scale, spherical_weight, rps_weight, cross_entropy_weight)
+        res = np.zeros(4, np.float64) if fetch else None
+        d = np.zeros(max(1, int(batch.counts.sum())), np.float32) if fetch else None
+        check(lib().laya_train_objective(self.handle, batch.handle, ctypes.byref(o), _np_ptr(res), _np_ptr(d)))
+        if res is None:
+            return None
+        grads, k0 = [], 0
+        for k in batch.counts:
+            grads.append(d[k0:k0 + k].copy())
+            k0 += k
+        return tuple(float(x) for x in res), grads
+
+    def backward(self, batch: Batch, dlogits: Optional[Sequence[np.ndarray]] = None):
+        """TrainableDecisionModel.Backward: accumulates gradients; dlogits per item, or None for the objective's."""
+        d = None if dlogits is None else _f32(np.concatenate([np.asarray(x, np.float32) for x in dlogits]))
+        check(lib().laya_train_backward(self.handle, batch.handle, _np_ptr(d)))
+
+    def set_lr(self, encoder_lr: float, head_lr: float):
+        lr = np.array([encoder_lr, head_lr], np.float64)
+        check(lib().laya_train_set_lr(self.handle, _np_ptr(lr), 2))
+
+    def clip_and_step(self, max_norm: float = 1.0, fetch_norm: bool = True) -> Optional[float]:
+        norm = np.zeros(1, np.float64) if fetch_norm else None
+        check(lib().laya_train_clip_and_step(self.handle, max_norm, _np_ptr(norm)))
+        return None if norm is None else float(norm[0])
+
+    def zero_grads(self):
+        check(lib().laya_train_zero_grads(self.handle))
+
+    def synchronize(self):
+        check(lib().laya_trainer_synchronize(self.handle))
+
+    def set_stream(self, stream_handle: Optional[int]):
+        check(lib().laya_trainer_set_stream(self.handle, ctypes.c_void_p(stream_handle or 0)))
+
+    def steps(self) -> int:
+        s = ctypes.c_int64()
+        check(lib().laya_train_steps(self.handle, ctypes.byref(s)))
+        return s.value
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(lib().laya_comm_unique_id(buf))
+        return buf.raw
+
+    def comm_init(self, uid: bytes, rank: int, world: int):
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        check(lib().laya_train_comm_init(self.handle, buf, rank, world))

@@ -1,0 +1,454 @@
+// flash.cu — attention forward and backward of the training step (bf16 operands, fp32 softmax and accumulators).
+//
+// Replaces Ops.AttentionForward/ForwardUnit and Ops.AttentionBackward/BackwardUnit with Rotary
+// (Laya.Training/Ops.cs:260-504):
+//   * per (segment, head), positions restarting at 0 in every segment; sliding layers see [i - W, i + W];
+//   * rotary (rotate half) applied to q and k as tiles are loaded; the backward rotates dq and dk back
+//     (Rotary.Apply with inverse: true) before writing them;
+//   * dropout on the probabilities (the decision head's layers in training) by the reference's counter hash
+//     Ops.Uniform(seed, (head << 42) | (row << 21) | key) with row the token's index in the batch and key the key's
+//     position in its segment, so masks are the reference's bit for bit;
+//   * forward keeps the row log-sum-exp; backward recomputes P from it:
+//       D_i = Σ_d dO_id · O_id;  dP_ij = mask_ij · dO_i·v_j;  dS_ij = scale · P_ij · (dP_ij − D_i)
+//       dV_j = Σ_i P_ij mask_ij dO_i;  dQ_i = Σ_j dS_ij k_j;  dK_j = Σ_i dS_ij q_i
+//     split into a query-tile kernel (dQ) and a key-tile kernel (dK, dV), each recomputing P: no atomics, so the
+//     gradients are deterministic.
+// Tiles are 64 queries × 64 keys; each of the 4 warps owns 16 rows; mma.sync m16n8k16 bf16 → fp32.
+#include "common.cuh"
+#include "internal.h"
+#include "train.h"
+
+namespace laya {
+namespace fa {
+
+constexpr int T64 = 64;
+constexpr int LDS = 64 + 8;   // smem row stride (bf16) to spread banks
+constexpr float LOG2E = 1.4426950408889634f;
+
+DEVI void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+DEVI void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+DEVI void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+DEVI uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Ops.Uniform (Ops.cs:227-234) on the device: the same 64-bit mixing, the same fp32 result.
+DEVI float dropout_uniform(uint64_t seed, uint64_t index) {
+    uint64_t z = seed + (index + 1ull) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f);
+}
+DEVI float drop_mult(const Args& a, int head, int row, int key) {
+    if (a.dropout <= 0.0f) return 1.0f;
+    const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
+    return dropout_uniform(a.seed, idx) < a.dropout ? 0.0f : a.keep;
+}
+
+// Loads 64 rows of one head's slice (columns col0 .. col0+HD) at segment positions [p0, p0+64) from a bf16 [T, ld]
+// buffer into smem, rotating pairs (i, i+HD/2) when cos/sin are given.  Rows past `limit` are zero.
+template <int HD>
+DEVI void load_rows(__nv_bfloat16* dst, const __nv_bfloat16* base, int ld, int p0, int limit, const float* cosv,
+                    const float* sinv) {
+    constexpr int HALF = HD / 2, J = HALF / 4;   // 4 pairs per step
+    for (int it = threadIdx.x; it < 64 * J; it += blockDim.x) {
+        const int r = it / J, j = it % J;
+        const int pos = p0 + r;
+        float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+        if (pos < limit) {
+            const __nv_bfloat16* src = base + static_cast<size_t>(pos) * ld;
+            const uint2 ua = *reinterpret_cast<const uint2*>(src + 4 * j);
+            const uint2 ub = *reinterpret_cast<const uint2*>(src + HALF + 4 * j);
+            const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ua);
+            const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&ub);
+            float2 f;
+            f = __bfloat1622float2(ha[0]); a[0] = f.x; a[1] = f.y;
+            f = __bfloat1622float2(ha[1]); a[2] = f.x; a[3] = f.y;
+            f = __bfloat1622float2(hb[0]); b[0] = f.x; b[1] = f.y;
+            f = __bfloat1622float2(hb[1]); b[2] = f.x; b[3] = f.y;
+            if (cosv) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float c = cosv[static_cast<size_t>(pos) * HALF + 4 * j + t];
+                    const float s = sinv[static_cast<size_t>(pos) * HALF + 4 * j + t];
+                    const float x = a[t], y = b[t];
+                    a[t] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+                    b[t] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
+                }
+            }
+        }
+        *reinterpret_cast<uint2*>(dst + r * LDS + 4 * j) = make_uint2(pack_bf16(a[0], a[1]), pack_bf16(a[2], a[3]));
+        *reinterpret_cast<uint2*>(dst + r * LDS + HALF + 4 * j) = make_uint2(pack_bf16(b[0], b[1]), pack_bf16(b[2], b[3]));
+    }
+}
+
+// Q fragments (A operand) of the warp's 16 rows from a [64][LDS] smem tile.
+template <int KS>
+DEVI void load_a_frags(const __nv_bfloat16* tile, int warp, int lane, uint32_t (&fa)[KS][4]) {
+    const int r = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+        ldsm_x4(smem_u32(tile + r * LDS + ks * 16 + 8 * (lane >> 4)), fa[ks][0], fa[ks][1], fa[ks][2], fa[ks][3]);
+}
+
+// acc[16 rows x 64 cols] += A(16 x HD frags) · Bᵀ where B rows are the 64 smem rows (B[k=d][n=row] = tile[row][d]).
+template <int KS>
+DEVI void mma_abt(float (&acc)[8][4], const uint32_t (&fa)[KS][4], const __nv_bfloat16* tile, int lane) {
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {
+            const int row = jp * 16 + (lane & 7) + 8 * (lane >> 4);
+            const int col = ks * 16 + 8 * ((lane >> 3) & 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(tile + row * LDS + col), b0, b1, b2, b3);
+            mma_bf16(acc[2 * jp], fa[ks][0], fa[ks][1], fa[ks][2], fa[ks][3], b0, b1);
+            mma_bf16(acc[2 * jp + 1], fa[ks][0], fa[ks][1], fa[ks][2], fa[ks][3], b2, b3);
+        }
+    }
+}
+
+// out[16 x HD] += P(16 x 64, as packed A frags from C frags) · tile(64 rows x HD)   (B[k=row][n=d] = tile[row][d])
+template <int NT>
+DEVI void mma_pv(float (&out)[NT][4], const uint32_t (&pa)[8][2], const __nv_bfloat16* tile, int lane) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int dp = 0; dp < NT / 2; ++dp) {
+            const int row = kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+            const int col = dp * 16 + 8 * (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(smem_u32(tile + row * LDS + col), b0, b1, b2, b3);
+            mma_bf16(out[2 * dp], pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1], b0, b1);
+            mma_bf16(out[2 * dp + 1], pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1], b2, b3);
+        }
+    }
+}
+
+DEVI bool visible(bool global, int W, int q, int k, int L) { return k < L && q < L && (global || (k >= q - W && k <= q + W)); }
+
+// ------------------------------------------------------------------------------------------------ forward
+template <int HD>
+__global__ void __launch_bounds__(128) fwd_kernel(Args a) {
+    constexpr int KS = HD / 16, NT = HD / 8;
+    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
+    const int tile = blockIdx.x;
+    if (tile >= *a.n_tiles) return;
+    const int head = blockIdx.y, item = a.tile_item[tile], q0 = a.tile_p0[tile];
+    const int seg0 = a.seg_start[item], L = a.seg_len[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    const bool global = a.window < 0;
+    const int W = a.window;
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD>(Qs, qb, a.ld, q0, L, a.cosv, a.sinv);
+    __syncthreads();
+    uint32_t fq[KS][4];
+    load_a_frags<KS>(Qs, warp, lane, fq);
+    float o[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
+    for (int k0 = kb; k0 < ke; k0 += T64) {
+        __syncthreads();
+        load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
+        load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
+        __syncthreads();
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        mma_abt<KS>(s, fq, Ks, lane);
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int kp = k0 + 8 * j + 2 * t4 + (e & 1);
+                const float v = visible(global, W, qp[e >> 1], kp, ke) ? __fmul_rn(s[j][e], a.scale) : -INFINITY;
+                s[j][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+        float alpha[2], msc[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+            const float mn = fmaxf(m_run[h], mx[h]);
+            alpha[h] = m_run[h] == -INFINITY ? 0.f : exp2f((m_run[h] - mn) * LOG2E);
+            msc[h] = mn * LOG2E;
+            m_run[h] = mn;
+        }
+        float rs[2] = {0.f, 0.f};
+        uint32_t pa[8][2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1;
+                const float pe = s[j][e] == -INFINITY ? 0.f : exp2f(fmaf(s[j][e], LOG2E, -msc[h]));
+                rs[h] += pe;   // the normaliser counts every probability, dropped or not
+                const int kp = k0 + 8 * j + 2 * t4 + (e & 1);
+                pv[e] = pe == 0.f ? 0.f : pe * drop_mult(a, head, seg0 + qp[h], kp);
+            }
+            pa[j][0] = pack_bf16(pv[0], pv[1]);
+            pa[j][1] = pack_bf16(pv[2], pv[3]);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+            rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+            l_run[h] = l_run[h] * alpha[h] + rs[h];
+        }
+#pragma unroll
+        for (int j = 0; j < NT; ++j) { o[j][0] *= alpha[0]; o[j][1] *= alpha[0]; o[j][2] *= alpha[1]; o[j][3] *= alpha[1]; }
+        mma_pv<NT>(o, pa, Vs, lane);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int q = qp[h];
+        if (q >= L) continue;
+        const float inv = l_run[h] > 0.f ? 1.0f / l_run[h] : 0.f;
+        __nv_bfloat16* orow = a.out + static_cast<size_t>(seg0 + q) * a.ldo + head * HD;
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+            *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t4) = pack_bf16(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+        if (t4 == 0) a.lse[static_cast<size_t>(seg0 + q) * a.heads + head] = m_run[h] + logf(l_run[h]);
+    }
+}
+
+// D_i = Σ_d dO · O per (token, head), fp32.
+__global__ void bwd_dot_kernel(Args a, int T) {
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (gw >= T * a.heads) return;
+    const int t = gw / a.heads, h = gw % a.heads;
+    const int hd = a.hidden / a.heads;
+    float s = 0.f;
+    for (int d = lane; d < hd; d += 32) {
+        s += __bfloat162float(a.dout[static_cast<size_t>(t) * a.ldo + h * hd + d]) *
+             __bfloat162float(a.out[static_cast<size_t>(t) * a.ldo + h * hd + d]);
+    }
+    s = warp_sum(s);
+    if (lane == 0) a.dsum[static_cast<size_t>(t) * a.heads + h] = s;
+}
+
+// Writes 16 rows x HD of a warp's fp32 accumulator as bf16 into a [T, ld] slice, rotating back by -θ when given.
+template <int NT>
+DEVI void store_rows(float (&acc)[NT][4], __nv_bfloat16* base, int ld, int seg0, int p0, int warp, int lane, int L,
+                     const float* cosv, const float* sinv) {
+    constexpr int HD = NT * 8, HALF = HD / 2;
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int pos = p0 + warp * 16 + g + 8 * h;
+        if (cosv) {
+            // pairs (i, i + HALF) live in n-tiles j and j + NT/2 of the same thread
+#pragma unroll
+            for (int j = 0; j < NT / 2; ++j)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int i = 8 * j + 2 * t4 + e;
+                    const float c = pos < L ? cosv[static_cast<size_t>(pos) * HALF + i] : 0.f;
+                    const float s = pos < L ? sinv[static_cast<size_t>(pos) * HALF + i] : 0.f;
+                    const float x = acc[j][2 * h + e], y = acc[j + NT / 2][2 * h + e];
+                    acc[j][2 * h + e] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+                    acc[j + NT / 2][2 * h + e] = __fsub_rn(__fmul_rn(y, c), __fmul_rn(x, s));
+                }
+        }
+        if (pos < L) {
+            __nv_bfloat16* row = base + static_cast<size_t>(seg0 + pos) * ld;
+#pragma unroll
+            for (int j = 0; j < NT; ++j)
+                *reinterpret_cast<uint32_t*>(row + 8 * j + 2 * t4) = pack_bf16(acc[j][2 * h], acc[j][2 * h + 1]);
+        }
+    }
+}
+
+// dQ for one 64-query tile of one head.
+template <int HD>
+__global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
+    constexpr int KS = HD / 16, NT = HD / 8;
+    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 dOs[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
+    const int tile = blockIdx.x;
+    if (tile >= *a.n_tiles) return;
+    const int head = blockIdx.y, item = a.tile_item[tile], q0 = a.tile_p0[tile];
+    const int seg0 = a.seg_start[item], L = a.seg_len[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    const bool global = a.window < 0;
+    const int W = a.window;
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD>(Qs, qb, a.ld, q0, L, a.cosv, a.sinv);
+    load_rows<HD>(dOs, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, L, nullptr, nullptr);
+    __syncthreads();
+    uint32_t fq[KS][4], fdo[KS][4];
+    load_a_frags<KS>(Qs, warp, lane, fq);
+    load_a_frags<KS>(dOs, warp, lane, fdo);
+    const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
+    float lse[2], dd[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const bool ok = qp[h] < L;
+        lse[h] = ok ? a.lse[static_cast<size_t>(seg0 + qp[h]) * a.heads + head] : 0.f;
+        dd[h] = ok ? a.dsum[static_cast<size_t>(seg0 + qp[h]) * a.heads + head] : 0.f;
+    }
+    float dq[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
+    for (int k0 = kb; k0 < ke; k0 += T64) {
+        __syncthreads();
+        load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
+        load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
+        __syncthreads();
+        float s[8][4], dp[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s[j][e] = dp[j][e] = 0.f;
+        mma_abt<KS>(s, fq, Ks, lane);
+        mma_abt<KS>(dp, fdo, Vs, lane);
+        uint32_t pa[8][2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float ds[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1;
+                const int kp = k0 + 8 * j + 2 * t4 + (e & 1);
+                float p = 0.f;
+                if (visible(global, W, qp[h], kp, ke)) p = __expf(__fmul_rn(s[j][e], a.scale) - lse[h]);
+                const float dpm = dp[j][e] * drop_mult(a, head, seg0 + qp[h], kp);
+                ds[e] = a.scale * p * (dpm - dd[h]);
+            }
+            pa[j][0] = pack_bf16(ds[0], ds[1]);
+            pa[j][1] = pack_bf16(ds[2], ds[3]);
+        }
+        mma_pv<NT>(dq, pa, Ks, lane);
+    }
+    store_rows<NT>(dq, a.dqkv + head * HD, a.lddq, seg0, q0, warp, lane, L, a.cosv, a.sinv);
+}
+
+// dK and dV for one 64-key tile of one head.
+template <int HD>
+__global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
+    constexpr int KS = HD / 16, NT = HD / 8;
+    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
+    __shared__ __align__(16) __nv_bfloat16 dOs[T64 * LDS];
+    __shared__ float lse_s[T64], dd_s[T64];
+    const int tile = blockIdx.x;
+    if (tile >= *a.n_tiles) return;
+    const int head = blockIdx.y, item = a.tile_item[tile], k0 = a.tile_p0[tile];
+    const int seg0 = a.seg_start[item], L = a.seg_len[item];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    const bool global = a.window < 0;
+    const int W = a.window;
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, L, a.cosv, a.sinv);
+    load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, L, nullptr, nullptr);
+    __syncthreads();
+    uint32_t fk[KS][4], fv[KS][4];
+    load_a_frags<KS>(Ks, warp, lane, fk);
+    load_a_frags<KS>(Vs, warp, lane, fv);
+    const int kp[2] = {k0 + warp * 16 + g, k0 + warp * 16 + g + 8};
+    float dk[NT][4], dv[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dk[j][e] = dv[j][e] = 0.f;
+    const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + T64 + W);
+    for (int q0 = qb0; q0 < qe; q0 += T64) {
+        __syncthreads();
+        load_rows<HD>(Qs, qb, a.ld, q0, qe, a.cosv, a.sinv);
+        load_rows<HD>(dOs, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, qe, nullptr, nullptr);
+        for (int r = threadIdx.x; r < T64; r += blockDim.x) {
+            const int q = q0 + r;
+            lse_s[r] = q < qe ? a.lse[static_cast<size_t>(seg0 + q) * a.heads + head] : 0.f;
+            dd_s[r] = q < qe ? a.dsum[static_cast<size_t>(seg0 + q) * a.heads + head] : 0.f;
+        }
+        __syncthreads();
+        // transposed scores: rows = this warp's 16 keys, columns = 64 queries
+        float st[8][4], dpt[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) st[j][e] = dpt[j][e] = 0.f;
+        mma_abt<KS>(st, fk, Qs, lane);
+        mma_abt<KS>(dpt, fv, dOs, lane);
+        uint32_t pm[8][2], dsa[8][2];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float pd[4], ds[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1;
+                const int qr = 8 * j + 2 * t4 + (e & 1);
+                const int q = q0 + qr;
+                float p = 0.f;
+                if (visible(global, W, q, kp[h], qe)) p = __expf(__fmul_rn(st[j][e], a.scale) - lse_s[qr]);
+                const float m = drop_mult(a, head, seg0 + q, kp[h]);
+                pd[e] = p * m;
+                ds[e] = a.scale * p * (dpt[j][e] * m - dd_s[qr]);
+            }
+            pm[j][0] = pack_bf16(pd[0], pd[1]);
+            pm[j][1] = pack_bf16(pd[2], pd[3]);
+            dsa[j][0] = pack_bf16(ds[0], ds[1]);
+            dsa[j][1] = pack_bf16(ds[2], ds[3]);
+        }
+        mma_pv<NT>(dv, pm, dOs, lane);
+        mma_pv<NT>(dk, dsa, Qs, lane);
+    }
+    store_rows<NT>(dk, a.dqkv + a.hidden + head * HD, a.lddq, seg0, k0, warp, lane, L, a.cosv, a.sinv);
+    store_rows<NT>(dv, a.dqkv + 2 * a.hidden + head * HD, a.lddq, seg0, k0, warp, lane, L, nullptr, nullptr);
+}
+
+}  // namespace fa
+
+int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    if (max_tiles <= 0) return OK;
+    const int hd = a.hidden / a.heads;
+    dim3 grid(max_tiles, a.heads);
+    if (hd == 64) fa::fwd_kernel<64><<<grid, 128, 0, s>>>(a);
+    else if (hd == 32) fa::fwd_kernel<32><<<grid, 128, 0, s>>>(a);
+    else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
+    if (max_tiles <= 0 || T <= 0) return OK;
+    const int hd = a.hidden / a.heads;
+    const long long warps = static_cast<long long>(T) * a.heads;
+    fa::bwd_dot_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(a, T);
+    count_launch();
+    dim3 grid(max_tiles, a.heads);
+    if (hd == 64) { fa::bwd_dq_kernel<64><<<grid, 128, 0, s>>>(a); fa::bwd_dkdv_kernel<64><<<grid, 128, 0, s>>>(a); }
+    else if (hd == 32) { fa::bwd_dq_kernel<32><<<grid, 128, 0, s>>>(a); fa::bwd_dkdv_kernel<32><<<grid, 128, 0, s>>>(a); }
+    else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
+    count_launch(2);
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+}  // namespace laya

@@ -25,3 +25,85 @@ struct Args {
 int gemm(const Args& a, cudaStream_t stream);
 }  // namespace bf
 }  // namespace laya
+
+namespace laya {
+
+// ---- flash.cu
+namespace fa {
+struct Args {
+    const __nv_bfloat16* qkv; int ld; int hidden; int heads;        // [T, ld] with q | k | v at 0, hidden, 2·hidden
+    const int32_t* seg_start; const int32_t* seg_len;
+    const int32_t* tile_item; const int32_t* tile_p0; const int32_t* n_tiles;   // 64-row tiles of every segment
+    int window;                                                      // < 0: global
+    float scale;                                                     // 1/sqrt(head_dim)
+    const float* cosv; const float* sinv;                            // [positions, head_dim/2] or null
+    float dropout; float keep; uint64_t seed;                        // dropout on the probabilities
+    __nv_bfloat16* out; int ldo; float* lse;                         // context [T, ldo] bf16, row log-sum-exp [T, heads]
+    const __nv_bfloat16* dout; float* dsum;                          // backward: d context [T, ldo], Σ dO·O [T, heads]
+    __nv_bfloat16* dqkv; int lddq;                                   // backward output [T, lddq]
+};
+}  // namespace fa
+int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
+int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s);
+
+// ---- train_kernels.cu
+namespace tr {
+struct Mask { float p; float keep; uint64_t seed; };   // inverted dropout by the counter hash; p = 0: identity
+struct LnFwd {
+    int rows, n;
+    const float* x; const int32_t* gather;                  // row r reads x[gather ? gather[r] : r]
+    const int32_t* ids; const float* table; int vocab;      // or an embedding gather
+    const float* w; const float* b; float eps;
+    int identity;                                           // layer 0: y16 = bf16(x)
+    __nv_bfloat16* y16; float* y32;                         // outputs (either may be null)
+    float* mean; float* rstd;
+    const float* temb; const int32_t* tok_item; const int32_t* qtype;   // y32 += type embedding
+    int* err;
+};
+struct LnBwd {
+    int rows, n;
+    const float* x; const int32_t* gather;                  // forward input rows
+    const float* mean; const float* rstd; const float* w;
+    const float* dy;                                        // [rows, n]
+    float* dx; int accumulate; const int32_t* scatter;      // dx rows (+= when accumulate, atomic += when scatter)
+    float* dw; float* db;                                   // parameter gradients (+=), may be null
+};
+struct AdamArgs {
+    size_t n;
+    float* param; const float* grad; float* m; float* v; __nv_bfloat16* shadow;
+    float decay, b1, b2, step_size, sqrt_c2, eps;
+    const double* gscale;                                   // clip factor (device), may be null
+};
+struct RlcdArgs {
+    int n_items, groups, M;                                 // items, noise groups, options (markers)
+    const int32_t* mk_start; const int32_t* mk_count; const int32_t* qtype;
+    const float* logits; const float* targets; const double* draws;   // draws [groups][M] standard normal
+    double sigma, scale, w_sph, w_rps, w_ce;
+    double* scratch;                                        // rlcd_scratch_bytes()
+    float* dlogits;                                         // [M]
+    double* result;                                         // loss, policy loss, cross-entropy, mean reward
+};
+}  // namespace tr
+size_t rlcd_scratch_bytes(int groups, int n_items, int M);
+int rlcd(const tr::RlcdArgs& a, cudaStream_t s);
+int ln_fwd(const tr::LnFwd& a, cudaStream_t s);
+int ln_bwd(const tr::LnBwd& a, cudaStream_t s);
+int geglu_fwd(const __nv_bfloat16* wide, int rows, int I, __nv_bfloat16* act, cudaStream_t s);
+int geglu_bwd(const __nv_bfloat16* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s);
+int add_masked(const float* a, const float* b, float* y, size_t n, tr::Mask m, cudaStream_t s);
+int relu_mask(const __nv_bfloat16* pre, __nv_bfloat16* act, size_t n, tr::Mask m, cudaStream_t s);
+int relu_mask_bwd(const float* d, const __nv_bfloat16* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s);
+int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s);
+int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
+int scatter_rows(const float* d, const int32_t* ids, int rows, int n, float* grad, cudaStream_t s);
+int colsum_f32(const float* d, int rows, int n, float* db, cudaStream_t s);
+int colsum_bf16(const __nv_bfloat16* d, int rows, int n, float* db, cudaStream_t s);
+int type_grad(const float* d, const int32_t* tok_item, const int32_t* qtype, int rows, int n, float* grad, cudaStream_t s);
+int scorer_out(const float* pre, int M, int n, const float* w2, const float* b2, float* logits, cudaStream_t s);
+int scorer_bwd(const float* pre, const float* dlogit, int M, int n, const float* w2, __nv_bfloat16* dpre, float* db1,
+               float* dw2, float* db2, cudaStream_t s);
+int sumsq(const float* g, size_t n, double* out, cudaStream_t s);
+int clip_scale(const double* sumsq, double max_norm, int world, double* scale, double* norm_out, cudaStream_t s);
+int adamw(const tr::AdamArgs& a, cudaStream_t s);
+
+}  // namespace laya

@@ -1,0 +1,576 @@
+// train_kernels.cu — the memory-bound kernels of the training step.
+//
+//   ln_fwd / ln_bwd        Ops.LayerNorm / Ops.LayerNormBackward (Laya.Training/Ops.cs:103-186); the forward keeps the
+//                          row mean and 1/std for the backward (the reference recomputes them in double).
+//   geglu_fwd / geglu_bwd  the GeGLU of EncoderLayerForward and its backward (TrainableDecisionModel.cs:391-398, 564-579;
+//                          Ops.GeluBackward, Ops.cs:194-218), exact-erf GELU.
+//   masked ops             ReLU, inverted dropout (Ops.Dropout, Ops.cs:244-258, the reference's counter hash) and the
+//                          residual adds of HeadLayerForward/Backward (TrainableDecisionModel.cs:428-468, 605-640).
+//   colsum                 bias gradients db += Σ_rows dy (Ops.LinearBackward, Ops.cs:64-68).
+//   scatters               embedding-row and type-embedding gradients (TrainableDecisionModel.cs:513-521, 538-548).
+//   scorer                 the option scorer's Linear(h, 1) and its backward (TrainableDecisionModel.cs:313-331, 484-504).
+//   adamw / sumsq          AdamW.Step and Gradients.ClipByGlobalNorm (AdamW.cs:29-130) over flat parameter buffers,
+//                          refreshing the bf16 copies the products read.
+// Every kernel moves each byte once with 16-byte accesses where the layout allows; a warp owns a row for row-wise ops.
+#include "common.cuh"
+#include "internal.h"
+#include "train.h"
+
+namespace laya {
+namespace tr {
+
+DEVI float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Ops.Uniform on the device (same mixing as fa::dropout_uniform).
+DEVI float uniform_hash(uint64_t seed, uint64_t index) {
+    uint64_t z = seed + (index + 1ull) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f);
+}
+DEVI float dmask(const Mask& m, size_t i) {
+    if (m.p <= 0.0f) return 1.0f;
+    return uniform_hash(m.seed, static_cast<uint64_t>(i)) < m.p ? 0.0f : m.keep;
+}
+
+// The derivative of exact GELU, Φ(u) + u·φ(u) (Ops.GeluBackward).
+DEVI float gelu_grad(float x) {
+    const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+    const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
+    return cdf + x * pdf;
+}
+DEVI float gelu_exact(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// ------------------------------------------------------------------------------------------------ LayerNorm
+// One warp per row; n <= 32·NPL.
+template <int NPL>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(LnFwd a) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row >= a.rows) return;
+    const int n = a.n;
+    const float* src;
+    if (a.table) {
+        int id = a.ids[row];
+        if (id < 0 || id >= a.vocab) { if (lane == 0) atomicExch(a.err, LAYA_DEV_ERR_BOUNDS); id = 0; }
+        src = a.table + static_cast<size_t>(id) * n;
+    } else {
+        src = a.x + static_cast<size_t>(a.gather ? a.gather[row] : row) * n;
+    }
+    float v[NPL];
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) { const int c = lane + 32 * i; v[i] = c < n ? src[c] : 0.f; }
+    if (a.identity) {
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < n) a.y16[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(v[i]);
+        }
+        return;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) s += v[i];
+    const float mean = warp_sum(s) / n;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) { const int c = lane + 32 * i; const float d = c < n ? v[i] - mean : 0.f; q += d * d; }
+    const float rstd = rsqrtf(warp_sum(q) / n + a.eps);
+    if (lane == 0) { a.mean[row] = mean; a.rstd[row] = rstd; }
+    const float* te = a.temb ? a.temb + static_cast<size_t>(a.qtype[a.tok_item[row]]) * n : nullptr;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+        const int c = lane + 32 * i;
+        if (c >= n) continue;
+        float y = (v[i] - mean) * rstd * a.w[c];
+        if (a.b) y += a.b[c];
+        if (a.y16) a.y16[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(y);
+        if (a.y32) a.y32[static_cast<size_t>(row) * n + c] = te ? y + te[c] : y;
+    }
+}
+
+// dx (+)= rstd·(g − mean(g) − x̂·mean(g·x̂)), g = dy·γ; dγ += Σ dy·x̂; dβ += Σ dy.  A CTA of 8 warps takes
+// LN_ROWS rows, each lane owns columns lane + 32i, and the CTA adds its column partials to dγ/dβ once.
+constexpr int LN_ROWS = 64;
+template <int NPL>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(LnBwd a) {
+    __shared__ float red[8][32 * NPL];   // column partials of the 8 warps, for dγ then dβ
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = a.n;
+    float pw[NPL], pb[NPL];
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) pw[i] = pb[i] = 0.f;
+    const int r0 = blockIdx.x * LN_ROWS;
+    for (int rr = warp; rr < LN_ROWS; rr += 8) {
+        const int r = r0 + rr;
+        if (r >= a.rows) break;
+        const int xr = a.gather ? a.gather[r] : r;
+        const float mean = a.mean[r], rstd = a.rstd[r];
+        float xh[NPL], g[NPL], dy[NPL];
+        float sg = 0.f, sgx = 0.f;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < n) {
+                const float x = a.x[static_cast<size_t>(xr) * n + c];
+                dy[i] = a.dy[static_cast<size_t>(r) * n + c];
+                xh[i] = (x - mean) * rstd;
+                g[i] = dy[i] * a.w[c];
+            } else {
+                dy[i] = xh[i] = g[i] = 0.f;
+            }
+            sg += g[i];
+            sgx += g[i] * xh[i];
+            pw[i] += dy[i] * xh[i];
+            pb[i] += dy[i];
+        }
+        const float mg = warp_sum(sg) / n, mgx = warp_sum(sgx) / n;
+        if (a.dx) {
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c >= n) continue;
+                const float d = rstd * (g[i] - mg - xh[i] * mgx);
+                float* dst = a.dx + static_cast<size_t>(a.scatter ? a.scatter[r] : r) * n + c;
+                if (a.scatter) atomicAdd(dst, d);
+                else *dst = a.accumulate ? *dst + d : d;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) red[warp][lane + 32 * i] = pw[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        float sw = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sw += red[w][c];
+        if (a.dw) atomicAdd(a.dw + c, sw);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) red[warp][lane + 32 * i] = pb[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        float sb = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sb += red[w][c];
+        if (a.db) atomicAdd(a.db + c, sb);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ GeGLU
+__global__ void geglu_fwd_kernel(const __nv_bfloat16* __restrict__ wide, int rows, int I, __nv_bfloat16* __restrict__ act) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(rows) * I) return;
+    const size_t r = i / I, c = i % I;
+    const float u = bf(wide[r * 2 * I + c]), g = bf(wide[r * 2 * I + I + c]);
+    act[i] = __float2bfloat16_rn(gelu_exact(u) * g);
+}
+// dgate = dy·gelu(u); du = dy·gate·gelu'(u)
+__global__ void geglu_bwd_kernel(const __nv_bfloat16* __restrict__ wide, const float* __restrict__ dact, int rows, int I,
+                                 __nv_bfloat16* __restrict__ dwide) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(rows) * I) return;
+    const size_t r = i / I, c = i % I;
+    const float u = bf(wide[r * 2 * I + c]), g = bf(wide[r * 2 * I + I + c]);
+    const float dy = dact[i];
+    dwide[r * 2 * I + I + c] = __float2bfloat16_rn(dy * gelu_exact(u));
+    dwide[r * 2 * I + c] = __float2bfloat16_rn(dy * g * gelu_grad(u));
+}
+
+// ------------------------------------------------------------------------------------------------ masked elementwise
+// y32 = a32 + mask(b32)   (a residual branch with dropout, HeadLayerForward)
+__global__ void add_masked_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, size_t n,
+                                  Mask m) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = a[i] + b[i] * dmask(m, i);
+}
+// act16 = bf16(mask(relu(pre16)))   (linear1 → ReLU → dropout, HeadLayerForward)
+__global__ void relu_mask_kernel(const __nv_bfloat16* __restrict__ pre, __nv_bfloat16* __restrict__ act, size_t n, Mask m) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    act[i] = __float2bfloat16_rn(fmaxf(bf(pre[i]), 0.f) * dmask(m, i));
+}
+// dx16 = bf16(mask(d32) · [pre > 0])
+__global__ void relu_mask_bwd_kernel(const float* __restrict__ d, const __nv_bfloat16* __restrict__ pre,
+                                     __nv_bfloat16* __restrict__ dx, size_t n, Mask m) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    dx[i] = __float2bfloat16_rn(bf(pre[i]) > 0.f ? d[i] * dmask(m, i) : 0.f);
+}
+// y16 = bf16(mask(x32))
+__global__ void cast_mask_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n, Mask m) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2bfloat16_rn(x[i] * dmask(m, i));
+}
+
+// db[c] += Σ_r d[r, c]  (d fp32 or bf16); a CTA takes 64 rows × 256 columns
+template <typename T>
+__global__ void colsum_kernel(const T* __restrict__ d, int rows, int n, float* __restrict__ db) {
+    const int c = blockIdx.y * blockDim.x + threadIdx.x;
+    if (c >= n) return;
+    const int r0 = blockIdx.x * 64, r1 = min(rows, r0 + 64);
+    float s = 0.f;
+    for (int r = r0; r < r1; ++r) {
+        if constexpr (sizeof(T) == 4) s += d[static_cast<size_t>(r) * n + c];
+        else s += bf(d[static_cast<size_t>(r) * n + c]);
+    }
+    atomicAdd(db + c, s);
+}
+
+// grad[ids[t]] += d[t]   (embedding rows)
+__global__ void scatter_rows_kernel(const float* __restrict__ d, const int32_t* __restrict__ ids, int rows, int n,
+                                    float* __restrict__ grad) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(rows) * n) return;
+    const size_t r = i / n, c = i % n;
+    atomicAdd(grad + static_cast<size_t>(ids[r]) * n + c, d[i]);
+}
+// gtype[qtype[item(t)]] += d[t]: 3 type rows accumulated in shared memory per 64 rows
+__global__ void type_grad_kernel(const float* __restrict__ d, const int32_t* __restrict__ tok_item,
+                                 const int32_t* __restrict__ qtype, int rows, int n, float* __restrict__ grad) {
+    extern __shared__ float acc[];   // [3][n]
+    for (int i = threadIdx.x; i < 3 * n; i += blockDim.x) acc[i] = 0.f;
+    __syncthreads();
+    const int r0 = blockIdx.x * 64, r1 = min(rows, r0 + 64);
+    for (int r = r0; r < r1; ++r) {
+        const int t = qtype[tok_item[r]];
+        for (int c = threadIdx.x; c < n; c += blockDim.x) acc[t * n + c] += d[static_cast<size_t>(r) * n + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 3 * n; i += blockDim.x)
+        if (acc[i] != 0.f) atomicAdd(grad + i, acc[i]);
+}
+
+// ------------------------------------------------------------------------------------------------ scorer
+// pre32 [M, n] (Linear1 + bias) → act = gelu(pre) (bf16 for the dW product of Linear2 is not needed: Linear2 is a
+// dot); logits[m] = Σ act·w2 + b2.  One warp per marker.
+__global__ void scorer_out_kernel(const float* __restrict__ pre, int M, int n, const float* __restrict__ w2,
+                                  const float* __restrict__ b2, float* __restrict__ logits) {
+    const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (m >= M) return;
+    float s = 0.f;
+    for (int c = lane; c < n; c += 32) s += gelu_exact(pre[static_cast<size_t>(m) * n + c]) * w2[c];
+    s = warp_sum(s);
+    if (lane == 0) logits[m] = s + b2[0];
+}
+// dpre[m, c] = dlogit[m] · w2[c] · gelu'(pre[m, c]) → bf16 for the dX / dW products, and in fp32 summed into db1;
+// dw2[c] += Σ_m dlogit[m] · gelu(pre[m, c]); db2 += Σ_m dlogit[m]   (Ops.LinearBackward + Ops.GeluBackward).
+__global__ void scorer_bwd_kernel(const float* __restrict__ pre, const float* __restrict__ dlogit, int M, int n,
+                                  const float* __restrict__ w2, __nv_bfloat16* __restrict__ dpre, float* __restrict__ db1,
+                                  float* __restrict__ dw2, float* __restrict__ db2) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < n) {
+        float acc = 0.f, acc1 = 0.f;
+        for (int m = 0; m < M; ++m) {
+            const float p = pre[static_cast<size_t>(m) * n + c];
+            acc += dlogit[m] * gelu_exact(p);
+            const float d = dlogit[m] * w2[c] * gelu_grad(p);
+            acc1 += d;
+            dpre[static_cast<size_t>(m) * n + c] = __float2bfloat16_rn(d);
+        }
+        if (dw2) atomicAdd(dw2 + c, acc);
+        if (db1) atomicAdd(db1 + c, acc1);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && db2) {
+        float s = 0.f;
+        for (int m = 0; m < M; ++m) s += dlogit[m];
+        atomicAdd(db2, s);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ optimizer
+// Σ g² over [0, n) in double, per CTA partials reduced with atomics (Gradients.ClipByGlobalNorm sums in double).
+__global__ void sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ out) {
+    double s = 0.0;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        s += static_cast<double>(g[i]) * g[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __shared__ double ws[32];
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += ws[w];
+        atomicAdd(out, t);
+    }
+}
+
+// AdamW.Step for one contiguous parameter range: g = grad · gscale (the clipping factor and the 1/world average folded
+// in), decoupled decay, bias-corrected moments, then the bf16 shadow the products read.
+__global__ void adamw_kernel(AdamArgs a) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= a.n) return;
+    const float gsc = a.gscale ? static_cast<float>(*a.gscale) : 1.0f;
+    const float g = __fmul_rn(a.grad[i], gsc);
+    float p = __fmul_rn(a.param[i], a.decay);
+    const float m = __fadd_rn(__fmul_rn(a.b1, a.m[i]), __fmul_rn(1.0f - a.b1, g));
+    const float v = __fadd_rn(__fmul_rn(a.b2, a.v[i]), __fmul_rn(__fmul_rn(1.0f - a.b2, g), g));
+    const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), a.sqrt_c2), a.eps);
+    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(a.step_size, m), den));
+    a.param[i] = p;
+    a.m[i] = m;
+    a.v[i] = v;
+    if (a.shadow) a.shadow[i] = __float2bfloat16_rn(p);
+}
+
+// Gradients.ClipByGlobalNorm on the rank average g_sum / world: norm = sqrt(Σ g_sum²) / world,
+// coef = max_norm / (norm + 1e-6); the factor applied to g_sum is min(1, coef) / world (world = 1: the reference's).
+__global__ void clip_scale_kernel(const double* sumsq, double max_norm, int world, double* scale, double* norm_out) {
+    const double norm = sqrt(*sumsq) / world;
+    const double coef = max_norm / (norm + 1e-6);
+    *scale = (coef < 1.0 ? coef : 1.0) / world;
+    if (norm_out) *norm_out = norm;
+}
+
+// ------------------------------------------------------------------------------------------------ objective
+// RlcdObjective.Compute with supplied standard-normal draws (RlcdObjective.cs:57-155) and Calibration.ProperReward
+// (Calibration.cs:76-119, every option unmasked), one CTA: (group, item) samples in parallel, then the advantage
+// normalisation and every running sum on one thread in the reference's order, so the result does not depend on the
+// launch shape.  Softmax is fp32 as SimdOps.Softmax (SimdOps.cs:275-291); everything else fp64.
+DEVI void softmax_f32(float* v, int k) {
+    float mx = -INFINITY;
+    for (int o = 0; o < k; ++o) mx = fmaxf(mx, v[o]);
+    if (mx == -INFINITY) { for (int o = 0; o < k; ++o) v[o] = 0.f; return; }
+    float total = 0.f;
+    for (int o = 0; o < k; ++o) { const float e = expf(v[o] - mx); v[o] = e; total = __fadd_rn(total, e); }
+    const float sc = total > 0.f ? 1.0f / total : 0.f;
+    for (int o = 0; o < k; ++o) v[o] = __fmul_rn(v[o], sc);
+}
+
+__global__ void __launch_bounds__(256) rlcd_kernel(RlcdArgs a) {
+    const int n = a.n_items, G = a.groups, M = a.M;
+    double* eps = a.scratch;                  // [G][M]
+    double* reward = eps + static_cast<size_t>(G) * M;   // [G][n]
+    double* adv = reward + static_cast<size_t>(G) * n;   // [G][n]
+    float* q = reinterpret_cast<float*>(adv + static_cast<size_t>(G) * n);   // [G][M] perturbed, then [M] clean
+    for (int p = threadIdx.x; p < G * n; p += blockDim.x) {
+        const int g = p / n, i = p % n;
+        const int k = a.mk_count[i], o0 = a.mk_start[i];
+        double* e = eps + static_cast<size_t>(g) * M + o0;
+        float* qq = q + static_cast<size_t>(g) * M + o0;
+        double mean = 0.0;
+        for (int o = 0; o < k; ++o) { e[o] = a.draws[static_cast<size_t>(g) * M + o0 + o] * a.sigma; mean += e[o]; }
+        mean /= k;
+        for (int o = 0; o < k; ++o) e[o] -= mean;
+        for (int o = 0; o < k; ++o) qq[o] = __double2float_rn(static_cast<double>(a.logits[o0 + o]) + e[o]);
+        softmax_f32(qq, k);
+        const float* t = a.targets + o0;
+        double logs = 0.0, dot = 0.0, nsq = 0.0;
+        for (int o = 0; o < k; ++o) {
+            const double qo = qq[o];
+            logs += t[o] * fmax(log(fmax(qo, 1e-12)), -9.21);
+            dot += t[o] * qo;
+            nsq += qo * qo;
+        }
+        double r = logs + a.w_sph * (dot / fmax(sqrt(nsq), 1e-9));
+        if (a.qtype[i] == 1) {   // QuestionType.Score: ranked probability score
+            const int kk = k > 2 ? k : 2;
+            double cq = 0.0, ct = 0.0, rps = 0.0;
+            for (int o = 0; o < k; ++o) { cq += qq[o]; ct += t[o]; rps += (cq - ct) * (cq - ct); }
+            r -= a.w_rps * rps / (kk - 1);
+        }
+        reward[static_cast<size_t>(g) * n + i] = r;
+    }
+    __syncthreads();
+    const int count = G * n;
+    if (threadIdx.x == 0) {
+        double total = 0.0;
+        for (int i = 0; i < n; ++i) {
+            double mean = 0.0;
+            for (int g = 0; g < G; ++g) mean += reward[static_cast<size_t>(g) * n + i];
+            mean /= G;
+            for (int g = 0; g < G; ++g) {
+                adv[static_cast<size_t>(g) * n + i] = reward[static_cast<size_t>(g) * n + i] - mean;
+                total += adv[static_cast<size_t>(g) * n + i];
+            }
+        }
+        const double gm = total / count;
+        double var = 0.0;
+        for (int g = 0; g < G; ++g)
+            for (int i = 0; i < n; ++i) {
+                const double d = adv[static_cast<size_t>(g) * n + i] - gm;
+                var += d * d;
+            }
+        const double sd = count > 1 ? sqrt(var / (count - 1)) : 0.0;
+        for (int j = 0; j < count; ++j) adv[j] /= sd + 1e-6;
+    }
+    __syncthreads();
+    // per item: policy-gradient term + soft cross-entropy gradient
+    float* pc = q;   // the clean softmax reuses group 0's slots
+    const double s2 = a.sigma * a.sigma;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int k = a.mk_count[i], o0 = a.mk_start[i];
+        for (int o = 0; o < k; ++o) pc[o0 + o] = a.logits[o0 + o];
+        softmax_f32(pc + o0, k);
+        const float* t = a.targets + o0;
+        double mass = 0.0;
+        for (int o = 0; o < k; ++o) mass += t[o];
+        for (int o = 0; o < k; ++o) {
+            double gr = 0.0;
+            for (int g = 0; g < G; ++g)
+                gr -= adv[static_cast<size_t>(g) * n + i] * eps[static_cast<size_t>(g) * M + o0 + o] / s2 / count;
+            gr += a.w_ce * (static_cast<double>(pc[o0 + o]) * mass - t[o]) / n;
+            a.dlogits[o0 + o] = __double2float_rn(gr * a.scale);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double policy = 0.0, ce = 0.0, rsum = 0.0;
+        for (int i = 0; i < n; ++i) {
+            const int k = a.mk_count[i], o0 = a.mk_start[i];
+            for (int g = 0; g < G; ++g) {
+                double logp = 0.0;
+                for (int o = 0; o < k; ++o) {
+                    const double e = eps[static_cast<size_t>(g) * M + o0 + o];
+                    logp -= e * e / (2 * s2);
+                }
+                policy -= adv[static_cast<size_t>(g) * n + i] * logp / count;
+                rsum += reward[static_cast<size_t>(g) * n + i];
+            }
+            for (int o = 0; o < k; ++o) ce -= a.targets[o0 + o] * log(fmax(static_cast<double>(pc[o0 + o]), 1e-30)) / n;
+        }
+        a.result[0] = policy + a.w_ce * ce;
+        a.result[1] = policy;
+        a.result[2] = ce;
+        a.result[3] = rsum / count;
+    }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+}
+
+}  // namespace tr
+
+// ------------------------------------------------------------------------------------------------ launchers
+static unsigned blocks_for(size_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+int ln_fwd(const tr::LnFwd& a, cudaStream_t s) {
+    if (a.rows <= 0) return OK;
+    const unsigned g = blocks_for(static_cast<size_t>(a.rows) * 32, 256);
+    if (a.n <= 128) tr::ln_fwd_kernel<4><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 256) tr::ln_fwd_kernel<8><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 768) tr::ln_fwd_kernel<24><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 1024) tr::ln_fwd_kernel<32><<<g, 256, 0, s>>>(a);
+    else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+int ln_bwd(const tr::LnBwd& a, cudaStream_t s) {
+    if (a.rows <= 0) return OK;
+    const unsigned g = blocks_for(static_cast<size_t>(a.rows), tr::LN_ROWS);
+    if (a.n <= 128) tr::ln_bwd_kernel<4><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 256) tr::ln_bwd_kernel<8><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 768) tr::ln_bwd_kernel<24><<<g, 256, 0, s>>>(a);
+    else if (a.n <= 1024) tr::ln_bwd_kernel<32><<<g, 256, 0, s>>>(a);
+    else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+#define LAUNCH1(kern, n, ...)                                                           \
+    do {                                                                                \
+        if ((n) > 0) {                                                                  \
+            tr::kern<<<blocks_for((n), 256), 256, 0, s>>>(__VA_ARGS__);                 \
+            count_launch();                                                             \
+            LAYA_CUDA(cudaGetLastError());                                              \
+        }                                                                               \
+        return OK;                                                                      \
+    } while (0)
+
+int geglu_fwd(const __nv_bfloat16* wide, int rows, int I, __nv_bfloat16* act, cudaStream_t s) {
+    LAUNCH1(geglu_fwd_kernel, static_cast<size_t>(rows) * I, wide, rows, I, act);
+}
+int geglu_bwd(const __nv_bfloat16* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s) {
+    LAUNCH1(geglu_bwd_kernel, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
+}
+int add_masked(const float* a, const float* b, float* y, size_t n, tr::Mask m, cudaStream_t s) {
+    LAUNCH1(add_masked_kernel, n, a, b, y, n, m);
+}
+int relu_mask(const __nv_bfloat16* pre, __nv_bfloat16* act, size_t n, tr::Mask m, cudaStream_t s) {
+    LAUNCH1(relu_mask_kernel, n, pre, act, n, m);
+}
+int relu_mask_bwd(const float* d, const __nv_bfloat16* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s) {
+    LAUNCH1(relu_mask_bwd_kernel, n, d, pre, dx, n, m);
+}
+int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s) { LAUNCH1(cast_mask_kernel, n, x, y, n, m); }
+int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) { LAUNCH1(f32_to_bf16_kernel, n, x, y, n); }
+int scatter_rows(const float* d, const int32_t* ids, int rows, int n, float* grad, cudaStream_t s) {
+    LAUNCH1(scatter_rows_kernel, static_cast<size_t>(rows) * n, d, ids, rows, n, grad);
+}
+
+int colsum_f32(const float* d, int rows, int n, float* db, cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return OK;
+    dim3 grid((rows + 63) / 64, (n + 255) / 256);
+    tr::colsum_kernel<float><<<grid, 256, 0, s>>>(d, rows, n, db);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int colsum_bf16(const __nv_bfloat16* d, int rows, int n, float* db, cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return OK;
+    dim3 grid((rows + 63) / 64, (n + 255) / 256);
+    tr::colsum_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(d, rows, n, db);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int type_grad(const float* d, const int32_t* tok_item, const int32_t* qtype, int rows, int n, float* grad, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    tr::type_grad_kernel<<<(rows + 63) / 64, 256, sizeof(float) * 3 * n, s>>>(d, tok_item, qtype, rows, n, grad);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int scorer_out(const float* pre, int M, int n, const float* w2, const float* b2, float* logits, cudaStream_t s) {
+    if (M <= 0) return OK;
+    tr::scorer_out_kernel<<<blocks_for(static_cast<size_t>(M) * 32, 256), 256, 0, s>>>(pre, M, n, w2, b2, logits);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int scorer_bwd(const float* pre, const float* dlogit, int M, int n, const float* w2, __nv_bfloat16* dpre, float* db1,
+               float* dw2, float* db2, cudaStream_t s) {
+    if (M <= 0) return OK;
+    tr::scorer_bwd_kernel<<<blocks_for(static_cast<size_t>(n), 256), 256, 0, s>>>(pre, dlogit, M, n, w2, dpre, db1, dw2, db2);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+size_t rlcd_scratch_bytes(int groups, int n_items, int M) {
+    return sizeof(double) * (static_cast<size_t>(groups) * M + 2 * static_cast<size_t>(groups) * n_items) +
+           sizeof(float) * static_cast<size_t>(groups > 0 ? groups : 1) * M;
+}
+int rlcd(const tr::RlcdArgs& a, cudaStream_t s) {
+    if (a.n_items <= 0) return OK;
+    tr::rlcd_kernel<<<1, 256, 0, s>>>(a);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int sumsq(const float* g, size_t n, double* out, cudaStream_t s) {
+    if (n == 0) return OK;
+    tr::sumsq_kernel<<<296, 256, 0, s>>>(g, n, out);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int clip_scale(const double* sumsq, double max_norm, int world, double* scale, double* norm_out, cudaStream_t s) {
+    tr::clip_scale_kernel<<<1, 1, 0, s>>>(sumsq, max_norm, world, scale, norm_out);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+int adamw(const tr::AdamArgs& a, cudaStream_t s) {
+    if (a.n == 0) return OK;
+    tr::adamw_kernel<<<blocks_for(a.n, 256), 256, 0, s>>>(a);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+}  // namespace laya

@@ -19,7 +19,8 @@ def declared():
 def test_header_declares_the_boundary():
     names = declared()
     for n in ["laya_ctx_create", "laya_upload_tensor", "laya_upload_q8_0", "laya_q8_0_linear", "laya_decision_forward",
-              "laya_last_error"]:
+              "laya_last_error", "laya_trainer_create", "laya_train_forward", "laya_train_backward",
+              "laya_train_objective", "laya_train_clip_and_step", "laya_train_comm_init"]:
         assert n in names
 
 
@@ -40,19 +41,32 @@ def test_no_cpu_fallback_without_a_gpu():
         laya_b200.Context(laya_b200.base_desc(max_tokens=128, max_items=4, max_markers=16))
 
 
-def test_model_desc_layout_matches_the_header(tmp_path):
-    """The ctypes mirror of laya_model_desc has the C compiler's size and field offsets."""
+@pytest.mark.parametrize("header,struct,cls", [("laya_b200.h", "laya_model_desc", "ModelDesc"),
+                                                ("laya_train.h", "laya_train_desc", "TrainDesc"),
+                                                ("laya_train.h", "laya_rlcd_desc", "RlcdDesc")])
+def test_struct_layouts_match_the_headers(tmp_path, header, struct, cls):
+    """The ctypes mirrors of the C ABI structs have the C compiler's size and field offsets."""
     import subprocess
     import laya_b200
-    fields = [f for f, _ in laya_b200.ModelDesc._fields_]
+    C = getattr(laya_b200, cls)
+    fields = [f for f, _ in C._fields_]
     src = tmp_path / "desc.c"
-    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "laya_b200.h"\nint main(void){printf("%zu", sizeof(laya_model_desc));'
-                   + "".join(f'printf(" %zu", offsetof(laya_model_desc, {f}));' for f in fields) + "return 0;}\n")
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "{header}"\nint main(void){{printf("%zu", sizeof({struct}));'
+                   + "".join(f'printf(" %zu", offsetof({struct}, {f}));' for f in fields) + "return 0;}\n")
     exe = tmp_path / "desc"
     subprocess.check_call(["gcc", "-I" + os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
     out = [int(v) for v in subprocess.check_output([str(exe)]).split()]
-    assert out[0] == ctypes.sizeof(laya_b200.ModelDesc)
-    assert out[1:] == [getattr(laya_b200.ModelDesc, f).offset for f in fields]
+    assert out[0] == ctypes.sizeof(C)
+    assert out[1:] == [getattr(C, f).offset for f in fields]
+
+
+def test_trainer_fails_loudly_without_a_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("this machine has a GPU")
+    import laya_b200
+    with pytest.raises(laya_b200.LayaError):
+        laya_b200.Trainer(laya_b200.base_desc(max_tokens=128, max_items=4, max_markers=16))
 
 
 def test_invalid_geometry_is_an_argument_error():

@@ -1,0 +1,258 @@
+"""The fine-tuning step on the B200 against the training oracle, through the C ABI of include/laya_train.h.
+
+Bars (bf16 tensor-core products, fp32 everything else):
+  * logits: max |gpu - oracle| / max |oracle| <= 2e-2 per item;
+  * every parameter gradient: cosine similarity >= 0.999 and max |gpu - oracle| / max |oracle| <= 2e-2;
+  * the objective (fp64 on the device) against the oracle on the same logits: 1e-5;
+  * clipping + AdamW on the device's own gradients: the norm to 1e-9 relative, parameters bit-identical to the
+    reference's fp32 element arithmetic (AdamW.cs:56-63);
+  * dropout masks are the reference's counter hash: training-mode parity holds only if every mask bit agrees.
+The oracle is the fp32 PyTorch restatement of TrainableDecisionModel pinned to the reference's training-tiny fixture
+(tests/test_oracle_train.py); the fixture's own logits and 57 gradients are checked directly here too.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, max_rel
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+COS = 0.999
+
+
+def tiny():
+    from oracle.model import EncoderConfig
+    g = json.load(open(os.path.join(GOLDEN, "training_tiny.json")))
+    w = dict(np.load(os.path.join(GOLDEN, "training_tiny_model.npz")))
+    cfg = EncoderConfig.from_hf(g["encoder_config"], head_layers=2, n_act=len(g["agent_config"]["act_costs"]) + 1)
+    return cfg, w, g
+
+
+def desc_for(cfg, **kw):
+    import laya_b200
+    kinds = [1 if cfg.kind(i) == "global" else 0 for i in range(cfg.layers)]
+    d = dict(hidden=cfg.hidden, intermediate=cfg.intermediate, layers=cfg.layers, heads=cfg.heads, vocab=cfg.vocab,
+             local_attention=cfg.local_attention, theta_global=cfg.theta_global, theta_local=cfg.theta_local,
+             norm_eps=cfg.norm_eps, head_layers=cfg.head_layers, n_act=cfg.n_act, layer_kinds=kinds)
+    d.update(kw)
+    return laya_b200.base_desc(**d)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    na, nb = np.linalg.norm(a), np.linalg.norm(b)
+    if na == 0 and nb == 0:
+        return 1.0
+    return float(a @ b / max(na * nb, 1e-300))
+
+
+def fixture_items(g):
+    from laya_b200 import TrainingItem
+    return [TrainingItem(np.array(it["ids"]), np.array(it["markers"]), it["qtype"]) for it in g["batch"]["items"]]
+
+
+def check_grads(t, want, skip=()):
+    bad = []
+    for name, gw in want.items():
+        if name in skip:
+            continue
+        got = t.gradient(name, gw.shape)
+        c, r = cosine(got, gw), max_rel(got, gw)
+        if c < COS or r > TOL:
+            bad.append(f"{name}: cos {c:.5f} rel {r:.2e}")
+    assert not bad, bad
+
+
+@pytest.fixture(scope="module")
+def tiny_trainer(cuda):
+    import laya_b200
+    cfg, w, g = tiny()
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=256, max_items=16, max_markers=64),
+                          laya_b200.train_desc(max_segment=128))
+    t.load(w)
+    yield cfg, w, g, t
+    t.close()
+
+
+def test_fixture_logits_and_every_gradient(tiny_trainer):
+    """TrainingGradientTests.LogitsMatchPyTorch / EveryGradientMatchesPyTorch (TrainingGradientTests.cs:44-85) at the
+    bf16 bars: loss = Σ coeff · logits, all 57 gradients; the action head gets none."""
+    cfg, w, g, t = tiny_trainer
+    items = g["batch"]["items"]
+    b = t.batch(fixture_items(g))
+    t.zero_grads()
+    logits = t.forward(b, training=False)
+    for l, it in zip(logits, items):
+        assert max_rel(l, it["logits"]) <= TOL, (l, it["logits"])
+    t.backward(b, [np.array(it["coeff"], np.float32) for it in items])
+    want = dict(np.load(os.path.join(GOLDEN, "training_tiny_grads.npz")))
+    assert len(want) == 57
+    check_grads(t, want)
+    for name in ("act_head.0.weight", "act_head.0.bias", "act_head.2.weight", "act_head.2.bias"):
+        assert not np.any(t.gradient(name, w[name].shape))
+    t.zero_grads()
+
+
+def test_training_mode_dropout_matches_the_oracle(tiny_trainer):
+    """Head dropout (p = 0.1) on the attention probabilities and the three residual branches, masks by Ops.Uniform
+    with TrainableDecisionModel.Salt: logits and gradients of the training forward against the oracle's."""
+    import torch
+    from oracle.train import TorchTrainModel, mix
+    cfg, w, g, t = tiny_trainer
+    items = g["batch"]["items"]
+    seed = mix(42, 7)
+    m = TorchTrainModel(cfg, w, head_dropout=0.1)
+    ref = m.forward(items, training=True, seed=seed)
+    loss = sum((l * torch.tensor(it["coeff"], dtype=torch.float32)).sum() for l, it in zip(ref, items))
+    loss.backward()
+    b = t.batch(fixture_items(g))
+    t.zero_grads()
+    logits = t.forward(b, training=True, seed=seed)
+    for l, r in zip(logits, ref):
+        assert max_rel(l, r.detach().numpy()) <= TOL
+    # dropout is really on: the training logits differ from the evaluation ones
+    ev = m.forward(items, training=False)
+    assert max(max_rel(r.detach().numpy(), e.detach().numpy()) for r, e in zip(ref, ev)) > 1e-3
+    t.backward(b, [np.array(it["coeff"], np.float32) for it in items])
+    check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")])
+    t.zero_grads()
+
+
+def test_objective_matches_the_oracle(tiny_trainer):
+    """RlcdObjective.Compute on the device against oracle.train.rlcd (pinned to the notebook's objective.json) on the
+    same logits, targets and draws."""
+    from oracle.train import rlcd
+    from laya_b200 import TrainingItem
+    cfg, w, g, t = tiny_trainer
+    rng = np.random.default_rng(5)
+    items = []
+    for it in g["batch"]["items"]:
+        k = len(it["markers"])
+        tg = rng.random(k).astype(np.float32)
+        items.append(TrainingItem(np.array(it["ids"]), np.array(it["markers"]), it["qtype"], tg / tg.sum()))
+    m = sum(it.options for it in items)
+    draws = rng.standard_normal((4, m))
+    b = t.batch(items, draws)
+    logits = t.forward(b, training=False)
+    (loss, policy, ce, reward), dl = t.objective(b, sigma=0.3, groups=4, scale=0.25)
+    per_item, o = [], 0
+    for it in items:
+        per_item.append(o)
+        o += it.options
+    dr = [[draws[gi, s:s + it.options] for s, it in zip(per_item, items)] for gi in range(4)]
+    want = rlcd(logits, [it.target for it in items], [it.question_type for it in items], 0.3, dr, scale=0.25)
+    assert abs(loss - want[0]) < 1e-5 and abs(policy - want[1]) < 1e-5
+    assert abs(ce - want[2]) < 1e-5 and abs(reward - want[3]) < 1e-5
+    for a, e in zip(dl, want[4]):
+        assert np.max(np.abs(a - e)) < 1e-6
+
+
+def test_clip_and_adamw_are_the_reference_arithmetic(tiny_trainer):
+    """Two optimizer steps on the device's own gradients: ClipByGlobalNorm's norm, then every parameter
+    bit-identical to AdamW.Step's fp32 arithmetic with the two groups' rates (AdamW.cs:29-73, 103-130)."""
+    from oracle.train import adamw_step
+    cfg, w, g, t = tiny_trainer
+    items = g["batch"]["items"]
+    names = t.names()
+    b = t.batch(fixture_items(g))
+    state = {n: (np.zeros(r * c, np.float32), np.zeros(r * c, np.float32)) for n, r, c in names}
+    lr = {0: 2.5e-5, 1: 1e-4}
+    t.set_lr(lr[0], lr[1])
+    for step in (1, 2):
+        t.zero_grads()
+        t.forward(b, training=False)
+        t.backward(b, [np.array(it["coeff"], np.float32) * 50 for it in items])
+        params = {n: t.download(n, (r, c)).ravel() for n, r, c in names}
+        grads = {n: t.gradient(n, (r, c)).ravel() for n, r, c in names}
+        norm = t.clip_and_step(max_norm=0.5)
+        want_norm = float(np.sqrt(sum(np.sum(gr.astype(np.float64) ** 2) for gr in grads.values())))
+        assert abs(norm - want_norm) <= 1e-9 * want_norm
+        coef = 0.5 / (norm + 1e-6)
+        assert coef < 1.0   # the clipping branch is exercised
+        for n, r, c in names:
+            p = params[n].copy()
+            gr = grads[n] * np.float32(coef)
+            m_, v_ = state[n]
+            adamw_step(p, gr, m_, v_, step, lr[0] if n.startswith("encoder.") else lr[1])
+            got = t.download(n, (r, c)).ravel()
+            assert np.array_equal(got.view(np.uint32), p.view(np.uint32)), n
+    assert t.steps() == 2
+    t.zero_grads()
+
+
+def test_frozen_encoder_layers(cuda):
+    """SetTrainableEncoderLayers(1): only the top layer, the final norm and the head train; frozen tensors get no
+    gradient and no update, and the trained ones get the full model's gradients."""
+    import laya_b200
+    cfg, w, g = tiny()
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=256, max_items=16, max_markers=64),
+                          laya_b200.train_desc(max_segment=128, trainable_encoder_layers=1))
+    t.load(w)
+    total, trainable = t.param_count()
+    assert total == sum(v.size for k, v in w.items() if k != "temperature")
+    frozen = [k for k in w if k.startswith("encoder.") and not k.startswith(("encoder.layers.3.", "encoder.final_norm"))]
+    assert trainable == total - sum(w[k].size for k in frozen)
+    items = g["batch"]["items"]
+    b = t.batch(fixture_items(g))
+    t.forward(b)
+    t.backward(b, [np.array(it["coeff"], np.float32) for it in items])
+    want = dict(np.load(os.path.join(GOLDEN, "training_tiny_grads.npz")))
+    check_grads(t, {k: v for k, v in want.items() if k not in frozen})
+    for k in frozen:
+        assert not np.any(t.gradient(k, w[k].shape)), k
+    t.clip_and_step(max_norm=1.0)
+    for k in frozen:
+        assert np.array_equal(t.download(k, w[k].shape), w[k]), k
+    t.close()
+
+
+def test_base_geometry_matches_the_oracle(cuda):
+    """ModernBERT-base widths (768, 12 heads × 64, I 1152; head 12 × 64, ff 3072) on two encoder layers (global and
+    sliding ±64) with ragged rows longer than the window: logits and every gradient against the oracle."""
+    import torch
+    import laya_b200
+    from laya_b200.workloads import training_batch, training_weights
+    from oracle.model import EncoderConfig
+    from oracle.train import TorchTrainModel
+    cfg = EncoderConfig(layers=2, vocab=3000)
+    w = training_weights(layers=2, vocab=3000, seed=3)
+    items, _ = training_batch(rows=3, min_len=150, max_len=300, vocab=3000, seed=4)
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=1024, max_items=8, max_markers=32),
+                          laya_b200.train_desc(max_segment=512))
+    t.load(w)
+    b = t.batch(items)
+    logits = t.forward(b, training=False)
+    m = TorchTrainModel(cfg, w)
+    oi = [{"ids": it.token_ids, "markers": list(it.marker_positions), "qtype": it.question_type} for it in items]
+    ref = m.forward(oi, training=False)
+    coeff = [np.random.default_rng(9).standard_normal(it.options).astype(np.float32) for it in items]
+    loss = sum((r * torch.from_numpy(c)).sum() for r, c in zip(ref, coeff))
+    loss.backward()
+    for l, r in zip(logits, ref):
+        assert max_rel(l, r.detach().numpy()) <= TOL
+    t.backward(b, coeff)
+    check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")])
+    t.close()
+
+
+def test_errors_are_reported_like_the_reference(tiny_trainer):
+    """Token ids outside the vocabulary and markers past their segment: ArgumentOutOfRangeException's code; a batch
+    larger than the trainer, or an objective before any forward: ArgumentException's."""
+    import laya_b200
+    from laya_b200 import TrainingItem
+    cfg, w, g, t = tiny_trainer
+    with pytest.raises(laya_b200.LayaOutOfRangeError):
+        t.batch([TrainingItem(np.array([1, 2, cfg.vocab]), np.array([0]), 0)])
+    with pytest.raises(laya_b200.LayaOutOfRangeError):
+        t.batch([TrainingItem(np.array([1, 2, 3]), np.array([3]), 0)])
+    with pytest.raises(laya_b200.LayaArgumentError):
+        t.batch([TrainingItem(np.arange(300) % 90, np.array([0]), 0)])
+    fresh = t.batch([TrainingItem(np.array([1, 2, 3]), np.array([1]), 0)], np.zeros((4, 1)))
+    with pytest.raises(laya_b200.LayaArgumentError):
+        t.objective(fresh, sigma=0.3)
+    with pytest.raises(laya_b200.LayaNotFoundError):
+        t.upload("encoder.layers.9.attn.Wo.weight", np.zeros((128, 128), np.float32))
