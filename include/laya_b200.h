@@ -173,11 +173,20 @@ int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const uint16_t* qx,
  * The bf16 tensor-core product of the training step on caller device buffers (PackedMatrix.Multiply as Ops.Linear and
  * Ops.LinearBackward use it, Laya.Training/Ops.cs:22-69): out[M, N] = A · Bᵀ (+ bias) with fp32 accumulation.
  * A is [M, K] (a_mn = 0, row stride lda) or stored transposed as [K, lda] (a_mn = 1); likewise B [N, K] or [K, ldb].
- * epilogue 0: out bf16 [M, ldo]; 1: out fp32; 2: out fp32 += product (accumulating gradients and residual streams).
+ * epilogue 0: out bf16 [M, ldo]; 1: out fp32; 2: out fp32 += product (accumulating gradients and residual streams;
+ * when few output tiles cover a long K, K is split into chunks that reduce-add, so the summation order may vary).
  * Bases 16-byte aligned, row strides multiples of 8 elements (4 for fp32 outputs).
  */
 int laya_gemm_bf16_device(laya_ctx* ctx, int M, int N, int K, const uint16_t* A, int lda, int a_mn, const uint16_t* B,
                           int ldb, int b_mn, const float* bias, int epilogue, void* out, int ldo);
+/*
+ * The same product with fp32 accuracy from bf16 tensor cores (the fine-tuning forward's products): the caller passes
+ * each fp32 operand as hi = bf16(x) and lo = bf16(x - hi) (same layouts), and gets A·Bᵀ + A_lo·Bᵀ + A·B_loᵀ.
+ * No reference counterpart beyond PackedMatrix.Multiply's fp32 result, which it reproduces to about 2^-16 relative.
+ */
+int laya_gemm_bf16_split_device(laya_ctx* ctx, int M, int N, int K, const uint16_t* A, const uint16_t* A_lo, int lda,
+                                int a_mn, const uint16_t* B, const uint16_t* B_lo, int ldb, int b_mn, const float* bias,
+                                int epilogue, void* out, int ldo);
 
 /*
  * laya_q8_0_linear_noalloc — the Q8_0 projection y = Q8_0(x) · W (+ bias) without any device allocation.

@@ -43,7 +43,19 @@ typedef struct laya_train_desc {
     int max_segment;               /* longest segment a batch may carry (rotary tables); <= 2^21 */
     int grad_accumulation;         /* GradientAccumulation: micro-batches per optimizer step (data parallel: the
                                       allreduce overlaps the backward of the last one); <= 0 means 1 */
+    int forward_mode;              /* LAYA_FORWARD_ACCURATE (0) or LAYA_FORWARD_BF16 (1), below */
 } laya_train_desc;
+
+/* Forward precision of the fine-tuning step.  The backward products are bf16 (fp32 accumulation) in both modes.
+ *   ACCURATE  every forward product (projections, attention scores and P·V) is formed from bf16 hi/lo parts of fp32
+ *             operands as hi·hi + lo·hi + hi·lo on the tensor cores — fp32-accurate activations, so ReLU masks and
+ *             every downstream gradient follow the fp32 reference path (Laya.Training runs fp32).  3x the forward
+ *             tensor work.
+ *   BF16      forward products from bf16 operands, as torch.autocast(bfloat16) runs the reference notebook's DDP
+ *             recipe: fastest, but a bf16 forward moves activations by ~1e-3 relative, which flips ReLU masks of the
+ *             decision head and so moves gradients away from the fp32 path by more than rounding. */
+#define LAYA_FORWARD_ACCURATE 0
+#define LAYA_FORWARD_BF16 1
 
 /* RlcdObjective settings (RlcdObjective.cs:31-35) and the per-call sigma and gradient scale. */
 typedef struct laya_rlcd_desc {

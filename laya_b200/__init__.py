@@ -16,10 +16,11 @@ library raises `LayaLibraryMissing`.
 from .api import (Context, DecisionModel, DecisionOutput, BatchItem, ModelDesc, PackedMatrixQ8_0, Q8_0,
                   LayaError, LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
                   LayaNotFoundError, LayaDeviceTimeout, LayaLibraryMissing, lib, library_path, base_desc,
-                  PRECISION_F32, PRECISION_Q8_0, Trainer, Batch, TrainingItem, TrainDesc, RlcdDesc, train_desc)
+                  PRECISION_F32, PRECISION_Q8_0, Trainer, Batch, TrainingItem, TrainDesc, RlcdDesc, train_desc,
+                  FORWARD_ACCURATE, FORWARD_BF16)
 
 __all__ = ["Context", "DecisionModel", "DecisionOutput", "BatchItem", "ModelDesc", "PackedMatrixQ8_0", "Q8_0",
            "LayaError", "LayaArgumentError", "LayaOutOfRangeError", "LayaNotSupportedError", "LayaCudaError",
            "LayaNotFoundError", "LayaDeviceTimeout", "LayaLibraryMissing", "lib", "library_path", "base_desc",
            "PRECISION_F32", "PRECISION_Q8_0", "Trainer", "Batch", "TrainingItem", "TrainDesc", "RlcdDesc",
-           "train_desc"]
+           "train_desc", "FORWARD_ACCURATE", "FORWARD_BF16"]

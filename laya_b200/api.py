@@ -93,6 +93,7 @@ _SIGS = {
     "laya_pack_q8_0": (_I, [_P, ctypes.c_char_p, _I, _P, _I, _I]),
     "laya_q8_0_linear_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P]),
     "laya_gemm_bf16_device": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I]),
+    "laya_gemm_bf16_split_device": (_I, [_P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _I, _I, _P, _I, _P, _I]),
     "laya_decision_forward": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "laya_decision_forward_device": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P]),
     "laya_encoder_forward": (_I, [_P, _P, _P, _I, _P]),
@@ -424,7 +425,11 @@ class TrainDesc(ctypes.Structure):
     _fields_ = [("trainable_encoder_layers", ctypes.c_int), ("head_dropout", ctypes.c_float),
                 ("beta1", ctypes.c_double), ("beta2", ctypes.c_double), ("eps", ctypes.c_double),
                 ("weight_decay", ctypes.c_double), ("encoder_lr", ctypes.c_double), ("head_lr", ctypes.c_double),
-                ("max_segment", ctypes.c_int), ("grad_accumulation", ctypes.c_int)]
+                ("max_segment", ctypes.c_int), ("grad_accumulation", ctypes.c_int), ("forward_mode", ctypes.c_int)]
+
+
+FORWARD_ACCURATE = 0   # fp32-accurate forward from bf16 hi/lo tensor-core products (the fp32 reference path)
+FORWARD_BF16 = 1       # bf16-operand forward (torch.autocast(bfloat16) numerics)
 
 
 class RlcdDesc(ctypes.Structure):
@@ -437,7 +442,7 @@ class RlcdDesc(ctypes.Structure):
 def train_desc(**kw) -> TrainDesc:
     """Trainer defaults (TrainerOptions: encoder 2.5e-5, head 1e-4, wd 0.01, dropout 0.1; AdamW 0.9/0.999/1e-8)."""
     d = dict(trainable_encoder_layers=-1, head_dropout=0.1, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
-             encoder_lr=2.5e-5, head_lr=1e-4, max_segment=0, grad_accumulation=1)
+             encoder_lr=2.5e-5, head_lr=1e-4, max_segment=0, grad_accumulation=1, forward_mode=FORWARD_ACCURATE)
     d.update(kw)
     return TrainDesc(**d)
 

@@ -953,6 +953,24 @@ int laya_gemm_bf16_device(laya_ctx* c, int M, int N, int K, const uint16_t* A, i
     a.A = reinterpret_cast<const __nv_bfloat16*>(A); a.lda = lda; a.a_mn = a_mn != 0;
     a.B = reinterpret_cast<const __nv_bfloat16*>(B); a.ldb = ldb; a.b_mn = b_mn != 0;
     a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.err = c->err;
+    a.ksplit_ok = epilogue == 2;
+    return bf::gemm(a, c->stream);
+}
+
+int laya_gemm_bf16_split_device(laya_ctx* c, int M, int N, int K, const uint16_t* A, const uint16_t* A_lo, int lda,
+                                int a_mn, const uint16_t* B, const uint16_t* B_lo, int ldb, int b_mn, const float* bias,
+                                int epilogue, void* out, int ldo) {
+    if (!c) { set_error("null context"); return ERR_ARGUMENT; }
+    if (!A_lo || !B_lo) { set_error("split product needs both low parts"); return ERR_ARGUMENT; }
+    if (epilogue < 0 || epilogue > 2) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    bf::Args a{};
+    a.M = M; a.N = N; a.K = K;
+    a.A = reinterpret_cast<const __nv_bfloat16*>(A); a.lda = lda; a.a_mn = a_mn != 0;
+    a.B = reinterpret_cast<const __nv_bfloat16*>(B); a.ldb = ldb; a.b_mn = b_mn != 0;
+    a.A2 = reinterpret_cast<const __nv_bfloat16*>(A_lo); a.B2 = reinterpret_cast<const __nv_bfloat16*>(B_lo);
+    a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.err = c->err;
+    a.ksplit_ok = epilogue == 2;
     return bf::gemm(a, c->stream);
 }
 

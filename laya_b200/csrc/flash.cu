@@ -14,6 +14,10 @@
 //     split into a query-tile kernel (dQ) and a key-tile kernel (dK, dV), each recomputing P: no atomics, so the
 //     gradients are deterministic.
 // Tiles are 64 queries × 64 keys; each of the 4 warps owns 16 rows; mma.sync m16n8k16 bf16 → fp32.
+// The accurate forward (qkv32 set) reads fp32 q, k, v and forms every product from bf16 hi/lo parts (three MMAs per
+// product), writing the context as hi and lo; the backward then reads the same fp32 q, k, v rounded to bf16.
+#include <type_traits>
+
 #include "common.cuh"
 #include "internal.h"
 #include "train.h"
@@ -58,27 +62,41 @@ DEVI float drop_mult(const Args& a, int head, int row, int key) {
     return dropout_uniform(a.seed, idx) < a.dropout ? 0.0f : a.keep;
 }
 
-// Loads 64 rows of one head's slice (columns col0 .. col0+HD) at segment positions [p0, p0+64) from a bf16 [T, ld]
-// buffer into smem, rotating pairs (i, i+HD/2) when cos/sin are given.  Rows past `limit` are zero.
-template <int HD>
-DEVI void load_rows(__nv_bfloat16* dst, const __nv_bfloat16* base, int ld, int p0, int limit, const float* cosv,
-                    const float* sinv) {
+// Loads 64 rows of one head's slice (columns col0 .. col0+HD) at segment positions [p0, p0+64) from a [T, ld] buffer
+// (bf16, or fp32 in the accurate forward) into smem, rotating pairs (i, i+HD/2) in fp32 when cos/sin are given.  Rows
+// past `limit` are zero.  With `lo` (fp32 sources only) the bf16 remainder x − bf16(x) goes to a second tile.
+DEVI void load4(const __nv_bfloat16* p, float (&v)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float2 f = __bfloat1622float2(h[0]);
+    v[0] = f.x; v[1] = f.y;
+    f = __bfloat1622float2(h[1]);
+    v[2] = f.x; v[3] = f.y;
+}
+DEVI void load4(const float* p, float (&v)[4]) {
+    const float4 f = *reinterpret_cast<const float4*>(p);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+DEVI uint2 pack4(const float (&v)[4]) { return make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3])); }
+DEVI uint2 pack4_lo(const float (&v)[4]) {
+    float r[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) r[t] = v[t] - __bfloat162float(__float2bfloat16_rn(v[t]));
+    return pack4(r);
+}
+
+template <int HD, typename Src>
+DEVI void load_rows(__nv_bfloat16* dst, __nv_bfloat16* lo, const Src* base, int ld, int p0, int limit,
+                    const float* cosv, const float* sinv) {
     constexpr int HALF = HD / 2, J = HALF / 4;   // 4 pairs per step
     for (int it = threadIdx.x; it < 64 * J; it += blockDim.x) {
         const int r = it / J, j = it % J;
         const int pos = p0 + r;
         float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
         if (pos < limit) {
-            const __nv_bfloat16* src = base + static_cast<size_t>(pos) * ld;
-            const uint2 ua = *reinterpret_cast<const uint2*>(src + 4 * j);
-            const uint2 ub = *reinterpret_cast<const uint2*>(src + HALF + 4 * j);
-            const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ua);
-            const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&ub);
-            float2 f;
-            f = __bfloat1622float2(ha[0]); a[0] = f.x; a[1] = f.y;
-            f = __bfloat1622float2(ha[1]); a[2] = f.x; a[3] = f.y;
-            f = __bfloat1622float2(hb[0]); b[0] = f.x; b[1] = f.y;
-            f = __bfloat1622float2(hb[1]); b[2] = f.x; b[3] = f.y;
+            const Src* src = base + static_cast<size_t>(pos) * ld;
+            load4(src + 4 * j, a);
+            load4(src + HALF + 4 * j, b);
             if (cosv) {
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
@@ -90,8 +108,12 @@ DEVI void load_rows(__nv_bfloat16* dst, const __nv_bfloat16* base, int ld, int p
                 }
             }
         }
-        *reinterpret_cast<uint2*>(dst + r * LDS + 4 * j) = make_uint2(pack_bf16(a[0], a[1]), pack_bf16(a[2], a[3]));
-        *reinterpret_cast<uint2*>(dst + r * LDS + HALF + 4 * j) = make_uint2(pack_bf16(b[0], b[1]), pack_bf16(b[2], b[3]));
+        *reinterpret_cast<uint2*>(dst + r * LDS + 4 * j) = pack4(a);
+        *reinterpret_cast<uint2*>(dst + r * LDS + HALF + 4 * j) = pack4(b);
+        if (lo) {
+            *reinterpret_cast<uint2*>(lo + r * LDS + 4 * j) = pack4_lo(a);
+            *reinterpret_cast<uint2*>(lo + r * LDS + HALF + 4 * j) = pack4_lo(b);
+        }
     }
 }
 
@@ -141,12 +163,19 @@ DEVI void mma_pv(float (&out)[NT][4], const uint32_t (&pa)[8][2], const __nv_bfl
 DEVI bool visible(bool global, int W, int q, int k, int L) { return k < L && q < L && (global || (k >= q - W && k <= q + W)); }
 
 // ------------------------------------------------------------------------------------------------ forward
-template <int HD>
+// SPLIT (the accurate forward): q, k, v come from fp32 and every product is taken as hi·hi + lo·hi + hi·lo of bf16
+// parts (scores and P·V), so the context is fp32-accurate; it is written as bf16 hi and lo parts.
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
-    constexpr int KS = HD / 16, NT = HD / 8;
-    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
+    constexpr int KS = HD / 16, NT = HD / 8, TILE = T64 * LDS;
+    using Src = typename std::conditional<SPLIT, float, __nv_bfloat16>::type;
+    extern __shared__ __align__(16) __nv_bfloat16 fsm[];
+    __nv_bfloat16* Qs = fsm;
+    __nv_bfloat16* Ks = fsm + TILE;
+    __nv_bfloat16* Vs = fsm + 2 * TILE;
+    __nv_bfloat16* Ql = SPLIT ? fsm + 3 * TILE : nullptr;
+    __nv_bfloat16* Kl = SPLIT ? fsm + 4 * TILE : nullptr;
+    __nv_bfloat16* Vl = SPLIT ? fsm + 5 * TILE : nullptr;
     const int tile = blockIdx.x;
     if (tile >= *a.n_tiles) return;
     const int head = blockIdx.y, item = a.tile_item[tile], q0 = a.tile_p0[tile];
@@ -154,11 +183,13 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD>(Qs, qb, a.ld, q0, L, a.cosv, a.sinv);
+    const Src* qb = (SPLIT ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
+                    static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD, Src>(Qs, Ql, qb, a.ld, q0, L, a.cosv, a.sinv);
     __syncthreads();
-    uint32_t fq[KS][4];
+    uint32_t fq[KS][4], fql[SPLIT ? KS : 1][4];
     load_a_frags<KS>(Qs, warp, lane, fq);
+    if constexpr (SPLIT) load_a_frags<KS>(Ql, warp, lane, fql);
     float o[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -167,13 +198,17 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
     for (int k0 = kb; k0 < ke; k0 += T64) {
         __syncthreads();
-        load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
-        load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
+        load_rows<HD, Src>(Ks, Kl, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
+        load_rows<HD, Src>(Vs, Vl, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
         __syncthreads();
         float s[8][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
         mma_abt<KS>(s, fq, Ks, lane);
+        if constexpr (SPLIT) {
+            mma_abt<KS>(s, fql, Ks, lane);
+            mma_abt<KS>(s, fq, Kl, lane);
+        }
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -195,7 +230,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
             m_run[h] = mn;
         }
         float rs[2] = {0.f, 0.f};
-        uint32_t pa[8][2];
+        uint32_t pa[8][2], pl[SPLIT ? 8 : 1][2];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             float pv[4];
@@ -209,6 +244,11 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
             }
             pa[j][0] = pack_bf16(pv[0], pv[1]);
             pa[j][1] = pack_bf16(pv[2], pv[3]);
+            if constexpr (SPLIT) {
+                const uint2 r = pack4_lo(pv);
+                pl[j][0] = r.x;
+                pl[j][1] = r.y;
+            }
         }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -219,6 +259,10 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
 #pragma unroll
         for (int j = 0; j < NT; ++j) { o[j][0] *= alpha[0]; o[j][1] *= alpha[0]; o[j][2] *= alpha[1]; o[j][3] *= alpha[1]; }
         mma_pv<NT>(o, pa, Vs, lane);
+        if constexpr (SPLIT) {
+            mma_pv<NT>(o, pl, Vs, lane);
+            mma_pv<NT>(o, pa, Vl, lane);
+        }
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -227,8 +271,15 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
         const float inv = l_run[h] > 0.f ? 1.0f / l_run[h] : 0.f;
         __nv_bfloat16* orow = a.out + static_cast<size_t>(seg0 + q) * a.ldo + head * HD;
 #pragma unroll
-        for (int j = 0; j < NT; ++j)
-            *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t4) = pack_bf16(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+        for (int j = 0; j < NT; ++j) {
+            const float c0 = o[j][2 * h] * inv, c1 = o[j][2 * h + 1] * inv;
+            *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t4) = pack_bf16(c0, c1);
+            if constexpr (SPLIT) {
+                __nv_bfloat16* lrow = a.out_lo + static_cast<size_t>(seg0 + q) * a.ldo + head * HD;
+                *reinterpret_cast<uint32_t*>(lrow + 8 * j + 2 * t4) =
+                    pack_bf16(c0 - __bfloat162float(__float2bfloat16_rn(c0)), c1 - __bfloat162float(__float2bfloat16_rn(c1)));
+            }
+        }
         if (t4 == 0) a.lse[static_cast<size_t>(seg0 + q) * a.heads + head] = m_run[h] + logf(l_run[h]);
     }
 }
@@ -281,7 +332,7 @@ DEVI void store_rows(float (&acc)[NT][4], __nv_bfloat16* base, int ld, int seg0,
 }
 
 // dQ for one 64-query tile of one head.
-template <int HD>
+template <int HD, typename Src>
 __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
     constexpr int KS = HD / 16, NT = HD / 8;
     __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
@@ -295,9 +346,11 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD>(Qs, qb, a.ld, q0, L, a.cosv, a.sinv);
-    load_rows<HD>(dOs, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, L, nullptr, nullptr);
+    const Src* qb = (sizeof(Src) == 4 ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
+                    static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD, Src>(Qs, nullptr, qb, a.ld, q0, L, a.cosv, a.sinv);
+    load_rows<HD, __nv_bfloat16>(dOs, nullptr, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, L,
+                                 nullptr, nullptr);
     __syncthreads();
     uint32_t fq[KS][4], fdo[KS][4];
     load_a_frags<KS>(Qs, warp, lane, fq);
@@ -316,8 +369,8 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
     const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
     for (int k0 = kb; k0 < ke; k0 += T64) {
         __syncthreads();
-        load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
-        load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
+        load_rows<HD, Src>(Ks, nullptr, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
+        load_rows<HD, Src>(Vs, nullptr, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
         __syncthreads();
         float s[8][4], dp[8][4];
 #pragma unroll
@@ -348,7 +401,7 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
 }
 
 // dK and dV for one 64-key tile of one head.
-template <int HD>
+template <int HD, typename Src>
 __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
     constexpr int KS = HD / 16, NT = HD / 8;
     __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
@@ -363,9 +416,10 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD>(Ks, qb + a.hidden, a.ld, k0, L, a.cosv, a.sinv);
-    load_rows<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, L, nullptr, nullptr);
+    const Src* qb = (sizeof(Src) == 4 ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
+                    static_cast<size_t>(seg0) * a.ld + head * HD;
+    load_rows<HD, Src>(Ks, nullptr, qb + a.hidden, a.ld, k0, L, a.cosv, a.sinv);
+    load_rows<HD, Src>(Vs, nullptr, qb + 2 * a.hidden, a.ld, k0, L, nullptr, nullptr);
     __syncthreads();
     uint32_t fk[KS][4], fv[KS][4];
     load_a_frags<KS>(Ks, warp, lane, fk);
@@ -379,8 +433,9 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
     const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + T64 + W);
     for (int q0 = qb0; q0 < qe; q0 += T64) {
         __syncthreads();
-        load_rows<HD>(Qs, qb, a.ld, q0, qe, a.cosv, a.sinv);
-        load_rows<HD>(dOs, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, qe, nullptr, nullptr);
+        load_rows<HD, Src>(Qs, nullptr, qb, a.ld, q0, qe, a.cosv, a.sinv);
+        load_rows<HD, __nv_bfloat16>(dOs, nullptr, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, qe,
+                                     nullptr, nullptr);
         for (int r = threadIdx.x; r < T64; r += blockDim.x) {
             const int q = q0 + r;
             lse_s[r] = q < qe ? a.lse[static_cast<size_t>(seg0 + q) * a.heads + head] : 0.f;
@@ -424,16 +479,38 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
 
 }  // namespace fa
 
-int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
-    if (max_tiles <= 0) return OK;
-    const int hd = a.hidden / a.heads;
-    dim3 grid(max_tiles, a.heads);
-    if (hd == 64) fa::fwd_kernel<64><<<grid, 128, 0, s>>>(a);
-    else if (hd == 32) fa::fwd_kernel<32><<<grid, 128, 0, s>>>(a);
-    else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
+template <int HD, bool SPLIT>
+static int launch_fwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    const int smem = (SPLIT ? 6 : 3) * fa::T64 * fa::LDS * 2;
+    static bool attr[64] = {false};
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        LAYA_CUDA(cudaFuncSetAttribute(fa::fwd_kernel<HD, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr[dev] = true;
+    }
+    fa::fwd_kernel<HD, SPLIT><<<dim3(max_tiles, a.heads), 128, smem, s>>>(a);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
+}
+
+int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    if (max_tiles <= 0) return OK;
+    const int hd = a.hidden / a.heads;
+    const bool split = a.qkv32 != nullptr;
+    if (split && !a.out_lo) { set_error("accurate attention needs the context's low part"); return ERR_ARGUMENT; }
+    if (hd == 64) return split ? launch_fwd<64, true>(a, max_tiles, s) : launch_fwd<64, false>(a, max_tiles, s);
+    if (hd == 32) return split ? launch_fwd<32, true>(a, max_tiles, s) : launch_fwd<32, false>(a, max_tiles, s);
+    set_error("attention supports head_dim 32 and 64");
+    return ERR_NOT_SUPPORTED;
+}
+
+template <int HD, typename Src>
+static void launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    dim3 grid(max_tiles, a.heads);
+    fa::bwd_dq_kernel<HD, Src><<<grid, 128, 0, s>>>(a);
+    fa::bwd_dkdv_kernel<HD, Src><<<grid, 128, 0, s>>>(a);
 }
 
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
@@ -442,9 +519,9 @@ int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
     const long long warps = static_cast<long long>(T) * a.heads;
     fa::bwd_dot_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(a, T);
     count_launch();
-    dim3 grid(max_tiles, a.heads);
-    if (hd == 64) { fa::bwd_dq_kernel<64><<<grid, 128, 0, s>>>(a); fa::bwd_dkdv_kernel<64><<<grid, 128, 0, s>>>(a); }
-    else if (hd == 32) { fa::bwd_dq_kernel<32><<<grid, 128, 0, s>>>(a); fa::bwd_dkdv_kernel<32><<<grid, 128, 0, s>>>(a); }
+    const bool f32 = a.qkv32 != nullptr;
+    if (hd == 64) { if (f32) launch_bwd<64, float>(a, max_tiles, s); else launch_bwd<64, __nv_bfloat16>(a, max_tiles, s); }
+    else if (hd == 32) { if (f32) launch_bwd<32, float>(a, max_tiles, s); else launch_bwd<32, __nv_bfloat16>(a, max_tiles, s); }
     else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
     count_launch(2);
     LAYA_CUDA(cudaGetLastError());

@@ -15,6 +15,8 @@
 //   warps 2-9   epilogue: 4 lane quarters × 2 column halves; each drains 32-column chunks with tcgen05.ld, adds the
 //               bias, converts, stages 32 rows × 128 B in shared memory and writes them with one TMA store (or TMA
 //               reduce-add for accumulating outputs: residual streams and parameter gradients).
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "train.h"
@@ -52,6 +54,8 @@ DEVI uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
 
 struct KParams {
     int M, N, K;
+    int splits;        // 1: A·Bᵀ;  3: A·Bᵀ + A2·Bᵀ + A·B2ᵀ (hi/lo operand pairs, an fp32-accurate product)
+    int ksplit;        // K chunks per output tile (accumulating outputs only: chunks reduce-add into the output)
     const float* bias;
     int* err;
 };
@@ -59,6 +63,7 @@ struct KParams {
 template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                      const __grid_constant__ CUtensorMap tmOut, KParams p) {
     using C = Cfg<BN, STAGES>;
     constexpr uint32_t IDESC = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, BM, BN) |
@@ -76,9 +81,15 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = warp_id(), lane = lane_id();
-    const int iters = (p.K + BK - 1) / BK;
+    const int kblocks = (p.K + BK - 1) / BK;
+    const int kchunk = (kblocks + p.ksplit - 1) / p.ksplit;   // k-blocks per work unit
     const int tiles_n = (p.N + BN - 1) / BN;
-    const int tiles = tiles_n * ((p.M + BM - 1) / BM);
+    const int tiles = tiles_n * ((p.M + BM - 1) / BM) * p.ksplit;   // work units: (output tile, K chunk)
+    // unit u: output tile u / ksplit, k-blocks [kb0, kb0 + nkb); split passes (A, B), (A2, B), (A, B2) per k-block
+    auto unit_k = [&](int u, int& kb0, int& nkb) {
+        kb0 = (u % p.ksplit) * kchunk;
+        nkb = min(kchunk, kblocks - kb0);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -87,7 +98,10 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
         fence_mbar_init();
     }
     if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-    if (warp == 0 && lane == 0) { prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmOut); }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmOut);
+        if (p.splits > 1) { prefetch_tmap(&tmA2); prefetch_tmap(&tmB2); }
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -98,24 +112,31 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
             uint32_t g = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-                for (int kb = 0; kb < iters; ++kb, ++g) {
+                const int ot = tile / p.ksplit;
+                const int m0 = (ot / tiles_n) * BM, n0 = (ot % tiles_n) * BN;
+                int kb0, nkb;
+                unit_k(tile, kb0, nkb);
+                const int iters = nkb * p.splits;
+                for (int it = 0; it < iters; ++it, ++g) {
                     const int s = g % STAGES;
+                    const int seg = it / nkb, kb = kb0 + it - seg * nkb;
+                    const CUtensorMap* mA = seg == 1 ? &tmA2 : &tmA;
+                    const CUtensorMap* mB = seg == 2 ? &tmB2 : &tmB;
                     if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
                     mbar_arrive_expect_tx(full + s, C::STAGE_BYTES);
                     uint8_t* a = sA + s * C::A_BYTES;
                     uint8_t* b = sB + s * C::B_BYTES;
                     if constexpr (A_MN) {
 #pragma unroll
-                        for (int j = 0; j < BM / 64; ++j) tma_load_2d(a + j * (BK * 128), &tmA, full + s, m0 + 64 * j, kb * BK);
+                        for (int j = 0; j < BM / 64; ++j) tma_load_2d(a + j * (BK * 128), mA, full + s, m0 + 64 * j, kb * BK);
                     } else {
-                        tma_load_2d(a, &tmA, full + s, kb * BK, m0);
+                        tma_load_2d(a, mA, full + s, kb * BK, m0);
                     }
                     if constexpr (B_MN) {
 #pragma unroll
-                        for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * (BK * 128), &tmB, full + s, n0 + 64 * j, kb * BK);
+                        for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * (BK * 128), mB, full + s, n0 + 64 * j, kb * BK);
                     } else {
-                        tma_load_2d(b, &tmB, full + s, kb * BK, n0);
+                        tma_load_2d(b, mB, full + s, kb * BK, n0);
                     }
                 }
             }
@@ -128,6 +149,9 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
                 const int buf = ti & 1;
                 if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();
+                int kb0, nkb;
+                unit_k(tile, kb0, nkb);
+                const int iters = nkb * p.splits;
                 for (int kb = 0; kb < iters; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
@@ -153,7 +177,9 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
         uint32_t ti = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
             const int buf = ti & 1;
-            const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+            const int ot = tile / p.ksplit;
+            const int m0 = (ot / tiles_n) * BM, n0 = (ot % tiles_n) * BN;
+            const float* bias = tile % p.ksplit == 0 ? p.bias : nullptr;   // once per output tile
             if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
             const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
@@ -177,10 +203,10 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
                             const int j = q * 8 + 2 * t;
                             float lo = __uint_as_float(j < 32 ? v0[j] : v1[j - 32]);
                             float hi = __uint_as_float(j + 1 < 32 ? v0[j + 1] : v1[j + 1 - 32]);
-                            if (p.bias) {
+                            if (bias) {
                                 const int col = gc0 + c * 64 + j;
-                                lo += col < p.N ? __ldg(p.bias + col) : 0.0f;
-                                hi += col + 1 < p.N ? __ldg(p.bias + col + 1) : 0.0f;
+                                lo += col < p.N ? __ldg(bias + col) : 0.0f;
+                                hi += col + 1 < p.N ? __ldg(bias + col + 1) : 0.0f;
                             }
                             __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
                             w[t] = *reinterpret_cast<uint32_t*>(&h);
@@ -207,9 +233,9 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
                         for (int t = 0; t < 4; ++t) {
                             const int j = q * 4 + t;
                             float x = __uint_as_float(v[j]);
-                            if (p.bias) {
+                            if (bias) {
                                 const int col = gc0 + c * 32 + j;
-                                x += col < p.N ? __ldg(p.bias + col) : 0.0f;
+                                x += col < p.N ? __ldg(bias + col) : 0.0f;
                             }
                             fp[t] = x;
                         }
@@ -242,14 +268,20 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
 template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
 static int launch(const Args& a, cudaStream_t stream) {
     using C = Cfg<BN, STAGES>;
-    CUtensorMap tA, tB, tO;
-    int rc;
-    if (A_MN) rc = make_tmap_2d(&tA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
-    else rc = make_tmap_2d(&tA, a.A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
-    if (!rc) {
-        if (B_MN) rc = make_tmap_2d(&tB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, static_cast<uint64_t>(a.ldb) * 2, BK, 64);
-        else rc = make_tmap_2d(&tB, a.B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, BN, BK);
-    }
+    CUtensorMap tA, tB, tA2, tB2, tO;
+    const bool split = a.A2 && a.B2;
+    auto map_a = [&](CUtensorMap* m, const void* ptr) {
+        if (A_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
+        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
+    };
+    auto map_b = [&](CUtensorMap* m, const void* ptr) {
+        if (B_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, static_cast<uint64_t>(a.ldb) * 2, BK, 64);
+        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, BN, BK);
+    };
+    int rc = map_a(&tA, a.A);
+    if (!rc) rc = map_b(&tB, a.B);
+    if (!rc) rc = map_a(&tA2, split ? a.A2 : a.A);
+    if (!rc) rc = map_b(&tB2, split ? a.B2 : a.B);
     if (!rc) {
         if (EPI == EPI_BF16)
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
@@ -269,8 +301,18 @@ static int launch(const Args& a, cudaStream_t stream) {
     }
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
     const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
-    KParams p{a.M, a.N, a.K, a.bias, a.err};
-    kern<<<tiles < nsm ? tiles : nsm, C::THREADS, C::SMEM, stream>>>(tA, tB, tO, p);
+    // Few output tiles over a long K (weight gradients: K = tokens) leave most SMs idle: an accumulating output
+    // splits K into chunks of at least 4 k-blocks whose partial tiles reduce-add into it.
+    int ksplit = 1;
+    if (EPI == EPI_F32_ADD && a.ksplit_ok && tiles < nsm) {
+        const int kblocks = (a.K + BK - 1) / BK;
+        ksplit = std::max(1, std::min((2 * nsm + tiles - 1) / tiles, kblocks / 4));
+        const int kchunk = (kblocks + ksplit - 1) / ksplit;
+        ksplit = (kblocks + kchunk - 1) / kchunk;   // every chunk non-empty: the last starts below kblocks
+    }
+    const int units = tiles * ksplit;
+    KParams p{a.M, a.N, a.K, split ? 3 : 1, ksplit, a.bias, a.err};
+    kern<<<units < nsm ? units : nsm, C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tO, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -287,7 +329,9 @@ static int dispatch_major(const Args& a, cudaStream_t s) {
 int gemm(const Args& a, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return OK;
     if (a.K <= 0) { set_error("bf16 product needs K > 0"); return ERR_ARGUMENT; }
-    const uintptr_t al = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.out);
+    if ((a.A2 != nullptr) != (a.B2 != nullptr)) { set_error("split product needs both low parts"); return ERR_ARGUMENT; }
+    const uintptr_t al = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.out) |
+                         reinterpret_cast<uintptr_t>(a.A2) | reinterpret_cast<uintptr_t>(a.B2);
     if ((al & 15) || (a.lda & 7) || (a.ldb & 7) || (a.epi == EPI_BF16 ? (a.ldo & 7) : (a.ldo & 3))) {
         set_error("bf16 product operands need 16-byte aligned bases and row strides");
         return ERR_ARGUMENT;

