@@ -3,8 +3,8 @@
 // Replaces Ops.AttentionForward/ForwardUnit and Ops.AttentionBackward/BackwardUnit with Rotary
 // (Laya.Training/Ops.cs:260-504):
 //   * per (segment, head), positions restarting at 0 in every segment; sliding layers see [i - W, i + W];
-//   * rotary (rotate half) applied to q and k as tiles are loaded; the backward rotates dq and dk back
-//     (Rotary.Apply with inverse: true) before writing them;
+//   * rotary (rotate half) is applied once per layer by the prep pass (q and k at their segment positions, fp32
+//     arithmetic as Rotary.Apply); the backward rotates dq and dk back (Rotary.Apply with inverse: true);
 //   * dropout on the probabilities (the decision head's layers in training) by the reference's counter hash
 //     Ops.Uniform(seed, (head << 42) | (row << 21) | key) with row the token's index in the batch and key the key's
 //     position in its segment, so masks are the reference's bit for bit;
@@ -13,10 +13,12 @@
 //       dV_j = Σ_i P_ij mask_ij dO_i;  dQ_i = Σ_j dS_ij k_j;  dK_j = Σ_i dS_ij q_i
 //     split into a query-tile kernel (dQ) and a key-tile kernel (dK, dV), each recomputing P: no atomics, so the
 //     gradients are deterministic.
-// Tiles are 64 queries × 64 keys; each of the 4 warps owns 16 rows; mma.sync m16n8k16 bf16 → fp32.
-// The accurate forward (qkv32 set) reads fp32 q, k, v and forms every product from bf16 hi/lo parts (three MMAs per
-// product), writing the context as hi and lo; the backward then reads the same fp32 q, k, v rounded to bf16.
-#include <type_traits>
+// Tiles are 64 queries × 64 keys; each of the 4 warps owns 16 rows; mma.sync m16n8k16 bf16 → fp32.  The streamed
+// operand (K/V in the forward and dQ kernels, Q/dO in the dK/dV kernel) is double-buffered with cp.async so the next
+// tile lands while the current one is multiplied.
+// The accurate forward (qkv_lo set) forms every product from bf16 hi/lo parts (three MMAs per product: scores and
+// P·V) and writes the context as hi and lo; the backward reads the hi parts.
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -26,7 +28,8 @@ namespace laya {
 namespace fa {
 
 constexpr int T64 = 64;
-constexpr int LDS = 64 + 8;   // smem row stride (bf16) to spread banks
+constexpr int LDS = 64 + 8;   // smem row stride (bf16): 144 bytes, 16-byte aligned rows, ldmatrix conflict-free
+constexpr int TILE = T64 * LDS;
 constexpr float LOG2E = 1.4426950408889634f;
 
 DEVI void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -62,9 +65,30 @@ DEVI float drop_mult(const Args& a, int head, int row, int key) {
     return dropout_uniform(a.seed, idx) < a.dropout ? 0.0f : a.keep;
 }
 
-// Loads 64 rows of one head's slice (columns col0 .. col0+HD) at segment positions [p0, p0+64) from a [T, ld] buffer
-// (bf16, or fp32 in the accurate forward) into smem, rotating pairs (i, i+HD/2) in fp32 when cos/sin are given.  Rows
-// past `limit` are zero.  With `lo` (fp32 sources only) the bf16 remainder x − bf16(x) goes to a second tile.
+DEVI void cp_async16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+DEVI void cp_async4(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+DEVI void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+DEVI void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 64 rows × HD bf16 at segment positions [p0, p0 + 64) of a [T, ld] buffer into a [64][LDS] smem tile; rows at or
+// past `limit` are zero-filled (their source address is the segment's first row, never read).
+template <int HD>
+DEVI void cp_tile(__nv_bfloat16* dst, const __nv_bfloat16* base, int ld, int p0, int limit) {
+    constexpr int CH = HD / 8;
+    for (int it = threadIdx.x; it < T64 * CH; it += blockDim.x) {
+        const int r = it / CH, c = it % CH;
+        const bool ok = p0 + r < limit;
+        const __nv_bfloat16* src = base + (ok ? static_cast<size_t>(p0 + r) * ld : 0) + c * 8;
+        cp_async16(smem_u32(dst + r * LDS + c * 8), src, ok);
+    }
+}
+
+// fp32 / bf16 quads
 DEVI void load4(const __nv_bfloat16* p, float (&v)[4]) {
     const uint2 u = *reinterpret_cast<const uint2*>(p);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -85,35 +109,45 @@ DEVI uint2 pack4_lo(const float (&v)[4]) {
     return pack4(r);
 }
 
+// ------------------------------------------------------------------------------------------------ prep
+// q and k rotated at their segment positions (Rotary.Apply, Ops.cs:490-503, fp32), v copied; from fp32 or bf16
+// [T, lds]; to bf16 hi [T, ldd] (+ the low parts in the accurate forward).  One thread per 4 rotation pairs.  In place
+// (src == hi, bf16) is allowed: a thread writes only what it read.
 template <int HD, typename Src>
-DEVI void load_rows(__nv_bfloat16* dst, __nv_bfloat16* lo, const Src* base, int ld, int p0, int limit,
-                    const float* cosv, const float* sinv) {
-    constexpr int HALF = HD / 2, J = HALF / 4;   // 4 pairs per step
-    for (int it = threadIdx.x; it < 64 * J; it += blockDim.x) {
-        const int r = it / J, j = it % J;
-        const int pos = p0 + r;
-        float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-        if (pos < limit) {
-            const Src* src = base + static_cast<size_t>(pos) * ld;
-            load4(src + 4 * j, a);
-            load4(src + HALF + 4 * j, b);
-            if (cosv) {
+__global__ void prep_kernel(const Src* src, int lds, int T, int hidden, int heads, const int32_t* __restrict__ tok_item,
+                            const int32_t* __restrict__ seg_start, const float* __restrict__ cosv,
+                            const float* __restrict__ sinv, __nv_bfloat16* hi, __nv_bfloat16* __restrict__ lo, int ldd) {
+    constexpr int HALF = HD / 2, J = HALF / 4;
+    const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<size_t>(T) * heads * 3 * J) return;
+    const int j = static_cast<int>(idx % J);
+    size_t rest = idx / J;
+    const int part = static_cast<int>(rest % 3);
+    rest /= 3;
+    const int h = static_cast<int>(rest % heads);
+    const int t = static_cast<int>(rest / heads);
+    const int col = part * hidden + h * HD + 4 * j;
+    float a[4], b[4];
+    load4(src + static_cast<size_t>(t) * lds + col, a);
+    load4(src + static_cast<size_t>(t) * lds + col + HALF, b);
+    if (part < 2 && cosv) {
+        const int pos = t - seg_start[tok_item[t]];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float c = cosv[static_cast<size_t>(pos) * HALF + 4 * j + t];
-                    const float s = sinv[static_cast<size_t>(pos) * HALF + 4 * j + t];
-                    const float x = a[t], y = b[t];
-                    a[t] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
-                    b[t] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
-                }
-            }
+        for (int e = 0; e < 4; ++e) {
+            const float c = cosv[static_cast<size_t>(pos) * HALF + 4 * j + e];
+            const float s = sinv[static_cast<size_t>(pos) * HALF + 4 * j + e];
+            const float x = a[e], y = b[e];
+            a[e] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+            b[e] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
         }
-        *reinterpret_cast<uint2*>(dst + r * LDS + 4 * j) = pack4(a);
-        *reinterpret_cast<uint2*>(dst + r * LDS + HALF + 4 * j) = pack4(b);
-        if (lo) {
-            *reinterpret_cast<uint2*>(lo + r * LDS + 4 * j) = pack4_lo(a);
-            *reinterpret_cast<uint2*>(lo + r * LDS + HALF + 4 * j) = pack4_lo(b);
-        }
+    }
+    __nv_bfloat16* d = hi + static_cast<size_t>(t) * ldd + col;
+    *reinterpret_cast<uint2*>(d) = pack4(a);
+    *reinterpret_cast<uint2*>(d + HALF) = pack4(b);
+    if (lo) {
+        __nv_bfloat16* l = lo + static_cast<size_t>(t) * ldd + col;
+        *reinterpret_cast<uint2*>(l) = pack4_lo(a);
+        *reinterpret_cast<uint2*>(l + HALF) = pack4_lo(b);
     }
 }
 
@@ -163,19 +197,14 @@ DEVI void mma_pv(float (&out)[NT][4], const uint32_t (&pa)[8][2], const __nv_bfl
 DEVI bool visible(bool global, int W, int q, int k, int L) { return k < L && q < L && (global || (k >= q - W && k <= q + W)); }
 
 // ------------------------------------------------------------------------------------------------ forward
-// SPLIT (the accurate forward): q, k, v come from fp32 and every product is taken as hi·hi + lo·hi + hi·lo of bf16
-// parts (scores and P·V), so the context is fp32-accurate; it is written as bf16 hi and lo parts.
+// SPLIT (the accurate forward): scores = qh·kh + ql·kh + qh·kl, context = Ph·vh + Pl·vh + Ph·vl, written as hi and lo.
 template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
-    constexpr int KS = HD / 16, NT = HD / 8, TILE = T64 * LDS;
-    using Src = typename std::conditional<SPLIT, float, __nv_bfloat16>::type;
+    constexpr int KS = HD / 16, NT = HD / 8;
+    constexpr int NQ = SPLIT ? 2 : 1, NB = SPLIT ? 4 : 2;   // Q tiles; tiles per K/V stage (K, V, K lo, V lo)
     extern __shared__ __align__(16) __nv_bfloat16 fsm[];
     __nv_bfloat16* Qs = fsm;
-    __nv_bfloat16* Ks = fsm + TILE;
-    __nv_bfloat16* Vs = fsm + 2 * TILE;
-    __nv_bfloat16* Ql = SPLIT ? fsm + 3 * TILE : nullptr;
-    __nv_bfloat16* Kl = SPLIT ? fsm + 4 * TILE : nullptr;
-    __nv_bfloat16* Vl = SPLIT ? fsm + 5 * TILE : nullptr;
+    __nv_bfloat16* stage0 = fsm + NQ * TILE;
     const int tile = blockIdx.x;
     if (tile >= *a.n_tiles) return;
     const int head = blockIdx.y, item = a.tile_item[tile], q0 = a.tile_p0[tile];
@@ -183,31 +212,53 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const Src* qb = (SPLIT ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
-                    static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD, Src>(Qs, Ql, qb, a.ld, q0, L, a.cosv, a.sinv);
-    __syncthreads();
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    const __nv_bfloat16* lb = SPLIT ? a.qkv_lo + static_cast<size_t>(seg0) * a.ld + head * HD : nullptr;
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
+    const int nk = (ke - kb + T64 - 1) / T64;
+    auto load_kv = [&](int j) {
+        __nv_bfloat16* d = stage0 + (j & 1) * NB * TILE;
+        const int k0 = kb + j * T64;
+        cp_tile<HD>(d, qb + a.hidden, a.ld, k0, ke);
+        cp_tile<HD>(d + TILE, qb + 2 * a.hidden, a.ld, k0, ke);
+        if constexpr (SPLIT) {
+            cp_tile<HD>(d + 2 * TILE, lb + a.hidden, a.ld, k0, ke);
+            cp_tile<HD>(d + 3 * TILE, lb + 2 * a.hidden, a.ld, k0, ke);
+        }
+    };
+    cp_tile<HD>(Qs, qb, a.ld, q0, L);
+    if constexpr (SPLIT) cp_tile<HD>(Qs + TILE, lb, a.ld, q0, L);
+    load_kv(0);
+    cp_commit();
     uint32_t fq[KS][4], fql[SPLIT ? KS : 1][4];
-    load_a_frags<KS>(Qs, warp, lane, fq);
-    if constexpr (SPLIT) load_a_frags<KS>(Ql, warp, lane, fql);
     float o[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
-    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
-    for (int k0 = kb; k0 < ke; k0 += T64) {
+    for (int jt = 0; jt < nk; ++jt) {
+        if (jt + 1 < nk) {
+            load_kv(jt + 1);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
         __syncthreads();
-        load_rows<HD, Src>(Ks, Kl, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
-        load_rows<HD, Src>(Vs, Vl, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
-        __syncthreads();
+        if (jt == 0) {
+            load_a_frags<KS>(Qs, warp, lane, fq);
+            if constexpr (SPLIT) load_a_frags<KS>(Qs + TILE, warp, lane, fql);
+        }
+        const __nv_bfloat16* Ks = stage0 + (jt & 1) * NB * TILE;
+        const __nv_bfloat16* Vs = Ks + TILE;
+        const int k0 = kb + jt * T64;
         float s[8][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
         mma_abt<KS>(s, fq, Ks, lane);
         if constexpr (SPLIT) {
             mma_abt<KS>(s, fql, Ks, lane);
-            mma_abt<KS>(s, fq, Kl, lane);
+            mma_abt<KS>(s, fq, Ks + 2 * TILE, lane);
         }
         float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -261,8 +312,9 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
         mma_pv<NT>(o, pa, Vs, lane);
         if constexpr (SPLIT) {
             mma_pv<NT>(o, pl, Vs, lane);
-            mma_pv<NT>(o, pa, Vl, lane);
+            mma_pv<NT>(o, pa, Ks + 3 * TILE, lane);
         }
+        __syncthreads();   // this stage is refilled by the prefetch two tiles on
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -331,14 +383,14 @@ DEVI void store_rows(float (&acc)[NT][4], __nv_bfloat16* base, int ld, int seg0,
     }
 }
 
-// dQ for one 64-query tile of one head.
-template <int HD, typename Src>
+// dQ for one 64-query tile of one head; K/V tiles double-buffered.
+template <int HD>
 __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
     constexpr int KS = HD / 16, NT = HD / 8;
-    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 dOs[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
+    extern __shared__ __align__(16) __nv_bfloat16 fsm[];
+    __nv_bfloat16* Qs = fsm;
+    __nv_bfloat16* dOs = fsm + TILE;
+    __nv_bfloat16* stage0 = fsm + 2 * TILE;   // [2][K, V]
     const int tile = blockIdx.x;
     if (tile >= *a.n_tiles) return;
     const int head = blockIdx.y, item = a.tile_item[tile], q0 = a.tile_p0[tile];
@@ -346,15 +398,18 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const Src* qb = (sizeof(Src) == 4 ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
-                    static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD, Src>(Qs, nullptr, qb, a.ld, q0, L, a.cosv, a.sinv);
-    load_rows<HD, __nv_bfloat16>(dOs, nullptr, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, L,
-                                 nullptr, nullptr);
-    __syncthreads();
-    uint32_t fq[KS][4], fdo[KS][4];
-    load_a_frags<KS>(Qs, warp, lane, fq);
-    load_a_frags<KS>(dOs, warp, lane, fdo);
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
+    const int nk = (ke - kb + T64 - 1) / T64;
+    auto load_kv = [&](int j) {
+        __nv_bfloat16* d = stage0 + (j & 1) * 2 * TILE;
+        cp_tile<HD>(d, qb + a.hidden, a.ld, kb + j * T64, ke);
+        cp_tile<HD>(d + TILE, qb + 2 * a.hidden, a.ld, kb + j * T64, ke);
+    };
+    cp_tile<HD>(Qs, qb, a.ld, q0, L);
+    cp_tile<HD>(dOs, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, L);
+    load_kv(0);
+    cp_commit();
     const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
     float lse[2], dd[2];
 #pragma unroll
@@ -363,15 +418,26 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
         lse[h] = ok ? a.lse[static_cast<size_t>(seg0 + qp[h]) * a.heads + head] : 0.f;
         dd[h] = ok ? a.dsum[static_cast<size_t>(seg0 + qp[h]) * a.heads + head] : 0.f;
     }
+    uint32_t fq[KS][4], fdo[KS][4];
     float dq[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) dq[j][0] = dq[j][1] = dq[j][2] = dq[j][3] = 0.f;
-    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + T64 + W);
-    for (int k0 = kb; k0 < ke; k0 += T64) {
+    for (int jt = 0; jt < nk; ++jt) {
+        if (jt + 1 < nk) {
+            load_kv(jt + 1);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
         __syncthreads();
-        load_rows<HD, Src>(Ks, nullptr, qb + a.hidden, a.ld, k0, ke, a.cosv, a.sinv);
-        load_rows<HD, Src>(Vs, nullptr, qb + 2 * a.hidden, a.ld, k0, ke, nullptr, nullptr);
-        __syncthreads();
+        if (jt == 0) {
+            load_a_frags<KS>(Qs, warp, lane, fq);
+            load_a_frags<KS>(dOs, warp, lane, fdo);
+        }
+        const __nv_bfloat16* Ks = stage0 + (jt & 1) * 2 * TILE;
+        const __nv_bfloat16* Vs = Ks + TILE;
+        const int k0 = kb + jt * T64;
         float s[8][4], dp[8][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -396,19 +462,20 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(Args a) {
             pa[j][1] = pack_bf16(ds[2], ds[3]);
         }
         mma_pv<NT>(dq, pa, Ks, lane);
+        __syncthreads();
     }
     store_rows<NT>(dq, a.dqkv + head * HD, a.lddq, seg0, q0, warp, lane, L, a.cosv, a.sinv);
 }
 
-// dK and dV for one 64-key tile of one head.
-template <int HD, typename Src>
+// dK and dV for one 64-key tile of one head; Q/dO tiles (with their rows' lse and D) double-buffered.
+template <int HD>
 __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
     constexpr int KS = HD / 16, NT = HD / 8;
-    __shared__ __align__(16) __nv_bfloat16 Ks[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Vs[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 Qs[T64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 dOs[T64 * LDS];
-    __shared__ float lse_s[T64], dd_s[T64];
+    extern __shared__ __align__(16) __nv_bfloat16 fsm[];
+    __nv_bfloat16* Ks = fsm;
+    __nv_bfloat16* Vs = fsm + TILE;
+    __nv_bfloat16* stage0 = fsm + 2 * TILE;                            // [2][Q, dO]
+    float* rows0 = reinterpret_cast<float*>(fsm + 6 * TILE);          // [2][lse 64, D 64]
     const int tile = blockIdx.x;
     if (tile >= *a.n_tiles) return;
     const int head = blockIdx.y, item = a.tile_item[tile], k0 = a.tile_p0[tile];
@@ -416,32 +483,52 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const bool global = a.window < 0;
     const int W = a.window;
-    const Src* qb = (sizeof(Src) == 4 ? reinterpret_cast<const Src*>(a.qkv32) : reinterpret_cast<const Src*>(a.qkv)) +
-                    static_cast<size_t>(seg0) * a.ld + head * HD;
-    load_rows<HD, Src>(Ks, nullptr, qb + a.hidden, a.ld, k0, L, a.cosv, a.sinv);
-    load_rows<HD, Src>(Vs, nullptr, qb + 2 * a.hidden, a.ld, k0, L, nullptr, nullptr);
-    __syncthreads();
+    const __nv_bfloat16* qb = a.qkv + static_cast<size_t>(seg0) * a.ld + head * HD;
+    const __nv_bfloat16* ob = a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD;
+    const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + T64 + W);
+    const int nq = (qe - qb0 + T64 - 1) / T64;
+    auto load_q = [&](int j) {
+        __nv_bfloat16* d = stage0 + (j & 1) * 2 * TILE;
+        float* rr = rows0 + (j & 1) * 2 * T64;
+        const int q0 = qb0 + j * T64;
+        cp_tile<HD>(d, qb, a.ld, q0, qe);
+        cp_tile<HD>(d + TILE, ob, a.ldo, q0, qe);
+        for (int r = threadIdx.x; r < T64; r += blockDim.x) {
+            const bool ok = q0 + r < qe;
+            const size_t at = ok ? static_cast<size_t>(seg0 + q0 + r) * a.heads + head : 0;
+            cp_async4(smem_u32(rr + r), a.lse + at, ok);
+            cp_async4(smem_u32(rr + T64 + r), a.dsum + at, ok);
+        }
+    };
+    cp_tile<HD>(Ks, qb + a.hidden, a.ld, k0, L);
+    cp_tile<HD>(Vs, qb + 2 * a.hidden, a.ld, k0, L);
+    load_q(0);
+    cp_commit();
     uint32_t fk[KS][4], fv[KS][4];
-    load_a_frags<KS>(Ks, warp, lane, fk);
-    load_a_frags<KS>(Vs, warp, lane, fv);
     const int kp[2] = {k0 + warp * 16 + g, k0 + warp * 16 + g + 8};
     float dk[NT][4], dv[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) dk[j][e] = dv[j][e] = 0.f;
-    const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + T64 + W);
-    for (int q0 = qb0; q0 < qe; q0 += T64) {
-        __syncthreads();
-        load_rows<HD, Src>(Qs, nullptr, qb, a.ld, q0, qe, a.cosv, a.sinv);
-        load_rows<HD, __nv_bfloat16>(dOs, nullptr, a.dout + static_cast<size_t>(seg0) * a.ldo + head * HD, a.ldo, q0, qe,
-                                     nullptr, nullptr);
-        for (int r = threadIdx.x; r < T64; r += blockDim.x) {
-            const int q = q0 + r;
-            lse_s[r] = q < qe ? a.lse[static_cast<size_t>(seg0 + q) * a.heads + head] : 0.f;
-            dd_s[r] = q < qe ? a.dsum[static_cast<size_t>(seg0 + q) * a.heads + head] : 0.f;
+    for (int jt = 0; jt < nq; ++jt) {
+        if (jt + 1 < nq) {
+            load_q(jt + 1);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
         }
         __syncthreads();
+        if (jt == 0) {
+            load_a_frags<KS>(Ks, warp, lane, fk);
+            load_a_frags<KS>(Vs, warp, lane, fv);
+        }
+        const __nv_bfloat16* Qs = stage0 + (jt & 1) * 2 * TILE;
+        const __nv_bfloat16* dOs = Qs + TILE;
+        const float* lse_s = rows0 + (jt & 1) * 2 * T64;
+        const float* dd_s = lse_s + T64;
+        const int q0 = qb0 + jt * T64;
         // transposed scores: rows = this warp's 16 keys, columns = 64 queries
         float st[8][4], dpt[8][4];
 #pragma unroll
@@ -472,6 +559,7 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
         }
         mma_pv<NT>(dv, pm, dOs, lane);
         mma_pv<NT>(dk, dsa, Qs, lane);
+        __syncthreads();
     }
     store_rows<NT>(dk, a.dqkv + a.hidden + head * HD, a.lddq, seg0, k0, warp, lane, L, a.cosv, a.sinv);
     store_rows<NT>(dv, a.dqkv + 2 * a.hidden + head * HD, a.lddq, seg0, k0, warp, lane, L, nullptr, nullptr);
@@ -479,16 +567,46 @@ __global__ void __launch_bounds__(128) bwd_dkdv_kernel(Args a) {
 
 }  // namespace fa
 
-template <int HD, bool SPLIT>
-static int launch_fwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
-    const int smem = (SPLIT ? 6 : 3) * fa::T64 * fa::LDS * 2;
-    static bool attr[64] = {false};
+// ------------------------------------------------------------------------------------------------ launchers
+template <class K>
+static int set_smem(K kern, int bytes) {
+    static thread_local std::vector<std::pair<const void*, int>> done;   // (kernel, device) already configured
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
-        LAYA_CUDA(cudaFuncSetAttribute(fa::fwd_kernel<HD, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr[dev] = true;
+    for (auto& d : done)
+        if (d.first == reinterpret_cast<const void*>(kern) && d.second == dev) return OK;
+    LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.push_back({reinterpret_cast<const void*>(kern), dev});
+    return OK;
+}
+
+int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int heads, const int32_t* tok_item,
+              const int32_t* seg_start, const float* cosv, const float* sinv, __nv_bfloat16* hi, __nv_bfloat16* lo,
+              int ldd, cudaStream_t s) {
+    if (T <= 0) return OK;
+    const int hd = hidden / heads;
+    const size_t n = static_cast<size_t>(T) * heads * 3 * (hd / 8);
+    const unsigned g = static_cast<unsigned>((n + 255) / 256);
+    if (hd == 64) {
+        if (src_f32) fa::prep_kernel<64, float><<<g, 256, 0, s>>>(static_cast<const float*>(src), lds, T, hidden, heads, tok_item, seg_start, cosv, sinv, hi, lo, ldd);
+        else fa::prep_kernel<64, __nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(src), lds, T, hidden, heads, tok_item, seg_start, cosv, sinv, hi, lo, ldd);
+    } else if (hd == 32) {
+        if (src_f32) fa::prep_kernel<32, float><<<g, 256, 0, s>>>(static_cast<const float*>(src), lds, T, hidden, heads, tok_item, seg_start, cosv, sinv, hi, lo, ldd);
+        else fa::prep_kernel<32, __nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(src), lds, T, hidden, heads, tok_item, seg_start, cosv, sinv, hi, lo, ldd);
+    } else {
+        set_error("attention supports head_dim 32 and 64");
+        return ERR_NOT_SUPPORTED;
     }
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+template <int HD, bool SPLIT>
+static int launch_fwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    const int smem = (SPLIT ? 10 : 5) * fa::TILE * 2;
+    int rc = set_smem(fa::fwd_kernel<HD, SPLIT>, smem);
+    if (rc) return rc;
     fa::fwd_kernel<HD, SPLIT><<<dim3(max_tiles, a.heads), 128, smem, s>>>(a);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
@@ -498,7 +616,7 @@ static int launch_fwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
     if (max_tiles <= 0) return OK;
     const int hd = a.hidden / a.heads;
-    const bool split = a.qkv32 != nullptr;
+    const bool split = a.qkv_lo != nullptr;
     if (split && !a.out_lo) { set_error("accurate attention needs the context's low part"); return ERR_ARGUMENT; }
     if (hd == 64) return split ? launch_fwd<64, true>(a, max_tiles, s) : launch_fwd<64, false>(a, max_tiles, s);
     if (hd == 32) return split ? launch_fwd<32, true>(a, max_tiles, s) : launch_fwd<32, false>(a, max_tiles, s);
@@ -506,11 +624,16 @@ int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
     return ERR_NOT_SUPPORTED;
 }
 
-template <int HD, typename Src>
-static void launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
+template <int HD>
+static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
+    const int smem_dq = 6 * fa::TILE * 2, smem_kv = 6 * fa::TILE * 2 + 4 * fa::T64 * 4;
+    int rc = set_smem(fa::bwd_dq_kernel<HD>, smem_dq);
+    if (!rc) rc = set_smem(fa::bwd_dkdv_kernel<HD>, smem_kv);
+    if (rc) return rc;
     dim3 grid(max_tiles, a.heads);
-    fa::bwd_dq_kernel<HD, Src><<<grid, 128, 0, s>>>(a);
-    fa::bwd_dkdv_kernel<HD, Src><<<grid, 128, 0, s>>>(a);
+    fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a);
+    fa::bwd_dkdv_kernel<HD><<<grid, 128, smem_kv, s>>>(a);
+    return OK;
 }
 
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
@@ -519,10 +642,11 @@ int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
     const long long warps = static_cast<long long>(T) * a.heads;
     fa::bwd_dot_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(a, T);
     count_launch();
-    const bool f32 = a.qkv32 != nullptr;
-    if (hd == 64) { if (f32) launch_bwd<64, float>(a, max_tiles, s); else launch_bwd<64, __nv_bfloat16>(a, max_tiles, s); }
-    else if (hd == 32) { if (f32) launch_bwd<32, float>(a, max_tiles, s); else launch_bwd<32, __nv_bfloat16>(a, max_tiles, s); }
+    int rc;
+    if (hd == 64) rc = launch_bwd<64>(a, max_tiles, s);
+    else if (hd == 32) rc = launch_bwd<32>(a, max_tiles, s);
     else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
+    if (rc) return rc;
     count_launch(2);
     LAYA_CUDA(cudaGetLastError());
     return OK;

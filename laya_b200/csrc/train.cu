@@ -184,14 +184,16 @@ struct laya_trainer {
     int Tc = 0, Mc = 0, Nc = 0, tiles_cap = 0;
     // tape
     std::vector<float*> X, X1, mean1, rstd1, mean2, rstd2, lse;
-    std::vector<bf16*> n1, qkv, ctx, n2, wide, act;          // bf16 (qkv, wide: the BF16 forward only)
+    std::vector<bf16*> n1, qkv, ctx, n2, wide, act;          // bf16; qkv with q, k rotated (wide: BF16 forward only)
     std::vector<bf16*> n1lo, ctxlo, n2lo, actlo;             // accurate forward: low parts
-    std::vector<float*> qkv32, wide32;                       // accurate forward: fp32 product outputs
+    std::vector<float*> wide32;                              // accurate forward: fp32 GeGLU input
+    float* ws_qkv32 = nullptr;                               // accurate forward: fp32 qkv of the current layer
+    bf16* ws_qkvlo = nullptr;                                //   and the low parts of its rotated q, k, v
     float *emb_mean = nullptr, *emb_rstd = nullptr, *f_mean = nullptr, *f_rstd = nullptr;
     std::vector<float*> HIN, HX1, hm1, hr1, hm2, hr2, hlse;
     std::vector<bf16*> hn1, hqkv, hctx, hn2, hpre, hact;
     std::vector<bf16*> hn1lo, hctxlo, hn2lo, hactlo;
-    std::vector<float*> hqkv32, hpre32;
+    std::vector<float*> hpre32;
     bf16* sn16 = nullptr;
     bf16* snlo = nullptr;
     float *smean = nullptr, *srstd = nullptr, *spre = nullptr, *logits = nullptr, *dlog = nullptr;
@@ -371,11 +373,11 @@ int lin_dw(laya_trainer* t, int T, int N, int K, const bf16* dy, const bf16* x, 
     return bf::gemm(a, t->stream);
 }
 
-fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const float* qkv32, int heads, int window,
+fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const bf16* qkv_lo, int heads, int window,
                    const float* cosv, const float* sinv, float dropout, uint64_t seed, bf16* out, bf16* out_lo,
                    float* lse) {
     fa::Args a{};
-    a.qkv = qkv; a.qkv32 = qkv32; a.out_lo = out_lo; a.ld = 3 * t->H; a.hidden = t->H; a.heads = heads;
+    a.qkv = qkv; a.qkv_lo = qkv_lo; a.out_lo = out_lo; a.ld = 3 * t->H; a.hidden = t->H; a.heads = heads;
     a.seg_start = b->seg_start; a.seg_len = b->seg_len;
     a.tile_item = b->tile_item; a.tile_p0 = b->tile_p0; a.n_tiles = b->n_tiles;
     a.window = window;
@@ -427,11 +429,20 @@ int enc_forward(laya_trainer* t, const laya_batch* b, int l) {
     } else {
         RC(ln_fwd(ln_args(t, T, t->X[l], p.n1, NONE, t->eps, t->n1[l], n1lo, nullptr, t->mean1[l], t->rstd1[l]), s));
     }
-    if (pr) RC(lin_fwd(t, T, 3 * H, H, t->n1[l], n1lo, p.qkv, nullptr, bf::EPI_F32, t->qkv32[l]));
-    else RC(lin_fwd(t, T, 3 * H, H, t->n1[l], nullptr, p.qkv, nullptr, bf::EPI_BF16, t->qkv[l]));
     const bool g = t->global[l];
-    fa::Args att = attn_args(t, b, at(t->qkv, l), at(t->qkv32, l), t->heads, g ? -1 : t->window,
-                             g ? t->cos_g : t->cos_l, g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], ctxlo, t->lse[l]);
+    const float* cosv = g ? t->cos_g : t->cos_l;
+    const float* sinv = g ? t->sin_g : t->sin_l;
+    if (pr) {   // fp32 qkv → rotated bf16 hi (kept for the backward) and lo (this forward only)
+        RC(lin_fwd(t, T, 3 * H, H, t->n1[l], n1lo, p.qkv, nullptr, bf::EPI_F32, t->ws_qkv32));
+        RC(attn_prep(t->ws_qkv32, 1, 3 * H, T, H, t->heads, b->tok_item, b->seg_start, cosv, sinv, t->qkv[l],
+                     t->ws_qkvlo, 3 * H, s));
+    } else {    // bf16 qkv rotated in place
+        RC(lin_fwd(t, T, 3 * H, H, t->n1[l], nullptr, p.qkv, nullptr, bf::EPI_BF16, t->qkv[l]));
+        RC(attn_prep(t->qkv[l], 0, 3 * H, T, H, t->heads, b->tok_item, b->seg_start, cosv, sinv, t->qkv[l], nullptr,
+                     3 * H, s));
+    }
+    fa::Args att = attn_args(t, b, t->qkv[l], pr ? t->ws_qkvlo : nullptr, t->heads, g ? -1 : t->window, cosv, sinv,
+                             0.f, 0, t->ctx[l], ctxlo, t->lse[l]);
     RC(flash_forward(att, b->tiles, s));
     LAYA_CUDA(cudaMemcpyAsync(t->X1[l], t->X[l], sizeof(float) * T * H, cudaMemcpyDeviceToDevice, s));
     RC(lin_fwd(t, T, H, H, t->ctx[l], ctxlo, p.wo, nullptr, bf::EPI_F32_ADD, t->X1[l]));
@@ -458,10 +469,15 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
     const bool pr = t->precise;
     bf16 *n1lo = at(t->hn1lo, l), *n2lo = at(t->hn2lo, l), *ctxlo = at(t->hctxlo, l), *actlo = at(t->hactlo, l);
     RC(ln_fwd(ln_args(t, T, t->HIN[l], p.n1w, p.n1b, 1e-5f, t->hn1[l], n1lo, nullptr, t->hm1[l], t->hr1[l]), s));
-    if (pr) RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, bf::EPI_F32, t->hqkv32[l]));
-    else RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], nullptr, p.inw, t->master + p.inb, bf::EPI_BF16, t->hqkv[l]));
+    if (pr) {   // no rotary in the head: the prep only splits fp32 qkv into hi and lo
+        RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, bf::EPI_F32, t->ws_qkv32));
+        RC(attn_prep(t->ws_qkv32, 1, 3 * H, T, H, t->HH, b->tok_item, b->seg_start, nullptr, nullptr, t->hqkv[l],
+                     t->ws_qkvlo, 3 * H, s));
+    } else {
+        RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], nullptr, p.inw, t->master + p.inb, bf::EPI_BF16, t->hqkv[l]));
+    }
     const tr::Mask m0 = head_mask(t, l, 0);
-    fa::Args att = attn_args(t, b, at(t->hqkv, l), at(t->hqkv32, l), t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
+    fa::Args att = attn_args(t, b, t->hqkv[l], pr ? t->ws_qkvlo : nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
                              t->hctx[l], ctxlo, t->hlse[l]);
     RC(flash_forward(att, b->tiles, s));
     RC(lin_fwd(t, T, H, H, t->hctx[l], ctxlo, p.outw, t->master + p.outb, bf::EPI_F32, t->R32));
@@ -546,8 +562,8 @@ int head_backward(laya_trainer* t, const laya_batch* b, int l) {
     RC(colsum_bf16(t->d16, T, H, G + p.outb, s));
     RC(lin_dx(t, T, H, H, t->d16, p.outw, bf::EPI_BF16, t->dctx16));
     const tr::Mask m0 = head_mask(t, l, 0);
-    fa::Args att = attn_args(t, b, at(t->hqkv, l), at(t->hqkv32, l), t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
-                             t->hctx[l], nullptr, t->hlse[l]);
+    fa::Args att = attn_args(t, b, t->hqkv[l], nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l],
+                             nullptr, t->hlse[l]);
     RC(flash_backward(att, b->tiles, T, s));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->hn1[l], p.inw));
     RC(colsum_bf16(t->dqkv16, T, 3 * H, G + p.inb, s));
@@ -576,8 +592,8 @@ int enc_backward(laya_trainer* t, const laya_batch* b, int l, bool need_dx) {
     RC(lin_dw(t, T, H, H, t->d16, t->ctx[l], p.wo));
     RC(lin_dx(t, T, H, H, t->d16, p.wo, bf::EPI_BF16, t->dctx16));
     const bool g = t->global[l];
-    fa::Args att = attn_args(t, b, at(t->qkv, l), at(t->qkv32, l), t->heads, g ? -1 : t->window,
-                             g ? t->cos_g : t->cos_l, g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], nullptr, t->lse[l]);
+    fa::Args att = attn_args(t, b, t->qkv[l], nullptr, t->heads, g ? -1 : t->window, g ? t->cos_g : t->cos_l,
+                             g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], nullptr, t->lse[l]);
     RC(flash_backward(att, b->tiles, T, s));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->n1[l], p.qkv));
     if (p.n1 == NONE) {
@@ -729,24 +745,25 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
         if ((rc = dalloc_t(t, &t->X[l], T * H))) return fail(rc);
     const bool pr = t->precise;
     if (pr) {
-        t->n1lo.resize(L); t->ctxlo.resize(L); t->n2lo.resize(L); t->actlo.resize(L); t->qkv32.resize(L);
-        t->wide32.resize(L);
+        t->n1lo.resize(L); t->ctxlo.resize(L); t->n2lo.resize(L); t->actlo.resize(L); t->wide32.resize(L);
+        if ((rc = dalloc_t(t, &t->ws_qkv32, T * 3 * H)) || (rc = dalloc_t(t, &t->ws_qkvlo, T * 3 * H))) return fail(rc);
     } else {
-        t->qkv.resize(L); t->wide.resize(L);
+        t->wide.resize(L);
     }
     for (int l = 0; l < L; ++l) {
         if ((rc = dalloc_t(t, &t->X1[l], T * H)) || (rc = dalloc_t(t, &t->mean1[l], T)) ||
             (rc = dalloc_t(t, &t->rstd1[l], T)) || (rc = dalloc_t(t, &t->mean2[l], T)) ||
             (rc = dalloc_t(t, &t->rstd2[l], T)) || (rc = dalloc_t(t, &t->lse[l], T * t->heads)) ||
             (rc = dalloc_t(t, &t->n1[l], T * H)) || (rc = dalloc_t(t, &t->ctx[l], T * H)) ||
-            (rc = dalloc_t(t, &t->n2[l], T * H)) || (rc = dalloc_t(t, &t->act[l], T * I)))
+            (rc = dalloc_t(t, &t->n2[l], T * H)) || (rc = dalloc_t(t, &t->act[l], T * I)) ||
+            (rc = dalloc_t(t, &t->qkv[l], T * 3 * H)))
             return fail(rc);
         if (pr) {
             if ((rc = dalloc_t(t, &t->n1lo[l], T * H)) || (rc = dalloc_t(t, &t->ctxlo[l], T * H)) ||
                 (rc = dalloc_t(t, &t->n2lo[l], T * H)) || (rc = dalloc_t(t, &t->actlo[l], T * I)) ||
-                (rc = dalloc_t(t, &t->qkv32[l], T * 3 * H)) || (rc = dalloc_t(t, &t->wide32[l], T * 2 * I)))
+                (rc = dalloc_t(t, &t->wide32[l], T * 2 * I)))
                 return fail(rc);
-        } else if ((rc = dalloc_t(t, &t->qkv[l], T * 3 * H)) || (rc = dalloc_t(t, &t->wide[l], T * 2 * I))) {
+        } else if ((rc = dalloc_t(t, &t->wide[l], T * 2 * I))) {
             return fail(rc);
         }
     }
@@ -754,12 +771,11 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
         (rc = dalloc_t(t, &t->f_rstd, T)))
         return fail(rc);
     t->HIN.resize(HL + 1); t->HX1.resize(HL); t->hm1.resize(HL); t->hr1.resize(HL); t->hm2.resize(HL); t->hr2.resize(HL);
-    t->hlse.resize(HL); t->hn1.resize(HL); t->hctx.resize(HL); t->hn2.resize(HL); t->hact.resize(HL);
+    t->hlse.resize(HL); t->hn1.resize(HL); t->hctx.resize(HL); t->hn2.resize(HL); t->hact.resize(HL); t->hqkv.resize(HL);
     if (pr) {
-        t->hn1lo.resize(HL); t->hctxlo.resize(HL); t->hn2lo.resize(HL); t->hactlo.resize(HL); t->hqkv32.resize(HL);
-        t->hpre32.resize(HL);
+        t->hn1lo.resize(HL); t->hctxlo.resize(HL); t->hn2lo.resize(HL); t->hactlo.resize(HL); t->hpre32.resize(HL);
     } else {
-        t->hqkv.resize(HL); t->hpre.resize(HL);
+        t->hpre.resize(HL);
     }
     for (int l = 0; l <= HL; ++l)
         if ((rc = dalloc_t(t, &t->HIN[l], T * H))) return fail(rc);
@@ -768,14 +784,14 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
             (rc = dalloc_t(t, &t->hm2[l], T)) || (rc = dalloc_t(t, &t->hr2[l], T)) ||
             (rc = dalloc_t(t, &t->hlse[l], T * t->HH)) || (rc = dalloc_t(t, &t->hn1[l], T * H)) ||
             (rc = dalloc_t(t, &t->hctx[l], T * H)) || (rc = dalloc_t(t, &t->hn2[l], T * H)) ||
-            (rc = dalloc_t(t, &t->hact[l], T * FF)))
+            (rc = dalloc_t(t, &t->hact[l], T * FF)) || (rc = dalloc_t(t, &t->hqkv[l], T * 3 * H)))
             return fail(rc);
         if (pr) {
             if ((rc = dalloc_t(t, &t->hn1lo[l], T * H)) || (rc = dalloc_t(t, &t->hctxlo[l], T * H)) ||
                 (rc = dalloc_t(t, &t->hn2lo[l], T * H)) || (rc = dalloc_t(t, &t->hactlo[l], T * FF)) ||
-                (rc = dalloc_t(t, &t->hqkv32[l], T * 3 * H)) || (rc = dalloc_t(t, &t->hpre32[l], T * FF)))
+                (rc = dalloc_t(t, &t->hpre32[l], T * FF)))
                 return fail(rc);
-        } else if ((rc = dalloc_t(t, &t->hqkv[l], T * 3 * H)) || (rc = dalloc_t(t, &t->hpre[l], T * FF))) {
+        } else if ((rc = dalloc_t(t, &t->hpre[l], T * FF))) {
             return fail(rc);
         }
     }

@@ -36,20 +36,26 @@ namespace laya {
 // ---- flash.cu
 namespace fa {
 struct Args {
-    const __nv_bfloat16* qkv; int ld; int hidden; int heads;        // [T, ld] with q | k | v at 0, hidden, 2·hidden
+    const __nv_bfloat16* qkv; int ld; int hidden; int heads;        // [T, ld] q | k | v at 0, hidden, 2·hidden; q, k rotated
     const int32_t* seg_start; const int32_t* seg_len;
     const int32_t* tile_item; const int32_t* tile_p0; const int32_t* n_tiles;   // 64-row tiles of every segment
     int window;                                                      // < 0: global
     float scale;                                                     // 1/sqrt(head_dim)
-    const float* cosv; const float* sinv;                            // [positions, head_dim/2] or null
+    const float* cosv; const float* sinv;                            // [positions, head_dim/2] or null: the backward's
+                                                                     // inverse rotation of dq and dk
     float dropout; float keep; uint64_t seed;                        // dropout on the probabilities
     __nv_bfloat16* out; int ldo; float* lse;                         // context [T, ldo] bf16, row log-sum-exp [T, heads]
     const __nv_bfloat16* dout; float* dsum;                          // backward: d context [T, ldo], Σ dO·O [T, heads]
     __nv_bfloat16* dqkv; int lddq;                                   // backward output [T, lddq]
-    const float* qkv32;                                              // accurate forward: fp32 [T, ld] (else null)
+    const __nv_bfloat16* qkv_lo;                                     // accurate forward: low parts of qkv (else null)
     __nv_bfloat16* out_lo;                                           // accurate forward: context low part
 };
 }  // namespace fa
+// q, k rotated at their segment positions (cosv null: no rotation), v copied, from fp32 or bf16 [T, lds] into bf16
+// hi [T, ldd] (+ lo parts when lo is set); in place when src == hi (bf16).
+int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int heads, const int32_t* tok_item,
+              const int32_t* seg_start, const float* cosv, const float* sinv, __nv_bfloat16* hi, __nv_bfloat16* lo,
+              int ldd, cudaStream_t s);
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s);
 
