@@ -1,18 +1,26 @@
 """Throughput of the hot path on B200s — one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|train|q8]
 
-Workload (config 2): the batched decision forward of a ModernBERT-base encoder + Laya decision
-head with every projection in Q8_0, 64 questions × 512 tokens per GPU (synthetic, seeded; laya_b200/workloads.py).
-A step is one forward over one such batch.  Inference shards by request: each rank runs its own batch with no
-collective on the data path (weak scaling); torch.distributed only brackets the timed region and takes the max of
-the per-rank times.
+Headline workload (config 3, the data-parallel fine-tune): per GPU 32 ModernBERT-base rows with valid lengths
+U{256..1024} (padding is not work: rows are concatenated), the Laya decision head, the RLCD objective with 4 noise
+groups, a global-norm clip and AdamW over fp32 masters — one step = forward + objective + backward + clip + AdamW +
+zero-grad (laya_b200/workloads.py, seeded, data seed 1000 + rank).  Products are bf16 tensor-core tiles; the default
+forward is the accurate one (bf16 hi/lo products, fp32-accurate activations: the parity-checked path).  With N GPUs
+every rank trains its own rows and the gradients are summed over NCCL in 25 MB buckets while the backward runs
+(weak scaling); torch.distributed only exchanges the NCCL id, brackets the timed region and takes the max of the
+per-rank times.
 
-`value` is device-resident throughput (inputs already in HBM, laya_decision_forward_device); `e2e` is the same
-through the host-pointer C ABI (laya_decision_forward), host↔device copies of each step's inputs and outputs inside
-the timed region.  `--impl reference` times the CPU restatement of the reference's path (oracle/) on the host cores.
+Nested `q8_0_encode` (config 2): the batched decision forward with every projection in Q8_0, 64 rows × 512 tokens per
+GPU, sharded by request with no collective.
+
+`value` is device-resident throughput (inputs staged in HBM before the timed region); `e2e` is the same step through
+the host-pointer C ABI with the step's inputs copied from pinned host memory and its result (the loss; the logits)
+read back inside the timed region.  `--impl reference` times the CPU restatement of the reference's path (oracle/)
+on the host cores.
 """
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -24,18 +32,27 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# config 3 (fine-tune)
+TR_ROWS, TR_MIN, TR_MAX, TR_GROUPS = 32, 256, 1024, 4
+TR_WORKLOAD = "config3_dp_finetune_step"
+# config 2 (Q8_0 encode)
 ROWS, SEQ = 64, 512
 TOKENS = ROWS * SEQ
-WORKLOAD = "config2_q8_0_decision_forward"
+Q8_WORKLOAD = "config2_q8_0_decision_forward"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-sample-rows", type=int, default=1, help="rows of 512 tokens in one CPU step")
+    ap.add_argument("--workload", default="all", choices=["all", "train", "q8"])
+    ap.add_argument("--forward", default="accurate", choices=["accurate", "bf16"],
+                    help="forward mode of the headline training step")
+    ap.add_argument("--no-bf16-forward", action="store_true", help="skip the extra BF16-forward measurement")
+    ap.add_argument("--cpu-sample-rows", type=int, default=1, help="rows of 512 tokens in one Q8_0 CPU step")
+    ap.add_argument("--cpu-train-tokens", type=int, default=256, help="tokens of the CPU fine-tune sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -47,8 +64,18 @@ def dist_env():
     return rank, world, local
 
 
-def config_block(world):
-    return {"workload": WORKLOAD, "rows_per_gpu": ROWS, "seq_len": SEQ, "tokens_per_gpu_step": TOKENS,
+def train_config(world, tokens, forward):
+    return {"workload": TR_WORKLOAD, "rows_per_gpu": TR_ROWS, "valid_len": f"U{{{TR_MIN}..{TR_MAX}}}",
+            "tokens_per_gpu_step": tokens,
+            "geometry": "ModernBERT-base 22x768 (12x64, GeGLU 1152, local 128 / global every 3rd) + 2 head layers",
+            "optimizer": "RLCD (4 groups) + clip 1.0 + AdamW, fp32 masters, bf16 products",
+            "forward": forward, "l2": "inputs larger than L2 (0.66 GB fp32 parameters + ~30 GB tape per step)",
+            "parallelism": f"dp{world}, NCCL allreduce in 25 MB buckets overlapped with the backward" if world > 1
+            else "dp1"}
+
+
+def q8_config(world):
+    return {"workload": Q8_WORKLOAD, "rows_per_gpu": ROWS, "seq_len": SEQ, "tokens_per_gpu_step": TOKENS,
             "geometry": "ModernBERT-base 22x768 (12x64, GeGLU 1152) + 2 head layers", "weights": "Q8_0 (config 2)",
             "l2": "inputs larger than L2 (Q8_0 weights ~150 MB + 0.5 GB activations per step)",
             "parallelism": f"request-sharded x{world}, no collective"}
@@ -103,7 +130,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------------------------------- CPU arms
-def oracle_step_seconds(rows, seed=1):
+def q8_cpu_seconds(rows, seed=1):
     """One bounded CPU sample: the oracle's Q8_0 decision forward over `rows` × 512 tokens of the same workload."""
     import numpy as np
     import oracle
@@ -119,32 +146,116 @@ def oracle_step_seconds(rows, seed=1):
     return time.perf_counter() - t0, oracle.lib().lo_num_threads()
 
 
-def cpu_baseline(rows):
-    secs, cores = oracle_step_seconds(rows)
+def q8_cpu_baseline(rows):
+    secs, cores = q8_cpu_seconds(rows)
     return {"value": rows * SEQ / secs, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{rows} x {SEQ} tokens, one full 22-layer Q8_0 decision forward ({secs:.1f} s)"}
+
+
+class CpuTrainStep:
+    """A bounded CPU sample of the fine-tune step: the oracle's fp32 restatement of TrainableDecisionModel (PyTorch
+    autograd on the host cores) over one row of the workload, the RLCD objective and AdamW over every parameter."""
+
+    def __init__(self, tokens):
+        import numpy as np
+        import torch
+        from laya_b200 import workloads
+        from oracle.model import EncoderConfig
+        from oracle.train import TorchTrainModel
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cores = torch.get_num_threads()
+        self.tokens = tokens
+        self.w = workloads.training_weights(seed=0)
+        self.model = TorchTrainModel(EncoderConfig(), self.w)
+        self.state = {k: (np.zeros(v.size, np.float32), np.zeros(v.size, np.float32)) for k, v in self.w.items()
+                      if k != "temperature"}
+        self.steps = 0
+
+    def run(self, seed):
+        """(seconds of forward + objective + backward over one row, seconds of clip + AdamW over every parameter)."""
+        import torch
+        from laya_b200 import workloads
+        from oracle.train import adamw_step, clip_by_global_norm, rlcd
+        items, draws = workloads.training_batch(rows=1, min_len=self.tokens, max_len=self.tokens, seed=seed,
+                                                groups=TR_GROUPS)
+        oi = [{"ids": it.token_ids, "markers": list(it.marker_positions), "qtype": it.question_type} for it in items]
+        t0 = time.perf_counter()
+        self.model.zero_grad()
+        logits = self.model.forward(oi, training=True, seed=seed)
+        k = items[0].options
+        _, _, _, _, grads = rlcd([l.detach().numpy() for l in logits], [it.target for it in items],
+                                 [it.question_type for it in items], 0.4, [[draws[g, :k]] for g in range(TR_GROUPS)])
+        sum((l * torch.from_numpy(g)).sum() for l, g in zip(logits, grads)).backward()
+        g = self.model.grads()
+        t1 = time.perf_counter()
+        clip_by_global_norm(list(g.values()), 1.0)
+        self.steps += 1
+        for name, p in self.model.p.items():
+            data = p.detach().numpy().reshape(-1)
+            m, v = self.state[name]
+            adamw_step(data, g[name].reshape(-1), m, v, self.steps, 2.5e-5 if name.startswith("encoder.") else 1e-4)
+        return t1 - t0, time.perf_counter() - t1
+
+    def rate(self, fb, opt):
+        """tokens/s with the optimizer amortised as the workload runs it: one clip + AdamW per step of
+        TR_ROWS rows (mean valid length (TR_MIN + TR_MAX) / 2)."""
+        step_tokens = TR_ROWS * (TR_MIN + TR_MAX) / 2
+        return self.tokens / (fb + opt * self.tokens / step_tokens)
+
+    def sample(self, fb, opt):
+        return (f"1 row x {self.tokens} tokens: fp32 forward + RLCD + backward ({fb:.2f} s), plus clip + AdamW over "
+                f"all {sum(v.size for v in self.w.values()) / 1e6:.0f}M parameters ({opt:.2f} s) amortised over a "
+                f"{TR_ROWS}-row step's {TR_ROWS * (TR_MIN + TR_MAX) // 2} tokens; CPU restatement (PyTorch autograd, "
+                f"numpy AdamW) of the reference's Laya.Training path")
+
+
+def train_cpu_baseline(tokens):
+    c = CpuTrainStep(tokens)
+    c.run(0)   # warm-up
+    fb, opt = c.run(1)
+    return {"value": c.rate(fb, opt), "unit": "tokens/s", "cores": c.cores, "kind": "port", "sample": c.sample(fb, opt)}
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rows = args.cpu_sample_rows
-    times = []
-    cores = None
+    if args.workload == "q8":
+        rows = args.cpu_sample_rows
+        times, cores = [], None
+        for i in range(args.warmup + args.steps):
+            s, cores = q8_cpu_seconds(rows, seed=1 + i)
+            if i >= args.warmup:
+                times.append(s)
+        per = statistics.mean(times)
+        value = rows * SEQ / per
+        line = {"impl": "reference", "metric": "Q8_0 encode tokens/s", "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1000,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic", "config": q8_config(world),
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": f"{rows} x {SEQ} tokens per step, CPU restatement of the reference path"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    c = CpuTrainStep(args.cpu_train_tokens)
+    fbs, opts = [], []
     for i in range(args.warmup + args.steps):
-        s, cores = oracle_step_seconds(rows, seed=1 + i)
+        fb, opt = c.run(i)
         if i >= args.warmup:
-            times.append(s)
-    per = statistics.mean(times)
-    value = rows * SEQ / per
-    line = {"impl": "reference", "metric": "Q8_0 encode tokens/s", "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1000,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": config_block(world),
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"{rows} x {SEQ} tokens per step, CPU restatement of the reference path"},
+            fbs.append(fb)
+            opts.append(opt)
+    fb, opt = statistics.mean(fbs), statistics.mean(opts)
+    value = c.rate(fb, opt)
+    line = {"impl": "reference", "metric": "fine-tune tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.cpu_train_tokens / value * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": train_config(world, args.cpu_train_tokens, "fp32 (CPU restatement)"),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": c.cores, "kind": "port",
+                             "sample": c.sample(fb, opt)},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "all" and not args.no_cpu_baseline:
+        line["q8_0_encode"] = {"metric": "Q8_0 encode tokens/s", **q8_cpu_baseline(args.cpu_sample_rows)}
     print(json.dumps(line), flush=True)
 
 
@@ -152,10 +263,9 @@ def run_reference(args):
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            p = json.load(f)
-        return p, "measured"
+            return json.load(f), "measured"
     except (OSError, ValueError):
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
 def load_traffic():
@@ -166,19 +276,164 @@ def load_traffic():
         return {}
 
 
-def run_ours(args):
+class Dist:
+    def __init__(self, rank, world, local):
+        import torch
+        import torch.distributed as dist
+        self.rank, self.world, self.local = rank, world, local
+        self.dist = dist if world > 1 else None
+        self.torch = torch
+        torch.cuda.set_device(local)
+        if world > 1:
+            dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
+                                    timeout=datetime.timedelta(seconds=180))
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def reduce(self, values, op):
+        t = self.torch.tensor(values, dtype=self.torch.float64, device="cuda")
+        if self.dist:
+            self.dist.all_reduce(t, op=op(self.dist))
+        return [float(v) for v in t]
+
+    def broadcast_bytes(self, b):
+        if not self.dist:
+            return b
+        obj = [b]
+        self.dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+
+def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
+    """Times the fine-tune step on this rank; returns a dict of per-rank measurements (rank 0 formats the line)."""
     import numpy as np
     import torch
-    import torch.distributed as dist
     import laya_b200
     from laya_b200 import workloads
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
+    from laya_b200.workloads import mix
+    rank, world, local = d.rank, d.world, d.local
+    w = workloads.training_weights(seed=0)                       # the same weights on every rank
+    tr = laya_b200.Trainer(laya_b200.base_desc(max_tokens=TR_ROWS * TR_MAX, max_items=TR_ROWS,
+                                               max_markers=TR_ROWS * 8),
+                           laya_b200.train_desc(max_segment=TR_MAX, forward_mode=forward_mode), device=local)
     if world > 1:
-        dist.init_process_group("nccl", init_method="env://", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=120))
+        uid = d.broadcast_bytes(laya_b200.Trainer.unique_id() if rank == 0 else None)
+        tr.comm_init(uid, rank, world)
+    stream = torch.cuda.Stream()
+    tr.set_stream(stream.cuda_stream)
+    tr.load(w)
+    del w
+    # two batches per rank staged on the device before the timed region (data seed 1000 + rank)
+    sets = [workloads.training_batch(rows=TR_ROWS, min_len=TR_MIN, max_len=TR_MAX, seed=1000 + rank + 64 * i,
+                                     groups=TR_GROUPS) for i in range(2)]
+    batches = [tr.batch(items, draws) for items, draws in sets]
+    tokens = [sum(len(it.token_ids) for it in items) for items, _ in sets]
+    options = [sum(it.options for it in items) for items, _ in sets]
 
+    def step(b, i):
+        tr.forward(b, training=True, seed=mix(42, i + 1), fetch=False)
+        tr.objective(b, sigma=0.4, groups=TR_GROUPS, fetch=False)
+        tr.backward(b)
+        tr.clip_and_step(1.0, fetch_norm=False)
+        tr.zero_grads()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(batches[i % 2], i)
+    tr.synchronize()
+    out = {}
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    d.barrier()
+    n0 = tr.launches()
+    if with_profile:
+        tr.set_profiling(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    done_tokens = 0
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            step(batches[i % 2], args.warmup + i)
+            done_tokens += tokens[i % 2]
+        e1.record(stream)
+    e1.synchronize()
+    out["launches"] = tr.launches() - n0
+    if with_profile:
+        out["prof"] = [tr.profile(k) for k in range(3)]
+        tr.set_profiling(False)
+    tr.synchronize()
+    d.barrier()
+    out["clocks"] = sampler.stop()
+    out["ms"] = e0.elapsed_time(e1) / args.steps
+    out["tokens"] = done_tokens
+    out["tokens_per_step"] = done_tokens / args.steps
+
+    if with_e2e:
+        # end to end: each step's batch from pinned host memory (ids, segments, markers, targets, draws), the loss
+        # read back (laya_train_objective with a host result synchronises the step)
+        L = laya_b200.lib()
+        host = []
+        for items, draws in sets:
+            ids = np.concatenate([np.asarray(it.token_ids, np.int64) for it in items]).astype(np.int32)
+            arrs = [ids, np.array([len(it.token_ids) for it in items], np.int32),
+                    np.array([it.question_type for it in items], np.int32),
+                    np.array([it.options for it in items], np.int32),
+                    np.concatenate([np.asarray(it.marker_positions, np.int32) for it in items]),
+                    np.concatenate([it.target for it in items]).astype(np.float32),
+                    np.ascontiguousarray(draws, np.float64)]
+            host.append([torch.from_numpy(a).pin_memory() for a in arrs])
+        h2d = [sum(int(a.nbytes) for a in hs) for hs in host]
+        staged = laya_b200.Batch(tr)
+        res = torch.zeros(4, dtype=torch.float64).pin_memory()
+        rl = laya_b200.RlcdDesc(TR_GROUPS, 0.4, 1.0, 0.75, 1.0, 1.0)
+        import ctypes
+
+        def step_host(i):
+            hs = host[i % 2]
+            laya_b200.api.check(L.laya_batch_set(tr.handle, staged.handle, hs[0].data_ptr(), hs[1].data_ptr(),
+                                                 hs[2].data_ptr(), TR_ROWS, hs[3].data_ptr(), hs[4].data_ptr(),
+                                                 hs[5].data_ptr(), hs[6].data_ptr(), TR_GROUPS))
+            laya_b200.api.check(L.laya_train_forward(tr.handle, staged.handle, 1, ctypes.c_uint64(mix(42, i + 1)),
+                                                     None))
+            laya_b200.api.check(L.laya_train_objective(tr.handle, staged.handle, ctypes.byref(rl), res.data_ptr(),
+                                                       None))
+            laya_b200.api.check(L.laya_train_backward(tr.handle, staged.handle, None))
+            laya_b200.api.check(L.laya_train_clip_and_step(tr.handle, ctypes.c_double(1.0), None))
+            laya_b200.api.check(L.laya_train_zero_grads(tr.handle))
+
+        for i in range(max(1, args.warmup // 2)):
+            step_host(i)
+        tr.synchronize()
+        d.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for i in range(args.steps):
+            step_host(i)
+        h1.record(stream)
+        h1.synchronize()
+        d.barrier()
+        out["e2e_ms"] = h0.elapsed_time(h1) / args.steps
+        out["h2d"] = sum(h2d[i % 2] for i in range(args.steps)) / args.steps
+        out["d2h"] = 4 * 8
+        out["loss"] = float(res[0])
+        staged.close()
+    for b in batches:
+        b.close()
+    tr.synchronize()
+    tr.close()
+    return out
+
+
+def q8_measure(args, d):
+    import numpy as np
+    import torch
+    import laya_b200
+    from laya_b200 import workloads
+    rank, world, local = d.rank, d.world, d.local
     w, q8 = workloads.decision_weights(seed=0)                    # the same weights on every rank
     model = laya_b200.DecisionModel(laya_b200.base_desc(max_tokens=TOKENS, max_items=ROWS, max_markers=ROWS * 8),
                                     w, q8, device=local)
@@ -203,17 +458,11 @@ def run_ours(args):
         for _ in range(args.warmup):
             step_device()
     model.ctx.synchronize()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # ---- timed region: device-resident
+    out = {}
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    barrier()
+    d.barrier()
     launches0 = model.ctx.launches()
     model.ctx.set_profiling(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -223,15 +472,14 @@ def run_ours(args):
             step_device()
         e1.record(stream)
     e1.synchronize()
-    launches = model.ctx.launches() - launches0
-    gemm_ms, gemm_ops, gemm_n = model.ctx.profile()
+    out["launches"] = model.ctx.launches() - launches0
+    out["gemm"] = model.ctx.profile()
     model.ctx.set_profiling(False)
     model.ctx.synchronize()
-    barrier()
-    clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    d.barrier()
+    out["clocks"] = sampler.stop()
+    out["ms"] = e0.elapsed_time(e1) / args.steps
 
-    # ---- timed region: end to end through the host-pointer C ABI (pinned host buffers)
     pin = [torch.from_numpy(v).pin_memory() for v in (ids, seg_len, qtype, counts, markers)]
     host_logits = torch.zeros(n_mark, dtype=torch.float32).pin_memory()
     host_act = torch.zeros(ROWS * 2, dtype=torch.float32).pin_memory()
@@ -243,52 +491,113 @@ def run_ours(args):
 
     for _ in range(max(1, args.warmup // 2)):
         step_host()
-    barrier()
+    d.barrier()
     h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     h0.record(stream)
     for _ in range(args.steps):
         step_host()
     h1.record(stream)
     h1.synchronize()
-    barrier()
-    e2e_ms = h0.elapsed_time(h1) / args.steps
-    h2d = sum(int(v.nbytes) for v in (ids, seg_len, qtype, counts, markers))
-    d2h = n_mark * 4 + ROWS * 2 * 4
-
-    # max over ranks
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = float(t[0]), float(t[1])
-
-    if rank == 0:
-        peaks, source = load_peaks()
-        bf16 = peaks.get("bf16_tflops", 1590.0)
-        i8_peak = 2.0 * bf16          # int8 dense rate is twice bf16 on B200; measured bf16 × 2
-        achieved = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
-        traffic = load_traffic().get("q8_gemm", {}).get("dram_bytes_per_launch")
-        line = {
-            "metric": "Q8_0 encode tokens/s", "value": world * TOKENS / (ms / 1e3), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": config_block(world),
-            "e2e": {"value": world * TOKENS / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "roofline": {"kernel": "q8_gemm_kernel (Q8_0 tcgen05 kind::i8 product + per-block rescale)",
-                         "bound": "tensor", "achieved": achieved, "peak": i8_peak, "unit": "TOP/s",
-                         "frac": achieved / i8_peak, "peak_source": f"2 x {source} bf16 burst ({bf16} TFLOP/s)",
-                         "traffic": traffic, "launches": gemm_n,
-                         "share_of_step": (gemm_ms / gemm_n) * (gemm_n / args.steps) / ms if gemm_n else None},
-            "gpu_launches": launches,
-            "clocks": clocks,
-        }
-        if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_rows)
-        print(json.dumps(line), flush=True)
+    d.barrier()
+    out["e2e_ms"] = h0.elapsed_time(h1) / args.steps
+    out["h2d"] = sum(int(v.nbytes) for v in (ids, seg_len, qtype, counts, markers))
+    out["d2h"] = n_mark * 4 + ROWS * 2 * 4
     model.ctx.close()
+    return out
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    d = Dist(rank, world, local)
+    peaks, source = load_peaks()
+    traffic = load_traffic()
+    bf16_sus = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1590.0))
+    SUM = lambda dist: dist.ReduceOp.SUM
+    MAX = lambda dist: dist.ReduceOp.MAX
+    line = None
+    if args.workload in ("all", "train"):
+        mode = 0 if args.forward == "accurate" else 1
+        r = train_measure(args, d, mode)
+        ms, e2e_ms = d.reduce([r["ms"], r["e2e_ms"]], MAX)
+        step_tokens, h2d = d.reduce([r["tokens_per_step"], r["h2d"]], SUM)   # all ranks, per step
+        alt = None
+        if args.workload == "all" and not args.no_bf16_forward:
+            ra = train_measure(args, d, 1 - mode, with_e2e=False, with_profile=False)
+            alt = (d.reduce([ra["ms"]], MAX)[0], d.reduce([ra["tokens_per_step"]], SUM)[0])
+        if rank == 0:
+            (g_ms, g_fl, g_n), (af_ms, af_fl, af_n), (ab_ms, ab_fl, ab_n) = r["prof"]
+            g_ach = g_fl / (g_ms / 1e3) / 1e12 if g_ms else 0.0
+            step_flops = (g_fl + af_fl + ab_fl) / args.steps
+            fwd = "accurate (bf16 hi/lo tensor-core products, fp32-accurate forward)" if mode == 0 else \
+                "bf16 (bf16-operand forward)"
+            value = step_tokens / (ms / 1e3)
+            line = {
+                "metric": "fine-tune tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": train_config(world, r["tokens_per_step"], fwd),
+                "e2e": {"value": step_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": r["d2h"] * world,
+                        "ms_per_step": e2e_ms},
+                "roofline": {"kernel": "gemm_bf16_kernel (tcgen05 bf16 products: forward, dX, split-K dW)",
+                             "bound": "tensor", "achieved": g_ach, "peak": bf16_sus, "unit": "TFLOP/s",
+                             "frac": g_ach / bf16_sus,
+                             "peak_source": f"{source} bf16 sustained (kernels timed inside a long step)",
+                             "traffic": traffic.get("bf16_gemm", {}).get("dram_bytes_per_launch"),
+                             "launches": g_n, "share_of_step": g_ms / args.steps / ms,
+                             "flops_per_launch": g_fl / g_n if g_n else None},
+                "attention": {"kernels": "flash fwd / dQ + dK,dV (mma.sync bf16, cp.async double-buffered)",
+                              "fwd_tflops": af_fl / (af_ms / 1e3) / 1e12 if af_ms else None,
+                              "bwd_tflops": ab_fl / (ab_ms / 1e3) / 1e12 if ab_ms else None,
+                              "share_of_step": (af_ms + ab_ms) / args.steps / ms},
+                "step_roofline": {"algorithmic_tflop_per_step": step_flops / 1e12,
+                                  "achieved": step_flops / (ms / 1e3) / 1e12, "peak": bf16_sus, "unit": "TFLOP/s",
+                                  "frac": step_flops / (ms / 1e3) / 1e12 / bf16_sus,
+                                  "note": "products 2MNK (fwd) + 4MNK (bwd); attention 4·hidden per visible pair "
+                                          "fwd, 2x bwd; no credit for the accurate forward's extra passes"},
+                "gpu_launches": r["launches"],
+                "clocks": r["clocks"],
+                "loss_last_e2e_step": r["loss"],
+            }
+            if alt:
+                line["bf16_forward" if mode == 0 else "accurate_forward"] = {
+                    "value": alt[1] / (alt[0] / 1e3), "unit": "tokens/s", "ms_per_step": alt[0]}
+            if not args.no_cpu_baseline:
+                line["cpu_baseline"] = train_cpu_baseline(args.cpu_train_tokens)
+    if args.workload in ("all", "q8"):
+        r = q8_measure(args, d)
+        ms, e2e_ms = d.reduce([r["ms"], r["e2e_ms"]], MAX)
+        if rank == 0:
+            gemm_ms, gemm_ops, gemm_n = r["gemm"]
+            bf16 = peaks.get("bf16_tflops", 1590.0)
+            i8_peak = 2.0 * bf16          # int8 dense rate is twice bf16 on B200: measured bf16 burst × 2
+            achieved = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+            q = {
+                "metric": "Q8_0 encode tokens/s", "value": world * TOKENS / (ms / 1e3), "unit": "tokens/s",
+                "n_gpus": world, "ms_per_step": ms, "dtype": "int8", "scaling": "weak", "config": q8_config(world),
+                "e2e": {"value": world * TOKENS / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
+                        "d2h_bytes_per_step": r["d2h"], "ms_per_step": e2e_ms},
+                "roofline": {"kernel": "q8_gemm_kernel (Q8_0 product: exact fp16-held codes on tcgen05 kind::f16, "
+                                       "per-block rescale)",
+                             "bound": "tensor", "achieved": achieved, "peak": i8_peak, "unit": "TOP/s",
+                             "frac": achieved / i8_peak, "peak_source": f"2 x {source} bf16 burst ({bf16} TFLOP/s)",
+                             "traffic": traffic.get("q8_gemm", {}).get("dram_bytes_per_launch"), "launches": gemm_n,
+                             "share_of_step": gemm_ms / args.steps / ms},
+                "gpu_launches": r["launches"], "clocks": r["clocks"]}
+            if not args.no_cpu_baseline:
+                q["cpu_baseline"] = q8_cpu_baseline(args.cpu_sample_rows)
+            if line is None:
+                q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "vs_baseline": None, "data": "synthetic"})
+                line = q
+            else:
+                line["q8_0_encode"] = q
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        d.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def main():

@@ -121,6 +121,15 @@ int laya_train_zero_grads(laya_trainer* t);
 /* AdamW.Steps. */
 int laya_train_steps(laya_trainer* t, int64_t* steps);
 
+/* Kernels this host thread has launched through the library (all trainers and contexts). */
+int laya_trainer_launches(laya_trainer* t, long long* count);
+/* Measurement: with profiling on, every tensor-core product (kind 0), attention forward (1) and attention backward (2)
+ * launch is bracketed by CUDA events on the trainer's stream; laya_trainer_profile returns and clears the summed
+ * milliseconds, algorithmic FLOPs (2·M·N·K per product whatever its passes; 4·hidden per visible query-key pair
+ * forward, twice that backward) and launch count of a kind.  No reference counterpart. */
+int laya_trainer_set_profiling(laya_trainer* t, int enabled);
+int laya_trainer_profile(laya_trainer* t, int kind, double* ms, double* flops, long long* launches);
+
 /* Data parallelism over NCCL (the reference notebook's DDP; no counterpart in the C# trainer).
  * laya_comm_unique_id fills 128 bytes on one rank; every rank passes the same bytes to laya_train_comm_init.
  * Gradients are then allreduced in 25 MB buckets on a stream of their own as the backward finishes them. */

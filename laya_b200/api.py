@@ -123,6 +123,10 @@ _SIGS = {
     "laya_train_clip_and_step": (_I, [_P, ctypes.c_double, _P]),
     "laya_train_zero_grads": (_I, [_P]),
     "laya_train_steps": (_I, [_P, ctypes.POINTER(ctypes.c_int64)]),
+    "laya_trainer_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_trainer_set_profiling": (_I, [_P, _I]),
+    "laya_trainer_profile": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(ctypes.c_longlong)]),
     "laya_comm_unique_id": (_I, [_P]),
     "laya_train_comm_init": (_I, [_P, _P, _I, _I]),
 }
@@ -628,6 +632,22 @@ class Trainer:
         s = ctypes.c_int64()
         check(lib().laya_train_steps(self.handle, ctypes.byref(s)))
         return s.value
+
+    def launches(self) -> int:
+        n = ctypes.c_longlong()
+        check(lib().laya_trainer_launches(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def set_profiling(self, enabled: bool):
+        check(lib().laya_trainer_set_profiling(self.handle, int(enabled)))
+
+    PRODUCTS, ATTENTION_FWD, ATTENTION_BWD = 0, 1, 2
+
+    def profile(self, kind: int) -> Tuple[float, float, int]:
+        """(milliseconds, algorithmic FLOPs, launches) of one kernel kind since the last call."""
+        ms, fl, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_longlong()
+        check(lib().laya_trainer_profile(self.handle, kind, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(n)))
+        return ms.value, fl.value, n.value
 
     @staticmethod
     def unique_id() -> bytes:

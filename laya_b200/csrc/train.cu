@@ -132,6 +132,7 @@ struct laya_batch {
     int device = 0;
     uint64_t id = 0;                 // unique over the process: a new batch at a freed one's address is not it
     uint64_t version = 0;            // bumped by every laya_batch_set
+    double pairs_global = 0, pairs_local = 0;   // visible (query, key) pairs: full segments; the sliding window
     int T = 0, n = 0, M = 0, tiles = 0, groups = 0;
     // device fields (one allocation, layout fixed by capacity)
     void* dev = nullptr;
@@ -215,6 +216,12 @@ struct laya_trainer {
     uint64_t fwd_seed = 0;
     bool have_logits = false, have_dlogits = false;
     Comm comm;
+    // profiling: CUDA events around each product (kind 0) and attention forward (1) / backward (2) launch
+    bool profiling = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
+    std::vector<std::pair<int, double>> ev_work;   // (kind, algorithmic FLOPs) of each used event pair
+    double prof_ms[3] = {0, 0, 0}, prof_flops[3] = {0, 0, 0};
+    long long prof_n[3] = {0, 0, 0};
     std::vector<void*> allocs;
 };
 
@@ -245,6 +252,39 @@ int check_device_error(laya_trainer* t) {
         set_error("index out of range on the device");
         return ERR_OUT_OF_RANGE;
     }
+    return OK;
+}
+
+// Runs `launch` between two CUDA events when profiling is on, charging `flops` algorithmic FLOPs to `kind`.
+template <class F>
+int timed(laya_trainer* t, int kind, double flops, F&& launch) {
+    if (!t->profiling) return launch();
+    if (t->ev_work.size() == t->ev_pool.size()) {
+        cudaEvent_t e0, e1;
+        LAYA_CUDA(cudaEventCreate(&e0));
+        LAYA_CUDA(cudaEventCreate(&e1));
+        t->ev_pool.push_back({e0, e1});
+    }
+    auto& ev = t->ev_pool[t->ev_work.size()];
+    LAYA_CUDA(cudaEventRecord(ev.first, t->stream));
+    const int rc = launch();
+    LAYA_CUDA(cudaEventRecord(ev.second, t->stream));
+    t->ev_work.push_back({kind, flops});
+    return rc;
+}
+
+int collect_profile(laya_trainer* t) {
+    if (t->ev_work.empty()) return OK;
+    LAYA_CUDA(cudaStreamSynchronize(t->stream));
+    for (size_t i = 0; i < t->ev_work.size(); ++i) {
+        float ms = 0;
+        LAYA_CUDA(cudaEventElapsedTime(&ms, t->ev_pool[i].first, t->ev_pool[i].second));
+        const int k = t->ev_work[i].first;
+        t->prof_ms[k] += ms;
+        t->prof_flops[k] += t->ev_work[i].second;
+        t->prof_n[k] += 1;
+    }
+    t->ev_work.clear();
     return OK;
 }
 
@@ -361,16 +401,16 @@ int lin_fwd(laya_trainer* t, int T, int N, int K, const bf16* x, const bf16* x_l
             void* out) {
     bf::Args a{T, N, K, x, K, 0, t->shadow + w, K, 0, bias, epi, out, N, t->err};
     if (x_lo) { a.A2 = x_lo; a.B2 = t->shadow_lo + w; }
-    return bf::gemm(a, t->stream);
+    return timed(t, 0, 2.0 * T * N * K, [&] { return bf::gemm(a, t->stream); });
 }
 int lin_dx(laya_trainer* t, int T, int N, int K, const bf16* dy, size_t w, int epi, void* dx) {
     bf::Args a{T, K, N, dy, N, 0, t->shadow + w, K, 1, nullptr, epi, dx, K, t->err};
-    return bf::gemm(a, t->stream);
+    return timed(t, 0, 2.0 * T * N * K, [&] { return bf::gemm(a, t->stream); });
 }
 int lin_dw(laya_trainer* t, int T, int N, int K, const bf16* dy, const bf16* x, size_t w) {
     bf::Args a{N, K, T, dy, N, 1, x, K, 1, nullptr, bf::EPI_F32_ADD, t->grad + w, K, t->err};
     a.ksplit_ok = 1;   // few output tiles over K = tokens: split K across the SMs
-    return bf::gemm(a, t->stream);
+    return timed(t, 0, 2.0 * T * N * K, [&] { return bf::gemm(a, t->stream); });
 }
 
 fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const bf16* qkv_lo, int heads, int window,
@@ -443,7 +483,7 @@ int enc_forward(laya_trainer* t, const laya_batch* b, int l) {
     }
     fa::Args att = attn_args(t, b, t->qkv[l], pr ? t->ws_qkvlo : nullptr, t->heads, g ? -1 : t->window, cosv, sinv,
                              0.f, 0, t->ctx[l], ctxlo, t->lse[l]);
-    RC(flash_forward(att, b->tiles, s));
+    RC(timed(t, 1, 4.0 * H * (g ? b->pairs_global : b->pairs_local), [&] { return flash_forward(att, b->tiles, s); }));
     LAYA_CUDA(cudaMemcpyAsync(t->X1[l], t->X[l], sizeof(float) * T * H, cudaMemcpyDeviceToDevice, s));
     RC(lin_fwd(t, T, H, H, t->ctx[l], ctxlo, p.wo, nullptr, bf::EPI_F32_ADD, t->X1[l]));
     RC(ln_fwd(ln_args(t, T, t->X1[l], p.n2, NONE, t->eps, t->n2[l], n2lo, nullptr, t->mean2[l], t->rstd2[l]), s));
@@ -479,7 +519,7 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
     const tr::Mask m0 = head_mask(t, l, 0);
     fa::Args att = attn_args(t, b, t->hqkv[l], pr ? t->ws_qkvlo : nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
                              t->hctx[l], ctxlo, t->hlse[l]);
-    RC(flash_forward(att, b->tiles, s));
+    RC(timed(t, 1, 4.0 * H * b->pairs_global, [&] { return flash_forward(att, b->tiles, s); }));
     RC(lin_fwd(t, T, H, H, t->hctx[l], ctxlo, p.outw, t->master + p.outb, bf::EPI_F32, t->R32));
     RC(add_masked(t->HIN[l], t->R32, t->HX1[l], n, head_mask(t, l, 1), s));
     RC(ln_fwd(ln_args(t, T, t->HX1[l], p.n2w, p.n2b, 1e-5f, t->hn2[l], n2lo, nullptr, t->hm2[l], t->hr2[l]), s));
@@ -564,7 +604,7 @@ int head_backward(laya_trainer* t, const laya_batch* b, int l) {
     const tr::Mask m0 = head_mask(t, l, 0);
     fa::Args att = attn_args(t, b, t->hqkv[l], nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l],
                              nullptr, t->hlse[l]);
-    RC(flash_backward(att, b->tiles, T, s));
+    RC(timed(t, 2, 8.0 * H * b->pairs_global, [&] { return flash_backward(att, b->tiles, T, s); }));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->hn1[l], p.inw));
     RC(colsum_bf16(t->dqkv16, T, 3 * H, G + p.inb, s));
     RC(lin_dx(t, T, 3 * H, H, t->dqkv16, p.inw, bf::EPI_F32, t->dN));
@@ -594,7 +634,7 @@ int enc_backward(laya_trainer* t, const laya_batch* b, int l, bool need_dx) {
     const bool g = t->global[l];
     fa::Args att = attn_args(t, b, t->qkv[l], nullptr, t->heads, g ? -1 : t->window, g ? t->cos_g : t->cos_l,
                              g ? t->sin_g : t->sin_l, 0.f, 0, t->ctx[l], nullptr, t->lse[l]);
-    RC(flash_backward(att, b->tiles, T, s));
+    RC(timed(t, 2, 8.0 * H * (g ? b->pairs_global : b->pairs_local), [&] { return flash_backward(att, b->tiles, T, s); }));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->n1[l], p.qkv));
     if (p.n1 == NONE) {
         // identity norm: dx += dqkv · Wqkv
@@ -843,6 +883,7 @@ int laya_trainer_destroy(laya_trainer* t) {
     if (t->comm.done) cudaEventDestroy(t->comm.done);
     if (t->comm.stream) cudaStreamDestroy(t->comm.stream);
     for (void* p : t->allocs) cudaFree(p);
+    for (auto& e : t->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
     if (t->h_red) cudaFreeHost(t->h_red);
     if (t->own) cudaStreamDestroy(t->own);
     delete t;
@@ -1042,6 +1083,13 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
     int32_t* hmc = reinterpret_cast<int32_t*>(h + b->o_mk_count);
     std::memcpy(h + b->o_ids, ids, sizeof(int32_t) * T);
     int start = 0, mk = 0, tiles = 0;
+    double pg = 0, pl = 0;
+    for (int i = 0; i < n_items; ++i) {
+        const double L = seg_len[i];
+        pg += L * L;
+        for (int q = 0; q < seg_len[i]; ++q)
+            pl += std::min(seg_len[i], q + t->window + 1) - std::max(0, q - t->window);
+    }
     for (int i = 0; i < n_items; ++i) {
         hs[i] = start; hl[i] = seg_len[i]; hq[i] = qtype[i]; hms[i] = mk; hmc[i] = marker_count[i];
         for (int p = 0; p < seg_len[i]; ++p) hti[start + p] = i;
@@ -1063,6 +1111,8 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
                                                         sizeof(double) * M);
     }
     b->T = static_cast<int>(T); b->n = n_items; b->M = static_cast<int>(M); b->tiles = tiles; b->groups = groups;
+    b->pairs_global = pg;
+    b->pairs_local = pl;
     b->version++;
     // one copy of the used prefix of the layout (draws last: copy exactly what this batch uses)
     const size_t used = b->o_draws + sizeof(double) * static_cast<size_t>(groups) * M;
@@ -1220,6 +1270,34 @@ int laya_train_zero_grads(laya_trainer* t) {
 int laya_train_steps(laya_trainer* t, int64_t* steps) {
     if (!t || !steps) { set_error("null argument"); return ERR_ARGUMENT; }
     *steps = t->steps;
+    return OK;
+}
+
+int laya_trainer_launches(laya_trainer* t, long long* count) {
+    if (!t || !count) { set_error("null argument"); return ERR_ARGUMENT; }
+    *count = launches();
+    return OK;
+}
+
+int laya_trainer_set_profiling(laya_trainer* t, int enabled) {
+    if (!t) { set_error("null trainer"); return ERR_ARGUMENT; }
+    DeviceGuard g(t->device);
+    RC(collect_profile(t));
+    t->profiling = enabled != 0;
+    for (int k = 0; k < 3; ++k) { t->prof_ms[k] = t->prof_flops[k] = 0; t->prof_n[k] = 0; }
+    return OK;
+}
+
+int laya_trainer_profile(laya_trainer* t, int kind, double* ms, double* flops, long long* n) {
+    if (!t) { set_error("null trainer"); return ERR_ARGUMENT; }
+    if (kind < 0 || kind > 2) { set_error("profile kind is 0 (products), 1 (attention forward) or 2 (backward)"); return ERR_ARGUMENT; }
+    DeviceGuard g(t->device);
+    RC(collect_profile(t));
+    if (ms) *ms = t->prof_ms[kind];
+    if (flops) *flops = t->prof_flops[kind];
+    if (n) *n = t->prof_n[kind];
+    t->prof_ms[kind] = t->prof_flops[kind] = 0;
+    t->prof_n[kind] = 0;
     return OK;
 }
 

@@ -141,3 +141,12 @@ def training_batch(rows=32, min_len=256, max_len=1024, vocab=50368, seed=1000, g
     m = sum(it.options for it in items)
     draws = rng.standard_normal((groups, m))
     return items, draws
+
+
+def mix(seed: int, salt: int) -> int:
+    """Ops.Mix (Laya.Training/Ops.cs:236-241): the per-micro-step dropout seed Trainer.Train derives,
+    Mix(Seed, microStep + 1) (Trainer.cs:129)."""
+    m = (1 << 64) - 1
+    z = (seed ^ ((salt * 0xD1B54A32D192ED03 + 0x8CB92BA72F3D8DD7) & m)) & m
+    z = ((z ^ (z >> 33)) * 0xFF51AFD7ED558CCD) & m
+    return z ^ (z >> 33)
