@@ -79,7 +79,7 @@ DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* er
 DEVI void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 2D tiled load (no multicast) into this CTA's shared memory, completing on an mbarrier.
+// 2D tiled load into this CTA's own shared memory only, completing on an mbarrier.
 DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -88,7 +88,7 @@ DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, i
         : "memory");
 }
 
-// Bulk tensor stores from this CTA's shared memory (no multicast), tracked by bulk groups of the issuing thread.
+// Bulk tensor stores from this CTA's shared memory, tracked by bulk groups of the issuing thread.
 DEVI void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
