@@ -33,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 # config 3 (fine-tune)
-TR_ROWS, TR_MIN, TR_MAX, TR_GROUPS = 32, 256, 1024, 4
+TR_ROWS, TR_MIN, TR_MAX, TR_GROUPS = 32, 256, 1024, 4   # rows per GPU: --train-rows
 TR_WORKLOAD = "config3_dp_finetune_step"
 # config 2 (Q8_0 encode)
 ROWS, SEQ = 64, 512
@@ -54,6 +54,13 @@ def parse():
     ap.add_argument("--cpu-sample-rows", type=int, default=1, help="rows of 512 tokens in one Q8_0 CPU step")
     ap.add_argument("--cpu-train-tokens", type=int, default=256, help="tokens of the CPU fine-tune sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--train-rows", type=int, default=TR_ROWS, help="rows per GPU of the fine-tune step")
+    ap.add_argument("--train-layers", type=int, default=22, help="encoder layers (fewer only for small captures)")
+    ap.add_argument("--kernel", choices=["q8_gemm", "bf16_gemm"],
+                    help="time one product alone at the workload's shapes (profiling captures), not the step")
+    ap.add_argument("--case", default="wqkv",
+                    help="q8_gemm: wqkv|wo|wi|mlp_wo; bf16_gemm: fwd_split|dx|dw (the Wqkv projection, 20480 tokens)")
+    ap.add_argument("--reps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -64,8 +71,8 @@ def dist_env():
     return rank, world, local
 
 
-def train_config(world, tokens, forward):
-    return {"workload": TR_WORKLOAD, "rows_per_gpu": TR_ROWS, "valid_len": f"U{{{TR_MIN}..{TR_MAX}}}",
+def train_config(world, tokens, forward, rows=TR_ROWS):
+    return {"workload": TR_WORKLOAD, "rows_per_gpu": rows, "valid_len": f"U{{{TR_MIN}..{TR_MAX}}}",
             "tokens_per_gpu_step": tokens,
             "geometry": "ModernBERT-base 22x768 (12x64, GeGLU 1152, local 128 / global every 3rd) + 2 head layers",
             "optimizer": "RLCD (4 groups) + clip 1.0 + AdamW, fp32 masters, bf16 products",
@@ -315,9 +322,10 @@ def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
     from laya_b200 import workloads
     from laya_b200.workloads import mix
     rank, world, local = d.rank, d.world, d.local
-    w = workloads.training_weights(seed=0)                       # the same weights on every rank
-    tr = laya_b200.Trainer(laya_b200.base_desc(max_tokens=TR_ROWS * TR_MAX, max_items=TR_ROWS,
-                                               max_markers=TR_ROWS * 8),
+    w = workloads.training_weights(layers=args.train_layers, seed=0)   # the same weights on every rank
+    rows = args.train_rows
+    tr = laya_b200.Trainer(laya_b200.base_desc(max_tokens=rows * TR_MAX, max_items=rows, max_markers=rows * 8,
+                                               layers=args.train_layers),
                            laya_b200.train_desc(max_segment=TR_MAX, forward_mode=forward_mode), device=local)
     if world > 1:
         uid = d.broadcast_bytes(laya_b200.Trainer.unique_id() if rank == 0 else None)
@@ -327,7 +335,7 @@ def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
     tr.load(w)
     del w
     # two batches per rank staged on the device before the timed region (data seed 1000 + rank)
-    sets = [workloads.training_batch(rows=TR_ROWS, min_len=TR_MIN, max_len=TR_MAX, seed=1000 + rank + 64 * i,
+    sets = [workloads.training_batch(rows=rows, min_len=TR_MIN, max_len=TR_MAX, seed=1000 + rank + 64 * i,
                                      groups=TR_GROUPS) for i in range(2)]
     batches = [tr.batch(items, draws) for items, draws in sets]
     tokens = [sum(len(it.token_ids) for it in items) for items, _ in sets]
@@ -395,7 +403,7 @@ def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
         def step_host(i):
             hs = host[i % 2]
             laya_b200.api.check(L.laya_batch_set(tr.handle, staged.handle, hs[0].data_ptr(), hs[1].data_ptr(),
-                                                 hs[2].data_ptr(), TR_ROWS, hs[3].data_ptr(), hs[4].data_ptr(),
+                                                 hs[2].data_ptr(), rows, hs[3].data_ptr(), hs[4].data_ptr(),
                                                  hs[5].data_ptr(), hs[6].data_ptr(), TR_GROUPS))
             laya_b200.api.check(L.laya_train_forward(tr.handle, staged.handle, 1, ctypes.c_uint64(mix(42, i + 1)),
                                                      None))
@@ -536,7 +544,7 @@ def run_ours(args):
                 "metric": "fine-tune tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": train_config(world, r["tokens_per_step"], fwd),
+                "config": train_config(world, r["tokens_per_step"], fwd, args.train_rows),
                 "e2e": {"value": step_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": r["d2h"] * world,
                         "ms_per_step": e2e_ms},
@@ -600,9 +608,75 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------------------- one product
+def run_kernel(args):
+    """One product alone at a workload shape, CUDA events over --reps launches (the command ncu captures)."""
+    import torch
+    import laya_b200
+    torch.cuda.set_device(0)
+    ctx = laya_b200.Context(laya_b200.base_desc(max_tokens=512, max_items=4, max_markers=16))
+    st = torch.cuda.current_stream()
+    ctx.set_stream(st.cuda_stream)
+    L = laya_b200.lib()
+    if args.kernel == "q8_gemm":
+        N, K = {"wqkv": (2304, 768), "wo": (768, 768), "wi": (2304, 768), "mlp_wo": (768, 1152)}[args.case]
+        M = TOKENS
+        qx = torch.randint(-127, 128, (M, K), device="cuda").to(torch.float16)
+        qw = torch.randint(-127, 128, (N, K), device="cuda").to(torch.float16)
+        ldx, ldw = (M + 127) // 128 * 128, (N + 127) // 128 * 128
+        dx = torch.rand((K // 32, ldx), device="cuda") * 0.01
+        dw = torch.rand((K // 32, ldw), device="cuda") * 0.002
+        out = torch.empty((M, N), device="cuda")
+        f = lambda: L.laya_q8_0_gemm_device(ctx.handle, qx.data_ptr(), dx.data_ptr(), ldx, M, qw.data_ptr(),
+                                            dw.data_ptr(), ldw, N, K, None, out.data_ptr(), N)
+        flops = 2.0 * M * N * K
+        desc = f"q8_gemm_kernel store epilogue, config-2 {args.case}: M={M} N={N} K={K}"
+    else:
+        T, H = 20480, 768
+        bf = torch.bfloat16
+        if args.case == "fwd_split":     # y = x·Wᵀ from hi/lo parts (accurate forward), fp32 out
+            M, N, K = T, 3 * H, H
+            A, Al = torch.randn(M, K, device="cuda").to(bf), torch.randn(M, K, device="cuda").to(bf) * 1e-3
+            B, Bl = torch.randn(N, K, device="cuda").to(bf), torch.randn(N, K, device="cuda").to(bf) * 1e-3
+            out = torch.zeros(M, N, device="cuda")
+            f = lambda: L.laya_gemm_bf16_split_device(ctx.handle, M, N, K, A.data_ptr(), Al.data_ptr(), K, 0,
+                                                      B.data_ptr(), Bl.data_ptr(), K, 0, None, 1, out.data_ptr(), N)
+        elif args.case == "dx":          # dx = dy·W, W read N-contiguous, fp32 out
+            M, N, K = T, H, 3 * H
+            A = torch.randn(M, K, device="cuda").to(bf)
+            B = torch.randn(K, N, device="cuda").to(bf)
+            out = torch.zeros(M, N, device="cuda")
+            f = lambda: L.laya_gemm_bf16_device(ctx.handle, M, N, K, A.data_ptr(), K, 0, B.data_ptr(), N, 1, None, 1,
+                                                out.data_ptr(), N)
+        else:                            # dW += dyᵀ·x, both read N-contiguous, K = tokens, split-K reduce-add
+            M, N, K = 3 * H, H, T
+            A = torch.randn(K, M, device="cuda").to(bf)
+            B = torch.randn(K, N, device="cuda").to(bf)
+            out = torch.zeros(M, N, device="cuda")
+            f = lambda: L.laya_gemm_bf16_device(ctx.handle, M, N, K, A.data_ptr(), M, 1, B.data_ptr(), N, 1, None, 2,
+                                                out.data_ptr(), N)
+        flops = 2.0 * M * N * K
+        desc = f"gemm_bf16_kernel {args.case}: M={M} N={N} K={K}"
+    for _ in range(3):
+        laya_b200.api.check(f())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.reps):
+        laya_b200.api.check(f())
+    e1.record()
+    e1.synchronize()
+    ctx.synchronize()
+    ms = e0.elapsed_time(e1) / args.reps
+    print(json.dumps({"kernel": desc, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "reps": args.reps}), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
