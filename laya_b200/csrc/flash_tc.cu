@@ -1,0 +1,404 @@
+// flash_tc.cu — the fine-tune attention forward on the 5th-generation tensor cores (head_dim 64).
+//
+// Same contract as fa::fwd_kernel (flash.cu; Ops.AttentionForward/ForwardUnit, Laya.Training/Ops.cs:260-366):
+// per (segment, head), q and k already rotated by the prep pass, sliding layers see keys [i - W, i + W], dropout on
+// the probabilities by the reference's counter hash, row log-sum-exp kept for the backward.  One CTA owns 128
+// queries of one head:
+//   warp 0      TMA producer: the Q tile once, then 128-key K and V tiles through a 2-stage ring.
+//   warp 1      TMEM owner and MMA issuer (one thread): S = Q·Kᵀ into one of two TMEM score buffers (columns
+//               [0, 128) and [128, 256); M 128, N 128, K 64), and O += P·V into columns [256, 320) (M 128, N 64,
+//               K 128; V read N-contiguous).  The scores of tile j + 1 are issued before P·V of tile j, so they are
+//               ready when the softmax warps finish tile j.
+//   warps 2-9   softmax: two warps per TMEM lane quarter, so thread (half, i) owns 64 key columns of query row i.
+//               Per key tile it reads its half-row of S from TMEM in one round trip, masks it branch-free against the
+//               row's visible key range, exchanges the half-row maxima through shared memory (one named barrier),
+//               exponentiates and sums, rescales its half of the O row in TMEM when the max moved, and writes its
+//               64-key half of P in bf16 into shared memory in the 128-byte-swizzled K-major layout the P·V MMA reads.
+//               At the end the two halves' row sums are combined and each warp stores its 32 context columns.
+// The accurate forward (SPLIT) keeps hi and lo bf16 parts of Q, K, V and P and issues three MMAs per product
+// (hi·hi + lo·hi + hi·lo), accumulating in the same TMEM columns.
+// Every wait is bounded (common.cuh): a protocol fault ends with an error status, never a hung GPU.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "train.h"
+
+namespace laya {
+namespace fat {
+
+constexpr int BQ = 128, BK = 128, HD = 64;
+constexpr int TILE = 128 * 128;   // bytes of one 128-row × 64-column bf16 tile
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <bool SPLIT>
+struct Cfg {
+    static constexpr int NQ = SPLIT ? 2 : 1;          // Q tiles (hi, lo)
+    static constexpr int NKV = SPLIT ? 4 : 2;         // tiles per ring stage: K, V (+ K lo, V lo)
+    static constexpr int STAGES = 2;
+    static constexpr int NP = SPLIT ? 2 : 1;          // parts of P (hi, lo), each two 64-key sub-tiles
+    static constexpr int NPB = SPLIT ? 1 : 2;         // P buffers: two let the next tile's P be written while P·V runs
+    static constexpr int TILES = NQ + STAGES * NKV + 2 * NP * NPB;
+    static constexpr int SMEM = 1024 + TILES * TILE + 256 + 2 * BQ * 4;   // + the two halves' row max / row sum
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+struct Params {
+    const int32_t* seg_start; const int32_t* seg_len;
+    const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq;
+    int window, hidden, heads;
+    float scale, dropout, keep;
+    uint64_t seed;
+    __nv_bfloat16* out; __nv_bfloat16* out_lo; int ldo;
+    float* lse;
+    int* err;
+};
+
+// MN-major operand, 128-byte swizzle (V as the N-contiguous B of P·V): 64-element atoms, 8-row K groups 1024 B apart.
+DEVI uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+DEVI void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+DEVI void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+DEVI uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+DEVI float lo_part(float x) { return x - __bfloat162float(__float2bfloat16_rn(x)); }
+// 2^x by the special-function unit (ex2.approx: ~2 ulp; 2^-inf = 0)
+DEVI float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+DEVI void named_bar_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+
+// Ops.Uniform (Ops.cs:227-234) at (head << 42) | (row << 21) | key.
+DEVI float drop_mult(const Params& p, int head, int row, int key) {
+    if (p.dropout <= 0.0f) return 1.0f;
+    const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
+    uint64_t z = p.seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f) < p.dropout ? 0.0f : p.keep;
+}
+
+template <bool SPLIT, bool DROP>
+__global__ void __launch_bounds__(320, 1)
+    fwd_tc_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml, Params p) {
+    using C = Cfg<SPLIT>;
+    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, BK);                                   // K-major A, B
+    constexpr uint32_t IDESC_PV = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);                      // B (V) MN-major
+    const int tile = blockIdx.x;
+    if (tile >= *p.n_tq) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;                                   // [NQ] tiles
+    uint8_t* sKV = smem + C::NQ * TILE;                   // [STAGES][NKV] tiles: K, V, K lo, V lo
+    uint8_t* sP = sKV + C::STAGES * C::NKV * TILE;        // [NPB][NP][2] sub-tiles (keys 0-63, 64-127)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::NP * C::NPB * TILE);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;       // [2] ring stages
+    uint64_t* kv_empty = bars + 3;      // [2]
+    uint64_t* s_full = bars + 5;        // [2] S buffers in TMEM
+    uint64_t* p_full = bars + 7;        // [2] by tile parity
+    uint64_t* o_done = bars + 9;        // [2] by tile parity
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(bars + 32);   // [2 halves][BQ]: row maxima per tile, then the row sums
+
+    const int head = blockIdx.y, item = p.tq_item[tile], q0 = p.tq_p0[tile];
+    const int seg0 = p.seg_start[item], L = p.seg_len[item];
+    const bool global = p.window < 0;
+    const int W = p.window;
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + BQ + W);
+    const int nk = (ke - kb + BK - 1) / BK;
+    const int warp = warp_id(), lane = lane_id();
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(kv_full + s, 1);
+            mbar_init(kv_empty + s, 1);
+            mbar_init(s_full + s, 1);
+            mbar_init(p_full + s, 8);
+            mbar_init(o_done + s, 1);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmh); if (SPLIT) prefetch_tmap(&tml); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tO = tmem + 2 * BK;   // S buffers at columns [0, 128) and [128, 256); O at [256, 320)
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const int xq = head * HD, xk = p.hidden + head * HD, xv = 2 * p.hidden + head * HD;
+            mbar_arrive_expect_tx(q_full, C::NQ * TILE);
+            tma_load_2d(sQ, &tmh, q_full, xq, seg0 + q0);
+            if constexpr (SPLIT) tma_load_2d(sQ + TILE, &tml, q_full, xq, seg0 + q0);
+            for (int j = 0; j < nk; ++j) {
+                const int s = j & 1;
+                if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+                uint8_t* st = sKV + s * C::NKV * TILE;
+                const int y = seg0 + kb + j * BK;
+                mbar_arrive_expect_tx(kv_full + s, C::NKV * TILE);
+                tma_load_2d(st, &tmh, kv_full + s, xk, y);
+                tma_load_2d(st + TILE, &tmh, kv_full + s, xv, y);
+                if constexpr (SPLIT) {
+                    tma_load_2d(st + 2 * TILE, &tml, kv_full + s, xk, y);
+                    tma_load_2d(st + 3 * TILE, &tml, kv_full + s, xv, y);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // iteration j issues S_j (into TMEM buffer j % 2) and then P·V of tile j - 1, so the scores of the next
+            // tile are computed while the softmax warps work on the current one
+            bool ok = mbar_wait(q_full, 0, abort_flag, p.err);
+            tc_fence_after();
+            const uint32_t aq = smem_u32(sQ), aql = smem_u32(sQ + TILE);
+            for (int j = 0; j <= nk && ok; ++j) {
+                if (j < nk) {
+                    const int s = j & 1;
+                    if (!mbar_wait(kv_full + s, (j >> 1) & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t ak = smem_u32(sKV + s * C::NKV * TILE), akl = ak + 2 * TILE;
+                    const uint32_t d = tS + s * BK;
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
+                    if constexpr (SPLIT) {
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; ++kk) {
+                            mma_f16(d, smem_desc_sw128(aql + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, 1u);
+                            mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(akl + kk * 32), IDESC_S, 1u);
+                        }
+                    }
+                    mma_commit(s_full + s);
+                }
+                if (j >= 1) {
+                    const int i = j - 1, s = i & 1;
+                    if (!mbar_wait(p_full + s, (i >> 1) & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t av = smem_u32(sKV + s * C::NKV * TILE) + TILE, avl = av + 2 * TILE;
+                    const uint32_t ap = smem_u32(sP + (i % C::NPB) * C::NP * 2 * TILE), apl = ap + 2 * TILE;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                        mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV,
+                                (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    if constexpr (SPLIT) {
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                            mma_f16(tO, smem_desc_sw128(apl + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV, 1u);
+                            mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(avl + kk * 2048, TILE), IDESC_PV, 1u);
+                        }
+                    }
+                    mma_commit(o_done + s);
+                    mma_commit(kv_empty + s);
+                }
+            }
+        }
+    } else {
+        // softmax: two warps per TMEM lane quarter, each owning 64 of the tile's 128 key columns (and 32 of O's 64)
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int q = q0 + row;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        constexpr int HK = BK / 2, HO = HD / 2;
+        // keys this row sees: [lo, hi] (empty for rows past the segment)
+        const int lo = q < L ? (global ? 0 : max(0, q - W)) : 1;
+        const int hi = q < L ? (global ? L - 1 : min(L - 1, q + W)) : 0;
+        const uint32_t span = static_cast<uint32_t>(hi - lo);
+        float m_run = -INFINITY, l_run = 0.f;
+        // `ok` is kept warp-uniform and the loop never exits early: the 256 softmax threads take the same named
+        // barriers in every case (an aborted protocol only skips the work between them)
+        bool ok = true;
+        for (int j = 0; j < nk; ++j) {
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full + (j & 1), (j >> 1) & 1, abort_flag, p.err));
+            const int k0 = kb + j * BK + half * HK;
+            uint32_t v[HK];
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (ok) {
+                tc_fence_after();
+                const uint32_t sb = tS + (j & 1) * BK;
+#pragma unroll
+                for (int c = 0; c < HK / 32; ++c)
+                    tmem_ld32(sb + lane_off + half * HK + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < HK; ++e) {
+                    const bool vis = static_cast<uint32_t>(k0 + e - lo) <= span;
+                    const float x = vis ? __fmul_rn(__uint_as_float(v[e]), p.scale) : -INFINITY;
+                    v[e] = __float_as_uint(x);
+                    mx4[e & 3] = fmaxf(mx4[e & 3], x);
+                }
+            }
+            // the row max over both halves
+            red[half * BQ + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            named_bar_sync(1, 256);
+            const float mx = fmaxf(red[row], red[BQ + row]);
+            named_bar_sync(1, 256);
+            if (!ok) continue;
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = m_run == -INFINITY ? 0.f : ex2(__fmul_rn(m_run - m_new, LOG2E));
+            const float msc = m_new == -INFINITY ? 0.f : m_new * LOG2E;
+            // O may be rescaled only once P·V of the previous tile is done; the P buffer of this tile may be
+            // rewritten once the P·V that last read it (tile j - NPB) is done
+            const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
+            if (rescale || j >= C::NPB) {
+                const int i = rescale ? j - 1 : j - C::NPB;
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done + (i & 1), (i >> 1) & 1, abort_flag, p.err));
+                if (!ok) continue;
+                tc_fence_after();
+                if (rescale) {
+                    uint32_t o[HO];
+                    tmem_ld32(tO + lane_off + half * HO, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < HO; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st32(tO + lane_off + half * HO, o);
+                    tmem_st_wait();
+                }
+            }
+            // P = exp(s - m); the row sum counts every probability, dropped or not
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int e = 0; e < HK; ++e) {
+                float pe = ex2(fmaf(__uint_as_float(v[e]), LOG2E, -msc));   // 2^-inf = 0 for masked keys
+                rs4[e & 3] += pe;
+                if constexpr (DROP) pe = pe == 0.f ? 0.f : pe * drop_mult(p, head, seg0 + q, k0 + e);
+                v[e] = __float_as_uint(pe);
+            }
+            // this half's 64 keys are sub-tile `half` of P buffer j % NPB: 16-byte chunk c of row `row`, swizzled by
+            // row % 8
+            uint8_t* prow = sP + (j % C::NPB) * C::NP * 2 * TILE + half * TILE + row * 128;
+#pragma unroll
+            for (int c = 0; c < HK / 8; ++c) {
+                const float* f = reinterpret_cast<const float*>(v + 8 * c);
+                uint8_t* dst = prow + ((c ^ (row & 7)) << 4);
+                *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]),
+                                                            pack2(f[6], f[7]));
+                if constexpr (SPLIT)
+                    *reinterpret_cast<uint4*>(dst + 2 * TILE) =
+                        make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
+                                   pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
+            }
+            l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+            m_run = m_new;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full + (j & 1));
+        }
+        // the row sum over both halves (every softmax thread reaches this barrier, aborted or not)
+        red[half * BQ + row] = l_run;
+        named_bar_sync(1, 256);
+        const float l_all = red[row] + red[BQ + row];
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(o_done + ((nk - 1) & 1), ((nk - 1) >> 1) & 1, abort_flag, p.err));
+        if (ok) {
+            tc_fence_after();
+            const float inv = l_all > 0.f ? 1.0f / l_all : 0.f;
+            uint32_t o[HO];
+            tmem_ld32(tO + lane_off + half * HO, o);
+            tmem_ld_wait();
+            if (q < L) {
+                __nv_bfloat16* orow = p.out + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
+#pragma unroll
+                for (int t = 0; t < HO / 8; ++t) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * t + e]) * inv;
+                    *reinterpret_cast<uint4*>(orow + 8 * t) =
+                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                    if constexpr (SPLIT) {
+                        __nv_bfloat16* lrow = p.out_lo + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
+                        *reinterpret_cast<uint4*>(lrow + 8 * t) =
+                            make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
+                                       pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
+                    }
+                }
+                if (half == 0) p.lse[static_cast<size_t>(seg0 + q) * p.heads + head] = m_run + logf(l_all);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace fat
+
+template <bool SPLIT, bool DROP>
+static int launch_tc(const fa::Args& a, cudaStream_t s) {
+    using C = fat::Cfg<SPLIT>;
+    CUtensorMap th, tl;
+    int rc = make_tmap_2d(&th, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                          static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (!rc) rc = make_tmap_2d(&tl, SPLIT ? a.qkv_lo : a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                               static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (rc) return rc;
+    static bool attr[64] = {false};
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<SPLIT, DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM));
+        attr[dev] = true;
+    }
+    fat::Params p{};
+    p.seg_start = a.seg_start; p.seg_len = a.seg_len;
+    p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
+    p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
+    p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
+    p.out = a.out; p.out_lo = a.out_lo; p.ldo = a.ldo; p.lse = a.lse; p.err = a.err;
+    fat::fwd_tc_kernel<SPLIT, DROP><<<dim3(a.max_tq, a.heads), 320, C::SMEM, s>>>(th, tl, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// The tcgen05 forward for head_dim 64; returns ERR_NOT_SUPPORTED for shapes it does not take (the caller then runs
+// the mma.sync forward).
+int flash_forward_tc(const fa::Args& a, cudaStream_t s) {
+    if (a.hidden / a.heads != fat::HD || !a.tq_item || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
+    if ((a.ld & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (a.qkv_lo && (reinterpret_cast<uintptr_t>(a.qkv_lo) & 15)))
+        return ERR_NOT_SUPPORTED;
+    if (a.qkv_lo && !a.out_lo) { set_error("accurate attention needs the context's low part"); return ERR_ARGUMENT; }
+    const bool drop = a.dropout > 0.f;
+    if (a.qkv_lo) return drop ? launch_tc<true, true>(a, s) : launch_tc<true, false>(a, s);
+    return drop ? launch_tc<false, true>(a, s) : launch_tc<false, false>(a, s);
+}
+
+}  // namespace laya

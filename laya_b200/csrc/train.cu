@@ -140,11 +140,12 @@ struct laya_batch {
     size_t bytes = 0;
     cudaEvent_t staged = nullptr;
     int32_t *ids, *seg_start, *seg_len, *qtype, *tok_item, *tile_item, *tile_p0, *n_tiles, *marker_rows, *mk_start,
-        *mk_count;
+        *mk_count, *tq_item, *tq_p0, *n_tq;
+    int tq = 0;                      // 128-row query tiles (tcgen05 attention forward)
     float* targets;
     double* draws;
     size_t o_ids, o_seg_start, o_seg_len, o_qtype, o_tok_item, o_tile_item, o_tile_p0, o_n_tiles, o_marker_rows,
-        o_mk_start, o_mk_count, o_targets, o_draws;
+        o_mk_start, o_mk_count, o_tq_item, o_tq_p0, o_n_tq, o_targets, o_draws;
 };
 
 struct Comm {
@@ -426,6 +427,8 @@ fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const 
     a.dropout = dropout; a.keep = dropout > 0.f ? 1.0f / (1.0f - dropout) : 1.0f; a.seed = seed;
     a.out = out; a.ldo = t->H; a.lse = lse;
     a.dqkv = t->dqkv16; a.lddq = 3 * t->H; a.dsum = t->dsum; a.dout = t->dctx16;
+    a.tq_item = b->tq_item; a.tq_p0 = b->tq_p0; a.n_tq = b->n_tq; a.max_tq = b->tq; a.T = b->T;
+    a.err = t->err;
     return a;
 }
 
@@ -1011,6 +1014,7 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
     b->o_ids = take(4 * T); b->o_seg_start = take(4 * N); b->o_seg_len = take(4 * N); b->o_qtype = take(4 * N);
     b->o_tok_item = take(4 * T); b->o_tile_item = take(4 * TL); b->o_tile_p0 = take(4 * TL); b->o_n_tiles = take(4);
     b->o_marker_rows = take(4 * M); b->o_mk_start = take(4 * N); b->o_mk_count = take(4 * N);
+    b->o_tq_item = take(4 * TL); b->o_tq_p0 = take(4 * TL); b->o_n_tq = take(4);
     b->o_targets = take(4 * M); b->o_draws = take(8 * MAX_GROUPS * M);
     b->bytes = o;
     if (cudaMalloc(&b->dev, o) != cudaSuccess || cudaMallocHost(&b->host, o) != cudaSuccess ||
@@ -1031,6 +1035,9 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
     b->marker_rows = reinterpret_cast<int32_t*>(base + b->o_marker_rows);
     b->mk_start = reinterpret_cast<int32_t*>(base + b->o_mk_start);
     b->mk_count = reinterpret_cast<int32_t*>(base + b->o_mk_count);
+    b->tq_item = reinterpret_cast<int32_t*>(base + b->o_tq_item);
+    b->tq_p0 = reinterpret_cast<int32_t*>(base + b->o_tq_p0);
+    b->n_tq = reinterpret_cast<int32_t*>(base + b->o_n_tq);
     b->targets = reinterpret_cast<float*>(base + b->o_targets);
     b->draws = reinterpret_cast<double*>(base + b->o_draws);
     *out = b;
@@ -1081,8 +1088,10 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
     int32_t* hmr = reinterpret_cast<int32_t*>(h + b->o_marker_rows);
     int32_t* hms = reinterpret_cast<int32_t*>(h + b->o_mk_start);
     int32_t* hmc = reinterpret_cast<int32_t*>(h + b->o_mk_count);
+    int32_t* hqi = reinterpret_cast<int32_t*>(h + b->o_tq_item);
+    int32_t* hqp = reinterpret_cast<int32_t*>(h + b->o_tq_p0);
     std::memcpy(h + b->o_ids, ids, sizeof(int32_t) * T);
-    int start = 0, mk = 0, tiles = 0;
+    int start = 0, mk = 0, tiles = 0, tq = 0;
     double pg = 0, pl = 0;
     for (int i = 0; i < n_items; ++i) {
         const double L = seg_len[i];
@@ -1094,6 +1103,7 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
         hs[i] = start; hl[i] = seg_len[i]; hq[i] = qtype[i]; hms[i] = mk; hmc[i] = marker_count[i];
         for (int p = 0; p < seg_len[i]; ++p) hti[start + p] = i;
         for (int p0 = 0; p0 < seg_len[i]; p0 += 64) { hit[tiles] = i; hp0[tiles] = p0; ++tiles; }
+        for (int p0 = 0; p0 < seg_len[i]; p0 += 128) { hqi[tq] = i; hqp[tq] = p0; ++tq; }
         for (int k = 0; k < marker_count[i]; ++k) {
             const int pos = std::max(0, markers[mk + k]);   // TrainableDecisionModel.cs:275
             if (pos >= seg_len[i]) { set_error("marker position past the end of its segment"); return ERR_OUT_OF_RANGE; }
@@ -1103,6 +1113,7 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
         mk += marker_count[i];
     }
     *reinterpret_cast<int32_t*>(h + b->o_n_tiles) = tiles;
+    *reinterpret_cast<int32_t*>(h + b->o_n_tq) = tq;
     if (targets) std::memcpy(h + b->o_targets, targets, sizeof(float) * M);
     else std::memset(h + b->o_targets, 0, sizeof(float) * M);
     if (groups > 0) {
@@ -1111,6 +1122,7 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
                                                         sizeof(double) * M);
     }
     b->T = static_cast<int>(T); b->n = n_items; b->M = static_cast<int>(M); b->tiles = tiles; b->groups = groups;
+    b->tq = tq;
     b->pairs_global = pg;
     b->pairs_local = pl;
     b->version++;

@@ -49,6 +49,9 @@ struct Args {
     __nv_bfloat16* dqkv; int lddq;                                   // backward output [T, lddq]
     const __nv_bfloat16* qkv_lo;                                     // accurate forward: low parts of qkv (else null)
     __nv_bfloat16* out_lo;                                           // accurate forward: context low part
+    // the tcgen05 forward (head_dim 64): 128-row query tiles of every segment, and the token count
+    const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq; int max_tq; int T;
+    int* err;
 };
 }  // namespace fa
 // q, k rotated at their segment positions (cosv null: no rotation), v copied, from fp32 or bf16 [T, lds] into bf16
@@ -57,6 +60,7 @@ int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int head
               const int32_t* seg_start, const float* cosv, const float* sinv, __nv_bfloat16* hi, __nv_bfloat16* lo,
               int ldd, cudaStream_t s);
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
+int flash_forward_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: head_dim 64 (ERR_NOT_SUPPORTED otherwise)
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s);
 
 // ---- train_kernels.cu
