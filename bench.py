@@ -54,8 +54,10 @@ def parse():
     ap.add_argument("--cpu-sample-rows", type=int, default=1, help="rows of 512 tokens in one Q8_0 CPU step")
     ap.add_argument("--cpu-train-tokens", type=int, default=256, help="tokens of the CPU fine-tune sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--train-rows", type=int, default=TR_ROWS, help="rows per GPU of the fine-tune step")
-    ap.add_argument("--train-layers", type=int, default=22, help="encoder layers (fewer only for small captures)")
+    ap.add_argument("--train-config", type=int, default=3, choices=[3, 4],
+                    help="3: ModernBERT-base, 32 rows x U{256..1024}; 4: ModernBERT-large, 4 rows x 8192 tokens")
+    ap.add_argument("--train-rows", type=int, default=None, help="rows per GPU of the fine-tune step")
+    ap.add_argument("--train-layers", type=int, default=None, help="encoder layers (fewer only for small captures)")
     ap.add_argument("--kernel", choices=["q8_gemm", "bf16_gemm"],
                     help="time one product alone at the workload's shapes (profiling captures), not the step")
     ap.add_argument("--case", default="wqkv",
@@ -71,10 +73,22 @@ def dist_env():
     return rank, world, local
 
 
-def train_config(world, tokens, forward, rows=TR_ROWS):
-    return {"workload": TR_WORKLOAD, "rows_per_gpu": rows, "valid_len": f"U{{{TR_MIN}..{TR_MAX}}}",
+# fine-tune geometries: (hidden, intermediate, layers, heads, rows per GPU, min length, max length)
+TRAIN_CONFIGS = {3: (768, 1152, 22, 12, TR_ROWS, TR_MIN, TR_MAX), 4: (1024, 2624, 28, 16, 4, 8192, 8192)}
+GEOMETRY = {3: "ModernBERT-base 22x768 (12x64, GeGLU 1152, local 128 / global every 3rd) + 2 head layers",
+            4: "ModernBERT-large 28x1024 (16x64, GeGLU 2624, local 128 / global every 3rd) + 2 head layers"}
+
+
+def train_shape(args):
+    H, I, layers, heads, rows, lo, hi = TRAIN_CONFIGS[args.train_config]
+    return (H, I, args.train_layers or layers, heads, args.train_rows or rows, lo, hi)
+
+
+def train_config(world, tokens, forward, rows=TR_ROWS, which=3, lens=(TR_MIN, TR_MAX)):
+    return {"workload": TR_WORKLOAD if which == 3 else "config4_large_long_context_finetune_step", "rows_per_gpu": rows,
+            "valid_len": f"U{{{lens[0]}..{lens[1]}}}" if lens[0] != lens[1] else str(lens[0]),
             "tokens_per_gpu_step": tokens,
-            "geometry": "ModernBERT-base 22x768 (12x64, GeGLU 1152, local 128 / global every 3rd) + 2 head layers",
+            "geometry": GEOMETRY[which],
             "optimizer": "RLCD (4 groups) + clip 1.0 + AdamW, fp32 masters, bf16 products",
             "forward": forward, "l2": "inputs larger than L2 (0.66 GB fp32 parameters + ~30 GB tape per step)",
             "parallelism": f"dp{world}, NCCL allreduce in 25 MB buckets overlapped with the backward" if world > 1
@@ -322,11 +336,11 @@ def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
     from laya_b200 import workloads
     from laya_b200.workloads import mix
     rank, world, local = d.rank, d.world, d.local
-    w = workloads.training_weights(layers=args.train_layers, seed=0)   # the same weights on every rank
-    rows = args.train_rows
-    tr = laya_b200.Trainer(laya_b200.base_desc(max_tokens=rows * TR_MAX, max_items=rows, max_markers=rows * 8,
-                                               layers=args.train_layers),
-                           laya_b200.train_desc(max_segment=TR_MAX, forward_mode=forward_mode), device=local)
+    H, I, layers, heads, rows, lo, hi = train_shape(args)
+    w = workloads.training_weights(hidden=H, intermediate=I, layers=layers, seed=0)   # the same weights on every rank
+    tr = laya_b200.Trainer(laya_b200.base_desc(hidden=H, intermediate=I, heads=heads, layers=layers,
+                                               max_tokens=rows * hi, max_items=rows, max_markers=rows * 8),
+                           laya_b200.train_desc(max_segment=hi, forward_mode=forward_mode), device=local)
     if world > 1:
         uid = d.broadcast_bytes(laya_b200.Trainer.unique_id() if rank == 0 else None)
         tr.comm_init(uid, rank, world)
@@ -335,7 +349,7 @@ def train_measure(args, d, forward_mode, with_e2e=True, with_profile=True):
     tr.load(w)
     del w
     # two batches per rank staged on the device before the timed region (data seed 1000 + rank)
-    sets = [workloads.training_batch(rows=rows, min_len=TR_MIN, max_len=TR_MAX, seed=1000 + rank + 64 * i,
+    sets = [workloads.training_batch(rows=rows, min_len=lo, max_len=hi, seed=1000 + rank + 64 * i,
                                      groups=TR_GROUPS) for i in range(2)]
     batches = [tr.batch(items, draws) for items, draws in sets]
     tokens = [sum(len(it.token_ids) for it in items) for items, _ in sets]
@@ -544,7 +558,8 @@ def run_ours(args):
                 "metric": "fine-tune tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": train_config(world, r["tokens_per_step"], fwd, args.train_rows),
+                "config": train_config(world, r["tokens_per_step"], fwd, train_shape(args)[4], args.train_config,
+                                       train_shape(args)[5:]),
                 "e2e": {"value": step_tokens / (e2e_ms / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": r["d2h"] * world,
                         "ms_per_step": e2e_ms},

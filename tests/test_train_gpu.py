@@ -284,6 +284,34 @@ def test_bf16_forward_mode_is_at_bf16_noise_level(cuda):
     t.close()
 
 
+def test_large_geometry_matches_the_oracle(cuda):
+    """ModernBERT-large widths (config 4: hidden 1024, 16 heads × 64, GeGLU 2624; head 16 × 64, ff 4096) on two encoder
+    layers (global and sliding ±64), rows past the window: logits and every gradient against the oracle."""
+    import torch
+    import laya_b200
+    from laya_b200.workloads import training_batch, training_weights
+    from oracle.model import EncoderConfig
+    from oracle.train import TorchTrainModel
+    cfg = EncoderConfig(hidden=1024, intermediate=2624, layers=2, heads=16, vocab=3000)
+    w = training_weights(hidden=1024, intermediate=2624, layers=2, vocab=3000, seed=5)
+    items, _ = training_batch(rows=2, min_len=200, max_len=400, vocab=3000, seed=6)
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=1024, max_items=4, max_markers=32),
+                          laya_b200.train_desc(max_segment=8192))
+    t.load(w)
+    b = t.batch(items)
+    logits = t.forward(b, training=False)
+    m = TorchTrainModel(cfg, w)
+    oi = [{"ids": it.token_ids, "markers": list(it.marker_positions), "qtype": it.question_type} for it in items]
+    ref = m.forward(oi, training=False)
+    coeff = [np.random.default_rng(11).standard_normal(it.options).astype(np.float32) for it in items]
+    sum((r * torch.from_numpy(c)).sum() for r, c in zip(ref, coeff)).backward()
+    for l, r in zip(logits, ref):
+        assert max_rel(l, r.detach().numpy()) <= TOL
+    t.backward(b, coeff)
+    check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")], elementwise=False)
+    t.close()
+
+
 def test_errors_are_reported_like_the_reference(tiny_trainer):
     """Token ids outside the vocabulary and markers past their segment: ArgumentOutOfRangeException's code; a batch
     larger than the trainer, or an objective before any forward: ArgumentException's."""
