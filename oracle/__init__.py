@@ -73,6 +73,14 @@ def lib():
             "lo_attention": (None, [_f32p, _c.c_int, _c.c_int, _i32p, _i32p, _c.c_int, _c.c_int, _c.c_void_p,
                                     _c.c_void_p, _f32p]),
             "lo_add": (None, [_f32p, _f32p, _c.c_long]),
+            "lo_rms_norm_rows": (None, [_f32p, _c.c_int, _c.c_int, _f32p, _c.c_float, _f32p]),
+            "lo_silu_vec": (None, [_f32p, _c.c_long]),
+            "lo_silu_multiply": (None, [_f32p, _c.c_int, _c.c_int, _f32p]),
+            "lo_multiply_sigmoid": (None, [_f32p, _f32p, _c.c_long]),
+            "lo_l2_normalize": (None, [_f32p, _c.c_int, _c.c_float, _c.c_float]),
+            "lo_rms_norm_gated": (None, [_f32p, _f32p, _f32p, _c.c_int, _c.c_float, _f32p]),
+            "lo_delta_rule": (None, [_f32p, _c.c_int, _c.c_int, _c.c_int, _f32p, _f32p, _f32p, _c.c_int, _f32p,
+                                     _f32p, _c.c_int, _f32p, _c.c_int]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -414,3 +414,107 @@ void lo_add(float *dst, const float *src, long n)
     #pragma omp parallel for schedule(static)
     for (long i = 0; i < n; ++i) dst[i] += src[i];
 }
+
+/* ------------------------------------------------------------------------------------------------ */
+/* The Qwen3.5 decoder behind Mica (DecoderKernels.cs, Qwen35Model.cs) */
+
+/* DecoderKernels.SumOfSquares (DecoderKernels.cs:15-28): lane accumulators by FMA, Vector.Sum, scalar tail. */
+static float lo_sum_squares(const float *v, int n)
+{
+    float acc[LO_W] = {0};
+    int i = 0;
+    for (; i <= n - LO_W; i += LO_W)
+        for (int l = 0; l < LO_W; ++l) acc[l] = fmaf(v[i + l], v[i + l], acc[l]);
+    float s = lo_hsum(acc);
+    for (; i < n; ++i) s += v[i] * v[i];
+    return s;
+}
+
+/* DecoderKernels.RmsNorm (DecoderKernels.cs:34-46): x · (1 / sqrt(Σx²/n + eps)) · scale, scale = 1 + weight. */
+void lo_rms_norm_rows(const float *in, int rows, int n, const float *scale, float eps, float *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const float *x = in + (long)r * n;
+        float *y = out + (long)r * n;
+        float inv = 1.0f / sqrtf(lo_sum_squares(x, n) / (float)n + eps);
+        for (int i = 0; i < n; ++i) y[i] = x[i] * inv * scale[i];
+    }
+}
+
+/* DecoderKernels.Sigmoid / Silu on Vector<float> (DecoderKernels.cs:150-151): 1 / (1 + SimdOps.Exp(-x)). */
+static float lo_sigmoid_vec(float x) { return 1.0f / (1.0f + lo_exp_vec(-x)); }
+
+void lo_silu_vec(float *v, long n)
+{
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; ++i) v[i] = v[i] * lo_sigmoid_vec(v[i]);
+}
+
+/* DecoderKernels.SiluMultiply (DecoderKernels.cs:97-107): silu(gate) · up, rows of width n in [gate | up] rows. */
+void lo_silu_multiply(const float *gate_up, int rows, int n, float *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const float *g = gate_up + (long)r * 2 * n, *u = g + n;
+        for (int i = 0; i < n; ++i) out[(long)r * n + i] = g[i] * lo_sigmoid_vec(g[i]) * u[i];
+    }
+}
+
+/* DecoderKernels.MultiplySigmoid (DecoderKernels.cs:125-135): values · sigmoid(gate). */
+void lo_multiply_sigmoid(float *v, const float *gate, long n)
+{
+    for (long i = 0; i < n; ++i) v[i] = v[i] * lo_sigmoid_vec(gate[i]);
+}
+
+/* DecoderKernels.L2Normalize (DecoderKernels.cs:67-85): x · (1 / sqrt(Σx² + eps)) (· extra). */
+void lo_l2_normalize(float *v, int n, float eps, float extra)
+{
+    float inv = 1.0f / sqrtf(lo_sum_squares(v, n) + eps);
+    for (int i = 0; i < n; ++i) {
+        float x = v[i] * inv;
+        v[i] = extra != 1.0f ? x * extra : x;
+    }
+}
+
+/* DecoderKernels.RmsNormGated (DecoderKernels.cs:52-64): weight · (x · inv) · silu(gate). */
+void lo_rms_norm_gated(const float *in, const float *gate, const float *weight, int n, float eps, float *out)
+{
+    float inv = 1.0f / sqrtf(lo_sum_squares(in, n) / (float)n + eps);
+    for (int i = 0; i < n; ++i) {
+        float g = gate[i];
+        out[i] = weight[i] * (in[i] * inv) * (g * lo_sigmoid_vec(g));
+    }
+}
+
+/* The gated delta rule of one value head (Qwen35Model.Recurrence, Qwen35Model.cs:924-972, the two-sweep form that
+ * DecoderKernels.GatedDeltaRule128 reproduces bit for bit), on a row-major [dk, dv] state, per token:
+ *   S ← S·g;  m = Sᵀk (FMA, i ascending);  δ = (v − m)·β;  S ← S + k ⊗ δ (FMA);  o = Sᵀq (FMA, i ascending). */
+void lo_delta_rule(float *state, int dk, int dv, int rows, const float *q, const float *k, const float *v, int stride,
+                   const float *decay, const float *beta, int gstride, float *out, int ostride)
+{
+    float *m = (float *)malloc(sizeof(float) * dv), *d = (float *)malloc(sizeof(float) * dv);
+    for (int t = 0; t < rows; ++t) {
+        const float *qt = q + (long)t * stride, *kt = k + (long)t * stride, *vt = v + (long)t * stride;
+        const float g = decay[(long)t * gstride], b = beta[(long)t * gstride];
+        float *ot = out + (long)t * ostride;
+        for (int j = 0; j < dv; ++j) m[j] = 0.0f;
+        for (int i = 0; i < dk; ++i) {
+            float *s = state + (long)i * dv;
+            for (int j = 0; j < dv; ++j) {
+                s[j] = s[j] * g;
+                m[j] = fmaf(s[j], kt[i], m[j]);
+            }
+        }
+        for (int j = 0; j < dv; ++j) { d[j] = (vt[j] - m[j]) * b; ot[j] = 0.0f; }
+        for (int i = 0; i < dk; ++i) {
+            float *s = state + (long)i * dv;
+            for (int j = 0; j < dv; ++j) {
+                s[j] = fmaf(d[j], kt[i], s[j]);
+                ot[j] = fmaf(s[j], qt[i], ot[j]);
+            }
+        }
+    }
+    free(m);
+    free(d);
+}
