@@ -9,6 +9,8 @@ host-side mirror of the reference's interfaces for that path, over ctypes:
   * `Q8_0`               — the quantizers on device buffers.
   * `Trainer`, `Batch`   — the fine-tuning step of include/laya_train.h (Laya.Training/TrainableDecisionModel.cs,
                            RlcdObjective.cs, AdamW.cs): forward, objective, backward, clip + AdamW, NCCL buckets.
+  * `Qwen35Model`        — the Mica decoder of include/laya_decoder.h (Mica/Models/Qwen35Model.cs) with Q8_0
+                           products: prefill of packed sequences, final-normed readout, label logits.
 
 There is no CPU fallback: importing works anywhere, but every call needs the built library and a B200; a missing
 library raises `LayaLibraryMissing`.
@@ -17,10 +19,12 @@ from .api import (Context, DecisionModel, DecisionOutput, BatchItem, ModelDesc, 
                   LayaError, LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
                   LayaNotFoundError, LayaDeviceTimeout, LayaLibraryMissing, lib, library_path, base_desc,
                   PRECISION_F32, PRECISION_Q8_0, Trainer, Batch, TrainingItem, TrainDesc, RlcdDesc, train_desc,
-                  FORWARD_ACCURATE, FORWARD_BF16)
+                  FORWARD_ACCURATE, FORWARD_BF16, Qwen35Model, DecoderDesc, decoder_desc, DECODER_LINEAR,
+                  DECODER_FULL)
 
 __all__ = ["Context", "DecisionModel", "DecisionOutput", "BatchItem", "ModelDesc", "PackedMatrixQ8_0", "Q8_0",
            "LayaError", "LayaArgumentError", "LayaOutOfRangeError", "LayaNotSupportedError", "LayaCudaError",
            "LayaNotFoundError", "LayaDeviceTimeout", "LayaLibraryMissing", "lib", "library_path", "base_desc",
            "PRECISION_F32", "PRECISION_Q8_0", "Trainer", "Batch", "TrainingItem", "TrainDesc", "RlcdDesc",
-           "train_desc", "FORWARD_ACCURATE", "FORWARD_BF16"]
+           "train_desc", "FORWARD_ACCURATE", "FORWARD_BF16", "Qwen35Model", "DecoderDesc", "decoder_desc",
+           "DECODER_LINEAR", "DECODER_FULL"]

@@ -129,6 +129,25 @@ _SIGS = {
                                   ctypes.POINTER(ctypes.c_longlong)]),
     "laya_comm_unique_id": (_I, [_P]),
     "laya_train_comm_init": (_I, [_P, _P, _I, _I]),
+    # include/laya_decoder.h
+    "laya_decoder_create": (_I, [_P, _I, ctypes.POINTER(_P)]),
+    "laya_decoder_destroy": (_I, [_P]),
+    "laya_decoder_set_stream": (_I, [_P, _P]),
+    "laya_decoder_get_stream": (_I, [_P, ctypes.POINTER(_P)]),
+    "laya_decoder_synchronize": (_I, [_P]),
+    "laya_decoder_upload": (_I, [_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P]),
+    "laya_decoder_upload_q8_0": (_I, [_P, ctypes.c_char_p, _P, _P, _I, _I]),
+    "laya_decoder_missing": (_I, [_P, ctypes.c_char_p, _I, ctypes.POINTER(_I)]),
+    "laya_decoder_forward": (_I, [_P, _P, _P, _I, _P, _I, _P, _P]),
+    "laya_decoder_forward_device": (_I, [_P, _P, _P, _I, _P, _I, _P, _P]),
+    "laya_decoder_logits": (_I, [_P, _P, _I, _P, _I, _P]),
+    "laya_decoder_layer": (_I, [_P, _I, _P, _P, _I, _P]),
+    "laya_decoder_record_enable": (_I, [_P, _I]),
+    "laya_decoder_record_get": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
+    "laya_decoder_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_decoder_set_profiling": (_I, [_P, _I]),
+    "laya_decoder_profile": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(ctypes.c_longlong)]),
 }
 
 
@@ -658,3 +677,154 @@ class Trainer:
     def comm_init(self, uid: bytes, rank: int, world: int):
         buf = ctypes.create_string_buffer(bytes(uid), 128)
         check(lib().laya_train_comm_init(self.handle, buf, rank, world))
+
+
+# --------------------------------------------------------------------------------------------------- Mica decoder
+DECODER_LINEAR, DECODER_FULL = 0, 1
+
+
+class DecoderDesc(ctypes.Structure):
+    """laya_decoder_desc: Qwen35Config (Mica/Models/Qwen35Config.cs:60-130) plus the capacity of one forward."""
+    _fields_ = [("hidden", ctypes.c_int), ("intermediate", ctypes.c_int), ("layers", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("eps", ctypes.c_float), ("layer_kinds", ctypes.POINTER(ctypes.c_int32)),
+                ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("rope_theta", ctypes.c_double), ("rotary_dim", ctypes.c_int), ("lin_k_heads", ctypes.c_int),
+                ("lin_v_heads", ctypes.c_int), ("lin_k_dim", ctypes.c_int), ("lin_v_dim", ctypes.c_int),
+                ("conv_kernel", ctypes.c_int), ("max_tokens", ctypes.c_int), ("max_seqs", ctypes.c_int)]
+
+
+def decoder_desc(kinds: Sequence[str], **kw) -> DecoderDesc:
+    """A DecoderDesc from layer kinds ("linear" | "full") and Qwen35Config fields; defaults are config 5's geometry
+    (h 2560, I 9216, vocab 151936, 16 q / 4 kv heads × 128 with a quarter rotated at θ 1e7, DeltaNet 16 × 128 key and
+    value heads, conv 4)."""
+    d = dict(hidden=2560, intermediate=9216, vocab=151936, eps=1e-6, heads=16, kv_heads=4, head_dim=128,
+             rope_theta=1e7, rotary_dim=32, lin_k_heads=16, lin_v_heads=16, lin_k_dim=128, lin_v_dim=128,
+             conv_kernel=4, max_tokens=16384, max_seqs=8)
+    d.update(kw)
+    arr = (ctypes.c_int32 * max(1, len(kinds)))(*[DECODER_FULL if k == "full" else DECODER_LINEAR for k in kinds])
+    desc = DecoderDesc(layers=len(kinds), **d)
+    desc.layer_kinds = ctypes.cast(arr, ctypes.POINTER(ctypes.c_int32))
+    desc._kinds_keepalive = arr
+    return desc
+
+
+class Qwen35Model:
+    """The Mica decoder on one B200 (include/laya_decoder.h), mirroring Qwen35Model (Mica/Models/Qwen35Model.cs)
+    with WeightPrecision.Q8_0: construct, `load(weights)` by checkpoint names, `forward(sequences, labels)` — every
+    sequence from an empty state, returning each sequence's final-normed last hidden row (Qwen35Sequence.Hidden) and
+    the label logits (Logits → TokenTable.QuantizedLogits) — `logits(hidden, ids)`, `layer(i, hidden, seq_lens)`."""
+
+    def __init__(self, desc: DecoderDesc, device: int = 0):
+        self.desc = desc
+        h = ctypes.c_void_p()
+        check(lib().laya_decoder_create(ctypes.byref(desc), device, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def upload(self, name: str, array: np.ndarray):
+        a = np.ascontiguousarray(array)
+        if a.dtype == np.float16:
+            dt = F16
+        else:
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            dt = F32
+        shape = (ctypes.c_int64 * max(1, a.ndim))(*a.shape)
+        check(lib().laya_decoder_upload(self.handle, name.encode(), dt, shape, a.ndim, _np_ptr(a)))
+
+    def upload_bf16_bits(self, name: str, bits: np.ndarray):
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        shape = (ctypes.c_int64 * max(1, a.ndim))(*a.shape)
+        check(lib().laya_decoder_upload(self.handle, name.encode(), BF16, shape, a.ndim, _np_ptr(a)))
+
+    def upload_q8_0(self, name: str, q: np.ndarray, d_fp16: np.ndarray):
+        q = np.ascontiguousarray(q, dtype=np.int8)
+        d = np.ascontiguousarray(d_fp16, dtype=np.float16).view(np.uint16)
+        N, K = q.shape
+        check(lib().laya_decoder_upload_q8_0(self.handle, name.encode(), _np_ptr(q), _np_ptr(d), N, K))
+
+    def load(self, weights: Dict[str, np.ndarray]):
+        for name, w in weights.items():
+            if name.endswith("lm_head.weight"):
+                continue
+            self.upload(name, w)
+
+    def missing(self) -> List[str]:
+        n = ctypes.c_int()
+        buf = ctypes.create_string_buffer(1 << 16)
+        check(lib().laya_decoder_missing(self.handle, buf, len(buf), ctypes.byref(n)))
+        return [x for x in buf.value.decode().split("\n") if x]
+
+    @staticmethod
+    def pack(sequences: Sequence[np.ndarray]):
+        lens = _i32([len(s) for s in sequences])
+        ids = _i32(np.concatenate([np.asarray(s, np.int64) for s in sequences]) if len(sequences) else [])
+        return ids, lens
+
+    def forward(self, sequences: Sequence[np.ndarray], labels: Optional[Sequence[int]] = None):
+        """Returns (hidden [n_seq, hidden], logits [n_seq, n_labels] or None)."""
+        ids, lens = self.pack(sequences)
+        lab = None if labels is None else _i32(labels)
+        hidden = np.zeros((len(sequences), self.desc.hidden), np.float32)
+        logits = None if lab is None else np.zeros((len(sequences), len(lab)), np.float32)
+        check(lib().laya_decoder_forward(self.handle, _np_ptr(ids), _np_ptr(lens), len(sequences), _np_ptr(lab),
+                                         0 if lab is None else len(lab), _np_ptr(hidden), _np_ptr(logits)))
+        return hidden, logits
+
+    def forward_device(self, ids_ptr: int, seq_lens: Sequence[int], labels: Sequence[int], hidden_ptr: int,
+                       logits_ptr: int):
+        lens, lab = _i32(seq_lens), _i32(labels)
+        check(lib().laya_decoder_forward_device(self.handle, ctypes.c_void_p(ids_ptr), _np_ptr(lens), len(lens),
+                                                _np_ptr(lab), len(lab), ctypes.c_void_p(hidden_ptr or 0),
+                                                ctypes.c_void_p(logits_ptr or 0)))
+
+    def logits(self, hidden: np.ndarray, ids: Sequence[int]) -> np.ndarray:
+        h = _f32(hidden).reshape(-1, self.desc.hidden)
+        lab = _i32(ids)
+        out = np.zeros((h.shape[0], len(lab)), np.float32)
+        check(lib().laya_decoder_logits(self.handle, _np_ptr(h), h.shape[0], _np_ptr(lab), len(lab), _np_ptr(out)))
+        return out
+
+    def layer(self, i: int, hidden: np.ndarray, seq_lens: Sequence[int]):
+        """One layer on hidden [T, hidden]: returns (mixer output, layer output)."""
+        x = _f32(hidden).copy()
+        lens = _i32(seq_lens)
+        mixer = np.zeros_like(x)
+        check(lib().laya_decoder_layer(self.handle, i, _np_ptr(x), _np_ptr(lens), len(lens), _np_ptr(mixer)))
+        return mixer, x
+
+    def record(self, enabled: bool):
+        check(lib().laya_decoder_record_enable(self.handle, 1 if enabled else 0))
+
+    def recorded(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(shape, np.float32)
+        check(lib().laya_decoder_record_get(self.handle, name.encode(), _np_ptr(out), out.size))
+        return out
+
+    def synchronize(self):
+        check(lib().laya_decoder_synchronize(self.handle))
+
+    def set_stream(self, stream_handle: Optional[int]):
+        check(lib().laya_decoder_set_stream(self.handle, ctypes.c_void_p(stream_handle or 0)))
+
+    def launches(self) -> int:
+        n = ctypes.c_longlong()
+        check(lib().laya_decoder_launches(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def set_profiling(self, enabled: bool):
+        check(lib().laya_decoder_set_profiling(self.handle, 1 if enabled else 0))
+
+    def profile(self, kind: int) -> Tuple[float, float, int]:
+        ms, ops, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_longlong()
+        check(lib().laya_decoder_profile(self.handle, kind, ctypes.byref(ms), ctypes.byref(ops), ctypes.byref(n)))
+        return ms.value, ops.value, n.value

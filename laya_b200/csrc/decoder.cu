@@ -1,0 +1,917 @@
+// decoder.cu — the Mica decoder behind include/laya_decoder.h: weights, workspace and the order of kernels of one
+// prefill (Qwen35Model.Forward, Mica/Models/Qwen35Model.cs:462-532) with every projection a Q8_0 product
+// (q8_gemm.cu) and the rest in decoder_kernels.cu.
+//
+// Device state:
+//   weights     per layer the stacked Q8_0 projections (fp16-held codes [N, K], block scales [K/32, ldw]) — DeltaNet
+//               in_proj [qkv | z | b | a] and out_proj, or attention [q·gate | k | v] and o_proj; MLP [gate | up]
+//               and down — plus the fp32 norms (1 + w), conv taps [K, conv_dim], −exp(A_log), dt_bias; the Q8_0
+//               token table [vocab, hidden] serves the embedding rows and the tied head.
+//   workspace   sized for max_tokens rows: the residual stream x [T, h] fp32; one projection output [T, widest];
+//               the DeltaNet conv/q/k/v [T, conv_dim] and core [T, value_dim]; fp16 q/k/v of full attention; the
+//               activation codes of the next product [T, widest K] with scales [widest K/32, ldx]; β and decay.
+//   inputs      ids, row → sequence, sequence starts and lengths, the 64-query tiles of full attention and the label
+//               ids travel in one pinned staging buffer and one host→device copy per forward.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/laya_b200.h"
+#include "../../include/laya_decoder.h"
+#include "common.cuh"
+#include "decoder.h"
+#include "internal.h"
+
+using namespace laya;
+
+namespace {
+
+#define RC(x)                      \
+    do {                           \
+        int rc_ = (x);             \
+        if (rc_ != OK) return rc_; \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int rup(int x, int m) { return (x + m - 1) / m * m; }
+
+float half_bits(uint16_t b) {
+    __half h;
+    memcpy(&h, &b, 2);
+    return __half2float(h);
+}
+float bf16_bits(uint16_t b) {
+    const uint32_t u = static_cast<uint32_t>(b) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+// A Q8_0 matrix whose rows may be filled piecewise (the stacked projections).
+struct QMat {
+    q8::code_t* q = nullptr;
+    float* d = nullptr;
+    int N = 0, K = 0, ldw = 0;
+};
+
+struct Part {          // a checkpoint tensor that is rows [row0, row0 + rows) of a stacked Q8_0 matrix
+    QMat* m;
+    int row0, rows;
+};
+
+struct Layer {
+    int kind = LAYA_DECODER_LINEAR;
+    QMat mix_in, mix_out, gate_up, down;   // in_proj | qkv; out_proj | o_proj; MLP
+    float *in_norm = nullptr, *post_norm = nullptr;
+    float *conv_w = nullptr, *neg_a = nullptr, *dt_bias = nullptr, *gnorm = nullptr;   // DeltaNet
+    float *qnorm = nullptr, *knorm = nullptr;                                         // full attention
+};
+
+// Vector parameters: destination and the transform applied on upload.
+enum VecKind { V_PLAIN = 0, V_ONE_PLUS = 1, V_NEG_EXP = 2, V_CONV = 3 };
+struct Vec {
+    float** dst;
+    int64_t count;
+    VecKind kind;
+};
+
+}  // namespace
+
+struct laya_decoder {
+    int device = 0;
+    cudaStream_t own = nullptr, stream = nullptr;
+    laya_decoder_desc d{};
+    std::vector<int> kinds;
+    int* err = nullptr;
+
+    // geometry
+    int cd = 0, key_dim = 0, vd = 0, nin = 0, ld_in = 0, q_width = 0, nqkv = 0, half = 0, maxK = 0, ldx = 0,
+        widest = 0, core_w = 0;
+
+    std::vector<Layer> layers;
+    QMat table;
+    float* final_norm = nullptr;
+    std::map<std::string, Part> parts;
+    std::map<std::string, Vec> vecs;
+    std::set<std::string> have;
+
+    // workspace
+    float *x = nullptr, *big = nullptr, *conv = nullptr, *core = nullptr, *beta = nullptr, *decay = nullptr,
+          *mix = nullptr;
+    __half *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
+    q8::code_t* qa = nullptr;
+    float* da = nullptr;
+    float *cosv = nullptr, *sinv = nullptr;
+    // readout
+    float *hid = nullptr, *dlast = nullptr, *logit_buf = nullptr;
+    q8::code_t* qlast = nullptr;
+    int ldl = 0, logit_cap = 0;
+    // inputs
+    int32_t* in_dev = nullptr;
+    int32_t* in_host = nullptr;
+    size_t in_cap = 0;
+    cudaEvent_t in_done = nullptr;
+    bool in_pending = false;
+    int32_t *ids = nullptr, *tok_seq = nullptr, *seq_start = nullptr, *seq_len = nullptr, *last_row = nullptr,
+            *tile_seq = nullptr, *tile_p0 = nullptr, *labels = nullptr;
+    int n_tiles = 0;
+
+    // profiling: 0 products, 1 delta rule, 2 full attention
+    bool profiling = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
+    std::vector<std::pair<int, double>> ev_work;
+    double prof_ms[3] = {0, 0, 0}, prof_ops[3] = {0, 0, 0};
+    long long prof_n[3] = {0, 0, 0};
+
+    // recorder
+    bool record = false;
+    std::map<std::string, std::pair<float*, size_t>> rec;
+
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+int dalloc(laya_decoder* c, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    c->allocs.push_back(*p);
+    return OK;
+}
+template <class T>
+int dalloc_t(laya_decoder* c, T** p, size_t count) {
+    return dalloc(c, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+int alloc_qmat(laya_decoder* c, QMat& m, int N, int K) {
+    m.N = N; m.K = K; m.ldw = rup(N, 128);
+    RC(dalloc_t(c, &m.q, static_cast<size_t>(N) * K));
+    RC(dalloc_t(c, &m.d, static_cast<size_t>(K / 32) * m.ldw));
+    LAYA_CUDA(cudaMemsetAsync(m.d, 0, sizeof(float) * static_cast<size_t>(K / 32) * m.ldw, c->stream));
+    return OK;
+}
+
+template <class F>
+int timed(laya_decoder* c, int kind, double ops, F&& launch) {
+    if (!c->profiling) return launch();
+    if (c->ev_work.size() == c->ev_pool.size()) {
+        cudaEvent_t e0, e1;
+        LAYA_CUDA(cudaEventCreate(&e0));
+        LAYA_CUDA(cudaEventCreate(&e1));
+        c->ev_pool.push_back({e0, e1});
+    }
+    auto& ev = c->ev_pool[c->ev_work.size()];
+    LAYA_CUDA(cudaEventRecord(ev.first, c->stream));
+    const int rc = launch();
+    LAYA_CUDA(cudaEventRecord(ev.second, c->stream));
+    c->ev_work.push_back({kind, ops});
+    return rc;
+}
+
+int collect_profile(laya_decoder* c) {
+    if (c->ev_work.empty()) return OK;
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    for (size_t i = 0; i < c->ev_work.size(); ++i) {
+        float ms = 0;
+        LAYA_CUDA(cudaEventElapsedTime(&ms, c->ev_pool[i].first, c->ev_pool[i].second));
+        const int k = c->ev_work[i].first;
+        c->prof_ms[k] += ms;
+        c->prof_ops[k] += c->ev_work[i].second;
+        c->prof_n[k] += 1;
+    }
+    c->ev_work.clear();
+    return OK;
+}
+
+int check_device_error(laya_decoder* c) {
+    int h = 0;
+    LAYA_CUDA(cudaMemcpyAsync(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    if (h != 0) {
+        LAYA_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+        LAYA_CUDA(cudaStreamSynchronize(c->stream));
+        if (h == LAYA_DEV_ERR_TIMEOUT) { set_error("a device-side wait timed out"); return ERR_DEVICE_TIMEOUT; }
+        set_error("token id outside the vocabulary");
+        return ERR_OUT_OF_RANGE;
+    }
+    return OK;
+}
+
+int record_copy(laya_decoder* c, const std::string& name, const float* src, size_t count) {
+    if (!c->record) return OK;
+    auto& b = c->rec[name];
+    if (b.second < count) {
+        if (b.first) cudaFree(b.first);
+        b.first = nullptr;
+        LAYA_CUDA(cudaMalloc(&b.first, count * sizeof(float)));
+        b.second = count;
+    }
+    LAYA_CUDA(cudaMemcpyAsync(b.first, src, count * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    return OK;
+}
+
+// y = Q8(x) · Wᵀ with the codes of x already in (c->qa, c->da).
+int product(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo) {
+    q8::GemmArgs a{};
+    a.M = T; a.N = w.N; a.K = w.K;
+    a.qx = c->qa; a.dx = c->da; a.ldx = c->ldx;
+    a.qw = w.q; a.dw = w.d; a.ldw = w.ldw;
+    a.epi = epi;
+    a.out = out; a.ldo = ldo;
+    a.err = c->err;
+    return timed(c, 0, 2.0 * T * static_cast<double>(w.N) * w.K, [&] { return q8::gemm(a, c->stream); });
+}
+
+int rms_codes(laya_decoder* c, const float* scale, int T) {
+    dec::RmsArgs r{};
+    r.rows = T; r.n = c->d.hidden; r.x = c->x; r.scale = scale; r.eps = c->d.eps;
+    r.q = c->qa; r.d = c->da; r.ldd = c->ldx;
+    return dec_rms_q8(r, c->stream);
+}
+
+// The mixer's output goes into the residual stream (the product's residual epilogue), or, when recording, into
+// c->mix first and then x += mix.
+int mixer_out(laya_decoder* c, const QMat& w, int T, int layer, bool keep_mix) {
+    const int h = c->d.hidden;
+    if (!c->record && !keep_mix) return product(c, w, T, q8::EPI_RESID, c->x, h);
+    RC(product(c, w, T, q8::EPI_STORE, c->mix, h));
+    RC(record_copy(c, "layers." + std::to_string(layer) + ".mixer", c->mix, static_cast<size_t>(T) * h));
+    return dec_add(c->x, c->mix, static_cast<size_t>(T) * h, c->stream);
+}
+
+// LinearAttention (Qwen35Model.cs:784-921).
+int linear_mixer(laya_decoder* c, const Layer& L, int T, int n_seq, int layer, bool keep_mix) {
+    const laya_decoder_desc& d = c->d;
+    RC(rms_codes(c, L.in_norm, T));
+    RC(product(c, L.mix_in, T, q8::EPI_STORE, c->big, c->ld_in));
+    dec::ConvArgs cv{};
+    cv.T = T; cv.cd = c->cd; cv.K = d.conv_kernel; cv.in = c->big; cv.ld_in = c->ld_in; cv.w = L.conv_w;
+    cv.tok_seq = c->tok_seq; cv.seq_start = c->seq_start; cv.out = c->conv;
+    RC(dec_conv_silu(cv, c->stream));
+    dec::HeadsArgs hd{};
+    hd.T = T; hd.kh = d.lin_k_heads; hd.vh = d.lin_v_heads; hd.dk = d.lin_k_dim; hd.key_dim = c->key_dim; hd.cd = c->cd;
+    hd.conv = c->conv; hd.qscale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.lin_k_dim)));
+    hd.proj = c->big; hd.ld_proj = c->ld_in; hd.b_col = c->cd + c->vd; hd.a_col = c->cd + c->vd + d.lin_v_heads;
+    hd.dt_bias = L.dt_bias; hd.neg_a = L.neg_a; hd.beta = c->beta; hd.decay = c->decay;
+    RC(dec_deltanet_heads(hd, c->stream));
+    dec::DeltaArgs dr{};
+    dr.dk = d.lin_k_dim; dr.dv = d.lin_v_dim; dr.vh = d.lin_v_heads; dr.ratio = d.lin_v_heads / d.lin_k_heads;
+    dr.key_dim = c->key_dim; dr.cd = c->cd; dr.conv = c->conv; dr.beta = c->beta; dr.decay = c->decay;
+    dr.seq_start = c->seq_start; dr.seq_len = c->seq_len; dr.out = c->core; dr.ld_out = c->vd;
+    const double rule_ops = static_cast<double>(T) * d.lin_v_heads * d.lin_k_dim * d.lin_v_dim * 8.0;
+    RC(timed(c, 1, rule_ops, [&] { return dec_delta_rule(dr, n_seq, c->stream); }));
+    dec::GatedArgs gn{};
+    gn.T = T; gn.vh = d.lin_v_heads; gn.dv = d.lin_v_dim; gn.core = c->core; gn.ld_core = c->vd;
+    gn.z = c->big + c->cd; gn.ld_z = c->ld_in; gn.weight = L.gnorm; gn.eps = d.eps; gn.out = c->core; gn.ld_out = c->vd;
+    RC(dec_gated_norm(gn, c->stream));
+    RC(q8::quantize_activations(c->core, T, c->vd, c->vd, c->qa, c->da, c->ldx, c->stream));
+    return mixer_out(c, L.mix_out, T, layer, keep_mix);
+}
+
+// FullAttention (Qwen35Model.cs:628-731).
+int full_mixer(laya_decoder* c, const Layer& L, int T, long long pairs, int layer, bool keep_mix) {
+    const laya_decoder_desc& d = c->d;
+    RC(rms_codes(c, L.in_norm, T));
+    RC(product(c, L.mix_in, T, q8::EPI_STORE, c->big, c->nqkv));
+    dec::PrepArgs pp{};
+    pp.T = T; pp.heads = d.heads; pp.kv_heads = d.kv_heads; pp.hd = d.head_dim; pp.half = c->half;
+    pp.q_width = c->q_width; pp.qkv = c->big; pp.ld_qkv = c->nqkv; pp.qnorm = L.qnorm; pp.knorm = L.knorm;
+    pp.eps = d.eps; pp.cosv = c->cosv; pp.sinv = c->sinv; pp.tok_seq = c->tok_seq; pp.seq_start = c->seq_start;
+    pp.q16 = c->q16; pp.k16 = c->k16; pp.v16 = c->v16;
+    dec::AttnArgs at{};
+    at.heads = d.heads; at.kv_heads = d.kv_heads; at.q16 = c->q16; at.k16 = c->k16; at.v16 = c->v16;
+    at.tile_seq = c->tile_seq; at.tile_p0 = c->tile_p0; at.seq_start = c->seq_start; at.seq_len = c->seq_len;
+    at.scale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.head_dim)));
+    at.qkv = c->big; at.ld_qkv = c->nqkv; at.out = c->core; at.ld_out = d.heads * d.head_dim;
+    const double att_ops = 4.0 * static_cast<double>(pairs) * d.heads * d.head_dim;
+    RC(timed(c, 2, att_ops, [&] {
+        int rc = dec_attn_prep(pp, c->stream);
+        return rc != OK ? rc : dec_attention(at, c->n_tiles, d.head_dim, c->stream);
+    }));
+    RC(q8::quantize_activations(c->core, T, d.heads * d.head_dim, d.heads * d.head_dim, c->qa, c->da, c->ldx, c->stream));
+    return mixer_out(c, L.mix_out, T, layer, keep_mix);
+}
+
+// Mlp (Qwen35Model.cs:602-621): silu(gate) · up fused with the codes of the down projection.
+int mlp(laya_decoder* c, const Layer& L, int T) {
+    const int I = c->d.intermediate;
+    RC(rms_codes(c, L.post_norm, T));
+    RC(product(c, L.gate_up, T, q8::EPI_STORE, c->big, 2 * I));
+    RC(dec_swiglu_q8(c->big, T, I, c->qa, c->da, c->ldx, c->stream));
+    return product(c, L.down, T, q8::EPI_RESID, c->x, c->d.hidden);
+}
+
+int run_layer(laya_decoder* c, int i, int T, int n_seq, long long pairs, bool keep_mix) {
+    const Layer& L = c->layers[i];
+    if (L.kind == LAYA_DECODER_FULL) RC(full_mixer(c, L, T, pairs, i, keep_mix));
+    else RC(linear_mixer(c, L, T, n_seq, i, keep_mix));
+    RC(mlp(c, L, T));
+    return record_copy(c, "layers." + std::to_string(i), c->x, static_cast<size_t>(T) * c->d.hidden);
+}
+
+// Host metadata of one forward → pinned staging → one copy.  Returns the causal (query, key) pairs of full attention.
+int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int n_seq, const int32_t* labels,
+          int n_labels, int* T_out, long long* pairs_out) {
+    if (n_seq <= 0 || n_seq > c->d.max_seqs) { set_error("sequence count outside 1..max_seqs"); return ERR_ARGUMENT; }
+    long long T = 0, pairs = 0;
+    int tiles = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        if (seq_len[s] <= 0) { set_error("every sequence needs at least one token"); return ERR_ARGUMENT; }
+        T += seq_len[s];
+        pairs += static_cast<long long>(seq_len[s]) * (seq_len[s] + 1) / 2;
+        tiles += (seq_len[s] + 63) / 64;
+    }
+    if (T > c->d.max_tokens) { set_error("more tokens than max_tokens"); return ERR_ARGUMENT; }
+    if (n_labels < 0 || (n_labels > 0 && !labels)) { set_error("invalid label list"); return ERR_ARGUMENT; }
+    for (int l = 0; l < n_labels; ++l)
+        if (labels[l] < 0 || labels[l] >= c->d.vocab) { set_error("label id outside the vocabulary"); return ERR_OUT_OF_RANGE; }
+    const size_t need = static_cast<size_t>(ids_host ? T : 0) + T + 3 * static_cast<size_t>(n_seq) + 2 * tiles + n_labels;
+    if (c->in_pending) { LAYA_CUDA(cudaEventSynchronize(c->in_done)); c->in_pending = false; }
+    if (need > c->in_cap) {
+        if (c->in_host) cudaFreeHost(c->in_host);
+        if (c->in_dev) cudaFree(c->in_dev);
+        c->in_host = nullptr; c->in_dev = nullptr;
+        c->in_cap = need + 1024;
+        LAYA_CUDA(cudaMallocHost(&c->in_host, c->in_cap * sizeof(int32_t)));
+        LAYA_CUDA(cudaMalloc(&c->in_dev, c->in_cap * sizeof(int32_t)));
+    }
+    int32_t* h = c->in_host;
+    size_t o = 0;
+    auto slot = [&](size_t n, int32_t** dev) {
+        *dev = c->in_dev + o;
+        int32_t* p = h + o;
+        o += n;
+        return p;
+    };
+    int32_t* ids_dev = nullptr;
+    if (ids_host) memcpy(slot(T, &ids_dev), ids_host, sizeof(int32_t) * T);
+    int32_t* ts = slot(T, &c->tok_seq);
+    int32_t* ss = slot(n_seq, &c->seq_start);
+    int32_t* sl = slot(n_seq, &c->seq_len);
+    int32_t* lr = slot(n_seq, &c->last_row);
+    int32_t* tsq = slot(tiles, &c->tile_seq);
+    int32_t* tp0 = slot(tiles, &c->tile_p0);
+    int32_t* lb = slot(n_labels, &c->labels);
+    int start = 0;
+    std::vector<std::pair<int, int>> tl;
+    for (int s = 0; s < n_seq; ++s) {
+        ss[s] = start; sl[s] = seq_len[s]; lr[s] = start + seq_len[s] - 1;
+        for (int t = 0; t < seq_len[s]; ++t) ts[start + t] = s;
+        for (int p0 = 0; p0 < seq_len[s]; p0 += 64) tl.push_back({p0, s});
+        start += seq_len[s];
+    }
+    // longest causal rows first
+    std::stable_sort(tl.begin(), tl.end(), [](const std::pair<int, int>& a, const std::pair<int, int>& b) { return a.first > b.first; });
+    for (int i = 0; i < tiles; ++i) { tsq[i] = tl[i].second; tp0[i] = tl[i].first; }
+    if (n_labels) memcpy(lb, labels, sizeof(int32_t) * n_labels);
+    c->n_tiles = tiles;
+    LAYA_CUDA(cudaMemcpyAsync(c->in_dev, h, o * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+    LAYA_CUDA(cudaEventRecord(c->in_done, c->stream));
+    c->in_pending = true;
+    if (ids_host) c->ids = ids_dev;
+    *T_out = static_cast<int>(T);
+    *pairs_out = pairs;
+    return OK;
+}
+
+int ready(laya_decoder* c) {
+    if (c->have.size() == c->parts.size() + c->vecs.size()) return OK;
+    for (auto& p : c->parts)
+        if (!c->have.count(p.first)) { set_error("missing tensor " + p.first); return ERR_NOT_FOUND; }
+    for (auto& v : c->vecs)
+        if (!c->have.count(v.first)) { set_error("missing tensor " + v.first); return ERR_NOT_FOUND; }
+    return OK;
+}
+
+// Embeddings → layers → final norm of every sequence's last row → label logits.
+int forward_body(laya_decoder* c, int T, int n_seq, long long pairs, int n_labels, float* hidden, float* logits) {
+    const int h = c->d.hidden;
+    RC(dec_embed(c->ids, T, h, c->d.vocab, c->table.q, c->table.d, c->table.ldw, c->x, c->err, c->stream));
+    RC(record_copy(c, "embeddings", c->x, static_cast<size_t>(T) * h));
+    for (int i = 0; i < c->d.layers; ++i) RC(run_layer(c, i, T, n_seq, pairs, false));
+    dec::RmsArgs r{};
+    r.rows = n_seq; r.n = h; r.x = c->x; r.row_map = c->last_row; r.scale = c->final_norm; r.eps = c->d.eps;
+    r.out32 = hidden ? hidden : c->hid; r.q = c->qlast; r.d = c->dlast; r.ldd = c->ldl;
+    RC(dec_rms_q8(r, c->stream));
+    if (c->record) {
+        dec::RmsArgs a = r;
+        a.rows = T; a.row_map = nullptr; a.out32 = c->mix; a.q = nullptr;
+        RC(dec_rms_q8(a, c->stream));
+        RC(record_copy(c, "norm", c->mix, static_cast<size_t>(T) * h));
+    }
+    if (n_labels > 0 && logits) {
+        dec::LogitArgs lg{};
+        lg.n_seq = n_seq; lg.n_labels = n_labels; lg.n = h; lg.vocab = c->d.vocab;
+        lg.qx = c->qlast; lg.dx = c->dlast; lg.ldx = c->ldl;
+        lg.qw = c->table.q; lg.dw = c->table.d; lg.ldw = c->table.ldw;
+        lg.labels = c->labels; lg.logits = logits; lg.err = c->err;
+        RC(dec_q8_logits(lg, c->stream));
+    }
+    return OK;
+}
+
+int ensure_logits(laya_decoder* c, size_t n) {
+    if (static_cast<size_t>(c->logit_cap) >= n) return OK;
+    if (c->logit_buf) cudaFree(c->logit_buf);
+    c->logit_buf = nullptr;
+    LAYA_CUDA(cudaMalloc(&c->logit_buf, std::max<size_t>(n, 64) * sizeof(float)));
+    c->logit_cap = static_cast<int>(std::max<size_t>(n, 64));
+    return OK;
+}
+
+std::string strip(const char* name) {
+    std::string n(name);
+    for (const char* p : {"model.language_model.", "model."})
+        if (n.rfind(p, 0) == 0) return n.substr(strlen(p));
+    return n;
+}
+
+// Register the tensors of the checkpoint: stacked projection parts and vectors.
+void register_tensors(laya_decoder* c) {
+    const laya_decoder_desc& d = c->d;
+    c->parts["embed_tokens.weight"] = {&c->table, 0, d.vocab};
+    c->vecs["norm.weight"] = {&c->final_norm, d.hidden, V_ONE_PLUS};
+    for (int i = 0; i < d.layers; ++i) {
+        Layer& L = c->layers[i];
+        const std::string p = "layers." + std::to_string(i) + ".";
+        c->vecs[p + "input_layernorm.weight"] = {&L.in_norm, d.hidden, V_ONE_PLUS};
+        c->vecs[p + "post_attention_layernorm.weight"] = {&L.post_norm, d.hidden, V_ONE_PLUS};
+        c->parts[p + "mlp.gate_proj.weight"] = {&L.gate_up, 0, d.intermediate};
+        c->parts[p + "mlp.up_proj.weight"] = {&L.gate_up, d.intermediate, d.intermediate};
+        c->parts[p + "mlp.down_proj.weight"] = {&L.down, 0, d.hidden};
+        if (L.kind == LAYA_DECODER_FULL) {
+            const std::string a = p + "self_attn.";
+            const int kvw = d.kv_heads * d.head_dim;
+            c->parts[a + "q_proj.weight"] = {&L.mix_in, 0, c->q_width};
+            c->parts[a + "k_proj.weight"] = {&L.mix_in, c->q_width, kvw};
+            c->parts[a + "v_proj.weight"] = {&L.mix_in, c->q_width + kvw, kvw};
+            c->parts[a + "o_proj.weight"] = {&L.mix_out, 0, d.hidden};
+            c->vecs[a + "q_norm.weight"] = {&L.qnorm, d.head_dim, V_ONE_PLUS};
+            c->vecs[a + "k_norm.weight"] = {&L.knorm, d.head_dim, V_ONE_PLUS};
+        } else {
+            const std::string a = p + "linear_attn.";
+            c->parts[a + "in_proj_qkv.weight"] = {&L.mix_in, 0, c->cd};
+            c->parts[a + "in_proj_z.weight"] = {&L.mix_in, c->cd, c->vd};
+            c->parts[a + "in_proj_b.weight"] = {&L.mix_in, c->cd + c->vd, d.lin_v_heads};
+            c->parts[a + "in_proj_a.weight"] = {&L.mix_in, c->cd + c->vd + d.lin_v_heads, d.lin_v_heads};
+            c->parts[a + "out_proj.weight"] = {&L.mix_out, 0, d.hidden};
+            c->vecs[a + "conv1d.weight"] = {&L.conv_w, static_cast<int64_t>(c->cd) * d.conv_kernel, V_CONV};
+            c->vecs[a + "A_log"] = {&L.neg_a, d.lin_v_heads, V_NEG_EXP};
+            c->vecs[a + "dt_bias"] = {&L.dt_bias, d.lin_v_heads, V_PLAIN};
+            c->vecs[a + "norm.weight"] = {&L.gnorm, d.lin_v_dim, V_PLAIN};
+        }
+    }
+}
+
+int check_desc(const laya_decoder_desc& d) {
+    auto bad = [](const char* m) { set_error(m); return ERR_ARGUMENT; };
+    if (d.hidden <= 0 || d.hidden % 32 || d.intermediate <= 0 || d.intermediate % 32 || d.layers < 0 || d.vocab <= 0)
+        return bad("hidden and intermediate must be positive multiples of 32");
+    if (d.layers > 0 && !d.layer_kinds) return bad("layer_kinds is required");
+    if (d.heads <= 0 || d.kv_heads <= 0 || d.heads % d.kv_heads) return bad("kv_heads must divide heads");
+    if (d.head_dim != 32 && d.head_dim != 64 && d.head_dim != 128) return bad("head_dim must be 32, 64 or 128");
+    if (d.rotary_dim < 0 || d.rotary_dim > d.head_dim || d.rotary_dim % 2) return bad("rotary_dim must be even and at most head_dim");
+    if (d.lin_k_heads <= 0 || d.lin_v_heads <= 0 || d.lin_v_heads % d.lin_k_heads) return bad("lin_v_heads must be a multiple of lin_k_heads");
+    if (d.lin_k_dim != 16 && d.lin_k_dim != 32 && d.lin_k_dim != 64 && d.lin_k_dim != 128) return bad("lin_k_dim must be 16, 32, 64 or 128");
+    if (d.lin_v_dim <= 0 || d.lin_v_dim > 128) return bad("lin_v_dim must be 1..128");
+    if ((d.lin_v_heads * d.lin_v_dim) % 32 || (d.heads * d.head_dim) % 32) return bad("value and attention widths must be multiples of 32");
+    if (d.conv_kernel <= 0 || d.conv_kernel > 16) return bad("conv_kernel must be 1..16");
+    if (d.max_tokens <= 0 || d.max_seqs <= 0) return bad("max_tokens and max_seqs must be positive");
+    if (!(d.eps > 0.0f)) return bad("eps must be positive");
+    for (int i = 0; i < d.layers; ++i)
+        if (d.layer_kinds[i] != LAYA_DECODER_LINEAR && d.layer_kinds[i] != LAYA_DECODER_FULL) return bad("unknown layer kind");
+    return OK;
+}
+
+int create(laya_decoder* c) {
+    const laya_decoder_desc& d = c->d;
+    c->key_dim = d.lin_k_heads * d.lin_k_dim;
+    c->vd = d.lin_v_heads * d.lin_v_dim;
+    c->cd = 2 * c->key_dim + c->vd;
+    c->nin = c->cd + c->vd + 2 * d.lin_v_heads;
+    c->ld_in = rup(c->nin, 4);
+    c->q_width = 2 * d.heads * d.head_dim;
+    c->nqkv = c->q_width + 2 * d.kv_heads * d.head_dim;
+    c->half = d.rotary_dim / 2;
+    c->maxK = std::max({d.hidden, d.intermediate, c->vd, d.heads * d.head_dim});
+    c->ldx = rup(d.max_tokens, 128);
+    c->widest = std::max({c->ld_in, c->nqkv, 2 * d.intermediate});
+    c->core_w = std::max(c->vd, d.heads * d.head_dim);
+    c->ldl = rup(d.max_seqs, 4);
+    const size_t T = d.max_tokens;
+    LAYA_CUDA(cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking));
+    c->stream = c->own;
+    LAYA_CUDA(cudaEventCreateWithFlags(&c->in_done, cudaEventDisableTiming));
+    RC(dalloc_t(c, &c->err, 1));
+    LAYA_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+
+    c->layers.resize(d.layers);
+    RC(alloc_qmat(c, c->table, d.vocab, d.hidden));
+    bool any_full = false, any_linear = false;
+    for (int i = 0; i < d.layers; ++i) {
+        Layer& L = c->layers[i];
+        L.kind = c->kinds[i];
+        if (L.kind == LAYA_DECODER_FULL) {
+            any_full = true;
+            RC(alloc_qmat(c, L.mix_in, c->nqkv, d.hidden));
+            RC(alloc_qmat(c, L.mix_out, d.hidden, d.heads * d.head_dim));
+        } else {
+            any_linear = true;
+            RC(alloc_qmat(c, L.mix_in, c->nin, d.hidden));
+            RC(alloc_qmat(c, L.mix_out, d.hidden, c->vd));
+        }
+        RC(alloc_qmat(c, L.gate_up, 2 * d.intermediate, d.hidden));
+        RC(alloc_qmat(c, L.down, d.hidden, d.intermediate));
+    }
+    register_tensors(c);
+    for (auto& v : c->vecs) RC(dalloc_t(c, v.second.dst, static_cast<size_t>(v.second.count)));
+
+    RC(dalloc_t(c, &c->x, T * d.hidden));
+    RC(dalloc_t(c, &c->mix, T * d.hidden));
+    RC(dalloc_t(c, &c->big, T * c->widest));
+    RC(dalloc_t(c, &c->core, T * c->core_w));
+    RC(dalloc_t(c, &c->qa, T * c->maxK));
+    RC(dalloc_t(c, &c->da, static_cast<size_t>(c->maxK / 32) * c->ldx));
+    if (any_linear) {
+        RC(dalloc_t(c, &c->conv, T * c->cd));
+        RC(dalloc_t(c, &c->beta, T * d.lin_v_heads));
+        RC(dalloc_t(c, &c->decay, T * d.lin_v_heads));
+    }
+    if (any_full) {
+        RC(dalloc_t(c, &c->q16, T * d.heads * d.head_dim));
+        RC(dalloc_t(c, &c->k16, T * d.kv_heads * d.head_dim));
+        RC(dalloc_t(c, &c->v16, T * d.kv_heads * d.head_dim));
+        // RoPE tables (Qwen35Model.cs:247-253): inv_freq = 1/θ^(2i/rotary_dim) and angle = pos·inv_freq in fp32
+        const int hf = std::max(c->half, 1);
+        std::vector<float> cs(T * hf), sn(T * hf);
+        std::vector<float> inv(hf);
+        for (int i = 0; i < c->half; ++i)
+            inv[i] = 1.0f / std::pow(static_cast<float>(d.rope_theta), static_cast<float>(2 * i) / static_cast<float>(d.rotary_dim));
+        for (size_t p = 0; p < T; ++p)
+            for (int i = 0; i < c->half; ++i) {
+                const float ang = static_cast<float>(p) * inv[i];
+                cs[p * hf + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
+                sn[p * hf + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+            }
+        RC(dalloc_t(c, &c->cosv, cs.size()));
+        RC(dalloc_t(c, &c->sinv, sn.size()));
+        LAYA_CUDA(cudaMemcpy(c->cosv, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+        LAYA_CUDA(cudaMemcpy(c->sinv, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    RC(dalloc_t(c, &c->hid, static_cast<size_t>(d.max_seqs) * d.hidden));
+    RC(dalloc_t(c, &c->qlast, static_cast<size_t>(d.max_seqs) * d.hidden));
+    RC(dalloc_t(c, &c->dlast, static_cast<size_t>(d.hidden / 32) * c->ldl));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    return OK;
+}
+
+// Quantize rows [row0, row0 + rows) of a stacked matrix from fp32 host rows.
+int fill_rows(laya_decoder* c, const Part& p, const float* host) {
+    QMat& m = *p.m;
+    float* tmp = nullptr;
+    const size_t n = static_cast<size_t>(p.rows) * m.K;
+    LAYA_CUDA(cudaMalloc(&tmp, n * sizeof(float)));
+    cudaError_t e = cudaMemcpyAsync(tmp, host, n * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+    int rc = e == cudaSuccess ? q8::quantize_weights(tmp, p.rows, m.K, m.q + static_cast<size_t>(p.row0) * m.K,
+                                                     m.d + p.row0, m.ldw, c->stream)
+                              : cuda_fail(e, "cudaMemcpyAsync");
+    cudaError_t s = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (rc != OK) return rc;
+    if (s != cudaSuccess) return cuda_fail(s, "cudaStreamSynchronize");
+    return OK;
+}
+
+int fill_rows_q8(laya_decoder* c, const Part& p, const int8_t* q, const uint16_t* d_fp16) {
+    QMat& m = *p.m;
+    const int nb = m.K / 32;
+    const size_t n = static_cast<size_t>(p.rows) * m.K;
+    std::vector<float> dt(static_cast<size_t>(nb) * p.rows);
+    for (int r = 0; r < p.rows; ++r)
+        for (int b = 0; b < nb; ++b) dt[static_cast<size_t>(b) * p.rows + r] = half_bits(d_fp16[static_cast<size_t>(r) * nb + b]);
+    int8_t* tmp = nullptr;
+    LAYA_CUDA(cudaMalloc(&tmp, n));
+    cudaError_t e = cudaMemcpyAsync(tmp, q, n, cudaMemcpyHostToDevice, c->stream);
+    int rc = e == cudaSuccess ? q8::widen_codes(tmp, m.q + static_cast<size_t>(p.row0) * m.K, n, c->stream)
+                              : cuda_fail(e, "cudaMemcpyAsync");
+    if (rc == OK) {
+        e = cudaMemcpy2DAsync(m.d + p.row0, static_cast<size_t>(m.ldw) * sizeof(float), dt.data(), static_cast<size_t>(p.rows) * sizeof(float),
+                              static_cast<size_t>(p.rows) * sizeof(float), nb, cudaMemcpyHostToDevice, c->stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy2DAsync");
+    }
+    cudaError_t s = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (rc != OK) return rc;
+    if (s != cudaSuccess) return cuda_fail(s, "cudaStreamSynchronize");
+    return OK;
+}
+
+int stage_input_rows(laya_decoder* c, const int32_t* seq_len, int n_seq, int* T_out, long long* pairs) {
+    return stage(c, nullptr, seq_len, n_seq, nullptr, 0, T_out, pairs);
+}
+
+}  // namespace
+
+// ================================================================================================ C ABI
+extern "C" {
+
+int laya_decoder_create(const laya_decoder_desc* desc, int device, laya_decoder** out) {
+    if (!desc || !out) { set_error("null argument"); return ERR_ARGUMENT; }
+    *out = nullptr;
+    RC(check_desc(*desc));
+    int n = 0;
+    LAYA_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) { set_error("invalid device ordinal"); return ERR_ARGUMENT; }
+    DeviceGuard g(device);
+    laya_decoder* c = new laya_decoder();
+    c->device = device;
+    c->d = *desc;
+    c->kinds.assign(desc->layer_kinds, desc->layer_kinds + desc->layers);
+    c->d.layer_kinds = nullptr;
+    const int rc = create(c);
+    if (rc != OK) {
+        laya_decoder_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return OK;
+}
+
+int laya_decoder_destroy(laya_decoder* c) {
+    if (!c) return OK;
+    DeviceGuard g(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (void* p : c->allocs) cudaFree(p);
+    for (auto& r : c->rec) cudaFree(r.second.first);
+    for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
+    if (c->logit_buf) cudaFree(c->logit_buf);
+    if (c->in_dev) cudaFree(c->in_dev);
+    if (c->in_host) cudaFreeHost(c->in_host);
+    if (c->in_done) cudaEventDestroy(c->in_done);
+    if (c->own) cudaStreamDestroy(c->own);
+    delete c;
+    return OK;
+}
+
+int laya_decoder_set_stream(laya_decoder* c, void* stream) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own;
+    return OK;
+}
+
+int laya_decoder_get_stream(laya_decoder* c, void** stream) {
+    if (!c || !stream) { set_error("null argument"); return ERR_ARGUMENT; }
+    *stream = c->stream;
+    return OK;
+}
+
+int laya_decoder_synchronize(laya_decoder* c) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
+}
+
+int laya_decoder_upload(laya_decoder* c, const char* name, int dtype, const int64_t* shape, int rank, const void* host) {
+    if (!c || !name || !host || rank < 0 || rank > 8 || (rank > 0 && !shape)) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    const std::string n = strip(name);
+    int64_t count = 1;
+    for (int i = 0; i < rank; ++i) {
+        if (shape[i] < 0) { set_error("negative dimension"); return ERR_ARGUMENT; }
+        count *= shape[i];
+    }
+    std::vector<float> tmp;
+    const float* src = nullptr;
+    switch (dtype) {
+        case LAYA_F32: src = static_cast<const float*>(host); break;
+        case LAYA_BF16:
+        case LAYA_F16: {
+            tmp.resize(count);
+            const uint16_t* b = static_cast<const uint16_t*>(host);
+            for (int64_t i = 0; i < count; ++i) tmp[i] = dtype == LAYA_BF16 ? bf16_bits(b[i]) : half_bits(b[i]);
+            src = tmp.data();
+            break;
+        }
+        default: set_error("unsupported dtype for a float tensor"); return ERR_ARGUMENT;
+    }
+    auto pt = c->parts.find(n);
+    if (pt != c->parts.end()) {
+        const Part& p = pt->second;
+        if (rank != 2 || shape[0] != p.rows || shape[1] != p.m->K) {
+            set_error(n + ": expected [" + std::to_string(p.rows) + ", " + std::to_string(p.m->K) + "]");
+            return ERR_ARGUMENT;
+        }
+        RC(fill_rows(c, p, src));
+        c->have.insert(n);
+        return OK;
+    }
+    auto vt = c->vecs.find(n);
+    if (vt == c->vecs.end()) { set_error("no decoder tensor named " + n); return ERR_NOT_FOUND; }
+    const Vec& v = vt->second;
+    if (count != v.count) { set_error(n + ": expected " + std::to_string(v.count) + " values"); return ERR_ARGUMENT; }
+    std::vector<float> val(count);
+    switch (v.kind) {
+        case V_PLAIN: memcpy(val.data(), src, count * sizeof(float)); break;
+        case V_ONE_PLUS: for (int64_t i = 0; i < count; ++i) val[i] = 1.0f + src[i]; break;
+        case V_NEG_EXP: for (int64_t i = 0; i < count; ++i) val[i] = -std::exp(src[i]); break;
+        case V_CONV: {   // [channels, 1, taps] → [taps, channels]
+            const int K = c->d.conv_kernel, cd = c->cd;
+            for (int ch = 0; ch < cd; ++ch)
+                for (int j = 0; j < K; ++j) val[static_cast<size_t>(j) * cd + ch] = src[static_cast<size_t>(ch) * K + j];
+            break;
+        }
+    }
+    LAYA_CUDA(cudaMemcpyAsync(*v.dst, val.data(), count * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    c->have.insert(n);
+    return OK;
+}
+
+int laya_decoder_upload_q8_0(laya_decoder* c, const char* name, const int8_t* q, const uint16_t* d_fp16, int N, int K) {
+    if (!c || !name || !q || !d_fp16) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    const std::string n = strip(name);
+    auto pt = c->parts.find(n);
+    if (pt == c->parts.end()) { set_error("no Q8_0 decoder tensor named " + n); return ERR_NOT_FOUND; }
+    const Part& p = pt->second;
+    if (N != p.rows || K != p.m->K) {
+        set_error(n + ": expected [" + std::to_string(p.rows) + ", " + std::to_string(p.m->K) + "]");
+        return ERR_ARGUMENT;
+    }
+    RC(fill_rows_q8(c, p, q, d_fp16));
+    c->have.insert(n);
+    return OK;
+}
+
+int laya_decoder_missing(laya_decoder* c, char* names, int cap, int* missing) {
+    if (!c || !missing) { set_error("null argument"); return ERR_ARGUMENT; }
+    std::string out;
+    int m = 0;
+    for (auto& p : c->parts)
+        if (!c->have.count(p.first)) { ++m; out += p.first + "\n"; }
+    for (auto& v : c->vecs)
+        if (!c->have.count(v.first)) { ++m; out += v.first + "\n"; }
+    *missing = m;
+    if (names && cap > 0) {
+        const size_t k = std::min(out.size(), static_cast<size_t>(cap - 1));
+        memcpy(names, out.data(), k);
+        names[k] = 0;
+    }
+    return OK;
+}
+
+int laya_decoder_forward_device(laya_decoder* c, const int32_t* ids, const int32_t* seq_len, int n_seq,
+                                const int32_t* label_ids, int n_labels, float* hidden, float* logits) {
+    if (!c || !ids || !seq_len) { set_error("null argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    RC(ready(c));
+    int T = 0;
+    long long pairs = 0;
+    RC(stage(c, nullptr, seq_len, n_seq, label_ids, n_labels, &T, &pairs));
+    c->ids = const_cast<int32_t*>(ids);
+    RC(forward_body(c, T, n_seq, pairs, n_labels, hidden, logits));
+    if (c->profiling) RC(collect_profile(c));
+    return OK;
+}
+
+int laya_decoder_forward(laya_decoder* c, const int32_t* ids, const int32_t* seq_len, int n_seq,
+                         const int32_t* label_ids, int n_labels, float* hidden, float* logits) {
+    if (!c || !ids || !seq_len) { set_error("null argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    RC(ready(c));
+    int T = 0;
+    long long pairs = 0;
+    RC(stage(c, ids, seq_len, n_seq, label_ids, n_labels, &T, &pairs));
+    const size_t nl = static_cast<size_t>(n_seq) * n_labels;
+    RC(ensure_logits(c, nl));
+    RC(forward_body(c, T, n_seq, pairs, n_labels, nullptr, logits && n_labels ? c->logit_buf : nullptr));
+    if (hidden)
+        LAYA_CUDA(cudaMemcpyAsync(hidden, c->hid, static_cast<size_t>(n_seq) * c->d.hidden * sizeof(float),
+                                  cudaMemcpyDeviceToHost, c->stream));
+    if (logits && n_labels)
+        LAYA_CUDA(cudaMemcpyAsync(logits, c->logit_buf, nl * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    RC(check_device_error(c));
+    if (c->profiling) RC(collect_profile(c));
+    return OK;
+}
+
+int laya_decoder_logits(laya_decoder* c, const float* hidden, int rows, const int32_t* ids, int n_ids, float* logits) {
+    if (!c || !hidden || !ids || !logits || rows <= 0 || n_ids <= 0) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    if (rows > c->d.max_seqs) { set_error("more rows than max_seqs"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    if (!c->have.count("embed_tokens.weight")) { set_error("missing tensor embed_tokens.weight"); return ERR_NOT_FOUND; }
+    for (int i = 0; i < n_ids; ++i)
+        if (ids[i] < 0 || ids[i] >= c->d.vocab) { set_error("label id outside the vocabulary"); return ERR_OUT_OF_RANGE; }
+    const int h = c->d.hidden;
+    const size_t nl = static_cast<size_t>(rows) * n_ids;
+    RC(ensure_logits(c, nl));
+    int32_t* lab = nullptr;
+    LAYA_CUDA(cudaMalloc(&lab, sizeof(int32_t) * n_ids));
+    cudaError_t e = cudaMemcpyAsync(lab, ids, sizeof(int32_t) * n_ids, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->hid, hidden, sizeof(float) * rows * h, cudaMemcpyHostToDevice, c->stream);
+    int rc = e == cudaSuccess ? q8::quantize_activations(c->hid, rows, h, h, c->qlast, c->dlast, c->ldl, c->stream)
+                              : cuda_fail(e, "cudaMemcpyAsync");
+    if (rc == OK) {
+        dec::LogitArgs lg{};
+        lg.n_seq = rows; lg.n_labels = n_ids; lg.n = h; lg.vocab = c->d.vocab;
+        lg.qx = c->qlast; lg.dx = c->dlast; lg.ldx = c->ldl;
+        lg.qw = c->table.q; lg.dw = c->table.d; lg.ldw = c->table.ldw;
+        lg.labels = lab; lg.logits = c->logit_buf; lg.err = c->err;
+        rc = dec_q8_logits(lg, c->stream);
+    }
+    if (rc == OK) {
+        e = cudaMemcpyAsync(logits, c->logit_buf, nl * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync");
+    }
+    cudaStreamSynchronize(c->stream);
+    cudaFree(lab);
+    if (rc != OK) return rc;
+    return check_device_error(c);
+}
+
+int laya_decoder_layer(laya_decoder* c, int layer, float* hidden, const int32_t* seq_len, int n_seq, float* mixer) {
+    if (!c || !hidden || !seq_len) { set_error("null argument"); return ERR_ARGUMENT; }
+    if (layer < 0 || layer >= c->d.layers) { set_error("layer index out of range"); return ERR_OUT_OF_RANGE; }
+    DeviceGuard g(c->device);
+    RC(ready(c));
+    int T = 0;
+    long long pairs = 0;
+    RC(stage_input_rows(c, seq_len, n_seq, &T, &pairs));
+    const size_t n = static_cast<size_t>(T) * c->d.hidden;
+    LAYA_CUDA(cudaMemcpyAsync(c->x, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    RC(run_layer(c, layer, T, n_seq, pairs, mixer != nullptr));
+    LAYA_CUDA(cudaMemcpyAsync(hidden, c->x, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (mixer) LAYA_CUDA(cudaMemcpyAsync(mixer, c->mix, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
+}
+
+int laya_decoder_record_enable(laya_decoder* c, int enabled) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    c->record = enabled != 0;
+    return OK;
+}
+
+int laya_decoder_record_get(laya_decoder* c, const char* name, float* host, int64_t count) {
+    if (!c || !name || !host) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    auto it = c->rec.find(name);
+    if (it == c->rec.end()) { set_error(std::string("nothing recorded as ") + name); return ERR_NOT_FOUND; }
+    if (count < static_cast<int64_t>(it->second.second)) { set_error("host buffer too small"); return ERR_ARGUMENT; }
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    LAYA_CUDA(cudaMemcpy(host, it->second.first, it->second.second * sizeof(float), cudaMemcpyDeviceToHost));
+    return OK;
+}
+
+int laya_decoder_launches(laya_decoder* c, long long* count) {
+    if (!c || !count) { set_error("null argument"); return ERR_ARGUMENT; }
+    *count = launches();
+    return OK;
+}
+
+int laya_decoder_set_profiling(laya_decoder* c, int enabled) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    RC(collect_profile(c));
+    c->profiling = enabled != 0;
+    for (int k = 0; k < 3; ++k) { c->prof_ms[k] = c->prof_ops[k] = 0; c->prof_n[k] = 0; }
+    return OK;
+}
+
+int laya_decoder_profile(laya_decoder* c, int kind, double* ms, double* ops, long long* n) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    if (kind < 0 || kind > 2) { set_error("profile kind is 0 (products), 1 (delta rule) or 2 (attention)"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    RC(collect_profile(c));
+    if (ms) *ms = c->prof_ms[kind];
+    if (ops) *ops = c->prof_ops[kind];
+    if (n) *n = c->prof_n[kind];
+    c->prof_ms[kind] = c->prof_ops[kind] = 0;
+    c->prof_n[kind] = 0;
+    return OK;
+}
+
+}  // extern "C"

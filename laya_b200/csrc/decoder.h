@@ -1,0 +1,114 @@
+// decoder.h — argument blocks and launchers of the Mica decoder kernels (decoder_kernels.cu); internal to the library.
+//
+// Token layout: the rows of all sequences of one forward packed back to back (T rows); seq_start / seq_len give each
+// sequence's rows and tok_seq the sequence of every row.  Every activation is row-major [T, width] fp32 unless noted.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace laya {
+namespace dec {
+
+// RMSNorm of rows (row r reads x[row_map ? row_map[r] : r]) · scale (= 1 + weight), optionally kept in fp32 (out32
+// [rows, n]) and/or quantized to Q8_0 (q [rows, n], d [n/32, ldd]).
+struct RmsArgs {
+    int rows, n;
+    const float* x;
+    const int32_t* row_map;
+    const float* scale;
+    float eps;
+    float* out32;
+    q8::code_t* q; float* d; int ldd;
+};
+
+// Causal depthwise conv over the first cd columns of in (row stride ld_in), taps w [K, cd] (tap-major), then SiLU.
+struct ConvArgs {
+    int T, cd, K;
+    const float* in; int ld_in;
+    const float* w;
+    const int32_t* tok_seq; const int32_t* seq_start;
+    float* out;   // [T, cd]
+};
+
+// In place on conv [T, cd] = [q (kh·dk) | k (kh·dk) | v]: L2 norm of every q head (· qscale) and k head; β and the
+// decay per (row, value head) from the b and a columns of the input projection.
+struct HeadsArgs {
+    int T, kh, vh, dk, key_dim, cd;
+    float* conv;
+    float qscale;
+    const float* proj; int ld_proj, b_col, a_col;
+    const float* dt_bias; const float* neg_a;   // [vh]; neg_a = −exp(A_log)
+    float* beta; float* decay;                  // [T, vh]
+};
+
+// The gated delta rule, one CTA per (sequence, value head): q, k, v from conv, output [T, ld_out] at h·dv.
+struct DeltaArgs {
+    int dk, dv, vh, ratio, key_dim, cd;
+    const float* conv;
+    const float* beta; const float* decay;
+    const int32_t* seq_start; const int32_t* seq_len;
+    float* out; int ld_out;
+};
+
+// RmsNormGated per (row, value head): weight · rmsnorm(core) · silu(z).
+struct GatedArgs {
+    int T, vh, dv;
+    const float* core; int ld_core;
+    const float* z; int ld_z;
+    const float* weight;
+    float eps;
+    float* out; int ld_out;
+};
+
+// Full attention input: qkv [T, ld_qkv] = [q_h | gate_h for each head h (2·hd each) | k (kv·hd) | v (kv·hd)].
+struct PrepArgs {
+    int T, heads, kv_heads, hd, half, q_width;
+    const float* qkv; int ld_qkv;
+    const float* qnorm; const float* knorm;   // 1 + weight
+    float eps;
+    const float* cosv; const float* sinv;     // [positions, half]
+    const int32_t* tok_seq; const int32_t* seq_start;
+    __half* q16; __half* k16; __half* v16;    // [T, heads·hd], [T, kv·hd], [T, kv·hd]
+};
+
+// Causal GQA attention over 64-query tiles (tile_seq, tile_p0), output · sigmoid(gate) into out [T, ld_out].
+struct AttnArgs {
+    int heads, kv_heads;
+    const __half* q16; const __half* k16; const __half* v16;
+    const int32_t* tile_seq; const int32_t* tile_p0;
+    const int32_t* seq_start; const int32_t* seq_len;
+    float scale;
+    const float* qkv; int ld_qkv;   // the gates
+    float* out; int ld_out;
+};
+
+// Label logits: per (sequence, label) the Q8_0 product of the sequence's final hidden codes with the label's row
+// of the Q8_0 token table.
+struct LogitArgs {
+    int n_seq, n_labels, n, vocab;
+    const q8::code_t* qx; const float* dx; int ldx;
+    const q8::code_t* qw; const float* dw; int ldw;
+    const int32_t* labels;
+    float* logits;
+    int* err;
+};
+
+}  // namespace dec
+
+int dec_rms_q8(const dec::RmsArgs& a, cudaStream_t s);
+int dec_embed(const int32_t* ids, int T, int n, int vocab, const q8::code_t* q, const float* d, int ldd, float* x,
+              int* err, cudaStream_t s);
+int dec_conv_silu(const dec::ConvArgs& a, cudaStream_t s);
+int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s);
+int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
+int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);
+int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s);
+int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);
+int dec_swiglu_q8(const float* gu, int rows, int I, q8::code_t* q, float* d, int ldd, cudaStream_t s);
+int dec_add(float* x, const float* y, size_t n, cudaStream_t s);
+int dec_q8_logits(const dec::LogitArgs& a, cudaStream_t s);
+
+}  // namespace laya

@@ -9,6 +9,11 @@ option markers at j·⌊L/(k+1)⌋, j = 1..k.
 Configs 1/3/4 (fine-tuning): every tensor N(0, 0.02) except LayerNorm γ = 1 and biases 0; rows of uniform token ids
 in [5, vocab) with a per-row valid length (config 3: U{256..1024}), the same five question kinds, soft targets U(0, 1)
 normalised per row, and the objective's standard-normal draws [groups, options].
+
+Config 5 (Mica hybrid decoder prefill): Qwen3.5 geometry (32 layers of [DeltaNet ×3, full ×1], h 2560, I 9216,
+vocab 151936); projections and the tied token table in Q8_0 (codes uniform in [-127, 127], block scales
+fp16(|N(0, scale)|)), norms, conv taps N(0, 0.02), A_log ~ U(0, 2), dt_bias 0; 8 rows × 2048 token ids uniform in
+[0, vocab), 26 label ids.  `decoder_weights` gives the same tensors in fp32 (N(0, std) projections) for parity cases.
 """
 from typing import Dict, List, Tuple
 
@@ -150,3 +155,93 @@ def mix(seed: int, salt: int) -> int:
     z = (seed ^ ((salt * 0xD1B54A32D192ED03 + 0x8CB92BA72F3D8DD7) & m)) & m
     z = ((z ^ (z >> 33)) * 0xFF51AFD7ED558CCD) & m
     return z ^ (z >> 33)
+
+
+# ----------------------------------------------------------------------------------------------- Mica decoder
+MICA_KINDS = (["linear"] * 3 + ["full"]) * 8
+MICA = dict(hidden=2560, intermediate=9216, vocab=151936, heads=16, kv_heads=4, head_dim=128, lin_k_heads=16,
+            lin_v_heads=16, lin_k_dim=128, lin_v_dim=128, conv_kernel=4)
+
+
+def decoder_shapes(kinds, hidden, intermediate, vocab, heads, kv_heads, head_dim, lin_k_heads, lin_v_heads,
+                   lin_k_dim, lin_v_dim, conv_kernel):
+    """(name, shape, kind) of every checkpoint tensor of a Qwen3.5 text decoder; kind is "proj" (a Q8_0 projection
+    or the token table), "norm", "conv", "A_log", "dt_bias"."""
+    kd, vd = lin_k_heads * lin_k_dim, lin_v_heads * lin_v_dim
+    cd = 2 * kd + vd
+    out = [("model.embed_tokens.weight", (vocab, hidden), "proj"), ("model.norm.weight", (hidden,), "norm")]
+    for i, k in enumerate(kinds):
+        p = f"model.layers.{i}."
+        out += [(p + "input_layernorm.weight", (hidden,), "norm"),
+                (p + "post_attention_layernorm.weight", (hidden,), "norm"),
+                (p + "mlp.gate_proj.weight", (intermediate, hidden), "proj"),
+                (p + "mlp.up_proj.weight", (intermediate, hidden), "proj"),
+                (p + "mlp.down_proj.weight", (hidden, intermediate), "proj")]
+        if k == "full":
+            a = p + "self_attn."
+            out += [(a + "q_proj.weight", (2 * heads * head_dim, hidden), "proj"),
+                    (a + "k_proj.weight", (kv_heads * head_dim, hidden), "proj"),
+                    (a + "v_proj.weight", (kv_heads * head_dim, hidden), "proj"),
+                    (a + "o_proj.weight", (hidden, heads * head_dim), "proj"),
+                    (a + "q_norm.weight", (head_dim,), "norm"), (a + "k_norm.weight", (head_dim,), "norm")]
+        else:
+            a = p + "linear_attn."
+            out += [(a + "in_proj_qkv.weight", (cd, hidden), "proj"), (a + "in_proj_z.weight", (vd, hidden), "proj"),
+                    (a + "in_proj_b.weight", (lin_v_heads, hidden), "proj"),
+                    (a + "in_proj_a.weight", (lin_v_heads, hidden), "proj"),
+                    (a + "out_proj.weight", (hidden, vd), "proj"), (a + "conv1d.weight", (cd, 1, conv_kernel), "conv"),
+                    (a + "A_log", (lin_v_heads,), "A_log"), (a + "dt_bias", (lin_v_heads,), "dt_bias"),
+                    (a + "norm.weight", (lin_v_dim,), "gnorm")]
+    return out
+
+
+def _vector(rng, shape, kind):
+    if kind == "A_log":
+        return rng.uniform(0.0, 2.0, shape).astype(np.float32)
+    if kind == "dt_bias":
+        return np.zeros(shape, np.float32)
+    if kind == "gnorm":
+        return (1.0 + rng.normal(0.0, 0.02, shape)).astype(np.float32)
+    return rng.normal(0.0, 0.02, shape).astype(np.float32)
+
+
+def decoder_weights(kinds, seed=0, std=0.02, **geometry) -> Dict[str, np.ndarray]:
+    """Every tensor in fp32 (projections N(0, std)), for parity cases small enough for the CPU oracle."""
+    g = dict(MICA)
+    g.update(geometry)
+    rng = np.random.default_rng(seed)
+    w = {}
+    for name, shape, kind in decoder_shapes(kinds, **g):
+        w[name] = rng.normal(0.0, std, shape).astype(np.float32) if kind == "proj" else _vector(rng, shape, kind)
+    return w
+
+
+def decoder_q8_weights(kinds, seed=0, q8_scale=0.0004, **geometry):
+    """(Q8_0 projections {name: (int8 codes [N, K], fp16 scales [N, K/32])}, fp32 vectors {name: array}).  The codes
+    of every projection are windows of one seeded pool of random bytes, so a 4-billion-parameter model is made in
+    seconds."""
+    g = dict(MICA)
+    g.update(geometry)
+    rng = np.random.default_rng(seed)
+    shapes = decoder_shapes(kinds, **g)
+    largest = max(int(np.prod(s)) for _, s, k in shapes if k == "proj")
+    pool = rng.integers(-127, 128, size=largest + 65537, dtype=np.int8)
+    scales = np.abs(rng.normal(0.0, q8_scale, size=largest // 32 + 4097)).astype(np.float16)
+    q8, vec = {}, {}
+    for name, shape, kind in shapes:
+        if kind == "proj":
+            n, k = shape
+            o = int(rng.integers(0, 65536))
+            so = int(rng.integers(0, 4096))
+            q8[name] = (pool[o:o + n * k].reshape(n, k), scales[so:so + n * k // 32].reshape(n, k // 32))
+        else:
+            vec[name] = _vector(rng, shape, kind)
+    return q8, vec
+
+
+def decoder_batch(rows=8, length=2048, vocab=151936, n_labels=26, seed=5):
+    """rows × length token ids uniform in [0, vocab) and n_labels distinct label ids."""
+    rng = np.random.default_rng(seed)
+    seqs = [rng.integers(0, vocab, size=length).astype(np.int32) for _ in range(rows)]
+    labels = rng.choice(vocab, size=n_labels, replace=False).astype(np.int32)
+    return seqs, labels

@@ -20,7 +20,8 @@ def test_header_declares_the_boundary():
     names = declared()
     for n in ["laya_ctx_create", "laya_upload_tensor", "laya_upload_q8_0", "laya_q8_0_linear", "laya_decision_forward",
               "laya_last_error", "laya_trainer_create", "laya_train_forward", "laya_train_backward",
-              "laya_train_objective", "laya_train_clip_and_step", "laya_train_comm_init"]:
+              "laya_train_objective", "laya_train_clip_and_step", "laya_train_comm_init", "laya_decoder_create",
+              "laya_decoder_upload", "laya_decoder_upload_q8_0", "laya_decoder_forward", "laya_decoder_logits"]:
         assert n in names
 
 
@@ -43,7 +44,8 @@ def test_no_cpu_fallback_without_a_gpu():
 
 @pytest.mark.parametrize("header,struct,cls", [("laya_b200.h", "laya_model_desc", "ModelDesc"),
                                                 ("laya_train.h", "laya_train_desc", "TrainDesc"),
-                                                ("laya_train.h", "laya_rlcd_desc", "RlcdDesc")])
+                                                ("laya_train.h", "laya_rlcd_desc", "RlcdDesc"),
+                                                ("laya_decoder.h", "laya_decoder_desc", "DecoderDesc")])
 def test_struct_layouts_match_the_headers(tmp_path, header, struct, cls):
     """The ctypes mirrors of the C ABI structs have the C compiler's size and field offsets."""
     import subprocess
@@ -73,3 +75,20 @@ def test_invalid_geometry_is_an_argument_error():
     import laya_b200
     with pytest.raises(laya_b200.LayaArgumentError):
         laya_b200.Context(laya_b200.base_desc(heads=7))
+
+
+def test_decoder_fails_loudly_without_a_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("this machine has a GPU")
+    import laya_b200
+    with pytest.raises(laya_b200.LayaError):
+        laya_b200.Qwen35Model(laya_b200.decoder_desc(["linear", "full"], max_tokens=64, max_seqs=2))
+
+
+def test_decoder_invalid_geometry_is_an_argument_error():
+    import laya_b200
+    with pytest.raises(laya_b200.LayaArgumentError):
+        laya_b200.Qwen35Model(laya_b200.decoder_desc(["linear"], lin_v_heads=3, lin_k_heads=2))
+    with pytest.raises(laya_b200.LayaArgumentError):
+        laya_b200.Qwen35Model(laya_b200.decoder_desc(["full"], head_dim=96))
