@@ -1,6 +1,6 @@
 """Throughput of the hot path on B200s — one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|train|q8]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|train|q8|decoder]
 
 Headline workload (config 3, the data-parallel fine-tune): per GPU 32 ModernBERT-base rows with valid lengths
 U{256..1024} (padding is not work: rows are concatenated), the Laya decision head, the RLCD objective with 4 noise
@@ -13,6 +13,10 @@ per-rank times.
 
 Nested `q8_0_encode` (config 2): the batched decision forward with every projection in Q8_0, 64 rows × 512 tokens per
 GPU, sharded by request with no collective.
+
+Nested `mica_prefill` (config 5): the Mica hybrid decoder (32 Qwen3.5 layers, [DeltaNet ×3, full] ×8, h 2560) with
+every projection and the tied token table in Q8_0, a prefill of 8 rows × 2048 token ids per GPU and the logits of 26
+label ids at each row's last position; replicas sharded by request with no collective.
 
 `value` is device-resident throughput (inputs staged in HBM before the timed region); `e2e` is the same step through
 the host-pointer C ABI with the step's inputs copied from pinned host memory and its result (the loss; the logits)
@@ -39,6 +43,10 @@ TR_WORKLOAD = "config3_dp_finetune_step"
 ROWS, SEQ = 64, 512
 TOKENS = ROWS * SEQ
 Q8_WORKLOAD = "config2_q8_0_decision_forward"
+# config 5 (Mica decoder prefill)
+DEC_ROWS, DEC_LEN, DEC_LABELS = 8, 2048, 26
+DEC_TOKENS = DEC_ROWS * DEC_LEN
+DEC_WORKLOAD = "config5_mica_hybrid_decoder_prefill"
 
 
 def parse():
@@ -47,7 +55,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "train", "q8"])
+    ap.add_argument("--workload", default="all", choices=["all", "train", "q8", "decoder"])
+    ap.add_argument("--dec-tokens", type=int, default=128, help="tokens of the decoder's CPU sample")
+    ap.add_argument("--dec-layers", type=int, default=32, help="decoder layers (fewer only for small captures)")
     ap.add_argument("--forward", default="accurate", choices=["accurate", "bf16"],
                     help="forward mode of the headline training step")
     ap.add_argument("--no-bf16-forward", action="store_true", help="skip the extra BF16-forward measurement")
@@ -99,6 +109,15 @@ def q8_config(world):
     return {"workload": Q8_WORKLOAD, "rows_per_gpu": ROWS, "seq_len": SEQ, "tokens_per_gpu_step": TOKENS,
             "geometry": "ModernBERT-base 22x768 (12x64, GeGLU 1152) + 2 head layers", "weights": "Q8_0 (config 2)",
             "l2": "inputs larger than L2 (Q8_0 weights ~150 MB + 0.5 GB activations per step)",
+            "parallelism": f"request-sharded x{world}, no collective"}
+
+
+def dec_config(world, layers=32):
+    return {"workload": DEC_WORKLOAD, "rows_per_gpu": DEC_ROWS, "seq_len": DEC_LEN, "tokens_per_gpu_step": DEC_TOKENS,
+            "geometry": f"Qwen3.5 hybrid {layers} layers ([DeltaNet x3, full] blocks), h 2560, I 9216, vocab 151936, "
+                        "DeltaNet 16x128 k/v heads, attention 16q/4kv x128, quarter RoPE theta 1e7",
+            "labels": DEC_LABELS, "weights": "Q8_0 projections + tied Q8_0 token table (config 5)",
+            "l2": "inputs larger than L2 (6.9 GB of fp16-held weight codes and ~2 GB of activations per step)",
             "parallelism": f"request-sharded x{world}, no collective"}
 
 
@@ -171,6 +190,49 @@ def q8_cpu_baseline(rows):
     secs, cores = q8_cpu_seconds(rows)
     return {"value": rows * SEQ / secs, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{rows} x {SEQ} tokens, one full 22-layer Q8_0 decision forward ({secs:.1f} s)"}
+
+
+def dec_cpu_baseline(tokens, reps=1):
+    """A bounded CPU sample of config 5: the oracle's Q8_0 restatement of Qwen35Model.Forward over one row of `tokens`
+    ids through one [DeltaNet x3, full] block of the workload's weights, scaled to the 32-layer model (x8)."""
+    import numpy as np
+    import oracle
+    from laya_b200 import workloads
+    from oracle.decoder import DecoderConfig, OracleDecoder, mica_config
+    oracle.build()
+    kinds = workloads.MICA_KINDS[:4]
+    q8, vec = workloads.decoder_q8_weights(kinds, seed=0)
+    base = mica_config()
+    cfg = DecoderConfig(**{**base.__dict__, "layers": 4, "kinds": kinds})
+    stacks = {}
+    for i, k in enumerate(kinds):
+        p = f"layers.{i}."
+        groups = [[p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"], [p + "mlp.down_proj.weight"]]
+        if k == "full":
+            a = p + "self_attn."
+            groups += [[a + "q_proj.weight", a + "k_proj.weight", a + "v_proj.weight"], [a + "o_proj.weight"]]
+        else:
+            a = p + "linear_attn."
+            groups += [[a + n + ".weight" for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")],
+                       [a + "out_proj.weight"]]
+        for g in groups:
+            stacks["|".join(g)] = (np.concatenate([q8["model." + n][0] for n in g], 0),
+                                   np.concatenate([q8["model." + n][1] for n in g], 0).astype(np.float32))
+    qe, de = q8["model.embed_tokens.weight"]
+    stacks["embed"] = (qe, de.astype(np.float32))
+    om = OracleDecoder(cfg, vec, precision="q8_0", q8=stacks)
+    seqs, labels = workloads.decoder_batch(rows=1, length=tokens, seed=5)
+    times = []
+    for _ in range(reps + 1):
+        t0 = time.perf_counter()
+        _, last = om.forward(seqs[0], record=False)
+        om.logits(last, labels)
+        times.append(time.perf_counter() - t0)
+    secs = statistics.mean(times[1:]) * 8.0
+    return {"value": tokens / secs, "unit": "tokens/s", "cores": oracle.lib().lo_num_threads(), "kind": "port",
+            "sample": f"1 row x {tokens} tokens through one [DeltaNet x3, full] block of the config-5 Q8_0 weights "
+                      f"({secs / 8:.2f} s), scaled x8 to the 32-layer model, plus the 26 label logits; CPU "
+                      f"restatement of the reference's Qwen35Model Q8_0 forward"}
 
 
 class CpuTrainStep:
@@ -259,6 +321,18 @@ def run_reference(args):
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    if args.workload == "decoder":
+        vals = [dec_cpu_baseline(args.dec_tokens) for _ in range(max(1, args.steps // 5))]
+        b = vals[-1]
+        value = statistics.mean(v["value"] for v in vals)
+        line = {"impl": "reference", "metric": "Mica prefill tokens/s", "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": len(vals), "warmup": 1, "ms_per_step": DEC_TOKENS / value * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic", "config": dec_config(world),
+                "cpu_baseline": {**b, "value": value},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     c = CpuTrainStep(args.cpu_train_tokens)
     fbs, opts = [], []
     for i in range(args.warmup + args.steps):
@@ -277,6 +351,7 @@ def run_reference(args):
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload == "all" and not args.no_cpu_baseline:
         line["q8_0_encode"] = {"metric": "Q8_0 encode tokens/s", **q8_cpu_baseline(args.cpu_sample_rows)}
+        line["mica_prefill"] = {"metric": "Mica prefill tokens/s", **dec_cpu_baseline(args.dec_tokens)}
     print(json.dumps(line), flush=True)
 
 
@@ -528,6 +603,87 @@ def q8_measure(args, d):
     return out
 
 
+def dec_measure(args, d):
+    import numpy as np
+    import torch
+    import laya_b200
+    from laya_b200 import workloads
+    rank, world, local = d.rank, d.world, d.local
+    kinds = workloads.MICA_KINDS[:args.dec_layers]
+    model = laya_b200.Qwen35Model(laya_b200.decoder_desc(kinds, max_tokens=DEC_TOKENS, max_seqs=DEC_ROWS),
+                                  device=local)
+    q8, vec = workloads.decoder_q8_weights(kinds, seed=0)          # the same weights on every rank
+    for name, (q, dd) in q8.items():
+        model.upload_q8_0(name, q, dd)
+    for name, v in vec.items():
+        model.upload(name, v)
+    del q8, vec
+    seqs, labels = workloads.decoder_batch(rows=DEC_ROWS, length=DEC_LEN, n_labels=DEC_LABELS, seed=5 + rank)
+    ids = np.concatenate(seqs).astype(np.int32)
+    lens = [len(s) for s in seqs]
+    stream = torch.cuda.Stream()
+    model.set_stream(stream.cuda_stream)
+    ids_dev = torch.from_numpy(ids).cuda()
+    hidden = torch.zeros((DEC_ROWS, 2560), dtype=torch.float32, device="cuda")
+    logits = torch.zeros((DEC_ROWS, DEC_LABELS), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step_device():
+        model.forward_device(ids_dev.data_ptr(), lens, labels, hidden.data_ptr(), logits.data_ptr())
+
+    for _ in range(args.warmup):
+        step_device()
+    model.synchronize()
+    out = {}
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    d.barrier()
+    launches0 = model.launches()
+    model.set_profiling(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    e1.record(stream)
+    e1.synchronize()
+    out["launches"] = model.launches() - launches0
+    out["prof"] = [model.profile(k) for k in range(3)]
+    model.set_profiling(False)
+    model.synchronize()
+    d.barrier()
+    out["clocks"] = sampler.stop()
+    out["ms"] = e0.elapsed_time(e1) / args.steps
+    out["finite"] = bool(torch.isfinite(logits).all().item())
+
+    pin_ids = torch.from_numpy(ids).pin_memory()
+    lens_np = np.asarray(lens, np.int32)
+    lab_np = np.asarray(labels, np.int32)
+    host_hidden = torch.zeros((DEC_ROWS, 2560), dtype=torch.float32).pin_memory()
+    host_logits = torch.zeros((DEC_ROWS, DEC_LABELS), dtype=torch.float32).pin_memory()
+    L = laya_b200.lib()
+
+    def step_host():
+        laya_b200.api.check(L.laya_decoder_forward(
+            model.handle, pin_ids.data_ptr(), lens_np.ctypes.data, DEC_ROWS, lab_np.ctypes.data, DEC_LABELS,
+            host_hidden.data_ptr(), host_logits.data_ptr()))
+
+    step_host()
+    d.barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(stream)
+    for _ in range(args.steps):
+        step_host()
+    h1.record(stream)
+    h1.synchronize()
+    d.barrier()
+    out["e2e_ms"] = h0.elapsed_time(h1) / args.steps
+    out["h2d"] = int(ids.nbytes + lens_np.nbytes + lab_np.nbytes)
+    out["d2h"] = int(host_hidden.numel() * 4 + host_logits.numel() * 4)
+    model.close()
+    return out
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_env()
@@ -616,6 +772,42 @@ def run_ours(args):
                 line = q
             else:
                 line["q8_0_encode"] = q
+    if args.workload in ("all", "decoder"):
+        r = dec_measure(args, d)
+        ms, e2e_ms = d.reduce([r["ms"], r["e2e_ms"]], MAX)
+        if rank == 0:
+            (g_ms, g_ops, g_n), (r_ms, r_ops, r_n), (a_ms, a_ops, a_n) = r["prof"]
+            bf16 = peaks.get("bf16_tflops", 1590.0)
+            i8_peak = 2.0 * bf16
+            achieved = g_ops / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+            q = {
+                "metric": "Mica prefill tokens/s", "value": world * DEC_TOKENS / (ms / 1e3), "unit": "tokens/s",
+                "n_gpus": world, "ms_per_step": ms, "dtype": "int8", "scaling": "weak",
+                "config": dec_config(world, args.dec_layers),
+                "e2e": {"value": world * DEC_TOKENS / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
+                        "d2h_bytes_per_step": r["d2h"], "ms_per_step": e2e_ms},
+                "roofline": {"kernel": "q8_gemm_kernel (Q8_0 products: exact fp16-held codes on tcgen05 kind::f16, "
+                                       "per-block rescale)",
+                             "bound": "tensor", "achieved": achieved, "peak": i8_peak, "unit": "TOP/s",
+                             "frac": achieved / i8_peak, "peak_source": f"2 x {source} bf16 burst ({bf16} TFLOP/s)",
+                             "traffic": traffic.get("q8_gemm_dec", {}).get("dram_bytes_per_launch"), "launches": g_n,
+                             "share_of_step": g_ms / args.steps / ms},
+                "delta_rule": {"kernel": "delta_rule_kernel (sequential gated delta rule, one CTA per sequence x "
+                                         "value head)", "ms_per_step": r_ms / args.steps,
+                               "share_of_step": r_ms / args.steps / ms,
+                               "gflops": r_ops / (r_ms / 1e3) / 1e9 if r_ms else None},
+                "attention": {"kernel": "attn_prep + attention_kernel (fp16 mma.sync, causal GQA, sigmoid gate)",
+                              "ms_per_step": a_ms / args.steps, "share_of_step": a_ms / args.steps / ms,
+                              "tflops": a_ops / (a_ms / 1e3) / 1e12 if a_ms else None},
+                "gpu_launches": r["launches"], "clocks": r["clocks"], "logits_finite": r["finite"]}
+            if not args.no_cpu_baseline:
+                q["cpu_baseline"] = dec_cpu_baseline(args.dec_tokens)
+            if line is None:
+                q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "vs_baseline": None, "data": "synthetic"})
+                line = q
+            else:
+                line["mica_prefill"] = q
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

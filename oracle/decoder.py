@@ -138,36 +138,34 @@ class OracleDecoder:
 
     def proj(self, x, names: List[str]):
         """Stack (Qwen35Model.cs:300-345): sibling projections stacked along the output, one product."""
-        w = np.concatenate([self.W(n) for n in names], 0)
         if self.precision == "q8_0":
             key = "|".join(names)
             if key not in self.q8:
-                self.q8[key] = q8_quantize_weights(w)
+                self.q8[key] = q8_quantize_weights(np.concatenate([self.W(n) for n in names], 0))
             qw, dw = self.q8[key]
             return q8_linear(f32(x), qw, dw)
         from . import linear_f32
-        return linear_f32(f32(x), f32(w))
+        return linear_f32(f32(x), f32(np.concatenate([self.W(n) for n in names], 0)))
 
     def embed(self, ids):
-        table = self.W("embed_tokens.weight")
         if self.precision == "q8_0":
             if "embed" not in self.q8:
-                self.q8["embed"] = q8_quantize_weights(table)
+                self.q8["embed"] = q8_quantize_weights(self.W("embed_tokens.weight"))
             q, d = self.q8["embed"]
             # TokenTable.Row (Qwen35Model.cs:1076-1082): q · scale, per 32-block
             return (q[ids].astype(np.float32) * np.repeat(d[ids], 32, axis=1)).astype(np.float32)
-        return table[ids].copy()
+        return self.W("embed_tokens.weight")[ids].copy()
 
     def logits(self, hidden, ids):
         """Logits (Qwen35Model.cs:563-575) or QuantizedLogits (:1091-1111) for the given ids."""
-        table = self.W("embed_tokens.weight")
         h = f32(hidden).reshape(1, -1)
         if self.precision == "q8_0":
             if "embed" not in self.q8:
-                self.q8["embed"] = q8_quantize_weights(table)
+                self.q8["embed"] = q8_quantize_weights(self.W("embed_tokens.weight"))
             q, d = self.q8["embed"]
             return q8_linear(h, q[ids], d[ids])[0]
         from . import dot
+        table = self.W("embed_tokens.weight")
         return np.array([dot(h[0], table[i]) for i in ids], np.float32)
 
     # ---------------------------------------------------------------------------------------------- layers

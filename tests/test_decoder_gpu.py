@@ -5,9 +5,10 @@ Bars, with rel(a, b) = ||a − b|| / ||b|| as Qwen35ParityTests states them (Qwe
   * the fixture: every recorded state and the logits within 0.2 × of what Q8_0 moves them from the exact model —
     the reference's own bar for a Q8_0 forward — and the first mixer within 1e-4 of the Q8_0 fixture;
   * the oracle, teacher-forced layer by layer (the oracle's input of each layer fed to the GPU layer): mixer and layer
-    output within 2e-3.  Exact agreement is not expected: full attention runs fp16 operands with an online softmax
-    (the oracle: fp32 with a two-pass softmax), and one ulp of an exp can move an activation code of the next Q8_0
-    product by one step;
+    output within 2e-3 for DeltaNet layers and 1e-2 for full-attention layers.  Exact agreement is not expected: one
+    ulp of an exp can move an activation code of the next Q8_0 product by one step, and full attention runs fp16
+    operands with an online softmax (the oracle: fp32 with a two-pass softmax) — fp16 q and k put a relative error of
+    about 2^-12 · |q·k| into every score, up to ~1e-3 after the exp at these head widths;
   * the label logits of the oracle's final hidden row: bit-exact (integer block dots, fma per block in block order);
   * batching: several sequences in one forward give each sequence's single-sequence results bit for bit.
 """
@@ -17,6 +18,7 @@ import pytest
 from conftest import GOLDEN, bits
 
 pytestmark = pytest.mark.gpu
+LAYER_BAR = {"linear": 2e-3, "full": 1e-2}
 
 
 def rel(expected, actual):
@@ -76,8 +78,9 @@ def test_tiny_teacher_forced_layers_match_the_oracle(tiny):
     for i in range(cfg.layers):
         mixer, out = m.layer(i, x, [len(ids)])
         want_mixer, want_out = orc.layer(i, x)
-        assert rel(want_mixer, mixer) < 2e-3, (i, "mixer", rel(want_mixer, mixer))
-        assert rel(want_out, out) < 2e-3, (i, rel(want_out, out))
+        bar = LAYER_BAR[cfg.kinds[i]]
+        assert rel(want_mixer, mixer) < bar, (i, "mixer", rel(want_mixer, mixer))
+        assert rel(want_out, out) < bar, (i, rel(want_out, out))
         x = states[f"layers.{i}"]
 
 
@@ -177,20 +180,26 @@ def test_mica_geometry_teacher_forced_layers(mica4):
     for i in range(cfg.layers):
         mixer, out = m.layer(i, x, [len(ids)])
         want_mixer, want_out = orc.layer(i, x)
-        assert rel(want_mixer, mixer) < 2e-3, (i, "mixer", rel(want_mixer, mixer))
-        assert rel(want_out, out) < 2e-3, (i, rel(want_out, out))
+        bar = LAYER_BAR[cfg.kinds[i]]
+        assert rel(want_mixer, mixer) < bar, (i, "mixer", rel(want_mixer, mixer))
+        assert rel(want_out, out) < bar, (i, rel(want_out, out))
         x = want_out
 
 
 def test_mica_geometry_label_logits(mica4):
-    """Two ragged sequences end to end: label logits within 1e-2 of the oracle's (relative to their norm)."""
+    """Two ragged sequences end to end (no teacher forcing), at the reference's own bar for a Q8_0 forward: the GPU's
+    final hidden rows and label logits no further from the Q8_0 oracle than 0.2 × the distance Q8_0 itself puts
+    between the oracle's fp32 and Q8_0 forwards."""
+    from oracle.decoder import OracleDecoder
     cfg, w, m, orc = mica4
+    exact = OracleDecoder(cfg, w, precision="f32")
     rng = np.random.default_rng(8)
     seqs = [rng.integers(0, cfg.vocab, 300), rng.integers(0, cfg.vocab, 129)]
     labels = rng.choice(cfg.vocab, 26, replace=False)
     hidden, logits = m.forward(seqs, labels)
     for s, seq in enumerate(seqs):
         _, last = orc.forward(seq, record=False)
-        assert rel(last, hidden[s]) < 1e-2, (s, rel(last, hidden[s]))
-        want = orc.logits(last, labels)
-        assert rel(want, logits[s]) < 1e-2, (s, rel(want, logits[s]))
+        _, last32 = exact.forward(seq, record=False)
+        want, want32 = orc.logits(last, labels), exact.logits(last32, labels)
+        assert rel(last, hidden[s]) <= 0.2 * rel(last32, last), (s, rel(last, hidden[s]), rel(last32, last))
+        assert rel(want, logits[s]) <= 0.2 * rel(want32, want), (s, rel(want, logits[s]), rel(want32, want))
