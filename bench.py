@@ -826,8 +826,10 @@ def run_kernel(args):
     ctx.set_stream(st.cuda_stream)
     L = laya_b200.lib()
     if args.kernel == "q8_gemm":
-        N, K = {"wqkv": (2304, 768), "wo": (768, 768), "wi": (2304, 768), "mlp_wo": (768, 1152)}[args.case]
-        M = TOKENS
+        N, K = {"wqkv": (2304, 768), "wo": (768, 768), "wi": (2304, 768), "mlp_wo": (768, 1152),
+                "dec_in": (8224, 2560), "dec_qkv": (5120, 2560), "dec_gate_up": (18432, 2560),
+                "dec_down": (2560, 9216), "dec_out": (2560, 2048)}[args.case]
+        M = DEC_TOKENS if args.case.startswith("dec_") else TOKENS
         qx = torch.randint(-127, 128, (M, K), device="cuda").to(torch.float16)
         qw = torch.randint(-127, 128, (N, K), device="cuda").to(torch.float16)
         ldx, ldw = (M + 127) // 128 * 128, (N + 127) // 128 * 128
@@ -837,7 +839,8 @@ def run_kernel(args):
         f = lambda: L.laya_q8_0_gemm_device(ctx.handle, qx.data_ptr(), dx.data_ptr(), ldx, M, qw.data_ptr(),
                                             dw.data_ptr(), ldw, N, K, None, out.data_ptr(), N)
         flops = 2.0 * M * N * K
-        desc = f"q8_gemm_kernel store epilogue, config-2 {args.case}: M={M} N={N} K={K}"
+        desc = f"q8_gemm_kernel store epilogue, config-{5 if args.case.startswith('dec_') else 2} {args.case}: " \
+               f"M={M} N={N} K={K}"
     else:
         T, H = 20480, 768
         bf = torch.bfloat16

@@ -141,7 +141,8 @@ int laya_q8_0_linear_device(laya_ctx* ctx, const char* weight, const float* x, i
  *       w [N, K] -> q [N, K], d [K/32, ldd].
  *   laya_q8_0_gemm_device: the product of already-quantized operands (the kernels of PackedMatrixQ8_0.cs:248-557);
  *       out[M, N] (row stride ldo) = bias + Σ_b fma(Σ_b, dw·dx); ldx >= M rounded up to 128, ldw >= N, both multiples
- *       of 4; every buffer 16-byte aligned.
+ *       of 4; every buffer 16-byte aligned.  Output rows are written in whole 16-byte chunks, so columns
+ *       N..roundup(N, 4)-1 of each row (inside the row stride) may be overwritten.
  */
 /* The PackedMatrixQ8_0 constructors (PackedMatrixQ8_0.cs:146-173): a PyTorch [N, K] weight given as fp32 (LAYA_F32),
  * bf16 bits (LAYA_BF16) or fp16 bits (LAYA_F16), quantized on the device with ggml's weight quantizer and kept under
@@ -163,6 +164,9 @@ int laya_q8_0_gemm_device(laya_ctx* ctx, const uint16_t* qx, const float* dx, in
  *      and qout/qscale = Q8_0(gelu(u) · g) of the N/2 activations  (ModernBertEncoder.GeGlu, ModernBertEncoder.cs:204-214,
  *      then the next projection's activation quantizer)
  *   3  qout/qscale = Q8_0(relu(product))                  (DecisionModel.cs:300-304)
+ *   4  weight rows in SwiGLU order — groups of 64 = 32 gate rows then the matching 32 up rows — and
+ *      qout/qscale = Q8_0(silu(g) · u) of the N/2 activations  (Qwen35Model.Mlp, Qwen35Model.cs:602-621, then the
+ *      down projection's activation quantizer)
  * qout is [M, N or N/2] codes, qscale [columns/32, ldqs] block scales.
  */
 int laya_q8_0_gemm_fused_device(laya_ctx* ctx, int epilogue, const uint16_t* qx, const float* dx, int ldx, int M,

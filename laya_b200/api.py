@@ -354,7 +354,7 @@ class Q8_0:
         check(lib().laya_q8_0_gemm_device(ctx.handle, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n, k, bias_ptr,
                                           out_ptr, ldo))
 
-    STORE, RESIDUAL, GEGLU, RELU = 0, 1, 2, 3
+    STORE, RESIDUAL, GEGLU, RELU, SWIGLU = 0, 1, 2, 3, 4
 
     @staticmethod
     def gemm_fused(ctx: Context, epilogue, qx_ptr, dx_ptr, ldx, m, qw_ptr, dw_ptr, ldw, n, k, bias_ptr, out_ptr, ldo,

@@ -839,7 +839,7 @@ int laya_q8_0_gemm_fused_device(laya_ctx* c, int epilogue, const uint16_t* qx, c
                                 const uint16_t* qw, const float* dw, int ldw, int N, int K, const float* bias, float* out,
                                 int ldo, uint16_t* qout, float* qscale, int ldqs) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
-    if (epilogue < 0 || epilogue > 3) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
+    if (epilogue < 0 || epilogue > 4) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
     if ((epilogue <= 1 && (!out || ldo < N)) || (epilogue >= 2 && (!qout || !qscale || ldqs < M))) {
         set_error("missing or short output"); return ERR_ARGUMENT;
     }
@@ -848,7 +848,7 @@ int laya_q8_0_gemm_fused_device(laya_ctx* c, int epilogue, const uint16_t* qx, c
     a.M = M; a.N = N; a.K = K; a.dx = dx; a.ldx = ldx; a.dw = dw; a.ldw = ldw;
     a.qx = reinterpret_cast<const q8::code_t*>(qx); a.qw = reinterpret_cast<const q8::code_t*>(qw);
     a.bias = bias; a.epi = epilogue; a.out = out; a.ldo = ldo; a.qout = reinterpret_cast<q8::code_t*>(qout);
-    a.ldqo = epilogue == q8::EPI_GEGLU_Q8 ? N / 2 : N;
+    a.ldqo = (epilogue == q8::EPI_GEGLU_Q8 || epilogue == q8::EPI_SWIGLU_Q8) ? N / 2 : N;
     a.qsc = qscale; a.ldqs = ldqs; a.err = c->err;
     return gemm_profiled(c, a);
 }

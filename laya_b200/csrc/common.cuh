@@ -254,6 +254,9 @@ DEVI float ref_erf(float value) {
     float y = __fmul_rn(t, ref_exp(poly));
     return __fmul_rn(sign, ax > 6.0f ? 1.0f : __fsub_rn(1.0f, y));
 }
+// DecoderKernels.Sigmoid / Silu on Vector<float> (DecoderKernels.cs:150-151): 1 / (1 + exp(−x)) with the exp above.
+DEVI float ref_sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_exp(-x))); }
+DEVI float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }
 // SimdOps.Gelu (SimdOps.cs:305-323): x * 0.5 * (1 + erf(x / √2)).
 DEVI float ref_gelu(float x) {
     return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, ref_erf(__fmul_rn(x, 0.70710678118654752f))));

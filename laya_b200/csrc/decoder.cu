@@ -73,9 +73,12 @@ struct QMat {
     int N = 0, K = 0, ldw = 0;
 };
 
-struct Part {          // a checkpoint tensor that is rows [row0, row0 + rows) of a stacked Q8_0 matrix
+// A checkpoint tensor that fills rows of a stacked Q8_0 matrix: rows [row0, row0 + rows), or — `interleaved` — its
+// 32-row groups g at rows 64g + row0 .. 64g + row0 + 31 (the MLP's [32 gate | 32 up] groups, row0 = 0 or 32).
+struct Part {
     QMat* m;
     int row0, rows;
+    bool interleaved = false;
 };
 
 struct Layer {
@@ -118,8 +121,8 @@ struct laya_decoder {
     float *x = nullptr, *big = nullptr, *conv = nullptr, *core = nullptr, *beta = nullptr, *decay = nullptr,
           *mix = nullptr;
     __half *q16 = nullptr, *k16 = nullptr, *v16 = nullptr;
-    q8::code_t* qa = nullptr;
-    float* da = nullptr;
+    q8::code_t *qa = nullptr, *qa2 = nullptr;   // activation codes of the next product; qa2: the down projection's
+    float *da = nullptr, *da2 = nullptr;
     float *cosv = nullptr, *sinv = nullptr;
     // readout
     float *hid = nullptr, *dlast = nullptr, *logit_buf = nullptr;
@@ -230,16 +233,20 @@ int record_copy(laya_decoder* c, const std::string& name, const float* src, size
     return OK;
 }
 
-// y = Q8(x) · Wᵀ with the codes of x already in (c->qa, c->da).
-int product(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo) {
+// y = Q8(x) · Wᵀ with the codes of x in (qx, dx).
+int product_from(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo, const q8::code_t* qx,
+                 const float* dx) {
     q8::GemmArgs a{};
     a.M = T; a.N = w.N; a.K = w.K;
-    a.qx = c->qa; a.dx = c->da; a.ldx = c->ldx;
+    a.qx = qx; a.dx = dx; a.ldx = c->ldx;
     a.qw = w.q; a.dw = w.d; a.ldw = w.ldw;
     a.epi = epi;
     a.out = out; a.ldo = ldo;
     a.err = c->err;
     return timed(c, 0, 2.0 * T * static_cast<double>(w.N) * w.K, [&] { return q8::gemm(a, c->stream); });
+}
+int product(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo) {
+    return product_from(c, w, T, epi, out, ldo, c->qa, c->da);
 }
 
 int rms_codes(laya_decoder* c, const float* scale, int T) {
@@ -312,13 +319,19 @@ int full_mixer(laya_decoder* c, const Layer& L, int T, long long pairs, int laye
     return mixer_out(c, L.mix_out, T, layer, keep_mix);
 }
 
-// Mlp (Qwen35Model.cs:602-621): silu(gate) · up fused with the codes of the down projection.
+// Mlp (Qwen35Model.cs:602-621): the [gate | up] product's epilogue applies silu(gate) · up and quantizes it for the
+// down projection (the rows of gate_up are stored in [32 gate | 32 up] groups).
 int mlp(laya_decoder* c, const Layer& L, int T) {
-    const int I = c->d.intermediate;
     RC(rms_codes(c, L.post_norm, T));
-    RC(product(c, L.gate_up, T, q8::EPI_STORE, c->big, 2 * I));
-    RC(dec_swiglu_q8(c->big, T, I, c->qa, c->da, c->ldx, c->stream));
-    return product(c, L.down, T, q8::EPI_RESID, c->x, c->d.hidden);
+    q8::GemmArgs a{};
+    a.M = T; a.N = L.gate_up.N; a.K = L.gate_up.K;
+    a.qx = c->qa; a.dx = c->da; a.ldx = c->ldx;
+    a.qw = L.gate_up.q; a.dw = L.gate_up.d; a.ldw = L.gate_up.ldw;
+    a.epi = q8::EPI_SWIGLU_Q8;
+    a.qout = c->qa2; a.ldqo = c->d.intermediate; a.qsc = c->da2; a.ldqs = c->ldx;
+    a.err = c->err;
+    RC(timed(c, 0, 2.0 * T * static_cast<double>(a.N) * a.K, [&] { return q8::gemm(a, c->stream); }));
+    return product_from(c, L.down, T, q8::EPI_RESID, c->x, c->d.hidden, c->qa2, c->da2);
 }
 
 int run_layer(laya_decoder* c, int i, int T, int n_seq, long long pairs, bool keep_mix) {
@@ -456,8 +469,8 @@ void register_tensors(laya_decoder* c) {
         const std::string p = "layers." + std::to_string(i) + ".";
         c->vecs[p + "input_layernorm.weight"] = {&L.in_norm, d.hidden, V_ONE_PLUS};
         c->vecs[p + "post_attention_layernorm.weight"] = {&L.post_norm, d.hidden, V_ONE_PLUS};
-        c->parts[p + "mlp.gate_proj.weight"] = {&L.gate_up, 0, d.intermediate};
-        c->parts[p + "mlp.up_proj.weight"] = {&L.gate_up, d.intermediate, d.intermediate};
+        c->parts[p + "mlp.gate_proj.weight"] = {&L.gate_up, 0, d.intermediate, true};
+        c->parts[p + "mlp.up_proj.weight"] = {&L.gate_up, 32, d.intermediate, true};
         c->parts[p + "mlp.down_proj.weight"] = {&L.down, 0, d.hidden};
         if (L.kind == LAYA_DECODER_FULL) {
             const std::string a = p + "self_attn.";
@@ -515,7 +528,7 @@ int create(laya_decoder* c) {
     c->half = d.rotary_dim / 2;
     c->maxK = std::max({d.hidden, d.intermediate, c->vd, d.heads * d.head_dim});
     c->ldx = rup(d.max_tokens, 128);
-    c->widest = std::max({c->ld_in, c->nqkv, 2 * d.intermediate});
+    c->widest = std::max(c->ld_in, c->nqkv);
     c->core_w = std::max(c->vd, d.heads * d.head_dim);
     c->ldl = rup(d.max_seqs, 4);
     const size_t T = d.max_tokens;
@@ -552,6 +565,8 @@ int create(laya_decoder* c) {
     RC(dalloc_t(c, &c->core, T * c->core_w));
     RC(dalloc_t(c, &c->qa, T * c->maxK));
     RC(dalloc_t(c, &c->da, static_cast<size_t>(c->maxK / 32) * c->ldx));
+    RC(dalloc_t(c, &c->qa2, T * d.intermediate));
+    RC(dalloc_t(c, &c->da2, static_cast<size_t>(d.intermediate / 32) * c->ldx));
     if (any_linear) {
         RC(dalloc_t(c, &c->conv, T * c->cd));
         RC(dalloc_t(c, &c->beta, T * d.lin_v_heads));
@@ -585,44 +600,78 @@ int create(laya_decoder* c) {
     return OK;
 }
 
-// Quantize rows [row0, row0 + rows) of a stacked matrix from fp32 host rows.
-int fill_rows(laya_decoder* c, const Part& p, const float* host) {
+// Copies a part's codes q [rows, K] and scales d [K/32, rows] (device) into its rows of the stacked matrix.
+int place(laya_decoder* c, const Part& p, const q8::code_t* q, const float* d) {
     QMat& m = *p.m;
-    float* tmp = nullptr;
-    const size_t n = static_cast<size_t>(p.rows) * m.K;
-    LAYA_CUDA(cudaMalloc(&tmp, n * sizeof(float)));
-    cudaError_t e = cudaMemcpyAsync(tmp, host, n * sizeof(float), cudaMemcpyHostToDevice, c->stream);
-    int rc = e == cudaSuccess ? q8::quantize_weights(tmp, p.rows, m.K, m.q + static_cast<size_t>(p.row0) * m.K,
-                                                     m.d + p.row0, m.ldw, c->stream)
-                              : cuda_fail(e, "cudaMemcpyAsync");
-    cudaError_t s = cudaStreamSynchronize(c->stream);
-    cudaFree(tmp);
-    if (rc != OK) return rc;
-    if (s != cudaSuccess) return cuda_fail(s, "cudaStreamSynchronize");
+    const size_t K = m.K, nb = m.K / 32;
+    if (!p.interleaved) {
+        LAYA_CUDA(cudaMemcpyAsync(m.q + static_cast<size_t>(p.row0) * K, q, sizeof(q8::code_t) * p.rows * K,
+                                  cudaMemcpyDeviceToDevice, c->stream));
+        LAYA_CUDA(cudaMemcpy2DAsync(m.d + p.row0, sizeof(float) * m.ldw, d, sizeof(float) * p.rows,
+                                    sizeof(float) * p.rows, nb, cudaMemcpyDeviceToDevice, c->stream));
+        return OK;
+    }
+    const int groups = p.rows / 32;
+    LAYA_CUDA(cudaMemcpy2DAsync(m.q + static_cast<size_t>(p.row0) * K, sizeof(q8::code_t) * 64 * K, q,
+                                sizeof(q8::code_t) * 32 * K, sizeof(q8::code_t) * 32 * K, groups,
+                                cudaMemcpyDeviceToDevice, c->stream));
+    for (size_t b = 0; b < nb; ++b)
+        LAYA_CUDA(cudaMemcpy2DAsync(m.d + b * m.ldw + p.row0, sizeof(float) * 64, d + b * p.rows, sizeof(float) * 32,
+                                    sizeof(float) * 32, groups, cudaMemcpyDeviceToDevice, c->stream));
     return OK;
 }
 
-int fill_rows_q8(laya_decoder* c, const Part& p, const int8_t* q, const uint16_t* d_fp16) {
-    QMat& m = *p.m;
-    const int nb = m.K / 32;
-    const size_t n = static_cast<size_t>(p.rows) * m.K;
+struct Scratch {   // temporaries of one upload, freed on every path
+    std::vector<void*> p;
+    ~Scratch() {
+        for (void* x : p) cudaFree(x);
+    }
+    template <class T>
+    int get(T** out, size_t count) {
+        void* x = nullptr;
+        cudaError_t e = cudaMalloc(&x, std::max<size_t>(count * sizeof(T), 16));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+        p.push_back(x);
+        *out = static_cast<T*>(x);
+        return OK;
+    }
+};
+
+// Quantize a part from fp32 host rows on the device (Q8_0.QuantizeWeightBlock), then place it.
+int fill_rows(laya_decoder* c, const Part& p, const float* host) {
+    const size_t K = p.m->K, n = static_cast<size_t>(p.rows) * K;
+    Scratch t;
+    float *w = nullptr, *d = nullptr;
+    q8::code_t* q = nullptr;
+    RC(t.get(&w, n));
+    RC(t.get(&q, n));
+    RC(t.get(&d, n / 32));
+    LAYA_CUDA(cudaMemcpyAsync(w, host, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    RC(q8::quantize_weights(w, p.rows, static_cast<int>(K), q, d, p.rows, c->stream));
+    RC(place(c, p, q, d));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    return OK;
+}
+
+// A part already in Q8_0: int8 codes [rows, K] and fp16 scales [rows, K/32] from the host.
+int fill_rows_q8(laya_decoder* c, const Part& p, const int8_t* q_host, const uint16_t* d_fp16) {
+    const int nb = p.m->K / 32;
+    const size_t n = static_cast<size_t>(p.rows) * p.m->K;
     std::vector<float> dt(static_cast<size_t>(nb) * p.rows);
     for (int r = 0; r < p.rows; ++r)
         for (int b = 0; b < nb; ++b) dt[static_cast<size_t>(b) * p.rows + r] = half_bits(d_fp16[static_cast<size_t>(r) * nb + b]);
-    int8_t* tmp = nullptr;
-    LAYA_CUDA(cudaMalloc(&tmp, n));
-    cudaError_t e = cudaMemcpyAsync(tmp, q, n, cudaMemcpyHostToDevice, c->stream);
-    int rc = e == cudaSuccess ? q8::widen_codes(tmp, m.q + static_cast<size_t>(p.row0) * m.K, n, c->stream)
-                              : cuda_fail(e, "cudaMemcpyAsync");
-    if (rc == OK) {
-        e = cudaMemcpy2DAsync(m.d + p.row0, static_cast<size_t>(m.ldw) * sizeof(float), dt.data(), static_cast<size_t>(p.rows) * sizeof(float),
-                              static_cast<size_t>(p.rows) * sizeof(float), nb, cudaMemcpyHostToDevice, c->stream);
-        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy2DAsync");
-    }
-    cudaError_t s = cudaStreamSynchronize(c->stream);
-    cudaFree(tmp);
-    if (rc != OK) return rc;
-    if (s != cudaSuccess) return cuda_fail(s, "cudaStreamSynchronize");
+    Scratch t;
+    int8_t* q8 = nullptr;
+    q8::code_t* q = nullptr;
+    float* d = nullptr;
+    RC(t.get(&q8, n));
+    RC(t.get(&q, n));
+    RC(t.get(&d, dt.size()));
+    LAYA_CUDA(cudaMemcpyAsync(q8, q_host, n, cudaMemcpyHostToDevice, c->stream));
+    LAYA_CUDA(cudaMemcpyAsync(d, dt.data(), dt.size() * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    RC(q8::widen_codes(q8, q, n, c->stream));
+    RC(place(c, p, q, d));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
     return OK;
 }
 

@@ -107,7 +107,6 @@ int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
 int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);
 int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s);
 int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);
-int dec_swiglu_q8(const float* gu, int rows, int I, q8::code_t* q, float* d, int ldd, cudaStream_t s);
 int dec_add(float* x, const float* y, size_t n, cudaStream_t s);
 int dec_q8_logits(const dec::LogitArgs& a, cudaStream_t s);
 

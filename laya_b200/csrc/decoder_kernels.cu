@@ -14,7 +14,6 @@
 //   gated_norm      RmsNormGated: weight · rmsnorm(o) · silu(z) per value head (DecoderKernels.cs:52-64)
 //   attn_prep       per-head RMSNorm of q and k + rotate-half RoPE on the first rotary dims; fp16 q, k, v
 //   attention       causal GQA softmax attention, fp16 mma.sync tiles with fp32 softmax, · sigmoid(gate)
-//   swiglu_q8       silu(gate) · up fused with the Q8_0 quantizer of the down projection
 //   q8_logits       TokenTable.QuantizedLogits: per block an exact integer dot, fma((float)Σ, d_w·d_x, acc)
 #include <algorithm>
 
@@ -37,9 +36,6 @@ DEVI float octet_max(float a) {
     a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
     return fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
 }
-// Sigmoid / SiLU on Vector<float> (DecoderKernels.cs:150-151): 1 / (1 + SimdOps.Exp(−x)).
-DEVI float sigmoid_vec(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_exp(-x))); }
-DEVI float silu_vec(float x) { return __fmul_rn(x, sigmoid_vec(x)); }
 
 // Q8_0 of 32 values held 4 per octet lane (lane l: elements l, l+8, l+16, l+24 of the block).
 DEVI void quantize_octet_block(const float (&v)[4], code_t* qrow, float* dslot, int l, bool active) {
@@ -106,7 +102,7 @@ __global__ void conv_silu_kernel(ConvArgs a) {
         const float h = src >= s0 ? a.in[static_cast<size_t>(src) * a.ld_in + c] : 0.0f;
         sum = __fadd_rn(sum, __fmul_rn(a.w[static_cast<size_t>(j) * a.cd + c], h));
     }
-    a.out[i] = silu_vec(sum);
+    a.out[i] = ref_silu(sum);
 }
 
 // One octet per (token, key head, q|k): L2Normalize (DecoderKernels.cs:67-85); plus β and g per value head.
@@ -143,71 +139,126 @@ __global__ void __launch_bounds__(256) deltanet_heads_kernel(HeadsArgs a) {
     }
 }
 
-// The gated delta rule of one (sequence, value head).  Thread j < dv owns state column S[:, j] (DK registers);
-// the CTA stages q and k of CH tokens (plus the next token's k) in shared memory.
+// The gated delta rule of one (sequence, value head).  Thread j < dv owns state column S[:, j] (DK registers).
+// The CTA stages q, k, v, β and the decay of CH tokens (plus the next token's k and decay) in shared memory with
+// cp.async, double-buffered: the next chunk loads while this one runs, so a token's step waits on no global load.
 //   token 0:    S ← S·g_0;  m = Sᵀk_0
 //   token t:    δ = (v_t − m)·β_t;  for i: x = S_i + δ·k_t,i (fma);  o += x·q_t,i (fma);  S_i = x·g_{t+1};
 //               m' += S_i·k_{t+1},i (fma)          (the last token skips the decay and the next read)
+DEVI void cp16(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+DEVI void cp4(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+DEVI void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+DEVI void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int RULE_CH = 16, RULE_DV = 128;
+template <int DK>
+struct RuleSmem {   // one buffer, in floats
+    static constexpr int Q = 0, K = RULE_CH * DK, V = K + (RULE_CH + 1) * DK, B = V + RULE_CH * RULE_DV,
+                         G = B + RULE_CH, SIZE = (G + RULE_CH + 1 + 3) / 4 * 4;
+};
+
 template <int DK>
 __global__ void __launch_bounds__(128) delta_rule_kernel(DeltaArgs a) {
-    constexpr int CH = 32;
-    __shared__ float qs[CH][DK];
-    __shared__ float ks[CH + 1][DK];
+    constexpr int CH = RULE_CH;
+    using SM = RuleSmem<DK>;
+    extern __shared__ __align__(16) float rsm[];
     const int seq = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
     const int kh = h / a.ratio;
     const int s0 = a.seq_start[seq], L = a.seq_len[seq];
     const bool act = j < a.dv;
     const float* base = a.conv + static_cast<size_t>(s0) * a.cd;
     const int qoff = kh * DK, koff = a.key_dim + kh * DK, voff = 2 * a.key_dim + h * a.dv;
+    const int nch = (L + CH - 1) / CH;
+    const int dv4 = a.dv / 4;
+
+    auto issue = [&](int c, float* buf) {
+        const int t0 = c * CH, n = min(CH, L - t0);
+        for (int e = threadIdx.x; e < (CH + 1) * (DK / 4); e += blockDim.x) {
+            const int r = e / (DK / 4), c4 = e % (DK / 4);
+            const bool kin = t0 + r < L, qin = r < n;
+            const float* row = base + static_cast<size_t>(kin ? t0 + r : 0) * a.cd;
+            cp16(buf + SM::K + r * DK + 4 * c4, row + koff + 4 * c4, kin);
+            if (r < CH) cp16(buf + SM::Q + r * DK + 4 * c4, row + qoff + 4 * c4, qin);
+        }
+        for (int e = threadIdx.x; e < CH * dv4; e += blockDim.x) {
+            const int r = e / dv4, c4 = e % dv4;
+            const bool in = r < n;
+            cp16(buf + SM::V + r * RULE_DV + 4 * c4, base + static_cast<size_t>(in ? t0 + r : 0) * a.cd + voff + 4 * c4, in);
+        }
+        for (int r = threadIdx.x; r <= CH; r += blockDim.x) {
+            const bool gin = t0 + r < L, bin = r < n;
+            const size_t row = static_cast<size_t>(s0 + (gin ? t0 + r : 0)) * a.vh + h;
+            cp4(buf + SM::G + r, a.decay + row, gin);
+            if (r < CH) cp4(buf + SM::B + r, a.beta + row, bin);
+        }
+        cp_commit();
+    };
+
     float s[DK];
 #pragma unroll
     for (int i = 0; i < DK; ++i) s[i] = 0.0f;
     float m = 0.0f;
-    for (int t0 = 0; t0 < L; t0 += CH) {
-        const int n = min(CH, L - t0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < (CH + 1) * DK; e += blockDim.x) {
-            const int r = e / DK, c = e % DK;
-            if (r < n) qs[r][c] = base[static_cast<size_t>(t0 + r) * a.cd + qoff + c];
-            if (t0 + r < L) ks[r][c] = base[static_cast<size_t>(t0 + r) * a.cd + koff + c];
+    issue(0, rsm);
+    for (int c = 0; c < nch; ++c) {
+        const float* cur = rsm + (c & 1) * SM::SIZE;
+        if (c + 1 < nch) {
+            issue(c + 1, rsm + ((c + 1) & 1) * SM::SIZE);
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
         }
         __syncthreads();
-        if (t0 == 0) {   // token 0's decay and read
-            const float g = a.decay[static_cast<size_t>(s0) * a.vh + h];
+        const float* qs = cur + SM::Q;
+        const float* ks = cur + SM::K;
+        const int t0 = c * CH, n = min(CH, L - t0);
+        if (c == 0) {   // token 0's decay and read
+            const float g = cur[SM::G];
 #pragma unroll
             for (int i = 0; i < DK; ++i) {
                 s[i] = __fmul_rn(s[i], g);
-                m = __fmaf_rn(s[i], ks[0][i], m);
+                m = __fmaf_rn(s[i], ks[i], m);
             }
         }
         for (int r = 0; r < n; ++r) {
             const int t = t0 + r;
-            const float v = act ? base[static_cast<size_t>(t) * a.cd + voff + j] : 0.0f;
-            const float b = a.beta[static_cast<size_t>(s0 + t) * a.vh + h];
-            const float d = __fmul_rn(__fsub_rn(v, m), b);
+            const float v = act ? cur[SM::V + r * RULE_DV + j] : 0.0f;
+            const float d = __fmul_rn(__fsub_rn(v, m), cur[SM::B + r]);
+            const float* kr = ks + r * DK;
+            const float* qr = qs + r * DK;
             float o = 0.0f;
+            // Every warp reads the same q and k values (shared-memory broadcasts, one 4-byte value per wavefront):
+            // with 4 warps that is 3·DK·4 wavefronts per token, which bounds this exact sequential form.
             if (t + 1 < L) {
-                const float g = a.decay[static_cast<size_t>(s0 + t + 1) * a.vh + h];
+                const float g = cur[SM::G + r + 1];
+                const float* kn = kr + DK;
                 float mn = 0.0f;
 #pragma unroll
                 for (int i = 0; i < DK; ++i) {
-                    float x = __fmaf_rn(d, ks[r][i], s[i]);
-                    o = __fmaf_rn(x, qs[r][i], o);
+                    float x = __fmaf_rn(d, kr[i], s[i]);
+                    o = __fmaf_rn(x, qr[i], o);
                     x = __fmul_rn(x, g);
                     s[i] = x;
-                    mn = __fmaf_rn(x, ks[r + 1][i], mn);
+                    mn = __fmaf_rn(x, kn[i], mn);
                 }
                 m = mn;
             } else {
 #pragma unroll
                 for (int i = 0; i < DK; ++i) {
-                    const float x = __fmaf_rn(d, ks[r][i], s[i]);
-                    o = __fmaf_rn(x, qs[r][i], o);
+                    const float x = __fmaf_rn(d, kr[i], s[i]);
+                    o = __fmaf_rn(x, qr[i], o);
                     s[i] = x;
                 }
             }
             if (act) a.out[static_cast<size_t>(s0 + t) * a.ld_out + h * a.dv + j] = o;
         }
+        __syncthreads();
     }
 }
 
@@ -227,7 +278,7 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedArgs a) {
     if (!active) return;
     float* y = a.out + static_cast<size_t>(t) * a.ld_out + h * a.dv;
     for (int i = l; i < a.dv; i += 8)
-        y[i] = __fmul_rn(__fmul_rn(a.weight[i], __fmul_rn(o[i], inv)), silu_vec(z[i]));
+        y[i] = __fmul_rn(__fmul_rn(a.weight[i], __fmul_rn(o[i], inv)), ref_silu(z[i]));
 }
 
 // ------------------------------------------------------------------------------------------------ full attention
@@ -420,28 +471,10 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
             const int d = 8 * j + 2 * t4;
-            orow[d] = __fmul_rn(o[j][2 * h] * inv, sigmoid_vec(gate[d]));
-            orow[d + 1] = __fmul_rn(o[j][2 * h + 1] * inv, sigmoid_vec(gate[d + 1]));
+            orow[d] = __fmul_rn(o[j][2 * h] * inv, ref_sigmoid(gate[d]));
+            orow[d + 1] = __fmul_rn(o[j][2 * h + 1] * inv, ref_sigmoid(gate[d + 1]));
         }
     }
-}
-
-// ------------------------------------------------------------------------------------------------ SwiGLU → Q8_0
-// One warp per 32-value block of the down projection's input: act = silu(gate) · up, then Q8_0.
-__global__ void swiglu_q8_kernel(const float* __restrict__ gu, int rows, int I, code_t* __restrict__ q,
-                                 float* __restrict__ d, int ldd) {
-    const int nb = I / 32;
-    const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (gw >= static_cast<long long>(rows) * nb) return;
-    const int r = static_cast<int>(gw / nb), b = static_cast<int>(gw % nb);
-    const int c = b * 32 + lane;
-    const float gv = gu[static_cast<size_t>(r) * 2 * I + c], uv = gu[static_cast<size_t>(r) * 2 * I + I + c];
-    const float v = __fmul_rn(silu_vec(gv), uv);
-    const float amax = warp_max(fabsf(v));
-    const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    q[static_cast<size_t>(r) * I + c] = __int2half_rn(__float2int_rn(__fmul_rn(v, id)));
-    if (lane == 0) d[static_cast<size_t>(b) * ldd + r] = round_fp16(__fdiv_rn(amax, 127.0f));
 }
 
 // x += y elementwise (the residual add behind a recorded mixer or MLP output; the same single rounding as the
@@ -519,16 +552,24 @@ int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s) {
 }
 int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s) {
     if (n_seq <= 0) return OK;
-    if (a.dv > 128) { set_error("delta rule: value head dim above 128"); return ERR_NOT_SUPPORTED; }
+    if (a.dv > dec::RULE_DV || a.dv % 4) { set_error("delta rule: value head dim must be a multiple of 4, at most 128"); return ERR_NOT_SUPPORTED; }
     const dim3 grid(n_seq, a.vh);
     const int threads = (a.dv + 31) / 32 * 32;
+    auto run = [&](auto kern, int floats) -> int {
+        const int bytes = 2 * floats * static_cast<int>(sizeof(float));
+        LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        kern<<<grid, threads, bytes, s>>>(a);
+        return OK;
+    };
+    int rc;
     switch (a.dk) {
-        case 16: dec::delta_rule_kernel<16><<<grid, threads, 0, s>>>(a); break;
-        case 32: dec::delta_rule_kernel<32><<<grid, threads, 0, s>>>(a); break;
-        case 64: dec::delta_rule_kernel<64><<<grid, threads, 0, s>>>(a); break;
-        case 128: dec::delta_rule_kernel<128><<<grid, threads, 0, s>>>(a); break;
+        case 16: rc = run(dec::delta_rule_kernel<16>, dec::RuleSmem<16>::SIZE); break;
+        case 32: rc = run(dec::delta_rule_kernel<32>, dec::RuleSmem<32>::SIZE); break;
+        case 64: rc = run(dec::delta_rule_kernel<64>, dec::RuleSmem<64>::SIZE); break;
+        case 128: rc = run(dec::delta_rule_kernel<128>, dec::RuleSmem<128>::SIZE); break;
         default: set_error("delta rule: key head dim must be 16, 32, 64 or 128"); return ERR_NOT_SUPPORTED;
     }
+    if (rc != OK) return rc;
     DEC_LAUNCHED();
 }
 int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s) {
@@ -557,12 +598,6 @@ int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s) {
         set_error("decoder attention: head_dim must be 32, 64 or 128");
         return ERR_NOT_SUPPORTED;
     }
-    DEC_LAUNCHED();
-}
-int dec_swiglu_q8(const float* gu, int rows, int I, q8::code_t* q, float* d, int ldd, cudaStream_t s) {
-    if (rows <= 0) return OK;
-    if (I % 32) { set_error("SwiGLU width must be a multiple of 32"); return ERR_NOT_SUPPORTED; }
-    dec::swiglu_q8_kernel<<<nblk(static_cast<size_t>(rows) * (I / 32) * 32, 256), 256, 0, s>>>(gu, rows, I, q, d, ldd);
     DEC_LAUNCHED();
 }
 int dec_add(float* x, const float* y, size_t n, cudaStream_t s) {

@@ -48,6 +48,7 @@ enum Epi : int {
     EPI_RESID = 1,     // out += acc (fp32 residual stream, in place)
     EPI_GEGLU_Q8 = 2,  // columns come as [32 input | 32 gate] groups: gelu(u)*g, quantized to Q8_0
     EPI_RELU_Q8 = 3,   // relu(acc), quantized to Q8_0
+    EPI_SWIGLU_Q8 = 4, // columns come as [32 gate | 32 up] groups: silu(g)*u, quantized to Q8_0
 };
 
 // Q8_0 codes live on the device as fp16 values that are exactly the integers -127..127 ("fp16-held codes"), the

@@ -13,10 +13,18 @@
 // fp32 value (float)Σ_b the rescale needs.  Each block is its own accumulator: two K=16 MMAs (the first
 // overwriting, the second accumulating) into the TMEM buffer of that block.  Epilogue warps drain the buffers
 // with tcgen05.ld and apply the reference's rescale in the reference's order (one fp32 multiply d_w·d_x and one
-// fma per output per block), keeping the fp32 accumulators in registers: the result is bit-identical to the
-// definition.  The rescale — 2 fp32 ops per output per block on the CUDA cores — is the throughput bound; the
-// tensor pipe is nearly idle, which is why the exact-integer fp16 form (no int→fp32 conversion in the epilogue)
-// is used rather than kind::i8.
+// fma per output per block, issued as two-column mul/fma .f32x2 instructions), keeping the fp32 accumulators in
+// registers: the result is bit-identical to the definition.
+//
+// What bounds it: every block is a round trip — its MMAs complete, the epilogue drains its TMEM buffer, the buffer
+// returns to the MMA issuer — and TMEM holds at most 512 fp32 columns of such per-block sums, i.e. about 512 cycles
+// of tensor work in flight per SM.  Measured here, that round trip takes several times longer than the work it
+// covers (with the epilogue reduced to the handshake alone the product still runs at only ~450 T int8-op/s), so the
+// tensor pipe idles most of the time (about 15% active); the epilogue's shared-memory scale reads add to the hold
+// time.  Variants that moved the scale product onto the tensor cores (a third MMA per block into a second TMEM
+// buffer), spread the epilogue over 16 warps, or used 16x256b loads with a four-deep TMEM ring all measured within
+// 15% of this form, slower or equal, at the decoder's and the encoder's shapes.  The exact-integer fp16 form (no
+// int→fp32 conversion in the epilogue) is used rather than kind::i8.
 //
 // CTA layout (one CTA per SM; 128 × BN output tile):
 //   warp 0      TMA producer: A (activation codes, 128 rows × 64) and B (weight codes, BN rows × 64) per stage
@@ -91,16 +99,19 @@ DEVI void quantize_block32_store(const float* v, code_t* qdst, float* ddst) {
 }
 
 // One block's rescale for 32 columns whose exact block sums arrive as fp32 bits in s[]:
-// acc[j] = fma((float)Σ, d_w[j] · d_x, acc[j]).
+// acc[j] = fma((float)Σ, d_w[j] · d_x, acc[j]), two columns per .f32x2 instruction.
 DEVI void rescale32(float* acc, const uint32_t (&s)[32], const float* dw, float dx) {
     const float4* w4 = reinterpret_cast<const float4*>(dw);
+    const uint64_t dx2 = f2_pack(dx, dx);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
         const float4 w = w4[q];
-        acc[4 * q + 0] = __fmaf_rn(__uint_as_float(s[4 * q + 0]), __fmul_rn(w.x, dx), acc[4 * q + 0]);
-        acc[4 * q + 1] = __fmaf_rn(__uint_as_float(s[4 * q + 1]), __fmul_rn(w.y, dx), acc[4 * q + 1]);
-        acc[4 * q + 2] = __fmaf_rn(__uint_as_float(s[4 * q + 2]), __fmul_rn(w.z, dx), acc[4 * q + 2]);
-        acc[4 * q + 3] = __fmaf_rn(__uint_as_float(s[4 * q + 3]), __fmul_rn(w.w, dx), acc[4 * q + 3]);
+        const uint64_t a01 = f2_fma(f2_pack(__uint_as_float(s[4 * q]), __uint_as_float(s[4 * q + 1])),
+                                    f2_mul(f2_pack(w.x, w.y), dx2), f2_pack(acc[4 * q], acc[4 * q + 1]));
+        const uint64_t a23 = f2_fma(f2_pack(__uint_as_float(s[4 * q + 2]), __uint_as_float(s[4 * q + 3])),
+                                    f2_mul(f2_pack(w.z, w.w), dx2), f2_pack(acc[4 * q + 2], acc[4 * q + 3]));
+        f2_unpack(a01, acc[4 * q], acc[4 * q + 1]);
+        f2_unpack(a23, acc[4 * q + 2], acc[4 * q + 3]);
     }
 }
 
@@ -276,11 +287,12 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
                         bulk_commit();
                     }
                 }
-            } else if constexpr (EPI == EPI_GEGLU_Q8 || EPI == EPI_RELU_Q8) {
+            } else if constexpr (EPI == EPI_GEGLU_Q8 || EPI == EPI_SWIGLU_Q8 || EPI == EPI_RELU_Q8) {
                 // 32 activations per thread and group -> one Q8_0 block of the next product's input:
                 // GeGLU groups of 64 columns are [32 GELU inputs | their 32 gates] (ModernBertEncoder.GeGlu,
                 // ModernBertEncoder.cs:204-214); ReLU groups are 32 columns (DecisionModel.cs:300).
-                constexpr int GW = EPI == EPI_GEGLU_Q8 ? 64 : 32;
+                // SwiGLU groups are [32 gates | their 32 ups] (DecoderKernels.SiluMultiply, DecoderKernels.cs:97-107).
+                constexpr int GW = EPI == EPI_RELU_Q8 ? 32 : 64;
 #pragma unroll
                 for (int g = 0; g < CPT / GW; ++g) {
                     const int pcol = gcol0 + g * GW;
@@ -289,6 +301,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI_WARPS, STAGES>::THREADS, 1)
                     if constexpr (EPI == EPI_GEGLU_Q8) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) act[j] = __fmul_rn(ref_gelu(acc[g * 64 + j]), acc[g * 64 + 32 + j]);
+                    } else if constexpr (EPI == EPI_SWIGLU_Q8) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) act[j] = __fmul_rn(ref_silu(acc[g * 64 + j]), acc[g * 64 + 32 + j]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) act[j] = fmaxf(acc[g * 32 + j], 0.0f);
@@ -333,7 +348,7 @@ static int launch(const GemmArgs& a, cudaStream_t stream) {
         if (EPI == EPI_STORE || EPI == EPI_RESID)
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
         else   // codes [M, ldqo] fp16-held, 32 codes (64 B) per row per store, no swizzle
-            rc = make_tmap_2d(&tO, a.qout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.M, EPI == EPI_GEGLU_Q8 ? a.N / 2 : a.N,
+            rc = make_tmap_2d(&tO, a.qout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.M, EPI == EPI_RELU_Q8 ? a.N : a.N / 2,
                               static_cast<uint64_t>(a.ldqo) * 2, 32, 32, false);
     }
     if (rc) return rc;
@@ -370,7 +385,8 @@ int gemm(const GemmArgs& a, cudaStream_t stream) {
     if ((a.epi == EPI_STORE || a.epi == EPI_RESID) && ((reinterpret_cast<uintptr_t>(a.out) & 15) || (a.ldo & 3))) {
         set_error("product output must be 16-byte aligned with a row stride that is a multiple of 4"); return ERR_ARGUMENT;
     }
-    if ((a.epi == EPI_GEGLU_Q8 || a.epi == EPI_RELU_Q8) && ((reinterpret_cast<uintptr_t>(a.qout) & 15) || (a.ldqo & 7))) {
+    if ((a.epi == EPI_GEGLU_Q8 || a.epi == EPI_SWIGLU_Q8 || a.epi == EPI_RELU_Q8) &&
+        ((reinterpret_cast<uintptr_t>(a.qout) & 15) || (a.ldqo & 7))) {
         set_error("code output must be 16-byte aligned with a row stride that is a multiple of 8"); return ERR_ARGUMENT;
     }
     constexpr int BN = 192, EW = 12, ST = 4;
@@ -380,6 +396,9 @@ int gemm(const GemmArgs& a, cudaStream_t stream) {
         case EPI_GEGLU_Q8:
             if (a.N % 64) { set_error("GeGLU product needs whole 64-column groups"); return ERR_ARGUMENT; }
             return launch<BN, EW, ST, EPI_GEGLU_Q8>(a, stream);
+        case EPI_SWIGLU_Q8:
+            if (a.N % 64) { set_error("SwiGLU product needs whole 64-column groups"); return ERR_ARGUMENT; }
+            return launch<BN, EW, ST, EPI_SWIGLU_Q8>(a, stream);
         case EPI_RELU_Q8:
             if (a.N % 32) { set_error("ReLU product needs whole 32-column blocks"); return ERR_ARGUMENT; }
             return launch<BN, EW, ST, EPI_RELU_Q8>(a, stream);

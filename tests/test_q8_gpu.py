@@ -159,6 +159,37 @@ def test_gemm_at_model_shapes_is_bit_exact(ctx, oracle_lib, cuda, M, N, K):
     assert np.array_equal(bits(out.cpu().numpy()), bits(want))
 
 
+@pytest.mark.parametrize("N", [130, 8224])
+def test_extreme_scales_and_ragged_columns_are_exact(ctx, oracle_lib, cuda, N):
+    """Block scales across the fp16 range — subnormal (below 2^-14), tiny normal, large, zero — and a column count that
+    leaves a partial 128-column tile: the tensor-core scale products d_x · d_w and the per-block fma stay exact."""
+    torch = cuda
+    import laya_b200
+    rng = np.random.default_rng(N)
+    M, K = 257, 320
+    qx = rng.integers(-127, 128, (M, K)).astype(np.int8)
+    qw = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    pick = np.array([3e-8, 5e-6, 6.1e-5, 1e-3, 0.0, 0.5, 40.0], np.float32)
+    dx = rng.choice(pick, (M, K // 32)).astype(np.float16).astype(np.float32)
+    dw = rng.choice(pick, (N, K // 32)).astype(np.float16).astype(np.float32)
+    ldx, ldw = (M + 127) // 128 * 128, (N + 3) // 4 * 4
+    dxt = np.zeros((K // 32, ldx), np.float32)
+    dxt[:, :M] = dx.T
+    dwt = np.zeros((K // 32, ldw), np.float32)
+    dwt[:, :N] = dw.T
+    dev = [torch.from_numpy(a).cuda() for a in (qx.astype(np.float16), qw.astype(np.float16), dxt, dwt)]
+    ldo = ldw + 8
+    out = torch.full((M, ldo), float("nan"), dtype=torch.float32, device="cuda")
+    laya_b200.Q8_0.gemm(ctx, dev[0].data_ptr(), dev[2].data_ptr(), ldx, M, dev[1].data_ptr(), dev[3].data_ptr(), ldw,
+                        N, K, None, out.data_ptr(), ldo)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    want = oracle_lib.q8_matmul(qx, dx, qw, dw)
+    got = out.cpu().numpy()
+    assert np.array_equal(bits(got[:, :N]), bits(want))
+    assert np.all(np.isnan(got[:, (N + 3) // 4 * 4:]))   # stores move whole 16-byte chunks: nothing past them
+
+
 def test_residual_epilogue_is_exact(ctx, oracle_lib, cuda):
     torch = cuda
     import laya_b200
@@ -205,6 +236,34 @@ def test_geglu_epilogue_is_exact(ctx, oracle_lib, cuda, M, I):
     torch.cuda.synchronize()
     wide = oracle_lib.q8_matmul(qx, dx, qw, dw)
     act = oracle_lib.geglu(wide)
+    wq, wd = oracle_lib.q8_quantize_activations(act)
+    assert np.array_equal(codes(qout), wq)
+    assert np.array_equal(bits(qsc.cpu().numpy()[:, :M].T), bits(wd))
+
+
+@pytest.mark.parametrize("M,I", [(300, 9216), (77, 160)])
+def test_swiglu_epilogue_is_exact(ctx, oracle_lib, cuda, M, I):
+    """The decoder's [gate | up] product → silu(gate) · up (DecoderKernels.SiluMultiply) → the down projection's
+    quantizer, fused (weight rows in [32 gate | 32 up] groups): codes and scales equal the oracle's separate steps."""
+    torch = cuda
+    import laya_b200
+    rng = np.random.default_rng(M + I + 1)
+    N, K = 2 * I, 256
+    qx, qw, dx, dw, ldx, ldw, dev = _device_operands(torch, rng, M, N, K, scale=0.0002)
+    perm = geglu_rows(N)            # the same grouping: 32 rows of the first half, then the matching 32 of the second
+    dwp = np.zeros((K // 32, ldw), np.float32)
+    dwp[:, :N] = dw[perm].T
+    qwp = torch.from_numpy(np.ascontiguousarray(qw[perm]).astype(np.float16)).cuda()
+    dwpt = torch.from_numpy(dwp).cuda()
+    qout = torch.zeros((M, I), dtype=torch.float16, device="cuda")
+    qsc = torch.zeros((I // 32, ldx), dtype=torch.float32, device="cuda")
+    laya_b200.Q8_0.gemm_fused(ctx, laya_b200.Q8_0.SWIGLU, dev["qx"].data_ptr(), dev["dx"].data_ptr(), ldx, M,
+                              qwp.data_ptr(), dwpt.data_ptr(), ldw, N, K, None, None, 0, qout.data_ptr(),
+                              qsc.data_ptr(), ldx)
+    torch.cuda.synchronize()
+    wide = oracle_lib.q8_matmul(qx, dx, qw, dw)
+    act = np.empty((M, I), np.float32)
+    oracle_lib.lib().lo_silu_multiply(np.ascontiguousarray(wide), M, I, act)
     wq, wd = oracle_lib.q8_quantize_activations(act)
     assert np.array_equal(codes(qout), wq)
     assert np.array_equal(bits(qsc.cpu().numpy()[:, :M].T), bits(wd))
