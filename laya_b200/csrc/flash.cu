@@ -636,7 +636,14 @@ static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
     if (rc) return rc;
     dim3 grid(max_tiles, a.heads);
     fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    if (HD == 64) {   // dK, dV on the tensor cores (flash_tc.cu) when the batch carries its 128-row tile list
+        rc = flash_backward_dkdv_tc(a, s);
+        if (rc != ERR_NOT_SUPPORTED) return rc;
+    }
     fa::bwd_dkdv_kernel<HD><<<grid, 128, smem_kv, s>>>(a);
+    count_launch();
     return OK;
 }
 
@@ -651,7 +658,6 @@ int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
     else if (hd == 32) rc = launch_bwd<32>(a, max_tiles, s);
     else { set_error("attention supports head_dim 32 and 64"); return ERR_NOT_SUPPORTED; }
     if (rc) return rc;
-    count_launch(2);
     LAYA_CUDA(cudaGetLastError());
     return OK;
 }

@@ -17,6 +17,7 @@
 //               At the end the two halves' row sums are combined and each warp stores its 32 context columns.
 // The accurate forward (SPLIT) keeps hi and lo bf16 parts of Q, K, V and P and issues three MMAs per product
 // (hi·hi + lo·hi + hi·lo), accumulating in the same TMEM columns.
+// The backward's dK/dV kernel (bwd_dkdv_tc_kernel, below) uses the same roles with keys in the TMEM lanes.
 // Every wait is bounded (common.cuh): a protocol fault ends with an error status, never a hung GPU.
 #include <algorithm>
 
@@ -358,6 +359,265 @@ __global__ void __launch_bounds__(320, 1)
     }
 }
 
+
+// ------------------------------------------------------------------------------------------------ backward: dK, dV
+// Same contract as fa::bwd_dkdv_kernel (flash.cu; Ops.AttentionBackward, Laya.Training/Ops.cs:368-470): for one
+// 128-key tile of one head, over every 128-query tile that sees it,
+//     Sᵀ = K·Qᵀ,  dPᵀ = V·dOᵀ  (M 128 keys, N 128 queries, K 64)          into TMEM columns [0, 128), [128, 256)
+//     Pᵀ = exp(scale·Sᵀ − lse) (· dropout),  dSᵀ = scale · P ∘ (dPᵀ·m − D)   by the softmax warps, bf16 into smem
+//     dV += Pᵀ·dO,  dK += dSᵀ·Q  (M 128 keys, N 64, K 128 queries; dO and Q read N-contiguous) into [256, 384)
+// then dK (rotated back by −θ at the key's position) and dV in bf16.  lse and D of the query tile are staged next to
+// its Q and dO tiles by the producer warp.
+struct BwdParams {
+    const int32_t* seg_start; const int32_t* seg_len;
+    const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq;
+    int window, hidden, heads;
+    float scale, dropout, keep;
+    uint64_t seed;
+    const float* lse; const float* dsum;
+    const float* cosv; const float* sinv;
+    __nv_bfloat16* dqkv; int lddq;
+    int* err;
+};
+constexpr int BWD_SMEM = 1024 + 10 * TILE + 2 * 2 * BQ * 4 + 256;   // K, V, 2 × (Q, dO), Pᵀ (2), dSᵀ (2); lse/D
+
+DEVI float drop_mult_b(const BwdParams& p, int head, int row, int key) {
+    if (p.dropout <= 0.0f) return 1.0f;
+    const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
+    uint64_t z = p.seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f) < p.dropout ? 0.0f : p.keep;
+}
+
+static_assert(BWD_SMEM <= 232448, "shared memory budget");
+
+template <bool DROP>
+__global__ void __launch_bounds__(320, 1)
+    bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmqkv, const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
+    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BK, BQ);                     // M keys, N queries, K-major
+    constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BK, HD) | (1u << 16);        // B (dO, Q) N-contiguous
+    const int tile = blockIdx.x;
+    if (tile >= *p.n_tq) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sK = smem;
+    uint8_t* sV = smem + TILE;
+    uint8_t* sQO = smem + 2 * TILE;        // [2 stages][Q, dO]
+    uint8_t* sP = smem + 6 * TILE;         // Pᵀ: 2 sub-tiles of 64 queries
+    uint8_t* sDS = smem + 8 * TILE;        // dSᵀ: 2 sub-tiles
+    float* sRow = reinterpret_cast<float*>(smem + 10 * TILE);   // [2 stages][lse 128 | D 128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + 2 * 2 * BQ);
+    uint64_t* kv_full = bars;
+    uint64_t* full = bars + 1;        // [2]
+    uint64_t* empty = bars + 3;       // [2]
+    uint64_t* st_full = bars + 5;
+    uint64_t* st_free = bars + 6;
+    uint64_t* pd_full = bars + 7;
+    uint64_t* pd_empty = bars + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int head = blockIdx.y, item = p.tq_item[tile], k0 = p.tq_p0[tile];
+    const int seg0 = p.seg_start[item], L = p.seg_len[item];
+    const bool global = p.window < 0;
+    const int W = p.window;
+    const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + BK + W);
+    const int nq = (qe - qb0 + BQ - 1) / BQ;
+    const int warp = warp_id(), lane = lane_id();
+
+    if (threadIdx.x == 0) {
+        mbar_init(kv_full, 1);
+        for (int s = 0; s < 2; ++s) { mbar_init(full + s, 2); mbar_init(empty + s, 1); }
+        mbar_init(st_full, 1);
+        mbar_init(st_free, 8);
+        mbar_init(pd_full, 8);
+        mbar_init(pd_empty, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmqkv); prefetch_tmap(&tmdo); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tDP = tmem + BQ, tDV = tmem + 2 * BQ, tDK = tmem + 2 * BQ + HD;
+
+    if (warp == 0) {
+        // ---- producer: K and V once; per query tile Q and dO by TMA, lse and D by the warp's lanes
+        if (lane == 0) {
+            mbar_arrive_expect_tx(kv_full, 2 * TILE);
+            tma_load_2d(sK, &tmqkv, kv_full, p.hidden + head * HD, seg0 + k0);
+            tma_load_2d(sV, &tmqkv, kv_full, 2 * p.hidden + head * HD, seg0 + k0);
+        }
+        for (int j = 0; j < nq; ++j) {
+            const int s = j & 1;
+            int got = 1;
+            if (lane == 0) got = mbar_wait(empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err);
+            if (!__shfl_sync(0xffffffffu, got, 0)) break;
+            __syncwarp();
+            const int q0 = qb0 + j * BQ;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(full + s, 2 * TILE);
+                tma_load_2d(sQO + s * 2 * TILE, &tmqkv, full + s, head * HD, seg0 + q0);
+                tma_load_2d(sQO + s * 2 * TILE + TILE, &tmdo, full + s, head * HD, seg0 + q0);
+            }
+            float* rows = sRow + s * 2 * BQ;
+#pragma unroll
+            for (int i = 0; i < BQ / 32; ++i) {
+                const int r = lane + 32 * i;
+                const bool in = q0 + r < qe;
+                const size_t at = static_cast<size_t>(seg0 + (in ? q0 + r : 0)) * p.heads + head;
+                rows[r] = in ? __ldg(p.lse + at) : 0.f;
+                rows[BQ + r] = in ? __ldg(p.dsum + at) : 0.f;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full + s);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer: Sᵀ/dPᵀ of tile j are issued before dV/dK of tile j − 1
+        if (lane == 0) {
+            bool ok = mbar_wait(kv_full, 0, abort_flag, p.err);
+            tc_fence_after();
+            const uint32_t ak = smem_u32(sK), av = smem_u32(sV);
+            for (int j = 0; j <= nq && ok; ++j) {
+                if (j < nq) {
+                    const int s = j & 1;
+                    if (!mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err)) break;
+                    if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t aq = smem_u32(sQO + s * 2 * TILE), ado = aq + TILE;
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        mma_f16(tS, smem_desc_sw128(ak + kk * 32), smem_desc_sw128(aq + kk * 32), IDESC_S, kk > 0);
+                        mma_f16(tDP, smem_desc_sw128(av + kk * 32), smem_desc_sw128(ado + kk * 32), IDESC_S, kk > 0);
+                    }
+                    mma_commit(st_full);
+                }
+                if (j >= 1) {
+                    const int i = j - 1, s = i & 1;
+                    if (!mbar_wait(pd_full, i & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t aq = smem_u32(sQO + s * 2 * TILE), ado = aq + TILE;
+                    const uint32_t ap = smem_u32(sP), ad = smem_u32(sDS);
+#pragma unroll
+                    for (int kk = 0; kk < BQ / 16; ++kk) {
+                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                        mma_f16(tDV, smem_desc_sw128(ap + po), desc_mn_sw128(ado + kk * 2048, TILE), IDESC_G, acc);
+                        mma_f16(tDK, smem_desc_sw128(ad + po), desc_mn_sw128(aq + kk * 2048, TILE), IDESC_G, acc);
+                    }
+                    mma_commit(empty + s);
+                    mma_commit(pd_empty);
+                }
+            }
+        }
+    } else {
+        // ---- softmax warps: thread (half, row) owns key row `row` and queries [64·half, 64·half + 64) of a tile
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int key = k0 + row;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        constexpr int HQ = BQ / 2;
+        const float sl2 = p.scale * LOG2E;
+        bool ok = true;
+        for (int j = 0; j < nq; ++j) {
+            const int s = j & 1;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err) &&
+                                             mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err));
+            // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
+            if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+            if (ok) tc_fence_after();
+            const float* rows = sRow + s * 2 * BQ;
+            const int q0 = qb0 + j * BQ + half * HQ;
+            uint8_t* prow = sP + half * TILE + row * 128;
+            uint8_t* drow = sDS + half * TILE + row * 128;
+            // two 32-query chunks: the second chunk's TMEM reads release the score buffers to the next tile's MMAs
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t sv[32], dv[32];
+                if (ok) {
+                    tmem_ld32(tS + lane_off + half * HQ + c * 32, sv);
+                    tmem_ld32(tDP + lane_off + half * HQ + c * 32, dv);
+                    tmem_ld_wait();
+                }
+                if (c == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(st_free);
+                }
+                if (!ok) continue;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int qi = half * HQ + c * 32 + e, q = q0 + c * 32 + e;
+                    const float lse = rows[qi], dd = rows[BQ + qi];
+                    const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
+                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
+                    const float m = DROP ? drop_mult_b(p, head, seg0 + q, key) : 1.0f;
+                    sv[e] = __float_as_uint(pe * m);
+                    dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                    const float* g = reinterpret_cast<const float*>(dv + 8 * u);
+                    const int off = ((c * 4 + u) ^ (row & 7)) << 4;
+                    *reinterpret_cast<uint4*>(prow + off) =
+                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                    *reinterpret_cast<uint4*>(drow + off) =
+                        make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
+                }
+            }
+            if (!ok) continue;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pd_full);
+        }
+        // dK (half 0, rotated back by −θ) and dV (half 1) once the last dV/dK MMAs are done
+        ok = __all_sync(0xffffffffu, ok && nq > 0 && mbar_wait(pd_empty, (nq - 1) & 1, abort_flag, p.err));
+        if (ok) {
+            tc_fence_after();
+            uint32_t a[HD];
+            const uint32_t src = (half == 0 ? tDK : tDV) + lane_off;
+            tmem_ld32(src, *reinterpret_cast<uint32_t(*)[32]>(a));
+            tmem_ld32(src + 32, *reinterpret_cast<uint32_t(*)[32]>(a + 32));
+            tmem_ld_wait();
+            if (key < L) {
+                float f[HD];
+#pragma unroll
+                for (int e = 0; e < HD; ++e) f[e] = __uint_as_float(a[e]);
+                if (half == 0 && p.cosv) {
+#pragma unroll
+                    for (int i = 0; i < HD / 2; ++i) {
+                        const float c = p.cosv[static_cast<size_t>(key) * (HD / 2) + i];
+                        const float sn = p.sinv[static_cast<size_t>(key) * (HD / 2) + i];
+                        const float x = f[i], y = f[i + HD / 2];
+                        f[i] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+                        f[i + HD / 2] = __fsub_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+                    }
+                }
+                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + key) * p.lddq + (half == 0 ? p.hidden : 2 * p.hidden) + head * HD;
+#pragma unroll
+                for (int t = 0; t < HD / 8; ++t)
+                    *reinterpret_cast<uint4*>(out + 8 * t) =
+                        make_uint4(pack2(f[8 * t], f[8 * t + 1]), pack2(f[8 * t + 2], f[8 * t + 3]),
+                                   pack2(f[8 * t + 4], f[8 * t + 5]), pack2(f[8 * t + 6], f[8 * t + 7]));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 }  // namespace fat
 
 template <bool SPLIT, bool DROP>
@@ -399,6 +659,44 @@ int flash_forward_tc(const fa::Args& a, cudaStream_t s) {
     const bool drop = a.dropout > 0.f;
     if (a.qkv_lo) return drop ? launch_tc<true, true>(a, s) : launch_tc<true, false>(a, s);
     return drop ? launch_tc<false, true>(a, s) : launch_tc<false, false>(a, s);
+}
+
+template <bool DROP>
+static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
+    CUtensorMap tq, tdo;
+    int rc = make_tmap_2d(&tq, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                          static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
+                               static_cast<uint64_t>(a.ldo) * 2, fat::BK, fat::HD, true);
+    if (rc) return rc;
+    static bool attr[64] = {false};
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        LAYA_CUDA(cudaFuncSetAttribute(fat::bwd_dkdv_tc_kernel<DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fat::BWD_SMEM));
+        attr[dev] = true;
+    }
+    fat::BwdParams p{};
+    p.seg_start = a.seg_start; p.seg_len = a.seg_len;
+    p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
+    p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
+    p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
+    p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
+    p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
+    fat::bwd_dkdv_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::BWD_SMEM, s>>>(tq, tdo, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// dK and dV by the tcgen05 kernel for head_dim 64 (ERR_NOT_SUPPORTED for shapes it does not take).
+int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s) {
+    if (a.hidden / a.heads != fat::HD || !a.tq_item || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
+    if ((a.ld & 7) || (a.ldo & 7) || (a.lddq & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15))
+        return ERR_NOT_SUPPORTED;
+    return a.dropout > 0.f ? launch_bwd_tc<true>(a, s) : launch_bwd_tc<false>(a, s);
 }
 
 }  // namespace laya
