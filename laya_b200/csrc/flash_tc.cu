@@ -31,6 +31,7 @@ namespace fat {
 constexpr int BQ = 128, BK = 128, HD = 64;
 constexpr int TILE = 128 * 128;   // bytes of one 128-row × 64-column bf16 tile
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_GAP = 8.0f;   // e^8 ≈ 2981: the largest probability before the running max is raised
 
 template <bool SPLIT>
 struct Cfg {
@@ -92,16 +93,34 @@ DEVI float ex2(float x) {
 }
 DEVI void named_bar_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
 
-// Ops.Uniform (Ops.cs:227-234) at (head << 42) | (row << 21) | key.
-DEVI float drop_mult(const Params& p, int head, int row, int key) {
-    if (p.dropout <= 0.0f) return 1.0f;
-    const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
-    uint64_t z = p.seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    z ^= z >> 31;
-    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f) < p.dropout ? 0.0f : p.keep;
-}
+// Ops.Uniform (Ops.cs:227-234) at (head << 42) | (row << 21) | key, the dropout mask's counter hash.
+// The same hash walked along consecutive indices: the first step's z = seed + (idx + 1)·φ advances by a fixed
+// multiple of φ per element (one key, or one row = 2^21 indices), and only bits 40..63 of the final value are used —
+// those equal bits 40..63 of the last product (the final xor-shift by 31 cannot reach them), so the last multiply
+// keeps only its high word.  u < dropout is compared as the integer bits < ceil(dropout · 2^24): the same test.
+struct DropWalk {
+    uint64_t z, step;
+    uint32_t thr;
+    float keep;
+    DEVI DropWalk(uint64_t seed, int head, int row, int key, uint64_t stride, float dropout, float keep_) {
+        const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
+        z = seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
+        step = stride * 0x9E3779B97F4A7C15ull;
+        thr = static_cast<uint32_t>(ceilf(dropout * 16777216.0f));
+        keep = keep_;
+    }
+    // the multiplier of the current index, then advance to the next
+    DEVI float next() {
+        uint64_t x = z ^ (z >> 30);
+        z += step;
+        x *= 0xBF58476D1CE4E5B9ull;
+        x ^= x >> 27;
+        const uint32_t lo = static_cast<uint32_t>(x), hi = static_cast<uint32_t>(x >> 32);
+        const uint32_t c_lo = 0x133111EBu, c_hi = 0x94D049BBu;   // 0x94D049BB133111EB
+        const uint32_t top = __umulhi(lo, c_lo) + lo * c_hi + hi * c_lo;
+        return (top >> 8) < thr ? 0.0f : keep;
+    }
+};
 
 template <bool SPLIT, bool DROP>
 __global__ void __launch_bounds__(320, 1)
@@ -268,11 +287,27 @@ __global__ void __launch_bounds__(320, 1)
             const float mx = fmaxf(red[row], red[BQ + row]);
             named_bar_sync(1, 256);
             if (!ok) continue;
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = m_run == -INFINITY ? 0.f : ex2(__fmul_rn(m_run - m_new, LOG2E));
+            // Lazy rescaling: the running max moves only when the tile's max exceeds it by more than RESCALE_GAP
+            // (natural log units), so probabilities stay below e^RESCALE_GAP and O is rescaled in TMEM rarely.  The
+            // result is the same softmax: every P of a row and its sum l use the same reference max.
+            const bool grow = mx > m_run + RESCALE_GAP;
+            const float m_new = grow ? mx : m_run;
+            const float alpha = (m_run == -INFINITY || !grow) ? (m_run == -INFINITY ? 0.f : 1.0f)
+                                                               : ex2(__fmul_rn(m_run - m_new, LOG2E));
             const float msc = m_new == -INFINITY ? 0.f : m_new * LOG2E;
+            // P = exp(s - m); the row sum counts every probability, dropped or not
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+            DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
+#pragma unroll
+            for (int e = 0; e < HK; ++e) {
+                float pe = ex2(fmaf(__uint_as_float(v[e]), LOG2E, -msc));   // 2^-inf = 0 for masked keys
+                rs4[e & 3] += pe;
+                if constexpr (DROP) pe = pe * walk.next();
+                v[e] = __float_as_uint(pe);
+            }
             // O may be rescaled only once P·V of the previous tile is done; the P buffer of this tile may be
-            // rewritten once the P·V that last read it (tile j - NPB) is done
+            // rewritten once the P·V that last read it (tile j - NPB) is done.  Waiting here, after the
+            // exponentials, lets them overlap that P·V.
             const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
             if (rescale || j >= C::NPB) {
                 const int i = rescale ? j - 1 : j - C::NPB;
@@ -288,15 +323,6 @@ __global__ void __launch_bounds__(320, 1)
                     tmem_st32(tO + lane_off + half * HO, o);
                     tmem_st_wait();
                 }
-            }
-            // P = exp(s - m); the row sum counts every probability, dropped or not
-            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int e = 0; e < HK; ++e) {
-                float pe = ex2(fmaf(__uint_as_float(v[e]), LOG2E, -msc));   // 2^-inf = 0 for masked keys
-                rs4[e & 3] += pe;
-                if constexpr (DROP) pe = pe == 0.f ? 0.f : pe * drop_mult(p, head, seg0 + q, k0 + e);
-                v[e] = __float_as_uint(pe);
             }
             // this half's 64 keys are sub-tile `half` of P buffer j % NPB: 16-byte chunk c of row `row`, swizzled by
             // row % 8
@@ -380,16 +406,6 @@ struct BwdParams {
     int* err;
 };
 constexpr int BWD_SMEM = 1024 + 10 * TILE + 2 * 2 * BQ * 4 + 256;   // K, V, 2 × (Q, dO), Pᵀ (2), dSᵀ (2); lse/D
-
-DEVI float drop_mult_b(const BwdParams& p, int head, int row, int key) {
-    if (p.dropout <= 0.0f) return 1.0f;
-    const uint64_t idx = (static_cast<uint64_t>(head) << 42) | (static_cast<uint64_t>(row) << 21) | static_cast<uint32_t>(key);
-    uint64_t z = p.seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    z ^= z >> 31;
-    return static_cast<float>(z >> 40) * (1.0f / 16777216.0f) < p.dropout ? 0.0f : p.keep;
-}
 
 static_assert(BWD_SMEM <= 232448, "shared memory budget");
 
@@ -528,8 +544,6 @@ __global__ void __launch_bounds__(320, 1)
             const int s = j & 1;
             ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err) &&
                                              mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err));
-            // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
-            if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
             if (ok) tc_fence_after();
             const float* rows = sRow + s * 2 * BQ;
             const int q0 = qb0 + j * BQ + half * HQ;
@@ -550,15 +564,22 @@ __global__ void __launch_bounds__(320, 1)
                     if (lane == 0) mbar_arrive(st_free);
                 }
                 if (!ok) continue;
+                fat::DropWalk walk(p.seed, head, seg0 + q0 + c * 32, key, 1ull << 21, p.dropout, p.keep);
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
                     const int qi = half * HQ + c * 32 + e, q = q0 + c * 32 + e;
                     const float lse = rows[qi], dd = rows[BQ + qi];
                     const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
                     const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
-                    const float m = DROP ? drop_mult_b(p, head, seg0 + q, key) : 1.0f;
+                    const float m = DROP ? walk.next() : 1.0f;
                     sv[e] = __float_as_uint(pe * m);
                     dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                }
+                // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten;
+                // waiting only now lets the first chunk's exponentials overlap those MMAs
+                if (c == 0 && j > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+                    if (!ok) continue;
                 }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
