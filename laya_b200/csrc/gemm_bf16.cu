@@ -344,9 +344,9 @@ int gemm(const Args& a, cudaStream_t stream) {
         }
     } else {
         switch (a.epi) {
-            case EPI_BF16: return dispatch_major<256, 3, EPI_BF16>(a, stream);
-            case EPI_F32: return dispatch_major<256, 3, EPI_F32>(a, stream);
-            case EPI_F32_ADD: return dispatch_major<256, 3, EPI_F32_ADD>(a, stream);
+            case EPI_BF16: return dispatch_major<256, 4, EPI_BF16>(a, stream);
+            case EPI_F32: return dispatch_major<256, 4, EPI_F32>(a, stream);
+            case EPI_F32_ADD: return dispatch_major<256, 4, EPI_F32_ADD>(a, stream);
         }
     }
     set_error("unknown bf16 product epilogue");
