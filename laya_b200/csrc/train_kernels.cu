@@ -444,10 +444,22 @@ __global__ void scorer_bwd_kernel(const float* __restrict__ pre, const float* __
 
 // ------------------------------------------------------------------------------------------------ optimizer
 // Σ g² over [0, n) in double, per CTA partials reduced with atomics (Gradients.ClipByGlobalNorm sums in double).
-__global__ void sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ out) {
-    double s = 0.0;
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
-        s += static_cast<double>(g[i]) * g[i];
+__global__ void __launch_bounds__(256) sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ out) {
+    // four independent fp64 accumulators over 16-byte loads keep enough loads in flight to stream at HBM rate
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    const size_t n4 = reinterpret_cast<uintptr_t>(g) & 15 ? 0 : n / 4;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = g4[i];
+        s0 = fma(static_cast<double>(v.x), static_cast<double>(v.x), s0);
+        s1 = fma(static_cast<double>(v.y), static_cast<double>(v.y), s1);
+        s2 = fma(static_cast<double>(v.z), static_cast<double>(v.z), s2);
+        s3 = fma(static_cast<double>(v.w), static_cast<double>(v.w), s3);
+    }
+    for (size_t i = 4 * n4 + static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        s0 = fma(static_cast<double>(g[i]), static_cast<double>(g[i]), s0);
+    double s = (s0 + s1) + (s2 + s3);
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     __shared__ double ws[32];
     if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
@@ -757,7 +769,7 @@ int rlcd(const tr::RlcdArgs& a, cudaStream_t s) {
 }
 int sumsq(const float* g, size_t n, double* out, cudaStream_t s) {
     if (n == 0) return OK;
-    tr::sumsq_kernel<<<296, 256, 0, s>>>(g, n, out);
+    tr::sumsq_kernel<<<148 * 8, 256, 0, s>>>(g, n, out);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
