@@ -91,7 +91,39 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, int T, int n, int 
 
 // ------------------------------------------------------------------------------------------------ DeltaNet
 // conv[t, c] = silu(Σ_j w[j, c] · in[t − (K−1) + j, c]) over taps inside t's sequence (zero history before it).
-__global__ void conv_silu_kernel(ConvArgs a) {
+// Thread = one channel over a run of CONV_RUN consecutive tokens: each input is read once (coalesced across
+// channels) and the last K−1 inputs ride along in registers; taps before the token's sequence start count as zero.
+constexpr int CONV_RUN = 32;
+template <int K>
+__global__ void __launch_bounds__(256) conv_silu_kernel(ConvArgs a) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int t0 = blockIdx.y * CONV_RUN;
+    if (c >= a.cd) return;
+    const int t1 = min(a.T, t0 + CONV_RUN);
+    float w[K], h[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) w[j] = a.w[static_cast<size_t>(j) * a.cd + c];
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {   // h[j] = in[t0 − (K−1) + j]; the mask below drops rows before a sequence start
+        const int src = t0 - (K - 1) + j;
+        h[j] = src >= 0 ? a.in[static_cast<size_t>(src) * a.ld_in + c] : 0.0f;
+    }
+    for (int t = t0; t < t1; ++t) {
+        h[K - 1] = a.in[static_cast<size_t>(t) * a.ld_in + c];
+        const int s0 = a.seq_start[a.tok_seq[t]];
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            const int src = t - (K - 1) + j;
+            sum = __fadd_rn(sum, __fmul_rn(w[j], src >= s0 ? h[j] : 0.0f));
+        }
+        a.out[static_cast<size_t>(t) * a.cd + c] = ref_silu(sum);
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) h[j] = h[j + 1];
+    }
+}
+// Any kernel size: one thread per (token, channel).
+__global__ void conv_silu_any_kernel(ConvArgs a) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(a.T) * a.cd) return;
     const int t = static_cast<int>(i / a.cd), c = static_cast<int>(i % a.cd);
@@ -541,7 +573,13 @@ int dec_embed(const int32_t* ids, int T, int n, int vocab, const q8::code_t* q, 
 }
 int dec_conv_silu(const dec::ConvArgs& a, cudaStream_t s) {
     if (a.T <= 0) return OK;
-    dec::conv_silu_kernel<<<nblk(static_cast<size_t>(a.T) * a.cd, 256), 256, 0, s>>>(a);
+    const dim3 grid((a.cd + 255) / 256, (a.T + dec::CONV_RUN - 1) / dec::CONV_RUN);
+    switch (a.K) {
+        case 2: dec::conv_silu_kernel<2><<<grid, 256, 0, s>>>(a); break;
+        case 3: dec::conv_silu_kernel<3><<<grid, 256, 0, s>>>(a); break;
+        case 4: dec::conv_silu_kernel<4><<<grid, 256, 0, s>>>(a); break;
+        default: dec::conv_silu_any_kernel<<<nblk(static_cast<size_t>(a.T) * a.cd, 256), 256, 0, s>>>(a); break;
+    }
     DEC_LAUNCHED();
 }
 int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s) {
