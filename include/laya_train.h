@@ -87,6 +87,14 @@ int laya_trainer_download_grad(laya_trainer* t, const char* name, float* host, i
 int laya_trainer_param_count(laya_trainer* t, int64_t* total, int64_t* trainable);
 /* Number of parameter tensors and the i-th one's name (for checkpoint loops). */
 int laya_trainer_param_info(laya_trainer* t, int index, const char** name, int64_t* rows, int64_t* cols);
+/* Checkpoints.  save: TrainableDecisionModel.Save's model.safetensors (TrainableDecisionModel.cs:649-661,
+ * SafetensorsWriter.cs:17-64) — every parameter by name in the dtype it was uploaded in (F32 / F16 / BF16, rounded to
+ * nearest even), written to path + ".tmp" then moved over path; with_optimizer != 0 adds AdamW's m and v
+ * ("optimizer.m.<name>", "optimizer.v.<name>", F32) and the step count ("__metadata__": "optimizer_step"), which the
+ * reference does not save.  restore: reads such a file (or the reference's): every parameter must be present with
+ * its shape; the optimizer state and step count come back when present and are reset otherwise. */
+int laya_trainer_save_checkpoint(laya_trainer* t, const char* path, int with_optimizer);
+int laya_trainer_restore_checkpoint(laya_trainer* t, const char* path);
 
 /* A batch resident on the device: TrainingItem token ids, question types, marker positions and soft targets,
  * plus the standard-normal draws of the objective ([groups][options] in item order, RlcdObjective.cs:57-66).

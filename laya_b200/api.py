@@ -127,6 +127,8 @@ _SIGS = {
     "laya_trainer_set_profiling": (_I, [_P, _I]),
     "laya_trainer_profile": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_trainer_save_checkpoint": (_I, [_P, ctypes.c_char_p, _I]),
+    "laya_trainer_restore_checkpoint": (_I, [_P, ctypes.c_char_p]),
     "laya_comm_unique_id": (_I, [_P]),
     "laya_train_comm_init": (_I, [_P, _P, _I, _I]),
     # include/laya_decoder.h
@@ -580,6 +582,13 @@ class Trainer:
         out = np.zeros(shape, np.float32)
         check(lib().laya_trainer_download(self.handle, name.encode(), _np_ptr(out), out.size))
         return out
+
+    def save_checkpoint(self, path: str, with_optimizer: bool = True):
+        """TrainableDecisionModel.Save's model.safetensors (parameters in their uploaded dtypes), plus AdamW's state."""
+        check(lib().laya_trainer_save_checkpoint(self.handle, os.fsencode(path), 1 if with_optimizer else 0))
+
+    def restore_checkpoint(self, path: str):
+        check(lib().laya_trainer_restore_checkpoint(self.handle, os.fsencode(path)))
 
     def gradient(self, name: str, shape) -> np.ndarray:
         out = np.zeros(shape, np.float32)

@@ -32,6 +32,7 @@
 #include "../../include/laya_train.h"
 #include "common.cuh"
 #include "internal.h"
+#include "safetensors.h"
 #include "train.h"
 
 using bf16 = __nv_bfloat16;
@@ -63,6 +64,8 @@ struct Param {
     size_t off;
     int group;
     bool trainable;
+    std::vector<int64_t> shape;   // as uploaded (else [cols] for a single row, [rows, cols] otherwise)
+    int stored = LAYA_F32;        // the dtype it was uploaded in: what a checkpoint writes it back as
 };
 struct EncP { size_t n1, qkv, wo, n2, wi, wo2; };
 struct HeadP { size_t n1w, n1b, inw, inb, outw, outb, n2w, n2b, l1w, l1b, l2w, l2b; };
@@ -293,6 +296,7 @@ int collect_profile(laya_trainer* t) {
 // The parameters TrainableDecisionModel reads (TrainableDecisionModel.cs:111-178), in buffer order.
 void add_param(laya_trainer* t, const std::string& name, int64_t rows, int64_t cols, int group) {
     Param p{name, rows, cols, t->P, group, true};
+    p.shape = rows == 1 ? std::vector<int64_t>{cols} : std::vector<int64_t>{rows, cols};
     t->index[name] = static_cast<int>(t->params.size());
     t->params.push_back(p);
     const size_t n = static_cast<size_t>(rows) * cols;
@@ -951,6 +955,9 @@ int laya_trainer_upload(laya_trainer* t, const char* name, int dtype, const int6
     RC(f32_split_bf16(t->master + p->off, t->shadow + p->off, t->shadow_lo ? t->shadow_lo + p->off : nullptr,
                       static_cast<size_t>(n), t->stream));
     LAYA_CUDA(cudaStreamSynchronize(t->stream));
+    Param& q = t->params[t->index[name]];
+    q.shape.assign(shape, shape + rank);
+    q.stored = dtype;
     return OK;
 }
 
@@ -971,6 +978,155 @@ int laya_trainer_download(laya_trainer* t, const char* name, float* host, int64_
 int laya_trainer_download_grad(laya_trainer* t, const char* name, float* host, int64_t count) {
     if (!t) { set_error("null trainer"); return ERR_ARGUMENT; }
     return download_range(t, name, t->grad, host, count);
+}
+
+// ------------------------------------------------------------------------------------------------ checkpoints
+// TrainableDecisionModel.Save's model.safetensors (TrainableDecisionModel.cs:649-661 through SafetensorsWriter,
+// Base/Io/SafetensorsWriter.cs:17-64): every parameter under its name, in the dtype it was loaded in, written to
+// path + ".tmp" and moved over path.  With the optimizer: AdamW's m and v as F32 "optimizer.m.<name>" /
+// "optimizer.v.<name>" and the step count in the metadata, so that a restore resumes the same trajectory (state the
+// reference does not save).
+int laya_trainer_save_checkpoint(laya_trainer* t, const char* path, int with_optimizer) {
+    if (!t || !path) { set_error("null argument"); return ERR_ARGUMENT; }
+    DeviceGuard g(t->device);
+    if (t->comm.stream) LAYA_CUDA(cudaStreamSynchronize(t->comm.stream));
+    std::vector<float> master(t->P), m, v;
+    LAYA_CUDA(cudaMemcpyAsync(master.data(), t->master, sizeof(float) * t->P, cudaMemcpyDeviceToHost, t->stream));
+    if (with_optimizer) {
+        m.resize(t->P);
+        v.resize(t->P);
+        LAYA_CUDA(cudaMemcpyAsync(m.data(), t->m, sizeof(float) * t->P, cudaMemcpyDeviceToHost, t->stream));
+        LAYA_CUDA(cudaMemcpyAsync(v.data(), t->v, sizeof(float) * t->P, cudaMemcpyDeviceToHost, t->stream));
+    }
+    LAYA_CUDA(cudaStreamSynchronize(t->stream));
+    struct Out { std::string name, dtype; const std::vector<int64_t>* shape; const float* data; size_t n; };
+    std::vector<Out> outs;
+    for (const Param& p : t->params) {
+        const int st = p.stored;
+        outs.push_back({p.name, st == LAYA_BF16 ? "BF16" : st == LAYA_F16 ? "F16" : "F32", &p.shape,
+                        master.data() + p.off, static_cast<size_t>(p.rows * p.cols)});
+    }
+    if (with_optimizer)
+        for (const Param& p : t->params) {
+            outs.push_back({"optimizer.m." + p.name, "F32", &p.shape, m.data() + p.off, static_cast<size_t>(p.rows * p.cols)});
+            outs.push_back({"optimizer.v." + p.name, "F32", &p.shape, v.data() + p.off, static_cast<size_t>(p.rows * p.cols)});
+        }
+    std::string js = "{";
+    if (with_optimizer)
+        js += "\"__metadata__\":{\"format\":\"laya_b200\",\"optimizer_step\":\"" + std::to_string(t->steps) + "\"},";
+    uint64_t off = 0;
+    for (size_t i = 0; i < outs.size(); ++i) {
+        const uint64_t bytes = outs[i].n * st::elem_size(outs[i].dtype);
+        js += "\"" + st::escape(outs[i].name) + "\":{\"dtype\":\"" + outs[i].dtype + "\",\"shape\":[";
+        for (size_t k = 0; k < outs[i].shape->size(); ++k) js += (k ? "," : "") + std::to_string((*outs[i].shape)[k]);
+        js += "],\"data_offsets\":[" + std::to_string(off) + "," + std::to_string(off + bytes) + "]}";
+        js += i + 1 < outs.size() ? "," : "";
+        off += bytes;
+    }
+    js += "}";
+    while (js.size() % 8) js += ' ';
+    const std::string tmp = std::string(path) + ".tmp";
+    std::FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (!f) { set_error(std::string("cannot create ") + tmp); return ERR_ARGUMENT; }
+    unsigned char len[8];
+    for (int i = 0; i < 8; ++i) len[i] = static_cast<unsigned char>((static_cast<uint64_t>(js.size()) >> (8 * i)) & 0xFF);
+    bool ok = std::fwrite(len, 1, 8, f) == 8 && std::fwrite(js.data(), 1, js.size(), f) == js.size();
+    std::vector<uint16_t> half;
+    for (const Out& o : outs) {
+        if (!ok) break;
+        if (o.dtype == "F32") {
+            ok = std::fwrite(o.data, sizeof(float), o.n, f) == o.n;
+        } else {
+            half.resize(o.n);
+            for (size_t i = 0; i < o.n; ++i) {
+                if (o.dtype == "BF16") half[i] = st::to_bf16(o.data[i]);
+                else {
+                    const __half hv = __float2half_rn(o.data[i]);   // (Half)value: round to nearest even
+                    std::memcpy(&half[i], &hv, 2);
+                }
+            }
+            ok = std::fwrite(half.data(), 2, o.n, f) == o.n;
+        }
+    }
+    ok = (std::fclose(f) == 0) && ok;
+    if (!ok || std::rename(tmp.c_str(), path) != 0) {
+        std::remove(tmp.c_str());
+        set_error(std::string("cannot write ") + path);
+        return ERR_ARGUMENT;
+    }
+    return OK;
+}
+
+// Loads a checkpoint written by laya_trainer_save_checkpoint or by the reference's Save: every parameter must be
+// present with its shape (F32, F16 or BF16); AdamW's state and step count are restored when the file has them and
+// reset otherwise.  The bf16 copies the products read are rebuilt from the loaded masters.
+int laya_trainer_restore_checkpoint(laya_trainer* t, const char* path) {
+    if (!t || !path) { set_error("null argument"); return ERR_ARGUMENT; }
+    std::FILE* f = std::fopen(path, "rb");
+    if (!f) { set_error(std::string("cannot open ") + path); return ERR_NOT_FOUND; }
+    st::Header h;
+    std::string err;
+    if (!st::read_header(f, &h, &err)) { std::fclose(f); set_error(std::string(path) + ": " + err); return ERR_ARGUMENT; }
+    auto load = [&](const st::Entry& e, float* dst, size_t n, const std::string& name) -> int {
+        const int es = st::elem_size(e.dtype);
+        if (es == 0) { set_error(name + ": unsupported dtype " + e.dtype); return ERR_ARGUMENT; }
+        int64_t count = 1;
+        for (int64_t d : e.shape) count *= d;
+        if (static_cast<size_t>(count) != n || e.end - e.begin != n * static_cast<uint64_t>(es)) {
+            set_error(name + ": shape or size does not match the model");
+            return ERR_ARGUMENT;
+        }
+        std::vector<unsigned char> raw(e.end - e.begin);
+        if (std::fseek(f, static_cast<long>(h.data_start + e.begin), SEEK_SET) != 0 ||
+            std::fread(raw.data(), 1, raw.size(), f) != raw.size()) {
+            set_error(name + ": file shorter than its header says");
+            return ERR_ARGUMENT;
+        }
+        if (es == 4) std::memcpy(dst, raw.data(), raw.size());
+        else
+            for (size_t i = 0; i < n; ++i) {
+                uint16_t b;
+                std::memcpy(&b, raw.data() + 2 * i, 2);
+                if (e.dtype == "BF16") dst[i] = st::from_bf16(b);
+                else { __half hv; std::memcpy(&hv, &b, 2); dst[i] = __half2float(hv); }
+            }
+        return OK;
+    };
+    std::vector<float> master(t->P, 0.f), m, v;
+    bool have_opt = h.metadata.count("optimizer_step") > 0;
+    if (have_opt) { m.assign(t->P, 0.f); v.assign(t->P, 0.f); }
+    int rc = OK;
+    for (Param& p : t->params) {
+        const size_t n = static_cast<size_t>(p.rows * p.cols);
+        auto it = h.tensors.find(p.name);
+        if (it == h.tensors.end()) { set_error(std::string(path) + " has no tensor " + p.name); rc = ERR_NOT_FOUND; break; }
+        if ((rc = load(it->second, master.data() + p.off, n, p.name)) != OK) break;
+        p.stored = it->second.dtype == "BF16" ? LAYA_BF16 : it->second.dtype == "F16" ? LAYA_F16 : LAYA_F32;
+        p.shape = it->second.shape;
+        if (have_opt) {
+            auto im = h.tensors.find("optimizer.m." + p.name), iv = h.tensors.find("optimizer.v." + p.name);
+            if (im == h.tensors.end() || iv == h.tensors.end()) { set_error(std::string(path) + " lacks the optimizer state of " + p.name); rc = ERR_NOT_FOUND; break; }
+            if ((rc = load(im->second, m.data() + p.off, n, im->first)) != OK) break;
+            if ((rc = load(iv->second, v.data() + p.off, n, iv->first)) != OK) break;
+        }
+    }
+    std::fclose(f);
+    if (rc != OK) return rc;
+    DeviceGuard g(t->device);
+    if (t->comm.stream) LAYA_CUDA(cudaStreamSynchronize(t->comm.stream));
+    LAYA_CUDA(cudaMemcpyAsync(t->master, master.data(), sizeof(float) * t->P, cudaMemcpyHostToDevice, t->stream));
+    RC(f32_split_bf16(t->master, t->shadow, t->shadow_lo, t->P, t->stream));
+    if (have_opt) {
+        LAYA_CUDA(cudaMemcpyAsync(t->m, m.data(), sizeof(float) * t->P, cudaMemcpyHostToDevice, t->stream));
+        LAYA_CUDA(cudaMemcpyAsync(t->v, v.data(), sizeof(float) * t->P, cudaMemcpyHostToDevice, t->stream));
+        t->steps = std::strtoll(h.metadata["optimizer_step"].c_str(), nullptr, 10);
+    } else {
+        LAYA_CUDA(cudaMemsetAsync(t->m, 0, sizeof(float) * t->P, t->stream));
+        LAYA_CUDA(cudaMemsetAsync(t->v, 0, sizeof(float) * t->P, t->stream));
+        t->steps = 0;
+    }
+    LAYA_CUDA(cudaStreamSynchronize(t->stream));
+    return OK;
 }
 
 int laya_trainer_param_count(laya_trainer* t, int64_t* total, int64_t* trainable) {
