@@ -87,6 +87,28 @@ int laya_trainer_download_grad(laya_trainer* t, const char* name, float* host, i
 int laya_trainer_param_count(laya_trainer* t, int64_t* total, int64_t* trainable);
 /* Number of parameter tensors and the i-th one's name (for checkpoint loops). */
 int laya_trainer_param_info(laya_trainer* t, int index, const char** name, int64_t* rows, int64_t* cols);
+/* Temperature calibration.  laya_temperature_fit: TemperatureFit (TemperatureFitting.cs:10-11) — the per-type
+ * temperatures (choice, score, noul; 1.2 for a type without samples) and every "type:size" bucket
+ * (QuestionTypes.TemperatureBucket, Base/Questions.cs:38-42) in first-seen order with its sample count, fitted when it
+ * has at least min_bucket_samples; every temperature clamped to [0.5, 5] (Calibration.ClampTemperature).
+ *   laya_fit_temperatures: TemperatureFitting.Fit (:78-101) on host samples — per sample its question type, option
+ *       count, and that many logits and targets, concatenated.  No device work.
+ *   laya_train_calibrate: Trainer.Calibrate (Laya.Training/Trainer.cs:200-211) — forward-only passes (no dropout) of
+ *       the batches on the device, then the same fit on their option logits and the batches' targets. */
+#define LAYA_MAX_TEMPERATURE_BUCKETS 12
+typedef struct {
+    float by_type[3];
+    int n_buckets;
+    char bucket[LAYA_MAX_TEMPERATURE_BUCKETS][16];
+    int bucket_count[LAYA_MAX_TEMPERATURE_BUCKETS];
+    int bucket_fitted[LAYA_MAX_TEMPERATURE_BUCKETS];
+    float bucket_temperature[LAYA_MAX_TEMPERATURE_BUCKETS];
+} laya_temperature_fit;
+int laya_fit_temperatures(const int32_t* qtype, const int32_t* options, const float* logits, const float* targets,
+                          int n, int min_bucket_samples, laya_temperature_fit* fit);
+int laya_train_calibrate(laya_trainer* t, laya_batch* const* batches, int n_batches, int min_bucket_samples,
+                         laya_temperature_fit* fit);
+
 /* Checkpoints.  save: TrainableDecisionModel.Save's model.safetensors (TrainableDecisionModel.cs:649-661,
  * SafetensorsWriter.cs:17-64) — every parameter by name in the dtype it was uploaded in (F32 / F16 / BF16, rounded to
  * nearest even), written to path + ".tmp" then moved over path; with_optimizer != 0 adds AdamW's m and v

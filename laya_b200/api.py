@@ -127,6 +127,8 @@ _SIGS = {
     "laya_trainer_set_profiling": (_I, [_P, _I]),
     "laya_trainer_profile": (_I, [_P, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(ctypes.c_longlong)]),
+    "laya_fit_temperatures": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "laya_train_calibrate": (_I, [_P, _P, _I, _I, _P]),
     "laya_trainer_save_checkpoint": (_I, [_P, ctypes.c_char_p, _I]),
     "laya_trainer_restore_checkpoint": (_I, [_P, ctypes.c_char_p]),
     "laya_comm_unique_id": (_I, [_P]),
@@ -445,6 +447,36 @@ class DecisionModel:
 
 
 # --------------------------------------------------------------------------------------------------- training
+MAX_TEMPERATURE_BUCKETS = 12
+
+
+class TemperatureFitDesc(ctypes.Structure):
+    """laya_temperature_fit (include/laya_train.h): TemperatureFit (Laya.Training/TemperatureFitting.cs:10-11)."""
+    _fields_ = [("by_type", ctypes.c_float * 3), ("n_buckets", ctypes.c_int),
+                ("bucket", (ctypes.c_char * 16) * MAX_TEMPERATURE_BUCKETS),
+                ("bucket_count", ctypes.c_int * MAX_TEMPERATURE_BUCKETS),
+                ("bucket_fitted", ctypes.c_int * MAX_TEMPERATURE_BUCKETS),
+                ("bucket_temperature", ctypes.c_float * MAX_TEMPERATURE_BUCKETS)]
+
+    def result(self):
+        """(by_type [choice, score, noul], {bucket: temperature} of the fitted buckets, {bucket: samples})."""
+        names = [self.bucket[i].value.decode() for i in range(self.n_buckets)]
+        fitted = {n: float(self.bucket_temperature[i]) for i, n in enumerate(names) if self.bucket_fitted[i]}
+        return [float(v) for v in self.by_type], fitted, {n: int(self.bucket_count[i]) for i, n in enumerate(names)}
+
+
+def fit_temperatures(samples, minimum_bucket_samples: int = 30):
+    """TemperatureFitting.Fit on host samples [(question_type, logits, target)] through the C ABI."""
+    q = _i32([s[0] for s in samples])
+    k = _i32([len(s[1]) for s in samples])
+    z = _f32(np.concatenate([np.asarray(s[1], np.float32) for s in samples]) if samples else np.zeros(0))
+    t = _f32(np.concatenate([np.asarray(s[2], np.float32) for s in samples]) if samples else np.zeros(0))
+    out = TemperatureFitDesc()
+    check(lib().laya_fit_temperatures(_np_ptr(q), _np_ptr(k), _np_ptr(z), _np_ptr(t), len(samples),
+                                      minimum_bucket_samples, ctypes.byref(out)))
+    return out.result()
+
+
 class TrainDesc(ctypes.Structure):
     """laya_train_desc (include/laya_train.h): TrainerOptions + AdamW settings (Trainer.cs:16-58)."""
     _fields_ = [("trainable_encoder_layers", ctypes.c_int), ("head_dropout", ctypes.c_float),
@@ -582,6 +614,13 @@ class Trainer:
         out = np.zeros(shape, np.float32)
         check(lib().laya_trainer_download(self.handle, name.encode(), _np_ptr(out), out.size))
         return out
+
+    def calibrate(self, batches: Sequence["Batch"], minimum_bucket_samples: int = 30):
+        """Trainer.Calibrate: forward-only passes over the batches, then TemperatureFitting.Fit on their logits."""
+        arr = (ctypes.c_void_p * max(1, len(batches)))(*[b.handle for b in batches])
+        out = TemperatureFitDesc()
+        check(lib().laya_train_calibrate(self.handle, arr, len(batches), minimum_bucket_samples, ctypes.byref(out)))
+        return out.result()
 
     def save_checkpoint(self, path: str, with_optimizer: bool = True):
         """TrainableDecisionModel.Save's model.safetensors (parameters in their uploaded dtypes), plus AdamW's state."""

@@ -980,6 +980,128 @@ int laya_trainer_download_grad(laya_trainer* t, const char* name, float* host, i
     return download_range(t, name, t->grad, host, count);
 }
 
+// ------------------------------------------------------------------------------------------------ calibration
+namespace {
+struct CalSample {
+    int qtype;
+    const float* logits;
+    const float* target;
+    int k;
+};
+const char* kTypeNames[3] = {"choice", "score", "noul"};
+
+// TemperatureFitting.FitOne (TemperatureFitting.cs:36-72): the temperature minimising the mean soft cross-entropy,
+// golden-section search over log T in double, samples in order; fewer than 10 samples give 1.
+float fit_one(const std::vector<const CalSample*>& ss) {
+    if (ss.size() < 10) return 1.0f;
+    auto objective = [&](double log_t) {
+        const double t = std::exp(log_t);
+        double total = 0.0;
+        for (const CalSample* sp : ss) {
+            double mx = -INFINITY;
+            for (int i = 0; i < sp->k; ++i) mx = std::max(mx, sp->logits[i] / t);
+            double sum = 0.0;
+            for (int i = 0; i < sp->k; ++i) sum += std::exp(sp->logits[i] / t - mx);
+            const double log_sum = mx + std::log(sum);
+            for (int i = 0; i < sp->k; ++i) total -= sp->target[i] * (sp->logits[i] / t - log_sum);
+        }
+        return total / static_cast<double>(ss.size());
+    };
+    double low = std::log(0.02), high = std::log(50.0);
+    const double ratio = (std::sqrt(5.0) - 1) / 2;
+    double a = high - ratio * (high - low), b = low + ratio * (high - low);
+    double fa = objective(a), fb = objective(b);
+    for (int it = 0; it < 80 && high - low > 1e-7; ++it) {
+        if (fa < fb) {
+            high = b; b = a; fb = fa;
+            a = high - ratio * (high - low);
+            fa = objective(a);
+        } else {
+            low = a; a = b; fa = fb;
+            b = low + ratio * (high - low);
+            fb = objective(b);
+        }
+    }
+    return static_cast<float>(std::exp((low + high) / 2));
+}
+// Calibration.ClampTemperature (Laya/Runtime/Calibration.cs:23-24).
+float clamp_temperature(float t) { return std::isfinite(t) ? std::min(std::max(t, 0.5f), 5.0f) : 1.0f; }
+
+// TemperatureFitting.Fit (TemperatureFitting.cs:78-101).
+int fit_temperatures(const std::vector<CalSample>& samples, int min_bucket, laya_temperature_fit* out) {
+    std::memset(out, 0, sizeof *out);
+    for (int q = 0; q < 3; ++q) {
+        std::vector<const CalSample*> sel;
+        for (const CalSample& sp : samples)
+            if (sp.qtype == q) sel.push_back(&sp);
+        out->by_type[q] = sel.empty() ? 1.2f : clamp_temperature(fit_one(sel));
+    }
+    std::vector<std::string> keys;
+    std::vector<std::vector<const CalSample*>> groups;
+    for (const CalSample& sp : samples) {
+        const int k = sp.k;
+        const std::string key = std::string(kTypeNames[sp.qtype == 0 ? 0 : sp.qtype == 1 ? 1 : 2]) + ":" +
+                                (k <= 2 ? "2" : k <= 5 ? "3-5" : k <= 10 ? "6-10" : "11+");
+        size_t g = 0;
+        while (g < keys.size() && keys[g] != key) ++g;
+        if (g == keys.size()) {
+            if (keys.size() == LAYA_MAX_TEMPERATURE_BUCKETS) { set_error("more temperature buckets than the fit holds"); return ERR_ARGUMENT; }
+            keys.push_back(key);
+            groups.emplace_back();
+        }
+        groups[g].push_back(&sp);
+    }
+    out->n_buckets = static_cast<int>(keys.size());
+    for (size_t g = 0; g < keys.size(); ++g) {
+        std::snprintf(out->bucket[g], sizeof out->bucket[g], "%s", keys[g].c_str());
+        out->bucket_count[g] = static_cast<int>(groups[g].size());
+        out->bucket_fitted[g] = static_cast<int>(groups[g].size()) >= min_bucket;
+        out->bucket_temperature[g] = out->bucket_fitted[g] ? clamp_temperature(fit_one(groups[g])) : 1.0f;
+    }
+    return OK;
+}
+}  // namespace
+
+int laya_fit_temperatures(const int32_t* qtype, const int32_t* options, const float* logits, const float* targets,
+                          int n, int min_bucket_samples, laya_temperature_fit* out) {
+    if (!out || n < 0 || (n > 0 && (!qtype || !options || !logits || !targets))) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    std::vector<CalSample> samples;
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        if (options[i] <= 0) { set_error("every sample needs at least one option"); return ERR_ARGUMENT; }
+        samples.push_back({qtype[i], logits + off, targets + off, options[i]});
+        off += static_cast<size_t>(options[i]);
+    }
+    return fit_temperatures(samples, min_bucket_samples, out);
+}
+
+// Trainer.Calibrate (Laya.Training/Trainer.cs:200-211): forward-only passes (no dropout) over the calibration
+// batches on the device, then TemperatureFitting.Fit on their option logits and soft targets.
+int laya_train_calibrate(laya_trainer* t, laya_batch* const* batches, int n_batches, int min_bucket_samples,
+                         laya_temperature_fit* out) {
+    if (!t || !out || n_batches < 0 || (n_batches > 0 && !batches)) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    std::vector<std::vector<float>> logits(n_batches), targets(n_batches);
+    std::vector<CalSample> samples;
+    for (int bi = 0; bi < n_batches; ++bi) {
+        laya_batch* b = batches[bi];
+        if (!b || b->owner != t) { set_error("batch does not belong to this trainer"); return ERR_ARGUMENT; }
+        logits[bi].resize(std::max(b->M, 1));
+        RC(laya_train_forward(t, b, 0, 0, logits[bi].data()));
+        // the batch's staged host copy holds its question types, option counts and targets
+        const char* h = static_cast<const char*>(b->host);
+        const int32_t* qt = reinterpret_cast<const int32_t*>(h + b->o_qtype);
+        const int32_t* mc = reinterpret_cast<const int32_t*>(h + b->o_mk_count);
+        const float* tg = reinterpret_cast<const float*>(h + b->o_targets);
+        targets[bi].assign(tg, tg + b->M);
+        size_t off = 0;
+        for (int i = 0; i < b->n; ++i) {
+            samples.push_back({qt[i], logits[bi].data() + off, targets[bi].data() + off, mc[i]});
+            off += static_cast<size_t>(mc[i]);
+        }
+    }
+    return fit_temperatures(samples, min_bucket_samples, out);
+}
+
 // ------------------------------------------------------------------------------------------------ checkpoints
 // TrainableDecisionModel.Save's model.safetensors (TrainableDecisionModel.cs:649-661 through SafetensorsWriter,
 // Base/Io/SafetensorsWriter.cs:17-64): every parameter under its name, in the dtype it was loaded in, written to

@@ -312,3 +312,73 @@ def clip_by_global_norm(grads: List[np.ndarray], max_norm: float) -> float:
         for g in grads:
             g *= np.float32(coef)
     return norm
+
+
+# ---------------------------------------------------------------------------------------------- calibration
+TYPE_NAMES = ("choice", "score", "noul")
+
+
+def temperature_bucket(qtype: int, options: int) -> str:
+    """QuestionTypes.TemperatureBucket (Base/Questions.cs:38-42)."""
+    size = "2" if options <= 2 else "3-5" if options <= 5 else "6-10" if options <= 10 else "11+"
+    return TYPE_NAMES[qtype if qtype in (0, 1) else 2] + ":" + size
+
+
+def clamp_temperature(t: float, lo: float = 0.5, hi: float = 5.0) -> float:
+    """Calibration.ClampTemperature (Laya/Runtime/Calibration.cs:23-24), in fp32."""
+    t = np.float32(t)
+    return float(np.clip(t, np.float32(lo), np.float32(hi))) if math.isfinite(t) else 1.0
+
+
+def fit_one(samples) -> float:
+    """TemperatureFitting.FitOne (TemperatureFitting.cs:36-72): golden-section search over log T of the mean soft
+    cross-entropy, in double, samples in order; fewer than 10 samples give 1."""
+    if len(samples) < 10:
+        return 1.0
+
+    def objective(log_t):
+        t = math.exp(log_t)
+        total = 0.0
+        for _, logits, target in samples:
+            z = [float(v) / t for v in logits]
+            mx = -math.inf
+            for v in z:
+                mx = max(mx, v)
+            s = 0.0
+            for v in z:
+                s += math.exp(v - mx)
+            log_sum = mx + math.log(s)
+            for v, tg in zip(z, target):
+                total -= float(tg) * (v - log_sum)
+        return total / len(samples)
+
+    low, high = math.log(0.02), math.log(50)
+    ratio = (math.sqrt(5) - 1) / 2
+    a, b = high - ratio * (high - low), low + ratio * (high - low)
+    fa, fb = objective(a), objective(b)
+    it = 0
+    while it < 80 and high - low > 1e-7:
+        if fa < fb:
+            high, b, fb = b, a, fa
+            a = high - ratio * (high - low)
+            fa = objective(a)
+        else:
+            low, a, fa = a, b, fb
+            b = low + ratio * (high - low)
+            fb = objective(b)
+        it += 1
+    return float(np.float32(math.exp((low + high) / 2)))
+
+
+def fit_temperatures(samples, minimum_bucket_samples=30):
+    """TemperatureFitting.Fit (TemperatureFitting.cs:78-101): samples are (qtype, logits, target); returns
+    (by_type[3], {bucket: temperature} for buckets with enough samples, {bucket: count} in first-seen order)."""
+    by_type = []
+    for q in range(3):
+        sel = [s for s in samples if s[0] == q]
+        by_type.append(1.2 if not sel else clamp_temperature(fit_one(sel)))
+    groups = {}
+    for s in samples:
+        groups.setdefault(temperature_bucket(s[0], len(s[1])), []).append(s)
+    by_bucket = {k: clamp_temperature(fit_one(v)) for k, v in groups.items() if len(v) >= minimum_bucket_samples}
+    return by_type, by_bucket, {k: len(v) for k, v in groups.items()}

@@ -92,3 +92,26 @@ def test_decoder_invalid_geometry_is_an_argument_error():
         laya_b200.Qwen35Model(laya_b200.decoder_desc(["linear"], lin_v_heads=3, lin_k_heads=2))
     with pytest.raises(laya_b200.LayaArgumentError):
         laya_b200.Qwen35Model(laya_b200.decoder_desc(["full"], head_dim=96))
+
+
+def test_temperature_fit_through_the_abi_is_the_oracle():
+    """laya_fit_temperatures (TemperatureFitting.Fit) is host code: on CPU it equals the oracle restatement bit for
+    bit and recovers the reference's known temperature (TrainingTests.cs:84-105)."""
+    import numpy as np
+    import laya_b200
+    from oracle.train import fit_temperatures, softmax_f32
+    rng = np.random.default_rng(7)
+    samples = []
+    for i in range(420):
+        k = [2, 4, 7, 12][i % 4]
+        q = [0, 1, 2][i % 3] if i < 400 else 0
+        z = (rng.random(k) * 8 - 4).astype(np.float32)
+        samples.append((q, z, softmax_f32(z / np.float32(2))))
+    got = laya_b200.fit_temperatures(samples, 30)
+    want = fit_temperatures(samples, 30)
+    assert [np.float32(v) for v in got[0]] == [np.float32(v) for v in want[0]]
+    assert {k: np.float32(v) for k, v in got[1].items()} == {k: np.float32(v) for k, v in want[1].items()}
+    assert got[2] == want[2]
+    one = [s for s in samples if s[0] == 0 and len(s[1]) == 4][:200]
+    t, b, c = laya_b200.fit_temperatures(one, 30)
+    assert abs(t[0] - 2.0) < 1e-3 and abs(t[2] - 1.2) < 1e-6 and abs(b["choice:3-5"] - 2.0) < 1e-3

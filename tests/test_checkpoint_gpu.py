@@ -144,3 +144,28 @@ def test_restore_errors(cuda, tmp_path):
     with pytest.raises(laya_b200.LayaNotFoundError):
         t.restore_checkpoint(str(tmp_path / "partial.safetensors"))
     t.close()
+
+
+def test_calibrate_is_the_fit_of_the_device_logits(cuda):
+    """Trainer.Calibrate (Laya.Training/Trainer.cs:200-211) on the device: forward-only passes over batches of 16,
+    then TemperatureFitting.Fit — equal, bit for bit, to the oracle's fit of the same batches' logits and targets."""
+    import laya_b200
+    from laya_b200 import workloads
+    from oracle.train import fit_temperatures
+    cfg, w, g = tiny()
+    t = make(cfg, w)
+    batches, samples = [], []
+    for i in range(3):
+        items, _ = workloads.training_batch(rows=16, min_len=8, max_len=15, vocab=cfg.vocab, seed=60 + i)
+        b = t.batch(items)
+        batches.append(b)
+        for it, z in zip(items, t.forward(b, training=False)):
+            samples.append((it.question_type, z, it.target))
+    got = t.calibrate(batches, minimum_bucket_samples=5)
+    want = fit_temperatures(samples, 5)
+    assert [np.float32(v) for v in got[0]] == [np.float32(v) for v in want[0]]
+    assert {k: np.float32(v) for k, v in got[1].items()} == {k: np.float32(v) for k, v in want[1].items()}
+    assert got[2] == want[2] and sum(got[2].values()) == 48
+    for b in batches:
+        b.close()
+    t.close()

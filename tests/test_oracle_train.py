@@ -89,3 +89,19 @@ def test_dropout_hash_is_deterministic_and_fair():
     assert np.array_equal(uniform(1234, np.arange(10, dtype=np.uint64)), u[:10])
     m = dropout_mask(100000, 0.1, mix(7, 3))
     assert abs((m == 0).mean() - 0.1) < 0.01
+
+
+def test_temperature_fitting_recovers_a_known_temperature():
+    """TrainingTests.TemperatureFittingRecoversAKnownTemperature (TrainingTests.cs:84-105): targets drawn from
+    softmax(z / 2) are best explained by T = 2; five samples are too few (1); a type without samples gets 1.2."""
+    from oracle.train import fit_one, fit_temperatures, softmax_f32
+    rng = np.random.default_rng(5)
+    samples = []
+    for _ in range(400):
+        z = (rng.random(4) * 8 - 4).astype(np.float32)
+        samples.append((0, z, softmax_f32(z / np.float32(2))))
+    assert abs(fit_one(samples) - 2.0) < 1e-3
+    assert fit_one(samples[:5]) == 1.0
+    by_type, by_bucket, counts = fit_temperatures(samples, 30)
+    assert abs(by_type[0] - 2.0) < 1e-3 and by_type[2] == np.float32(1.2)
+    assert abs(by_bucket["choice:3-5"] - 2.0) < 1e-3 and counts == {"choice:3-5": 400}
