@@ -16,7 +16,9 @@ GPU, sharded by request with no collective.
 
 Nested `mica_prefill` (config 5): the Mica hybrid decoder (32 Qwen3.5 layers, [DeltaNet ×3, full] ×8, h 2560) with
 every projection and the tied token table in Q8_0, a prefill of 8 rows × 2048 token ids per GPU and the logits of 26
-label ids at each row's last position; replicas sharded by request with no collective.
+label ids at each row's last position; replicas sharded by request with no collective.  Beside it,
+`mica_shared_prefix`: the same prompts served as one multi-question request whose shared prefix is read once into a
+decoder state and cloned per question (MicaJudge.Predict), the effective prompt tokens/s.
 
 `value` is device-resident throughput (inputs staged in HBM before the timed region); `e2e` is the same step through
 the host-pointer C ABI with the step's inputs copied from pinned host memory and its result (the loss; the logits)
@@ -46,6 +48,7 @@ Q8_WORKLOAD = "config2_q8_0_decision_forward"
 # config 5 (Mica decoder prefill)
 DEC_ROWS, DEC_LEN, DEC_LABELS = 8, 2048, 26
 DEC_TOKENS = DEC_ROWS * DEC_LEN
+DEC_SHARED = 1792   # prompt tokens the questions of one Mica request share (the shared-prefix nested line)
 DEC_WORKLOAD = "config5_mica_hybrid_decoder_prefill"
 
 
@@ -680,8 +683,47 @@ def dec_measure(args, d):
     out["e2e_ms"] = h0.elapsed_time(h1) / args.steps
     out["h2d"] = int(ids.nbytes + lens_np.nbytes + lab_np.nbytes)
     out["d2h"] = int(host_hidden.numel() * 4 + host_logits.numel() * 4)
+    out["shared"] = shared_prefix_measure(args, d, model, stream, labels)
     model.close()
     return out
+
+
+def shared_prefix_measure(args, d, model, stream, labels):
+    """A multi-question Mica request as MicaJudge.Predict serves it (MicaJudge.cs:166-229): the questions' common
+    prefix read once into a state (Readout = false), then every question's remainder in one batched pass, each from
+    its own clone of the prefix state, with the label logits.  The same prompts as the prefill step (DEC_ROWS
+    questions of DEC_LEN tokens), DEC_SHARED of them shared.  Timed per request through the host-pointer C ABI."""
+    import numpy as np
+    import torch
+    import laya_b200
+    rng = np.random.default_rng(11 + d.rank)
+    prefix = rng.integers(0, 151936, DEC_SHARED).astype(np.int64)
+    rests = [rng.integers(0, 151936, DEC_LEN - DEC_SHARED).astype(np.int64) for _ in range(DEC_ROWS)]
+
+    def request():
+        state = model.new_state(DEC_LEN)
+        model.read(prefix, state)
+        branches = [laya_b200.Qwen35Sequence(r, state if i == DEC_ROWS - 1 else state.clone())
+                    for i, r in enumerate(rests)]
+        model.forward_sequences(branches, labels)
+        for q in branches:
+            q.state.close()
+        return branches
+
+    for _ in range(max(1, args.warmup)):
+        request()
+    d.barrier()
+    launches0 = model.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = request()
+    e1.record(stream)
+    e1.synchronize()
+    d.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    return {"ms": ms, "launches": (model.launches() - launches0) // args.steps,
+            "finite": all(bool(np.isfinite(q.logits).all()) for q in out)}
 
 
 def run_ours(args):
@@ -774,7 +816,7 @@ def run_ours(args):
                 line["q8_0_encode"] = q
     if args.workload in ("all", "decoder"):
         r = dec_measure(args, d)
-        ms, e2e_ms = d.reduce([r["ms"], r["e2e_ms"]], MAX)
+        ms, e2e_ms, sp_ms = d.reduce([r["ms"], r["e2e_ms"], r["shared"]["ms"]], MAX)
         if rank == 0:
             (g_ms, g_ops, g_n), (r_ms, r_ops, r_n), (a_ms, a_ops, a_n) = r["prof"]
             bf16 = peaks.get("bf16_tflops", 1590.0)
@@ -800,6 +842,15 @@ def run_ours(args):
                               "ms_per_step": a_ms / args.steps, "share_of_step": a_ms / args.steps / ms,
                               "tflops": a_ops / (a_ms / 1e3) / 1e12 if a_ms else None},
                 "gpu_launches": r["launches"], "clocks": r["clocks"], "logits_finite": r["finite"]}
+            q["mica_shared_prefix"] = {
+                "metric": "Mica prompt tokens/s, shared prefix read once into a state (MicaJudge.Predict)",
+                "value": world * DEC_TOKENS / (sp_ms / 1e3), "unit": "tokens/s", "ms_per_request": sp_ms,
+                "requests_per_s": world / (sp_ms / 1e3),
+                "config": {"questions": DEC_ROWS, "prompt_tokens": DEC_LEN, "shared_prefix": DEC_SHARED,
+                           "path": "laya_decoder_state_create + forward_states(read prefix) + state_clone x"
+                                   f"{DEC_ROWS - 1} + forward_states(all remainders, label logits), host buffers"},
+                "vs_prefill_every_prompt_ms": e2e_ms, "gpu_launches_per_request": r["shared"]["launches"],
+                "logits_finite": r["shared"]["finite"]}
             if not args.no_cpu_baseline:
                 q["cpu_baseline"] = dec_cpu_baseline(args.dec_tokens)
             if line is None:

@@ -17,6 +17,9 @@
  *                                     (teacher-forced parity of a single layer; not in the reference's surface)
  *   laya_decoder_record_*             the IStateRecorder of Forward (:468, :505-509, :519-528): "embeddings",
  *                                     "layers.{i}.mixer", "layers.{i}", "norm"
+ *   laya_decoder_state_* / _mark_*    Qwen35State (:38-197): NewState, Clone, Save / Rewind, Length, Bytes, Dispose
+ *   laya_decoder_forward_states       Forward over sequences that continue states, with in-pass Checkpoints
+ *                                     (:462-532, :734-749, :880-895) — Mica's shared-prefix reuse (MicaJudge.cs:166-229)
  *
  * Weights are the Hugging Face checkpoint's tensors by name ("model." or "model.language_model." prefixes are
  * accepted and dropped).  Projections (q/k/v/o, in_proj_*, out_proj, gate/up/down) and embed_tokens are kept as Q8_0:
@@ -100,6 +103,49 @@ int laya_decoder_logits(laya_decoder* dec, const float* hidden, int rows, const 
  * layer's mixer output (before its residual add). */
 int laya_decoder_layer(laya_decoder* dec, int layer, float* hidden, const int32_t* seq_len, int n_seq,
                        float* mixer);
+
+/* States (Qwen35State, Qwen35Model.cs:38-197): what the decoder remembers of the tokens a sequence has read, in device
+ * memory — keys and values of every full-attention layer (fp16 [capacity, kv_heads·head_dim], normed and rotated as
+ * attention reads them), and the conv tail [conv_kernel − 1, conv dim] plus the delta-rule state
+ * [lin_v_heads, lin_k_dim, lin_v_dim] (fp32) of every DeltaNet layer.  Reading a prompt in several forwards through
+ * one state gives bit for bit the hidden state and logits of reading it in one forward.  State calls are
+ * asynchronous on the decoder's stream; a state belongs to the decoder that made it (destroying the decoder frees
+ * its states' memory; the handles must still be destroyed). */
+typedef struct laya_decoder_state laya_decoder_state;
+typedef struct laya_decoder_mark laya_decoder_mark;
+
+/* Qwen35Model.NewState (:419): a state that has read nothing, with room for `capacity` tokens (a hint: the key and
+ * value caches grow on demand to the next power of two, as Qwen35State.GrowCache does, :146-154). */
+int laya_decoder_state_create(laya_decoder* dec, int capacity, laya_decoder_state** out);
+/* Qwen35State.Dispose (:187-196). */
+int laya_decoder_state_destroy(laya_decoder_state* state);
+/* Qwen35State.Length (:62) and Bytes (:183-184): tokens read; device bytes held. */
+int laya_decoder_state_length(const laya_decoder_state* state, int* length);
+int laya_decoder_state_bytes(const laya_decoder_state* state, int64_t* bytes);
+/* Qwen35State.Clone (:112-117): an independent copy — what is read into one never reaches the other. */
+int laya_decoder_state_clone(laya_decoder_state* state, laya_decoder_state** out);
+/* Qwen35State.Save (:127-131) / Rewind (:134-143) / Mark.Dispose (:174-180): a mark keeps the length and a copy of the
+ * conv tails and delta-rule states; rewinding copies them back and moves the length back (keys and values are not
+ * copied: what is read next overwrites them).  A mark longer than the state, or of another decoder:
+ * LAYA_ERR_ARGUMENT. */
+int laya_decoder_state_save(laya_decoder_state* state, laya_decoder_mark** out);
+int laya_decoder_state_rewind(laya_decoder_state* state, const laya_decoder_mark* mark);
+int laya_decoder_mark_destroy(laya_decoder_mark* mark);
+
+/* Qwen35Model.Forward(IReadOnlyList<Qwen35Sequence>) (:462-532) over states: sequence s reads its seq_len[s] tokens
+ * after what states[s] holds and advances it (n_seq distinct states of this decoder).  readout [n_seq] (may be
+ * NULL) is Qwen35Sequence.Readout; hidden / logits rows are written for every sequence and meaningful for those
+ * with readout.  Checkpoints (Qwen35Sequence.Checkpoints / Snapshots, :214-221; MicaJudge.cs:87, :189-212):
+ * n_checkpoints [n_seq] (may be NULL), checkpoints the concatenated token counts of each sequence (strictly
+ * ascending within 1..seq_len[s]), and snapshots [Σ n_checkpoints] receives one new state per checkpoint — owned by
+ * the caller — holding what its sequence held after that many tokens.  Qwen35Model.Read (:437-439) is this call with
+ * hidden and logits NULL.  ids, seq_len, label ids and results are host arrays; the call returns when the results are
+ * on the host.  Invalid arguments and ids outside the vocabulary are rejected before any state changes. */
+int laya_decoder_forward_states(laya_decoder* dec, const int32_t* ids, const int32_t* seq_len, int n_seq,
+                                laya_decoder_state* const* states, const int32_t* readout,
+                                const int32_t* n_checkpoints, const int32_t* checkpoints,
+                                laya_decoder_state** snapshots, const int32_t* label_ids, int n_labels, float* hidden,
+                                float* logits);
 
 /* Recorder of the next forwards (single or several sequences; rows packed): 1 on, 0 off. */
 int laya_decoder_record_enable(laya_decoder* dec, int enabled);

@@ -19,12 +19,14 @@ from .api import (Context, DecisionModel, DecisionOutput, BatchItem, ModelDesc, 
                   LayaError, LayaArgumentError, LayaOutOfRangeError, LayaNotSupportedError, LayaCudaError,
                   LayaNotFoundError, LayaDeviceTimeout, LayaLibraryMissing, lib, library_path, base_desc,
                   PRECISION_F32, PRECISION_Q8_0, Trainer, Batch, TrainingItem, TrainDesc, RlcdDesc, train_desc,
-                  FORWARD_ACCURATE, FORWARD_BF16, Qwen35Model, DecoderDesc, decoder_desc, DECODER_LINEAR,
+                  FORWARD_ACCURATE, FORWARD_BF16, Qwen35Model, Qwen35State, Qwen35Sequence, Qwen35Mark, DecoderDesc,
+                  decoder_desc, DECODER_LINEAR,
                   DECODER_FULL, fit_temperatures, TemperatureFitDesc)
 
 __all__ = ["Context", "DecisionModel", "DecisionOutput", "BatchItem", "ModelDesc", "PackedMatrixQ8_0", "Q8_0",
            "LayaError", "LayaArgumentError", "LayaOutOfRangeError", "LayaNotSupportedError", "LayaCudaError",
            "LayaNotFoundError", "LayaDeviceTimeout", "LayaLibraryMissing", "lib", "library_path", "base_desc",
            "PRECISION_F32", "PRECISION_Q8_0", "Trainer", "Batch", "TrainingItem", "TrainDesc", "RlcdDesc",
-           "train_desc", "FORWARD_ACCURATE", "FORWARD_BF16", "Qwen35Model", "DecoderDesc", "decoder_desc",
+           "train_desc", "FORWARD_ACCURATE", "FORWARD_BF16", "Qwen35Model", "Qwen35State", "Qwen35Sequence", "Qwen35Mark",
+           "DecoderDesc", "decoder_desc",
            "DECODER_LINEAR", "DECODER_FULL", "fit_temperatures", "TemperatureFitDesc"]

@@ -146,6 +146,15 @@ _SIGS = {
     "laya_decoder_forward_device": (_I, [_P, _P, _P, _I, _P, _I, _P, _P]),
     "laya_decoder_logits": (_I, [_P, _P, _I, _P, _I, _P]),
     "laya_decoder_layer": (_I, [_P, _I, _P, _P, _I, _P]),
+    "laya_decoder_state_create": (_I, [_P, _I, ctypes.POINTER(_P)]),
+    "laya_decoder_state_destroy": (_I, [_P]),
+    "laya_decoder_state_length": (_I, [_P, ctypes.POINTER(_I)]),
+    "laya_decoder_state_bytes": (_I, [_P, ctypes.POINTER(ctypes.c_int64)]),
+    "laya_decoder_state_clone": (_I, [_P, ctypes.POINTER(_P)]),
+    "laya_decoder_state_save": (_I, [_P, ctypes.POINTER(_P)]),
+    "laya_decoder_state_rewind": (_I, [_P, _P]),
+    "laya_decoder_mark_destroy": (_I, [_P]),
+    "laya_decoder_forward_states": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P]),
     "laya_decoder_record_enable": (_I, [_P, _I]),
     "laya_decoder_record_get": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
     "laya_decoder_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
@@ -756,11 +765,91 @@ def decoder_desc(kinds: Sequence[str], **kw) -> DecoderDesc:
     return desc
 
 
+class Qwen35Mark:
+    """Qwen35State.Mark (Qwen35Model.cs:158-181): a saved point of a state; close() is Dispose."""
+
+    def __init__(self, handle, length: int):
+        self.handle = handle
+        self.length = length
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_decoder_mark_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Qwen35State:
+    """Qwen35State (Qwen35Model.cs:38-197) in device memory: what the decoder remembers of the tokens read so far.
+    Length, Bytes, Clone, Save / Rewind; close() is Dispose."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    @property
+    def length(self) -> int:
+        n = ctypes.c_int()
+        check(lib().laya_decoder_state_length(self.handle, ctypes.byref(n)))
+        return n.value
+
+    @property
+    def bytes(self) -> int:
+        n = ctypes.c_int64()
+        check(lib().laya_decoder_state_bytes(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def clone(self) -> "Qwen35State":
+        h = ctypes.c_void_p()
+        check(lib().laya_decoder_state_clone(self.handle, ctypes.byref(h)))
+        return Qwen35State(h)
+
+    def save(self) -> Qwen35Mark:
+        h = ctypes.c_void_p()
+        check(lib().laya_decoder_state_save(self.handle, ctypes.byref(h)))
+        return Qwen35Mark(h, self.length)
+
+    def rewind(self, mark: Qwen35Mark):
+        check(lib().laya_decoder_state_rewind(self.handle, mark.handle))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().laya_decoder_state_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Qwen35Sequence:
+    """Qwen35Sequence (Qwen35Model.cs:199-221): tokens read after what `state` holds; `readout`; `checkpoints`
+    (token counts, ascending) after which to snapshot the state.  A forward sets `hidden`, `logits` and
+    `snapshots` (new states owned by the caller)."""
+
+    def __init__(self, tokens, state: Qwen35State, readout: bool = True, checkpoints: Optional[Sequence[int]] = None):
+        self.tokens = np.asarray(tokens, np.int64)
+        self.state = state
+        self.readout = readout
+        self.checkpoints = list(checkpoints or [])
+        self.hidden = None
+        self.logits = None
+        self.snapshots: List[Qwen35State] = []
+
+
 class Qwen35Model:
     """The Mica decoder on one B200 (include/laya_decoder.h), mirroring Qwen35Model (Mica/Models/Qwen35Model.cs)
     with WeightPrecision.Q8_0: construct, `load(weights)` by checkpoint names, `forward(sequences, labels)` — every
     sequence from an empty state, returning each sequence's final-normed last hidden row (Qwen35Sequence.Hidden) and
-    the label logits (Logits → TokenTable.QuantizedLogits) — `logits(hidden, ids)`, `layer(i, hidden, seq_lens)`."""
+    the label logits (Logits → TokenTable.QuantizedLogits) — `logits(hidden, ids)`, `layer(i, hidden, seq_lens)`;
+    and with states: `new_state()`, `forward_sequences([Qwen35Sequence])`, `forward_state(tokens, state)`,
+    `read(tokens, state)`."""
 
     def __init__(self, desc: DecoderDesc, device: int = 0):
         self.desc = desc
@@ -827,6 +916,48 @@ class Qwen35Model:
         check(lib().laya_decoder_forward(self.handle, _np_ptr(ids), _np_ptr(lens), len(sequences), _np_ptr(lab),
                                          0 if lab is None else len(lab), _np_ptr(hidden), _np_ptr(logits)))
         return hidden, logits
+
+    def new_state(self, capacity: int = 0) -> Qwen35State:
+        """NewState (Qwen35Model.cs:419)."""
+        h = ctypes.c_void_p()
+        check(lib().laya_decoder_state_create(self.handle, capacity, ctypes.byref(h)))
+        return Qwen35State(h)
+
+    def forward_sequences(self, sequences: Sequence[Qwen35Sequence], labels: Optional[Sequence[int]] = None):
+        """Forward(IReadOnlyList<Qwen35Sequence>) (Qwen35Model.cs:462-532): each sequence continues its state."""
+        ids, lens = self.pack([q.tokens for q in sequences])
+        n = len(sequences)
+        states = (ctypes.c_void_p * max(1, n))(*[q.state.handle for q in sequences])
+        readout = _i32([1 if q.readout else 0 for q in sequences])
+        ncp = _i32([len(q.checkpoints) for q in sequences])
+        cps = _i32([c for q in sequences for c in q.checkpoints])
+        n_snap = int(ncp.sum())
+        snaps = (ctypes.c_void_p * max(1, n_snap))()
+        lab = None if labels is None else _i32(labels)
+        hidden = np.zeros((n, self.desc.hidden), np.float32)
+        logits = None if lab is None else np.zeros((n, len(lab)), np.float32)
+        check(lib().laya_decoder_forward_states(self.handle, _np_ptr(ids), _np_ptr(lens), n, states, _np_ptr(readout),
+                                                _np_ptr(ncp), _np_ptr(cps) if n_snap else None, snaps,
+                                                _np_ptr(lab), 0 if lab is None else len(lab), _np_ptr(hidden),
+                                                _np_ptr(logits)))
+        k = 0
+        for i, q in enumerate(sequences):
+            q.hidden = hidden[i].copy() if q.readout else None
+            q.logits = None if logits is None or not q.readout else logits[i].copy()
+            q.snapshots = [Qwen35State(ctypes.c_void_p(snaps[k + j])) for j in range(len(q.checkpoints))]
+            k += len(q.checkpoints)
+        return sequences
+
+    def forward_state(self, tokens, state: Qwen35State, labels: Optional[Sequence[int]] = None):
+        """Forward(ReadOnlySpan<int>, Qwen35State) (Qwen35Model.cs:423-430): the final-normed hidden row of the last
+        token (and the label logits when labels are given)."""
+        q = self.forward_sequences([Qwen35Sequence(tokens, state)], labels)[0]
+        return q.hidden if labels is None else (q.hidden, q.logits)
+
+    def read(self, tokens, state: Qwen35State, checkpoints: Optional[Sequence[int]] = None):
+        """Read (Qwen35Model.cs:436-439): tokens into the state without output; returns the checkpoint snapshots."""
+        q = self.forward_sequences([Qwen35Sequence(tokens, state, readout=False, checkpoints=checkpoints)])[0]
+        return q.snapshots
 
     def forward_device(self, ids_ptr: int, seq_lens: Sequence[int], labels: Sequence[int], hidden_ptr: int,
                        logits_ptr: int):

@@ -137,6 +137,16 @@ struct laya_decoder {
     int32_t *ids = nullptr, *tok_seq = nullptr, *seq_start = nullptr, *seq_len = nullptr, *last_row = nullptr,
             *tile_seq = nullptr, *tile_p0 = nullptr, *labels = nullptr;
     int n_tiles = 0;
+    // the states of the current forward: positions already read, checkpoints, and the pointer tables
+    // ptrs [2·layers·n_seq]: per layer two rows of one entry per sequence (full: keys, values; DeltaNet: conv tail,
+    // recurrent state — 0 without a state), then [2·layers·n_snap] the same for the snapshots
+    int32_t *pos0 = nullptr, *snap_begin = nullptr, *snap_at = nullptr;
+    uint64_t* ptrs = nullptr;
+    int cur_seqs = 0, cur_snaps = 0;
+    bool with_states = false;
+    int rope_cap = 0;
+    std::set<laya_decoder_state*> states;
+    std::set<laya_decoder_mark*> marks;
 
     // profiling: 0 products, 1 delta rule, 2 full attention
     bool profiling = false;
@@ -150,6 +160,25 @@ struct laya_decoder {
     std::map<std::string, std::pair<float*, size_t>> rec;
 
     std::vector<void*> allocs;
+};
+
+// Qwen35State in device memory: one stream-ordered block — first the fixed part (per DeltaNet layer its conv tail
+// [K−1, cd] and recurrent state [vh, dk, dv], fp32), then per full-attention layer keys and values
+// [capacity, kv·hd] fp16.  dec is cleared when the decoder goes first (the block is freed with it).
+struct laya_decoder_state {
+    laya_decoder* dec = nullptr;
+    int capacity = 0, length = 0;
+    char* block = nullptr;
+    size_t fixed = 0, bytes = 0;
+    std::vector<float*> tail, rec;
+    std::vector<__half*> k, v;
+};
+// Qwen35State.Mark: the length and a copy of the fixed part.
+struct laya_decoder_mark {
+    laya_decoder* dec = nullptr;
+    int length = 0;
+    char* block = nullptr;
+    size_t bytes = 0;
 };
 
 namespace {
@@ -233,6 +262,16 @@ int record_copy(laya_decoder* c, const std::string& name, const float* src, size
     return OK;
 }
 
+template <class T>
+T* const* seq_table(laya_decoder* c, int layer, int which) {
+    return reinterpret_cast<T* const*>(c->ptrs + (2 * static_cast<size_t>(layer) + which) * c->cur_seqs);
+}
+template <class T>
+T* const* snap_table(laya_decoder* c, int layer, int which) {
+    return reinterpret_cast<T* const*>(c->ptrs + 2 * static_cast<size_t>(c->d.layers) * c->cur_seqs +
+                                       (2 * static_cast<size_t>(layer) + which) * c->cur_snaps);
+}
+
 // y = Q8(x) · Wᵀ with the codes of x in (qx, dx).
 int product_from(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo, const q8::code_t* qx,
                  const float* dx) {
@@ -274,7 +313,15 @@ int linear_mixer(laya_decoder* c, const Layer& L, int T, int n_seq, int layer, b
     dec::ConvArgs cv{};
     cv.T = T; cv.cd = c->cd; cv.K = d.conv_kernel; cv.in = c->big; cv.ld_in = c->ld_in; cv.w = L.conv_w;
     cv.tok_seq = c->tok_seq; cv.seq_start = c->seq_start; cv.out = c->conv;
+    cv.tails = c->with_states ? seq_table<float>(c, layer, 0) : nullptr;
     RC(dec_conv_silu(cv, c->stream));
+    if (c->with_states) {
+        dec::ConvStateArgs cs{};
+        cs.n_seq = n_seq; cs.cd = c->cd; cs.K = d.conv_kernel; cs.in = c->big; cs.ld_in = c->ld_in;
+        cs.seq_start = c->seq_start; cs.seq_len = c->seq_len; cs.tails = cv.tails;
+        if (c->cur_snaps) { cs.snap_begin = c->snap_begin; cs.snap_at = c->snap_at; cs.snap_tails = snap_table<float>(c, layer, 0); }
+        RC(dec_conv_state(cs, c->stream));
+    }
     dec::HeadsArgs hd{};
     hd.T = T; hd.kh = d.lin_k_heads; hd.vh = d.lin_v_heads; hd.dk = d.lin_k_dim; hd.key_dim = c->key_dim; hd.cd = c->cd;
     hd.conv = c->conv; hd.qscale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.lin_k_dim)));
@@ -285,6 +332,10 @@ int linear_mixer(laya_decoder* c, const Layer& L, int T, int n_seq, int layer, b
     dr.dk = d.lin_k_dim; dr.dv = d.lin_v_dim; dr.vh = d.lin_v_heads; dr.ratio = d.lin_v_heads / d.lin_k_heads;
     dr.key_dim = c->key_dim; dr.cd = c->cd; dr.conv = c->conv; dr.beta = c->beta; dr.decay = c->decay;
     dr.seq_start = c->seq_start; dr.seq_len = c->seq_len; dr.out = c->core; dr.ld_out = c->vd;
+    if (c->with_states) {
+        dr.rec = seq_table<float>(c, layer, 1);
+        if (c->cur_snaps) { dr.snap_begin = c->snap_begin; dr.snap_at = c->snap_at; dr.snap_rec = snap_table<float>(c, layer, 1); }
+    }
     const double rule_ops = static_cast<double>(T) * d.lin_v_heads * d.lin_k_dim * d.lin_v_dim * 8.0;
     RC(timed(c, 1, rule_ops, [&] { return dec_delta_rule(dr, n_seq, c->stream); }));
     dec::GatedArgs gn{};
@@ -304,10 +355,11 @@ int full_mixer(laya_decoder* c, const Layer& L, int T, long long pairs, int laye
     pp.T = T; pp.heads = d.heads; pp.kv_heads = d.kv_heads; pp.hd = d.head_dim; pp.half = c->half;
     pp.q_width = c->q_width; pp.qkv = c->big; pp.ld_qkv = c->nqkv; pp.qnorm = L.qnorm; pp.knorm = L.knorm;
     pp.eps = d.eps; pp.cosv = c->cosv; pp.sinv = c->sinv; pp.tok_seq = c->tok_seq; pp.seq_start = c->seq_start;
-    pp.q16 = c->q16; pp.k16 = c->k16; pp.v16 = c->v16;
+    pp.pos0 = c->pos0; pp.q16 = c->q16; pp.kc = seq_table<__half>(c, layer, 0); pp.vc = seq_table<__half>(c, layer, 1);
     dec::AttnArgs at{};
-    at.heads = d.heads; at.kv_heads = d.kv_heads; at.q16 = c->q16; at.k16 = c->k16; at.v16 = c->v16;
+    at.heads = d.heads; at.kv_heads = d.kv_heads; at.q16 = c->q16; at.kc = pp.kc; at.vc = pp.vc;
     at.tile_seq = c->tile_seq; at.tile_p0 = c->tile_p0; at.seq_start = c->seq_start; at.seq_len = c->seq_len;
+    at.pos0 = c->pos0;
     at.scale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.head_dim)));
     at.qkv = c->big; at.ld_qkv = c->nqkv; at.out = c->core; at.ld_out = d.heads * d.head_dim;
     const double att_ops = 4.0 * static_cast<double>(pairs) * d.heads * d.head_dim;
@@ -342,23 +394,36 @@ int run_layer(laya_decoder* c, int i, int T, int n_seq, long long pairs, bool ke
     return record_copy(c, "layers." + std::to_string(i), c->x, static_cast<size_t>(T) * c->d.hidden);
 }
 
+// The states a forward's sequences continue, and the snapshot states its checkpoints fill (validated by the caller).
+struct StateView {
+    laya_decoder_state* const* states = nullptr;   // [n_seq]
+    const int32_t* n_cp = nullptr;                 // [n_seq] or null
+    const int32_t* cps = nullptr;                  // concatenated checkpoints
+    laya_decoder_state* const* snaps = nullptr;    // [n_snap]
+    int n_snap = 0;
+};
+
 // Host metadata of one forward → pinned staging → one copy.  Returns the causal (query, key) pairs of full attention.
 int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int n_seq, const int32_t* labels,
-          int n_labels, int* T_out, long long* pairs_out) {
+          int n_labels, int* T_out, long long* pairs_out, const StateView* sv = nullptr) {
     if (n_seq <= 0 || n_seq > c->d.max_seqs) { set_error("sequence count outside 1..max_seqs"); return ERR_ARGUMENT; }
     long long T = 0, pairs = 0;
     int tiles = 0;
     for (int s = 0; s < n_seq; ++s) {
         if (seq_len[s] <= 0) { set_error("every sequence needs at least one token"); return ERR_ARGUMENT; }
+        const long long p0 = sv ? sv->states[s]->length : 0;
         T += seq_len[s];
-        pairs += static_cast<long long>(seq_len[s]) * (seq_len[s] + 1) / 2;
+        pairs += static_cast<long long>(seq_len[s]) * (seq_len[s] + 1) / 2 + p0 * seq_len[s];
         tiles += (seq_len[s] + 63) / 64;
     }
     if (T > c->d.max_tokens) { set_error("more tokens than max_tokens"); return ERR_ARGUMENT; }
     if (n_labels < 0 || (n_labels > 0 && !labels)) { set_error("invalid label list"); return ERR_ARGUMENT; }
     for (int l = 0; l < n_labels; ++l)
         if (labels[l] < 0 || labels[l] >= c->d.vocab) { set_error("label id outside the vocabulary"); return ERR_OUT_OF_RANGE; }
-    const size_t need = static_cast<size_t>(ids_host ? T : 0) + T + 3 * static_cast<size_t>(n_seq) + 2 * tiles + n_labels;
+    const int n_snap = sv ? sv->n_snap : 0;
+    const size_t n_ptr = 2 * static_cast<size_t>(c->d.layers) * (n_seq + n_snap);
+    const size_t need = static_cast<size_t>(ids_host ? T : 0) + T + 3 * static_cast<size_t>(n_seq) + 2 * tiles +
+                        n_labels + n_seq + (n_seq + 1) + n_snap + 1 + 2 * n_ptr;
     if (c->in_pending) { LAYA_CUDA(cudaEventSynchronize(c->in_done)); c->in_pending = false; }
     if (need > c->in_cap) {
         if (c->in_host) cudaFreeHost(c->in_host);
@@ -385,17 +450,60 @@ int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int 
     int32_t* tsq = slot(tiles, &c->tile_seq);
     int32_t* tp0 = slot(tiles, &c->tile_p0);
     int32_t* lb = slot(n_labels, &c->labels);
+    int32_t* ps = slot(n_seq, &c->pos0);
+    int32_t* sb = slot(n_seq + 1, &c->snap_begin);
+    int32_t* sa = slot(n_snap, &c->snap_at);
+    if (o & 1) ++o;   // 8-byte alignment of the pointer tables (the device buffer is 256-byte aligned)
+    int32_t* dummy = nullptr;
+    uint64_t* pt = reinterpret_cast<uint64_t*>(slot(2 * n_ptr, &dummy));
+    c->ptrs = reinterpret_cast<uint64_t*>(dummy);
     int start = 0;
-    std::vector<std::pair<int, int>> tl;
+    std::vector<std::pair<int, int>> tl;   // (key positions before the tile's last query, tile index)
+    std::vector<std::pair<int, int>> tile_of;
     for (int s = 0; s < n_seq; ++s) {
         ss[s] = start; sl[s] = seq_len[s]; lr[s] = start + seq_len[s] - 1;
+        ps[s] = sv ? sv->states[s]->length : 0;
         for (int t = 0; t < seq_len[s]; ++t) ts[start + t] = s;
-        for (int p0 = 0; p0 < seq_len[s]; p0 += 64) tl.push_back({p0, s});
+        for (int p0 = 0; p0 < seq_len[s]; p0 += 64) {
+            tl.push_back({ps[s] + p0, static_cast<int>(tile_of.size())});
+            tile_of.push_back({p0, s});
+        }
         start += seq_len[s];
     }
     // longest causal rows first
     std::stable_sort(tl.begin(), tl.end(), [](const std::pair<int, int>& a, const std::pair<int, int>& b) { return a.first > b.first; });
-    for (int i = 0; i < tiles; ++i) { tsq[i] = tl[i].second; tp0[i] = tl[i].first; }
+    for (int i = 0; i < tiles; ++i) { tsq[i] = tile_of[tl[i].second].second; tp0[i] = tile_of[tl[i].second].first; }
+    sb[0] = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        const int n = (sv && sv->n_cp) ? sv->n_cp[s] : 0;
+        for (int k = 0; k < n; ++k) sa[sb[s] + k] = sv->cps[sb[s] + k];
+        sb[s + 1] = sb[s] + n;
+    }
+    const size_t ldkv = static_cast<size_t>(c->d.kv_heads) * c->d.head_dim;
+    for (int i = 0; i < c->d.layers; ++i) {
+        const bool full = c->kinds[i] == LAYA_DECODER_FULL;
+        uint64_t* a = pt + (2 * static_cast<size_t>(i)) * n_seq;
+        uint64_t* b = a + n_seq;
+        for (int s = 0; s < n_seq; ++s) {
+            if (sv) {
+                const laya_decoder_state* st = sv->states[s];
+                a[s] = reinterpret_cast<uint64_t>(full ? static_cast<void*>(st->k[i]) : static_cast<void*>(st->tail[i]));
+                b[s] = reinterpret_cast<uint64_t>(full ? static_cast<void*>(st->v[i]) : static_cast<void*>(st->rec[i]));
+            } else {
+                a[s] = full ? reinterpret_cast<uint64_t>(c->k16 + ss[s] * ldkv) : 0;
+                b[s] = full ? reinterpret_cast<uint64_t>(c->v16 + ss[s] * ldkv) : 0;
+            }
+        }
+        uint64_t* sa_ = pt + 2 * static_cast<size_t>(c->d.layers) * n_seq + (2 * static_cast<size_t>(i)) * n_snap;
+        for (int k = 0; k < n_snap; ++k) {
+            const laya_decoder_state* st = sv->snaps[k];
+            sa_[k] = full ? 0 : reinterpret_cast<uint64_t>(st->tail[i]);
+            sa_[n_snap + k] = full ? 0 : reinterpret_cast<uint64_t>(st->rec[i]);
+        }
+    }
+    c->cur_seqs = n_seq;
+    c->cur_snaps = n_snap;
+    c->with_states = sv != nullptr;
     if (n_labels) memcpy(lb, labels, sizeof(int32_t) * n_labels);
     c->n_tiles = tiles;
     LAYA_CUDA(cudaMemcpyAsync(c->in_dev, h, o * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
@@ -516,6 +624,38 @@ int check_desc(const laya_decoder_desc& d) {
     return OK;
 }
 
+// RoPE tables for positions [0, positions) (Qwen35Model.cs:247-253): inv_freq = 1/θ^(2i/rotary_dim) and
+// angle = pos·inv_freq in fp32.  Grown (rebuilt) when a state reads past them; the old tables are freed after the work
+// queued on the stream.
+int ensure_rope(laya_decoder* c, int positions) {
+    if (positions <= c->rope_cap) return OK;
+    const laya_decoder_desc& d = c->d;
+    const int hf = std::max(c->half, 1);
+    const size_t n = static_cast<size_t>(positions) * hf;
+    std::vector<float> cs(n), sn(n), inv(hf);
+    for (int i = 0; i < c->half; ++i)
+        inv[i] = 1.0f / std::pow(static_cast<float>(d.rope_theta), static_cast<float>(2 * i) / static_cast<float>(d.rotary_dim));
+    for (size_t p = 0; p < static_cast<size_t>(positions); ++p)
+        for (int i = 0; i < c->half; ++i) {
+            const float ang = static_cast<float>(p) * inv[i];
+            cs[p * hf + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
+            sn[p * hf + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+        }
+    float *nc = nullptr, *ns = nullptr;
+    LAYA_CUDA(cudaMallocAsync(&nc, n * sizeof(float), c->stream));
+    cudaError_t e = cudaMallocAsync(&ns, n * sizeof(float), c->stream);
+    if (e != cudaSuccess) { cudaFreeAsync(nc, c->stream); return cuda_fail(e, "cudaMallocAsync"); }
+    LAYA_CUDA(cudaMemcpyAsync(nc, cs.data(), n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    LAYA_CUDA(cudaMemcpyAsync(ns, sn.data(), n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));   // the host tables go out of scope
+    if (c->cosv) cudaFreeAsync(c->cosv, c->stream);
+    if (c->sinv) cudaFreeAsync(c->sinv, c->stream);
+    c->cosv = nc;
+    c->sinv = ns;
+    c->rope_cap = positions;
+    return OK;
+}
+
 int create(laya_decoder* c) {
     const laya_decoder_desc& d = c->d;
     c->key_dim = d.lin_k_heads * d.lin_k_dim;
@@ -576,22 +716,7 @@ int create(laya_decoder* c) {
         RC(dalloc_t(c, &c->q16, T * d.heads * d.head_dim));
         RC(dalloc_t(c, &c->k16, T * d.kv_heads * d.head_dim));
         RC(dalloc_t(c, &c->v16, T * d.kv_heads * d.head_dim));
-        // RoPE tables (Qwen35Model.cs:247-253): inv_freq = 1/θ^(2i/rotary_dim) and angle = pos·inv_freq in fp32
-        const int hf = std::max(c->half, 1);
-        std::vector<float> cs(T * hf), sn(T * hf);
-        std::vector<float> inv(hf);
-        for (int i = 0; i < c->half; ++i)
-            inv[i] = 1.0f / std::pow(static_cast<float>(d.rope_theta), static_cast<float>(2 * i) / static_cast<float>(d.rotary_dim));
-        for (size_t p = 0; p < T; ++p)
-            for (int i = 0; i < c->half; ++i) {
-                const float ang = static_cast<float>(p) * inv[i];
-                cs[p * hf + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
-                sn[p * hf + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
-            }
-        RC(dalloc_t(c, &c->cosv, cs.size()));
-        RC(dalloc_t(c, &c->sinv, sn.size()));
-        LAYA_CUDA(cudaMemcpy(c->cosv, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
-        LAYA_CUDA(cudaMemcpy(c->sinv, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+        RC(ensure_rope(c, static_cast<int>(T)));
     }
     RC(dalloc_t(c, &c->hid, static_cast<size_t>(d.max_seqs) * d.hidden));
     RC(dalloc_t(c, &c->qlast, static_cast<size_t>(d.max_seqs) * d.hidden));
@@ -675,6 +800,112 @@ int fill_rows_q8(laya_decoder* c, const Part& p, const int8_t* q_host, const uin
     return OK;
 }
 
+// ------------------------------------------------------------------------------------------------ states
+size_t pad256(size_t b) { return (b + 255) / 256 * 256; }
+size_t state_fixed_bytes(const laya_decoder* c) {
+    const laya_decoder_desc& d = c->d;
+    size_t b = 0;
+    for (int i = 0; i < d.layers; ++i)
+        if (c->kinds[i] != LAYA_DECODER_FULL)
+            b += pad256(sizeof(float) * (d.conv_kernel - 1) * c->cd) +
+                 pad256(sizeof(float) * static_cast<size_t>(d.lin_v_heads) * d.lin_k_dim * d.lin_v_dim);
+    return b;
+}
+size_t state_kv_bytes(const laya_decoder* c, int capacity) {   // one cache (keys or values) of one layer
+    return pad256(sizeof(__half) * static_cast<size_t>(capacity) * c->d.kv_heads * c->d.head_dim);
+}
+void state_bind(laya_decoder_state* st) {
+    const laya_decoder* c = st->dec;
+    const laya_decoder_desc& d = c->d;
+    st->tail.assign(d.layers, nullptr);
+    st->rec.assign(d.layers, nullptr);
+    st->k.assign(d.layers, nullptr);
+    st->v.assign(d.layers, nullptr);
+    char* p = st->block;
+    for (int i = 0; i < d.layers; ++i)
+        if (c->kinds[i] != LAYA_DECODER_FULL) {
+            st->tail[i] = reinterpret_cast<float*>(p);
+            p += pad256(sizeof(float) * (d.conv_kernel - 1) * c->cd);
+            st->rec[i] = reinterpret_cast<float*>(p);
+            p += pad256(sizeof(float) * static_cast<size_t>(d.lin_v_heads) * d.lin_k_dim * d.lin_v_dim);
+        }
+    const size_t kv = state_kv_bytes(c, st->capacity);
+    for (int i = 0; i < d.layers; ++i)
+        if (c->kinds[i] == LAYA_DECODER_FULL) {
+            st->k[i] = reinterpret_cast<__half*>(p);
+            p += kv;
+            st->v[i] = reinterpret_cast<__half*>(p);
+            p += kv;
+        }
+}
+int n_full_layers(const laya_decoder* c) {
+    int n = 0;
+    for (int k : c->kinds) n += k == LAYA_DECODER_FULL;
+    return n;
+}
+// A block for `capacity` tokens on the decoder's stream; the fixed part zeroed when `zero`.
+int state_block(laya_decoder* c, int capacity, bool zero, char** block, size_t* bytes) {
+    const size_t fixed = state_fixed_bytes(c);
+    *bytes = std::max<size_t>(fixed + 2 * n_full_layers(c) * state_kv_bytes(c, capacity), 256);
+    void* p = nullptr;
+    LAYA_CUDA(cudaMallocAsync(&p, *bytes, c->stream));
+    *block = static_cast<char*>(p);
+    if (zero && fixed) LAYA_CUDA(cudaMemsetAsync(p, 0, fixed, c->stream));
+    return OK;
+}
+// Copies what `from` holds (fixed part, keys and values of its first `from->length` positions) into `to`.
+int state_copy(laya_decoder* c, const laya_decoder_state* from, laya_decoder_state* to) {
+    if (from->fixed) LAYA_CUDA(cudaMemcpyAsync(to->block, from->block, from->fixed, cudaMemcpyDeviceToDevice, c->stream));
+    const size_t row = sizeof(__half) * static_cast<size_t>(c->d.kv_heads) * c->d.head_dim;
+    if (from->length > 0)
+        for (int i = 0; i < c->d.layers; ++i)
+            if (c->kinds[i] == LAYA_DECODER_FULL) {
+                LAYA_CUDA(cudaMemcpyAsync(to->k[i], from->k[i], row * from->length, cudaMemcpyDeviceToDevice, c->stream));
+                LAYA_CUDA(cudaMemcpyAsync(to->v[i], from->v[i], row * from->length, cudaMemcpyDeviceToDevice, c->stream));
+            }
+    to->length = from->length;
+    return OK;
+}
+int state_new(laya_decoder* c, int capacity, laya_decoder_state** out) {
+    laya_decoder_state* st = new laya_decoder_state();
+    st->dec = c;
+    st->capacity = capacity;
+    st->fixed = state_fixed_bytes(c);
+    const int rc = state_block(c, capacity, true, &st->block, &st->bytes);
+    if (rc != OK) { delete st; return rc; }
+    state_bind(st);
+    c->states.insert(st);
+    *out = st;
+    return OK;
+}
+void state_free(laya_decoder_state* st) {
+    if (st->dec) {
+        if (st->block) cudaFreeAsync(st->block, st->dec->stream);
+        st->dec->states.erase(st);
+    }
+    delete st;
+}
+// Qwen35State.GrowCache (Qwen35Model.cs:146-154): room for `needed` positions, the next power of two at least.
+int state_grow(laya_decoder* c, laya_decoder_state* st, int needed) {
+    if (needed <= st->capacity) return OK;
+    long long cap = 1;
+    while (cap < needed) cap <<= 1;
+    laya_decoder_state grown;
+    grown.dec = c;
+    grown.capacity = static_cast<int>(std::min<long long>(cap, INT32_MAX));
+    grown.fixed = st->fixed;
+    RC(state_block(c, grown.capacity, false, &grown.block, &grown.bytes));
+    state_bind(&grown);
+    const int rc = state_copy(c, st, &grown);
+    if (rc != OK) { cudaFreeAsync(grown.block, c->stream); return rc; }
+    cudaFreeAsync(st->block, c->stream);
+    st->block = grown.block;
+    st->bytes = grown.bytes;
+    st->capacity = grown.capacity;
+    st->tail = grown.tail; st->rec = grown.rec; st->k = grown.k; st->v = grown.v;
+    return OK;
+}
+
 int stage_input_rows(laya_decoder* c, const int32_t* seq_len, int n_seq, int* T_out, long long* pairs) {
     return stage(c, nullptr, seq_len, n_seq, nullptr, 0, T_out, pairs);
 }
@@ -710,6 +941,10 @@ int laya_decoder_destroy(laya_decoder* c) {
     if (!c) return OK;
     DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    for (laya_decoder_state* st : c->states) { cudaFree(st->block); st->block = nullptr; st->dec = nullptr; }
+    for (laya_decoder_mark* m : c->marks) { cudaFree(m->block); m->block = nullptr; m->dec = nullptr; }
+    if (c->cosv) cudaFree(c->cosv);
+    if (c->sinv) cudaFree(c->sinv);
     for (void* p : c->allocs) cudaFree(p);
     for (auto& r : c->rec) cudaFree(r.second.first);
     for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
@@ -863,6 +1098,199 @@ int laya_decoder_forward(laya_decoder* c, const int32_t* ids, const int32_t* seq
     if (logits && n_labels)
         LAYA_CUDA(cudaMemcpyAsync(logits, c->logit_buf, nl * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     RC(check_device_error(c));
+    if (c->profiling) RC(collect_profile(c));
+    return OK;
+}
+
+int laya_decoder_state_create(laya_decoder* c, int capacity, laya_decoder_state** out) {
+    if (!c || !out || capacity < 0) { set_error("invalid argument"); return ERR_ARGUMENT; }
+    *out = nullptr;
+    DeviceGuard g(c->device);
+    return state_new(c, capacity, out);
+}
+
+int laya_decoder_state_destroy(laya_decoder_state* st) {
+    if (!st) return OK;
+    if (st->dec) {
+        DeviceGuard g(st->dec->device);
+        state_free(st);
+    } else {
+        delete st;
+    }
+    return OK;
+}
+
+int laya_decoder_state_length(const laya_decoder_state* st, int* length) {
+    if (!st || !length) { set_error("null argument"); return ERR_ARGUMENT; }
+    *length = st->length;
+    return OK;
+}
+
+int laya_decoder_state_bytes(const laya_decoder_state* st, int64_t* bytes) {
+    if (!st || !bytes) { set_error("null argument"); return ERR_ARGUMENT; }
+    *bytes = st->dec ? static_cast<int64_t>(st->bytes) : 0;
+    return OK;
+}
+
+int laya_decoder_state_clone(laya_decoder_state* st, laya_decoder_state** out) {
+    if (!st || !out) { set_error("null argument"); return ERR_ARGUMENT; }
+    *out = nullptr;
+    if (!st->dec) { set_error("the state's decoder was destroyed"); return ERR_ARGUMENT; }
+    laya_decoder* c = st->dec;
+    DeviceGuard g(c->device);
+    laya_decoder_state* copy = nullptr;
+    RC(state_new(c, st->capacity, &copy));
+    const int rc = state_copy(c, st, copy);
+    if (rc != OK) { state_free(copy); return rc; }
+    *out = copy;
+    return OK;
+}
+
+int laya_decoder_state_save(laya_decoder_state* st, laya_decoder_mark** out) {
+    if (!st || !out) { set_error("null argument"); return ERR_ARGUMENT; }
+    *out = nullptr;
+    if (!st->dec) { set_error("the state's decoder was destroyed"); return ERR_ARGUMENT; }
+    laya_decoder* c = st->dec;
+    DeviceGuard g(c->device);
+    laya_decoder_mark* m = new laya_decoder_mark();
+    m->dec = c;
+    m->length = st->length;
+    m->bytes = st->fixed;
+    if (m->bytes) {
+        void* p = nullptr;
+        cudaError_t e = cudaMallocAsync(&p, m->bytes, c->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(p, st->block, m->bytes, cudaMemcpyDeviceToDevice, c->stream);
+        m->block = static_cast<char*>(p);
+        if (e != cudaSuccess) {
+            if (p) cudaFreeAsync(p, c->stream);
+            delete m;
+            return cuda_fail(e, "state save");
+        }
+    }
+    c->marks.insert(m);
+    *out = m;
+    return OK;
+}
+
+int laya_decoder_state_rewind(laya_decoder_state* st, const laya_decoder_mark* m) {
+    if (!st || !m) { set_error("null argument"); return ERR_ARGUMENT; }
+    if (!st->dec || m->dec != st->dec) { set_error("the mark belongs to another decoder"); return ERR_ARGUMENT; }
+    if (m->length > st->length) { set_error("a mark can only rewind, not advance"); return ERR_ARGUMENT; }
+    laya_decoder* c = st->dec;
+    DeviceGuard g(c->device);
+    if (m->bytes) LAYA_CUDA(cudaMemcpyAsync(st->block, m->block, m->bytes, cudaMemcpyDeviceToDevice, c->stream));
+    st->length = m->length;
+    return OK;
+}
+
+int laya_decoder_mark_destroy(laya_decoder_mark* m) {
+    if (!m) return OK;
+    if (m->dec) {
+        DeviceGuard g(m->dec->device);
+        if (m->block) cudaFreeAsync(m->block, m->dec->stream);
+        m->dec->marks.erase(m);
+    }
+    delete m;
+    return OK;
+}
+
+int laya_decoder_forward_states(laya_decoder* c, const int32_t* ids, const int32_t* seq_len, int n_seq,
+                                laya_decoder_state* const* states, const int32_t* readout, const int32_t* n_checkpoints,
+                                const int32_t* checkpoints, laya_decoder_state** snapshots, const int32_t* label_ids,
+                                int n_labels, float* hidden, float* logits) {
+    (void)readout;   // every sequence's row is computed; rows of sequences without readout are not needed
+    if (!c || !ids || !seq_len || !states) { set_error("null argument"); return ERR_ARGUMENT; }
+    if (n_seq <= 0 || n_seq > c->d.max_seqs) { set_error("sequence count outside 1..max_seqs"); return ERR_ARGUMENT; }
+    DeviceGuard g(c->device);
+    RC(ready(c));
+    // validate everything before any device work: a rejected call leaves every state as it was
+    std::set<const laya_decoder_state*> seen;
+    int n_snap = 0, longest = 0;
+    long long T = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        const laya_decoder_state* st = states[s];
+        if (!st || st->dec != c) { set_error("a state is null or belongs to another decoder"); return ERR_ARGUMENT; }
+        if (!seen.insert(st).second) { set_error("two sequences continue the same state"); return ERR_ARGUMENT; }
+        if (seq_len[s] <= 0) { set_error("every sequence needs at least one token"); return ERR_ARGUMENT; }
+        if (static_cast<long long>(st->length) + seq_len[s] > INT32_MAX / 2) { set_error("state too long"); return ERR_ARGUMENT; }
+        const int n = n_checkpoints ? n_checkpoints[s] : 0;
+        if (n < 0 || (n > 0 && (!checkpoints || !snapshots))) { set_error("invalid checkpoint list"); return ERR_ARGUMENT; }
+        for (int k = 0; k < n; ++k) {
+            const int cp = checkpoints[n_snap + k];
+            const int prev = k ? checkpoints[n_snap + k - 1] : 0;
+            if (cp <= prev || cp > seq_len[s]) { set_error("checkpoints must ascend strictly within 1..seq_len"); return ERR_ARGUMENT; }
+        }
+        n_snap += n;
+        T += seq_len[s];
+        longest = std::max(longest, st->length + seq_len[s]);
+    }
+    if (T > c->d.max_tokens) { set_error("more tokens than max_tokens"); return ERR_ARGUMENT; }
+    for (long long t = 0; t < T; ++t)
+        if (ids[t] < 0 || ids[t] >= c->d.vocab) { set_error("token id outside the vocabulary"); return ERR_OUT_OF_RANGE; }
+    for (int l = 0; l < n_labels; ++l)
+        if (!label_ids || label_ids[l] < 0 || label_ids[l] >= c->d.vocab) { set_error("label id outside the vocabulary"); return ERR_OUT_OF_RANGE; }
+
+    for (int s = 0; s < n_seq; ++s) RC(state_grow(c, states[s], states[s]->length + seq_len[s]));
+    if (n_full_layers(c) > 0) RC(ensure_rope(c, longest));
+    std::vector<laya_decoder_state*> snaps;
+    auto fail = [&](int rc) {
+        for (laya_decoder_state* x : snaps) state_free(x);
+        return rc;
+    };
+    for (int s = 0, k0 = 0; s < n_seq; ++s) {
+        const int n = n_checkpoints ? n_checkpoints[s] : 0;
+        for (int k = 0; k < n; ++k) {
+            laya_decoder_state* x = nullptr;
+            const int rc = state_new(c, states[s]->length + checkpoints[k0 + k], &x);
+            if (rc != OK) return fail(rc);
+            snaps.push_back(x);
+        }
+        k0 += n;
+    }
+    StateView sv;
+    sv.states = states;
+    sv.n_cp = n_checkpoints;
+    sv.cps = checkpoints;
+    sv.snaps = snaps.data();
+    sv.n_snap = n_snap;
+    int Ti = 0;
+    long long pairs = 0;
+    int rc = stage(c, ids, seq_len, n_seq, label_ids, n_labels, &Ti, &pairs, &sv);
+    const size_t nl = static_cast<size_t>(n_seq) * n_labels;
+    if (rc == OK) rc = ensure_logits(c, nl);
+    if (rc == OK) rc = forward_body(c, Ti, n_seq, pairs, n_labels, nullptr, logits && n_labels ? c->logit_buf : nullptr);
+    c->with_states = false;
+    c->cur_snaps = 0;
+    // snapshots take their sequence's keys and values up to the checkpoint (SnapshotKeysAndValues, :734-749)
+    const size_t row = sizeof(__half) * static_cast<size_t>(c->d.kv_heads) * c->d.head_dim;
+    for (int s = 0, k0 = 0; s < n_seq && rc == OK; ++s) {
+        const int n = n_checkpoints ? n_checkpoints[s] : 0;
+        for (int k = 0; k < n && rc == OK; ++k) {
+            laya_decoder_state* x = snaps[k0 + k];
+            const size_t len = static_cast<size_t>(states[s]->length) + checkpoints[k0 + k];
+            for (int i = 0; i < c->d.layers && rc == OK; ++i) {
+                if (c->kinds[i] != LAYA_DECODER_FULL) continue;
+                cudaError_t e = cudaMemcpyAsync(x->k[i], states[s]->k[i], row * len, cudaMemcpyDeviceToDevice, c->stream);
+                if (e == cudaSuccess) e = cudaMemcpyAsync(x->v[i], states[s]->v[i], row * len, cudaMemcpyDeviceToDevice, c->stream);
+                if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync");
+            }
+            x->length = static_cast<int>(len);
+        }
+        k0 += n;
+    }
+    if (rc == OK && hidden) {
+        cudaError_t e = cudaMemcpyAsync(hidden, c->hid, static_cast<size_t>(n_seq) * c->d.hidden * sizeof(float),
+                                        cudaMemcpyDeviceToHost, c->stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync");
+    }
+    if (rc == OK && logits && n_labels) {
+        cudaError_t e = cudaMemcpyAsync(logits, c->logit_buf, nl * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpyAsync");
+    }
+    if (rc == OK) rc = check_device_error(c);
+    if (rc != OK) return fail(rc);
+    for (int s = 0; s < n_seq; ++s) states[s]->length += seq_len[s];
+    for (int k = 0; k < n_snap; ++k) snapshots[k] = snaps[k];
     if (c->profiling) RC(collect_profile(c));
     return OK;
 }

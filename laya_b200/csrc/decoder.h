@@ -2,6 +2,11 @@
 //
 // Token layout: the rows of all sequences of one forward packed back to back (T rows); seq_start / seq_len give each
 // sequence's rows and tok_seq the sequence of every row.  Every activation is row-major [T, width] fp32 unless noted.
+// A sequence may continue a state: pos0[s] tokens already read, whose keys and values sit in the state's caches
+// (kc / vc [positions, kv·hd] fp16), conv tail (tails [K−1, cd]) and delta-rule state (rec [vh, dk, dv]).  Pointer
+// tables are device arrays with one entry per sequence (an entry of 0: no state — zero history, nothing kept).
+// Snapshots: snap_begin [n_seq + 1] delimits each sequence's checkpoints snap_at (token counts of its read,
+// ascending), and the snapshot states' tails / rec receive the state after that many tokens.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -30,7 +35,17 @@ struct ConvArgs {
     const float* in; int ld_in;
     const float* w;
     const int32_t* tok_seq; const int32_t* seq_start;
+    float* const* tails;   // per sequence (may be null): its history before the first row
     float* out;   // [T, cd]
+};
+
+// After the conv: each snapshot's tail and then each state's own tail (the last K−1 pre-conv rows of its history).
+struct ConvStateArgs {
+    int n_seq, cd, K;
+    const float* in; int ld_in;
+    const int32_t* seq_start; const int32_t* seq_len;
+    float* const* tails;
+    const int32_t* snap_begin; const int32_t* snap_at; float* const* snap_tails;
 };
 
 // In place on conv [T, cd] = [q (kh·dk) | k (kh·dk) | v]: L2 norm of every q head (· qscale) and k head; β and the
@@ -51,6 +66,8 @@ struct DeltaArgs {
     const float* beta; const float* decay;
     const int32_t* seq_start; const int32_t* seq_len;
     float* out; int ld_out;
+    float* const* rec;   // per sequence (may be null): initial state in, final state out
+    const int32_t* snap_begin; const int32_t* snap_at; float* const* snap_rec;   // may be null
 };
 
 // RmsNormGated per (row, value head): weight · rmsnorm(core) · silu(z).
@@ -70,16 +87,18 @@ struct PrepArgs {
     const float* qnorm; const float* knorm;   // 1 + weight
     float eps;
     const float* cosv; const float* sinv;     // [positions, half]
-    const int32_t* tok_seq; const int32_t* seq_start;
-    __half* q16; __half* k16; __half* v16;    // [T, heads·hd], [T, kv·hd], [T, kv·hd]
+    const int32_t* tok_seq; const int32_t* seq_start; const int32_t* pos0;
+    __half* q16;                              // [T, heads·hd]
+    __half* const* kc; __half* const* vc;     // per sequence: rows at positions pos0 + (t − seq_start)
 };
 
 // Causal GQA attention over 64-query tiles (tile_seq, tile_p0), output · sigmoid(gate) into out [T, ld_out].
 struct AttnArgs {
     int heads, kv_heads;
-    const __half* q16; const __half* k16; const __half* v16;
+    const __half* q16;
+    __half* const* kc; __half* const* vc;   // per sequence: keys and values of positions [0, pos0 + seq_len)
     const int32_t* tile_seq; const int32_t* tile_p0;
-    const int32_t* seq_start; const int32_t* seq_len;
+    const int32_t* seq_start; const int32_t* seq_len; const int32_t* pos0;
     float scale;
     const float* qkv; int ld_qkv;   // the gates
     float* out; int ld_out;
@@ -102,6 +121,7 @@ int dec_rms_q8(const dec::RmsArgs& a, cudaStream_t s);
 int dec_embed(const int32_t* ids, int T, int n, int vocab, const q8::code_t* q, const float* d, int ldd, float* x,
               int* err, cudaStream_t s);
 int dec_conv_silu(const dec::ConvArgs& a, cudaStream_t s);
+int dec_conv_state(const dec::ConvStateArgs& a, cudaStream_t s);
 int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s);
 int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
 int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);

@@ -90,9 +90,14 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, int T, int n, int 
 }
 
 // ------------------------------------------------------------------------------------------------ DeltaNet
-// conv[t, c] = silu(Σ_j w[j, c] · in[t − (K−1) + j, c]) over taps inside t's sequence (zero history before it).
+// conv[t, c] = silu(Σ_j w[j, c] · in[t − (K−1) + j, c]) over t's sequence history: its rows, preceded by the K−1 rows
+// of its state's conv tail (zero without a state).
 // Thread = one channel over a run of CONV_RUN consecutive tokens: each input is read once (coalesced across
-// channels) and the last K−1 inputs ride along in registers; taps before the token's sequence start count as zero.
+// channels) and the last K−1 inputs ride along in registers; taps before the token's sequence start read the tail.
+DEVI float conv_history(const ConvArgs& a, int seq, int before, int c) {   // before ∈ [−(K−1), −1]
+    const float* tail = a.tails ? a.tails[seq] : nullptr;
+    return tail ? tail[static_cast<size_t>(a.K - 1 + before) * a.cd + c] : 0.0f;
+}
 constexpr int CONV_RUN = 32;
 template <int K>
 __global__ void __launch_bounds__(256) conv_silu_kernel(ConvArgs a) {
@@ -110,12 +115,13 @@ __global__ void __launch_bounds__(256) conv_silu_kernel(ConvArgs a) {
     }
     for (int t = t0; t < t1; ++t) {
         h[K - 1] = a.in[static_cast<size_t>(t) * a.ld_in + c];
-        const int s0 = a.seq_start[a.tok_seq[t]];
+        const int seq = a.tok_seq[t];
+        const int s0 = a.seq_start[seq];
         float sum = 0.0f;
 #pragma unroll
         for (int j = 0; j < K; ++j) {
             const int src = t - (K - 1) + j;
-            sum = __fadd_rn(sum, __fmul_rn(w[j], src >= s0 ? h[j] : 0.0f));
+            sum = __fadd_rn(sum, __fmul_rn(w[j], src >= s0 ? h[j] : conv_history(a, seq, src - s0, c)));
         }
         a.out[static_cast<size_t>(t) * a.cd + c] = ref_silu(sum);
 #pragma unroll
@@ -127,14 +133,37 @@ __global__ void conv_silu_any_kernel(ConvArgs a) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<size_t>(a.T) * a.cd) return;
     const int t = static_cast<int>(i / a.cd), c = static_cast<int>(i % a.cd);
-    const int s0 = a.seq_start[a.tok_seq[t]];
+    const int seq = a.tok_seq[t];
+    const int s0 = a.seq_start[seq];
     float sum = 0.0f;
     for (int j = 0; j < a.K; ++j) {
         const int src = t - (a.K - 1) + j;
-        const float h = src >= s0 ? a.in[static_cast<size_t>(src) * a.ld_in + c] : 0.0f;
+        const float h = src >= s0 ? a.in[static_cast<size_t>(src) * a.ld_in + c] : conv_history(a, seq, src - s0, c);
         sum = __fadd_rn(sum, __fmul_rn(a.w[static_cast<size_t>(j) * a.cd + c], h));
     }
     a.out[i] = ref_silu(sum);
+}
+
+// Thread = (sequence, channel): the snapshots' tails (history rows [cp − (K−1), cp) of the read), then the state's own
+// tail (rows [L − (K−1), L)), history row r < 0 being row K−1+r of the old tail.  The own tail is rewritten in place in
+// ascending order: row j reads old row L + j > j, not yet overwritten (Qwen35Model.cs:814-830).
+__global__ void __launch_bounds__(256) conv_state_kernel(ConvStateArgs a) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, seq = blockIdx.y;
+    if (c >= a.cd) return;
+    float* tail = a.tails[seq];
+    if (!tail) return;
+    const int s0 = a.seq_start[seq], L = a.seq_len[seq], keep = a.K - 1;
+    auto hist = [&](int r) {
+        return r >= 0 ? a.in[static_cast<size_t>(s0 + r) * a.ld_in + c] : tail[static_cast<size_t>(keep + r) * a.cd + c];
+    };
+    if (a.snap_begin) {
+        for (int k = a.snap_begin[seq]; k < a.snap_begin[seq + 1]; ++k) {
+            float* dst = a.snap_tails[k];
+            const int cp = a.snap_at[k];
+            for (int j = 0; j < keep; ++j) dst[static_cast<size_t>(j) * a.cd + c] = hist(cp - keep + j);
+        }
+    }
+    for (int j = 0; j < keep; ++j) tail[static_cast<size_t>(j) * a.cd + c] = hist(L - keep + j);
 }
 
 // One octet per (token, key head, q|k): L2Normalize (DecoderKernels.cs:67-85); plus β and g per value head.
@@ -174,9 +203,11 @@ __global__ void __launch_bounds__(256) deltanet_heads_kernel(HeadsArgs a) {
 // The gated delta rule of one (sequence, value head).  Thread j < dv owns state column S[:, j] (DK registers).
 // The CTA stages q, k, v, β and the decay of CH tokens (plus the next token's k and decay) in shared memory with
 // cp.async, double-buffered: the next chunk loads while this one runs, so a token's step waits on no global load.
-//   token 0:    S ← S·g_0;  m = Sᵀk_0
+//   token 0:    S ← S·g_0;  m = Sᵀk_0            (S: the sequence's state, or zero)
 //   token t:    δ = (v_t − m)·β_t;  for i: x = S_i + δ·k_t,i (fma);  o += x·q_t,i (fma);  S_i = x·g_{t+1};
 //               m' += S_i·k_{t+1},i (fma)          (the last token skips the decay and the next read)
+// A checkpoint after token t splits that fused step into the same operations in the same order: the update, the copy
+// of S to the snapshot, then the next token's decay and read.  The final S goes back to the state.
 DEVI void cp16(float* dst, const float* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
                  : "memory");
@@ -233,9 +264,15 @@ __global__ void __launch_bounds__(128) delta_rule_kernel(DeltaArgs a) {
         cp_commit();
     };
 
+    const size_t head_off = static_cast<size_t>(h) * DK * a.dv;
+    float* rec = a.rec ? a.rec[seq] : nullptr;
     float s[DK];
 #pragma unroll
-    for (int i = 0; i < DK; ++i) s[i] = 0.0f;
+    for (int i = 0; i < DK; ++i) s[i] = (rec && act) ? rec[head_off + static_cast<size_t>(i) * a.dv + j] : 0.0f;
+    int sk = a.snap_begin ? a.snap_begin[seq] : 0;
+    const int se = a.snap_begin ? a.snap_begin[seq + 1] : 0;
+    int next_cp = sk < se ? a.snap_at[sk] : -1;   // token count of the next checkpoint
+    int stop = next_cp > 0 ? next_cp : L;          // the fused step runs while t + 1 < stop
     float m = 0.0f;
     issue(0, rsm);
     for (int c = 0; c < nch; ++c) {
@@ -267,7 +304,7 @@ __global__ void __launch_bounds__(128) delta_rule_kernel(DeltaArgs a) {
             float o = 0.0f;
             // Every warp reads the same q and k values (shared-memory broadcasts, one 4-byte value per wavefront):
             // with 4 warps that is 3·DK·4 wavefronts per token, which bounds this exact sequential form.
-            if (t + 1 < L) {
+            if (t + 1 < stop) {
                 const float g = cur[SM::G + r + 1];
                 const float* kn = kr + DK;
                 float mn = 0.0f;
@@ -287,10 +324,35 @@ __global__ void __launch_bounds__(128) delta_rule_kernel(DeltaArgs a) {
                     o = __fmaf_rn(x, qr[i], o);
                     s[i] = x;
                 }
+                if (t + 1 == next_cp) {   // the same for every thread of the CTA
+                    float* dst = a.snap_rec[sk] + head_off;
+                    if (act) {
+#pragma unroll
+                        for (int i = 0; i < DK; ++i) dst[static_cast<size_t>(i) * a.dv + j] = s[i];
+                    }
+                    ++sk;
+                    next_cp = sk < se ? a.snap_at[sk] : -1;
+                    stop = next_cp > 0 ? next_cp : L;
+                    if (t + 1 < L) {   // the next token's decay and read (staged: k and g of row r + 1 ≤ CH)
+                        const float g = cur[SM::G + r + 1];
+                        const float* kn = kr + DK;
+                        float mn = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < DK; ++i) {
+                            s[i] = __fmul_rn(s[i], g);
+                            mn = __fmaf_rn(s[i], kn[i], mn);
+                        }
+                        m = mn;
+                    }
+                }
             }
             if (act) a.out[static_cast<size_t>(s0 + t) * a.ld_out + h * a.dv + j] = o;
         }
         __syncthreads();
+    }
+    if (rec && act) {
+#pragma unroll
+        for (int i = 0; i < DK; ++i) rec[head_off + static_cast<size_t>(i) * a.dv + j] = s[i];
     }
 }
 
@@ -335,9 +397,10 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepArgs a) {
     float* buf = sh + (warp * 4 + oct) * a.hd;
     for (int i = l; i < a.hd; i += 8) buf[i] = __fmul_rn(__fmul_rn(src[i], inv), sc[i]);
     __syncwarp();
-    const int pos = t - a.seq_start[a.tok_seq[t]];
-    __half* dst = isq ? a.q16 + static_cast<size_t>(t) * a.heads * a.hd + h * a.hd
-                      : a.k16 + static_cast<size_t>(t) * a.kv_heads * a.hd + h * a.hd;
+    const int seq = a.tok_seq[t];
+    const int pos = a.pos0[seq] + t - a.seq_start[seq];
+    const size_t kv_row = static_cast<size_t>(pos) * a.kv_heads * a.hd + h * a.hd;
+    __half* dst = isq ? a.q16 + static_cast<size_t>(t) * a.heads * a.hd + h * a.hd : a.kc[seq] + kv_row;
     if (active) {
         for (int i = l; i < a.hd; i += 8) {
             float y = buf[i];
@@ -351,7 +414,7 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(PrepArgs a) {
         }
         if (!isq) {
             const float* vs = a.qkv + static_cast<size_t>(t) * a.ld_qkv + a.q_width + a.kv_heads * a.hd + h * a.hd;
-            __half* vd = a.v16 + static_cast<size_t>(t) * a.kv_heads * a.hd + h * a.hd;
+            __half* vd = a.vc[seq] + kv_row;
             for (int i = l; i < a.hd; i += 8) vd[i] = __float2half_rn(vs[i]);
         }
     }
@@ -388,19 +451,20 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     const int tile = blockIdx.x;
     const int head = blockIdx.y, kvh = head / (a.heads / a.kv_heads);
     const int seq = a.tile_seq[tile], q0 = a.tile_p0[tile];
-    const int s0 = a.seq_start[seq], L = a.seq_len[seq];
+    const int s0 = a.seq_start[seq], L = a.seq_len[seq], P = a.pos0[seq];   // queries: positions P + [0, L)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const int ldq = a.heads * HD, ldkv = a.kv_heads * HD;
-    auto load = [&](__half* dst, const __half* src, int ld, int p0) {
+    // rows p0 .. p0+63 of src (row stride ld), those < limit; the rest zero
+    auto load = [&](__half* dst, const __half* src, int ld, int p0, int limit) {
         constexpr int CH = HD / 8;
         for (int e = threadIdx.x; e < T64 * CH; e += blockDim.x) {
             const int r = e / CH, c = e % CH;
             uint4 v = make_uint4(0, 0, 0, 0);
-            if (p0 + r < L) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(s0 + p0 + r) * ld + c * 8);
+            if (p0 + r < limit) v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(p0 + r) * ld + c * 8);
             *reinterpret_cast<uint4*>(dst + r * LDS + c * 8) = v;
         }
     };
-    load(Qs, a.q16 + head * HD, ldq, q0);
+    load(Qs, a.q16 + static_cast<size_t>(s0) * ldq + head * HD, ldq, q0, L);
     __syncthreads();
     uint32_t fq[KS][4];
     {
@@ -413,12 +477,16 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};
-    const int ke = min(L, q0 + T64);   // causal: keys up to the tile's last query
+    const int qp[2] = {q0 + warp * 16 + g, q0 + warp * 16 + g + 8};   // rows of the read
+    const int ke = P + min(L, q0 + T64);   // causal: key positions up to the tile's last query
+    const __half* kbase = a.kc[seq] + kvh * HD;
+    const __half* vbase = a.vc[seq] + kvh * HD;
+    // Key tiles start at position 0 whatever P is, so a row's softmax runs over the same tiles in the same order as
+    // when its sequence is read in one pass (tiles past the row are fully masked and change nothing).
     for (int k0 = 0; k0 < ke; k0 += T64) {
         __syncthreads();
-        load(Ks, a.k16 + kvh * HD, ldkv, k0);
-        load(Vs, a.v16 + kvh * HD, ldkv, k0);
+        load(Ks, kbase, ldkv, k0, P + L);
+        load(Vs, vbase, ldkv, k0, P + L);
         __syncthreads();
         float s[8][4];
 #pragma unroll
@@ -442,7 +510,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
             for (int e = 0; e < 4; ++e) {
                 const int kp = k0 + 8 * j + 2 * t4 + (e & 1);
                 const int q = qp[e >> 1];
-                const float v = (kp <= q && kp < L && q < L) ? __fmul_rn(s[j][e], a.scale) : -INFINITY;
+                const float v = (kp <= P + q && q < L) ? __fmul_rn(s[j][e], a.scale) : -INFINITY;
                 s[j][e] = v;
                 mx[e >> 1] = fmaxf(mx[e >> 1], v);
             }
@@ -580,6 +648,11 @@ int dec_conv_silu(const dec::ConvArgs& a, cudaStream_t s) {
         case 4: dec::conv_silu_kernel<4><<<grid, 256, 0, s>>>(a); break;
         default: dec::conv_silu_any_kernel<<<nblk(static_cast<size_t>(a.T) * a.cd, 256), 256, 0, s>>>(a); break;
     }
+    DEC_LAUNCHED();
+}
+int dec_conv_state(const dec::ConvStateArgs& a, cudaStream_t s) {
+    if (a.n_seq <= 0 || a.K < 2) return OK;
+    dec::conv_state_kernel<<<dim3((a.cd + 255) / 256, a.n_seq), 256, 0, s>>>(a);
     DEC_LAUNCHED();
 }
 int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s) {

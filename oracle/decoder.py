@@ -103,8 +103,52 @@ def _sigmoid_scalar(x):
     return (np.float32(1) / (np.float32(1) + np.exp(-x))).astype(np.float32)
 
 
+class OracleState:
+    """Qwen35State (Qwen35Model.cs:38-197): what the decoder remembers of the tokens it has read — keys and values of
+    every full-attention layer (normed and rotated, fp32), the conv tail (the last kernel − 1 pre-convolution rows)
+    and the delta-rule state [value heads, dk, dv] of every DeltaNet layer, and the token count."""
+
+    def __init__(self, cfg: "DecoderConfig"):
+        self.length = 0
+        self.keys, self.values, self.tail, self.rec = {}, {}, {}, {}
+        for i, kind in enumerate(cfg.kinds):
+            if kind == "full":
+                self.keys[i] = np.zeros((0, cfg.kv_heads, cfg.head_dim), np.float32)
+                self.values[i] = np.zeros((0, cfg.kv_heads, cfg.head_dim), np.float32)
+            else:
+                self.tail[i] = np.zeros((cfg.conv_kernel - 1, cfg.conv_dim), np.float32)
+                self.rec[i] = np.zeros((cfg.lin_v_heads, cfg.lin_dk, cfg.lin_dv), np.float32)
+
+    def clone(self):
+        """Clone (:112-117): an independent copy."""
+        o = OracleState.__new__(OracleState)
+        o.length = self.length
+        o.keys = {i: a.copy() for i, a in self.keys.items()}
+        o.values = {i: a.copy() for i, a in self.values.items()}
+        o.tail = {i: a.copy() for i, a in self.tail.items()}
+        o.rec = {i: a.copy() for i, a in self.rec.items()}
+        return o
+
+    def save(self):
+        """Save (:127-131): the length and copies of the conv tails and recurrent states (keys and values stay)."""
+        return (self.length, {i: a.copy() for i, a in self.tail.items()}, {i: a.copy() for i, a in self.rec.items()})
+
+    def rewind(self, mark):
+        """Rewind (:134-143): back to a saved point of this state; a mark cannot advance it."""
+        length, tail, rec = mark
+        if length > self.length:
+            raise ValueError("a mark can only rewind, not advance")
+        for i in self.tail:
+            self.tail[i] = tail[i].copy()
+            self.rec[i] = rec[i].copy()
+        for i in self.keys:
+            self.keys[i] = self.keys[i][:length].copy()
+            self.values[i] = self.values[i][:length].copy()
+        self.length = length
+
+
 class OracleDecoder:
-    """Qwen35Model forward over one sequence (fp32 or Q8_0 products)."""
+    """Qwen35Model forward over one sequence (fp32 or Q8_0 products), from an empty state or continuing one."""
 
     def __init__(self, cfg: DecoderConfig, weights: Dict[str, np.ndarray], precision: str = "f32",
                  q8: Optional[Dict[str, tuple]] = None, prefix: str = "model."):
@@ -169,7 +213,9 @@ class OracleDecoder:
         return np.array([dot(h[0], table[i]) for i in ids], np.float32)
 
     # ---------------------------------------------------------------------------------------------- layers
-    def full_attention(self, i, x):
+    def full_attention(self, i, x, state=None, checkpoints=(), snapshots=()):
+        """Each row's key and value join the state's cache (positions continue from its length); every row attends
+        to the cache up to itself.  Snapshots take the keys and values up to their checkpoint (:734-749)."""
         c = self.cfg
         p = f"layers.{i}.self_attn."
         T = x.shape[0]
@@ -180,7 +226,8 @@ class OracleDecoder:
         kvw = KV * hd
         half = c.rotary_dim // 2
         qn, kn = self.one_plus(p + "q_norm.weight"), self.one_plus(p + "k_norm.weight")
-        pos = np.arange(T, dtype=np.float32)
+        start = state.length if state is not None else 0
+        pos = np.arange(start, start + T, dtype=np.float32)
         ang = (pos[:, None] * self.inv_freq[None, :]).astype(np.float32)
         cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
         q = np.empty((T, H, hd), np.float32)
@@ -194,6 +241,12 @@ class OracleDecoder:
             a, b = arr[..., :half].copy(), arr[..., half:2 * half].copy()
             arr[..., :half] = a * cos[:, None, :] - b * sin[:, None, :]
             arr[..., half:2 * half] = b * cos[:, None, :] + a * sin[:, None, :]
+        if state is not None:
+            k = np.concatenate([state.keys[i][:start], k], 0)
+            v = np.concatenate([state.values[i][:start], v], 0)
+            state.keys[i], state.values[i] = k, v
+            for cp, snap in zip(checkpoints, snapshots):
+                snap.keys[i], snap.values[i] = k[:start + cp].copy(), v[:start + cp].copy()
         scale = np.float32(1) / np.float32(math.sqrt(hd))
         out = np.zeros((T, H, hd), np.float32)
         groups = H // KV
@@ -201,21 +254,24 @@ class OracleDecoder:
         for h in range(H):
             kh = h // groups
             for t in range(T):
-                s = np.array([dot(q[t, h], k[j, kh]) for j in range(t + 1)], np.float32) * scale
+                at = start + t
+                s = np.array([dot(q[t, h], k[j, kh]) for j in range(at + 1)], np.float32) * scale
                 e = np.exp(s - s.max()).astype(np.float32)
                 tot = np.float32(0)
                 for val in e:
                     tot = np.float32(tot + val)
                 inv = np.float32(1) / tot
                 o = np.zeros(hd, np.float32)
-                for j in range(t + 1):
+                for j in range(at + 1):
                     o = (np.float64(e[j] * inv) * v[j, kh].astype(np.float64) + o).astype(np.float32)
                 out[t, h] = o
         out = out.reshape(T, H * hd)
         self.L.lo_multiply_sigmoid(out.reshape(-1), f32(g.reshape(T, H * hd)).reshape(-1), out.size)
         return self.proj(out, [p + "o_proj.weight"])
 
-    def linear_attention(self, i, x):
+    def linear_attention(self, i, x, state=None, checkpoints=(), snapshots=()):
+        """The conv reads the state's tail before the rows and the recurrence continues its state; both are advanced.
+        A checkpoint splits the recurrence there and copies the tail and the state out (:814-830, :880-895)."""
         c = self.cfg
         p = f"layers.{i}.linear_attn."
         T = x.shape[0]
@@ -226,7 +282,12 @@ class OracleDecoder:
                                   p + "in_proj_a.weight"])
         wconv = self.W(p + "conv1d.weight").reshape(cd, c.conv_kernel)     # [channel, tap]
         K = c.conv_kernel
-        hist = np.concatenate([np.zeros((K - 1, cd), np.float32), proj[:, :cd]], 0)
+        prev = state.tail[i] if state is not None else np.zeros((K - 1, cd), np.float32)
+        hist = np.concatenate([prev, proj[:, :cd]], 0)
+        if state is not None:
+            for cp, snap in zip(checkpoints, snapshots):
+                snap.tail[i] = hist[cp:cp + K - 1].copy()
+            state.tail[i] = hist[T:T + K - 1].copy()
         conv = np.zeros((T, cd), np.float32)
         for j in range(K):                                                   # taps in order, multiply then add
             conv = (conv + (wconv[:, j][None, :] * hist[j:j + T])).astype(np.float32)
@@ -252,13 +313,25 @@ class OracleDecoder:
         flat = conv.reshape(-1)
         beta = f32(beta)
         g = f32(g)
+        gf, bf = g.reshape(-1), beta.reshape(-1)
         for h in range(VH):
             kh = h // ratio
-            state = np.zeros((dk, dv), np.float32)
+            S = state.rec[i][h].copy() if state is not None else np.zeros((dk, dv), np.float32)
             tmp = np.zeros(T * vd, np.float32)
-            self.L.lo_delta_rule(state, dk, dv, T, f32(flat[kh * dk:]), f32(flat[kd + kh * dk:]),
-                                 f32(flat[2 * kd + h * dv:]), cd, f32(g.reshape(-1)[h:]), f32(beta.reshape(-1)[h:]),
-                                 VH, tmp, vd)
+            done = 0
+            for until, snap in list(zip(checkpoints, snapshots)) + [(T, None)]:
+                if until > done:
+                    o0 = done * cd
+                    seg = np.zeros((until - done) * vd, np.float32)
+                    self.L.lo_delta_rule(S, dk, dv, until - done, f32(flat[o0 + kh * dk:]), f32(flat[o0 + kd + kh * dk:]),
+                                         f32(flat[o0 + 2 * kd + h * dv:]), cd, f32(gf[done * VH + h:]),
+                                         f32(bf[done * VH + h:]), VH, seg, vd)
+                    tmp[done * vd:until * vd] = seg
+                    done = until
+                if snap is not None:
+                    snap.rec[i][h] = S
+            if state is not None:
+                state.rec[i][h] = S
             core[:, h * dv:(h + 1) * dv] = tmp.reshape(T, vd)[:, :dv]
         z = proj[:, cd:cd + vd]
         wn = self.W(p + "norm.weight")
@@ -278,26 +351,43 @@ class OracleDecoder:
         self.L.lo_silu_multiply(f32(gu), T, I, act)
         return self.proj(act, [f"layers.{i}.mlp.down_proj.weight"])
 
-    def layer(self, i, x):
+    def layer(self, i, x, state=None, checkpoints=(), snapshots=()):
         """One decoder layer: (mixer output, layer output) — Forward's loop body (Qwen35Model.cs:485-500)."""
-        mixer = self.full_attention(i, x) if self.cfg.kinds[i] == "full" else self.linear_attention(i, x)
+        mix = self.full_attention if self.cfg.kinds[i] == "full" else self.linear_attention
+        mixer = mix(i, x, state, checkpoints, snapshots)
         x = (x + mixer).astype(np.float32)
         x = (x + self.mlp(i, x)).astype(np.float32)
         return mixer, x
 
-    def forward(self, ids, record: bool = True):
-        """Returns (states by the reference's recorder names, the final-normed last hidden state)."""
+    def new_state(self):
+        """NewState (Qwen35Model.cs:419): a state that has read nothing."""
+        return OracleState(self.cfg)
+
+    def forward(self, ids, record: bool = True, state: Optional[OracleState] = None, checkpoints=()):
+        """Returns (states by the reference's recorder names, the final-normed last hidden state).  With `state`, the
+        tokens are read after what it holds and it is advanced; `checkpoints` (token counts 1..len(ids), ascending)
+        add a third result, one new state per checkpoint (Qwen35Sequence.Checkpoints / Snapshots, :214-221)."""
         ids = np.asarray(ids, np.int64)
+        if checkpoints and state is None:
+            state = self.new_state()
+        snapshots = [self.new_state() for _ in checkpoints]
+        start = state.length if state is not None else 0
         x = self.embed(ids)
         states = {"embeddings": x.copy()} if record else {}
         for i in range(self.cfg.layers):
-            mixer, x = self.layer(i, x)
+            mixer, x = self.layer(i, x, state, tuple(checkpoints), snapshots)
             if record:
                 states[f"layers.{i}.mixer"] = mixer
                 states[f"layers.{i}"] = x.copy()
+        if state is not None:
+            state.length = start + len(ids)
+            for cp, snap in zip(checkpoints, snapshots):
+                snap.length = start + cp
         normed = self.rms(x, "norm.weight")
         if record:
             states["norm"] = normed
+        if checkpoints:
+            return states, normed[-1].copy(), snapshots
         return states, normed[-1].copy()
 
 

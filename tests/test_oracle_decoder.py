@@ -94,3 +94,54 @@ def test_delta_rule_is_the_two_sweep_recurrence(oracle_lib):
                 o = (o + S[i] * q[t, i]).astype(np.float32)
         np.testing.assert_allclose(out[t], o, rtol=0 if hasattr(math, "fma") else 1e-6, atol=0 if hasattr(math, "fma") else 1e-6)
     np.testing.assert_allclose(state, S, rtol=0 if hasattr(math, "fma") else 1e-6, atol=0 if hasattr(math, "fma") else 1e-6)
+
+
+def test_reading_in_pieces_is_exactly_reading_at_once(tiny):
+    """Qwen35ParityTests.ReadingInPiecesIsExactlyReadingAtOnce (:139-157), on the oracle's state."""
+    from oracle.decoder import OracleDecoder
+    cfg, w, ids, _, _ = tiny
+    m = OracleDecoder(cfg, w, precision="q8_0")
+    _, once = m.forward(ids, record=False)
+    state = m.new_state()
+    m.forward(ids[:61], record=False, state=state)
+    branch = state.clone()
+    m.forward(ids[61:101], record=False, state=state)
+    _, pieces = m.forward(ids[101:], record=False, state=state)
+    assert np.array_equal(once, pieces) and state.length == len(ids)
+    assert branch.length == 61
+    _, again = m.forward(ids[61:], record=False, state=branch)
+    assert np.array_equal(once, again)
+
+
+def test_rewinding_to_a_mark_reads_the_same_as_a_fresh_state(tiny):
+    """Qwen35StateTests.RewindingToAMarkReadsTheSameAsAFreshState (:176-196)."""
+    from oracle.decoder import OracleDecoder
+    cfg, w, _, _, _ = tiny
+    m = OracleDecoder(cfg, w)
+    prefix = [(i * 37) % 128 for i in range(70)]
+    a, b = [5, 9, 11, 100], [7, 7, 7, 7, 7, 7, 1]
+    state = m.new_state()
+    m.forward(prefix, record=False, state=state)
+    mark = state.save()
+    _, first = m.forward(a, record=False, state=state)
+    state.rewind(mark)
+    _, second = m.forward(b, record=False, state=state)
+    assert np.array_equal(m.forward(prefix + a, record=False)[1], first)
+    assert np.array_equal(m.forward(prefix + b, record=False)[1], second)
+    with pytest.raises(ValueError):
+        m.new_state().rewind(mark)
+
+
+def test_checkpoints_are_the_states_of_shorter_reads(tiny):
+    """Qwen35BatchTests.CheckpointsAreTheStatesOfShorterReads (:233-252)."""
+    from oracle.decoder import OracleDecoder
+    cfg, w, _, _, _ = tiny
+    m = OracleDecoder(cfg, w, precision="q8_0")
+    tokens = [(i * 37 + 5 * 11) % 128 for i in range(60)]
+    rest = [(i * 37 + 6 * 11) % 128 for i in range(9)]
+    _, _, snaps = m.forward(tokens, record=False, state=m.new_state(), checkpoints=[5, 16, 33])
+    for at, snap in zip([5, 16, 33], snaps):
+        assert snap.length == at
+        ref = m.new_state()
+        m.forward(tokens[:at], record=False, state=ref)
+        assert np.array_equal(m.forward(rest, record=False, state=ref)[1], m.forward(rest, record=False, state=snap)[1])
