@@ -1,6 +1,6 @@
 """Throughput of the hot path on B200s — one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|train|q8|decoder]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|train|q8|f32|decoder]
 
 Headline workload (config 3, the data-parallel fine-tune): per GPU 32 ModernBERT-base rows with valid lengths
 U{256..1024} (padding is not work: rows are concatenated), the Laya decision head, the RLCD objective with 4 noise
@@ -19,6 +19,9 @@ every projection and the tied token table in Q8_0, a prefill of 8 rows × 2048 t
 label ids at each row's last position; replicas sharded by request with no collective.  Beside it,
 `mica_shared_prefix`: the same prompts served as one multi-question request whose shared prefix is read once into a
 decoder state and cloned per question (MicaJudge.Predict), the effective prompt tokens/s.
+
+Nested `systemone_f32`: the decision forward's fp32-accurate path (the reference's PackedMatrix products, here split
+bf16 products) on a bf16 checkpoint of ModernBERT-large geometry, config 2's 64 × 512 batch.
 
 `value` is device-resident throughput (inputs staged in HBM before the timed region); `e2e` is the same step through
 the host-pointer C ABI with the step's inputs copied from pinned host memory and its result (the loss; the logits)
@@ -58,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "train", "q8", "decoder"])
+    ap.add_argument("--workload", default="all", choices=["all", "train", "q8", "f32", "decoder"])
     ap.add_argument("--dec-tokens", type=int, default=128, help="tokens of the decoder's CPU sample")
     ap.add_argument("--dec-layers", type=int, default=32, help="decoder layers (fewer only for small captures)")
     ap.add_argument("--forward", default="accurate", choices=["accurate", "bf16"],
@@ -195,6 +198,32 @@ def q8_cpu_baseline(rows):
             "sample": f"{rows} x {SEQ} tokens, one full 22-layer Q8_0 decision forward ({secs:.1f} s)"}
 
 
+def f32_cpu_seconds(tokens, seed=1):
+    """One bounded CPU sample of the fp32 decision forward: the oracle's fp32 restatement (PackedMatrix products)
+    over one row of `tokens` tokens of the ModernBERT-large bf16 checkpoint."""
+    import numpy as np
+    import oracle
+    from laya_b200 import workloads
+    from oracle.model import EncoderConfig, Item, OracleModel
+    oracle.build()
+    w = workloads.bf16_checkpoint_weights(**LARGE, seed=0)
+    om = OracleModel(EncoderConfig(**LARGE), w)
+    items = workloads.decision_batch(rows=1, length=tokens, seed=seed)
+    its = [Item(np.asarray(it.token_ids), list(it.marker_positions), it.type) for it in items]
+    t0 = time.perf_counter()
+    om.forward(its)
+    return time.perf_counter() - t0, oracle.lib().lo_num_threads()
+
+
+F32_CPU_TOKENS = 512
+
+
+def f32_cpu_baseline(tokens=F32_CPU_TOKENS):
+    secs, cores = f32_cpu_seconds(tokens)
+    return {"value": tokens / secs, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 x {tokens} tokens, one full 28-layer fp32 decision forward ({secs:.1f} s)"}
+
+
 def dec_cpu_baseline(tokens, reps=1):
     """A bounded CPU sample of config 5: the oracle's Q8_0 restatement of Qwen35Model.Forward over one row of `tokens`
     ids through one [DeltaNet x3, full] block of the workload's weights, scaled to the 32-layer model (x8)."""
@@ -322,6 +351,17 @@ def run_reference(args):
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                                  "sample": f"{rows} x {SEQ} tokens per step, CPU restatement of the reference path"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    if args.workload == "f32":
+        b = f32_cpu_baseline()
+        line = {"impl": "reference", "metric": "decision forward tokens/s, fp32-accurate path on a bf16 checkpoint",
+                "value": b["value"], "unit": "tokens/s", "n_gpus": world, "steps": 1, "warmup": 0,
+                "ms_per_step": F32_CPU_TOKENS / b["value"] * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "systemone_f32_modernbert_large", "rows_per_gpu": ROWS, "seq_len": SEQ},
+                "cpu_baseline": b,
+                "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
     if args.workload == "decoder":
@@ -539,6 +579,32 @@ def q8_measure(args, d):
                                     w, q8, device=local)
     del w, q8
     items = workloads.decision_batch(rows=ROWS, length=SEQ, seed=1 + rank)
+    return decision_timing(args, d, model, items)
+
+
+LARGE = dict(hidden=1024, intermediate=2624, layers=28, heads=16, vocab=50368)   # ModernBERT-large (config 4)
+
+
+def f32_measure(args, d):
+    """The decision forward's fp32-accurate path (LAYA_PRECISION_F32) on a bf16 checkpoint of ModernBERT-large
+    geometry (the released English / TypedDecisions checkpoints' encoder) with the decision head, config 2's batch."""
+    import laya_b200
+    from laya_b200 import workloads
+    w = workloads.bf16_checkpoint_weights(**LARGE, seed=0)
+    desc = laya_b200.base_desc(max_tokens=TOKENS, max_items=ROWS, max_markers=ROWS * 8,
+                               precision=laya_b200.PRECISION_F32, **LARGE)
+    model = laya_b200.DecisionModel(desc, w, device=d.local)
+    del w
+    items = workloads.decision_batch(rows=ROWS, length=SEQ, seed=1 + d.rank)
+    return decision_timing(args, d, model, items)
+
+
+def decision_timing(args, d, model, items):
+    """Device-resident and host-pointer timings of the batched decision forward over `items`."""
+    import numpy as np
+    import torch
+    import laya_b200
+    local = d.local
     ids, seg_len, qtype, counts, markers = model.pack(items)
     n_mark = int(counts.sum())
     stream = torch.cuda.Stream()
@@ -814,6 +880,38 @@ def run_ours(args):
                 line = q
             else:
                 line["q8_0_encode"] = q
+    if args.workload in ("all", "f32"):
+        r = f32_measure(args, d)
+        ms, e2e_ms = d.reduce([r["ms"], r["e2e_ms"]], MAX)
+        if rank == 0:
+            g_ms, g_ops, g_n = r["gemm"]
+            bf16 = peaks.get("bf16_tflops", 1590.0)
+            H, I, Ls = LARGE["hidden"], LARGE["intermediate"], LARGE["layers"]
+            # two bf16 passes per product (bf16 weights): executed = 2 x algorithmic
+            executed = g_ops / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+            q = {"metric": "decision forward tokens/s, fp32-accurate path on a bf16 checkpoint",
+                 "value": world * TOKENS / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms,
+                 "dtype": "bf16 split (fp32-accurate)", "scaling": "weak",
+                 "config": {"workload": "systemone_f32_modernbert_large", "rows_per_gpu": ROWS, "seq_len": SEQ,
+                            "geometry": f"ModernBERT-large encoder ({Ls} layers, h {H}, 16x64, GeGLU I {I}) + "
+                                        "2 head layers + scorer + act head",
+                            "weights": "bf16 values (a bf16 checkpoint), products x_hi.W + x_lo.W",
+                            "parallelism": f"request-sharded x{world}, no collective"},
+                 "e2e": {"value": world * TOKENS / (e2e_ms / 1e3), "unit": "tokens/s",
+                         "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"], "ms_per_step": e2e_ms},
+                 "roofline": {"kernel": "gemm_bf16_kernel (split product, two passes)", "bound": "tensor",
+                              "achieved": executed / 2, "executed": executed, "peak": bf16, "unit": "TFLOP/s",
+                              "frac": executed / bf16, "peak_source": f"{source} bf16 burst",
+                              "launches": g_n, "share_of_step": g_ms / args.steps / ms},
+                 "gpu_launches": r["launches"], "clocks": r["clocks"]}
+            if not args.no_cpu_baseline:
+                q["cpu_baseline"] = f32_cpu_baseline()
+            if line is None:
+                q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "vs_baseline": None, "data": "synthetic"})
+                line = q
+            else:
+                line["systemone_f32"] = q
     if args.workload in ("all", "decoder"):
         r = dec_measure(args, d)
         ms, e2e_ms, sp_ms = d.reduce([r["ms"], r["e2e_ms"], r["shared"]["ms"]], MAX)

@@ -185,7 +185,8 @@ int laya_gemm_bf16_device(laya_ctx* ctx, int M, int N, int K, const uint16_t* A,
                           int ldb, int b_mn, const float* bias, int epilogue, void* out, int ldo);
 /*
  * The same product with fp32 accuracy from bf16 tensor cores (the fine-tuning forward's products): the caller passes
- * each fp32 operand as hi = bf16(x) and lo = bf16(x - hi) (same layouts), and gets A·Bᵀ + A_lo·Bᵀ + A·B_loᵀ.
+ * each fp32 operand as hi = bf16(x) and lo = bf16(x - hi) (same layouts), and gets A·Bᵀ + A_lo·Bᵀ + A·B_loᵀ; with
+ * B_lo NULL (B exactly bf16, as a bf16 checkpoint's weights are) A·Bᵀ + A_lo·Bᵀ, two passes instead of three.
  * No reference counterpart beyond PackedMatrix.Multiply's fp32 result, which it reproduces to about 2^-16 relative.
  */
 int laya_gemm_bf16_split_device(laya_ctx* ctx, int M, int N, int K, const uint16_t* A, const uint16_t* A_lo, int lda,

@@ -226,7 +226,27 @@ __global__ void __launch_bounds__(128) attention_kernel(Args a) {
         }
     }
 
-    // Normalise, quantize to Q8_0 (two 32-dim blocks per head), store codes and scales.
+    // Normalise, quantize to Q8_0 (two 32-dim blocks per head), store codes and scales — or, without a code buffer,
+    // store the context split into hi/lo bf16 parts for a split product.
+    if (a.q == nullptr) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int qp = qpos[h];
+            if (qp >= L) continue;
+            const float inv = l_run[h] > 0.0f ? 1.0f / l_run[h] : 0.0f;
+            const size_t row = static_cast<size_t>(seg0 + qp) * a.hidden + head * HD;
+#pragma unroll
+            for (int j = 0; j < HD / 8; ++j) {
+                const float v0 = o[j][2 * h] * inv, v1 = o[j][2 * h + 1] * inv;
+                const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
+                const size_t c = row + 8 * j + 2 * t4;
+                *reinterpret_cast<__nv_bfloat162*>(a.hi + c) = __halves2bfloat162(h0, h1);
+                *reinterpret_cast<__nv_bfloat162*>(a.lo + c) =
+                    __floats2bfloat162_rn(__fsub_rn(v0, __bfloat162float(h0)), __fsub_rn(v1, __bfloat162float(h1)));
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int qp = qpos[h];

@@ -94,6 +94,14 @@ struct QWeight {
     bool geglu = false;    // rows stored in [32 input | 32 gate] groups
 };
 
+// A projection of the fp32-accurate path: the weight as hi = bf16(w) and lo = bf16(w − hi), lo dropped when every
+// weight is a bf16 value (a bf16 checkpoint) — the product is then two passes instead of three.
+struct BWeight {
+    __nv_bfloat16* hi = nullptr;
+    __nv_bfloat16* lo = nullptr;
+    int N = 0, K = 0;
+};
+
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 // GeGLU row order: group g of 64 rows = input rows [32g, 32g+32) then gate rows [I + 32g, I + 32g + 32).
@@ -118,6 +126,7 @@ struct laya_ctx {
 
     std::map<std::string, DevBuf> f32;     // fp32 tensors by name (element count = bytes/4)
     std::map<std::string, QWeight> q8;     // Q8_0 projections by name
+    std::map<std::string, BWeight> bw;     // fp32-accurate projections by name (LAYA_PRECISION_F32)
 
     // rotary tables [maxpos, 32]
     int maxpos = 0;
@@ -133,6 +142,9 @@ struct laya_ctx {
     int32_t *seg_start = nullptr, *mk_start = nullptr, *qt_start = nullptr, *qt_item = nullptr, *qt_q0 = nullptr,
             *n_qt = nullptr, *tok_item = nullptr, *marker_row = nullptr, *marker_item = nullptr;
     float *logits = nullptr, *act = nullptr;
+    // LAYA_PRECISION_F32 workspace: activations split into hi/lo bf16 parts, the widest projection output fp32
+    __nv_bfloat16 *xh0 = nullptr, *xl0 = nullptr, *xh1 = nullptr, *xl1 = nullptr;
+    float* wide = nullptr;
 
     // profiling of the Q8_0 products
     bool profiling = false;
@@ -188,8 +200,9 @@ int need_f32(laya_ctx* c, const std::string& name, const float** out) {
     return OK;
 }
 
-bool is_q8_projection(const laya_ctx* c, const std::string& n) {
-    if (c->d.precision != LAYA_PRECISION_Q8_0) return false;
+// The projections the reference runs through PackedMatrix (ModernBertEncoder.Pack, DecisionModel.cs:61-72): Q8_0 in a
+// Q8_0 context, split bf16 in an fp32 one.
+bool is_projection(const std::string& n) {
     if (n.rfind("encoder.layers.", 0) == 0)
         return ends_with(n, "attn.Wqkv.weight") || ends_with(n, "attn.Wo.weight") || ends_with(n, "mlp.Wi.weight") ||
                ends_with(n, "mlp.Wo.weight");
@@ -197,6 +210,9 @@ bool is_q8_projection(const laya_ctx* c, const std::string& n) {
         return ends_with(n, "self_attn.in_proj_weight") || ends_with(n, "self_attn.out_proj.weight") ||
                ends_with(n, "linear1.weight") || ends_with(n, "linear2.weight");
     return false;
+}
+bool is_q8_projection(const laya_ctx* c, const std::string& n) {
+    return c->d.precision == LAYA_PRECISION_Q8_0 && is_projection(n);
 }
 
 int check_device_error(laya_ctx* c) {
@@ -262,6 +278,34 @@ int q8_proj(laya_ctx* c, const std::string& name, const q8::code_t* qx, const fl
     return gemm_profiled(c, a);
 }
 
+// Projection of the fp32-accurate path: out[M, N] (fp32; epi EPI_F32 stores, EPI_F32_ADD adds into out) =
+// (xh + xl) · (Wh + Wl)ᵀ + bias from the split operands (two or three bf16 passes, fp32 accumulation).
+int bf_proj(laya_ctx* c, const std::string& name, const __nv_bfloat16* xh, const __nv_bfloat16* xl, int M,
+            const float* bias, int epi, float* out, int ldo) {
+    auto it = c->bw.find(name);
+    if (it == c->bw.end()) { set_error("missing projection " + name); return ERR_NOT_FOUND; }
+    const BWeight& w = it->second;
+    bf::Args a{};
+    a.M = M; a.N = w.N; a.K = w.K;
+    a.A = xh; a.lda = w.K; a.a_mn = 0;
+    a.B = w.hi; a.ldb = w.K; a.b_mn = 0;
+    a.A2 = xl; a.B2 = w.lo;
+    a.bias = bias; a.epi = epi; a.out = out; a.ldo = ldo; a.err = c->err;
+    if (!c->profiling) return bf::gemm(a, c->stream);
+    if (c->ev_used == c->ev_pool.size()) {
+        cudaEvent_t e0, e1;
+        LAYA_CUDA(cudaEventCreate(&e0));
+        LAYA_CUDA(cudaEventCreate(&e1));
+        c->ev_pool.push_back({e0, e1});
+    }
+    auto& ev = c->ev_pool[c->ev_used++];
+    LAYA_CUDA(cudaEventRecord(ev.first, c->stream));
+    const int rc = bf::gemm(a, c->stream);
+    LAYA_CUDA(cudaEventRecord(ev.second, c->stream));
+    c->ev_ops.push_back(2.0 * M * static_cast<double>(w.N) * w.K);
+    return rc;
+}
+
 int record_copy(laya_ctx* c, const std::string& name, const float* src, size_t count) {
     if (!c->record) return OK;
     DevBuf& b = c->rec[name];
@@ -280,8 +324,71 @@ int record_copy(laya_ctx* c, const std::string& name, const float* src, size_t c
         if (rc_ != OK) return rc_; \
     } while (0)
 
+// One encoder layer of the fp32-accurate path: the same steps as encoder_layer below with split bf16 products.
+int encoder_layer_f32(laya_ctx* c, int i, int T) {
+    const int H = c->d.hidden, I = c->d.intermediate;
+    const std::string p = "encoder.layers." + std::to_string(i) + ".";
+    LnArgs ln{};
+    ln.rows = T; ln.n = H; ln.x = c->h; ln.eps = c->d.norm_eps; ln.err = c->err;
+    ln.w = F(c, p + "attn_norm.weight"); ln.b = F(c, p + "attn_norm.bias");
+    ln.apply_ln = ln.w != nullptr;
+    ln.hi = c->xh0; ln.lo = c->xl0;
+    RC(ln_q8(ln, c->stream));
+    RC(bf_proj(c, p + "attn.Wqkv.weight", c->xh0, c->xl0, T, F(c, p + "attn.Wqkv.bias"), bf::EPI_F32, c->qkv, 3 * H));
+    const bool global = c->kinds[i] != 0;
+    attn::Args at{};
+    at.qkv = c->qkv; at.ld = 3 * H; at.hidden = H; at.heads = c->d.heads;
+    at.seg_start = c->seg_start; at.seg_len = c->seg_len;
+    at.qtile_item = c->qt_item; at.qtile_q0 = c->qt_q0; at.n_qtiles = c->n_qt;
+    at.window = global ? -1 : c->d.local_attention / 2;
+    at.scale = 1.0f / std::sqrt(static_cast<float>(H / c->d.heads));
+    at.cosv = global ? c->cos_g : c->cos_l; at.sinv = global ? c->sin_g : c->sin_l;
+    at.hi = c->xh0; at.lo = c->xl0;
+    RC(attention(at, c->max_qtiles, c->stream));
+    RC(bf_proj(c, p + "attn.Wo.weight", c->xh0, c->xl0, T, F(c, p + "attn.Wo.bias"), bf::EPI_F32_ADD, c->h, H));
+    RC(need_f32(c, p + "mlp_norm.weight", &ln.w));
+    ln.b = F(c, p + "mlp_norm.bias"); ln.apply_ln = 1;
+    RC(ln_q8(ln, c->stream));
+    RC(bf_proj(c, p + "mlp.Wi.weight", c->xh0, c->xl0, T, F(c, p + "mlp.Wi.bias"), bf::EPI_F32, c->wide, 2 * I));
+    RC(geglu_fwd_f32(c->wide, T, I, c->xh1, c->xl1, c->stream));
+    RC(bf_proj(c, p + "mlp.Wo.weight", c->xh1, c->xl1, T, F(c, p + "mlp.Wo.bias"), bf::EPI_F32_ADD, c->h, H));
+    return record_copy(c, "encoder.layers." + std::to_string(i) + ".output", c->h, static_cast<size_t>(T) * H);
+}
+
+// One decision-head layer of the fp32-accurate path (head_layer below, split bf16 products, ReLU in fp32).
+int head_layer_f32(laya_ctx* c, int i, int T) {
+    const int H = c->d.hidden;
+    const std::string p = "head.layers." + std::to_string(i) + ".";
+    LnArgs ln{};
+    ln.rows = T; ln.n = H; ln.x = c->h; ln.eps = 1e-5f; ln.err = c->err; ln.apply_ln = 1;
+    RC(need_f32(c, p + "norm1.weight", &ln.w));
+    ln.b = F(c, p + "norm1.bias");
+    ln.hi = c->xh0; ln.lo = c->xl0;
+    RC(ln_q8(ln, c->stream));
+    RC(bf_proj(c, p + "self_attn.in_proj_weight", c->xh0, c->xl0, T, F(c, p + "self_attn.in_proj_bias"), bf::EPI_F32,
+               c->qkv, 3 * H));
+    attn::Args at{};
+    at.qkv = c->qkv; at.ld = 3 * H; at.hidden = H; at.heads = std::max(1, H / 64);
+    at.seg_start = c->seg_start; at.seg_len = c->seg_len;
+    at.qtile_item = c->qt_item; at.qtile_q0 = c->qt_q0; at.n_qtiles = c->n_qt;
+    at.window = -1; at.cosv = nullptr; at.sinv = nullptr;
+    at.scale = 1.0f / std::sqrt(static_cast<float>(H / at.heads));
+    at.hi = c->xh0; at.lo = c->xl0;
+    RC(attention(at, c->max_qtiles, c->stream));
+    RC(bf_proj(c, p + "self_attn.out_proj.weight", c->xh0, c->xl0, T, F(c, p + "self_attn.out_proj.bias"),
+               bf::EPI_F32_ADD, c->h, H));
+    RC(need_f32(c, p + "norm2.weight", &ln.w));
+    ln.b = F(c, p + "norm2.bias");
+    RC(ln_q8(ln, c->stream));
+    RC(bf_proj(c, p + "linear1.weight", c->xh0, c->xl0, T, F(c, p + "linear1.bias"), bf::EPI_F32, c->wide, 4 * H));
+    RC(relu_mask_f32(c->wide, c->xh1, c->xl1, static_cast<size_t>(T) * 4 * H, tr::Mask{0.0f, 1.0f, 0}, c->stream));
+    RC(bf_proj(c, p + "linear2.weight", c->xh1, c->xl1, T, F(c, p + "linear2.bias"), bf::EPI_F32_ADD, c->h, H));
+    return record_copy(c, "head.layers." + std::to_string(i) + ".output", c->h, static_cast<size_t>(T) * H);
+}
+
 // One encoder layer on c->h (ModernBertEncoder.Forward loop body, ModernBertEncoder.cs:155-183).
 int encoder_layer(laya_ctx* c, int i, int T) {
+    if (c->d.precision == LAYA_PRECISION_F32) return encoder_layer_f32(c, i, T);
     const int H = c->d.hidden;
     const std::string p = "encoder.layers." + std::to_string(i) + ".";
     LnArgs ln{};
@@ -317,6 +424,7 @@ int encoder_layer(laya_ctx* c, int i, int T) {
 
 // One decision-head layer on c->h (DecisionModel.HeadForward, DecisionModel.cs:236-307).
 int head_layer(laya_ctx* c, int i, int T) {
+    if (c->d.precision == LAYA_PRECISION_F32) return head_layer_f32(c, i, T);
     const int H = c->d.hidden;
     const std::string p = "head.layers." + std::to_string(i) + ".";
     LnArgs ln{};
@@ -418,8 +526,8 @@ int forward_staged(laya_ctx* c, int n_items, int T, int n_markers, float* logits
 }
 
 int check_forward_args(laya_ctx* c, int n_items, long long T, long long n_markers) {
-    if (c->d.precision != LAYA_PRECISION_Q8_0) {
-        set_error("the forward of this build runs Q8_0 projections; create the context with LAYA_PRECISION_Q8_0");
+    if (c->d.precision != LAYA_PRECISION_Q8_0 && c->d.precision != LAYA_PRECISION_F32) {
+        set_error("unknown precision");
         return ERR_NOT_SUPPORTED;
     }
     if (n_items < 0 || n_items > c->d.max_items) { set_error("item count outside [0, max_items]"); return ERR_ARGUMENT; }
@@ -488,6 +596,33 @@ float bf16_bits_to_float(uint16_t b) {
     float f;
     memcpy(&f, &bits, 4);
     return f;
+}
+
+// A projection of the fp32-accurate path from fp32 values: hi = bf16(w) (round to nearest even), lo = bf16(w − hi),
+// lo kept only when some weight is not a bf16 value.
+int store_split(laya_ctx* c, const std::string& name, int N, int K, const float* w) {
+    const size_t n = static_cast<size_t>(N) * K;
+    std::vector<__nv_bfloat16> hi(n), lo(n);
+    bool exact = true;
+    for (size_t i = 0; i < n; ++i) {
+        hi[i] = __float2bfloat16_rn(w[i]);
+        const float r = w[i] - __bfloat162float(hi[i]);
+        lo[i] = __float2bfloat16_rn(r);
+        exact = exact && r == 0.0f;
+    }
+    BWeight& b = c->bw[name];
+    if (b.hi) cudaFree(b.hi);
+    if (b.lo) cudaFree(b.lo);
+    b = BWeight{};
+    b.N = N; b.K = K;
+    LAYA_CUDA(cudaMalloc(&b.hi, n * sizeof(__nv_bfloat16)));
+    LAYA_CUDA(cudaMemcpyAsync(b.hi, hi.data(), n * sizeof(__nv_bfloat16), cudaMemcpyHostToDevice, c->stream));
+    if (!exact) {
+        LAYA_CUDA(cudaMalloc(&b.lo, n * sizeof(__nv_bfloat16)));
+        LAYA_CUDA(cudaMemcpyAsync(b.lo, lo.data(), n * sizeof(__nv_bfloat16), cudaMemcpyHostToDevice, c->stream));
+    }
+    LAYA_CUDA(cudaStreamSynchronize(c->stream));
+    return OK;
 }
 
 int store_q8(laya_ctx* c, const std::string& name, const int8_t* q_host, const float* d_rows_host, int N, int K,
@@ -607,6 +742,16 @@ int laya_ctx_create(const laya_model_desc* desc, int device, laya_ctx** out) {
         (rc = dalloc_t(c, &c->logits, std::max(1, d.max_markers))) ||
         (rc = dalloc_t(c, &c->act, static_cast<size_t>(d.max_items) * c->d.n_act)))
         return fail(rc);
+    if (d.precision == LAYA_PRECISION_F32) {
+        const size_t widest = std::max(2 * static_cast<size_t>(I), 4 * static_cast<size_t>(H));
+        if ((rc = dalloc_t(c, &c->xh0, T * H)) || (rc = dalloc_t(c, &c->xl0, T * H)) ||
+            (rc = dalloc_t(c, &c->xh1, T * c->maxk)) || (rc = dalloc_t(c, &c->xl1, T * c->maxk)) ||
+            (rc = dalloc_t(c, &c->wide, T * widest)))
+            return fail(rc);
+    } else if (d.precision != LAYA_PRECISION_Q8_0) {
+        set_error("unknown precision");
+        return fail(ERR_ARGUMENT);
+    }
     // activation scales padding rows read by the products must be finite: zero both scale buffers once
     cudaMemsetAsync(c->da0, 0, sizeof(float) * (H / 32) * L, c->stream);
     cudaMemsetAsync(c->da1, 0, sizeof(float) * (c->maxk / 32) * L, c->stream);
@@ -644,6 +789,7 @@ int laya_ctx_destroy(laya_ctx* c) {
     for (void* p : c->allocs) cudaFree(p);
     for (auto& kv : c->f32) cudaFree(kv.second.p);
     for (auto& kv : c->q8) { cudaFree(kv.second.q); cudaFree(kv.second.d); }
+    for (auto& kv : c->bw) { cudaFree(kv.second.hi); if (kv.second.lo) cudaFree(kv.second.lo); }
     for (auto& kv : c->rec) cudaFree(kv.second.p);
     for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
     if (c->own) cudaStreamDestroy(c->own);
@@ -731,6 +877,10 @@ int laya_upload_tensor(laya_ctx* c, const char* name, int dtype, const int64_t* 
         if (rank != 2 || shape[1] % 32) { set_error(n + ": a Q8_0 projection needs [out, in] with in a multiple of 32"); return ERR_ARGUMENT; }
         return store_q8(c, n, nullptr, nullptr, static_cast<int>(shape[0]), static_cast<int>(shape[1]), true, src);
     }
+    if (c->d.precision == LAYA_PRECISION_F32 && is_projection(n)) {
+        if (rank != 2 || shape[1] % 8) { set_error(n + ": a projection needs [out, in] with in a multiple of 8"); return ERR_ARGUMENT; }
+        return store_split(c, n, static_cast<int>(shape[0]), static_cast<int>(shape[1]), src);
+    }
     std::vector<float> perm;
     if (ends_with(n, "mlp.Wi.bias") && c->d.precision == LAYA_PRECISION_Q8_0) {
         const int N = static_cast<int>(count);
@@ -772,6 +922,17 @@ int laya_download_tensor(laya_ctx* c, const char* name, float* host, int64_t cou
         if (ends_with(n, "mlp.Wi.bias") && c->d.precision == LAYA_PRECISION_Q8_0)
             for (int p = 0; p < have; ++p) host[geglu_src_row(p, static_cast<int>(have / 2))] = tmp[p];
         else memcpy(host, tmp.data(), have * sizeof(float));
+        return OK;
+    }
+    auto bt = c->bw.find(n);
+    if (bt != c->bw.end()) {
+        const BWeight& w = bt->second;
+        const size_t m = static_cast<size_t>(w.N) * w.K;
+        if (count < static_cast<int64_t>(m)) { set_error("host buffer too small"); return ERR_ARGUMENT; }
+        std::vector<__nv_bfloat16> hi(m), lo(m);
+        LAYA_CUDA(cudaMemcpy(hi.data(), w.hi, m * sizeof(__nv_bfloat16), cudaMemcpyDeviceToHost));
+        if (w.lo) LAYA_CUDA(cudaMemcpy(lo.data(), w.lo, m * sizeof(__nv_bfloat16), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < m; ++i) host[i] = __bfloat162float(hi[i]) + (w.lo ? __bfloat162float(lo[i]) : 0.0f);
         return OK;
     }
     auto jt = c->q8.find(n);
@@ -961,7 +1122,7 @@ int laya_gemm_bf16_split_device(laya_ctx* c, int M, int N, int K, const uint16_t
                                 int a_mn, const uint16_t* B, const uint16_t* B_lo, int ldb, int b_mn, const float* bias,
                                 int epilogue, void* out, int ldo) {
     if (!c) { set_error("null context"); return ERR_ARGUMENT; }
-    if (!A_lo || !B_lo) { set_error("split product needs both low parts"); return ERR_ARGUMENT; }
+    if (!A_lo) { set_error("split product needs the low part of A"); return ERR_ARGUMENT; }
     if (epilogue < 0 || epilogue > 2) { set_error("unknown epilogue"); return ERR_ARGUMENT; }
     DeviceGuard g(c->device);
     bf::Args a{};

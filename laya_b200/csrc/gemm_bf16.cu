@@ -54,7 +54,8 @@ DEVI uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
 
 struct KParams {
     int M, N, K;
-    int splits;        // 1: A·Bᵀ;  3: A·Bᵀ + A2·Bᵀ + A·B2ᵀ (hi/lo operand pairs, an fp32-accurate product)
+    int splits;        // 1: A·Bᵀ;  2: A·Bᵀ + A2·Bᵀ (B exactly bf16);  3: A·Bᵀ + A2·Bᵀ + A·B2ᵀ (hi/lo operand
+                       // pairs, an fp32-accurate product)
     int ksplit;        // K chunks per output tile (accumulating outputs only: chunks reduce-add into the output)
     const float* bias;
     int* err;
@@ -269,7 +270,8 @@ template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
 static int launch(const Args& a, cudaStream_t stream) {
     using C = Cfg<BN, STAGES>;
     CUtensorMap tA, tB, tA2, tB2, tO;
-    const bool split = a.A2 && a.B2;
+    const int splits = a.A2 ? (a.B2 ? 3 : 2) : 1;   // passes (A, B), (A2, B), (A, B2)
+    const bool split = splits > 1;
     auto map_a = [&](CUtensorMap* m, const void* ptr) {
         if (A_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
         return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
@@ -281,7 +283,7 @@ static int launch(const Args& a, cudaStream_t stream) {
     int rc = map_a(&tA, a.A);
     if (!rc) rc = map_b(&tB, a.B);
     if (!rc) rc = map_a(&tA2, split ? a.A2 : a.A);
-    if (!rc) rc = map_b(&tB2, split ? a.B2 : a.B);
+    if (!rc) rc = map_b(&tB2, splits == 3 ? a.B2 : a.B);
     if (!rc) {
         if (EPI == EPI_BF16)
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
@@ -311,7 +313,7 @@ static int launch(const Args& a, cudaStream_t stream) {
         ksplit = (kblocks + kchunk - 1) / kchunk;   // every chunk non-empty: the last starts below kblocks
     }
     const int units = tiles * ksplit;
-    KParams p{a.M, a.N, a.K, split ? 3 : 1, ksplit, a.bias, a.err};
+    KParams p{a.M, a.N, a.K, splits, ksplit, a.bias, a.err};
     kern<<<units < nsm ? units : nsm, C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tO, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
@@ -329,7 +331,7 @@ static int dispatch_major(const Args& a, cudaStream_t s) {
 int gemm(const Args& a, cudaStream_t stream) {
     if (a.M <= 0 || a.N <= 0) return OK;
     if (a.K <= 0) { set_error("bf16 product needs K > 0"); return ERR_ARGUMENT; }
-    if ((a.A2 != nullptr) != (a.B2 != nullptr)) { set_error("split product needs both low parts"); return ERR_ARGUMENT; }
+    if (a.B2 && !a.A2) { set_error("a split product with a low part of B needs the low part of A"); return ERR_ARGUMENT; }
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.out) |
                          reinterpret_cast<uintptr_t>(a.A2) | reinterpret_cast<uintptr_t>(a.B2);
     if ((al & 15) || (a.lda & 7) || (a.ldb & 7) || (a.epi == EPI_BF16 ? (a.ldo & 7) : (a.ldo & 3))) {

@@ -1,5 +1,6 @@
 // kernels.h — argument blocks and launchers of the laya_b200 kernels (internal to the library).
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -22,6 +23,7 @@ struct LnArgs {
     const int32_t* tok_item;   // final LN: question of each token
     const int32_t* qtype;      // final LN: type of each question
     __half* q; float* d; int ldd;   // Q8_0 output: fp16-held codes [rows, n], scales [n/32, ldd]
+    __nv_bfloat16* hi; __nv_bfloat16* lo;   // or (q null) the output split as hi = bf16(y), lo = bf16(y − hi) [rows, n]
     int* err;
 };
 int ln_q8(const LnArgs& a, cudaStream_t s);
@@ -38,6 +40,7 @@ struct Args {
     float scale;                      // 1/sqrt(head_dim), applied to every dot product
     const float* cosv; const float* sinv;   // [positions, head_dim/2] or null (no rotary)
     __half* q; float* d; int ldd;     // context codes (fp16-held) [T, hidden], scales [hidden/32, ldd]
+    __nv_bfloat16* hi; __nv_bfloat16* lo;   // or (q null) the context split as hi = bf16(c), lo = bf16(c − hi)
 };
 }  // namespace attn
 int attention(const attn::Args& a, int max_qtiles, cudaStream_t stream);

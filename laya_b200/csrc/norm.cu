@@ -70,6 +70,17 @@ __global__ void __launch_bounds__(256) ln_kernel(LnArgs a) {
         }
     }
 
+    if (MODE == LN_Q8 && a.q == nullptr) {   // the fp32-accurate path: hi/lo bf16 parts for a split product
+        if (!active) return;
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            const size_t o = static_cast<size_t>(r) * n + l + 8 * i;
+            const __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+            a.hi[o] = h;
+            a.lo[o] = __float2bfloat16_rn(__fsub_rn(v[i], __bfloat162float(h)));
+        }
+        return;
+    }
     if constexpr (MODE == LN_Q8) {
         // 32-value blocks: thread l holds elements l, l+8, l+16, l+24 of each block.
 #pragma unroll

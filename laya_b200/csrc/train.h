@@ -14,7 +14,8 @@ enum Epi : int {
 // out[M, N] = A · Bᵀ with A [M, K] and B [N, K] in the logical view; a_mn / b_mn say the operand is stored with the
 // M (N) index contiguous instead of K: A as [K, lda] and B as [K, ldb].  Row strides in elements.
 // With A2 and B2 (the bf16 remainders x − bf16(x) of fp32 operands, same layout and strides as A and B) the product
-// is A·Bᵀ + A2·Bᵀ + A·B2ᵀ: the three leading terms of (A + A2)(B + B2)ᵀ, accurate to about 2^-16 relative.
+// is A·Bᵀ + A2·Bᵀ + A·B2ᵀ: the three leading terms of (A + A2)(B + B2)ᵀ, accurate to about 2^-16 relative.  With A2
+// alone (B exactly bf16, as a bf16 checkpoint's weights are) it is A·Bᵀ + A2·Bᵀ, to the same accuracy.
 struct Args {
     int M, N, K;
     const __nv_bfloat16* A; int lda; int a_mn;

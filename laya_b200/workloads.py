@@ -131,6 +131,50 @@ def training_weights(hidden=768, intermediate=1152, layers=22, vocab=50368, head
     return w
 
 
+def bf16_checkpoint_weights(hidden=1024, intermediate=2624, layers=28, vocab=50368, head_layers=2, n_act=2,
+                            act_hidden=256, std=0.02, seed=0, **_) -> Dict[str, np.ndarray]:
+    """The tensors of training_weights' names and shapes as a bf16 checkpoint holds them: N(0, std) draws truncated
+    to bf16 values (returned as fp32), LayerNorm γ = 1, biases 0.  float32 draws, so a 400M-parameter model is made
+    in seconds."""
+    rng = np.random.default_rng(seed)
+    shapes = {k: v.shape for k, v in training_weights(hidden=8, intermediate=8, layers=layers, vocab=8, head_layers=head_layers,
+                                                      n_act=n_act, act_hidden=8, seed=0).items()}
+    out: Dict[str, np.ndarray] = {}
+    H, I = hidden, intermediate
+    real = {"encoder.embeddings.tok_embeddings.weight": (vocab, H), "type_emb.weight": (3, H),
+            "scorer.3.weight": (1, H), "scorer.3.bias": (1,), "act_head.0.weight": (act_hidden, H + 4),
+            "act_head.0.bias": (act_hidden,), "act_head.2.weight": (n_act, act_hidden), "act_head.2.bias": (n_act,)}
+    for name in shapes:
+        if name in real:
+            shape = real[name]
+        elif name.endswith(("attn.Wqkv.weight", "self_attn.in_proj_weight")):
+            shape = (3 * H, H)
+        elif name.endswith("self_attn.in_proj_bias"):
+            shape = (3 * H,)
+        elif name.endswith("mlp.Wi.weight"):
+            shape = (2 * I, H)
+        elif name.endswith("mlp.Wo.weight"):
+            shape = (H, I)
+        elif name.endswith("linear1.weight"):
+            shape = (4 * H, H)
+        elif name.endswith("linear1.bias"):
+            shape = (4 * H,)
+        elif name.endswith("linear2.weight"):
+            shape = (H, 4 * H)
+        elif name.endswith((".weight", ".bias")) and len(shapes[name]) == 2:
+            shape = (H, H)
+        else:
+            shape = (H,)
+        if name.endswith("bias"):
+            out[name] = np.zeros(shape, np.float32)
+        elif len(shape) == 1:
+            out[name] = np.ones(shape, np.float32)
+        else:
+            x = rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
+            out[name] = (x.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+    return out
+
+
 def training_batch(rows=32, min_len=256, max_len=1024, vocab=50368, seed=1000, groups=4):
     """(items, draws): rows with valid length U{min_len..max_len}, kinds round-robin, markers at j·⌊L/(k+1)⌋,
     targets U(0, 1) normalised, draws standard normal [groups, total options]."""
