@@ -315,56 +315,134 @@ DEVI void st_split(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, float v) {
     if (lo) lo[i] = __float2bfloat16_rn(v - bf(h));
 }
 
-// act = gelu(u) · gate, [u | gate] = wide row (bf16, or fp32 in the accurate forward with act's low part)
+// Four consecutive elements per thread: 16-byte fp32 and 8-byte bf16 accesses (callers guarantee 4-element alignment).
+struct F4 { float v[4]; };
+DEVI F4 ldv4(const float* p) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    return F4{{x.x, x.y, x.z, x.w}};
+}
+DEVI F4 ldv4(const __nv_bfloat16* p) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&x.x), b = *reinterpret_cast<const __nv_bfloat162*>(&x.y);
+    return F4{{__low2float(a), __high2float(a), __low2float(b), __high2float(b)}};
+}
+DEVI void st4(__nv_bfloat16* p, const F4& f) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(f.v[0], f.v[1]), b = __floats2bfloat162_rn(f.v[2], f.v[3]);
+    uint2 x;
+    x.x = *reinterpret_cast<const uint32_t*>(&a);
+    x.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = x;
+}
+DEVI void st4_split(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, const F4& f) {
+    F4 h, l;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        h.v[k] = bf(__float2bfloat16_rn(f.v[k]));
+        l.v[k] = f.v[k] - h.v[k];
+    }
+    st4(hi + i, h);   // h holds bf16 values: rounding them again is exact
+    if (lo) st4(lo + i, l);
+}
+
+// act = gelu(u) · gate, [u | gate] = wide row (bf16, or fp32 in the accurate forward with act's low part).
+// Thread = 4 consecutive columns of one row (I a multiple of 4).
 template <typename Src>
 __global__ void geglu_fwd_kernel(const Src* __restrict__ wide, int rows, int I, __nv_bfloat16* __restrict__ act,
                                  __nv_bfloat16* __restrict__ act_lo) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<size_t>(rows) * I) return;
-    const size_t r = i / I, c = i % I;
-    const float u = ld_f(wide + r * 2 * I + c), g = ld_f(wide + r * 2 * I + I + c);
-    st_split(act, act_lo, i, gelu_exact(u) * g);
+    const unsigned I4 = static_cast<unsigned>(I) >> 2;
+    const unsigned j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= static_cast<unsigned>(rows) * I4) return;
+    const unsigned r = j / I4, c = (j - r * I4) * 4;
+    const Src* row = wide + static_cast<size_t>(r) * 2 * I;
+    const F4 u = ldv4(row + c), g = ldv4(row + I + c);
+    F4 o;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o.v[k] = gelu_exact(u.v[k]) * g.v[k];
+    st4_split(act, act_lo, static_cast<size_t>(r) * I + c, o);
 }
 // dgate = dy·gelu(u); du = dy·gate·gelu'(u)
 template <typename Src>
 __global__ void geglu_bwd_kernel(const Src* __restrict__ wide, const float* __restrict__ dact, int rows, int I,
                                  __nv_bfloat16* __restrict__ dwide) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<size_t>(rows) * I) return;
-    const size_t r = i / I, c = i % I;
-    const float u = ld_f(wide + r * 2 * I + c), g = ld_f(wide + r * 2 * I + I + c);
-    const float dy = dact[i];
-    dwide[r * 2 * I + I + c] = __float2bfloat16_rn(dy * gelu_exact(u));
-    dwide[r * 2 * I + c] = __float2bfloat16_rn(dy * g * gelu_grad(u));
+    const unsigned I4 = static_cast<unsigned>(I) >> 2;
+    const unsigned j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= static_cast<unsigned>(rows) * I4) return;
+    const unsigned r = j / I4, c = (j - r * I4) * 4;
+    const Src* row = wide + static_cast<size_t>(r) * 2 * I;
+    const F4 u = ldv4(row + c), g = ldv4(row + I + c), dy = ldv4(dact + static_cast<size_t>(r) * I + c);
+    F4 dg, du;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        dg.v[k] = dy.v[k] * gelu_exact(u.v[k]);
+        du.v[k] = dy.v[k] * g.v[k] * gelu_grad(u.v[k]);
+    }
+    __nv_bfloat16* out = dwide + static_cast<size_t>(r) * 2 * I;
+    st4(out + I + c, dg);
+    st4(out + c, du);
 }
 
 // ------------------------------------------------------------------------------------------------ masked elementwise
+// Elementwise kernels: thread = 4 consecutive elements (4-element aligned buffers; a ragged tail element by element).
 // y32 = a32 + mask(b32)   (a residual branch with dropout, HeadLayerForward)
 __global__ void add_masked_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, size_t n,
                                   Mask m) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = a[i] + b[i] * dmask(m, i);
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i >= n) return;
+    if (i + 4 > n) {   // the ragged tail
+        for (size_t k = i; k < n; ++k) y[k] = a[k] + b[k] * dmask(m, k);
+        return;
+    }
+    const F4 x = ldv4(a + i), z = ldv4(b + i);
+    float4 o;
+    o.x = x.v[0] + z.v[0] * dmask(m, i);
+    o.y = x.v[1] + z.v[1] * dmask(m, i + 1);
+    o.z = x.v[2] + z.v[2] * dmask(m, i + 2);
+    o.w = x.v[3] + z.v[3] * dmask(m, i + 3);
+    *reinterpret_cast<float4*>(y + i) = o;
 }
 // act = mask(relu(pre))   (linear1 → ReLU → dropout, HeadLayerForward); pre bf16 or fp32 (+ act's low part)
 template <typename Src>
 __global__ void relu_mask_kernel(const Src* __restrict__ pre, __nv_bfloat16* __restrict__ act,
                                  __nv_bfloat16* __restrict__ act_lo, size_t n, Mask m) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i >= n) return;
-    st_split(act, act_lo, i, fmaxf(ld_f(pre + i), 0.f) * dmask(m, i));
+    if (i + 4 > n) {
+        for (size_t k = i; k < n; ++k) st_split(act, act_lo, k, fmaxf(ld_f(pre + k), 0.f) * dmask(m, k));
+        return;
+    }
+    F4 x = ldv4(pre + i);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x.v[k] = fmaxf(x.v[k], 0.f) * dmask(m, i + k);
+    st4_split(act, act_lo, i, x);
 }
 // dx16 = bf16(mask(d32) · [pre > 0])
 template <typename Src>
 __global__ void relu_mask_bwd_kernel(const float* __restrict__ d, const Src* __restrict__ pre,
                                      __nv_bfloat16* __restrict__ dx, size_t n, Mask m) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i >= n) return;
-    dx[i] = __float2bfloat16_rn(ld_f(pre + i) > 0.f ? d[i] * dmask(m, i) : 0.f);
+    if (i + 4 > n) {
+        for (size_t k = i; k < n; ++k) dx[k] = __float2bfloat16_rn(ld_f(pre + k) > 0.f ? d[k] * dmask(m, k) : 0.f);
+        return;
+    }
+    const F4 p = ldv4(pre + i);
+    F4 g = ldv4(d + i);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) g.v[k] = p.v[k] > 0.f ? g.v[k] * dmask(m, i + k) : 0.f;
+    st4(dx + i, g);
 }
 // y16 = bf16(mask(x32))
 __global__ void cast_mask_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n, Mask m) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = __float2bfloat16_rn(x[i] * dmask(m, i));
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i >= n) return;
+    if (i + 4 > n) {
+        for (size_t k = i; k < n; ++k) y[k] = __float2bfloat16_rn(x[k] * dmask(m, k));
+        return;
+    }
+    F4 v = ldv4(x + i);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v.v[k] = v.v[k] * dmask(m, i + k);
+    st4(y + i, v);
 }
 
 // db[c] += Σ_r d[r, c]  (d fp32 or bf16); a CTA takes 64 rows × 256 columns
@@ -613,13 +691,15 @@ __global__ void __launch_bounds__(256) rlcd_kernel(RlcdArgs a) {
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 4 <= n) st4(y + i, ldv4(x + i));
+    else for (size_t k = i; k < n; ++k) y[k] = __float2bfloat16_rn(x[k]);
 }
 __global__ void f32_split_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
                                  size_t n) {
-    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) st_split(hi, lo, i, x[i]);
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i + 4 <= n) st4_split(hi, lo, i, ldv4(x + i));
+    else for (size_t k = i; k < n; ++k) st_split(hi, lo, k, x[k]);
 }
 
 }  // namespace tr
@@ -682,37 +762,85 @@ int ln_bwd(const tr::LnBwd& a, cudaStream_t s) {
         return OK;                                                                      \
     } while (0)
 
+// The 4-wide kernels need 4-element-aligned addresses (and, for GeGLU, rows of a multiple of 4 columns).
+static bool aligned4(size_t n, std::initializer_list<const void*> ptrs, size_t elem_bytes_min = 2) {
+    (void)n;
+    for (const void* p : ptrs)
+        if (p && (reinterpret_cast<uintptr_t>(p) % (4 * elem_bytes_min))) return false;
+    return true;
+}
+#define LAUNCH4(kern, n, ...)                                                           \
+    do {                                                                                \
+        if ((n) > 0) {                                                                  \
+            tr::kern<<<blocks_for(((n) + 3) / 4, 256), 256, 0, s>>>(__VA_ARGS__);       \
+            count_launch();                                                             \
+            LAYA_CUDA(cudaGetLastError());                                              \
+        }                                                                               \
+        return OK;                                                                      \
+    } while (0)
+#define REQUIRE4(n, ...)                                                                                        \
+    do {                                                                                                        \
+        if (!aligned4((n), {__VA_ARGS__})) {                                                                    \
+            set_error("elementwise kernel: buffers must be 4-element aligned");                                 \
+            return ERR_ARGUMENT;                                                                                \
+        }                                                                                                       \
+    } while (0)
+
+static int geglu_width(int I) {
+    if (I % 4) { set_error("GeGLU width must be a multiple of 4"); return ERR_ARGUMENT; }
+    return OK;
+}
 int geglu_fwd(const __nv_bfloat16* wide, int rows, int I, __nv_bfloat16* act, cudaStream_t s) {
-    LAUNCH1(geglu_fwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, rows, I, act, nullptr);
+    if (geglu_width(I) != OK) return ERR_ARGUMENT;
+    REQUIRE4(static_cast<size_t>(I), wide, act);
+    LAUNCH4(geglu_fwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, rows, I, act, nullptr);
 }
 int geglu_fwd_f32(const float* wide, int rows, int I, __nv_bfloat16* act, __nv_bfloat16* act_lo, cudaStream_t s) {
-    LAUNCH1(geglu_fwd_kernel<float>, static_cast<size_t>(rows) * I, wide, rows, I, act, act_lo);
+    if (geglu_width(I) != OK) return ERR_ARGUMENT;
+    REQUIRE4(static_cast<size_t>(I), wide, act, act_lo);
+    LAUNCH4(geglu_fwd_kernel<float>, static_cast<size_t>(rows) * I, wide, rows, I, act, act_lo);
 }
 int geglu_bwd(const __nv_bfloat16* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s) {
-    LAUNCH1(geglu_bwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
+    if (geglu_width(I) != OK) return ERR_ARGUMENT;
+    REQUIRE4(static_cast<size_t>(I), wide, dact, dwide);
+    LAUNCH4(geglu_bwd_kernel<__nv_bfloat16>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
 }
 int geglu_bwd_f32(const float* wide, const float* dact, int rows, int I, __nv_bfloat16* dwide, cudaStream_t s) {
-    LAUNCH1(geglu_bwd_kernel<float>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
+    if (geglu_width(I) != OK) return ERR_ARGUMENT;
+    REQUIRE4(static_cast<size_t>(I), wide, dact, dwide);
+    LAUNCH4(geglu_bwd_kernel<float>, static_cast<size_t>(rows) * I, wide, dact, rows, I, dwide);
 }
 int add_masked(const float* a, const float* b, float* y, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(add_masked_kernel, n, a, b, y, n, m);
+    REQUIRE4(n, a, b, y);
+    LAUNCH4(add_masked_kernel, n, a, b, y, n, m);
 }
 int relu_mask(const __nv_bfloat16* pre, __nv_bfloat16* act, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_kernel<__nv_bfloat16>, n, pre, act, nullptr, n, m);
+    REQUIRE4(n, pre, act);
+    LAUNCH4(relu_mask_kernel<__nv_bfloat16>, n, pre, act, nullptr, n, m);
 }
 int relu_mask_f32(const float* pre, __nv_bfloat16* act, __nv_bfloat16* act_lo, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_kernel<float>, n, pre, act, act_lo, n, m);
+    REQUIRE4(n, pre, act, act_lo);
+    LAUNCH4(relu_mask_kernel<float>, n, pre, act, act_lo, n, m);
 }
 int relu_mask_bwd(const float* d, const __nv_bfloat16* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_bwd_kernel<__nv_bfloat16>, n, d, pre, dx, n, m);
+    REQUIRE4(n, d, pre, dx);
+    LAUNCH4(relu_mask_bwd_kernel<__nv_bfloat16>, n, d, pre, dx, n, m);
 }
 int relu_mask_bwd_f32(const float* d, const float* pre, __nv_bfloat16* dx, size_t n, tr::Mask m, cudaStream_t s) {
-    LAUNCH1(relu_mask_bwd_kernel<float>, n, d, pre, dx, n, m);
+    REQUIRE4(n, d, pre, dx);
+    LAUNCH4(relu_mask_bwd_kernel<float>, n, d, pre, dx, n, m);
 }
-int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s) { LAUNCH1(cast_mask_kernel, n, x, y, n, m); }
-int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) { LAUNCH1(f32_to_bf16_kernel, n, x, y, n); }
+int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream_t s) {
+    REQUIRE4(n, x, y);
+    LAUNCH4(cast_mask_kernel, n, x, y, n, m);
+}
+int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
+    REQUIRE4(n, x, y);
+    LAUNCH4(f32_to_bf16_kernel, n, x, y, n);
+}
 int f32_split_bf16(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, size_t n, cudaStream_t s) {
-    LAUNCH1(f32_split_kernel, n, x, hi, lo, n);
+    REQUIRE4(n, x, hi, lo);
+    LAUNCH4(f32_split_kernel, n, x, hi, lo, n);
 }
 int scatter_rows(const float* d, const int32_t* ids, int rows, int n, float* grad, cudaStream_t s) {
     LAUNCH1(scatter_rows_kernel, static_cast<size_t>(rows) * n, d, ids, rows, n, grad);
