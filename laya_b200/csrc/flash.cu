@@ -635,9 +635,14 @@ static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
     if (!rc) rc = set_smem(fa::bwd_dkdv_kernel<HD>, smem_kv);
     if (rc) return rc;
     dim3 grid(max_tiles, a.heads);
-    fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a);
-    count_launch();
-    LAYA_CUDA(cudaGetLastError());
+    rc = HD == 64 ? flash_backward_dq_tc(a, s) : ERR_NOT_SUPPORTED;   // dQ on the tensor cores (flash_tc.cu)
+    if (rc == ERR_NOT_SUPPORTED) {
+        fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a);
+        count_launch();
+        LAYA_CUDA(cudaGetLastError());
+    } else if (rc != OK) {
+        return rc;
+    }
     if (HD == 64) {   // dK, dV on the tensor cores (flash_tc.cu) when the batch carries its 128-row tile list
         rc = flash_backward_dkdv_tc(a, s);
         if (rc != ERR_NOT_SUPPORTED) return rc;

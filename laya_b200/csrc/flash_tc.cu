@@ -17,7 +17,8 @@
 //               At the end the two halves' row sums are combined and each warp stores its 32 context columns.
 // The accurate forward (SPLIT) keeps hi and lo bf16 parts of Q, K, V and P and issues three MMAs per product
 // (hi·hi + lo·hi + hi·lo), accumulating in the same TMEM columns.
-// The backward's dK/dV kernel (bwd_dkdv_tc_kernel, below) uses the same roles with keys in the TMEM lanes.
+// The backward's dK/dV kernel (bwd_dkdv_tc_kernel, below) uses the same roles with keys in the TMEM lanes, and its dQ
+// kernel (bwd_dq_tc_kernel) the forward's layout with dP = dO·Vᵀ beside S and dQ += dS·K in place of P·V.
 // Every wait is bounded (common.cuh): a protocol fault ends with an error status, never a hung GPU.
 #include <algorithm>
 
@@ -639,6 +640,220 @@ __global__ void __launch_bounds__(320, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ backward: dQ
+// Same contract as fa::bwd_dq_kernel (flash.cu): for one 128-query tile of one head, over every 128-key tile it sees,
+//     S = Q·Kᵀ,  dP = dO·Vᵀ  (M 128 queries, N 128 keys, K 64)                into TMEM columns [0, 128), [128, 256)
+//     P = exp(scale·S − lse) (· dropout),  dS = scale · P ∘ (dP·m − D)       by the softmax warps, bf16 into smem
+//     dQ += dS·K  (M 128 queries, N 64, K 128 keys; K read N-contiguous)     into [256, 320)
+// then dQ rotated back by −θ at the query's position, in bf16.  Roles as in the forward: warp 0 loads Q and dO once
+// and K, V through a 2-stage ring; warp 1 issues the MMAs (S and dP of tile j before dQ of tile j − 1); warps 2-9
+// are the softmax warps, thread (half, row) owning query row `row` and keys [64·half, 64·half + 64) of a tile.
+constexpr int DQ_SMEM = 1024 + 8 * TILE + 256;   // Q, dO, 2 × (K, V), dS (two 64-key sub-tiles); barriers
+static_assert(DQ_SMEM <= 232448, "shared memory budget");
+
+template <bool DROP>
+__global__ void __launch_bounds__(320, 1)
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmqkv, const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
+    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, BK);                     // M queries, N keys, K-major
+    constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);        // B (K) N-contiguous
+    const int tile = blockIdx.x;
+    if (tile >= *p.n_tq) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sDO = smem + TILE;
+    uint8_t* sKV = smem + 2 * TILE;        // [2 stages][K, V]
+    uint8_t* sDS = smem + 6 * TILE;        // dS: 2 sub-tiles of 64 keys
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8 * TILE);
+    uint64_t* qo_full = bars;
+    uint64_t* kv_full = bars + 1;     // [2]
+    uint64_t* kv_empty = bars + 3;    // [2]
+    uint64_t* st_full = bars + 5;
+    uint64_t* st_free = bars + 6;
+    uint64_t* ds_full = bars + 7;
+    uint64_t* ds_empty = bars + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int head = blockIdx.y, item = p.tq_item[tile], q0 = p.tq_p0[tile];
+    const int seg0 = p.seg_start[item], L = p.seg_len[item];
+    const bool global = p.window < 0;
+    const int W = p.window;
+    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + BQ + W);
+    const int nk = (ke - kb + BK - 1) / BK;
+    const int warp = warp_id(), lane = lane_id();
+
+    if (threadIdx.x == 0) {
+        mbar_init(qo_full, 1);
+        for (int s = 0; s < 2; ++s) { mbar_init(kv_full + s, 1); mbar_init(kv_empty + s, 1); }
+        mbar_init(st_full, 1);
+        mbar_init(st_free, 8);
+        mbar_init(ds_full, 8);
+        mbar_init(ds_empty, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmqkv); prefetch_tmap(&tmdo); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tDP = tmem + BK, tDQ = tmem + 2 * BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(qo_full, 2 * TILE);
+            tma_load_2d(sQ, &tmqkv, qo_full, head * HD, seg0 + q0);
+            tma_load_2d(sDO, &tmdo, qo_full, head * HD, seg0 + q0);
+            for (int j = 0; j < nk; ++j) {
+                const int s = j & 1;
+                if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+                uint8_t* st = sKV + s * 2 * TILE;
+                const int y = seg0 + kb + j * BK;
+                mbar_arrive_expect_tx(kv_full + s, 2 * TILE);
+                tma_load_2d(st, &tmqkv, kv_full + s, p.hidden + head * HD, y);
+                tma_load_2d(st + TILE, &tmqkv, kv_full + s, 2 * p.hidden + head * HD, y);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = mbar_wait(qo_full, 0, abort_flag, p.err);
+            tc_fence_after();
+            const uint32_t aq = smem_u32(sQ), ado = smem_u32(sDO);
+            for (int j = 0; j <= nk && ok; ++j) {
+                if (j < nk) {
+                    const int s = j & 1;
+                    if (!mbar_wait(kv_full + s, (j >> 1) & 1, abort_flag, p.err)) break;
+                    if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t ak = smem_u32(sKV + s * 2 * TILE), av = ak + TILE;
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        mma_f16(tS, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
+                        mma_f16(tDP, smem_desc_sw128(ado + kk * 32), smem_desc_sw128(av + kk * 32), IDESC_S, kk > 0);
+                    }
+                    mma_commit(st_full);
+                }
+                if (j >= 1) {
+                    const int i = j - 1, s = i & 1;
+                    if (!mbar_wait(ds_full, i & 1, abort_flag, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t ak = smem_u32(sKV + s * 2 * TILE), ads = smem_u32(sDS);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                        mma_f16(tDQ, smem_desc_sw128(ads + po), desc_mn_sw128(ak + kk * 2048, TILE), IDESC_G,
+                                (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(kv_empty + s);
+                    mma_commit(ds_empty);
+                }
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int q = q0 + row;
+        const bool qin = q < L;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        constexpr int HK = BK / 2;
+        const float sl2 = p.scale * LOG2E;
+        const size_t at = static_cast<size_t>(seg0 + (qin ? q : 0)) * p.heads + head;
+        const float lse2 = qin ? __ldg(p.lse + at) * LOG2E : 0.f, dd = qin ? __ldg(p.dsum + at) : 0.f;
+        // keys this row sees: [lo, lo + span] (none for rows past the segment)
+        const int lo = global ? 0 : max(0, q - W);
+        const int span = (global ? L - 1 : min(L - 1, q + W)) - lo;
+        bool ok = true;
+        for (int j = 0; j < nk; ++j) {
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err));
+            if (ok) tc_fence_after();
+            const int k0 = kb + j * BK + half * HK;
+            uint8_t* drow = sDS + half * TILE + row * 128;
+            // two 32-key chunks: the second chunk's TMEM reads release S and dP to the next tile's MMAs
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t sv[32], dv[32];
+                if (ok) {
+                    tmem_ld32(tS + lane_off + half * HK + c * 32, sv);
+                    tmem_ld32(tDP + lane_off + half * HK + c * 32, dv);
+                    tmem_ld_wait();
+                }
+                if (c == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(st_free);
+                }
+                if (!ok) continue;
+                DropWalk walk(p.seed, head, seg0 + q, k0 + c * 32, 1, p.dropout, p.keep);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int k = k0 + c * 32 + e;
+                    const bool vis = qin && static_cast<unsigned>(k - lo) <= static_cast<unsigned>(span);
+                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse2)) : 0.f;
+                    const float m = DROP ? walk.next() : 1.0f;
+                    sv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                }
+                // dS of the previous tile must have been read by its dQ MMAs before it is rewritten; waiting only
+                // now lets the first chunk's exponentials overlap those MMAs
+                if (c == 0 && j > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(ds_empty, (j - 1) & 1, abort_flag, p.err));
+                    if (!ok) continue;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                    *reinterpret_cast<uint4*>(drow + (((c * 4 + u) ^ (row & 7)) << 4)) =
+                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                }
+            }
+            if (!ok) continue;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+        }
+        // dQ once the last dQ MMAs are done: half 0 rotates the whole row back by −θ and stores it
+        ok = __all_sync(0xffffffffu, ok && nk > 0 && mbar_wait(ds_empty, (nk - 1) & 1, abort_flag, p.err));
+        if (ok && half == 0) {
+            tc_fence_after();
+            uint32_t a[HD];
+            tmem_ld32(tDQ + lane_off, *reinterpret_cast<uint32_t(*)[32]>(a));
+            tmem_ld32(tDQ + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(a + 32));
+            tmem_ld_wait();
+            if (qin) {
+                float f[HD];
+#pragma unroll
+                for (int e = 0; e < HD; ++e) f[e] = __uint_as_float(a[e]);
+                if (p.cosv) {
+#pragma unroll
+                    for (int i = 0; i < HD / 2; ++i) {
+                        const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
+                        const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
+                        const float x = f[i], y = f[i + HD / 2];
+                        f[i] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+                        f[i + HD / 2] = __fsub_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+                    }
+                }
+                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + q) * p.lddq + head * HD;
+#pragma unroll
+                for (int t = 0; t < HD / 8; ++t)
+                    *reinterpret_cast<uint4*>(out + 8 * t) =
+                        make_uint4(pack2(f[8 * t], f[8 * t + 1]), pack2(f[8 * t + 2], f[8 * t + 3]),
+                                   pack2(f[8 * t + 4], f[8 * t + 5]), pack2(f[8 * t + 6], f[8 * t + 7]));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 }  // namespace fat
 
 template <bool SPLIT, bool DROP>
@@ -718,6 +933,44 @@ int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s) {
         (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15))
         return ERR_NOT_SUPPORTED;
     return a.dropout > 0.f ? launch_bwd_tc<true>(a, s) : launch_bwd_tc<false>(a, s);
+}
+
+template <bool DROP>
+static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
+    CUtensorMap tq, tdo;
+    int rc = make_tmap_2d(&tq, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                          static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
+                               static_cast<uint64_t>(a.ldo) * 2, fat::BK, fat::HD, true);
+    if (rc) return rc;
+    static bool attr[64] = {false};
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        LAYA_CUDA(cudaFuncSetAttribute(fat::bwd_dq_tc_kernel<DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       fat::DQ_SMEM));
+        attr[dev] = true;
+    }
+    fat::BwdParams p{};
+    p.seg_start = a.seg_start; p.seg_len = a.seg_len;
+    p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
+    p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
+    p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
+    p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
+    p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
+    fat::bwd_dq_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::DQ_SMEM, s>>>(tq, tdo, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// dQ by the tcgen05 kernel for head_dim 64 (ERR_NOT_SUPPORTED for shapes it does not take).
+int flash_backward_dq_tc(const fa::Args& a, cudaStream_t s) {
+    if (a.hidden / a.heads != fat::HD || !a.tq_item || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
+    if ((a.ld & 7) || (a.ldo & 7) || (a.lddq & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15))
+        return ERR_NOT_SUPPORTED;
+    return a.dropout > 0.f ? launch_dq_tc<true>(a, s) : launch_dq_tc<false>(a, s);
 }
 
 }  // namespace laya

@@ -63,6 +63,7 @@ int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int head
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
 int flash_forward_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: head_dim 64 (ERR_NOT_SUPPORTED otherwise)
 int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: dK, dV for head_dim 64
+int flash_backward_dq_tc(const fa::Args& a, cudaStream_t s);     // flash_tc.cu: dQ for head_dim 64
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s);
 
 // ---- train_kernels.cu
