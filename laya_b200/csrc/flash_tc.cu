@@ -641,20 +641,35 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ backward: dQ
-// Same contract as fa::bwd_dq_kernel (flash.cu): for one 128-query tile of one head, over every 128-key tile it sees,
-//     S = Q·Kᵀ,  dP = dO·Vᵀ  (M 128 queries, N 128 keys, K 64)                into TMEM columns [0, 128), [128, 256)
+// Same contract as fa::bwd_dq_kernel (flash.cu): for one 128-query tile of one head, over every 64-key tile it sees,
+//     S = Q·Kᵀ,  dP = dO·Vᵀ  (M 128 queries, N 64 keys, K 64)                into TMEM columns [0, 64), [64, 128)
 //     P = exp(scale·S − lse) (· dropout),  dS = scale · P ∘ (dP·m − D)       by the softmax warps, bf16 into smem
-//     dQ += dS·K  (M 128 queries, N 64, K 128 keys; K read N-contiguous)     into [256, 320)
+//     dQ += dS·K  (M 128 queries, N 64, K 64 keys; K read N-contiguous)      into [128, 192)
 // then dQ rotated back by −θ at the query's position, in bf16.  Roles as in the forward: warp 0 loads Q and dO once
 // and K, V through a 2-stage ring; warp 1 issues the MMAs (S and dP of tile j before dQ of tile j − 1); warps 2-9
-// are the softmax warps, thread (half, row) owning query row `row` and keys [64·half, 64·half + 64) of a tile.
-constexpr int DQ_SMEM = 1024 + 8 * TILE + 256;   // Q, dO, 2 × (K, V), dS (two 64-key sub-tiles); barriers
-static_assert(DQ_SMEM <= 232448, "shared memory budget");
+// are the softmax warps, thread (half, row) owning query row `row` and keys [32·half, 32·half + 32) of a tile.
+// 64-key tiles keep a CTA within 256 TMEM columns and 82 KB of shared memory, so two CTAs share an SM and one's
+// MMA round trips overlap the other's softmax (a sliding-window tile sees only a few key tiles).
+constexpr int DQ_BK = 64;
+constexpr int DQ_KTILE = DQ_BK * 128;                        // bytes of one 64-key × 64-column bf16 tile
+constexpr int DQ_SMEM = 1024 + 2 * TILE + 4 * DQ_KTILE + TILE + 256;   // Q, dO, 2 × (K, V), dS; barriers
+static_assert(2 * DQ_SMEM <= 232448, "two CTAs per SM");
+
+DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
 
 template <bool DROP>
-__global__ void __launch_bounds__(320, 1)
-    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmqkv, const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
-    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, BK);                     // M queries, N keys, K-major
+__global__ void __launch_bounds__(320, 2)
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+                     const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
+    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, DQ_BK);                  // M queries, N keys, K-major
     constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);        // B (K) N-contiguous
     const int tile = blockIdx.x;
     if (tile >= *p.n_tq) return;
@@ -662,9 +677,9 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* sDO = smem + TILE;
-    uint8_t* sKV = smem + 2 * TILE;        // [2 stages][K, V]
-    uint8_t* sDS = smem + 6 * TILE;        // dS: 2 sub-tiles of 64 keys
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8 * TILE);
+    uint8_t* sKV = smem + 2 * TILE;                 // [2 stages][K, V], 64 keys each
+    uint8_t* sDS = sKV + 4 * DQ_KTILE;              // dS [128 queries × 64 keys]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + TILE);
     uint64_t* qo_full = bars;
     uint64_t* kv_full = bars + 1;     // [2]
     uint64_t* kv_empty = bars + 3;    // [2]
@@ -680,7 +695,7 @@ __global__ void __launch_bounds__(320, 1)
     const bool global = p.window < 0;
     const int W = p.window;
     const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + BQ + W);
-    const int nk = (ke - kb + BK - 1) / BK;
+    const int nk = (ke - kb + DQ_BK - 1) / DQ_BK;
     const int warp = warp_id(), lane = lane_id();
 
     if (threadIdx.x == 0) {
@@ -693,27 +708,27 @@ __global__ void __launch_bounds__(320, 1)
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-    if (warp == 0 && lane == 0) { prefetch_tmap(&tmqkv); prefetch_tmap(&tmdo); }
+    if (warp == 1) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmq); prefetch_tmap(&tmkv); prefetch_tmap(&tmdo); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tDP = tmem + BK, tDQ = tmem + 2 * BK;
+    const uint32_t tS = tmem, tDP = tmem + DQ_BK, tDQ = tmem + 2 * DQ_BK;
 
     if (warp == 0) {
         if (lane == 0) {
             mbar_arrive_expect_tx(qo_full, 2 * TILE);
-            tma_load_2d(sQ, &tmqkv, qo_full, head * HD, seg0 + q0);
+            tma_load_2d(sQ, &tmq, qo_full, head * HD, seg0 + q0);
             tma_load_2d(sDO, &tmdo, qo_full, head * HD, seg0 + q0);
             for (int j = 0; j < nk; ++j) {
                 const int s = j & 1;
                 if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
-                uint8_t* st = sKV + s * 2 * TILE;
-                const int y = seg0 + kb + j * BK;
-                mbar_arrive_expect_tx(kv_full + s, 2 * TILE);
-                tma_load_2d(st, &tmqkv, kv_full + s, p.hidden + head * HD, y);
-                tma_load_2d(st + TILE, &tmqkv, kv_full + s, 2 * p.hidden + head * HD, y);
+                uint8_t* st = sKV + s * 2 * DQ_KTILE;
+                const int y = seg0 + kb + j * DQ_BK;
+                mbar_arrive_expect_tx(kv_full + s, 2 * DQ_KTILE);
+                tma_load_2d(st, &tmkv, kv_full + s, p.hidden + head * HD, y);
+                tma_load_2d(st + DQ_KTILE, &tmkv, kv_full + s, 2 * p.hidden + head * HD, y);
             }
         }
     } else if (warp == 1) {
@@ -727,7 +742,7 @@ __global__ void __launch_bounds__(320, 1)
                     if (!mbar_wait(kv_full + s, (j >> 1) & 1, abort_flag, p.err)) break;
                     if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
                     tc_fence_after();
-                    const uint32_t ak = smem_u32(sKV + s * 2 * TILE), av = ak + TILE;
+                    const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), av = ak + DQ_KTILE;
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {
                         mma_f16(tS, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
@@ -739,13 +754,11 @@ __global__ void __launch_bounds__(320, 1)
                     const int i = j - 1, s = i & 1;
                     if (!mbar_wait(ds_full, i & 1, abort_flag, p.err)) break;
                     tc_fence_after();
-                    const uint32_t ak = smem_u32(sKV + s * 2 * TILE), ads = smem_u32(sDS);
+                    const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), ads = smem_u32(sDS);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
-                        mma_f16(tDQ, smem_desc_sw128(ads + po), desc_mn_sw128(ak + kk * 2048, TILE), IDESC_G,
+                    for (int kk = 0; kk < DQ_BK / 16; ++kk)
+                        mma_f16(tDQ, smem_desc_sw128(ads + kk * 32), desc_mn_sw128(ak + kk * 2048, DQ_KTILE), IDESC_G,
                                 (i > 0 || kk > 0) ? 1u : 0u);
-                    }
                     mma_commit(kv_empty + s);
                     mma_commit(ds_empty);
                 }
@@ -758,90 +771,91 @@ __global__ void __launch_bounds__(320, 1)
         const int q = q0 + row;
         const bool qin = q < L;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        constexpr int HK = BK / 2;
+        constexpr int HK = DQ_BK / 2;
         const float sl2 = p.scale * LOG2E;
         const size_t at = static_cast<size_t>(seg0 + (qin ? q : 0)) * p.heads + head;
         const float lse2 = qin ? __ldg(p.lse + at) * LOG2E : 0.f, dd = qin ? __ldg(p.dsum + at) : 0.f;
-        // keys this row sees: [lo, lo + span] (none for rows past the segment)
+        // keys this row sees: [lo, lo + span]
         const int lo = global ? 0 : max(0, q - W);
         const int span = (global ? L - 1 : min(L - 1, q + W)) - lo;
+        uint8_t* drow = sDS + row * 128;
         bool ok = true;
         for (int j = 0; j < nk; ++j) {
             ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err));
-            if (ok) tc_fence_after();
-            const int k0 = kb + j * BK + half * HK;
-            uint8_t* drow = sDS + half * TILE + row * 128;
-            // two 32-key chunks: the second chunk's TMEM reads release S and dP to the next tile's MMAs
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t sv[32], dv[32];
-                if (ok) {
-                    tmem_ld32(tS + lane_off + half * HK + c * 32, sv);
-                    tmem_ld32(tDP + lane_off + half * HK + c * 32, dv);
-                    tmem_ld_wait();
-                }
-                if (c == 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(st_free);
-                }
-                if (!ok) continue;
-                DropWalk walk(p.seed, head, seg0 + q, k0 + c * 32, 1, p.dropout, p.keep);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int k = k0 + c * 32 + e;
-                    const bool vis = qin && static_cast<unsigned>(k - lo) <= static_cast<unsigned>(span);
-                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse2)) : 0.f;
-                    const float m = DROP ? walk.next() : 1.0f;
-                    sv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
-                }
-                // dS of the previous tile must have been read by its dQ MMAs before it is rewritten; waiting only
-                // now lets the first chunk's exponentials overlap those MMAs
-                if (c == 0 && j > 0) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(ds_empty, (j - 1) & 1, abort_flag, p.err));
-                    if (!ok) continue;
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
-                    *reinterpret_cast<uint4*>(drow + (((c * 4 + u) ^ (row & 7)) << 4)) =
-                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-                }
+            const int k0 = kb + j * DQ_BK + half * HK;
+            uint32_t sv[32], dv[32];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(tS + lane_off + half * HK, sv);
+                tmem_ld32(tDP + lane_off + half * HK, dv);
+                tmem_ld_wait();
             }
+            // S and dP are in registers: release them to the next tile's MMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(st_free);
             if (!ok) continue;
+            DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const bool vis = qin && static_cast<unsigned>(k0 + e - lo) <= static_cast<unsigned>(span);
+                const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse2)) : 0.f;
+                const float m = DROP ? walk.next() : 1.0f;
+                sv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+            }
+            // dS of the previous tile must have been read by its dQ MMAs before it is rewritten
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(ds_empty, (j - 1) & 1, abort_flag, p.err));
+                if (!ok) continue;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                *reinterpret_cast<uint4*>(drow + (((half * 4 + u) ^ (row & 7)) << 4)) =
+                    make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+            }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(ds_full);
         }
-        // dQ once the last dQ MMAs are done: half 0 rotates the whole row back by −θ and stores it
+        // dQ once the last dQ MMAs are done: half h rotates the pairs (i, i + 32) for i in [16h, 16h + 16) back by
+        // −θ and stores them
         ok = __all_sync(0xffffffffu, ok && nk > 0 && mbar_wait(ds_empty, (nk - 1) & 1, abort_flag, p.err));
-        if (ok && half == 0) {
+        if (ok) {
             tc_fence_after();
-            uint32_t a[HD];
-            tmem_ld32(tDQ + lane_off, *reinterpret_cast<uint32_t(*)[32]>(a));
-            tmem_ld32(tDQ + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(a + 32));
+            uint32_t x[16], y[16];
+            tmem_ld16(tDQ + lane_off + half * 16, x);
+            tmem_ld16(tDQ + lane_off + 32 + half * 16, y);
             tmem_ld_wait();
             if (qin) {
-                float f[HD];
+                float a[16], b[16];
 #pragma unroll
-                for (int e = 0; e < HD; ++e) f[e] = __uint_as_float(a[e]);
+                for (int e = 0; e < 16; ++e) {
+                    a[e] = __uint_as_float(x[e]);
+                    b[e] = __uint_as_float(y[e]);
+                }
                 if (p.cosv) {
 #pragma unroll
-                    for (int i = 0; i < HD / 2; ++i) {
+                    for (int e = 0; e < 16; ++e) {
+                        const int i = half * 16 + e;
                         const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
                         const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
-                        const float x = f[i], y = f[i + HD / 2];
-                        f[i] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
-                        f[i + HD / 2] = __fsub_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+                        const float u = a[e], v = b[e];
+                        a[e] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
+                        b[e] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
                     }
                 }
-                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + q) * p.lddq + head * HD;
+                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + q) * p.lddq + head * HD + half * 16;
 #pragma unroll
-                for (int t = 0; t < HD / 8; ++t)
+                for (int t = 0; t < 2; ++t) {
                     *reinterpret_cast<uint4*>(out + 8 * t) =
-                        make_uint4(pack2(f[8 * t], f[8 * t + 1]), pack2(f[8 * t + 2], f[8 * t + 3]),
-                                   pack2(f[8 * t + 4], f[8 * t + 5]), pack2(f[8 * t + 6], f[8 * t + 7]));
+                        make_uint4(pack2(a[8 * t], a[8 * t + 1]), pack2(a[8 * t + 2], a[8 * t + 3]),
+                                   pack2(a[8 * t + 4], a[8 * t + 5]), pack2(a[8 * t + 6], a[8 * t + 7]));
+                    *reinterpret_cast<uint4*>(out + 32 + 8 * t) =
+                        make_uint4(pack2(b[8 * t], b[8 * t + 1]), pack2(b[8 * t + 2], b[8 * t + 3]),
+                                   pack2(b[8 * t + 4], b[8 * t + 5]), pack2(b[8 * t + 6], b[8 * t + 7]));
+                }
             }
         }
     }
@@ -850,7 +864,7 @@ __global__ void __launch_bounds__(320, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc(tmem, 256);
     }
 }
 
@@ -937,11 +951,13 @@ int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s) {
 
 template <bool DROP>
 static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
-    CUtensorMap tq, tdo;
+    CUtensorMap tq, tkv, tdo;
     int rc = make_tmap_2d(&tq, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
-                          static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+                          static_cast<uint64_t>(a.ld) * 2, fat::BQ, fat::HD, true);
+    if (!rc) rc = make_tmap_2d(&tkv, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                               static_cast<uint64_t>(a.ld) * 2, fat::DQ_BK, fat::HD, true);
     if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
-                               static_cast<uint64_t>(a.ldo) * 2, fat::BK, fat::HD, true);
+                               static_cast<uint64_t>(a.ldo) * 2, fat::BQ, fat::HD, true);
     if (rc) return rc;
     static bool attr[64] = {false};
     int dev = 0;
@@ -958,7 +974,7 @@ static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
-    fat::bwd_dq_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::DQ_SMEM, s>>>(tq, tdo, p);
+    fat::bwd_dq_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::DQ_SMEM, s>>>(tq, tkv, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
