@@ -834,7 +834,7 @@ def run_ours(args):
                              "traffic": traffic.get("bf16_gemm", {}).get("dram_bytes_per_launch"),
                              "launches": g_n, "share_of_step": g_ms / args.steps / ms,
                              "flops_per_launch": g_fl / g_n if g_n else None},
-                "attention": {"kernels": "tcgen05 flash forward and dK/dV (head_dim 64), mma.sync dQ",
+                "attention": {"kernels": "tcgen05 flash forward, dK/dV and dQ (head_dim 64)",
                               "fwd_tflops": af_fl / (af_ms / 1e3) / 1e12 if af_ms else None,
                               "bwd_tflops": ab_fl / (ab_ms / 1e3) / 1e12 if ab_ms else None,
                               "share_of_step": (af_ms + ab_ms) / args.steps / ms},
