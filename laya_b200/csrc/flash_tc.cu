@@ -389,12 +389,13 @@ __global__ void __launch_bounds__(320, 1)
 
 // ------------------------------------------------------------------------------------------------ backward: dK, dV
 // Same contract as fa::bwd_dkdv_kernel (flash.cu; Ops.AttentionBackward, Laya.Training/Ops.cs:368-470): for one
-// 128-key tile of one head, over every 128-query tile that sees it,
-//     Sᵀ = K·Qᵀ,  dPᵀ = V·dOᵀ  (M 128 keys, N 128 queries, K 64)          into TMEM columns [0, 128), [128, 256)
+// 128-key tile of one head, over every 64-query tile that sees it,
+//     Sᵀ = K·Qᵀ,  dPᵀ = V·dOᵀ  (M 128 keys, N 64 queries, K 64)            into TMEM columns [0, 64), [64, 128)
 //     Pᵀ = exp(scale·Sᵀ − lse) (· dropout),  dSᵀ = scale · P ∘ (dPᵀ·m − D)   by the softmax warps, bf16 into smem
-//     dV += Pᵀ·dO,  dK += dSᵀ·Q  (M 128 keys, N 64, K 128 queries; dO and Q read N-contiguous) into [256, 384)
+//     dV += Pᵀ·dO,  dK += dSᵀ·Q  (M 128 keys, N 64, K 64 queries; dO and Q read N-contiguous) into [128, 256)
 // then dK (rotated back by −θ at the key's position) and dV in bf16.  lse and D of the query tile are staged next to
-// its Q and dO tiles by the producer warp.
+// its Q and dO tiles by the producer warp.  64-query tiles keep a CTA within 256 TMEM columns and ~98 KB of shared
+// memory, so two CTAs share an SM and one's MMA round trips overlap the other's softmax.
 struct BwdParams {
     const int32_t* seg_start; const int32_t* seg_len;
     const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq;
@@ -406,14 +407,27 @@ struct BwdParams {
     __nv_bfloat16* dqkv; int lddq;
     int* err;
 };
-constexpr int BWD_SMEM = 1024 + 10 * TILE + 2 * 2 * BQ * 4 + 256;   // K, V, 2 × (Q, dO), Pᵀ (2), dSᵀ (2); lse/D
+constexpr int BQ2 = 64;                          // queries per tile of the dK/dV kernel
+constexpr int QTILE2 = BQ2 * 128;                // bytes of one 64-row × 64-column bf16 tile
+constexpr int BWD_SMEM = 1024 + 2 * TILE + 4 * QTILE2 + 2 * TILE + 2 * 2 * BQ2 * 4 + 256;   // K, V, 2 × (Q, dO),
+                                                                                             // Pᵀ, dSᵀ; lse/D
+static_assert(2 * BWD_SMEM <= 232448, "two CTAs per SM");
 
-static_assert(BWD_SMEM <= 232448, "shared memory budget");
+DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
 
 template <bool DROP>
-__global__ void __launch_bounds__(320, 1)
-    bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmqkv, const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
-    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BK, BQ);                     // M keys, N queries, K-major
+__global__ void __launch_bounds__(320, 2)
+    bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmq,
+                       const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
+    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BK, BQ2);                    // M keys, N queries, K-major
     constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BK, HD) | (1u << 16);        // B (dO, Q) N-contiguous
     const int tile = blockIdx.x;
     if (tile >= *p.n_tq) return;
@@ -421,11 +435,11 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sK = smem;
     uint8_t* sV = smem + TILE;
-    uint8_t* sQO = smem + 2 * TILE;        // [2 stages][Q, dO]
-    uint8_t* sP = smem + 6 * TILE;         // Pᵀ: 2 sub-tiles of 64 queries
-    uint8_t* sDS = smem + 8 * TILE;        // dSᵀ: 2 sub-tiles
-    float* sRow = reinterpret_cast<float*>(smem + 10 * TILE);   // [2 stages][lse 128 | D 128]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + 2 * 2 * BQ);
+    uint8_t* sQO = smem + 2 * TILE;              // [2 stages][Q, dO], 64 rows each
+    uint8_t* sP = sQO + 4 * QTILE2;              // Pᵀ [128 keys × 64 queries]
+    uint8_t* sDS = sP + TILE;                    // dSᵀ
+    float* sRow = reinterpret_cast<float*>(sDS + TILE);   // [2 stages][lse 64 | D 64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + 2 * 2 * BQ2);
     uint64_t* kv_full = bars;
     uint64_t* full = bars + 1;        // [2]
     uint64_t* empty = bars + 3;       // [2]
@@ -441,7 +455,7 @@ __global__ void __launch_bounds__(320, 1)
     const bool global = p.window < 0;
     const int W = p.window;
     const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? L : min(L, k0 + BK + W);
-    const int nq = (qe - qb0 + BQ - 1) / BQ;
+    const int nq = (qe - qb0 + BQ2 - 1) / BQ2;
     const int warp = warp_id(), lane = lane_id();
 
     if (threadIdx.x == 0) {
@@ -454,20 +468,20 @@ __global__ void __launch_bounds__(320, 1)
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
-    if (warp == 0 && lane == 0) { prefetch_tmap(&tmqkv); prefetch_tmap(&tmdo); }
+    if (warp == 1) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) { prefetch_tmap(&tmk); prefetch_tmap(&tmq); prefetch_tmap(&tmdo); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tDP = tmem + BQ, tDV = tmem + 2 * BQ, tDK = tmem + 2 * BQ + HD;
+    const uint32_t tS = tmem, tDP = tmem + BQ2, tDV = tmem + 2 * BQ2, tDK = tmem + 2 * BQ2 + HD;
 
     if (warp == 0) {
         // ---- producer: K and V once; per query tile Q and dO by TMA, lse and D by the warp's lanes
         if (lane == 0) {
             mbar_arrive_expect_tx(kv_full, 2 * TILE);
-            tma_load_2d(sK, &tmqkv, kv_full, p.hidden + head * HD, seg0 + k0);
-            tma_load_2d(sV, &tmqkv, kv_full, 2 * p.hidden + head * HD, seg0 + k0);
+            tma_load_2d(sK, &tmk, kv_full, p.hidden + head * HD, seg0 + k0);
+            tma_load_2d(sV, &tmk, kv_full, 2 * p.hidden + head * HD, seg0 + k0);
         }
         for (int j = 0; j < nq; ++j) {
             const int s = j & 1;
@@ -475,20 +489,20 @@ __global__ void __launch_bounds__(320, 1)
             if (lane == 0) got = mbar_wait(empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err);
             if (!__shfl_sync(0xffffffffu, got, 0)) break;
             __syncwarp();
-            const int q0 = qb0 + j * BQ;
+            const int q0 = qb0 + j * BQ2;
             if (lane == 0) {
-                mbar_arrive_expect_tx(full + s, 2 * TILE);
-                tma_load_2d(sQO + s * 2 * TILE, &tmqkv, full + s, head * HD, seg0 + q0);
-                tma_load_2d(sQO + s * 2 * TILE + TILE, &tmdo, full + s, head * HD, seg0 + q0);
+                mbar_arrive_expect_tx(full + s, 2 * QTILE2);
+                tma_load_2d(sQO + s * 2 * QTILE2, &tmq, full + s, head * HD, seg0 + q0);
+                tma_load_2d(sQO + s * 2 * QTILE2 + QTILE2, &tmdo, full + s, head * HD, seg0 + q0);
             }
-            float* rows = sRow + s * 2 * BQ;
+            float* rows = sRow + s * 2 * BQ2;
 #pragma unroll
-            for (int i = 0; i < BQ / 32; ++i) {
+            for (int i = 0; i < BQ2 / 32; ++i) {
                 const int r = lane + 32 * i;
                 const bool in = q0 + r < qe;
                 const size_t at = static_cast<size_t>(seg0 + (in ? q0 + r : 0)) * p.heads + head;
                 rows[r] = in ? __ldg(p.lse + at) : 0.f;
-                rows[BQ + r] = in ? __ldg(p.dsum + at) : 0.f;
+                rows[BQ2 + r] = in ? __ldg(p.dsum + at) : 0.f;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(full + s);
@@ -505,7 +519,7 @@ __global__ void __launch_bounds__(320, 1)
                     if (!mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err)) break;
                     if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
                     tc_fence_after();
-                    const uint32_t aq = smem_u32(sQO + s * 2 * TILE), ado = aq + TILE;
+                    const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {
                         mma_f16(tS, smem_desc_sw128(ak + kk * 32), smem_desc_sw128(aq + kk * 32), IDESC_S, kk > 0);
@@ -517,14 +531,13 @@ __global__ void __launch_bounds__(320, 1)
                     const int i = j - 1, s = i & 1;
                     if (!mbar_wait(pd_full, i & 1, abort_flag, p.err)) break;
                     tc_fence_after();
-                    const uint32_t aq = smem_u32(sQO + s * 2 * TILE), ado = aq + TILE;
+                    const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
                     const uint32_t ap = smem_u32(sP), ad = smem_u32(sDS);
 #pragma unroll
-                    for (int kk = 0; kk < BQ / 16; ++kk) {
-                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                    for (int kk = 0; kk < BQ2 / 16; ++kk) {
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                        mma_f16(tDV, smem_desc_sw128(ap + po), desc_mn_sw128(ado + kk * 2048, TILE), IDESC_G, acc);
-                        mma_f16(tDK, smem_desc_sw128(ad + po), desc_mn_sw128(aq + kk * 2048, TILE), IDESC_G, acc);
+                        mma_f16(tDV, smem_desc_sw128(ap + kk * 32), desc_mn_sw128(ado + kk * 2048, QTILE2), IDESC_G, acc);
+                        mma_f16(tDK, smem_desc_sw128(ad + kk * 32), desc_mn_sw128(aq + kk * 2048, QTILE2), IDESC_G, acc);
                     }
                     mma_commit(empty + s);
                     mma_commit(pd_empty);
@@ -532,102 +545,123 @@ __global__ void __launch_bounds__(320, 1)
             }
         }
     } else {
-        // ---- softmax warps: thread (half, row) owns key row `row` and queries [64·half, 64·half + 64) of a tile
+        // ---- softmax warps: thread (half, row) owns key row `row` and queries [32·half, 32·half + 32) of a tile
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         const int key = k0 + row;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        constexpr int HQ = BQ / 2;
+        constexpr int HQ = BQ2 / 2;
         const float sl2 = p.scale * LOG2E;
+        uint8_t* prow = sP + row * 128;
+        uint8_t* drow = sDS + row * 128;
         bool ok = true;
         for (int j = 0; j < nq; ++j) {
             const int s = j & 1;
             ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err) &&
                                              mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err));
-            if (ok) tc_fence_after();
-            const float* rows = sRow + s * 2 * BQ;
-            const int q0 = qb0 + j * BQ + half * HQ;
-            uint8_t* prow = sP + half * TILE + row * 128;
-            uint8_t* drow = sDS + half * TILE + row * 128;
-            // two 32-query chunks: the second chunk's TMEM reads release the score buffers to the next tile's MMAs
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t sv[32], dv[32];
-                if (ok) {
-                    tmem_ld32(tS + lane_off + half * HQ + c * 32, sv);
-                    tmem_ld32(tDP + lane_off + half * HQ + c * 32, dv);
-                    tmem_ld_wait();
-                }
-                if (c == 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(st_free);
-                }
-                if (!ok) continue;
-                fat::DropWalk walk(p.seed, head, seg0 + q0 + c * 32, key, 1ull << 21, p.dropout, p.keep);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int qi = half * HQ + c * 32 + e, q = q0 + c * 32 + e;
-                    const float lse = rows[qi], dd = rows[BQ + qi];
-                    const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
-                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
-                    const float m = DROP ? walk.next() : 1.0f;
-                    sv[e] = __float_as_uint(pe * m);
-                    dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
-                }
-                // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten;
-                // waiting only now lets the first chunk's exponentials overlap those MMAs
-                if (c == 0 && j > 0) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
-                    if (!ok) continue;
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
-                    const float* g = reinterpret_cast<const float*>(dv + 8 * u);
-                    const int off = ((c * 4 + u) ^ (row & 7)) << 4;
-                    *reinterpret_cast<uint4*>(prow + off) =
-                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-                    *reinterpret_cast<uint4*>(drow + off) =
-                        make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
-                }
+            const float* rows = sRow + s * 2 * BQ2;
+            const int q0 = qb0 + j * BQ2 + half * HQ;
+            uint32_t sv[32], dv[32];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(tS + lane_off + half * HQ, sv);
+                tmem_ld32(tDP + lane_off + half * HQ, dv);
+                tmem_ld_wait();
             }
+            // Sᵀ and dPᵀ are in registers: release them to the next tile's MMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(st_free);
             if (!ok) continue;
+            fat::DropWalk walk(p.seed, head, seg0 + q0, key, 1ull << 21, p.dropout, p.keep);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int qi = half * HQ + e, q = q0 + e;
+                const float lse = rows[qi], dd = rows[BQ2 + qi];
+                const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
+                const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
+                const float m = DROP ? walk.next() : 1.0f;
+                sv[e] = __float_as_uint(pe * m);
+                dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+            }
+            // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+                if (!ok) continue;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                const float* g = reinterpret_cast<const float*>(dv + 8 * u);
+                const int off = ((half * 4 + u) ^ (row & 7)) << 4;
+                *reinterpret_cast<uint4*>(prow + off) =
+                    make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                *reinterpret_cast<uint4*>(drow + off) =
+                    make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
+            }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(pd_full);
         }
-        // dK (half 0, rotated back by −θ) and dV (half 1) once the last dV/dK MMAs are done
+        // dK (half 0, rotated back by −θ, pairs (i, i + 32) sixteen at a time) and dV (half 1, 32 columns at a time)
+        // once the last dV/dK MMAs are done
         ok = __all_sync(0xffffffffu, ok && nq > 0 && mbar_wait(pd_empty, (nq - 1) & 1, abort_flag, p.err));
         if (ok) {
             tc_fence_after();
-            uint32_t a[HD];
-            const uint32_t src = (half == 0 ? tDK : tDV) + lane_off;
-            tmem_ld32(src, *reinterpret_cast<uint32_t(*)[32]>(a));
-            tmem_ld32(src + 32, *reinterpret_cast<uint32_t(*)[32]>(a + 32));
-            tmem_ld_wait();
-            if (key < L) {
-                float f[HD];
+            __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + key) * p.lddq + (half == 0 ? p.hidden : 2 * p.hidden) + head * HD;
+            if (half == 0) {
+#pragma unroll 1
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t x[16], y[16];
+                    tmem_ld16(tDK + lane_off + pc * 16, x);
+                    tmem_ld16(tDK + lane_off + 32 + pc * 16, y);
+                    tmem_ld_wait();
+                    if (key < L) {
+                        float a[16], b[16];
 #pragma unroll
-                for (int e = 0; e < HD; ++e) f[e] = __uint_as_float(a[e]);
-                if (half == 0 && p.cosv) {
+                        for (int e = 0; e < 16; ++e) {
+                            a[e] = __uint_as_float(x[e]);
+                            b[e] = __uint_as_float(y[e]);
+                        }
+                        if (p.cosv) {
 #pragma unroll
-                    for (int i = 0; i < HD / 2; ++i) {
-                        const float c = p.cosv[static_cast<size_t>(key) * (HD / 2) + i];
-                        const float sn = p.sinv[static_cast<size_t>(key) * (HD / 2) + i];
-                        const float x = f[i], y = f[i + HD / 2];
-                        f[i] = __fadd_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
-                        f[i + HD / 2] = __fsub_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+                            for (int e = 0; e < 16; ++e) {
+                                const int i = pc * 16 + e;
+                                const float c = p.cosv[static_cast<size_t>(key) * (HD / 2) + i];
+                                const float sn = p.sinv[static_cast<size_t>(key) * (HD / 2) + i];
+                                const float u = a[e], v = b[e];
+                                a[e] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
+                                b[e] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                            }
+                        }
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            *reinterpret_cast<uint4*>(out + pc * 16 + 8 * t) =
+                                make_uint4(pack2(a[8 * t], a[8 * t + 1]), pack2(a[8 * t + 2], a[8 * t + 3]),
+                                           pack2(a[8 * t + 4], a[8 * t + 5]), pack2(a[8 * t + 6], a[8 * t + 7]));
+                            *reinterpret_cast<uint4*>(out + 32 + pc * 16 + 8 * t) =
+                                make_uint4(pack2(b[8 * t], b[8 * t + 1]), pack2(b[8 * t + 2], b[8 * t + 3]),
+                                           pack2(b[8 * t + 4], b[8 * t + 5]), pack2(b[8 * t + 6], b[8 * t + 7]));
+                        }
                     }
                 }
-                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + key) * p.lddq + (half == 0 ? p.hidden : 2 * p.hidden) + head * HD;
+            } else {
+#pragma unroll 1
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t x[32];
+                    tmem_ld32(tDV + lane_off + pc * 32, x);
+                    tmem_ld_wait();
+                    if (key < L) {
 #pragma unroll
-                for (int t = 0; t < HD / 8; ++t)
-                    *reinterpret_cast<uint4*>(out + 8 * t) =
-                        make_uint4(pack2(f[8 * t], f[8 * t + 1]), pack2(f[8 * t + 2], f[8 * t + 3]),
-                                   pack2(f[8 * t + 4], f[8 * t + 5]), pack2(f[8 * t + 6], f[8 * t + 7]));
+                        for (int t = 0; t < 4; ++t) {
+                            const float* f = reinterpret_cast<const float*>(x + 8 * t);
+                            *reinterpret_cast<uint4*>(out + pc * 32 + 8 * t) =
+                                make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                        }
+                    }
+                }
             }
         }
     }
@@ -636,7 +670,7 @@ __global__ void __launch_bounds__(320, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc(tmem, 256);
     }
 }
 
@@ -655,15 +689,6 @@ constexpr int DQ_KTILE = DQ_BK * 128;                        // bytes of one 64-
 constexpr int DQ_SMEM = 1024 + 2 * TILE + 4 * DQ_KTILE + TILE + 256;   // Q, dO, 2 × (K, V), dS; barriers
 static_assert(2 * DQ_SMEM <= 232448, "two CTAs per SM");
 
-DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-}
 
 template <bool DROP>
 __global__ void __launch_bounds__(320, 2)
@@ -913,11 +938,13 @@ int flash_forward_tc(const fa::Args& a, cudaStream_t s) {
 
 template <bool DROP>
 static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
-    CUtensorMap tq, tdo;
-    int rc = make_tmap_2d(&tq, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+    CUtensorMap tk, tq, tdo;
+    int rc = make_tmap_2d(&tk, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
                           static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (!rc) rc = make_tmap_2d(&tq, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                               static_cast<uint64_t>(a.ld) * 2, fat::BQ2, fat::HD, true);
     if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
-                               static_cast<uint64_t>(a.ldo) * 2, fat::BK, fat::HD, true);
+                               static_cast<uint64_t>(a.ldo) * 2, fat::BQ2, fat::HD, true);
     if (rc) return rc;
     static bool attr[64] = {false};
     int dev = 0;
@@ -934,7 +961,7 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
-    fat::bwd_dkdv_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::BWD_SMEM, s>>>(tq, tdo, p);
+    fat::bwd_dkdv_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::BWD_SMEM, s>>>(tk, tq, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
