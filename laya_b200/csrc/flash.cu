@@ -336,19 +336,30 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
     }
 }
 
-// D_i = Σ_d dO · O per (token, head), fp32.
+// D_i = Σ_d dO · O per (token, head), fp32.  HD/8 lanes per (token, head), each reading 8 consecutive bf16 of dO
+// and O with one 16-byte load apiece, then a shuffle sum over the group.
+template <int HD>
 __global__ void bwd_dot_kernel(Args a, int T) {
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (gw >= T * a.heads) return;
-    const int t = gw / a.heads, h = gw % a.heads;
-    const int hd = a.hidden / a.heads;
+    constexpr int G = HD / 8;   // lanes per (token, head)
+    const int gt = blockIdx.x * blockDim.x + threadIdx.x;
+    const int item = gt / G, l = gt % G;
+    const bool active = item < T * a.heads;
+    const int it = active ? item : 0;
+    const int t = it / a.heads, h = it % a.heads;
+    const size_t off = static_cast<size_t>(t) * a.ldo + h * HD + 8 * l;
+    const uint4 x = *reinterpret_cast<const uint4*>(a.dout + off), y = *reinterpret_cast<const uint4*>(a.out + off);
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
     float s = 0.f;
-    for (int d = lane; d < hd; d += 32) {
-        s += __bfloat162float(a.dout[static_cast<size_t>(t) * a.ldo + h * hd + d]) *
-             __bfloat162float(a.out[static_cast<size_t>(t) * a.ldo + h * hd + d]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 u = __bfloat1622float2(xa[k]), v = __bfloat1622float2(ya[k]);
+        s = fmaf(u.x, v.x, s);
+        s = fmaf(u.y, v.y, s);
     }
-    s = warp_sum(s);
-    if (lane == 0) a.dsum[static_cast<size_t>(t) * a.heads + h] = s;
+#pragma unroll
+    for (int m = G / 2; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+    if (active && l == 0) a.dsum[static_cast<size_t>(t) * a.heads + h] = s;
 }
 
 // Writes 16 rows x HD of a warp's fp32 accumulator as bf16 into a [T, ld] slice, rotating back by -θ when given.
@@ -655,8 +666,13 @@ static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
     if (max_tiles <= 0 || T <= 0) return OK;
     const int hd = a.hidden / a.heads;
-    const long long warps = static_cast<long long>(T) * a.heads;
-    fa::bwd_dot_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(a, T);
+    const long long threads = static_cast<long long>(T) * a.heads * (hd / 8);
+    if ((a.ldo & 7) || (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15)) {
+        set_error("attention backward: dO and O need 16-byte aligned rows");
+        return ERR_ARGUMENT;
+    }
+    if (hd == 64) fa::bwd_dot_kernel<64><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(a, T);
+    else if (hd == 32) fa::bwd_dot_kernel<32><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(a, T);
     count_launch();
     int rc;
     if (hd == 64) rc = launch_bwd<64>(a, max_tiles, s);

@@ -252,6 +252,12 @@ __global__ void __launch_bounds__(256) ln_bwd_vec_kernel(LnBwd a) {
         const float* xr = a.x + static_cast<size_t>(a.gather ? a.gather[r] : r) * n + 4 * lane;
         const float* dyr = a.dy + static_cast<size_t>(r) * n + 4 * lane;
         const float mean = a.mean[r], rstd = a.rstd[r];
+        float* dst = a.dx ? a.dx + static_cast<size_t>(a.scatter ? a.scatter[r] : r) * n + 4 * lane : nullptr;
+        // the accumulated dx is read with the row's inputs, so the row waits on one round of loads
+        const bool acc_in = dst && a.accumulate && !a.scatter;
+        float4 prev[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) prev[i] = acc_in ? ld4(dst + 128 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 xh[VPL], g[VPL];
         float sg = 0.f, sgx = 0.f;
 #pragma unroll
@@ -265,8 +271,7 @@ __global__ void __launch_bounds__(256) ln_bwd_vec_kernel(LnBwd a) {
             pb[i].x += dy.x; pb[i].y += dy.y; pb[i].z += dy.z; pb[i].w += dy.w;
         }
         const float mg = warp_sum(sg) / n, mgx = warp_sum(sgx) / n;
-        if (a.dx) {
-            float* dst = a.dx + static_cast<size_t>(a.scatter ? a.scatter[r] : r) * n + 4 * lane;
+        if (dst) {
 #pragma unroll
             for (int i = 0; i < VPL; ++i) {
                 float4 d = make_float4(rstd * (g[i].x - mg - xh[i].x * mgx), rstd * (g[i].y - mg - xh[i].y * mgx),
@@ -276,8 +281,7 @@ __global__ void __launch_bounds__(256) ln_bwd_vec_kernel(LnBwd a) {
                     atomicAdd(p, d.x); atomicAdd(p + 1, d.y); atomicAdd(p + 2, d.z); atomicAdd(p + 3, d.w);
                 } else {
                     if (a.accumulate) {
-                        const float4 o = ld4(p);
-                        d.x += o.x; d.y += o.y; d.z += o.z; d.w += o.w;
+                        d.x += prev[i].x; d.y += prev[i].y; d.z += prev[i].z; d.w += prev[i].w;
                     }
                     *reinterpret_cast<float4*>(p) = d;
                 }
@@ -457,6 +461,41 @@ __global__ void colsum_kernel(const T* __restrict__ d, int rows, int n, float* _
         else s += bf(d[static_cast<size_t>(r) * n + c]);
     }
     atomicAdd(db + c, s);
+}
+
+// db[c] += Σ_r d[r, c] for bf16 d with n a multiple of 8: a CTA takes 256 rows × 256 columns, thread (row lane rl,
+// column group cg) summing 8 columns of rows rl, rl + 8, … with one 16-byte load per row; the 8 row lanes then meet in
+// shared memory.
+constexpr int CS_ROWS = 256;
+__global__ void __launch_bounds__(256) colsum8_kernel(const __nv_bfloat16* __restrict__ d, int rows, int n,
+                                                      float* __restrict__ db) {
+    __shared__ float part[8][256];
+    const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
+    const int c0 = blockIdx.y * 256 + cg * 8;
+    const int r0 = blockIdx.x * CS_ROWS, r1 = min(rows, r0 + CS_ROWS);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (c0 < n) {
+        for (int r = r0 + rl; r < r1; r += 8) {
+            const uint4 x = *reinterpret_cast<const uint4*>(d + static_cast<size_t>(r) * n + c0);
+            const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 u = __bfloat1622float2(xa[k]);
+                acc[2 * k] += u.x;
+                acc[2 * k + 1] += u.y;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) part[rl][cg * 8 + k] = acc[k];
+    __syncthreads();
+    const int c = blockIdx.y * 256 + threadIdx.x;
+    if (c < n) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sum += part[q][threadIdx.x];
+        atomicAdd(db + c, sum);
+    }
 }
 
 // grad[ids[t]] += d[t]   (embedding rows)
@@ -856,6 +895,12 @@ int colsum_f32(const float* d, int rows, int n, float* db, cudaStream_t s) {
 }
 int colsum_bf16(const __nv_bfloat16* d, int rows, int n, float* db, cudaStream_t s) {
     if (rows <= 0 || n <= 0) return OK;
+    if (n % 8 == 0 && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+        tr::colsum8_kernel<<<dim3((rows + tr::CS_ROWS - 1) / tr::CS_ROWS, (n + 255) / 256), 256, 0, s>>>(d, rows, n, db);
+        count_launch();
+        LAYA_CUDA(cudaGetLastError());
+        return OK;
+    }
     dim3 grid((rows + 63) / 64, (n + 255) / 256);
     tr::colsum_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(d, rows, n, db);
     count_launch();
