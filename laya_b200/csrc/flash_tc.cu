@@ -123,14 +123,17 @@ struct DropWalk {
     }
 };
 
+// Persistent: a CTA walks work items (query tile, head) = blockIdx.x, blockIdx.x + gridDim.x, …, and every barrier
+// phase runs on across items (key tiles are counted globally), so the next item's Q and first K/V tiles load and its
+// first scores are computed while the softmax warps finish the current item.
 template <bool SPLIT, bool DROP>
 __global__ void __launch_bounds__(320, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml, Params p) {
     using C = Cfg<SPLIT>;
     constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, BK);                                   // K-major A, B
     constexpr uint32_t IDESC_PV = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);                      // B (V) MN-major
-    const int tile = blockIdx.x;
-    if (tile >= *p.n_tq) return;
+    const int n_items = *p.n_tq * p.heads;
+    if (static_cast<int>(blockIdx.x) >= n_items) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;                                   // [NQ] tiles
@@ -143,20 +146,32 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* s_full = bars + 5;        // [2] S buffers in TMEM
     uint64_t* p_full = bars + 7;        // [2] by tile parity
     uint64_t* o_done = bars + 9;        // [2] by tile parity
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    uint64_t* q_empty = bars + 11;      // Q read by the item's last score MMAs
+    uint64_t* o_free = bars + 12;       // O read by the item's epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* red = reinterpret_cast<float*>(bars + 32);   // [2 halves][BQ]: row maxima per tile, then the row sums
 
-    const int head = blockIdx.y, item = p.tq_item[tile], q0 = p.tq_p0[tile];
-    const int seg0 = p.seg_start[item], L = p.seg_len[item];
     const bool global = p.window < 0;
     const int W = p.window;
-    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + BQ + W);
-    const int nk = (ke - kb + BK - 1) / BK;
     const int warp = warp_id(), lane = lane_id();
+    // the key range of an item's query tile
+    auto span_of = [&](int item, int& head, int& seg0, int& L, int& q0, int& kb, int& nk) {
+        const int tile = item / p.heads;
+        head = item - tile * p.heads;
+        const int it = p.tq_item[tile];
+        q0 = p.tq_p0[tile];
+        seg0 = p.seg_start[it];
+        L = p.seg_len[it];
+        kb = global ? 0 : max(0, q0 - W);
+        const int ke = global ? L : min(L, q0 + BQ + W);
+        nk = (ke - kb + BK - 1) / BK;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(o_free, 8);
         for (int s = 0; s < 2; ++s) {
             mbar_init(kv_full + s, 1);
             mbar_init(kv_empty + s, 1);
@@ -177,73 +192,93 @@ __global__ void __launch_bounds__(320, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const int xq = head * HD, xk = p.hidden + head * HD, xv = 2 * p.hidden + head * HD;
-            mbar_arrive_expect_tx(q_full, C::NQ * TILE);
-            tma_load_2d(sQ, &tmh, q_full, xq, seg0 + q0);
-            if constexpr (SPLIT) tma_load_2d(sQ + TILE, &tml, q_full, xq, seg0 + q0);
-            for (int j = 0; j < nk; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
-                uint8_t* st = sKV + s * C::NKV * TILE;
-                const int y = seg0 + kb + j * BK;
-                mbar_arrive_expect_tx(kv_full + s, C::NKV * TILE);
-                tma_load_2d(st, &tmh, kv_full + s, xk, y);
-                tma_load_2d(st + TILE, &tmh, kv_full + s, xv, y);
-                if constexpr (SPLIT) {
-                    tma_load_2d(st + 2 * TILE, &tml, kv_full + s, xk, y);
-                    tma_load_2d(st + 3 * TILE, &tml, kv_full + s, xv, y);
+            uint32_t g = 0, n = 0;   // key tiles and items loaded so far
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+                int head, seg0, L, q0, kb, nk;
+                span_of(item, head, seg0, L, q0, kb, nk);
+                const int xq = head * HD, xk = p.hidden + head * HD, xv = 2 * p.hidden + head * HD;
+                if (!mbar_wait(q_empty, (n & 1) ^ 1, abort_flag, p.err)) break;
+                mbar_arrive_expect_tx(q_full, C::NQ * TILE);
+                tma_load_2d(sQ, &tmh, q_full, xq, seg0 + q0);
+                if constexpr (SPLIT) tma_load_2d(sQ + TILE, &tml, q_full, xq, seg0 + q0);
+                for (int j = 0; j < nk; ++j, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(kv_empty + s, ((g >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    uint8_t* st = sKV + s * C::NKV * TILE;
+                    const int y = seg0 + kb + j * BK;
+                    mbar_arrive_expect_tx(kv_full + s, C::NKV * TILE);
+                    tma_load_2d(st, &tmh, kv_full + s, xk, y);
+                    tma_load_2d(st + TILE, &tmh, kv_full + s, xv, y);
+                    if constexpr (SPLIT) {
+                        tma_load_2d(st + 2 * TILE, &tml, kv_full + s, xk, y);
+                        tma_load_2d(st + 3 * TILE, &tml, kv_full + s, xv, y);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // iteration j issues S_j (into TMEM buffer j % 2) and then P·V of tile j - 1, so the scores of the next
-            // tile are computed while the softmax warps work on the current one
-            bool ok = mbar_wait(q_full, 0, abort_flag, p.err);
-            tc_fence_after();
+            // per item, iteration j issues S_j (into TMEM buffer g % 2) and then P·V of tile j − 1, so the scores of
+            // the next tile are computed while the softmax warps work on the current one
+            uint32_t base = 0, n = 0;
+            bool ok = true;
             const uint32_t aq = smem_u32(sQ), aql = smem_u32(sQ + TILE);
-            for (int j = 0; j <= nk && ok; ++j) {
-                if (j < nk) {
-                    const int s = j & 1;
-                    if (!mbar_wait(kv_full + s, (j >> 1) & 1, abort_flag, p.err)) break;
-                    tc_fence_after();
-                    const uint32_t ak = smem_u32(sKV + s * C::NKV * TILE), akl = ak + 2 * TILE;
-                    const uint32_t d = tS + s * BK;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+                int head, seg0, L, q0, kb, nk;
+                span_of(item, head, seg0, L, q0, kb, nk);
+                if (!mbar_wait(q_full, n & 1, abort_flag, p.err)) break;
+                tc_fence_after();
+                for (int j = 0; j <= nk; ++j) {
+                    if (j < nk) {
+                        const uint32_t g = base + j;
+                        const int s = g & 1;
+                        if (!mbar_wait(kv_full + s, (g >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t ak = smem_u32(sKV + s * C::NKV * TILE), akl = ak + 2 * TILE;
+                        const uint32_t d = tS + s * BK;
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk)
-                        mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
-                    if constexpr (SPLIT) {
+                        for (int kk = 0; kk < HD / 16; ++kk)
+                            mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
+                        if constexpr (SPLIT) {
 #pragma unroll
-                        for (int kk = 0; kk < HD / 16; ++kk) {
-                            mma_f16(d, smem_desc_sw128(aql + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, 1u);
-                            mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(akl + kk * 32), IDESC_S, 1u);
+                            for (int kk = 0; kk < HD / 16; ++kk) {
+                                mma_f16(d, smem_desc_sw128(aql + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, 1u);
+                                mma_f16(d, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(akl + kk * 32), IDESC_S, 1u);
+                            }
                         }
+                        mma_commit(s_full + s);
+                        if (j == nk - 1) mma_commit(q_empty);   // Q free once the item's last scores are done
                     }
-                    mma_commit(s_full + s);
-                }
-                if (j >= 1) {
-                    const int i = j - 1, s = i & 1;
-                    if (!mbar_wait(p_full + s, (i >> 1) & 1, abort_flag, p.err)) break;
-                    tc_fence_after();
-                    const uint32_t av = smem_u32(sKV + s * C::NKV * TILE) + TILE, avl = av + 2 * TILE;
-                    const uint32_t ap = smem_u32(sP + (i % C::NPB) * C::NP * 2 * TILE), apl = ap + 2 * TILE;
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
-                        mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV,
-                                (i > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    if constexpr (SPLIT) {
+                    if (j >= 1) {
+                        const int i = j - 1;
+                        const uint32_t gi = base + i;
+                        const int s = gi & 1;
+                        if (!mbar_wait(p_full + s, (gi >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                        // the first P·V of an item overwrites O: the previous item's epilogue must have read it
+                        if (i == 0 && !mbar_wait(o_free, (n & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t av = smem_u32(sKV + s * C::NKV * TILE) + TILE, avl = av + 2 * TILE;
+                        const uint32_t ap = smem_u32(sP + (gi % C::NPB) * C::NP * 2 * TILE), apl = ap + 2 * TILE;
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) {
                             const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
-                            mma_f16(tO, smem_desc_sw128(apl + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV, 1u);
-                            mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(avl + kk * 2048, TILE), IDESC_PV, 1u);
+                            mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV,
+                                    (i > 0 || kk > 0) ? 1u : 0u);
                         }
+                        if constexpr (SPLIT) {
+#pragma unroll
+                            for (int kk = 0; kk < BK / 16; ++kk) {
+                                const uint32_t po = (kk >> 2) * TILE + (kk & 3) * 32;
+                                mma_f16(tO, smem_desc_sw128(apl + po), desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV, 1u);
+                                mma_f16(tO, smem_desc_sw128(ap + po), desc_mn_sw128(avl + kk * 2048, TILE), IDESC_PV, 1u);
+                            }
+                        }
+                        mma_commit(o_done + s);
+                        mma_commit(kv_empty + s);
                     }
-                    mma_commit(o_done + s);
-                    mma_commit(kv_empty + s);
                 }
+                base += nk;
             }
         }
     } else {
@@ -251,130 +286,144 @@ __global__ void __launch_bounds__(320, 1)
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
-        const int q = q0 + row;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         constexpr int HK = BK / 2, HO = HD / 2;
-        // keys this row sees: [lo, hi] (empty for rows past the segment)
-        const int lo = q < L ? (global ? 0 : max(0, q - W)) : 1;
-        const int hi = q < L ? (global ? L - 1 : min(L - 1, q + W)) : 0;
-        const uint32_t span = static_cast<uint32_t>(hi - lo);
-        float m_run = -INFINITY, l_run = 0.f;
-        // `ok` is kept warp-uniform and the loop never exits early: the 256 softmax threads take the same named
+        // `ok` is kept warp-uniform and the loops never exit early: the 256 softmax threads take the same named
         // barriers in every case (an aborted protocol only skips the work between them)
         bool ok = true;
-        for (int j = 0; j < nk; ++j) {
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full + (j & 1), (j >> 1) & 1, abort_flag, p.err));
-            const int k0 = kb + j * BK + half * HK;
-            uint32_t v[HK];
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (ok) {
-                tc_fence_after();
-                const uint32_t sb = tS + (j & 1) * BK;
+        uint32_t base = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            int head, seg0, L, q0, kb, nk;
+            span_of(item, head, seg0, L, q0, kb, nk);
+            const int q = q0 + row;
+            // keys this row sees: [lo, hi] (empty for rows past the segment)
+            const int lo = q < L ? (global ? 0 : max(0, q - W)) : 1;
+            const int hi = q < L ? (global ? L - 1 : min(L - 1, q + W)) : 0;
+            const uint32_t span = static_cast<uint32_t>(hi - lo);
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < nk; ++j) {
+                const uint32_t g = base + j;
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full + (g & 1), (g >> 1) & 1, abort_flag, p.err));
+                const int k0 = kb + j * BK + half * HK;
+                uint32_t v[HK];
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (ok) {
+                    tc_fence_after();
+                    const uint32_t sb = tS + (g & 1) * BK;
 #pragma unroll
-                for (int c = 0; c < HK / 32; ++c)
-                    tmem_ld32(sb + lane_off + half * HK + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < HK; ++e) {
-                    const bool vis = static_cast<uint32_t>(k0 + e - lo) <= span;
-                    const float x = vis ? __fmul_rn(__uint_as_float(v[e]), p.scale) : -INFINITY;
-                    v[e] = __float_as_uint(x);
-                    mx4[e & 3] = fmaxf(mx4[e & 3], x);
-                }
-            }
-            // the row max over both halves
-            red[half * BQ + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-            named_bar_sync(1, 256);
-            const float mx = fmaxf(red[row], red[BQ + row]);
-            named_bar_sync(1, 256);
-            if (!ok) continue;
-            // Lazy rescaling: the running max moves only when the tile's max exceeds it by more than RESCALE_GAP
-            // (natural log units), so probabilities stay below e^RESCALE_GAP and O is rescaled in TMEM rarely.  The
-            // result is the same softmax: every P of a row and its sum l use the same reference max.
-            const bool grow = mx > m_run + RESCALE_GAP;
-            const float m_new = grow ? mx : m_run;
-            const float alpha = (m_run == -INFINITY || !grow) ? (m_run == -INFINITY ? 0.f : 1.0f)
-                                                               : ex2(__fmul_rn(m_run - m_new, LOG2E));
-            const float msc = m_new == -INFINITY ? 0.f : m_new * LOG2E;
-            // P = exp(s - m); the row sum counts every probability, dropped or not
-            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-            DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
-#pragma unroll
-            for (int e = 0; e < HK; ++e) {
-                float pe = ex2(fmaf(__uint_as_float(v[e]), LOG2E, -msc));   // 2^-inf = 0 for masked keys
-                rs4[e & 3] += pe;
-                if constexpr (DROP) pe = pe * walk.next();
-                v[e] = __float_as_uint(pe);
-            }
-            // O may be rescaled only once P·V of the previous tile is done; the P buffer of this tile may be
-            // rewritten once the P·V that last read it (tile j - NPB) is done.  Waiting here, after the
-            // exponentials, lets them overlap that P·V.
-            const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
-            if (rescale || j >= C::NPB) {
-                const int i = rescale ? j - 1 : j - C::NPB;
-                ok = __all_sync(0xffffffffu, mbar_wait(o_done + (i & 1), (i >> 1) & 1, abort_flag, p.err));
-                if (!ok) continue;
-                tc_fence_after();
-                if (rescale) {
-                    uint32_t o[HO];
-                    tmem_ld32(tO + lane_off + half * HO, o);
+                    for (int c = 0; c < HK / 32; ++c)
+                        tmem_ld32(sb + lane_off + half * HK + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < HO; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tmem_st32(tO + lane_off + half * HO, o);
-                    tmem_st_wait();
-                }
-            }
-            // this half's 64 keys are sub-tile `half` of P buffer j % NPB: 16-byte chunk c of row `row`, swizzled by
-            // row % 8
-            uint8_t* prow = sP + (j % C::NPB) * C::NP * 2 * TILE + half * TILE + row * 128;
-#pragma unroll
-            for (int c = 0; c < HK / 8; ++c) {
-                const float* f = reinterpret_cast<const float*>(v + 8 * c);
-                uint8_t* dst = prow + ((c ^ (row & 7)) << 4);
-                *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]),
-                                                            pack2(f[6], f[7]));
-                if constexpr (SPLIT)
-                    *reinterpret_cast<uint4*>(dst + 2 * TILE) =
-                        make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
-                                   pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
-            }
-            l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
-            m_run = m_new;
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full + (j & 1));
-        }
-        // the row sum over both halves (every softmax thread reaches this barrier, aborted or not)
-        red[half * BQ + row] = l_run;
-        named_bar_sync(1, 256);
-        const float l_all = red[row] + red[BQ + row];
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(o_done + ((nk - 1) & 1), ((nk - 1) >> 1) & 1, abort_flag, p.err));
-        if (ok) {
-            tc_fence_after();
-            const float inv = l_all > 0.f ? 1.0f / l_all : 0.f;
-            uint32_t o[HO];
-            tmem_ld32(tO + lane_off + half * HO, o);
-            tmem_ld_wait();
-            if (q < L) {
-                __nv_bfloat16* orow = p.out + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
-#pragma unroll
-                for (int t = 0; t < HO / 8; ++t) {
-                    float f[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * t + e]) * inv;
-                    *reinterpret_cast<uint4*>(orow + 8 * t) =
-                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-                    if constexpr (SPLIT) {
-                        __nv_bfloat16* lrow = p.out_lo + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
-                        *reinterpret_cast<uint4*>(lrow + 8 * t) =
-                            make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
-                                       pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
+                    for (int e = 0; e < HK; ++e) {
+                        const bool vis = static_cast<uint32_t>(k0 + e - lo) <= span;
+                        const float x = vis ? __fmul_rn(__uint_as_float(v[e]), p.scale) : -INFINITY;
+                        v[e] = __float_as_uint(x);
+                        mx4[e & 3] = fmaxf(mx4[e & 3], x);
                     }
                 }
-                if (half == 0) p.lse[static_cast<size_t>(seg0 + q) * p.heads + head] = m_run + logf(l_all);
+                // the row max over both halves
+                red[half * BQ + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                named_bar_sync(1, 256);
+                const float mx = fmaxf(red[row], red[BQ + row]);
+                named_bar_sync(1, 256);
+                if (!ok) continue;
+                // Lazy rescaling: the running max moves only when the tile's max exceeds it by more than
+                // RESCALE_GAP (natural log units), so probabilities stay below e^RESCALE_GAP and O is rescaled in TMEM
+                // rarely.  Every P of a row and its sum l use the same reference max.
+                const bool grow = mx > m_run + RESCALE_GAP;
+                const float m_new = grow ? mx : m_run;
+                const float alpha = (m_run == -INFINITY || !grow) ? (m_run == -INFINITY ? 0.f : 1.0f)
+                                                                   : ex2(__fmul_rn(m_run - m_new, LOG2E));
+                const float msc = m_new == -INFINITY ? 0.f : m_new * LOG2E;
+                // P = exp(s - m); the row sum counts every probability, dropped or not
+                float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+                DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
+#pragma unroll
+                for (int e = 0; e < HK; ++e) {
+                    float pe = ex2(fmaf(__uint_as_float(v[e]), LOG2E, -msc));   // 2^-inf = 0 for masked keys
+                    rs4[e & 3] += pe;
+                    if constexpr (DROP) pe = pe * walk.next();
+                    v[e] = __float_as_uint(pe);
+                }
+                // O may be rescaled only once P·V of the previous tile is done; the P buffer of this tile may be
+                // rewritten once the P·V that last read it (tile g − NPB) is done — for an item's first tile the
+                // previous item's epilogue already waited for every earlier P·V.  Waiting here, after the
+                // exponentials, lets them overlap that P·V.
+                const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
+                if (rescale || j >= C::NPB) {
+                    const uint32_t i = rescale ? g - 1 : g - C::NPB;
+                    ok = __all_sync(0xffffffffu, mbar_wait(o_done + (i & 1), (i >> 1) & 1, abort_flag, p.err));
+                    if (!ok) continue;
+                    tc_fence_after();
+                    if (rescale) {
+                        uint32_t o[HO];
+                        tmem_ld32(tO + lane_off + half * HO, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < HO; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st32(tO + lane_off + half * HO, o);
+                        tmem_st_wait();
+                    }
+                }
+                // this half's 64 keys are sub-tile `half` of P buffer g % NPB: 16-byte chunk c of row `row`,
+                // swizzled by row % 8
+                uint8_t* prow = sP + (g % C::NPB) * C::NP * 2 * TILE + half * TILE + row * 128;
+#pragma unroll
+                for (int c = 0; c < HK / 8; ++c) {
+                    const float* f = reinterpret_cast<const float*>(v + 8 * c);
+                    uint8_t* dst = prow + ((c ^ (row & 7)) << 4);
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]),
+                                                                pack2(f[6], f[7]));
+                    if constexpr (SPLIT)
+                        *reinterpret_cast<uint4*>(dst + 2 * TILE) =
+                            make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
+                                       pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
+                }
+                l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+                m_run = m_new;
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full + (g & 1));
             }
+            // the row sum over both halves (every softmax thread reaches this barrier, aborted or not)
+            red[half * BQ + row] = l_run;
+            named_bar_sync(1, 256);
+            const float l_all = red[row] + red[BQ + row];
+            named_bar_sync(1, 256);   // both halves have read the sums before the next item's maxima overwrite them
+            const uint32_t last = base + nk - 1;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(o_done + (last & 1), (last >> 1) & 1, abort_flag, p.err));
+            if (ok) {
+                tc_fence_after();
+                const float inv = l_all > 0.f ? 1.0f / l_all : 0.f;
+                uint32_t o[HO];
+                tmem_ld32(tO + lane_off + half * HO, o);
+                tmem_ld_wait();
+                // O is in registers: the next item's first P·V may overwrite it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_free);
+                if (q < L) {
+                    __nv_bfloat16* orow = p.out + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
+#pragma unroll
+                    for (int t = 0; t < HO / 8; ++t) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * t + e]) * inv;
+                        *reinterpret_cast<uint4*>(orow + 8 * t) =
+                            make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                        if constexpr (SPLIT) {
+                            __nv_bfloat16* lrow = p.out_lo + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
+                            *reinterpret_cast<uint4*>(lrow + 8 * t) =
+                                make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
+                                           pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
+                        }
+                    }
+                    if (half == 0) p.lse[static_cast<size_t>(seg0 + q) * p.heads + head] = m_run + logf(l_all);
+                }
+            }
+            base += nk;
         }
     }
 
@@ -918,7 +967,10 @@ static int launch_tc(const fa::Args& a, cudaStream_t s) {
     p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.out = a.out; p.out_lo = a.out_lo; p.ldo = a.ldo; p.lse = a.lse; p.err = a.err;
-    fat::fwd_tc_kernel<SPLIT, DROP><<<dim3(a.max_tq, a.heads), 320, C::SMEM, s>>>(th, tl, p);
+    static int sms[64] = {0};
+    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    fat::fwd_tc_kernel<SPLIT, DROP><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, tl, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
