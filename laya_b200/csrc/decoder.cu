@@ -141,12 +141,15 @@ struct laya_decoder {
     // ptrs [2·layers·n_seq]: per layer two rows of one entry per sequence (full: keys, values; DeltaNet: conv tail,
     // recurrent state — 0 without a state), then [2·layers·n_snap] the same for the snapshots
     int32_t *pos0 = nullptr, *snap_begin = nullptr, *snap_at = nullptr;
+    int32_t *lt_seq = nullptr, *lt_p0 = nullptr;   // the attention tile holding each sequence's last row
+    float *xl = nullptr, *corel = nullptr;         // the last layer's readout rows: residual and attention output
     uint64_t* ptrs = nullptr;
     int cur_seqs = 0, cur_snaps = 0;
     bool with_states = false;
     int rope_cap = 0;
     std::set<laya_decoder_state*> states;
     std::set<laya_decoder_mark*> marks;
+    cudaMemPool_t pool = nullptr;   // state and mark blocks: freed blocks stay in the pool for the next request
 
     // profiling: 0 products, 1 delta rule, 2 full attention
     bool profiling = false;
@@ -288,9 +291,9 @@ int product(laya_decoder* c, const QMat& w, int T, int epi, float* out, int ldo)
     return product_from(c, w, T, epi, out, ldo, c->qa, c->da);
 }
 
-int rms_codes(laya_decoder* c, const float* scale, int T) {
+int rms_codes(laya_decoder* c, const float* scale, int T, const float* x = nullptr) {
     dec::RmsArgs r{};
-    r.rows = T; r.n = c->d.hidden; r.x = c->x; r.scale = scale; r.eps = c->d.eps;
+    r.rows = T; r.n = c->d.hidden; r.x = x ? x : c->x; r.scale = scale; r.eps = c->d.eps;
     r.q = c->qa; r.d = c->da; r.ldd = c->ldx;
     return dec_rms_q8(r, c->stream);
 }
@@ -373,8 +376,9 @@ int full_mixer(laya_decoder* c, const Layer& L, int T, long long pairs, int laye
 
 // Mlp (Qwen35Model.cs:602-621): the [gate | up] product's epilogue applies silu(gate) · up and quantizes it for the
 // down projection (the rows of gate_up are stored in [32 gate | 32 up] groups).
-int mlp(laya_decoder* c, const Layer& L, int T) {
-    RC(rms_codes(c, L.post_norm, T));
+int mlp(laya_decoder* c, const Layer& L, int T, float* x = nullptr) {
+    x = x ? x : c->x;
+    RC(rms_codes(c, L.post_norm, T, x));
     q8::GemmArgs a{};
     a.M = T; a.N = L.gate_up.N; a.K = L.gate_up.K;
     a.qx = c->qa; a.dx = c->da; a.ldx = c->ldx;
@@ -383,7 +387,7 @@ int mlp(laya_decoder* c, const Layer& L, int T) {
     a.qout = c->qa2; a.ldqo = c->d.intermediate; a.qsc = c->da2; a.ldqs = c->ldx;
     a.err = c->err;
     RC(timed(c, 0, 2.0 * T * static_cast<double>(a.N) * a.K, [&] { return q8::gemm(a, c->stream); }));
-    return product_from(c, L.down, T, q8::EPI_RESID, c->x, c->d.hidden, c->qa2, c->da2);
+    return product_from(c, L.down, T, q8::EPI_RESID, x, c->d.hidden, c->qa2, c->da2);
 }
 
 int run_layer(laya_decoder* c, int i, int T, int n_seq, long long pairs, bool keep_mix) {
@@ -392,6 +396,36 @@ int run_layer(laya_decoder* c, int i, int T, int n_seq, long long pairs, bool ke
     else RC(linear_mixer(c, L, T, n_seq, i, keep_mix));
     RC(mlp(c, L, T));
     return record_copy(c, "layers." + std::to_string(i), c->x, static_cast<size_t>(T) * c->d.hidden);
+}
+
+// The last layer when it is full attention and nothing is recorded (Qwen35Model.cs:488-490, ReadoutRows :563-573):
+// every row's keys and values are made (later reads attend to them), but only the tiles holding each sequence's last
+// row go through attention, and only those rows through o_proj and the MLP — gathered into xl, where the final norm
+// reads them.  Rows are independent in every product, so the readout is the unpruned forward's, bit for bit.
+int last_layer_pruned(laya_decoder* c, const Layer& L, int T, int n_seq) {
+    const laya_decoder_desc& d = c->d;
+    const int h = d.hidden, ao = d.heads * d.head_dim;
+    RC(rms_codes(c, L.in_norm, T));
+    RC(product(c, L.mix_in, T, q8::EPI_STORE, c->big, c->nqkv));
+    dec::PrepArgs pp{};
+    pp.T = T; pp.heads = d.heads; pp.kv_heads = d.kv_heads; pp.hd = d.head_dim; pp.half = c->half;
+    pp.q_width = c->q_width; pp.qkv = c->big; pp.ld_qkv = c->nqkv; pp.qnorm = L.qnorm; pp.knorm = L.knorm;
+    pp.eps = d.eps; pp.cosv = c->cosv; pp.sinv = c->sinv; pp.tok_seq = c->tok_seq; pp.seq_start = c->seq_start;
+    const int layer = d.layers - 1;
+    pp.pos0 = c->pos0; pp.q16 = c->q16; pp.kc = seq_table<__half>(c, layer, 0); pp.vc = seq_table<__half>(c, layer, 1);
+    dec::AttnArgs at{};
+    at.heads = d.heads; at.kv_heads = d.kv_heads; at.q16 = c->q16; at.kc = pp.kc; at.vc = pp.vc;
+    at.tile_seq = c->lt_seq; at.tile_p0 = c->lt_p0; at.seq_start = c->seq_start; at.seq_len = c->seq_len;
+    at.pos0 = c->pos0;
+    at.scale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.head_dim)));
+    at.qkv = c->big; at.ld_qkv = c->nqkv; at.out = c->core; at.ld_out = ao;
+    RC(dec_attn_prep(pp, c->stream));
+    RC(dec_attention(at, n_seq, d.head_dim, c->stream));
+    RC(dec_gather_rows(c->core, ao, c->last_row, n_seq, ao, c->corel, ao, c->stream));
+    RC(dec_gather_rows(c->x, h, c->last_row, n_seq, h, c->xl, h, c->stream));
+    RC(q8::quantize_activations(c->corel, n_seq, ao, ao, c->qa, c->da, c->ldx, c->stream));
+    RC(product(c, L.mix_out, n_seq, q8::EPI_RESID, c->xl, h));
+    return mlp(c, L, n_seq, c->xl);
 }
 
 // The states a forward's sequences continue, and the snapshot states its checkpoints fill (validated by the caller).
@@ -423,7 +457,7 @@ int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int 
     const int n_snap = sv ? sv->n_snap : 0;
     const size_t n_ptr = 2 * static_cast<size_t>(c->d.layers) * (n_seq + n_snap);
     const size_t need = static_cast<size_t>(ids_host ? T : 0) + T + 3 * static_cast<size_t>(n_seq) + 2 * tiles +
-                        n_labels + n_seq + (n_seq + 1) + n_snap + 1 + 2 * n_ptr;
+                        n_labels + n_seq + (n_seq + 1) + n_snap + 2 * n_seq + 1 + 2 * n_ptr;
     if (c->in_pending) { LAYA_CUDA(cudaEventSynchronize(c->in_done)); c->in_pending = false; }
     if (need > c->in_cap) {
         if (c->in_host) cudaFreeHost(c->in_host);
@@ -453,6 +487,8 @@ int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int 
     int32_t* ps = slot(n_seq, &c->pos0);
     int32_t* sb = slot(n_seq + 1, &c->snap_begin);
     int32_t* sa = slot(n_snap, &c->snap_at);
+    int32_t* lts = slot(n_seq, &c->lt_seq);
+    int32_t* ltp = slot(n_seq, &c->lt_p0);
     if (o & 1) ++o;   // 8-byte alignment of the pointer tables (the device buffer is 256-byte aligned)
     int32_t* dummy = nullptr;
     uint64_t* pt = reinterpret_cast<uint64_t*>(slot(2 * n_ptr, &dummy));
@@ -463,6 +499,8 @@ int stage(laya_decoder* c, const int32_t* ids_host, const int32_t* seq_len, int 
     for (int s = 0; s < n_seq; ++s) {
         ss[s] = start; sl[s] = seq_len[s]; lr[s] = start + seq_len[s] - 1;
         ps[s] = sv ? sv->states[s]->length : 0;
+        lts[s] = s;
+        ltp[s] = (seq_len[s] - 1) / 64 * 64;
         for (int t = 0; t < seq_len[s]; ++t) ts[start + t] = s;
         for (int p0 = 0; p0 < seq_len[s]; p0 += 64) {
             tl.push_back({ps[s] + p0, static_cast<int>(tile_of.size())});
@@ -529,9 +567,12 @@ int forward_body(laya_decoder* c, int T, int n_seq, long long pairs, int n_label
     const int h = c->d.hidden;
     RC(dec_embed(c->ids, T, h, c->d.vocab, c->table.q, c->table.d, c->table.ldw, c->x, c->err, c->stream));
     RC(record_copy(c, "embeddings", c->x, static_cast<size_t>(T) * h));
-    for (int i = 0; i < c->d.layers; ++i) RC(run_layer(c, i, T, n_seq, pairs, false));
+    const bool prune = !c->record && c->layers.back().kind == LAYA_DECODER_FULL;
+    for (int i = 0; i < c->d.layers - (prune ? 1 : 0); ++i) RC(run_layer(c, i, T, n_seq, pairs, false));
+    if (prune) RC(last_layer_pruned(c, c->layers.back(), T, n_seq));
     dec::RmsArgs r{};
-    r.rows = n_seq; r.n = h; r.x = c->x; r.row_map = c->last_row; r.scale = c->final_norm; r.eps = c->d.eps;
+    r.rows = n_seq; r.n = h; r.x = prune ? c->xl : c->x; r.row_map = prune ? nullptr : c->last_row;
+    r.scale = c->final_norm; r.eps = c->d.eps;
     r.out32 = hidden ? hidden : c->hid; r.q = c->qlast; r.d = c->dlast; r.ldd = c->ldl;
     RC(dec_rms_q8(r, c->stream));
     if (c->record) {
@@ -624,6 +665,9 @@ int check_desc(const laya_decoder_desc& d) {
     return OK;
 }
 
+// A stream-ordered block from the decoder's pool.
+cudaError_t pool_alloc(laya_decoder* c, void** p, size_t bytes) { return cudaMallocFromPoolAsync(p, bytes, c->pool, c->stream); }
+
 // RoPE tables for positions [0, positions) (Qwen35Model.cs:247-253): inv_freq = 1/θ^(2i/rotary_dim) and
 // angle = pos·inv_freq in fp32.  Grown (rebuilt) when a state reads past them; the old tables are freed after the work
 // queued on the stream.
@@ -677,6 +721,15 @@ int create(laya_decoder* c) {
     LAYA_CUDA(cudaEventCreateWithFlags(&c->in_done, cudaEventDisableTiming));
     RC(dalloc_t(c, &c->err, 1));
     LAYA_CUDA(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
+    {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = c->device;
+        LAYA_CUDA(cudaMemPoolCreate(&c->pool, &props));
+        uint64_t keep = UINT64_MAX;   // never trim: a request's clones reuse the blocks the previous one freed
+        LAYA_CUDA(cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    }
 
     c->layers.resize(d.layers);
     RC(alloc_qmat(c, c->table, d.vocab, d.hidden));
@@ -717,6 +770,8 @@ int create(laya_decoder* c) {
         RC(dalloc_t(c, &c->k16, T * d.kv_heads * d.head_dim));
         RC(dalloc_t(c, &c->v16, T * d.kv_heads * d.head_dim));
         RC(ensure_rope(c, static_cast<int>(T)));
+        RC(dalloc_t(c, &c->xl, static_cast<size_t>(d.max_seqs) * d.hidden));
+        RC(dalloc_t(c, &c->corel, static_cast<size_t>(d.max_seqs) * d.heads * d.head_dim));
     }
     RC(dalloc_t(c, &c->hid, static_cast<size_t>(d.max_seqs) * d.hidden));
     RC(dalloc_t(c, &c->qlast, static_cast<size_t>(d.max_seqs) * d.hidden));
@@ -848,7 +903,7 @@ int state_block(laya_decoder* c, int capacity, bool zero, char** block, size_t* 
     const size_t fixed = state_fixed_bytes(c);
     *bytes = std::max<size_t>(fixed + 2 * n_full_layers(c) * state_kv_bytes(c, capacity), 256);
     void* p = nullptr;
-    LAYA_CUDA(cudaMallocAsync(&p, *bytes, c->stream));
+    LAYA_CUDA(pool_alloc(c, &p, *bytes));
     *block = static_cast<char*>(p);
     if (zero && fixed) LAYA_CUDA(cudaMemsetAsync(p, 0, fixed, c->stream));
     return OK;
@@ -952,6 +1007,7 @@ int laya_decoder_destroy(laya_decoder* c) {
     if (c->in_dev) cudaFree(c->in_dev);
     if (c->in_host) cudaFreeHost(c->in_host);
     if (c->in_done) cudaEventDestroy(c->in_done);
+    if (c->pool) cudaMemPoolDestroy(c->pool);
     if (c->own) cudaStreamDestroy(c->own);
     delete c;
     return OK;
@@ -1158,7 +1214,7 @@ int laya_decoder_state_save(laya_decoder_state* st, laya_decoder_mark** out) {
     m->bytes = st->fixed;
     if (m->bytes) {
         void* p = nullptr;
-        cudaError_t e = cudaMallocAsync(&p, m->bytes, c->stream);
+        cudaError_t e = pool_alloc(c, &p, m->bytes);
         if (e == cudaSuccess) e = cudaMemcpyAsync(p, st->block, m->bytes, cudaMemcpyDeviceToDevice, c->stream);
         m->block = static_cast<char*>(p);
         if (e != cudaSuccess) {

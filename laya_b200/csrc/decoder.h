@@ -128,6 +128,8 @@ int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);
 int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s);
 int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);
 int dec_add(float* x, const float* y, size_t n, cudaStream_t s);
+int dec_gather_rows(const float* src, int ld_src, const int32_t* map, int rows, int n, float* dst, int ld_dst,
+                    cudaStream_t s);
 int dec_q8_logits(const dec::LogitArgs& a, cudaStream_t s);
 
 }  // namespace laya

@@ -577,6 +577,15 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     }
 }
 
+// dst[r, :n] = src[map[r], :n] (the readout rows of the last layer)
+__global__ void gather_rows_kernel(const float* __restrict__ src, int ld_src, const int32_t* __restrict__ map, int rows,
+                                   int n, float* __restrict__ dst, int ld_dst) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<size_t>(rows) * n) return;
+    const int r = static_cast<int>(i / n), c = static_cast<int>(i % n);
+    dst[static_cast<size_t>(r) * ld_dst + c] = src[static_cast<size_t>(map[r]) * ld_src + c];
+}
+
 // x += y elementwise (the residual add behind a recorded mixer or MLP output; the same single rounding as the
 // product's residual epilogue).
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
@@ -709,6 +718,12 @@ int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s) {
         set_error("decoder attention: head_dim must be 32, 64 or 128");
         return ERR_NOT_SUPPORTED;
     }
+    DEC_LAUNCHED();
+}
+int dec_gather_rows(const float* src, int ld_src, const int32_t* map, int rows, int n, float* dst, int ld_dst,
+                    cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return OK;
+    dec::gather_rows_kernel<<<nblk(static_cast<size_t>(rows) * n, 256), 256, 0, s>>>(src, ld_src, map, rows, n, dst, ld_dst);
     DEC_LAUNCHED();
 }
 int dec_add(float* x, const float* y, size_t n, cudaStream_t s) {
