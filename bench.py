@@ -850,7 +850,7 @@ def run_ours(args):
             if alt:
                 line["bf16_forward" if mode == 0 else "accurate_forward"] = {
                     "value": alt[1] / (alt[0] / 1e3), "unit": "tokens/s", "ms_per_step": alt[0]}
-            if not args.no_cpu_baseline:
+            if not args.no_cpu_baseline and world == 1:   # the CPU sample: rank 0 at N = 1 only
                 line["cpu_baseline"] = train_cpu_baseline(args.cpu_train_tokens)
     if args.workload in ("all", "q8"):
         r = q8_measure(args, d)
@@ -872,7 +872,7 @@ def run_ours(args):
                              "traffic": traffic.get("q8_gemm", {}).get("dram_bytes_per_launch"), "launches": gemm_n,
                              "share_of_step": gemm_ms / args.steps / ms},
                 "gpu_launches": r["launches"], "clocks": r["clocks"]}
-            if not args.no_cpu_baseline:
+            if not args.no_cpu_baseline and world == 1:   # the CPU sample: rank 0 at N = 1 only
                 q["cpu_baseline"] = q8_cpu_baseline(args.cpu_sample_rows)
             if line is None:
                 q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -904,7 +904,7 @@ def run_ours(args):
                               "frac": executed / bf16, "peak_source": f"{source} bf16 burst",
                               "launches": g_n, "share_of_step": g_ms / args.steps / ms},
                  "gpu_launches": r["launches"], "clocks": r["clocks"]}
-            if not args.no_cpu_baseline:
+            if not args.no_cpu_baseline and world == 1:   # the CPU sample: rank 0 at N = 1 only
                 q["cpu_baseline"] = f32_cpu_baseline()
             if line is None:
                 q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -949,7 +949,7 @@ def run_ours(args):
                                    f"{DEC_ROWS - 1} + forward_states(all remainders, label logits), host buffers"},
                 "vs_prefill_every_prompt_ms": e2e_ms, "gpu_launches_per_request": r["shared"]["launches"],
                 "logits_finite": r["shared"]["finite"]}
-            if not args.no_cpu_baseline:
+            if not args.no_cpu_baseline and world == 1:   # the CPU sample: rank 0 at N = 1 only
                 q["cpu_baseline"] = dec_cpu_baseline(args.dec_tokens)
             if line is None:
                 q.update({"steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
