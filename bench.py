@@ -395,6 +395,8 @@ def run_reference(args):
     if args.workload == "all" and not args.no_cpu_baseline:
         line["q8_0_encode"] = {"metric": "Q8_0 encode tokens/s", **q8_cpu_baseline(args.cpu_sample_rows)}
         line["mica_prefill"] = {"metric": "Mica prefill tokens/s", **dec_cpu_baseline(args.dec_tokens)}
+        line["systemone_f32"] = {"metric": "decision forward tokens/s, fp32-accurate path on a bf16 checkpoint",
+                                 **f32_cpu_baseline()}
     print(json.dumps(line), flush=True)
 
 
