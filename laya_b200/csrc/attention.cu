@@ -279,7 +279,52 @@ __global__ void __launch_bounds__(128) attention_kernel(Args a) {
     }
 }
 
+// One thread per 4 rotation pairs of one (token, head, q|k|v): the rotary of load_tile_rope, fp16 out.
+__global__ void prep16_kernel(const float* __restrict__ src, int ld, int T, int hidden, int heads,
+                              const int32_t* __restrict__ tok_item, const int32_t* __restrict__ seg_start,
+                              const float* __restrict__ cosv, const float* __restrict__ sinv, __half* __restrict__ out,
+                              int ldo) {
+    constexpr int HD = 64, HALF = HD / 2, J = HALF / 4;
+    const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<size_t>(T) * heads * 3 * J) return;
+    const int j = static_cast<int>(idx % J);
+    size_t rest = idx / J;
+    const int part = static_cast<int>(rest % 3);
+    rest /= 3;
+    const int h = static_cast<int>(rest % heads);
+    const int t = static_cast<int>(rest / heads);
+    const int col = part * hidden + h * HD + 4 * j;
+    float4 a = *reinterpret_cast<const float4*>(src + static_cast<size_t>(t) * ld + col);
+    float4 b = *reinterpret_cast<const float4*>(src + static_cast<size_t>(t) * ld + col + HALF);
+    if (part < 2 && cosv) {
+        const int pos = t - seg_start[tok_item[t]];
+        const float4 c = *reinterpret_cast<const float4*>(cosv + static_cast<size_t>(pos) * HALF + 4 * j);
+        const float4 sn = *reinterpret_cast<const float4*>(sinv + static_cast<size_t>(pos) * HALF + 4 * j);
+        float4 ra, rb;
+        ra.x = __fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, sn.x)); rb.x = __fadd_rn(__fmul_rn(b.x, c.x), __fmul_rn(a.x, sn.x));
+        ra.y = __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, sn.y)); rb.y = __fadd_rn(__fmul_rn(b.y, c.y), __fmul_rn(a.y, sn.y));
+        ra.z = __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, sn.z)); rb.z = __fadd_rn(__fmul_rn(b.z, c.z), __fmul_rn(a.z, sn.z));
+        ra.w = __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, sn.w)); rb.w = __fadd_rn(__fmul_rn(b.w, c.w), __fmul_rn(a.w, sn.w));
+        a = ra; b = rb;
+    }
+    __half* d = out + static_cast<size_t>(t) * ldo + col;
+    *reinterpret_cast<uint2*>(d) = make_uint2(pack_half2(a.x, a.y), pack_half2(a.z, a.w));
+    *reinterpret_cast<uint2*>(d + HALF) = make_uint2(pack_half2(b.x, b.y), pack_half2(b.z, b.w));
+}
+
 }  // namespace attn
+
+int attn_prep16(const float* qkv, int ld, int T, int hidden, int heads, const int32_t* tok_item, const int32_t* seg_start,
+                const float* cosv, const float* sinv, __half* out, int ldo, cudaStream_t stream) {
+    if (T <= 0) return OK;
+    if (hidden != 64 * heads || (ld & 3) || (ldo & 7)) { set_error("fp16 attention prep: head_dim 64, aligned rows"); return ERR_ARGUMENT; }
+    const size_t n = static_cast<size_t>(T) * heads * 3 * 8;
+    attn::prep16_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(qkv, ld, T, hidden, heads, tok_item,
+                                                                                   seg_start, cosv, sinv, out, ldo);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
 
 int attention(const attn::Args& a, int max_qtiles, cudaStream_t stream) {
     if (max_qtiles <= 0) return OK;

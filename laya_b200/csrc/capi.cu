@@ -142,6 +142,10 @@ struct laya_ctx {
     int32_t *seg_start = nullptr, *mk_start = nullptr, *qt_start = nullptr, *qt_item = nullptr, *qt_q0 = nullptr,
             *n_qt = nullptr, *tok_item = nullptr, *marker_row = nullptr, *marker_item = nullptr;
     float *logits = nullptr, *act = nullptr;
+    // the tensor-core attention (head_dim 64): rotated fp16 q | k | v and the 128-row query tiles
+    __half* qkv16 = nullptr;
+    int max_tq = 0;
+    int32_t *tq_start = nullptr, *tq_item = nullptr, *tq_p0 = nullptr, *n_tq = nullptr;
     // LAYA_PRECISION_F32 workspace: activations split into hi/lo bf16 parts, the widest projection output fp32
     __nv_bfloat16 *xh0 = nullptr, *xl0 = nullptr, *xh1 = nullptr, *xl1 = nullptr;
     float* wide = nullptr;
@@ -324,6 +328,25 @@ int record_copy(laya_ctx* c, const std::string& name, const float* src, size_t c
         if (rc_ != OK) return rc_; \
     } while (0)
 
+// Attention of the Q8_0 forward with the context out as Q8_0 codes in (qa1, da1): the tensor-core kernel for head_dim
+// 64 (the q, k, v rows rotated into fp16 first), the mma.sync kernel otherwise.
+int attend_q8(laya_ctx* c, attn::Args& at, int T) {
+    if (c->qkv16 && at.hidden == 64 * at.heads) {
+        RC(attn_prep16(at.qkv, at.ld, T, at.hidden, at.heads, c->tok_item, c->seg_start, at.cosv, at.sinv, c->qkv16,
+                       at.ld, c->stream));
+        InferAttn ia{};
+        ia.qkv16 = c->qkv16; ia.ld = at.ld; ia.hidden = at.hidden; ia.heads = at.heads; ia.T = T;
+        ia.seg_start = c->seg_start; ia.seg_len = c->seg_len;
+        ia.tq_item = c->tq_item; ia.tq_p0 = c->tq_p0; ia.n_tq = c->n_tq; ia.max_tq = c->max_tq;
+        ia.window = at.window; ia.scale = at.scale;
+        ia.q = c->qa1; ia.d = c->da1; ia.ldd = c->ldx; ia.err = c->err;
+        const int rc = flash_forward_tc_q8(ia, c->stream);
+        if (rc != ERR_NOT_SUPPORTED) return rc;
+    }
+    at.q = c->qa1; at.d = c->da1; at.ldd = c->ldx;
+    return attention(at, c->max_qtiles, c->stream);
+}
+
 // One encoder layer of the fp32-accurate path: the same steps as encoder_layer below with split bf16 products.
 int encoder_layer_f32(laya_ctx* c, int i, int T) {
     const int H = c->d.hidden, I = c->d.intermediate;
@@ -407,8 +430,7 @@ int encoder_layer(laya_ctx* c, int i, int T) {
     at.window = global ? -1 : c->d.local_attention / 2;
     at.scale = 1.0f / std::sqrt(static_cast<float>(H / c->d.heads));
     at.cosv = global ? c->cos_g : c->cos_l; at.sinv = global ? c->sin_g : c->sin_l;
-    at.q = c->qa1; at.d = c->da1; at.ldd = c->ldx;
-    RC(attention(at, c->max_qtiles, c->stream));
+    RC(attend_q8(c, at, T));
     RC(q8_proj(c, p + "attn.Wo.weight", c->qa1, c->da1, T, F(c, p + "attn.Wo.bias"), q8::EPI_RESID, c->h, H, nullptr,
                nullptr));
     const float* mw;
@@ -441,8 +463,7 @@ int head_layer(laya_ctx* c, int i, int T) {
     at.qtile_item = c->qt_item; at.qtile_q0 = c->qt_q0; at.n_qtiles = c->n_qt;
     at.window = -1; at.cosv = nullptr; at.sinv = nullptr;
     at.scale = 1.0f / std::sqrt(static_cast<float>(H / at.heads));
-    at.q = c->qa1; at.d = c->da1; at.ldd = c->ldx;
-    RC(attention(at, c->max_qtiles, c->stream));
+    RC(attend_q8(c, at, T));
     RC(q8_proj(c, p + "self_attn.out_proj.weight", c->qa1, c->da1, T, F(c, p + "self_attn.out_proj.bias"),
                q8::EPI_RESID, c->h, H, nullptr, nullptr));
     RC(need_f32(c, p + "norm2.weight", &ln.w));
@@ -463,6 +484,7 @@ int run_plan(laya_ctx* c, int n_items, int T, int n_markers) {
     pa.qt_item = c->qt_item; pa.qt_q0 = c->qt_q0; pa.n_qtiles = c->n_qt;
     pa.tok_item = c->tok_item; pa.marker_row = c->marker_row; pa.marker_item = c->marker_item;
     pa.err = c->err;
+    pa.max_tq = c->max_tq; pa.tq_start = c->tq_start; pa.tq_item = c->tq_item; pa.tq_p0 = c->tq_p0; pa.n_tq = c->n_tq;
     return plan(pa, c->stream);
 }
 
@@ -741,6 +763,12 @@ int laya_ctx_create(const laya_model_desc* desc, int device, laya_ctx** out) {
         (rc = dalloc_t(c, &c->marker_item, std::max(1, d.max_markers))) ||
         (rc = dalloc_t(c, &c->logits, std::max(1, d.max_markers))) ||
         (rc = dalloc_t(c, &c->act, static_cast<size_t>(d.max_items) * c->d.n_act)))
+        return fail(rc);
+    c->max_tq = d.max_tokens / 128 + d.max_items + 1;
+    if ((rc = dalloc_t(c, &c->tq_start, d.max_items)) || (rc = dalloc_t(c, &c->tq_item, c->max_tq)) ||
+        (rc = dalloc_t(c, &c->tq_p0, c->max_tq)) || (rc = dalloc_t(c, &c->n_tq, 1)))
+        return fail(rc);
+    if (d.precision == LAYA_PRECISION_Q8_0 && d.hidden / d.heads == 64 && (rc = dalloc_t(c, &c->qkv16, T * 3 * H)))
         return fail(rc);
     if (d.precision == LAYA_PRECISION_F32) {
         const size_t widest = std::max(2 * static_cast<size_t>(I), 4 * static_cast<size_t>(H));

@@ -55,6 +55,7 @@ struct Params {
     __nv_bfloat16* out; __nv_bfloat16* out_lo; int ldo;
     float* lse;
     int* err;
+    __half* q8; float* q8d; int q8ldd;   // inference: the context as Q8_0 codes [T, hidden] and scales [hidden/32, ldd]
 };
 
 // MN-major operand, 128-byte swizzle (V as the N-contiguous B of P·V): 64-element atoms, 8-row K groups 1024 B apart.
@@ -81,6 +82,10 @@ DEVI void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 DEVI void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+DEVI uint32_t pack2h(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
 DEVI uint32_t pack2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -126,12 +131,17 @@ struct DropWalk {
 // Persistent: a CTA walks work items (query tile, head) = blockIdx.x, blockIdx.x + gridDim.x, …, and every barrier
 // phase runs on across items (key tiles are counted globally), so the next item's Q and first K/V tiles load and its
 // first scores are computed while the softmax warps finish the current item.
-template <bool SPLIT, bool DROP>
+// INFER: the decision forward's attention — fp16 Q, K, V and P (kind::f16 with f16 operands), and the context leaves
+// as Q8_0 codes for the Wo product: each softmax thread holds one 32-column block of its row (Q8_0.QuantizeActivations,
+// PackedMatrixQ8_0.cs:50-71: d = amax/127 stored fp16, q = round-half-even(x · 127/amax)).
+template <bool SPLIT, bool DROP, bool INFER = false>
 __global__ void __launch_bounds__(320, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml, Params p) {
+    static_assert(!INFER || (!SPLIT && !DROP), "the inference form is single-pass without dropout");
     using C = Cfg<SPLIT>;
-    constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, BK);                                   // K-major A, B
-    constexpr uint32_t IDESC_PV = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);                      // B (V) MN-major
+    constexpr uint32_t OPF = INFER ? 0u : 1u;                                                    // f16 : bf16
+    constexpr uint32_t IDESC_S = make_idesc(1, OPF, OPF, BQ, BK);                                // K-major A, B
+    constexpr uint32_t IDESC_PV = make_idesc(1, OPF, OPF, BQ, HD) | (1u << 16);                  // B (V) MN-major
     const int n_items = *p.n_tq * p.heads;
     if (static_cast<int>(blockIdx.x) >= n_items) return;
     extern __shared__ uint8_t smem_raw[];
@@ -373,8 +383,12 @@ __global__ void __launch_bounds__(320, 1)
                 for (int c = 0; c < HK / 8; ++c) {
                     const float* f = reinterpret_cast<const float*>(v + 8 * c);
                     uint8_t* dst = prow + ((c ^ (row & 7)) << 4);
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]),
-                                                                pack2(f[6], f[7]));
+                    if constexpr (INFER)
+                        *reinterpret_cast<uint4*>(dst) = make_uint4(pack2h(f[0], f[1]), pack2h(f[2], f[3]),
+                                                                    pack2h(f[4], f[5]), pack2h(f[6], f[7]));
+                    else
+                        *reinterpret_cast<uint4*>(dst) = make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]),
+                                                                    pack2(f[4], f[5]), pack2(f[6], f[7]));
                     if constexpr (SPLIT)
                         *reinterpret_cast<uint4*>(dst + 2 * TILE) =
                             make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
@@ -404,7 +418,26 @@ __global__ void __launch_bounds__(320, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(o_free);
-                if (q < L) {
+                if (INFER && q < L) {
+                    float f[HO];
+                    float m = 0.f;
+#pragma unroll
+                    for (int e = 0; e < HO; ++e) {
+                        f[e] = __uint_as_float(o[e]) * inv;
+                        m = fmaxf(m, fabsf(f[e]));
+                    }
+                    const float id = m != 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+                    const size_t tok = static_cast<size_t>(seg0 + q);
+                    __half* qrow = p.q8 + tok * p.hidden + head * HD + half * HO;
+#pragma unroll
+                    for (int t = 0; t < HO / 8; ++t) {
+                        __half hq[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) hq[e] = __int2half_rn(__float2int_rn(__fmul_rn(f[8 * t + e], id)));
+                        *reinterpret_cast<uint4*>(qrow + 8 * t) = *reinterpret_cast<const uint4*>(hq);
+                    }
+                    p.q8d[static_cast<size_t>(head * 2 + half) * p.q8ldd + tok] = round_fp16(__fdiv_rn(m, 127.0f));
+                } else if (q < L) {
                     __nv_bfloat16* orow = p.out + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
 #pragma unroll
                     for (int t = 0; t < HO / 8; ++t) {
@@ -971,6 +1004,39 @@ static int launch_tc(const fa::Args& a, cudaStream_t s) {
     if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
     const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
     fat::fwd_tc_kernel<SPLIT, DROP><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, tl, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// The decision forward's attention on the tensor cores (head_dim 64): q, k, v already rotated, fp16 [T, ld], the
+// context out as Q8_0 codes and scales.
+int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s) {
+    if (a.hidden / a.heads != fat::HD || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
+    if ((a.ld & 7) || (reinterpret_cast<uintptr_t>(a.qkv16) & 15)) return ERR_NOT_SUPPORTED;
+    using C = fat::Cfg<false>;
+    CUtensorMap th;
+    int rc = make_tmap_2d(&th, a.qkv16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.T, 3 * a.hidden,
+                          static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
+    if (rc) return rc;
+    static bool attr[64] = {false};
+    static int sms[64] = {0};
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !attr[dev]) {
+        LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM));
+        LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+        attr[dev] = true;
+    }
+    fat::Params p{};
+    p.seg_start = a.seg_start; p.seg_len = a.seg_len;
+    p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
+    p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
+    p.scale = a.scale; p.keep = 1.0f;
+    p.q8 = a.q; p.q8d = a.d; p.q8ldd = a.ldd; p.err = a.err;
+    const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    fat::fwd_tc_kernel<false, false, true><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, th, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;

@@ -66,12 +66,14 @@ DEVI void ref_layer_norm(const float* x, int n, const float* w, const float* b, 
 
 // ------------------------------------------------------------------------------------------------ plan
 // Exclusive block-wide scan of v[0..n) into out[0..n); returns the total (every thread).
+// transform_tiles: count ⌈v / transform_tiles⌉ (tiles of that many rows) instead of v.
 DEVI int block_scan(const int32_t* v, int n, int32_t* out, int* sh, int transform_tiles) {
     const int tid = threadIdx.x, nt = blockDim.x;
     const int per = (n + nt - 1) / nt;
     const int lo = min(n, tid * per), hi = min(n, lo + per);
+    const int tt = transform_tiles;
     int local = 0;
-    for (int i = lo; i < hi; ++i) local += transform_tiles ? (v[i] + 63) / 64 : v[i];
+    for (int i = lo; i < hi; ++i) local += tt ? (v[i] + tt - 1) / tt : v[i];
     sh[tid] = local;
     __syncthreads();
     for (int off = 1; off < nt; off <<= 1) {
@@ -82,7 +84,7 @@ DEVI int block_scan(const int32_t* v, int n, int32_t* out, int* sh, int transfor
     }
     int run = sh[tid] - local;
     const int total = sh[nt - 1];
-    for (int i = lo; i < hi; ++i) { out[i] = run; run += transform_tiles ? (v[i] + 63) / 64 : v[i]; }
+    for (int i = lo; i < hi; ++i) { out[i] = run; run += tt ? (v[i] + tt - 1) / tt : v[i]; }
     __syncthreads();
     return total;
 }
@@ -94,7 +96,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
         if (a.seg_len[i] < 0 || a.marker_count[i] < 0) atomicExch(a.err, LAYA_DEV_ERR_BOUNDS);
     const int tokens = block_scan(a.seg_len, n, a.seg_start, sh, 0);
     const int markers = block_scan(a.marker_count, n, a.mk_start, sh, 0);
-    const int tiles = block_scan(a.seg_len, n, a.qt_start, sh, 1);
+    const int tiles = block_scan(a.seg_len, n, a.qt_start, sh, 64);
     if (threadIdx.x == 0) {
         if (tokens != a.n_tokens || markers != a.n_markers || tiles > a.max_qtiles) atomicExch(a.err, LAYA_DEV_ERR_BOUNDS);
         *a.n_qtiles = min(tiles, a.max_qtiles);
@@ -103,6 +105,17 @@ __global__ void __launch_bounds__(1024) plan_kernel(PlanArgs a) {
         const int t0 = a.qt_start[i], nt = (a.seg_len[i] + 63) / 64;
         for (int j = 0; j < nt; ++j)
             if (t0 + j < a.max_qtiles) { a.qt_item[t0 + j] = i; a.qt_q0[t0 + j] = 64 * j; }
+    }
+    if (!a.tq_start) return;
+    const int tiles128 = block_scan(a.seg_len, n, a.tq_start, sh, 128);
+    if (threadIdx.x == 0) {
+        if (tiles128 > a.max_tq) atomicExch(a.err, LAYA_DEV_ERR_BOUNDS);
+        *a.n_tq = min(tiles128, a.max_tq);
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int t0 = a.tq_start[i], nt = (a.seg_len[i] + 127) / 128;
+        for (int j = 0; j < nt; ++j)
+            if (t0 + j < a.max_tq) { a.tq_item[t0 + j] = i; a.tq_p0[t0 + j] = 128 * j; }
     }
 }
 

@@ -53,8 +53,14 @@ struct PlanArgs {
     int32_t* qt_item; int32_t* qt_q0; int32_t* n_qtiles;
     int32_t* tok_item; int32_t* marker_row; int32_t* marker_item;
     int* err;
+    // 128-row query tiles (the tensor-core attention), when tq_start is given
+    int max_tq; int32_t* tq_start; int32_t* tq_item; int32_t* tq_p0; int32_t* n_tq;
 };
 int plan(const PlanArgs& a, cudaStream_t stream);
+// fp32 q | k | v rows [T, ld] → fp16 [T, ldo], q and k rotated at the token's position in its segment (cos/sin
+// [positions, head_dim/2], or none): the tensor-core attention's operands.
+int attn_prep16(const float* qkv, int ld, int T, int hidden, int heads, const int32_t* tok_item, const int32_t* seg_start,
+                const float* cosv, const float* sinv, __half* out, int ldo, cudaStream_t stream);
 
 struct ScorerArgs {
     int n_markers, hidden;

@@ -64,6 +64,17 @@ int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
 int flash_forward_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: head_dim 64 (ERR_NOT_SUPPORTED otherwise)
 int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: dK, dV for head_dim 64
 int flash_backward_dq_tc(const fa::Args& a, cudaStream_t s);     // flash_tc.cu: dQ for head_dim 64
+// The decision forward's attention (inference) on the tensor cores: qkv16 [T, ld] fp16 = rotated q | k | v, 128-row
+// query tiles of every segment, context out as Q8_0 codes q [T, hidden] and scales d [hidden/32, ldd].
+struct InferAttn {
+    const __half* qkv16; int ld; int hidden, heads, T;
+    const int32_t* seg_start; const int32_t* seg_len;
+    const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq; int max_tq;
+    int window; float scale;
+    __half* q; float* d; int ldd;
+    int* err;
+};
+int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s);
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s);
 
 // ---- train_kernels.cu
