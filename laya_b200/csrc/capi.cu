@@ -328,9 +328,11 @@ int record_copy(laya_ctx* c, const std::string& name, const float* src, size_t c
         if (rc_ != OK) return rc_; \
     } while (0)
 
-// Attention of the Q8_0 forward with the context out as Q8_0 codes in (qa1, da1): the tensor-core kernel for head_dim
-// 64 (the q, k, v rows rotated into fp16 first), the mma.sync kernel otherwise.
+// Attention of the decision forward, the context out as Q8_0 codes in (qa1, da1) — or, when at.hi is set (the
+// fp32-accurate path), as bf16 hi/lo parts there: the tensor-core kernel for head_dim 64 (the q, k, v rows rotated
+// into fp16 first), the mma.sync kernel otherwise.
 int attend_q8(laya_ctx* c, attn::Args& at, int T) {
+    const bool split_out = at.hi != nullptr;   // the fp32-accurate path: hi/lo context instead of Q8_0 codes
     if (c->qkv16 && at.hidden == 64 * at.heads) {
         RC(attn_prep16(at.qkv, at.ld, T, at.hidden, at.heads, c->tok_item, c->seg_start, at.cosv, at.sinv, c->qkv16,
                        at.ld, c->stream));
@@ -339,11 +341,13 @@ int attend_q8(laya_ctx* c, attn::Args& at, int T) {
         ia.seg_start = c->seg_start; ia.seg_len = c->seg_len;
         ia.tq_item = c->tq_item; ia.tq_p0 = c->tq_p0; ia.n_tq = c->n_tq; ia.max_tq = c->max_tq;
         ia.window = at.window; ia.scale = at.scale;
-        ia.q = c->qa1; ia.d = c->da1; ia.ldd = c->ldx; ia.err = c->err;
+        if (split_out) { ia.hi = at.hi; ia.lo = at.lo; }
+        else { ia.q = c->qa1; ia.d = c->da1; ia.ldd = c->ldx; }
+        ia.err = c->err;
         const int rc = flash_forward_tc_q8(ia, c->stream);
         if (rc != ERR_NOT_SUPPORTED) return rc;
     }
-    at.q = c->qa1; at.d = c->da1; at.ldd = c->ldx;
+    if (!split_out) { at.q = c->qa1; at.d = c->da1; at.ldd = c->ldx; }
     return attention(at, c->max_qtiles, c->stream);
 }
 
@@ -367,7 +371,7 @@ int encoder_layer_f32(laya_ctx* c, int i, int T) {
     at.scale = 1.0f / std::sqrt(static_cast<float>(H / c->d.heads));
     at.cosv = global ? c->cos_g : c->cos_l; at.sinv = global ? c->sin_g : c->sin_l;
     at.hi = c->xh0; at.lo = c->xl0;
-    RC(attention(at, c->max_qtiles, c->stream));
+    RC(attend_q8(c, at, T));
     RC(bf_proj(c, p + "attn.Wo.weight", c->xh0, c->xl0, T, F(c, p + "attn.Wo.bias"), bf::EPI_F32_ADD, c->h, H));
     RC(need_f32(c, p + "mlp_norm.weight", &ln.w));
     ln.b = F(c, p + "mlp_norm.bias"); ln.apply_ln = 1;
@@ -397,7 +401,7 @@ int head_layer_f32(laya_ctx* c, int i, int T) {
     at.window = -1; at.cosv = nullptr; at.sinv = nullptr;
     at.scale = 1.0f / std::sqrt(static_cast<float>(H / at.heads));
     at.hi = c->xh0; at.lo = c->xl0;
-    RC(attention(at, c->max_qtiles, c->stream));
+    RC(attend_q8(c, at, T));
     RC(bf_proj(c, p + "self_attn.out_proj.weight", c->xh0, c->xl0, T, F(c, p + "self_attn.out_proj.bias"),
                bf::EPI_F32_ADD, c->h, H));
     RC(need_f32(c, p + "norm2.weight", &ln.w));
@@ -768,8 +772,7 @@ int laya_ctx_create(const laya_model_desc* desc, int device, laya_ctx** out) {
     if ((rc = dalloc_t(c, &c->tq_start, d.max_items)) || (rc = dalloc_t(c, &c->tq_item, c->max_tq)) ||
         (rc = dalloc_t(c, &c->tq_p0, c->max_tq)) || (rc = dalloc_t(c, &c->n_tq, 1)))
         return fail(rc);
-    if (d.precision == LAYA_PRECISION_Q8_0 && d.hidden / d.heads == 64 && (rc = dalloc_t(c, &c->qkv16, T * 3 * H)))
-        return fail(rc);
+    if (d.hidden / d.heads == 64 && (rc = dalloc_t(c, &c->qkv16, T * 3 * H))) return fail(rc);
     if (d.precision == LAYA_PRECISION_F32) {
         const size_t widest = std::max(2 * static_cast<size_t>(I), 4 * static_cast<size_t>(H));
         if ((rc = dalloc_t(c, &c->xh0, T * H)) || (rc = dalloc_t(c, &c->xl0, T * H)) ||

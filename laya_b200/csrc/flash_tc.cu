@@ -134,10 +134,12 @@ struct DropWalk {
 // INFER: the decision forward's attention — fp16 Q, K, V and P (kind::f16 with f16 operands), and the context leaves
 // as Q8_0 codes for the Wo product: each softmax thread holds one 32-column block of its row (Q8_0.QuantizeActivations,
 // PackedMatrixQ8_0.cs:50-71: d = amax/127 stored fp16, q = round-half-even(x · 127/amax)).
-template <bool SPLIT, bool DROP, bool INFER = false>
+// INFER 2: the same fp16 operands with the context as bf16 hi/lo parts (the fp32-accurate decision forward).
+template <bool SPLIT, bool DROP, int INFER = 0>
 __global__ void __launch_bounds__(320, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml, Params p) {
     static_assert(!INFER || (!SPLIT && !DROP), "the inference form is single-pass without dropout");
+    constexpr bool Q8OUT = INFER == 1, HILO = SPLIT || INFER == 2;
     using C = Cfg<SPLIT>;
     constexpr uint32_t OPF = INFER ? 0u : 1u;                                                    // f16 : bf16
     constexpr uint32_t IDESC_S = make_idesc(1, OPF, OPF, BQ, BK);                                // K-major A, B
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(320, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(o_free);
-                if (INFER && q < L) {
+                if (Q8OUT && q < L) {
                     float f[HO];
                     float m = 0.f;
 #pragma unroll
@@ -446,14 +448,14 @@ __global__ void __launch_bounds__(320, 1)
                         for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(o[8 * t + e]) * inv;
                         *reinterpret_cast<uint4*>(orow + 8 * t) =
                             make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-                        if constexpr (SPLIT) {
+                        if constexpr (HILO) {
                             __nv_bfloat16* lrow = p.out_lo + static_cast<size_t>(seg0 + q) * p.ldo + head * HD + half * HO;
                             *reinterpret_cast<uint4*>(lrow + 8 * t) =
                                 make_uint4(pack2(lo_part(f[0]), lo_part(f[1])), pack2(lo_part(f[2]), lo_part(f[3])),
                                            pack2(lo_part(f[4]), lo_part(f[5])), pack2(lo_part(f[6]), lo_part(f[7])));
                         }
                     }
-                    if (half == 0) p.lse[static_cast<size_t>(seg0 + q) * p.heads + head] = m_run + logf(l_all);
+                    if (!INFER && half == 0) p.lse[static_cast<size_t>(seg0 + q) * p.heads + head] = m_run + logf(l_all);
                 }
             }
             base += nk;
@@ -1011,9 +1013,8 @@ static int launch_tc(const fa::Args& a, cudaStream_t s) {
 
 // The decision forward's attention on the tensor cores (head_dim 64): q, k, v already rotated, fp16 [T, ld], the
 // context out as Q8_0 codes and scales.
-int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s) {
-    if (a.hidden / a.heads != fat::HD || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
-    if ((a.ld & 7) || (reinterpret_cast<uintptr_t>(a.qkv16) & 15)) return ERR_NOT_SUPPORTED;
+template <int MODE>
+static int launch_infer_tc(const InferAttn& a, cudaStream_t s) {
     using C = fat::Cfg<false>;
     CUtensorMap th;
     int rc = make_tmap_2d(&th, a.qkv16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.T, 3 * a.hidden,
@@ -1024,7 +1025,7 @@ int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s) {
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
     if (dev < 64 && !attr[dev]) {
-        LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<false, false, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM));
         LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
         attr[dev] = true;
@@ -1035,11 +1036,21 @@ int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s) {
     p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
     p.scale = a.scale; p.keep = 1.0f;
     p.q8 = a.q; p.q8d = a.d; p.q8ldd = a.ldd; p.err = a.err;
+    p.out = a.hi; p.out_lo = a.lo; p.ldo = a.hidden;
     const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
-    fat::fwd_tc_kernel<false, false, true><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, th, p);
+    fat::fwd_tc_kernel<false, false, MODE><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, th, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
+}
+
+int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s) {
+    if (a.hidden / a.heads != fat::HD || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
+    if ((a.ld & 7) || (reinterpret_cast<uintptr_t>(a.qkv16) & 15)) return ERR_NOT_SUPPORTED;
+    if (a.q) return launch_infer_tc<1>(a, s);
+    if (!a.hi || !a.lo || (reinterpret_cast<uintptr_t>(a.hi) & 15) || (reinterpret_cast<uintptr_t>(a.lo) & 15))
+        return ERR_NOT_SUPPORTED;
+    return launch_infer_tc<2>(a, s);
 }
 
 // The tcgen05 forward for head_dim 64; returns ERR_NOT_SUPPORTED for shapes it does not take (the caller then runs

@@ -71,7 +71,8 @@ struct InferAttn {
     const int32_t* seg_start; const int32_t* seg_len;
     const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq; int max_tq;
     int window; float scale;
-    __half* q; float* d; int ldd;
+    __half* q; float* d; int ldd;            // Q8_0 codes and scales, or (q null) ...
+    __nv_bfloat16* hi; __nv_bfloat16* lo;     // ... the context as bf16 hi/lo parts [T, hidden]
     int* err;
 };
 int flash_forward_tc_q8(const InferAttn& a, cudaStream_t s);
