@@ -396,7 +396,9 @@ class DecisionModel:
     """The decision model's batched inference forward on the device (DecisionModel + ModernBertEncoder).
 
     `weights` maps safetensors names to arrays; `q8` maps projection names to (codes int8 [N, K], scales fp16
-    [N, K/32]) for checkpoints already in Q8_0.  Projections given as floats are quantized on the device.
+    [N, K/32]) for checkpoints already in Q8_0.  In a PRECISION_Q8_0 context projections given as floats are quantized
+    on the device; in a PRECISION_F32 context they are kept as bf16 hi/lo parts (the lo part dropped when every weight
+    is a bf16 value) and the forward runs the fp32-accurate split products (PackedMatrix, DecisionModel.cs:50-99).
     """
 
     def __init__(self, desc: ModelDesc, weights: Dict[str, np.ndarray], q8: Optional[Dict] = None, device: int = 0):
