@@ -646,44 +646,50 @@ __global__ void __launch_bounds__(320, 2)
                                              mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err));
             const float* rows = sRow + s * 2 * BQ2;
             const int q0 = qb0 + j * BQ2 + half * HQ;
-            uint32_t sv[32], dv[32];
-            if (ok) {
-                tc_fence_after();
-                tmem_ld32(tS + lane_off + half * HQ, sv);
-                tmem_ld32(tDP + lane_off + half * HQ, dv);
-                tmem_ld_wait();
-            }
-            // Sᵀ and dPᵀ are in registers: release them to the next tile's MMAs
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(st_free);
-            if (!ok) continue;
             fat::DropWalk walk(p.seed, head, seg0 + q0, key, 1ull << 21, p.dropout, p.keep);
+            // the half-row's 32 queries in two 16-query pieces (fewer live registers)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int qi = half * HQ + e, q = q0 + e;
-                const float lse = rows[qi], dd = rows[BQ2 + qi];
-                const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
-                const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
-                const float m = DROP ? walk.next() : 1.0f;
-                sv[e] = __float_as_uint(pe * m);
-                dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
-            }
-            // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+            for (int pc = 0; pc < 2; ++pc) {
+                uint32_t sv[16], dv[16];
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld16(tS + lane_off + half * HQ + pc * 16, sv);
+                    tmem_ld16(tDP + lane_off + half * HQ + pc * 16, dv);
+                    tmem_ld_wait();
+                }
+                if (pc == 1) {   // Sᵀ and dPᵀ are in registers: release them to the next tile's MMAs
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(st_free);
+                }
                 if (!ok) continue;
-            }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float* f = reinterpret_cast<const float*>(sv + 8 * u);
-                const float* g = reinterpret_cast<const float*>(dv + 8 * u);
-                const int off = ((half * 4 + u) ^ (row & 7)) << 4;
-                *reinterpret_cast<uint4*>(prow + off) =
-                    make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-                *reinterpret_cast<uint4*>(drow + off) =
-                    make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
+                for (int e = 0; e < 16; ++e) {
+                    const int qi = half * HQ + pc * 16 + e, q = q0 + pc * 16 + e;
+                    const float lse = rows[qi], dd = rows[BQ2 + qi];
+                    const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
+                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
+                    const float m = DROP ? walk.next() : 1.0f;
+                    sv[e] = __float_as_uint(pe * m);
+                    dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                }
+                // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
+                if (pc == 0 && j > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+                    if (!ok) continue;
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                    const float* g = reinterpret_cast<const float*>(dv + 8 * u);
+                    const int off = ((half * 4 + pc * 2 + u) ^ (row & 7)) << 4;
+                    *reinterpret_cast<uint4*>(prow + off) =
+                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+                    *reinterpret_cast<uint4*>(drow + off) =
+                        make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
+                }
             }
+            if (!ok) continue;
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
@@ -774,14 +780,15 @@ constexpr int DQ_SMEM = 1024 + 2 * TILE + 4 * DQ_KTILE + TILE + 256;   // Q, dO,
 static_assert(2 * DQ_SMEM <= 232448, "two CTAs per SM");
 
 
+// Persistent like the forward: a CTA walks (query tile, head) items and every barrier phase runs on across items.
 template <bool DROP>
 __global__ void __launch_bounds__(320, 2)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
                      const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
     constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BQ, DQ_BK);                  // M queries, N keys, K-major
     constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BQ, HD) | (1u << 16);        // B (K) N-contiguous
-    const int tile = blockIdx.x;
-    if (tile >= *p.n_tq) return;
+    const int n_items = *p.n_tq * p.heads;
+    if (static_cast<int>(blockIdx.x) >= n_items) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
@@ -796,19 +803,30 @@ __global__ void __launch_bounds__(320, 2)
     uint64_t* st_free = bars + 6;
     uint64_t* ds_full = bars + 7;
     uint64_t* ds_empty = bars + 8;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    uint64_t* qo_empty = bars + 9;    // Q and dO read by the item's last S and dP MMAs
+    uint64_t* dq_free = bars + 10;    // dQ read by the item's epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    const int head = blockIdx.y, item = p.tq_item[tile], q0 = p.tq_p0[tile];
-    const int seg0 = p.seg_start[item], L = p.seg_len[item];
     const bool global = p.window < 0;
     const int W = p.window;
-    const int kb = global ? 0 : max(0, q0 - W), ke = global ? L : min(L, q0 + BQ + W);
-    const int nk = (ke - kb + DQ_BK - 1) / DQ_BK;
     const int warp = warp_id(), lane = lane_id();
+    auto span_of = [&](int item, int& head, int& seg0, int& L, int& q0, int& kb, int& nk) {
+        const int tile = item / p.heads;
+        head = item - tile * p.heads;
+        const int it = p.tq_item[tile];
+        q0 = p.tq_p0[tile];
+        seg0 = p.seg_start[it];
+        L = p.seg_len[it];
+        kb = global ? 0 : max(0, q0 - W);
+        const int ke = global ? L : min(L, q0 + BQ + W);
+        nk = (ke - kb + DQ_BK - 1) / DQ_BK;
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(qo_full, 1);
+        mbar_init(qo_empty, 1);
+        mbar_init(dq_free, 8);
         for (int s = 0; s < 2; ++s) { mbar_init(kv_full + s, 1); mbar_init(kv_empty + s, 1); }
         mbar_init(st_full, 1);
         mbar_init(st_free, 8);
@@ -827,145 +845,185 @@ __global__ void __launch_bounds__(320, 2)
 
     if (warp == 0) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(qo_full, 2 * TILE);
-            tma_load_2d(sQ, &tmq, qo_full, head * HD, seg0 + q0);
-            tma_load_2d(sDO, &tmdo, qo_full, head * HD, seg0 + q0);
-            for (int j = 0; j < nk; ++j) {
-                const int s = j & 1;
-                if (!mbar_wait(kv_empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
-                uint8_t* st = sKV + s * 2 * DQ_KTILE;
-                const int y = seg0 + kb + j * DQ_BK;
-                mbar_arrive_expect_tx(kv_full + s, 2 * DQ_KTILE);
-                tma_load_2d(st, &tmkv, kv_full + s, p.hidden + head * HD, y);
-                tma_load_2d(st + DQ_KTILE, &tmkv, kv_full + s, 2 * p.hidden + head * HD, y);
+            uint32_t g = 0, n = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+                int head, seg0, L, q0, kb, nk;
+                span_of(item, head, seg0, L, q0, kb, nk);
+                if (!mbar_wait(qo_empty, (n & 1) ^ 1, abort_flag, p.err)) break;
+                mbar_arrive_expect_tx(qo_full, 2 * TILE);
+                tma_load_2d(sQ, &tmq, qo_full, head * HD, seg0 + q0);
+                tma_load_2d(sDO, &tmdo, qo_full, head * HD, seg0 + q0);
+                for (int j = 0; j < nk; ++j, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(kv_empty + s, ((g >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    uint8_t* st = sKV + s * 2 * DQ_KTILE;
+                    const int y = seg0 + kb + j * DQ_BK;
+                    mbar_arrive_expect_tx(kv_full + s, 2 * DQ_KTILE);
+                    tma_load_2d(st, &tmkv, kv_full + s, p.hidden + head * HD, y);
+                    tma_load_2d(st + DQ_KTILE, &tmkv, kv_full + s, 2 * p.hidden + head * HD, y);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            bool ok = mbar_wait(qo_full, 0, abort_flag, p.err);
-            tc_fence_after();
+            uint32_t base = 0, n = 0;
+            bool ok = true;
             const uint32_t aq = smem_u32(sQ), ado = smem_u32(sDO);
-            for (int j = 0; j <= nk && ok; ++j) {
-                if (j < nk) {
-                    const int s = j & 1;
-                    if (!mbar_wait(kv_full + s, (j >> 1) & 1, abort_flag, p.err)) break;
-                    if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
-                    tc_fence_after();
-                    const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), av = ak + DQ_KTILE;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
+                int head, seg0, L, q0, kb, nk;
+                span_of(item, head, seg0, L, q0, kb, nk);
+                if (!mbar_wait(qo_full, n & 1, abort_flag, p.err)) break;
+                tc_fence_after();
+                for (int j = 0; j <= nk; ++j) {
+                    if (j < nk) {
+                        const uint32_t g = base + j;
+                        const int s = g & 1;
+                        if (!mbar_wait(kv_full + s, (g >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                        // S and dP of the previous tile (of this item or the last) must have been read
+                        if (g > 0 && !mbar_wait(st_free, (g - 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), av = ak + DQ_KTILE;
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
-                        mma_f16(tS, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
-                        mma_f16(tDP, smem_desc_sw128(ado + kk * 32), smem_desc_sw128(av + kk * 32), IDESC_S, kk > 0);
+                        for (int kk = 0; kk < HD / 16; ++kk) {
+                            mma_f16(tS, smem_desc_sw128(aq + kk * 32), smem_desc_sw128(ak + kk * 32), IDESC_S, kk > 0);
+                            mma_f16(tDP, smem_desc_sw128(ado + kk * 32), smem_desc_sw128(av + kk * 32), IDESC_S, kk > 0);
+                        }
+                        mma_commit(st_full);
+                        if (j == nk - 1) mma_commit(qo_empty);
                     }
-                    mma_commit(st_full);
-                }
-                if (j >= 1) {
-                    const int i = j - 1, s = i & 1;
-                    if (!mbar_wait(ds_full, i & 1, abort_flag, p.err)) break;
-                    tc_fence_after();
-                    const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), ads = smem_u32(sDS);
+                    if (j >= 1) {
+                        const int i = j - 1;
+                        const uint32_t gi = base + i;
+                        const int s = gi & 1;
+                        if (!mbar_wait(ds_full, gi & 1, abort_flag, p.err)) { ok = false; break; }
+                        // the item's first dQ MMA overwrites dQ: the previous item's epilogue must have read it
+                        if (i == 0 && !mbar_wait(dq_free, (n & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t ak = smem_u32(sKV + s * 2 * DQ_KTILE), ads = smem_u32(sDS);
 #pragma unroll
-                    for (int kk = 0; kk < DQ_BK / 16; ++kk)
-                        mma_f16(tDQ, smem_desc_sw128(ads + kk * 32), desc_mn_sw128(ak + kk * 2048, DQ_KTILE), IDESC_G,
-                                (i > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(kv_empty + s);
-                    mma_commit(ds_empty);
+                        for (int kk = 0; kk < DQ_BK / 16; ++kk)
+                            mma_f16(tDQ, smem_desc_sw128(ads + kk * 32), desc_mn_sw128(ak + kk * 2048, DQ_KTILE), IDESC_G,
+                                    (i > 0 || kk > 0) ? 1u : 0u);
+                        mma_commit(kv_empty + s);
+                        mma_commit(ds_empty);
+                    }
                 }
+                base += nk;
             }
         }
     } else {
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
-        const int q = q0 + row;
-        const bool qin = q < L;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         constexpr int HK = DQ_BK / 2;
         const float sl2 = p.scale * LOG2E;
-        const size_t at = static_cast<size_t>(seg0 + (qin ? q : 0)) * p.heads + head;
-        const float lse2 = qin ? __ldg(p.lse + at) * LOG2E : 0.f, dd = qin ? __ldg(p.dsum + at) : 0.f;
-        // keys this row sees: [lo, lo + span]
-        const int lo = global ? 0 : max(0, q - W);
-        const int span = (global ? L - 1 : min(L - 1, q + W)) - lo;
         uint8_t* drow = sDS + row * 128;
         bool ok = true;
-        for (int j = 0; j < nk; ++j) {
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err));
-            const int k0 = kb + j * DQ_BK + half * HK;
-            uint32_t sv[32], dv[32];
-            if (ok) {
-                tc_fence_after();
-                tmem_ld32(tS + lane_off + half * HK, sv);
-                tmem_ld32(tDP + lane_off + half * HK, dv);
-                tmem_ld_wait();
-            }
-            // S and dP are in registers: release them to the next tile's MMAs
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(st_free);
-            if (!ok) continue;
-            DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
+        uint32_t base = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            int head, seg0, L, q0, kb, nk;
+            span_of(item, head, seg0, L, q0, kb, nk);
+            const int q = q0 + row;
+            const bool qin = q < L;
+            const size_t at = static_cast<size_t>(seg0 + (qin ? q : 0)) * p.heads + head;
+            const float lse2 = qin ? __ldg(p.lse + at) * LOG2E : 0.f, dd = qin ? __ldg(p.dsum + at) : 0.f;
+            // keys this row sees: [lo, lo + span]
+            const int lo = global ? 0 : max(0, q - W);
+            const int span = (global ? L - 1 : min(L - 1, q + W)) - lo;
+            for (int j = 0; j < nk; ++j) {
+                const uint32_t g = base + j;
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, g & 1, abort_flag, p.err));
+                const int k0 = kb + j * DQ_BK + half * HK;
+                DropWalk walk(p.seed, head, seg0 + q, k0, 1, p.dropout, p.keep);
+                // the half-row's 32 keys in two 16-key pieces (fewer live registers): read S and dP, form dS, store it
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const bool vis = qin && static_cast<unsigned>(k0 + e - lo) <= static_cast<unsigned>(span);
-                const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse2)) : 0.f;
-                const float m = DROP ? walk.next() : 1.0f;
-                sv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
-            }
-            // dS of the previous tile must have been read by its dQ MMAs before it is rewritten
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(ds_empty, (j - 1) & 1, abort_flag, p.err));
-                if (!ok) continue;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float* f = reinterpret_cast<const float*>(sv + 8 * u);
-                *reinterpret_cast<uint4*>(drow + (((half * 4 + u) ^ (row & 7)) << 4)) =
-                    make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(ds_full);
-        }
-        // dQ once the last dQ MMAs are done: half h rotates the pairs (i, i + 32) for i in [16h, 16h + 16) back by
-        // −θ and stores them
-        ok = __all_sync(0xffffffffu, ok && nk > 0 && mbar_wait(ds_empty, (nk - 1) & 1, abort_flag, p.err));
-        if (ok) {
-            tc_fence_after();
-            uint32_t x[16], y[16];
-            tmem_ld16(tDQ + lane_off + half * 16, x);
-            tmem_ld16(tDQ + lane_off + 32 + half * 16, y);
-            tmem_ld_wait();
-            if (qin) {
-                float a[16], b[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    a[e] = __uint_as_float(x[e]);
-                    b[e] = __uint_as_float(y[e]);
-                }
-                if (p.cosv) {
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t sv[16], dv[16];
+                    if (ok) {
+                        tc_fence_after();
+                        tmem_ld16(tS + lane_off + half * HK + pc * 16, sv);
+                        tmem_ld16(tDP + lane_off + half * HK + pc * 16, dv);
+                        tmem_ld_wait();
+                    }
+                    if (pc == 1) {   // S and dP are in registers: release them to the next tile's MMAs
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(st_free);
+                    }
+                    if (!ok) continue;
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const int i = half * 16 + e;
-                        const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
-                        const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
-                        const float u = a[e], v = b[e];
-                        a[e] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
-                        b[e] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                        const int k = k0 + pc * 16 + e;
+                        const bool vis = qin && static_cast<unsigned>(k - lo) <= static_cast<unsigned>(span);
+                        const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse2)) : 0.f;
+                        const float m = DROP ? walk.next() : 1.0f;
+                        sv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                    }
+                    // dS of the previous tile must have been read by its dQ MMAs before it is rewritten
+                    if (pc == 0 && g > 0) {
+                        ok = __all_sync(0xffffffffu, mbar_wait(ds_empty, (g - 1) & 1, abort_flag, p.err));
+                        if (!ok) continue;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const float* f = reinterpret_cast<const float*>(sv + 8 * u);
+                        *reinterpret_cast<uint4*>(drow + (((half * 4 + pc * 2 + u) ^ (row & 7)) << 4)) =
+                            make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
                     }
                 }
-                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + q) * p.lddq + head * HD + half * 16;
+                if (!ok) continue;
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(ds_full);
+            }
+            // dQ once the item's last dQ MMAs are done: half h rotates the pairs (i, i + 32) for i in [16h, 16h + 16)
+            // back by −θ and stores them
+            const uint32_t last = base + nk - 1;
+            ok = __all_sync(0xffffffffu, ok && nk > 0 && mbar_wait(ds_empty, last & 1, abort_flag, p.err));
+            if (ok) {
+                tc_fence_after();
+                uint32_t x[16], y[16];
+                tmem_ld16(tDQ + lane_off + half * 16, x);
+                tmem_ld16(tDQ + lane_off + 32 + half * 16, y);
+                tmem_ld_wait();
+                // dQ is in registers: the next item's first dQ MMA may overwrite it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(dq_free);
+                if (qin) {
+                    float a[16], b[16];
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    *reinterpret_cast<uint4*>(out + 8 * t) =
-                        make_uint4(pack2(a[8 * t], a[8 * t + 1]), pack2(a[8 * t + 2], a[8 * t + 3]),
-                                   pack2(a[8 * t + 4], a[8 * t + 5]), pack2(a[8 * t + 6], a[8 * t + 7]));
-                    *reinterpret_cast<uint4*>(out + 32 + 8 * t) =
-                        make_uint4(pack2(b[8 * t], b[8 * t + 1]), pack2(b[8 * t + 2], b[8 * t + 3]),
-                                   pack2(b[8 * t + 4], b[8 * t + 5]), pack2(b[8 * t + 6], b[8 * t + 7]));
+                    for (int e = 0; e < 16; ++e) {
+                        a[e] = __uint_as_float(x[e]);
+                        b[e] = __uint_as_float(y[e]);
+                    }
+                    if (p.cosv) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const int i = half * 16 + e;
+                            const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
+                            const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
+                            const float u = a[e], v = b[e];
+                            a[e] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
+                            b[e] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                        }
+                    }
+                    __nv_bfloat16* out = p.dqkv + static_cast<size_t>(seg0 + q) * p.lddq + head * HD + half * 16;
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        *reinterpret_cast<uint4*>(out + 8 * t) =
+                            make_uint4(pack2(a[8 * t], a[8 * t + 1]), pack2(a[8 * t + 2], a[8 * t + 3]),
+                                       pack2(a[8 * t + 4], a[8 * t + 5]), pack2(a[8 * t + 6], a[8 * t + 7]));
+                        *reinterpret_cast<uint4*>(out + 32 + 8 * t) =
+                            make_uint4(pack2(b[8 * t], b[8 * t + 1]), pack2(b[8 * t + 2], b[8 * t + 3]),
+                                       pack2(b[8 * t + 4], b[8 * t + 5]), pack2(b[8 * t + 6], b[8 * t + 7]));
+                    }
                 }
             }
+            base += nk;
         }
     }
 
@@ -1130,7 +1188,10 @@ static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
-    fat::bwd_dq_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::DQ_SMEM, s>>>(tq, tkv, tdo, p);
+    static int sms[64] = {0};
+    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    const int items = a.max_tq * a.heads, slots = 2 * (dev < 64 && sms[dev] > 0 ? sms[dev] : 148);   // 2 CTAs per SM
+    fat::bwd_dq_tc_kernel<DROP><<<items < slots ? items : slots, 320, fat::DQ_SMEM, s>>>(tq, tkv, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
