@@ -206,7 +206,7 @@ struct laya_trainer {
     float *R32 = nullptr, *dH = nullptr, *dN = nullptr, *dbig32 = nullptr, *dsum = nullptr, *dsn = nullptr;
     bf16 *d16 = nullptr, *dctx16 = nullptr, *dqkv16 = nullptr, *dbig16 = nullptr, *dpre16 = nullptr;
     float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;
-    double* red = nullptr;   // [0] Σg², [1] gradient factor, [2] norm, [4..7] objective results
+    double* red = nullptr;   // [0] Σg², [1] gradient factor, [2] norm, [4..7] objective results, [8..] Σg² partials
     double* rl_scratch = nullptr;
     double* h_red = nullptr;   // pinned
     int* err = nullptr;
@@ -765,7 +765,7 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
     const size_t P = t->P;
     if ((rc = dalloc_t(t, &t->master, P)) || (rc = dalloc_t(t, &t->grad, P)) || (rc = dalloc_t(t, &t->m, P)) ||
         (rc = dalloc_t(t, &t->v, P)) || (rc = dalloc_t(t, &t->shadow, P)) || (rc = dalloc_t(t, &t->err, 1)) ||
-        (rc = dalloc_t(t, &t->red, 8)))
+        (rc = dalloc_t(t, &t->red, 8 + SUMSQ_BLOCKS)))
         return fail(rc);
     if (t->precise) {
         if ((rc = dalloc_t(t, &t->shadow_lo, P))) return fail(rc);
@@ -1512,8 +1512,8 @@ int laya_train_clip_and_step(laya_trainer* t, double max_norm, double* norm) {
     const int world = c.comm ? c.world : 1;
     LAYA_CUDA(cudaMemsetAsync(t->red, 0, sizeof(double) * 3, s));
     if (max_norm > 0 || norm) {
-        RC(sumsq(t->grad + tb, t->P - tb, t->red, s));
-        RC(clip_scale(t->red, max_norm > 0 ? max_norm : 1e300, world, t->red + 1, t->red + 2, s));
+        RC(sumsq(t->grad + tb, t->P - tb, t->red + 8, s));
+        RC(clip_scale(t->red + 8, max_norm > 0 ? max_norm : 1e300, world, t->red, t->red + 1, t->red + 2, s));
     } else if (world > 1) {
         const double inv = 1.0 / world;
         LAYA_CUDA(cudaMemcpyAsync(t->red + 1, &inv, sizeof(double), cudaMemcpyHostToDevice, s));

@@ -140,8 +140,12 @@ int type_grad(const float* d, const int32_t* tok_item, const int32_t* qtype, int
 int scorer_out(const float* pre, int M, int n, const float* w2, const float* b2, float* logits, cudaStream_t s);
 int scorer_bwd(const float* pre, const float* dlogit, int M, int n, const float* w2, __nv_bfloat16* dpre, float* db1,
                float* dw2, float* db2, cudaStream_t s);
-int sumsq(const float* g, size_t n, double* out, cudaStream_t s);
-int clip_scale(const double* sumsq, double max_norm, int world, double* scale, double* norm_out, cudaStream_t s);
+// Σ g² in a fixed order: SUMSQ_BLOCKS per-block partials (no atomics), summed by clip_scale in a fixed tree, so that
+// ranks holding the same gradient compute the same norm bit for bit.
+constexpr int SUMSQ_BLOCKS = 148 * 8;
+int sumsq(const float* g, size_t n, double* partials, cudaStream_t s);
+int clip_scale(const double* partials, double max_norm, int world, double* sumsq, double* scale, double* norm_out,
+               cudaStream_t s);
 int adamw(const tr::AdamArgs& a, cudaStream_t s);
 
 }  // namespace laya

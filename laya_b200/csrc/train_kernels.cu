@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(256) sumsq_kernel(const float* __restrict__ g,
     if (threadIdx.x == 0) {
         double t = 0.0;
         for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += ws[w];
-        atomicAdd(out, t);
+        out[blockIdx.x] = t;   // one partial per block: the sum order does not depend on scheduling
     }
 }
 
@@ -608,8 +608,20 @@ __global__ void adamw_kernel(AdamArgs a) {
 
 // Gradients.ClipByGlobalNorm on the rank average g_sum / world: norm = sqrt(Σ g_sum²) / world,
 // coef = max_norm / (norm + 1e-6); the factor applied to g_sum is min(1, coef) / world (world = 1: the reference's).
-__global__ void clip_scale_kernel(const double* sumsq, double max_norm, int world, double* scale, double* norm_out) {
-    const double norm = sqrt(*sumsq) / world;
+// One CTA of 256 threads: the SUMSQ_BLOCKS partials summed in a fixed order (strided per thread, then a fixed tree).
+__global__ void __launch_bounds__(256) clip_scale_kernel(const double* partials, double max_norm, int world,
+                                                         double* sumsq, double* scale, double* norm_out) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < SUMSQ_BLOCKS; i += blockDim.x) s += partials[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __shared__ double ws[8];
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += ws[w];
+    *sumsq = t;
+    const double norm = sqrt(t) / world;
     const double coef = max_norm / (norm + 1e-6);
     *scale = (coef < 1.0 ? coef : 1.0) / world;
     if (norm_out) *norm_out = norm;
@@ -940,15 +952,19 @@ int rlcd(const tr::RlcdArgs& a, cudaStream_t s) {
     LAYA_CUDA(cudaGetLastError());
     return OK;
 }
-int sumsq(const float* g, size_t n, double* out, cudaStream_t s) {
-    if (n == 0) return OK;
-    tr::sumsq_kernel<<<148 * 8, 256, 0, s>>>(g, n, out);
+int sumsq(const float* g, size_t n, double* partials, cudaStream_t s) {
+    if (n == 0) {
+        LAYA_CUDA(cudaMemsetAsync(partials, 0, sizeof(double) * SUMSQ_BLOCKS, s));
+        return OK;
+    }
+    tr::sumsq_kernel<<<SUMSQ_BLOCKS, 256, 0, s>>>(g, n, partials);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
 }
-int clip_scale(const double* sumsq, double max_norm, int world, double* scale, double* norm_out, cudaStream_t s) {
-    tr::clip_scale_kernel<<<1, 1, 0, s>>>(sumsq, max_norm, world, scale, norm_out);
+int clip_scale(const double* partials, double max_norm, int world, double* sumsq, double* scale, double* norm_out,
+               cudaStream_t s) {
+    tr::clip_scale_kernel<<<1, 256, 0, s>>>(partials, max_norm, world, sumsq, scale, norm_out);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;

@@ -329,3 +329,23 @@ def test_errors_are_reported_like_the_reference(tiny_trainer):
         t.objective(fresh, sigma=0.3)
     with pytest.raises(laya_b200.LayaNotFoundError):
         t.upload("encoder.layers.9.attn.Wo.weight", np.zeros((128, 128), np.float32))
+
+
+def test_gradient_norm_is_the_same_bits_every_time(cuda):
+    """ClipByGlobalNorm's Σg² is summed in a fixed order (per-block partials, then a fixed tree), so the same gradient
+    gives the same norm bit for bit: data-parallel ranks holding the same all-reduced gradient clip it identically."""
+    import laya_b200
+    cfg, w, g = tiny()
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=256, max_items=16, max_markers=64),
+                          laya_b200.train_desc(max_segment=128))
+    t.load(w)
+    items = g["batch"]["items"]
+    b = t.batch(fixture_items(g))
+    t.zero_grads()
+    t.forward(b, training=False)
+    t.backward(b, [np.array(it["coeff"], np.float32) * 50 for it in items])
+    # each call clips and steps on the same (untouched) gradient buffer
+    norms = [t.clip_and_step(max_norm=0.5) for _ in range(4)]
+    assert len({np.float64(n).tobytes() for n in norms}) == 1, norms
+    b.close()
+    t.close()
