@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "ksplit.h"
 #include "train.h"
 
 namespace laya {
@@ -303,22 +304,8 @@ static int launch(const Args& a, cudaStream_t stream) {
     }
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
     const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
-    // Few output tiles over a long K (weight gradients: K = tokens) leave most SMs idle: an accumulating output
-    // splits K into chunks of at least 4 k-blocks whose partial tiles reduce-add into it. The chunk count minimises
-    // (rounds of units over the SMs) × (k-blocks per unit + one for the unit's epilogue), so the last round is not
-    // left mostly idle.
-    int ksplit = 1;
-    if (EPI == EPI_F32_ADD && a.ksplit_ok && tiles < nsm) {
-        const int kblocks = (a.K + BK - 1) / BK;
-        long best = -1;
-        for (int want = 1; want <= std::max(1, kblocks / 4); ++want) {
-            const int kchunk = (kblocks + want - 1) / want;
-            const int ks = (kblocks + kchunk - 1) / kchunk;   // every chunk non-empty: the last starts below kblocks
-            const long rounds = (static_cast<long>(tiles) * ks + nsm - 1) / nsm;
-            const long cost = rounds * (kchunk + 1);
-            if (best < 0 || cost < best) { best = cost; ksplit = ks; }
-        }
-    }
+    // an accumulating product may split K (ksplit.h: few output tiles over a long K)
+    const int ksplit = EPI == EPI_F32_ADD && a.ksplit_ok ? choose_ksplit(tiles, (a.K + BK - 1) / BK, nsm) : 1;
     const int units = tiles * ksplit;
     KParams p{a.M, a.N, a.K, splits, ksplit, a.bias, a.err};
     kern<<<units < nsm ? units : nsm, C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tO, p);
