@@ -1046,23 +1046,22 @@ static int launch_tc(const fa::Args& a, cudaStream_t s) {
     if (!rc) rc = make_tmap_2d(&tl, SPLIT ? a.qkv_lo : a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
                                static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
     if (rc) return rc;
-    static bool attr[64] = {false};
-    int dev = 0;
+    static DeviceOnce attr;
+    int dev = 0, nsm = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<SPLIT, DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM));
-        attr[dev] = true;
+        attr.mark(dev);
     }
+    if (int e = sm_count(dev, &nsm)) return e;
     fat::Params p{};
     p.seg_start = a.seg_start; p.seg_len = a.seg_len;
     p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
     p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.out = a.out; p.out_lo = a.out_lo; p.ldo = a.ldo; p.lse = a.lse; p.err = a.err;
-    static int sms[64] = {0};
-    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-    const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    const int items = a.max_tq * a.heads;
     fat::fwd_tc_kernel<SPLIT, DROP><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, tl, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
@@ -1078,16 +1077,15 @@ static int launch_infer_tc(const InferAttn& a, cudaStream_t s) {
     int rc = make_tmap_2d(&th, a.qkv16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.T, 3 * a.hidden,
                           static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true);
     if (rc) return rc;
-    static bool attr[64] = {false};
-    static int sms[64] = {0};
-    int dev = 0;
+    static DeviceOnce attr;
+    int dev = 0, nsm = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(fat::fwd_tc_kernel<false, false, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM));
-        LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-        attr[dev] = true;
+        attr.mark(dev);
     }
+    if (int e = sm_count(dev, &nsm)) return e;
     fat::Params p{};
     p.seg_start = a.seg_start; p.seg_len = a.seg_len;
     p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
@@ -1095,7 +1093,7 @@ static int launch_infer_tc(const InferAttn& a, cudaStream_t s) {
     p.scale = a.scale; p.keep = 1.0f;
     p.q8 = a.q; p.q8d = a.d; p.q8ldd = a.ldd; p.err = a.err;
     p.out = a.hi; p.out_lo = a.lo; p.ldo = a.hidden;
-    const int items = a.max_tq * a.heads, nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    const int items = a.max_tq * a.heads;
     fat::fwd_tc_kernel<false, false, MODE><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, th, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
@@ -1133,13 +1131,13 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
     if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
                                static_cast<uint64_t>(a.ldo) * 2, fat::BQ2, fat::HD, true);
     if (rc) return rc;
-    static bool attr[64] = {false};
+    static DeviceOnce attr;
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(fat::bwd_dkdv_tc_kernel<DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        fat::BWD_SMEM));
-        attr[dev] = true;
+        attr.mark(dev);
     }
     fat::BwdParams p{};
     p.seg_start = a.seg_start; p.seg_len = a.seg_len;
@@ -1173,14 +1171,15 @@ static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
     if (!rc) rc = make_tmap_2d(&tdo, a.dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.hidden,
                                static_cast<uint64_t>(a.ldo) * 2, fat::BQ, fat::HD, true);
     if (rc) return rc;
-    static bool attr[64] = {false};
-    int dev = 0;
+    static DeviceOnce attr;
+    int dev = 0, nsm = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    if (dev < 64 && !attr[dev]) {
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(fat::bwd_dq_tc_kernel<DROP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        fat::DQ_SMEM));
-        attr[dev] = true;
+        attr.mark(dev);
     }
+    if (int e = sm_count(dev, &nsm)) return e;
     fat::BwdParams p{};
     p.seg_start = a.seg_start; p.seg_len = a.seg_len;
     p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
@@ -1188,9 +1187,7 @@ static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
-    static int sms[64] = {0};
-    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-    const int items = a.max_tq * a.heads, slots = 2 * (dev < 64 && sms[dev] > 0 ? sms[dev] : 148);   // 2 CTAs per SM
+    const int items = a.max_tq * a.heads, slots = 2 * nsm;   // 2 CTAs per SM
     fat::bwd_dq_tc_kernel<DROP><<<items < slots ? items : slots, 320, fat::DQ_SMEM, s>>>(tq, tkv, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());

@@ -295,15 +295,14 @@ static int launch(const Args& a, cudaStream_t stream) {
     auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, EPI>;
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    static uint64_t attr_set = 0;
-    static int sms[64] = {0};
-    if (dev < 64 && !(attr_set & (1ull << dev))) {
+    static DeviceOnce attr;   // per instantiation
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-        attr_set |= 1ull << dev;
+        attr.mark(dev);
     }
+    int nsm = 0;
+    if (int e = sm_count(dev, &nsm)) return e;
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
-    const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
     // an accumulating product may split K (ksplit.h: few output tiles over a long K)
     const int ksplit = EPI == EPI_F32_ADD && a.ksplit_ok ? choose_ksplit(tiles, (a.K + BK - 1) / BK, nsm) : 1;
     const int units = tiles * ksplit;

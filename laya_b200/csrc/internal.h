@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include <string>
 
 namespace laya {
@@ -31,6 +33,31 @@ int cuda_fail(cudaError_t e, const char* what);
         cudaError_t e_ = (call);                             \
         if (e_ != cudaSuccess) return ::laya::cuda_fail(e_, #call); \
     } while (0)
+
+// Once-per-device launcher set-up (a kernel's dynamic shared-memory limit), safe when several host threads launch at
+// once: a race repeats the idempotent set-up call, it never skips it. Devices 64 and above are set up on every call.
+struct DeviceOnce {
+    std::atomic<uint64_t> bits{0};
+    bool done(int dev) const { return dev >= 0 && dev < 64 && ((bits.load(std::memory_order_acquire) >> dev) & 1u); }
+    void mark(int dev) {
+        if (dev >= 0 && dev < 64) bits.fetch_or(uint64_t{1} << dev, std::memory_order_release);
+    }
+};
+
+// The device's multiprocessor count, cached per device (thread-safe).
+inline int sm_count(int dev, int* out) {
+    static std::atomic<int> cache[64];
+    if (dev >= 0 && dev < 64) {
+        const int v = cache[dev].load(std::memory_order_relaxed);
+        if (v > 0) { *out = v; return OK; }
+    }
+    int v = 0;
+    const cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
+    if (dev >= 0 && dev < 64) cache[dev].store(v, std::memory_order_relaxed);
+    *out = v;
+    return OK;
+}
 
 // 2-D tensor map over a row-major [rows, cols] matrix, tile box [box_rows, box_cols]; out-of-range elements read
 // as zero.  swizzle128: 128-byte swizzle (MMA operand tiles) or none (plain tiles such as block scales).

@@ -355,16 +355,16 @@ static int launch(const GemmArgs& a, cudaStream_t stream) {
     auto kern = q8_gemm_kernel<BN, EPI_WARPS, STAGES, EPI>;
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
-    static uint64_t attr_set = 0;   // per instantiation, one bit per device
-    if (dev < 64 && !(attr_set & (1ull << dev))) {
+    static DeviceOnce attr;   // per instantiation
+    if (!attr.done(dev)) {
         LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        attr_set |= 1ull << dev;
+        attr.mark(dev);
     }
     KParams p{a.M, a.N, a.K, a.bias, a.out, a.ldo, a.qout, a.ldqo, a.qsc, a.ldqs, a.err};
-    static int sms[64] = {0};
-    if (dev < 64 && sms[dev] == 0) LAYA_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    int nsm = 0;
+    if (int e = sm_count(dev, &nsm)) return e;
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BM - 1) / BM);
-    const int ctas = tiles < (dev < 64 ? sms[dev] : 148) ? tiles : (dev < 64 ? sms[dev] : 148);
+    const int ctas = tiles < nsm ? tiles : nsm;
     kern<<<ctas, C::THREADS, C::SMEM, stream>>>(tA, tB, tDX, tDW, tO, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
