@@ -202,7 +202,8 @@ int laya_gemm_bf16_split_device(laya_ctx* ctx, int M, int N, int K, const uint16
  *   output_stride a multiple of 4); weight_codes
  *   [N, K] and weight_scales [K/32, ldw] are a projection in the device layout of laya_q8_0_quantize_weights_device
  *   (16-byte aligned, ldw >= N and a multiple of 4); bias [N] or NULL.  Enqueued on `stream` (NULL: the legacy default
- *   stream); the call returns without synchronising.
+ *   stream).  The call then waits for that stream and reads back the product's status word: a bounded device-side
+ *   wait that gave up returns LAYA_ERR_DEVICE_TIMEOUT (message in laya_last_error()), and y is then not valid.
  * The scratch (activation codes, their scales, a status word) is one static device array of LAYA_NOALLOC_SCRATCH_BYTES
  * that every GPU loading the library holds until the process exits; a call needs about rows·K·2 + rows·K/8 bytes of it,
  * and larger calls fail with LAYA_ERR_ARGUMENT before anything runs.  The first call on a device looks up the array's

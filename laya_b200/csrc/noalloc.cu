@@ -80,8 +80,12 @@ extern "C" int laya_q8_0_linear_noalloc(const float* x, int rows, int input_stri
     q8::code_t* codes = reinterpret_cast<q8::code_t*>(static_cast<unsigned char*>(base) + kStatusBytes);
     float* scales = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + kStatusBytes + code_bytes);
 
-    // The array keeps whatever the previous call left; only the status word must start at zero.
+    // The array keeps whatever the previous call left.  Two things must start at zero: the status word, and the
+    // scales of the padded rows [rows, ldx) of each block row, which the product reads with the rest of its 128-row
+    // tile (their accumulators are never stored, but an old call's bytes there could be NaN or Inf).
     LAYA_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+    if (ldx > static_cast<size_t>(rows))
+        LAYA_CUDA(cudaMemset2DAsync(scales + rows, ldx * sizeof(float), 0, (ldx - rows) * sizeof(float), K / 32, s));
     int rc = q8::quantize_activations(x, rows, input_stride, K, codes, scales, static_cast<int>(ldx), s);
     if (rc != OK) return rc;
     q8::GemmArgs a{};
@@ -90,5 +94,14 @@ extern "C" int laya_q8_0_linear_noalloc(const float* x, int rows, int input_stri
     a.qw = reinterpret_cast<const q8::code_t*>(weight_codes); a.dw = weight_scales; a.ldw = ldw;
     a.bias = bias; a.epi = q8::EPI_STORE; a.out = y; a.ldo = output_stride;
     a.err = status;
-    return q8::gemm(a, s);
+    rc = q8::gemm(a, s);
+    if (rc != OK) return rc;
+    // The product's waits are bounded; one that gives up writes the status word and leaves y incomplete.  The next
+    // call clears the word, so read it now: copy it to the host and wait for the stream.
+    int h = 0;
+    LAYA_CUDA(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, s));
+    LAYA_CUDA(cudaStreamSynchronize(s));
+    if (h == LAYA_DEV_ERR_TIMEOUT) { set_error("a device-side wait of the product timed out; y is not valid"); return ERR_DEVICE_TIMEOUT; }
+    if (h != 0) { set_error("the product reported device error " + std::to_string(h) + "; y is not valid"); return ERR_CUDA; }
+    return OK;
 }

@@ -59,6 +59,51 @@ def test_no_alloc_projection_equals_the_allocating_one(cuda):
     ctx.close()
 
 
+def _need(rows, K):
+    """Bytes of the static scratch one call takes: a 256-byte status word, the codes [rows, K] (2 bytes each, padded
+    to 256 bytes) and the block scales [K/32, rows rounded up to 128] (4 bytes each)."""
+    ldx = (rows + 127) // 128 * 128
+    return 256 + (rows * K * 2 + 255) // 256 * 256 + (K // 32) * ldx * 4
+
+
+def _largest_rows(K, limit=8 << 20):
+    rows = limit // (2 * K)
+    while _need(rows, K) > limit:
+        rows -= 1
+    return rows
+
+
+@pytest.mark.parametrize("K", [3072, 9216])
+def test_no_alloc_at_the_scratch_limit(cuda, K):
+    """The largest call that fits the scratch equals the allocating path bit for bit, twice (the second call with
+    fewer rows, so it reads scales the first call left in the padded rows), and one row more is rejected."""
+    torch = cuda
+    import laya_b200
+    L = laya_b200.lib()
+    rows = _largest_rows(K)
+    assert _need(rows, K) <= 8 << 20 < _need(rows + 1, K)
+    ctx = laya_b200.Context(laya_b200.base_desc(max_tokens=256, max_items=4, max_markers=16))
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    rng = np.random.default_rng(K)
+    N = 256
+    codes, scales, ldw = _weight(torch, laya_b200, ctx, rng, N, K)
+    stream = torch.cuda.current_stream().cuda_stream
+    for call, r in enumerate([rows, rows - 77]):
+        x = torch.from_numpy(rng.normal(0, 1, (r, K)).astype(np.float32)).cuda()
+        y = torch.full((r, N), float("nan"), dtype=torch.float32, device="cuda")
+        laya_b200.api.check(L.laya_q8_0_linear_noalloc(
+            x.data_ptr(), r, K, codes.data_ptr(), scales.data_ptr(), ldw, N, K, None, y.data_ptr(), N, stream))
+        want = _allocating_path(torch, laya_b200, ctx, x, r, K, codes, scales, ldw, N, K, None)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(y.cpu().numpy()), bits(want.cpu().numpy())), f"K={K} call {call} differs"
+    x = torch.zeros((rows + 1, K), dtype=torch.float32, device="cuda")
+    y = torch.zeros((rows + 1, N), dtype=torch.float32, device="cuda")
+    rc = L.laya_q8_0_linear_noalloc(x.data_ptr(), rows + 1, K, codes.data_ptr(), scales.data_ptr(), ldw, N, K, None,
+                                    y.data_ptr(), N, stream)
+    assert rc == 1 and b"scratch" in L.laya_last_error()
+    ctx.close()
+
+
 def test_no_alloc_rejects_calls_beyond_its_scratch(cuda):
     torch = cuda
     import laya_b200
