@@ -17,6 +17,7 @@ from typing import Dict, List, Optional
 
 import numpy as np
 import torch
+from torch.utils.checkpoint import checkpoint
 
 from .model import EncoderConfig
 
@@ -119,6 +120,12 @@ class TorchTrainModel:
                 c, s = self.rope(kind, L)
                 q, k = apply_rope(q, c[:L], s[:L]), apply_rope(k, c[:L], s[:L])
             q, k = self.round_operand(q), self.round_operand(k)
+            if L * L * heads > (1 << 27) and dropout == 0:
+                # long rows (an 8192-token row holds 16 × 8192² scores): one head at a time, its scores recomputed
+                # in the backward instead of kept, so the oracle stays within a few GB of host memory
+                outs.append(torch.cat([checkpoint(self._head_unit, q[:, hh], k[:, hh], v[:, hh], window, float(scale),
+                                                  use_reentrant=False) for hh in range(heads)], 1))
+                continue
             sc = torch.einsum("thd,jhd->htj", q, k) * float(scale)
             if window >= 0:
                 i = torch.arange(L)
@@ -135,6 +142,15 @@ class TorchTrainModel:
                 pr = pr * torch.from_numpy(m)
             outs.append(torch.einsum("htj,jhd->thd", self.round_operand(pr), self.round_operand(v)).reshape(L, H))
         return torch.cat(outs, 0)
+
+    def _head_unit(self, q, k, v, window, scale):
+        """Ops.ForwardUnit (Ops.cs:329-366) for one (segment, head): q, k, v [L, d]."""
+        L = q.shape[0]
+        sc = (q @ k.t()) * scale
+        if window >= 0:
+            i = torch.arange(L)
+            sc = sc.masked_fill((i[:, None] - i[None, :]).abs() > window, float("-inf"))
+        return self.round_operand(torch.softmax(sc, -1)) @ self.round_operand(v)
 
     def forward(self, items, training=False, seed=0):
         """TrainableDecisionModel.Forward (TrainableDecisionModel.cs:248-353): option logits per item."""
