@@ -74,7 +74,7 @@ def parse():
                     help="3: ModernBERT-base, 32 rows x U{256..1024}; 4: ModernBERT-large, 4 rows x 8192 tokens")
     ap.add_argument("--train-rows", type=int, default=None, help="rows per GPU of the fine-tune step")
     ap.add_argument("--train-layers", type=int, default=None, help="encoder layers (fewer only for small captures)")
-    ap.add_argument("--kernel", choices=["q8_gemm", "bf16_gemm"],
+    ap.add_argument("--kernel", choices=["q8_gemm", "bf16_gemm", "mma_peak"],
                     help="time one product alone at the workload's shapes (profiling captures), not the step")
     ap.add_argument("--case", default="wqkv",
                     help="q8_gemm: wqkv|wo|wi|mlp_wo; bf16_gemm: fwd_split|dx|dw (the Wqkv projection, 20480 tokens)")
@@ -967,10 +967,34 @@ def run_ours(args):
 
 
 # --------------------------------------------------------------------------------------------------- one product
+def run_mma_peak():
+    """The tensor-core rate per MMA form and width on this device (laya_mma_peak): one CTA per SM issuing back-to-back
+    M 128 x N MMAs from fixed shared-memory (or, TS, tensor-memory) operands.  One JSON line per (form, N)."""
+    import ctypes
+    import torch
+    import laya_b200
+    torch.cuda.set_device(0)
+    L = laya_b200.lib()
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    forms = {"bf16": (0, 16), "f16": (1, 16), "i8": (2, 32), "bf16_ts": (3, 16), "bf16_mn": (4, 16),
+             "bf16_ts_mn": (5, 16)}
+    reps = 20000
+    for name, (form, k) in forms.items():
+        for n in (64, 128, 256):
+            ms, cyc = ctypes.c_double(), ctypes.c_double()
+            laya_b200.api.check(L.laya_mma_peak(form, n, reps, ctypes.byref(ms), ctypes.byref(cyc)))
+            ops = nsm * reps * 4 * 2.0 * 128 * n * k
+            print(json.dumps({"kernel": "mma_peak", "form": name, "M": 128, "N": n, "K": k,
+                              "tops": ops / (ms.value / 1e3) / 1e12, "cycles_per_mma": cyc.value,
+                              "ops_per_clk_per_sm": 2.0 * 128 * n * k / cyc.value, "ms": ms.value}), flush=True)
+
+
 def run_kernel(args):
     """One product alone at a workload shape, CUDA events over --reps launches (the command ncu captures)."""
     import torch
     import laya_b200
+    if args.kernel == "mma_peak":
+        return run_mma_peak()
     torch.cuda.set_device(0)
     ctx = laya_b200.Context(laya_b200.base_desc(max_tokens=512, max_items=4, max_markers=16))
     st = torch.cuda.current_stream()

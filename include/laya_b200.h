@@ -253,6 +253,22 @@ int laya_record_get(laya_ctx* ctx, const char* name, float* host, int64_t count)
  */
 int laya_encoder_layer(laya_ctx* ctx, int layer, float* hidden, const int32_t* seg_len, int n_items);
 
+/*
+ * laya_mma_peak — a measurement, not part of the reference's interface (it has no counterpart there): the rate of
+ * the tensor cores on the current device for one MMA form, the denominator the library's product kernels are
+ * reported against.  One CTA per SM issues `reps` rounds of four back-to-back M 128 × N (64, 128 or 256) MMAs of
+ * one 128-byte k-block from fixed shared-memory operands into one TMEM accumulator.  *ms: the launch's elapsed time;
+ * *cycles_per_mma: mean SM cycles per MMA instruction seen by the issuing threads.  Work per launch:
+ * SMs × reps × 4 × 2 × 128 × N × K (K 16 for the 16-bit forms, 32 for int8).
+ */
+#define LAYA_MMA_BF16 0      /* kind::f16, bf16 operands, fp32 accumulate */
+#define LAYA_MMA_F16 1       /* kind::f16, fp16 operands (the Q8_0 product's form) */
+#define LAYA_MMA_I8 2        /* kind::i8, s8 operands, s32 accumulate */
+#define LAYA_MMA_BF16_TS 3   /* kind::f16 bf16 with A read from tensor memory */
+#define LAYA_MMA_BF16_MN 4   /* kind::f16 bf16 with B read N-contiguous (MN-major) */
+#define LAYA_MMA_BF16_TS_MN 5   /* A from tensor memory, B N-contiguous (the attention P·V form) */
+int laya_mma_peak(int form, int n, int reps, double* ms, double* cycles_per_mma);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,7 @@ _SIGS = {
     "laya_q8_0_gemm_fused_device": (_I, [_P, _I, _P, _P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _I]),
     "laya_pack_q8_0": (_I, [_P, ctypes.c_char_p, _I, _P, _I, _I]),
     "laya_q8_0_linear_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P]),
+    "laya_mma_peak": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "laya_gemm_bf16_device": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _P, _I, _P, _I]),
     "laya_gemm_bf16_split_device": (_I, [_P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _I, _I, _P, _I, _P, _I]),
     "laya_decision_forward": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P]),

@@ -106,6 +106,13 @@ DEVI void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory
 DEVI void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 DEVI void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Warms L2 with a tile a later TMA load will read (no shared-memory write, no completion to wait for).
+DEVI void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 DEVI void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -192,6 +199,11 @@ DEVI uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 DEVI uint64_t f2_mul(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+DEVI uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
 DEVI uint64_t f2_sub(uint64_t a, uint64_t b) {

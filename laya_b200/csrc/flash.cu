@@ -629,8 +629,10 @@ int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s) {
     const int hd = a.hidden / a.heads;
     const bool split = a.qkv_lo != nullptr;
     if (split && !a.out_lo) { set_error("accurate attention needs the context's low part"); return ERR_ARGUMENT; }
-    if (hd == 64) {   // the tcgen05 forward (flash_tc.cu) when the batch carries its 128-row tile list
-        const int rc = flash_forward_tc(a, s);
+    if (hd == 64) {   // the tcgen05 forwards (flash_pp.cu, flash_tc.cu) when the batch carries their tile lists
+        int rc = flash_forward_pp(a, s);
+        if (rc != ERR_NOT_SUPPORTED) return rc;
+        rc = flash_forward_tc(a, s);
         if (rc != ERR_NOT_SUPPORTED) return rc;
         return split ? launch_fwd<64, true>(a, max_tiles, s) : launch_fwd<64, false>(a, max_tiles, s);
     }

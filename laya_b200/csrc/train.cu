@@ -143,12 +143,13 @@ struct laya_batch {
     size_t bytes = 0;
     cudaEvent_t staged = nullptr;
     int32_t *ids, *seg_start, *seg_len, *qtype, *tok_item, *tile_item, *tile_p0, *n_tiles, *marker_rows, *mk_start,
-        *mk_count, *tq_item, *tq_p0, *n_tq;
-    int tq = 0;                      // 128-row query tiles (tcgen05 attention forward)
+        *mk_count, *tq_item, *tq_p0, *n_tq, *tp_item, *tp_p0, *n_tp;
+    int tq = 0;                      // 128-row query tiles (tcgen05 attention)
+    int tp = 0;                      // 256-row pair tiles (the two-tile attention forward), longest segments first
     float* targets;
     double* draws;
     size_t o_ids, o_seg_start, o_seg_len, o_qtype, o_tok_item, o_tile_item, o_tile_p0, o_n_tiles, o_marker_rows,
-        o_mk_start, o_mk_count, o_tq_item, o_tq_p0, o_n_tq, o_targets, o_draws;
+        o_mk_start, o_mk_count, o_tq_item, o_tq_p0, o_n_tq, o_tp_item, o_tp_p0, o_n_tp, o_targets, o_draws;
 };
 
 struct Comm {
@@ -432,6 +433,7 @@ fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const 
     a.out = out; a.ldo = t->H; a.lse = lse;
     a.dqkv = t->dqkv16; a.lddq = 3 * t->H; a.dsum = t->dsum; a.dout = t->dctx16;
     a.tq_item = b->tq_item; a.tq_p0 = b->tq_p0; a.n_tq = b->n_tq; a.max_tq = b->tq; a.T = b->T;
+    a.tp_item = b->tp_item; a.tp_p0 = b->tp_p0; a.n_tp = b->n_tp; a.max_tp = b->tp;
     a.err = t->err;
     return a;
 }
@@ -1293,6 +1295,7 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
     b->o_tok_item = take(4 * T); b->o_tile_item = take(4 * TL); b->o_tile_p0 = take(4 * TL); b->o_n_tiles = take(4);
     b->o_marker_rows = take(4 * M); b->o_mk_start = take(4 * N); b->o_mk_count = take(4 * N);
     b->o_tq_item = take(4 * TL); b->o_tq_p0 = take(4 * TL); b->o_n_tq = take(4);
+    b->o_tp_item = take(4 * TL); b->o_tp_p0 = take(4 * TL); b->o_n_tp = take(4);
     b->o_targets = take(4 * M); b->o_draws = take(8 * MAX_GROUPS * M);
     b->bytes = o;
     if (cudaMalloc(&b->dev, o) != cudaSuccess || cudaMallocHost(&b->host, o) != cudaSuccess ||
@@ -1316,6 +1319,9 @@ int laya_batch_create(laya_trainer* t, laya_batch** out) {
     b->tq_item = reinterpret_cast<int32_t*>(base + b->o_tq_item);
     b->tq_p0 = reinterpret_cast<int32_t*>(base + b->o_tq_p0);
     b->n_tq = reinterpret_cast<int32_t*>(base + b->o_n_tq);
+    b->tp_item = reinterpret_cast<int32_t*>(base + b->o_tp_item);
+    b->tp_p0 = reinterpret_cast<int32_t*>(base + b->o_tp_p0);
+    b->n_tp = reinterpret_cast<int32_t*>(base + b->o_n_tp);
     b->targets = reinterpret_cast<float*>(base + b->o_targets);
     b->draws = reinterpret_cast<double*>(base + b->o_draws);
     *out = b;
@@ -1368,6 +1374,8 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
     int32_t* hmc = reinterpret_cast<int32_t*>(h + b->o_mk_count);
     int32_t* hqi = reinterpret_cast<int32_t*>(h + b->o_tq_item);
     int32_t* hqp = reinterpret_cast<int32_t*>(h + b->o_tq_p0);
+    int32_t* hpi = reinterpret_cast<int32_t*>(h + b->o_tp_item);
+    int32_t* hpp = reinterpret_cast<int32_t*>(h + b->o_tp_p0);
     std::memcpy(h + b->o_ids, ids, sizeof(int32_t) * T);
     int start = 0, mk = 0, tiles = 0, tq = 0;
     double pg = 0, pl = 0;
@@ -1392,6 +1400,14 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
     }
     *reinterpret_cast<int32_t*>(h + b->o_n_tiles) = tiles;
     *reinterpret_cast<int32_t*>(h + b->o_n_tq) = tq;
+    // pair tiles, longest segments first (a persistent CTA walks them in this order: the long items start first)
+    std::vector<int> order(n_items);
+    for (int i = 0; i < n_items; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return seg_len[x] > seg_len[y]; });
+    int tp = 0;
+    for (int i : order)
+        for (int p0 = 0; p0 < seg_len[i]; p0 += 256) { hpi[tp] = i; hpp[tp] = p0; ++tp; }
+    *reinterpret_cast<int32_t*>(h + b->o_n_tp) = tp;
     if (targets) std::memcpy(h + b->o_targets, targets, sizeof(float) * M);
     else std::memset(h + b->o_targets, 0, sizeof(float) * M);
     if (groups > 0) {
@@ -1401,6 +1417,7 @@ int laya_batch_set(laya_trainer* t, laya_batch* b, const int32_t* ids, const int
     }
     b->T = static_cast<int>(T); b->n = n_items; b->M = static_cast<int>(M); b->tiles = tiles; b->groups = groups;
     b->tq = tq;
+    b->tp = tp;
     b->pairs_global = pg;
     b->pairs_local = pl;
     b->version++;

@@ -52,6 +52,8 @@ struct Args {
     __nv_bfloat16* out_lo;                                           // accurate forward: context low part
     // the tcgen05 forward (head_dim 64): 128-row query tiles of every segment, and the token count
     const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq; int max_tq; int T;
+    // the two-tile forward: 256-row pair tiles of every segment
+    const int32_t* tp_item = nullptr; const int32_t* tp_p0 = nullptr; const int32_t* n_tp = nullptr; int max_tp = 0;
     int* err;
 };
 }  // namespace fa
@@ -62,6 +64,7 @@ int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int head
               int ldd, cudaStream_t s);
 int flash_forward(const fa::Args& a, int max_tiles, cudaStream_t s);
 int flash_forward_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: head_dim 64 (ERR_NOT_SUPPORTED otherwise)
+int flash_forward_pp(const fa::Args& a, cudaStream_t s);   // flash_pp.cu: head_dim 64, two query tiles per CTA
 int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: dK, dV for head_dim 64
 int flash_backward_dq_tc(const fa::Args& a, cudaStream_t s);     // flash_tc.cu: dQ for head_dim 64
 // The decision forward's attention (inference) on the tensor cores: qkv16 [T, ld] fp16 = rotated q | k | v, 128-row
