@@ -337,29 +337,42 @@ __global__ void __launch_bounds__(128) fwd_kernel(Args a) {
 }
 
 // D_i = Σ_d dO · O per (token, head), fp32.  HD/8 lanes per (token, head), each reading 8 consecutive bf16 of dO
-// and O with one 16-byte load apiece, then a shuffle sum over the group.
+// and O with one 16-byte load apiece, then a shuffle sum over the group; a thread takes DOT_ROWS tokens T/DOT_ROWS
+// apart, with every load issued before the first sum.
+constexpr int DOT_ROWS = 4;
 template <int HD>
 __global__ void bwd_dot_kernel(Args a, int T) {
     constexpr int G = HD / 8;   // lanes per (token, head)
+    const int per = (T + DOT_ROWS - 1) / DOT_ROWS;   // tokens per slice
     const int gt = blockIdx.x * blockDim.x + threadIdx.x;
     const int item = gt / G, l = gt % G;
-    const bool active = item < T * a.heads;
+    const bool active = item < per * a.heads;
     const int it = active ? item : 0;
-    const int t = it / a.heads, h = it % a.heads;
-    const size_t off = static_cast<size_t>(t) * a.ldo + h * HD + 8 * l;
-    const uint4 x = *reinterpret_cast<const uint4*>(a.dout + off), y = *reinterpret_cast<const uint4*>(a.out + off);
-    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
-    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
-    float s = 0.f;
+    const int t0 = it / a.heads, h = it % a.heads;
+    uint4 x[DOT_ROWS], y[DOT_ROWS];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const float2 u = __bfloat1622float2(xa[k]), v = __bfloat1622float2(ya[k]);
-        s = fmaf(u.x, v.x, s);
-        s = fmaf(u.y, v.y, s);
+    for (int r = 0; r < DOT_ROWS; ++r) {
+        const int t = t0 + r * per;
+        const size_t off = static_cast<size_t>(t < T ? t : 0) * a.ldo + h * HD + 8 * l;
+        x[r] = *reinterpret_cast<const uint4*>(a.dout + off);
+        y[r] = *reinterpret_cast<const uint4*>(a.out + off);
     }
 #pragma unroll
-    for (int m = G / 2; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-    if (active && l == 0) a.dsum[static_cast<size_t>(t) * a.heads + h] = s;
+    for (int r = 0; r < DOT_ROWS; ++r) {
+        const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x[r]);
+        const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y[r]);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 u = __bfloat1622float2(xa[k]), v = __bfloat1622float2(ya[k]);
+            s = fmaf(u.x, v.x, s);
+            s = fmaf(u.y, v.y, s);
+        }
+#pragma unroll
+        for (int m = G / 2; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+        const int t = t0 + r * per;
+        if (active && l == 0 && t < T) a.dsum[static_cast<size_t>(t) * a.heads + h] = s;
+    }
 }
 
 // Writes 16 rows x HD of a warp's fp32 accumulator as bf16 into a [T, ld] slice, rotating back by -θ when given.
@@ -668,7 +681,7 @@ static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
 int flash_backward(const fa::Args& a, int max_tiles, int T, cudaStream_t s) {
     if (max_tiles <= 0 || T <= 0) return OK;
     const int hd = a.hidden / a.heads;
-    const long long threads = static_cast<long long>(T) * a.heads * (hd / 8);
+    const long long threads = static_cast<long long>((T + fa::DOT_ROWS - 1) / fa::DOT_ROWS) * a.heads * (hd / 8);
     if ((a.ldo & 7) || (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.out) & 15)) {
         set_error("attention backward: dO and O need 16-byte aligned rows");
         return ERR_ARGUMENT;

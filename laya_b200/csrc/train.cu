@@ -205,6 +205,7 @@ struct laya_trainer {
     float *smean = nullptr, *srstd = nullptr, *spre = nullptr, *logits = nullptr, *dlog = nullptr;
     // workspace
     float *R32 = nullptr, *dH = nullptr, *dN = nullptr, *dbig32 = nullptr, *dsum = nullptr, *dsn = nullptr;
+    float* ln_part = nullptr;                                // LayerNorm backward: per-CTA dγ/dβ partials
     bf16 *d16 = nullptr, *dctx16 = nullptr, *dqkv16 = nullptr, *dbig16 = nullptr, *dpre16 = nullptr;
     float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;
     double* red = nullptr;   // [0] Σg², [1] gradient factor, [2] norm, [4..7] objective results, [8..] Σg² partials
@@ -459,6 +460,7 @@ tr::LnBwd lnb_args(laya_trainer* t, int rows, const float* x, const float* mean,
     a.rows = rows; a.n = t->H; a.x = x; a.mean = mean; a.rstd = rstd; a.w = t->master + w;
     a.dy = dy; a.dx = dx; a.accumulate = accumulate;
     a.dw = t->grad + w; a.db = b == NONE ? nullptr : t->grad + b;
+    a.part = t->ln_part;
     return a;
 }
 
@@ -856,6 +858,11 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
         return fail(rc);
     if ((rc = dalloc(t, reinterpret_cast<void**>(&t->rl_scratch), rlcd_scratch_bytes(MAX_GROUPS, t->Nc, t->Mc))))
         return fail(rc);
+    {   // the LayerNorm backward's per-CTA dγ/dβ partials
+        int nsm = 0;
+        if ((rc = sm_count(t->device, &nsm))) return fail(rc);
+        if ((rc = dalloc_t(t, &t->ln_part, static_cast<size_t>(nsm) * tr::LN_PART_CTAS_PER_SM * 2 * H))) return fail(rc);
+    }
 
     // Rotary tables (Rotary, Ops.cs:446-480): angles in double, stored fp32, [position, head_dim/2].
     const int half = t->hd / 2;

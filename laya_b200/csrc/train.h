@@ -103,7 +103,9 @@ struct LnBwd {
     const float* dy;                                        // [rows, n]
     float* dx; int accumulate; const int32_t* scatter;      // dx rows (+= when accumulate, atomic += when scatter)
     float* dw; float* db;                                   // parameter gradients (+=), may be null
+    float* part;                                            // scratch for per-CTA dγ/dβ partials ([ctas][2n]), or null
 };
+constexpr int LN_PART_CTAS_PER_SM = 1;                      // ln_bwd's persistent grid: part holds SMs × this × 2n floats
 struct AdamArgs {
     size_t n;
     float* param; const float* grad; float* m; float* v; __nv_bfloat16* shadow; __nv_bfloat16* shadow_lo;

@@ -12,6 +12,8 @@
 //   adamw / sumsq          AdamW.Step and Gradients.ClipByGlobalNorm (AdamW.cs:29-130) over flat parameter buffers,
 //                          refreshing the bf16 copies the products read.
 // Every kernel moves each byte once with 16-byte accesses where the layout allows; a warp owns a row for row-wise ops.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "train.h"
@@ -307,6 +309,108 @@ __global__ void __launch_bounds__(256) ln_bwd_vec_kernel(LnBwd a) {
 #pragma unroll
         for (int w = 0; w < 8; ++w) sb += red[w][c];
         if (a.db) atomicAdd(a.db + c, sb);
+    }
+}
+
+// The persistent LayerNorm backward for n = 128·VPL: a warp per row, rows strided over a grid of
+// LN_PART_CTAS_PER_SM CTAs of LNB_WARPS warps per SM, every load of a row (x, dy and the accumulated dx) issued
+// before its reductions.
+// dγ and dβ partials stay per (warp, lane, column) in shared memory (no atomics); at the end each CTA sums its warps
+// in a fixed order into part[cta][2n], and ln_bwd_reduce_kernel adds the CTAs' partials to dγ and dβ in a fixed
+// order — the same gradient bits on every run.
+constexpr int LNB_WARPS = 16;
+template <int VPL>
+__global__ void __launch_bounds__(LNB_WARPS * 32, 1) ln_bwd_rows_kernel(LnBwd a) {
+    extern __shared__ float4 lnp[];   // [LNB_WARPS][dγ | dβ][VPL][32 lanes] float4
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, n = a.n;
+    float4* pw = lnp + (warp * 2) * VPL * 32 + lane;
+    float4* pb = pw + VPL * 32;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) pw[32 * i] = pb[32 * i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = blockIdx.x * LNB_WARPS + warp; r < a.rows; r += gridDim.x * LNB_WARPS) {
+        const float* xr = a.x + static_cast<size_t>(a.gather ? a.gather[r] : r) * n + 4 * lane;
+        const float* dyr = a.dy + static_cast<size_t>(r) * n + 4 * lane;
+        float* dst = a.dx ? a.dx + static_cast<size_t>(a.scatter ? a.scatter[r] : r) * n + 4 * lane : nullptr;
+        const bool acc_in = dst && a.accumulate && !a.scatter;
+        float4 x[VPL], dy[VPL], prev[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            x[i] = ld4(xr + 128 * i);
+            dy[i] = ld4(dyr + 128 * i);
+            prev[i] = acc_in ? ld4(dst + 128 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const float mean = a.mean[r], rstd = a.rstd[r];
+        float sg = 0.f, sgx = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const float4 w = ld4(a.w + 4 * lane + 128 * i);
+            float4 xh = make_float4((x[i].x - mean) * rstd, (x[i].y - mean) * rstd, (x[i].z - mean) * rstd,
+                                    (x[i].w - mean) * rstd);
+            float4 q = pw[32 * i], b = pb[32 * i];
+            q.x += dy[i].x * xh.x; q.y += dy[i].y * xh.y; q.z += dy[i].z * xh.z; q.w += dy[i].w * xh.w;
+            b.x += dy[i].x; b.y += dy[i].y; b.z += dy[i].z; b.w += dy[i].w;
+            pw[32 * i] = q;
+            pb[32 * i] = b;
+            const float4 g = make_float4(dy[i].x * w.x, dy[i].y * w.y, dy[i].z * w.z, dy[i].w * w.w);
+            sg += (g.x + g.y) + (g.z + g.w);
+            sgx += (g.x * xh.x + g.y * xh.y) + (g.z * xh.z + g.w * xh.w);
+            x[i] = xh;    // x̂ and g replace x and dy
+            dy[i] = g;
+        }
+        const float mg = warp_sum(sg) / n, mgx = warp_sum(sgx) / n;
+        if (!dst) continue;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            float4 d = make_float4(rstd * (dy[i].x - mg - x[i].x * mgx), rstd * (dy[i].y - mg - x[i].y * mgx),
+                                   rstd * (dy[i].z - mg - x[i].z * mgx), rstd * (dy[i].w - mg - x[i].w * mgx));
+            float* p = dst + 128 * i;
+            if (a.scatter) {
+                atomicAdd(p, d.x); atomicAdd(p + 1, d.y); atomicAdd(p + 2, d.z); atomicAdd(p + 3, d.w);
+            } else {
+                if (a.accumulate) { d.x += prev[i].x; d.y += prev[i].y; d.z += prev[i].z; d.w += prev[i].w; }
+                *reinterpret_cast<float4*>(p) = d;
+            }
+        }
+    }
+    if (!a.dw && !a.db) return;
+    __syncthreads();
+    // column c = 128·i + 4·l + k lives in lane l's float4 i, component k; the 8 warps summed in order
+    const float* lf = reinterpret_cast<const float*>(lnp);
+    for (int c = threadIdx.x; c < 2 * n; c += blockDim.x) {
+        const int which = c >= n, cc = c - which * n, i = cc >> 7, l = (cc & 127) >> 2, k = cc & 3;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < LNB_WARPS; ++w) sum += lf[(((w * 2 + which) * VPL + i) * 32 + l) * 4 + k];
+        a.part[static_cast<size_t>(blockIdx.x) * 2 * n + c] = sum;
+    }
+}
+
+// dγ += Σ_cta part[cta][c], dβ += Σ_cta part[cta][n + c] in a fixed order: a CTA takes 32 columns; its 32 warps sum
+// the CTAs b ≡ warp (mod 32) in increasing b, then warp 0 adds the 32 sums in warp order.
+__global__ void __launch_bounds__(1024) ln_bwd_reduce_kernel(const float* __restrict__ part, int ctas, int n, float* dw,
+                                                            float* db) {
+    __shared__ float red[32][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 32 + lane;
+    float sum = 0.f;
+    if (c < 2 * n) {
+        int b = warp;
+        for (; b + 96 < ctas; b += 128) {   // four loads in flight, summed in b order
+            float s4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s4[u] = part[static_cast<size_t>(b + 32 * u) * 2 * n + c];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) sum += s4[u];
+        }
+        for (; b < ctas; b += 32) sum += part[static_cast<size_t>(b) * 2 * n + c];
+    }
+    red[warp][lane] = sum;
+    __syncthreads();
+    if (warp == 0 && c < 2 * n) {
+        float t = 0.f;
+        for (int w = 0; w < 32; ++w) t += red[w][lane];
+        float* dst = c < n ? dw : db;
+        if (dst) dst[c < n ? c : c - n] += t;
     }
 }
 
@@ -741,10 +845,19 @@ __global__ void __launch_bounds__(256) rlcd_kernel(RlcdArgs a) {
     }
 }
 
+// Eight elements per thread: two 16-byte loads, one 16-byte store.
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
-    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-    if (i + 4 <= n) st4(y + i, ldv4(x + i));
-    else for (size_t k = i; k < n; ++k) y[k] = __float2bfloat16_rn(x[k]);
+    const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+    if (i + 8 <= n) {
+        const float4 a = *reinterpret_cast<const float4*>(x + i), b = *reinterpret_cast<const float4*>(x + i + 4);
+        const __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w),
+                             h2 = __floats2bfloat162_rn(b.x, b.y), h3 = __floats2bfloat162_rn(b.z, b.w);
+        *reinterpret_cast<uint4*>(y + i) =
+            make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                       *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+    } else {
+        for (size_t k = i; k < n; ++k) y[k] = __float2bfloat16_rn(x[k]);
+    }
 }
 __global__ void f32_split_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
                                  size_t n) {
@@ -779,8 +892,39 @@ int ln_fwd(const tr::LnFwd& a, cudaStream_t s) {
     return OK;
 }
 
+template <int VPL>
+static int ln_bwd_rows(const tr::LnBwd& a, cudaStream_t s) {
+    constexpr int smem = tr::LNB_WARPS * 2 * VPL * 32 * 16;
+    static DeviceOnce attr;
+    int dev = 0, nsm = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (!attr.done(dev)) {
+        LAYA_CUDA(cudaFuncSetAttribute(tr::ln_bwd_rows_kernel<VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr.mark(dev);
+    }
+    if (int e = sm_count(dev, &nsm)) return e;
+    const int want = (a.rows + tr::LNB_WARPS - 1) / tr::LNB_WARPS, cap = tr::LN_PART_CTAS_PER_SM * nsm;
+    const int ctas = want < cap ? want : cap;
+    tr::ln_bwd_rows_kernel<VPL><<<ctas, tr::LNB_WARPS * 32, smem, s>>>(a);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    if (a.dw || a.db) {
+        tr::ln_bwd_reduce_kernel<<<blocks_for(2 * static_cast<size_t>(a.n), 32), 1024, 0, s>>>(a.part, ctas, a.n, a.dw, a.db);
+        count_launch();
+        LAYA_CUDA(cudaGetLastError());
+    }
+    return OK;
+}
+
 int ln_bwd(const tr::LnBwd& a, cudaStream_t s) {
     if (a.rows <= 0) return OK;
+    if (a.part && a.n % 128 == 0) {   // the persistent form (widths 768 and 1024: ModernBERT-base and -large)
+        switch (a.n / 128) {
+            case 6: return ln_bwd_rows<6>(a, s);
+            case 8: return ln_bwd_rows<8>(a, s);
+            default: break;
+        }
+    }
     if (a.n % 128 == 0 && a.n <= 1024 && a.n != 384 && a.n != 640 && a.n != 896) {
         const unsigned g = blocks_for(static_cast<size_t>(a.rows), tr::LN_ROWS_V);
         switch (a.n / 128) {
@@ -886,8 +1030,15 @@ int cast_mask(const float* x, __nv_bfloat16* y, size_t n, tr::Mask m, cudaStream
     LAUNCH4(cast_mask_kernel, n, x, y, n, m);
 }
 int f32_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
-    REQUIRE4(n, x, y);
-    LAUNCH4(f32_to_bf16_kernel, n, x, y, n);
+    if (n == 0) return OK;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15)) {
+        set_error("f32_to_bf16: buffers must be 16-byte aligned");
+        return ERR_ARGUMENT;
+    }
+    tr::f32_to_bf16_kernel<<<blocks_for((n + 7) / 8, 256), 256, 0, s>>>(x, y, n);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
 }
 int f32_split_bf16(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, size_t n, cudaStream_t s) {
     REQUIRE4(n, x, hi, lo);
