@@ -176,13 +176,23 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------------------------------- CPU arms
+def cpu_products():
+    """Switch the oracle's products to the AVX-512 restatements of the reference's panel kernels when this CPU has
+    them (same bits as the scalar definitions); returns the phrase the baseline's `sample` carries."""
+    import oracle
+    oracle.build()
+    if oracle.set_fast(True):
+        return "products by AVX-512 restatements of PackedMatrixQ8_0.Panel512 (VNNI) and PackedMatrix's panel kernel"
+    return "products by the scalar restatement (this CPU has no AVX-512 VNNI)"
+
+
 def q8_cpu_seconds(rows, seed=1):
     """One bounded CPU sample: the oracle's Q8_0 decision forward over `rows` × 512 tokens of the same workload."""
     import numpy as np
     import oracle
     from laya_b200 import workloads
     from oracle.model import EncoderConfig, Item, OracleModel
-    oracle.build()
+    cpu_products()
     w, q8 = workloads.decision_weights(seed=0)
     om = OracleModel(EncoderConfig(), w, workloads.dequantized(q8))
     items = workloads.decision_batch(rows=rows, length=SEQ, seed=seed)
@@ -195,7 +205,7 @@ def q8_cpu_seconds(rows, seed=1):
 def q8_cpu_baseline(rows):
     secs, cores = q8_cpu_seconds(rows)
     return {"value": rows * SEQ / secs, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{rows} x {SEQ} tokens, one full 22-layer Q8_0 decision forward ({secs:.1f} s)"}
+            "sample": f"{rows} x {SEQ} tokens, one full 22-layer Q8_0 decision forward ({secs:.1f} s); {cpu_products()}"}
 
 
 def f32_cpu_seconds(tokens, seed=1):
@@ -205,7 +215,7 @@ def f32_cpu_seconds(tokens, seed=1):
     import oracle
     from laya_b200 import workloads
     from oracle.model import EncoderConfig, Item, OracleModel
-    oracle.build()
+    cpu_products()
     w = workloads.bf16_checkpoint_weights(**LARGE, seed=0)
     om = OracleModel(EncoderConfig(**LARGE), w)
     items = workloads.decision_batch(rows=1, length=tokens, seed=seed)
@@ -221,7 +231,7 @@ F32_CPU_TOKENS = 512
 def f32_cpu_baseline(tokens=F32_CPU_TOKENS):
     secs, cores = f32_cpu_seconds(tokens)
     return {"value": tokens / secs, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"1 x {tokens} tokens, one full 28-layer fp32 decision forward ({secs:.1f} s)"}
+            "sample": f"1 x {tokens} tokens, one full 28-layer fp32 decision forward ({secs:.1f} s); {cpu_products()}"}
 
 
 def dec_cpu_baseline(tokens, reps=1):
@@ -231,7 +241,7 @@ def dec_cpu_baseline(tokens, reps=1):
     import oracle
     from laya_b200 import workloads
     from oracle.decoder import DecoderConfig, OracleDecoder, mica_config
-    oracle.build()
+    products = cpu_products()
     kinds = workloads.MICA_KINDS[:4]
     q8, vec = workloads.decoder_q8_weights(kinds, seed=0)
     base = mica_config()
@@ -264,7 +274,7 @@ def dec_cpu_baseline(tokens, reps=1):
     return {"value": tokens / secs, "unit": "tokens/s", "cores": oracle.lib().lo_num_threads(), "kind": "port",
             "sample": f"1 row x {tokens} tokens through one [DeltaNet x3, full] block of the config-5 Q8_0 weights "
                       f"({secs / 8:.2f} s), scaled x8 to the 32-layer model, plus the 26 label logits; CPU "
-                      f"restatement of the reference's Qwen35Model Q8_0 forward"}
+                      f"restatement of the reference's Qwen35Model Q8_0 forward, {products}"}
 
 
 class CpuTrainStep:
@@ -349,7 +359,8 @@ def run_reference(args):
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
                 "data": "synthetic", "config": q8_config(world),
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                 "sample": f"{rows} x {SEQ} tokens per step, CPU restatement of the reference path"},
+                                 "sample": f"{rows} x {SEQ} tokens per step, CPU restatement of the reference path; "
+                                           f"{cpu_products()}"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return

@@ -23,14 +23,84 @@ CFLAGS = ["-O3", "-fPIC", "-shared", "-fopenmp", "-mavx2", "-mfma", "-ffp-contra
           "-std=c11", "-Wall"]
 
 
+# The AVX-512 restatements of the reference's panel kernels (laya_vnni.c), for the timed CPU baseline only.
+VNNI_PATH = os.path.join(HERE, "liblaya_vnni.so")
+VNNI_SRC = os.path.join(HERE, "laya_vnni.c")
+VNNI_CFLAGS = ["-O3", "-fPIC", "-shared", "-fopenmp", "-mavx512f", "-mavx512bw", "-mavx512vnni", "-ffp-contract=off",
+               "-std=c11", "-Wall"]
+
+
 def build(force=False):
-    """Compile laya_oracle.c into liblaya_oracle.so (gcc, a few seconds)."""
-    if not force and os.path.exists(LIB_PATH) and os.path.getmtime(LIB_PATH) >= os.path.getmtime(SRC_PATH):
-        return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
-    subprocess.check_call(["gcc", *CFLAGS, SRC_PATH, "-o", tmp, "-lm"])
-    os.replace(tmp, LIB_PATH)
+    """Compile laya_oracle.c into liblaya_oracle.so and laya_vnni.c into liblaya_vnni.so (gcc, a few seconds)."""
+    for src, out, flags in ((SRC_PATH, LIB_PATH, CFLAGS), (VNNI_SRC, VNNI_PATH, VNNI_CFLAGS)):
+        if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(src):
+            continue
+        tmp = out + ".tmp"
+        subprocess.check_call(["gcc", *flags, src, "-o", tmp, "-lm"])
+        os.replace(tmp, out)
     return LIB_PATH
+
+
+_vnni = None
+_FAST = False
+_packed = {}   # id(weight) -> (weight, packed): packed once, as the reference packs at load
+
+
+def vnni_lib():
+    """The AVX-512 VNNI kernels, or None when this CPU lacks them (or the library was not built)."""
+    global _vnni
+    if _vnni is None:
+        if not os.path.exists(VNNI_PATH):
+            build()
+        L = ctypes.CDLL(VNNI_PATH)
+        L.lv_supported.restype = ctypes.c_int
+        L.lv_q8_packed_bytes.restype = ctypes.c_long
+        L.lv_q8_packed_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.lv_q8_pack.argtypes = [_i8p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.lv_q8_matmul.argtypes = [_i8p, _f32p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_void_p]
+        L.lv_f32_packed_floats.restype = ctypes.c_long
+        L.lv_f32_packed_floats.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.lv_f32_pack.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.lv_linear_f32.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_void_p, _f32p, ctypes.c_int]
+        L.lv_attention.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _i32p, _i32p, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_void_p, ctypes.c_void_p, _f32p]
+        _vnni = L if L.lv_supported() else False
+    return _vnni or None
+
+
+def set_fast(enabled=True):
+    """Route q8_matmul, linear_f32 and attention through the AVX-512 kernels (same bits; for timing the CPU
+    baseline).
+    Returns whether the fast path is in use (False when the CPU lacks AVX-512 VNNI)."""
+    global _FAST
+    _FAST = bool(enabled) and vnni_lib() is not None
+    return _FAST
+
+
+def _packed_q8(qw, dw):
+    key = id(qw)
+    hit = _packed.get(key)
+    if hit is not None and hit[0] is qw:
+        return hit[1]
+    N, K = qw.shape
+    buf = np.zeros(vnni_lib().lv_q8_packed_bytes(N, K), np.uint8)
+    vnni_lib().lv_q8_pack(np.ascontiguousarray(qw), f32(dw), N, K, buf.ctypes.data)
+    _packed[key] = (qw, buf)
+    return buf
+
+
+def _packed_f32(w):
+    key = id(w)
+    hit = _packed.get(key)
+    if hit is not None and hit[0] is w:
+        return hit[1]
+    N, K = w.shape
+    buf = np.zeros(vnni_lib().lv_f32_packed_floats(N, K), np.float32)
+    vnni_lib().lv_f32_pack(f32(w), N, K, buf)
+    _packed[key] = (w, buf)
+    return buf
 
 
 _lib = None
@@ -133,6 +203,11 @@ def q8_matmul(qx, dx, qw, dw, bias=None):
     N = qw.shape[0]
     out = np.zeros((rows, N), np.float32)
     b = None if bias is None else f32(bias)
+    if _FAST:
+        scratch = np.empty(rows * K, np.uint8)
+        vnni_lib().lv_q8_matmul(np.ascontiguousarray(qx), f32(dx), rows, _packed_q8(qw, dw).ctypes.data, N, K, _ptr(b),
+                                out, N, scratch.ctypes.data)
+        return out
     lib().lo_q8_matmul(np.ascontiguousarray(qx), f32(dx), rows, np.ascontiguousarray(qw), f32(dw), N, K, _ptr(b),
                        out, N)
     return out
@@ -153,11 +228,14 @@ def q8_block_dots(qx, qw):
 
 def linear_f32(x, w, bias=None):
     x = f32(x)
-    w = f32(w)
     rows, K = x.shape
     N = w.shape[0]
     out = np.zeros((rows, N), np.float32)
     b = None if bias is None else f32(bias)
+    if _FAST:
+        vnni_lib().lv_linear_f32(x, rows, K, _packed_f32(w), N, K, _ptr(b), out, N)
+        return out
+    w = f32(w)
     lib().lo_linear_f32(x, rows, K, w, N, K, _ptr(b), out, N)
     return out
 
@@ -212,6 +290,9 @@ def attention(qkv, hidden, heads, seg_start, seg_len, window=-1, rope=None):
     c = s = None
     if rope is not None:
         c, s = rope
+    if _FAST and (hidden // heads) % 16 == 0:
+        vnni_lib().lv_attention(qkv, hidden, heads, ss, sl, len(ss), int(window), _ptr(c), _ptr(s), out)
+        return out
     lib().lo_attention(qkv, hidden, heads, ss, sl, len(ss), int(window), _ptr(c), _ptr(s), out)
     return out
 
