@@ -10,7 +10,8 @@
 // run as two independent chains on the tensor core, so one tile's softmax overlaps the other's MMAs:
 //   warp 0      TMA producer: Q of A and B once per item, then K and V tiles through a STAGES-deep ring.
 //   warp 1      TMEM owner and MMA issuer (one thread): S_X = Q_X·Kᵀ into TMEM columns [128·X, 128·X + 128)
-//               (M 128, N 128, K 64), O_X += P_X·V into [256 + 64·X, +64) with P_X read from TMEM (the A operand
+//               (M 128, N 128, K 64), O_X += P_X·V into [256 + 128·slot + 64·X, +64) — two O slots alternating by
+//               item, so an item's first P·V need not wait for the previous item's epilogue — with P_X read from TMEM (the A operand
 //               of the P·V MMA), in the order … P·V_A(j), S_A(j + 1), P·V_B(j), S_B(j + 1) ….  P_X(j) lives in the
 //               columns of S_X(j); S_X(j + 1) is issued after P·V_X(j), and MMAs issued by one thread run in order.
 //   warps 2-5   softmax of tile A, warps 6-9 of tile B: one thread per query row holds the row's 128 scores, so the
@@ -202,10 +203,10 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* s_full = bars + 2;        // [2] by tile
     uint64_t* p_full = bars + 4;        // [2]
     uint64_t* o_done = bars + 6;        // [2]
-    uint64_t* o_free = bars + 8;        // [2]
-    uint64_t* kv_full = bars + 10;      // [S]
-    uint64_t* kv_empty = bars + 10 + S; // [S]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10 + 2 * S);
+    uint64_t* o_free = bars + 8;        // [2 tiles][2 O slots]
+    uint64_t* kv_full = bars + 12;      // [S]
+    uint64_t* kv_empty = bars + 12 + S; // [S]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12 + 2 * S);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = warp_id(), lane = lane_id();
@@ -216,7 +217,8 @@ __global__ void __launch_bounds__(320, 1)
             mbar_init(s_full + x, 1);
             mbar_init(p_full + x, 4);
             mbar_init(o_done + x, 1);
-            mbar_init(o_free + x, 4);
+            mbar_init(o_free + 2 * x, 4);
+            mbar_init(o_free + 2 * x + 1, 4);
         }
         for (int s = 0; s < S; ++s) { mbar_init(kv_full + s, 1); mbar_init(kv_empty + s, 1); }
         *abort_flag = 0;
@@ -320,13 +322,15 @@ __global__ void __launch_bounds__(320, 1)
                 auto issue_pv = [&](int x, int j) -> bool {
                     const bool first = j == sp.jlo[x];
                     if (!mbar_wait(p_full + x, pc[x]++ & 1, abort_flag, p.err)) return false;
-                    // the item's first P·V overwrites O_X: the previous item's epilogue must have read it
-                    if (first && !mbar_wait(o_free + x, (oc[x] & 1) ^ 1, abort_flag, p.err)) return false;
+                    // O_X alternates between two TMEM slots by item; the item's first P·V overwrites its slot, which
+                    // the epilogue of the item two back must have read
+                    const uint32_t slot = oc[x] & 1;
+                    if (first && !mbar_wait(o_free + 2 * x + slot, ((oc[x] >> 1) & 1) ^ 1, abort_flag, p.err)) return false;
                     tc_fence_after();
                     const uint32_t g = base + j;
                     const int s = g % S;
                     const uint32_t av = smem_u32(sKV + s * C::NKV * TILE) + TILE, avl = av + 2 * TILE;
-                    const uint32_t tp = tmem + x * BK, tpl = tp + BK / 2, to = tmem + 2 * BK + x * HD;
+                    const uint32_t tp = tmem + x * BK, tpl = tp + BK / 2, to = tmem + 2 * BK + slot * 2 * HD + x * HD;
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
                         mma_ts(to, tp + kk * 8, desc_mn_sw128(av + kk * 2048, TILE), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(320, 1)
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        const uint32_t tS = tmem + lane_off + x * BK, tO = tmem + lane_off + 2 * BK + x * HD;
+        const uint32_t tS = tmem + lane_off + x * BK;
         const bool global = p.window < 0;
         const int W = p.window;
         const float c2 = p.scale * LOG2E;           // scores → log2 units
@@ -377,6 +381,8 @@ __global__ void __launch_bounds__(320, 1)
             const bool qin = q < sp.L;
             const int lo = qin ? (global ? 0 : max(0, q - W)) : -(1 << 30);
             const uint32_t span = qin ? static_cast<uint32_t>((global ? sp.L - 1 : min(sp.L - 1, q + W)) - lo) : 0u;
+            const uint32_t oslot = oc & 1;   // this item's O slot (the MMA thread alternates them the same way)
+            const uint32_t tO = tmem + lane_off + 2 * BK + oslot * 2 * HD + x * HD;
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = sp.jlo[x]; j < sp.jhi[x]; ++j) {
                 ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full + x, sc++ & 1, abort_flag, p.err));
@@ -480,10 +486,10 @@ __global__ void __launch_bounds__(320, 1)
             tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(o));
             tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
             tmem_ld_wait();
-            // O_X is in registers: the next item's first P·V may overwrite it
+            // O_X is in registers: the item two ahead may overwrite this slot
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(o_free + x);
+            if (lane == 0) mbar_arrive(o_free + 2 * x + oslot);
             if (!qin) continue;
             const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
             const size_t tok = static_cast<size_t>(sp.seg0 + q);
