@@ -150,6 +150,62 @@ DEVI void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------ CTA pairs
+// Two CTAs of a cluster (ranks 2k, 2k+1, on the two SMs of one TPC) working one tcgen05 product: the even rank issues
+// the M = 256 MMAs, each CTA holds its 128 rows of A, its half of B's N and its 128 accumulator lanes.
+DEVI uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster arrives and waits (release / acquire at cluster scope).
+DEVI void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of the same shared-memory offset in cluster CTA `rank`.
+DEVI uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+DEVI void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// 2D tiled load into this CTA's own shared memory whose byte count completes on an mbarrier of either CTA of the
+// pair (the even rank's, which the MMA issuer waits on).  No multicast: each CTA loads only its own tiles.
+DEVI void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+        : "memory");
+}
+// One warp of EACH CTA of the pair runs these: the same columns are allocated (freed) in both CTAs' TMEM.
+DEVI void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+DEVI void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+DEVI void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A · Bᵀ, M = 256 over the pair; issued by the even rank only.
+DEVI void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on the mbarrier at a shared::cluster address (this CTA's or the peer's) when the pair MMAs this
+// thread issued so far have completed.
+DEVI void mma_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+
 // 32 lanes × 32 consecutive 32-bit columns: thread i of the warp gets row (lane base + i).
 DEVI void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(

@@ -16,6 +16,8 @@
 //               bias, converts, stages 32 rows × 128 B in shared memory and writes them with one TMA store (or TMA
 //               reduce-add for accumulating outputs: residual streams and parameter gradients).
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -61,6 +63,78 @@ struct KParams {
     const float* bias;
     int* err;
 };
+
+// Drains one warp's share of an accumulator — 32 TMEM lanes (rows gr0..gr0+31) × COLS columns from gc0 — adds the
+// bias, converts, and writes it through a 4 KB staging tile with TMA stores (reduce-adds for EPI_F32_ADD).
+template <int COLS, int EPI>
+DEVI void drain_rows(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, const float* bias, int N, int gc0,
+                     int gr0, int lane) {
+    if constexpr (EPI == EPI_BF16) {
+        // 64 columns per chunk: 64 bf16 = one 128-byte swizzled row per lane
+#pragma unroll 1
+        for (int c = 0; c < COLS / 64; ++c) {
+            uint32_t v0[32], v1[32];
+            tmem_ld32(tbase + c * 64, v0);
+            tmem_ld32(tbase + c * 64 + 32, v1);
+            tmem_ld_wait();
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                uint32_t w[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int j = q * 8 + 2 * t;
+                    float lo = __uint_as_float(j < 32 ? v0[j] : v1[j - 32]);
+                    float hi = __uint_as_float(j + 1 < 32 ? v0[j + 1] : v1[j + 1 - 32]);
+                    if (bias) {
+                        const int col = gc0 + c * 64 + j;
+                        lo += col < N ? __ldg(bias + col) : 0.0f;
+                        hi += col + 1 < N ? __ldg(bias + col + 1) : 0.0f;
+                    }
+                    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+                    w[t] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) { tma_store_2d(tmOut, gc0 + c * 64, gr0, stage); bulk_commit(); }
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < COLS / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c * 32, v);
+            tmem_ld_wait();
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4 f;
+                float* fp = &f.x;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int j = q * 4 + t;
+                    float x = __uint_as_float(v[j]);
+                    if (bias) {
+                        const int col = gc0 + c * 32 + j;
+                        x += col < N ? __ldg(bias + col) : 0.0f;
+                    }
+                    fp[t] = x;
+                }
+                *reinterpret_cast<float4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = f;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (EPI == EPI_F32_ADD) tma_reduce_add_2d(tmOut, gc0 + c * 32, gr0, stage);
+                else tma_store_2d(tmOut, gc0 + c * 32, gr0, stage);
+                bulk_commit();
+            }
+        }
+    }
+}
 
 template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
@@ -187,71 +261,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
             const int gc0 = n0 + half * COLS;
             const int gr0 = m0 + quarter * 32;
-            if constexpr (EPI == EPI_BF16) {
-                // 64 columns per chunk: 64 bf16 = one 128-byte swizzled row per lane
-#pragma unroll 1
-                for (int c = 0; c < COLS / 64; ++c) {
-                    uint32_t v0[32], v1[32];
-                    tmem_ld32(tbase + c * 64, v0);
-                    tmem_ld32(tbase + c * 64 + 32, v1);
-                    tmem_ld_wait();
-                    if (lane == 0) bulk_wait_read_all();
-                    __syncwarp();
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int j = q * 8 + 2 * t;
-                            float lo = __uint_as_float(j < 32 ? v0[j] : v1[j - 32]);
-                            float hi = __uint_as_float(j + 1 < 32 ? v0[j + 1] : v1[j + 1 - 32]);
-                            if (bias) {
-                                const int col = gc0 + c * 64 + j;
-                                lo += col < p.N ? __ldg(bias + col) : 0.0f;
-                                hi += col + 1 < p.N ? __ldg(bias + col + 1) : 0.0f;
-                            }
-                            __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-                            w[t] = *reinterpret_cast<uint32_t*>(&h);
-                        }
-                        *reinterpret_cast<uint4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) { tma_store_2d(&tmOut, gc0 + c * 64, gr0, stage); bulk_commit(); }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < COLS / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(tbase + c * 32, v);
-                    tmem_ld_wait();
-                    if (lane == 0) bulk_wait_read_all();
-                    __syncwarp();
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        float4 f;
-                        float* fp = &f.x;
-#pragma unroll
-                        for (int t = 0; t < 4; ++t) {
-                            const int j = q * 4 + t;
-                            float x = __uint_as_float(v[j]);
-                            if (bias) {
-                                const int col = gc0 + c * 32 + j;
-                                x += col < p.N ? __ldg(bias + col) : 0.0f;
-                            }
-                            fp[t] = x;
-                        }
-                        *reinterpret_cast<float4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = f;
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if constexpr (EPI == EPI_F32_ADD) tma_reduce_add_2d(&tmOut, gc0 + c * 32, gr0, stage);
-                        else tma_store_2d(&tmOut, gc0 + c * 32, gr0, stage);
-                        bulk_commit();
-                    }
-                }
-            }
+            drain_rows<COLS, EPI>(tbase, stage, &tmOut, bias, p.N, gc0, gr0, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty + buf);
@@ -264,6 +274,189 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ CTA-pair form
+// Output tiles of 256 × 256 over a cluster of two CTAs (the SM pair of one TPC). Each CTA loads its own 128 rows of
+// A and its own 128 rows of B's N per stage — 32 KB instead of the 48 KB a one-CTA 128 × 256 tile loads for the same
+// MMA work, so shared-memory fill and L2 → SM traffic per flop drop by a third — and the even rank issues
+// tcgen05.mma.cta_group::2 (M = 256, N = 256) reading both CTAs' stages. Each CTA's TMEM holds its 128 rows of the
+// accumulator (two buffers of 256 columns) and its own epilogue warps drain them exactly as in the one-CTA kernel.
+//   full[s]   even rank only: its producer arms it with both CTAs' bytes; both CTAs' loads complete on it.
+//   empty[s]  in both CTAs: the MMA issuer commits to its own and to the peer's when a stage is consumed.
+//   tfull[b]  in both CTAs: committed likewise when an accumulator buffer is complete.
+//   tempty[b] even rank only: all 16 epilogue warps of the pair arrive when a buffer is drained.
+// No load is multicast; the pair exchanges only mbarrier arrivals and the MMA's own operand traffic.
+constexpr int PAIR_BN = 256;
+
+template <int STAGES>
+struct PairCfg {
+    static constexpr int A_BYTES = BM * BK * 2;                  // this CTA's 128 rows of A
+    static constexpr int B_BYTES = (PAIR_BN / 2) * BK * 2;       // this CTA's 128 rows of B
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGE_OUT = 4096;
+    static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_WARPS * STAGE_OUT + BAR_BYTES;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+template <int STAGES, int A_MN, int B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THREADS, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                          const __grid_constant__ CUtensorMap tmOut, KParams p) {
+    using C = PairCfg<STAGES>;
+    constexpr int BN = PAIR_BN;
+    constexpr uint32_t IDESC = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, 2 * BM, BN) |
+                               (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
+    extern __shared__ uint8_t smem_raw[];
+    // both CTAs run the same code on the same dynamic-shared-memory base, so every buffer sits at the same offset in
+    // both: the MMA's descriptors and the mapa'd barrier addresses rely on it
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * C::STAGE_OUT);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = warp_id(), lane = lane_id();
+    const uint32_t rank = cluster_rank();          // 0: issues the MMAs; 1: its peer
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int kblocks = (p.K + BK - 1) / BK;
+    const int kchunk = (kblocks + p.ksplit - 1) / p.ksplit;
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_n * ((p.M + 2 * BM - 1) / (2 * BM)) * p.ksplit;
+    auto unit_k = [&](int u, int& kb0, int& nkb) {
+        kb0 = (u % p.ksplit) * kchunk;
+        nkb = min(kchunk, kblocks - kb0);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(tfull + b, 1); mbar_init(tempty + b, 2 * EPI_WARPS); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc_pair(tmem_slot, 512); tmem_relinquish_pair(); }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA); prefetch_tmap(&tmB); prefetch_tmap(&tmOut);
+        if (p.splits > 1) { prefetch_tmap(&tmA2); prefetch_tmap(&tmB2); }
+    }
+    // barriers initialised in both CTAs before either side arrives on, or loads into, the other's
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full0 = cluster_addr(full, 0);    // the even rank's full barriers
+            uint32_t g = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += npairs) {
+                const int ot = tile / p.ksplit;
+                const int m0 = (ot / tiles_n) * (2 * BM) + static_cast<int>(rank) * BM;
+                const int n0 = (ot % tiles_n) * BN + static_cast<int>(rank) * (BN / 2);
+                int kb0, nkb;
+                unit_k(tile, kb0, nkb);
+                const int iters = nkb * p.splits;
+                for (int it = 0; it < iters; ++it, ++g) {
+                    const int s = g % STAGES;
+                    const int seg = it / nkb, kb = kb0 + it - seg * nkb;
+                    const CUtensorMap* mA = seg == 1 ? &tmA2 : &tmA;
+                    const CUtensorMap* mB = seg == 2 ? &tmB2 : &tmB;
+                    if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * C::STAGE_BYTES);
+                    const uint32_t bar = full0 + 8u * static_cast<uint32_t>(s);
+                    uint8_t* a = sA + s * C::A_BYTES;
+                    uint8_t* b = sB + s * C::B_BYTES;
+                    if constexpr (A_MN) {
+#pragma unroll
+                        for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a + j * (BK * 128), mA, bar, m0 + 64 * j, kb * BK);
+                    } else {
+                        tma_load_2d_pair(a, mA, bar, kb * BK, m0);
+                    }
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 2 / 64; ++j) tma_load_2d_pair(b + j * (BK * 128), mB, bar, n0 + 64 * j, kb * BK);
+                    } else {
+                        tma_load_2d_pair(b, mB, bar, kb * BK, n0);
+                    }
+                }
+            }
+            // every stage's last use released before this CTA may exit (the issuer's commits land in this CTA)
+            for (int i = 0; i < STAGES && ok; ++i, ++g)
+                if (!mbar_wait(empty + g % STAGES, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) ok = false;
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            const uint32_t empty1 = cluster_addr(empty, 1), tfull1 = cluster_addr(tfull, 1);
+            uint32_t g = 0, ti = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += npairs, ++ti) {
+                const int buf = ti & 1;
+                if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+                tc_fence_after();
+                int kb0, nkb;
+                unit_k(tile, kb0, nkb);
+                const int iters = nkb * p.splits;
+                for (int kb = 0; kb < iters; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(sA + s * C::A_BYTES), b = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = A_MN ? smem_desc_mn_sw128(a + kk * 2048, BK * 128) : smem_desc_sw128(a + kk * 32);
+                        const uint64_t bd = B_MN ? smem_desc_mn_sw128(b + kk * 2048, BK * 128) : smem_desc_sw128(b + kk * 32);
+                        mma_f16_pair(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit_pair(smem_u32(empty + s));
+                    mma_commit_pair(empty1 + 8u * static_cast<uint32_t>(s));
+                }
+                mma_commit_pair(smem_u32(tfull + buf));
+                mma_commit_pair(tfull1 + 8u * static_cast<uint32_t>(buf));
+            }
+            // both buffers drained by both CTAs' epilogues before the accumulators are freed
+            for (int i = 0; i < 2 && ok; ++i, ++ti)
+                if (!mbar_wait(tempty + (ti & 1), ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) ok = false;
+        }
+    } else {
+        const int e = warp - 2;
+        const int quarter = warp & 3;
+        const int half = e >> 2;
+        constexpr int COLS = BN / 2;
+        uint8_t* stage = sOut + e * C::STAGE_OUT;
+        const uint32_t tempty0 = cluster_addr(tempty, 0);
+        uint32_t ti = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++ti) {
+            const int buf = ti & 1;
+            const int ot = tile / p.ksplit;
+            const int m0 = (ot / tiles_n) * (2 * BM) + static_cast<int>(rank) * BM, n0 = (ot % tiles_n) * BN;
+            const float* bias = tile % p.ksplit == 0 ? p.bias : nullptr;
+            if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
+            drain_rows<COLS, EPI>(tbase, stage, &tmOut, bias, p.N, n0 + half * COLS, m0 + quarter * 32, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * static_cast<uint32_t>(buf));
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    // neither CTA leaves while the other may still arrive on its barriers or read its stages
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
     }
 }
 
@@ -313,12 +506,86 @@ static int launch(const Args& a, cudaStream_t stream) {
     return OK;
 }
 
+// The pair kernel's launch: grid = 2 × (pairs resident at once, at most the work units), 74 pairs on 148 SMs.
+template <int STAGES, int A_MN, int B_MN, int EPI>
+static int launch_pair(const Args& a, cudaStream_t stream) {
+    using C = PairCfg<STAGES>;
+    CUtensorMap tA, tB, tA2, tB2, tO;
+    const int splits = a.A2 ? (a.B2 ? 3 : 2) : 1;
+    const bool split = splits > 1;
+    auto map_a = [&](CUtensorMap* m, const void* ptr) {
+        if (A_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
+        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
+    };
+    auto map_b = [&](CUtensorMap* m, const void* ptr) {   // each CTA loads 128 of the tile's 256 B rows
+        if (B_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, static_cast<uint64_t>(a.ldb) * 2, BK, 64);
+        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, PAIR_BN / 2, BK);
+    };
+    int rc = map_a(&tA, a.A);
+    if (!rc) rc = map_b(&tB, a.B);
+    if (!rc) rc = map_a(&tA2, split ? a.A2 : a.A);
+    if (!rc) rc = map_b(&tB2, splits == 3 ? a.B2 : a.B);
+    if (!rc) {
+        if (EPI == EPI_BF16)
+            rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
+        else
+            rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
+    }
+    if (rc) return rc;
+    auto kern = gemm_bf16_pair_kernel<STAGES, A_MN, B_MN, EPI>;
+    int dev = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    static DeviceOnce attr;
+    static std::atomic<int> resident[64];   // pairs resident at once, per device
+    int pairs = dev >= 0 && dev < 64 ? resident[dev].load(std::memory_order_relaxed) : 0;
+    if (!attr.done(dev) || pairs <= 0) {
+        LAYA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        int nsm = 0;
+        if (int e = sm_count(dev, &nsm)) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(nsm & ~1);
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
+        LAYA_CUDA(cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg));
+        if (pairs <= 0) { set_error("the bf16 pair product cannot place a cluster of two CTAs"); return ERR_CUDA; }
+        pairs = std::min(pairs, nsm / 2);
+        if (dev >= 0 && dev < 64) resident[dev].store(pairs, std::memory_order_relaxed);
+        attr.mark(dev);
+    }
+    const int tiles = ((a.N + PAIR_BN - 1) / PAIR_BN) * ((a.M + 2 * BM - 1) / (2 * BM));
+    const int ksplit = EPI == EPI_F32_ADD && a.ksplit_ok ? choose_ksplit(tiles, (a.K + BK - 1) / BK, pairs) : 1;
+    const int units = tiles * ksplit;
+    KParams p{a.M, a.N, a.K, splits, ksplit, a.bias, a.err};
+    kern<<<2 * std::min(units, pairs), C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tO, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+template <int STAGES, int EPI>
+static int dispatch_pair(const Args& a, cudaStream_t s) {
+    if (!a.a_mn && !a.b_mn) return launch_pair<STAGES, 0, 0, EPI>(a, s);
+    if (!a.a_mn && a.b_mn) return launch_pair<STAGES, 0, 1, EPI>(a, s);
+    if (a.a_mn && a.b_mn) return launch_pair<STAGES, 1, 1, EPI>(a, s);
+    return launch_pair<STAGES, 1, 0, EPI>(a, s);
+}
+
 template <int BN, int STAGES, int EPI>
 static int dispatch_major(const Args& a, cudaStream_t s) {
     if (!a.a_mn && !a.b_mn) return launch<BN, STAGES, 0, 0, EPI>(a, s);
     if (!a.a_mn && a.b_mn) return launch<BN, STAGES, 0, 1, EPI>(a, s);
     if (a.a_mn && a.b_mn) return launch<BN, STAGES, 1, 1, EPI>(a, s);
     return launch<BN, STAGES, 1, 0, EPI>(a, s);
+}
+
+// Products with N > 128 and more than one 128-row tile run on CTA pairs unless LAYA_GEMM_PAIR=0 is set in the
+// environment (read once), which keeps the one-CTA 128 × 256 kernel: a diagnostic for comparing the two forms.
+static bool pair_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("LAYA_GEMM_PAIR");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 int gemm(const Args& a, cudaStream_t stream) {
@@ -336,6 +603,12 @@ int gemm(const Args& a, cudaStream_t stream) {
             case EPI_BF16: return dispatch_major<128, 4, EPI_BF16>(a, stream);
             case EPI_F32: return dispatch_major<128, 4, EPI_F32>(a, stream);
             case EPI_F32_ADD: return dispatch_major<128, 4, EPI_F32_ADD>(a, stream);
+        }
+    } else if (a.M > BM && pair_enabled()) {
+        switch (a.epi) {
+            case EPI_BF16: return dispatch_pair<6, EPI_BF16>(a, stream);
+            case EPI_F32: return dispatch_pair<6, EPI_F32>(a, stream);
+            case EPI_F32_ADD: return dispatch_pair<6, EPI_F32_ADD>(a, stream);
         }
     } else {
         switch (a.epi) {
