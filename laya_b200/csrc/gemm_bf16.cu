@@ -64,15 +64,16 @@ struct KParams {
     int* err;
 };
 
-// Drains one warp's share of an accumulator — 32 TMEM lanes (rows gr0..gr0+31) × COLS columns from gc0 — adds the
-// bias, converts, and writes it through a 4 KB staging tile with TMA stores (reduce-adds for EPI_F32_ADD).
-template <int COLS, int EPI>
+// Drains one warp's share of an accumulator — 32 TMEM lanes (rows gr0..gr0+31) × cols columns from gc0, cols a
+// multiple of 64 — adds the bias, converts, and writes it through a 4 KB staging tile with TMA stores (reduce-adds for
+// EPI_F32_ADD).
+template <int EPI>
 DEVI void drain_rows(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, const float* bias, int N, int gc0,
-                     int gr0, int lane) {
+                     int gr0, int lane, int cols) {
     if constexpr (EPI == EPI_BF16) {
         // 64 columns per chunk: 64 bf16 = one 128-byte swizzled row per lane
 #pragma unroll 1
-        for (int c = 0; c < COLS / 64; ++c) {
+        for (int c = 0; c < cols / 64; ++c) {
             uint32_t v0[32], v1[32];
             tmem_ld32(tbase + c * 64, v0);
             tmem_ld32(tbase + c * 64 + 32, v1);
@@ -103,7 +104,7 @@ DEVI void drain_rows(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, c
         }
     } else {
 #pragma unroll 1
-        for (int c = 0; c < COLS / 32; ++c) {
+        for (int c = 0; c < cols / 32; ++c) {
             uint32_t v[32];
             tmem_ld32(tbase + c * 32, v);
             tmem_ld_wait();
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
             const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
             const int gc0 = n0 + half * COLS;
             const int gr0 = m0 + quarter * 32;
-            drain_rows<COLS, EPI>(tbase, stage, &tmOut, bias, p.N, gc0, gr0, lane);
+            drain_rows<EPI>(tbase, stage, &tmOut, bias, p.N, gc0, gr0, lane, COLS);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty + buf);
@@ -288,12 +289,17 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
 //   tfull[b]  in both CTAs: committed likewise when an accumulator buffer is complete.
 //   tempty[b] even rank only: all 16 epilogue warps of the pair arrive when a buffer is drained.
 // No load is multicast; the pair exchanges only mbarrier arrivals and the MMA's own operand traffic.
+//
+// Narrow units (256 × 128, N = 128 per MMA, 64 B rows per CTA): the last tile column when N mod 256 is in (0, 128],
+// so no MMA work is spent past N, and every tile of a last partial round of tiles when that round holds at most half
+// the pairs — split in two along N, it ends in half the time (240 tiles of N = 768 on 74 pairs: 3 full rounds and 18
+// tiles, which become 36 narrow units).
 constexpr int PAIR_BN = 256;
 
 template <int STAGES>
 struct PairCfg {
     static constexpr int A_BYTES = BM * BK * 2;                  // this CTA's 128 rows of A
-    static constexpr int B_BYTES = (PAIR_BN / 2) * BK * 2;       // this CTA's 128 rows of B
+    static constexpr int B_BYTES = (PAIR_BN / 2) * BK * 2;       // this CTA's 128 rows of B (64 for a narrow unit)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_OUT = 4096;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
@@ -302,15 +308,55 @@ struct PairCfg {
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
+struct PairParams {
+    KParams k;
+    int units;        // work units walked by the pairs
+    int split_from;   // units from here on are the halves of tiles split along N (split_from + 2·(tiles − split_from))
+};
+
+// One work unit of the pair kernel: output rows [m0, m0 + 256), columns [n0, n0 + (wide ? 256 : 128)), k-blocks
+// [kb0, kb0 + nkb); skip for the empty second half of a tile that was narrow already.
+struct PairUnit {
+    int m0, n0, kb0, nkb;
+    bool wide, first, skip;
+};
+
+DEVI PairUnit pair_unit(const PairParams& pp, int u, int tiles_n, int kchunk, int kblocks) {
+    const KParams& p = pp.k;
+    int tile = u, half = -1;
+    if (u >= pp.split_from) {
+        tile = pp.split_from + ((u - pp.split_from) >> 1);
+        half = (u - pp.split_from) & 1;
+    }
+    const int ot = tile / p.ksplit;
+    const int nt = ot % tiles_n;
+    PairUnit r;
+    r.m0 = (ot / tiles_n) * (2 * BM);
+    r.n0 = nt * PAIR_BN;
+    r.wide = !(nt == tiles_n - 1 && p.N - r.n0 <= PAIR_BN / 2);
+    r.skip = false;
+    if (half >= 0) {
+        if (r.wide) { r.n0 += (PAIR_BN / 2) * half; r.wide = false; }
+        else r.skip = half == 1;
+    }
+    r.kb0 = (tile % p.ksplit) * kchunk;
+    r.nkb = min(kchunk, kblocks - r.kb0);
+    r.first = tile % p.ksplit == 0;
+    return r;
+}
+
 template <int STAGES, int A_MN, int B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THREADS, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                          const __grid_constant__ CUtensorMap tmOut, KParams p) {
+                          const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmB2n,
+                          const __grid_constant__ CUtensorMap tmOut, PairParams pp) {
     using C = PairCfg<STAGES>;
     constexpr int BN = PAIR_BN;
-    constexpr uint32_t IDESC = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, 2 * BM, BN) |
-                               (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
+    constexpr uint32_t IDESC_BASE = (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
+    constexpr uint32_t IDESC_WIDE = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, 2 * BM, BN) | IDESC_BASE;
+    constexpr uint32_t IDESC_NARROW = make_idesc(1, 1, 1, 2 * BM, BN / 2) | IDESC_BASE;
+    const KParams& p = pp.k;
     extern __shared__ uint8_t smem_raw[];
     // both CTAs run the same code on the same dynamic-shared-memory base, so every buffer sits at the same offset in
     // both: the MMA's descriptors and the mapa'd barrier addresses rely on it
@@ -331,11 +377,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
     const int kblocks = (p.K + BK - 1) / BK;
     const int kchunk = (kblocks + p.ksplit - 1) / p.ksplit;
     const int tiles_n = (p.N + BN - 1) / BN;
-    const int tiles = tiles_n * ((p.M + 2 * BM - 1) / (2 * BM)) * p.ksplit;
-    auto unit_k = [&](int u, int& kb0, int& nkb) {
-        kb0 = (u % p.ksplit) * kchunk;
-        nkb = min(kchunk, kblocks - kb0);
-    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
@@ -359,20 +400,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
             const uint32_t full0 = cluster_addr(full, 0);    // the even rank's full barriers
             uint32_t g = 0;
             bool ok = true;
-            for (int tile = pair; tile < tiles && ok; tile += npairs) {
-                const int ot = tile / p.ksplit;
-                const int m0 = (ot / tiles_n) * (2 * BM) + static_cast<int>(rank) * BM;
-                const int n0 = (ot % tiles_n) * BN + static_cast<int>(rank) * (BN / 2);
-                int kb0, nkb;
-                unit_k(tile, kb0, nkb);
-                const int iters = nkb * p.splits;
+            for (int u = pair; u < pp.units && ok; u += npairs) {
+                const PairUnit w = pair_unit(pp, u, tiles_n, kchunk, kblocks);
+                if (w.skip) continue;
+                const int bn = w.wide ? BN / 2 : BN / 4;     // B rows (N) this CTA loads
+                const int m0 = w.m0 + static_cast<int>(rank) * BM;
+                const int n0 = w.n0 + static_cast<int>(rank) * bn;
+                const uint32_t bytes = 2u * static_cast<uint32_t>(C::A_BYTES + bn * BK * 2);
+                const int iters = w.nkb * p.splits;
                 for (int it = 0; it < iters; ++it, ++g) {
                     const int s = g % STAGES;
-                    const int seg = it / nkb, kb = kb0 + it - seg * nkb;
+                    const int seg = it / w.nkb, kb = w.kb0 + it - seg * w.nkb;
                     const CUtensorMap* mA = seg == 1 ? &tmA2 : &tmA;
-                    const CUtensorMap* mB = seg == 2 ? &tmB2 : &tmB;
+                    const CUtensorMap* mB = seg == 2 ? (w.wide || B_MN ? &tmB2 : &tmB2n) : (w.wide || B_MN ? &tmB : &tmBn);
                     if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
-                    if (rank == 0) mbar_arrive_expect_tx(full + s, 2 * C::STAGE_BYTES);
+                    if (rank == 0) mbar_arrive_expect_tx(full + s, bytes);
                     const uint32_t bar = full0 + 8u * static_cast<uint32_t>(s);
                     uint8_t* a = sA + s * C::A_BYTES;
                     uint8_t* b = sB + s * C::B_BYTES;
@@ -383,8 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
                         tma_load_2d_pair(a, mA, bar, kb * BK, m0);
                     }
                     if constexpr (B_MN) {
-#pragma unroll
-                        for (int j = 0; j < BN / 2 / 64; ++j) tma_load_2d_pair(b + j * (BK * 128), mB, bar, n0 + 64 * j, kb * BK);
+                        for (int j = 0; j < bn / 64; ++j) tma_load_2d_pair(b + j * (BK * 128), mB, bar, n0 + 64 * j, kb * BK);
                     } else {
                         tma_load_2d_pair(b, mB, bar, kb * BK, n0);
                     }
@@ -399,13 +440,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
             const uint32_t empty1 = cluster_addr(empty, 1), tfull1 = cluster_addr(tfull, 1);
             uint32_t g = 0, ti = 0;
             bool ok = true;
-            for (int tile = pair; tile < tiles && ok; tile += npairs, ++ti) {
+            for (int u = pair; u < pp.units && ok; u += npairs) {
+                const PairUnit w = pair_unit(pp, u, tiles_n, kchunk, kblocks);
+                if (w.skip) continue;
+                const uint32_t idesc = w.wide ? IDESC_WIDE : IDESC_NARROW;
                 const int buf = ti & 1;
                 if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();
-                int kb0, nkb;
-                unit_k(tile, kb0, nkb);
-                const int iters = nkb * p.splits;
+                const int iters = w.nkb * p.splits;
                 for (int kb = 0; kb < iters; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
@@ -415,13 +457,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t ad = A_MN ? smem_desc_mn_sw128(a + kk * 2048, BK * 128) : smem_desc_sw128(a + kk * 32);
                         const uint64_t bd = B_MN ? smem_desc_mn_sw128(b + kk * 2048, BK * 128) : smem_desc_sw128(b + kk * 32);
-                        mma_f16_pair(tmem + static_cast<uint32_t>(buf * BN), ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        mma_f16_pair(tmem + static_cast<uint32_t>(buf * BN), ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     mma_commit_pair(smem_u32(empty + s));
                     mma_commit_pair(empty1 + 8u * static_cast<uint32_t>(s));
                 }
                 mma_commit_pair(smem_u32(tfull + buf));
                 mma_commit_pair(tfull1 + 8u * static_cast<uint32_t>(buf));
+                ++ti;
             }
             // both buffers drained by both CTAs' epilogues before the accumulators are freed
             for (int i = 0; i < 2 && ok; ++i, ++ti)
@@ -431,22 +474,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
         const int e = warp - 2;
         const int quarter = warp & 3;
         const int half = e >> 2;
-        constexpr int COLS = BN / 2;
         uint8_t* stage = sOut + e * C::STAGE_OUT;
         const uint32_t tempty0 = cluster_addr(tempty, 0);
         uint32_t ti = 0;
-        for (int tile = pair; tile < tiles; tile += npairs, ++ti) {
+        for (int u = pair; u < pp.units; u += npairs) {
+            const PairUnit w = pair_unit(pp, u, tiles_n, kchunk, kblocks);
+            if (w.skip) continue;
+            const int cols = w.wide ? BN / 2 : BN / 4;     // this warp's columns of the unit
             const int buf = ti & 1;
-            const int ot = tile / p.ksplit;
-            const int m0 = (ot / tiles_n) * (2 * BM) + static_cast<int>(rank) * BM, n0 = (ot % tiles_n) * BN;
-            const float* bias = tile % p.ksplit == 0 ? p.bias : nullptr;
+            const int m0 = w.m0 + static_cast<int>(rank) * BM;
             if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * COLS);
-            drain_rows<COLS, EPI>(tbase, stage, &tmOut, bias, p.N, n0 + half * COLS, m0 + quarter * 32, lane);
+            const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * cols);
+            drain_rows<EPI>(tbase, stage, &tmOut, w.first ? p.bias : nullptr, p.N, w.n0 + half * cols, m0 + quarter * 32,
+                            lane, cols);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * static_cast<uint32_t>(buf));
+            ++ti;
         }
         if (lane == 0) bulk_wait_all();
     }
@@ -510,21 +555,26 @@ static int launch(const Args& a, cudaStream_t stream) {
 template <int STAGES, int A_MN, int B_MN, int EPI>
 static int launch_pair(const Args& a, cudaStream_t stream) {
     using C = PairCfg<STAGES>;
-    CUtensorMap tA, tB, tA2, tB2, tO;
+    CUtensorMap tA, tB, tA2, tB2, tBn, tB2n, tO;
     const int splits = a.A2 ? (a.B2 ? 3 : 2) : 1;
     const bool split = splits > 1;
     auto map_a = [&](CUtensorMap* m, const void* ptr) {
         if (A_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.M, static_cast<uint64_t>(a.lda) * 2, BK, 64);
         return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.K, static_cast<uint64_t>(a.lda) * 2, BM, BK);
     };
-    auto map_b = [&](CUtensorMap* m, const void* ptr) {   // each CTA loads 128 of the tile's 256 B rows
+    // each CTA loads `rows` of the unit's B rows: 128 of a 256-wide unit, 64 of a narrow one (an N-contiguous B is
+    // loaded as 64-column boxes either way)
+    auto map_b = [&](CUtensorMap* m, const void* ptr, uint32_t rows) {
         if (B_MN) return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.N, static_cast<uint64_t>(a.ldb) * 2, BK, 64);
-        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, PAIR_BN / 2, BK);
+        return make_tmap_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, static_cast<uint64_t>(a.ldb) * 2, rows, BK);
     };
+    const void* b2 = splits == 3 ? a.B2 : a.B;
     int rc = map_a(&tA, a.A);
-    if (!rc) rc = map_b(&tB, a.B);
+    if (!rc) rc = map_b(&tB, a.B, PAIR_BN / 2);
     if (!rc) rc = map_a(&tA2, split ? a.A2 : a.A);
-    if (!rc) rc = map_b(&tB2, splits == 3 ? a.B2 : a.B);
+    if (!rc) rc = map_b(&tB2, b2, PAIR_BN / 2);
+    if (!rc) rc = map_b(&tBn, a.B, PAIR_BN / 4);
+    if (!rc) rc = map_b(&tB2n, b2, PAIR_BN / 4);
     if (!rc) {
         if (EPI == EPI_BF16)
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
@@ -554,9 +604,13 @@ static int launch_pair(const Args& a, cudaStream_t stream) {
     }
     const int tiles = ((a.N + PAIR_BN - 1) / PAIR_BN) * ((a.M + 2 * BM - 1) / (2 * BM));
     const int ksplit = EPI == EPI_F32_ADD && a.ksplit_ok ? choose_ksplit(tiles, (a.K + BK - 1) / BK, pairs) : 1;
-    const int units = tiles * ksplit;
-    KParams p{a.M, a.N, a.K, splits, ksplit, a.bias, a.err};
-    kern<<<2 * std::min(units, pairs), C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tO, p);
+    PairParams pp{KParams{a.M, a.N, a.K, splits, ksplit, a.bias, a.err}, tiles * ksplit, tiles * ksplit};
+    const int rem = tiles % pairs;
+    if (ksplit == 1 && rem > 0 && 2 * rem <= pairs) {   // the last partial round, split along N
+        pp.split_from = tiles - rem;
+        pp.units = pp.split_from + 2 * rem;
+    }
+    kern<<<2 * std::min(pp.units, pairs), C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tBn, tB2n, tO, pp);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;

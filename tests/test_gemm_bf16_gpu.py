@@ -10,7 +10,11 @@ from conftest import max_rel
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(1000, 2304, 768), (304, 768, 1152), (72, 96, 128), (136, 200, 72), (4096, 1152, 768)]
+# CTA-pair tilings: (1000, 2304) every tile split along N (36 tiles, 74 pairs); (4096, 1152) a narrow last column and
+# a split last round; (20480, 768) three full rounds and a split fourth; (2304, 1152, 4096) a narrow last column with
+# the K split of accumulating outputs; (72, 96) and (136, 200) the one-CTA kernels and a single pair tile.
+SHAPES = [(1000, 2304, 768), (304, 768, 1152), (72, 96, 128), (136, 200, 72), (4096, 1152, 768), (20480, 768, 256),
+          (2304, 1152, 4096)]
 LAYOUTS = [(0, 0), (0, 1), (1, 1)]
 
 
