@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--workload", default="all", choices=["all", "train", "q8", "f32", "decoder"])
     ap.add_argument("--dec-tokens", type=int, default=128, help="tokens of the decoder's CPU sample")
     ap.add_argument("--dec-layers", type=int, default=32, help="decoder layers (fewer only for small captures)")
+    ap.add_argument("--delta-rule", default="chunked", choices=["chunked", "per-token"],
+                    help="decoder prefill: the delta rule in 64-token tensor-core chunks (default) or the per-token "
+                         "sweep in the reference's floating-point order")
     ap.add_argument("--forward", default="accurate", choices=["accurate", "bf16"],
                     help="forward mode of the headline training step")
     ap.add_argument("--no-bf16-forward", action="store_true", help="skip the extra BF16-forward measurement")
@@ -721,6 +724,7 @@ def dec_measure(args, d):
     lens = [len(s) for s in seqs]
     stream = torch.cuda.Stream()
     model.set_stream(stream.cuda_stream)
+    model.set_chunked_delta_rule(args.delta_rule == "chunked")
     ids_dev = torch.from_numpy(ids).cuda()
     hidden = torch.zeros((DEC_ROWS, 2560), dtype=torch.float32, device="cuda")
     logits = torch.zeros((DEC_ROWS, DEC_LABELS), dtype=torch.float32, device="cuda")
@@ -959,8 +963,11 @@ def run_ours(args):
                              "frac": achieved / i8_peak, "peak_source": I8_SOURCE,
                              "traffic": traffic.get("q8_gemm_dec", {}).get("dram_bytes_per_launch"), "launches": g_n,
                              "share_of_step": g_ms / args.steps / ms},
-                "delta_rule": {"kernel": "delta_rule_kernel (sequential gated delta rule, one CTA per sequence x "
-                                         "value head)", "ms_per_step": r_ms / args.steps,
+                "delta_rule": {"kernel": "delta_chunk_kernel (gated delta rule in 64-token chunks, tcgen05 "
+                                         "fp32-accurate products, one CTA per sequence x value head)"
+                                         if args.delta_rule == "chunked" else
+                                         "delta_rule_kernel (per-token sweep, one CTA per sequence x value head)",
+                               "ms_per_step": r_ms / args.steps,
                                "share_of_step": r_ms / args.steps / ms,
                                "gflops": r_ops / (r_ms / 1e3) / 1e9 if r_ms else None},
                 "attention": {"kernel": "attn_prep + attention_kernel (fp16 mma.sync, causal GQA, sigmoid gate)",

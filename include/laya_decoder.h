@@ -147,6 +147,15 @@ int laya_decoder_forward_states(laya_decoder* dec, const int32_t* ids, const int
                                 laya_decoder_state** snapshots, const int32_t* label_ids, int n_labels, float* hidden,
                                 float* logits);
 
+/* How the DeltaNet layers' delta rule runs for reads without a decoder state (laya_decoder_forward,
+ * laya_decoder_layer): 0 (the default) the per-token sweep, bit-identical to DecoderKernels.GatedDeltaRule128
+ * (DecoderKernels.cs:151-259), so a stateless read gives the same bits as a read through a state; 1 in 64-token
+ * chunks on the tensor cores where the key and value head dims are 128 — fp32-accurate products, so it agrees with
+ * the sweep to rounding (~1e-5 relative), not bit for bit, and the Q8_0 activation codes downstream may differ.
+ * Reads through states always run the per-token sweep: reading in pieces must give the bits of reading at once
+ * (Qwen35State, Qwen35Model.cs:38-197). */
+int laya_decoder_set_chunked_delta_rule(laya_decoder* dec, int enabled);
+
 /* Recorder of the next forwards (single or several sequences; rows packed): 1 on, 0 off. */
 int laya_decoder_record_enable(laya_decoder* dec, int enabled);
 int laya_decoder_record_get(laya_decoder* dec, const char* name, float* host, int64_t count);

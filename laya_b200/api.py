@@ -156,6 +156,7 @@ _SIGS = {
     "laya_decoder_state_rewind": (_I, [_P, _P]),
     "laya_decoder_mark_destroy": (_I, [_P]),
     "laya_decoder_forward_states": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P]),
+    "laya_decoder_set_chunked_delta_rule": (_I, [_P, _I]),
     "laya_decoder_record_enable": (_I, [_P, _I]),
     "laya_decoder_record_get": (_I, [_P, ctypes.c_char_p, _P, ctypes.c_int64]),
     "laya_decoder_launches": (_I, [_P, ctypes.POINTER(ctypes.c_longlong)]),
@@ -983,6 +984,11 @@ class Qwen35Model:
         mixer = np.zeros_like(x)
         check(lib().laya_decoder_layer(self.handle, i, _np_ptr(x), _np_ptr(lens), len(lens), _np_ptr(mixer)))
         return mixer, x
+
+    def set_chunked_delta_rule(self, enabled: bool):
+        """Stateless reads: the delta rule in 64-token tensor-core chunks (True) or the per-token sweep, bit-identical
+        to the reference's (False, the default).  Reads through states always take the per-token sweep."""
+        check(lib().laya_decoder_set_chunked_delta_rule(self.handle, 1 if enabled else 0))
 
     def record(self, enabled: bool):
         check(lib().laya_decoder_record_enable(self.handle, 1 if enabled else 0))

@@ -158,9 +158,12 @@ struct laya_decoder {
     double prof_ms[3] = {0, 0, 0}, prof_ops[3] = {0, 0, 0};
     long long prof_n[3] = {0, 0, 0};
 
-    // recorder
+    bool chunked_rule = false;   // stateless reads: the delta rule in 64-token chunks where it applies (opt-in)
+
+    // recorder: name → (buffer, capacity in floats, floats of the last copy)
     bool record = false;
-    std::map<std::string, std::pair<float*, size_t>> rec;
+    struct Recorded { float* p = nullptr; size_t cap = 0, count = 0; };
+    std::map<std::string, Recorded> rec;
 
     std::vector<void*> allocs;
 };
@@ -255,13 +258,14 @@ int check_device_error(laya_decoder* c) {
 int record_copy(laya_decoder* c, const std::string& name, const float* src, size_t count) {
     if (!c->record) return OK;
     auto& b = c->rec[name];
-    if (b.second < count) {
-        if (b.first) cudaFree(b.first);
-        b.first = nullptr;
-        LAYA_CUDA(cudaMalloc(&b.first, count * sizeof(float)));
-        b.second = count;
+    if (b.cap < count) {
+        if (b.p) cudaFree(b.p);
+        b.p = nullptr;
+        LAYA_CUDA(cudaMalloc(&b.p, count * sizeof(float)));
+        b.cap = count;
     }
-    LAYA_CUDA(cudaMemcpyAsync(b.first, src, count * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    b.count = count;
+    LAYA_CUDA(cudaMemcpyAsync(b.p, src, count * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
     return OK;
 }
 
@@ -335,12 +339,15 @@ int linear_mixer(laya_decoder* c, const Layer& L, int T, int n_seq, int layer, b
     dr.dk = d.lin_k_dim; dr.dv = d.lin_v_dim; dr.vh = d.lin_v_heads; dr.ratio = d.lin_v_heads / d.lin_k_heads;
     dr.key_dim = c->key_dim; dr.cd = c->cd; dr.conv = c->conv; dr.beta = c->beta; dr.decay = c->decay;
     dr.seq_start = c->seq_start; dr.seq_len = c->seq_len; dr.out = c->core; dr.ld_out = c->vd;
+    dr.err = c->err;
+    dr.chunked = c->chunked_rule && !c->with_states;
     if (c->with_states) {
         dr.rec = seq_table<float>(c, layer, 1);
         if (c->cur_snaps) { dr.snap_begin = c->snap_begin; dr.snap_at = c->snap_at; dr.snap_rec = snap_table<float>(c, layer, 1); }
     }
     const double rule_ops = static_cast<double>(T) * d.lin_v_heads * d.lin_k_dim * d.lin_v_dim * 8.0;
     RC(timed(c, 1, rule_ops, [&] { return dec_delta_rule(dr, n_seq, c->stream); }));
+    RC(record_copy(c, "layers." + std::to_string(layer) + ".rule", c->core, static_cast<size_t>(T) * c->vd));
     dec::GatedArgs gn{};
     gn.T = T; gn.vh = d.lin_v_heads; gn.dv = d.lin_v_dim; gn.core = c->core; gn.ld_core = c->vd;
     gn.z = c->big + c->cd; gn.ld_z = c->ld_in; gn.weight = L.gnorm; gn.eps = d.eps; gn.out = c->core; gn.ld_out = c->vd;
@@ -1001,7 +1008,7 @@ int laya_decoder_destroy(laya_decoder* c) {
     if (c->cosv) cudaFree(c->cosv);
     if (c->sinv) cudaFree(c->sinv);
     for (void* p : c->allocs) cudaFree(p);
-    for (auto& r : c->rec) cudaFree(r.second.first);
+    for (auto& r : c->rec) cudaFree(r.second.p);
     for (auto& e : c->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
     if (c->logit_buf) cudaFree(c->logit_buf);
     if (c->in_dev) cudaFree(c->in_dev);
@@ -1402,6 +1409,12 @@ int laya_decoder_layer(laya_decoder* c, int layer, float* hidden, const int32_t*
     return check_device_error(c);
 }
 
+int laya_decoder_set_chunked_delta_rule(laya_decoder* c, int enabled) {
+    if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
+    c->chunked_rule = enabled != 0;
+    return OK;
+}
+
 int laya_decoder_record_enable(laya_decoder* c, int enabled) {
     if (!c) { set_error("null decoder"); return ERR_ARGUMENT; }
     c->record = enabled != 0;
@@ -1413,9 +1426,9 @@ int laya_decoder_record_get(laya_decoder* c, const char* name, float* host, int6
     DeviceGuard g(c->device);
     auto it = c->rec.find(name);
     if (it == c->rec.end()) { set_error(std::string("nothing recorded as ") + name); return ERR_NOT_FOUND; }
-    if (count < static_cast<int64_t>(it->second.second)) { set_error("host buffer too small"); return ERR_ARGUMENT; }
+    if (count < static_cast<int64_t>(it->second.count)) { set_error("host buffer too small"); return ERR_ARGUMENT; }
     LAYA_CUDA(cudaStreamSynchronize(c->stream));
-    LAYA_CUDA(cudaMemcpy(host, it->second.first, it->second.second * sizeof(float), cudaMemcpyDeviceToHost));
+    LAYA_CUDA(cudaMemcpy(host, it->second.p, it->second.count * sizeof(float), cudaMemcpyDeviceToHost));
     return OK;
 }
 

@@ -68,6 +68,8 @@ struct DeltaArgs {
     float* out; int ld_out;
     float* const* rec;   // per sequence (may be null): initial state in, final state out
     const int32_t* snap_begin; const int32_t* snap_at; float* const* snap_rec;   // may be null
+    int* err;            // device error word (the chunked kernel's bounded waits)
+    bool chunked = false;   // a stateless read may take the chunked form (delta_chunk.cu)
 };
 
 // RmsNormGated per (row, value head): weight · rmsnorm(core) · silu(z).
@@ -124,6 +126,8 @@ int dec_conv_silu(const dec::ConvArgs& a, cudaStream_t s);
 int dec_conv_state(const dec::ConvStateArgs& a, cudaStream_t s);
 int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s);
 int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
+// delta_chunk.cu: stateless reads at key/value head dims 128 (ERR_NOT_SUPPORTED otherwise)
+int dec_delta_rule_chunked(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
 int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);
 int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s);
 int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);

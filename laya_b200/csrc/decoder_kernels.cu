@@ -672,6 +672,8 @@ int dec_deltanet_heads(const dec::HeadsArgs& a, cudaStream_t s) {
 }
 int dec_delta_rule(const dec::DeltaArgs& a, int n_seq, cudaStream_t s) {
     if (n_seq <= 0) return OK;
+    const int chunked = dec_delta_rule_chunked(a, n_seq, s);   // 64-token chunks on the tensor cores where it applies
+    if (chunked != ERR_NOT_SUPPORTED) return chunked;
     if (a.dv > dec::RULE_DV || a.dv % 4) { set_error("delta rule: value head dim must be a multiple of 4, at most 128"); return ERR_NOT_SUPPORTED; }
     const dim3 grid(n_seq, a.vh);
     const int threads = (a.dv + 31) / 32 * 32;
