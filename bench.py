@@ -970,7 +970,7 @@ def run_ours(args):
                                "ms_per_step": r_ms / args.steps,
                                "share_of_step": r_ms / args.steps / ms,
                                "gflops": r_ops / (r_ms / 1e3) / 1e9 if r_ms else None},
-                "attention": {"kernel": "attn_prep + attention_kernel (fp16 mma.sync, causal GQA, sigmoid gate)",
+                "attention": {"kernel": "attn_prep + attention_tc_kernel (tcgen05 fp16, causal GQA, two query heads per CTA, sigmoid gate)",
                               "ms_per_step": a_ms / args.steps, "share_of_step": a_ms / args.steps / ms,
                               "tflops": a_ops / (a_ms / 1e3) / 1e12 if a_ms else None},
                 "gpu_launches": r["launches"], "clocks": r["clocks"], "logits_finite": r["finite"]}

@@ -372,6 +372,7 @@ int full_mixer(laya_decoder* c, const Layer& L, int T, long long pairs, int laye
     at.pos0 = c->pos0;
     at.scale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.head_dim)));
     at.qkv = c->big; at.ld_qkv = c->nqkv; at.out = c->core; at.ld_out = d.heads * d.head_dim;
+    at.err = c->err;
     const double att_ops = 4.0 * static_cast<double>(pairs) * d.heads * d.head_dim;
     RC(timed(c, 2, att_ops, [&] {
         int rc = dec_attn_prep(pp, c->stream);
@@ -426,6 +427,7 @@ int last_layer_pruned(laya_decoder* c, const Layer& L, int T, int n_seq) {
     at.pos0 = c->pos0;
     at.scale = 1.0f / static_cast<float>(std::sqrt(static_cast<double>(d.head_dim)));
     at.qkv = c->big; at.ld_qkv = c->nqkv; at.out = c->core; at.ld_out = ao;
+    at.err = c->err;
     RC(dec_attn_prep(pp, c->stream));
     RC(dec_attention(at, n_seq, d.head_dim, c->stream));
     RC(dec_gather_rows(c->core, ao, c->last_row, n_seq, ao, c->corel, ao, c->stream));

@@ -104,6 +104,7 @@ struct AttnArgs {
     float scale;
     const float* qkv; int ld_qkv;   // the gates
     float* out; int ld_out;
+    int* err = nullptr;   // device error word (the tcgen05 kernel's bounded waits)
 };
 
 // Label logits: per (sequence, label) the Q8_0 product of the sequence's final hidden codes with the label's row
@@ -131,6 +132,8 @@ int dec_delta_rule_chunked(const dec::DeltaArgs& a, int n_seq, cudaStream_t s);
 int dec_gated_norm(const dec::GatedArgs& a, cudaStream_t s);
 int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s);
 int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);
+// dec_attn_tc.cu: the tcgen05 form for head_dim 128 (ERR_NOT_SUPPORTED for anything else)
+int dec_attention_tc(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s);
 int dec_add(float* x, const float* y, size_t n, cudaStream_t s);
 int dec_gather_rows(const float* src, int ld_src, const int32_t* map, int rows, int n, float* dst, int ld_dst,
                     cudaStream_t s);

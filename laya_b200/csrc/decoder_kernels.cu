@@ -707,6 +707,8 @@ int dec_attn_prep(const dec::PrepArgs& a, cudaStream_t s) {
 }
 int dec_attention(const dec::AttnArgs& a, int n_tiles, int hd, cudaStream_t s) {
     if (n_tiles <= 0) return OK;
+    const int tc = dec_attention_tc(a, n_tiles, hd, s);   // tcgen05 where it applies (head_dim 128)
+    if (tc != ERR_NOT_SUPPORTED) return tc;
     const dim3 grid(n_tiles, a.heads);
     if (hd == 128) {
         const int smem = 3 * dec::T64 * (128 + 8) * 2;

@@ -276,3 +276,20 @@ def test_chunked_delta_rule_agrees_with_the_per_token_sweep(mica_long):
     finally:
         m.set_chunked_delta_rule(False)
         m.record(False)
+
+
+def test_mica_geometry_reads_in_pieces_equal_reads_at_once(mica_long):
+    """Qwen35State's promise at config 5's widths (head_dim 128: the tcgen05 attention; the per-token delta rule of
+    reads through states): 300 tokens read at once and in three pieces (61, 139, 100) give the same bits."""
+    cfg, m = mica_long
+    ids = np.random.default_rng(5).integers(0, cfg.vocab, 300)
+    a, b = m.new_state(), m.new_state()
+    try:
+        whole = m.forward_state(ids, a)
+        m.forward_state(ids[:61], b)
+        m.forward_state(ids[61:200], b)
+        pieces = m.forward_state(ids[200:], b)
+        assert np.array_equal(whole.view(np.uint32), pieces.view(np.uint32))
+    finally:
+        a.close()
+        b.close()
