@@ -296,11 +296,16 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES>::THREADS, 1)
 // tiles, which become 36 narrow units).
 constexpr int PAIR_BN = 256;
 
-template <int STAGES>
+// SPL: the operand parts one stage carries for a k-block — 1: A, B; 2: A, A2, B (A·Bᵀ + A2·Bᵀ); 3: A, A2, B, B2
+// (A·Bᵀ + A2·Bᵀ + A·B2ᵀ, the hi/lo passes of an fp32-accurate product).  Each part is loaded once per k-block and the
+// stage's MMAs take every pass from it, so a split product moves 4 tiles per k-block instead of 6.
+template <int STAGES, int SPL>
 struct PairCfg {
     static constexpr int A_BYTES = BM * BK * 2;                  // this CTA's 128 rows of A
     static constexpr int B_BYTES = (PAIR_BN / 2) * BK * 2;       // this CTA's 128 rows of B (64 for a narrow unit)
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int NA = SPL >= 2 ? 2 : 1;                  // A parts per stage (hi, lo)
+    static constexpr int NB = SPL == 3 ? 2 : 1;                  // B parts per stage
+    static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
     static constexpr int STAGE_OUT = 4096;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
@@ -345,13 +350,13 @@ DEVI PairUnit pair_unit(const PairParams& pp, int u, int tiles_n, int kchunk, in
     return r;
 }
 
-template <int STAGES, int A_MN, int B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THREADS, 1)
+template <int STAGES, int SPL, int A_MN, int B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, SPL>::THREADS, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                           const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmB2n,
                           const __grid_constant__ CUtensorMap tmOut, PairParams pp) {
-    using C = PairCfg<STAGES>;
+    using C = PairCfg<STAGES, SPL>;
     constexpr int BN = PAIR_BN;
     constexpr uint32_t IDESC_BASE = (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
     constexpr uint32_t IDESC_WIDE = make_idesc(/*D f32*/ 1, /*A bf16*/ 1, /*B bf16*/ 1, 2 * BM, BN) | IDESC_BASE;
@@ -361,8 +366,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
     // both CTAs run the same code on the same dynamic-shared-memory base, so every buffer sits at the same offset in
     // both: the MMA's descriptors and the mapa'd barrier addresses rely on it
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    // stage s: [A | A2 | B | B2] (the parts SPL carries), each 1024-aligned
+    auto part_a = [&](int s, int i) { return smem + s * C::STAGE_BYTES + i * C::A_BYTES; };
+    auto part_b = [&](int s, int i) { return smem + s * C::STAGE_BYTES + C::NA * C::A_BYTES + i * C::B_BYTES; };
     uint8_t* sOut = smem + STAGES * C::STAGE_BYTES;
     uint64_t* full = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * C::STAGE_OUT);
     uint64_t* empty = full + STAGES;
@@ -406,28 +412,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
                 const int bn = w.wide ? BN / 2 : BN / 4;     // B rows (N) this CTA loads
                 const int m0 = w.m0 + static_cast<int>(rank) * BM;
                 const int n0 = w.n0 + static_cast<int>(rank) * bn;
-                const uint32_t bytes = 2u * static_cast<uint32_t>(C::A_BYTES + bn * BK * 2);
-                const int iters = w.nkb * p.splits;
-                for (int it = 0; it < iters; ++it, ++g) {
+                const uint32_t bytes = 2u * static_cast<uint32_t>(C::NA * C::A_BYTES + C::NB * bn * BK * 2);
+                for (int it = 0; it < w.nkb; ++it, ++g) {
                     const int s = g % STAGES;
-                    const int seg = it / w.nkb, kb = w.kb0 + it - seg * w.nkb;
-                    const CUtensorMap* mA = seg == 1 ? &tmA2 : &tmA;
-                    const CUtensorMap* mB = seg == 2 ? (w.wide || B_MN ? &tmB2 : &tmB2n) : (w.wide || B_MN ? &tmB : &tmBn);
+                    const int kb = w.kb0 + it;
                     if (!mbar_wait(empty + s, ((g / STAGES) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
                     if (rank == 0) mbar_arrive_expect_tx(full + s, bytes);
                     const uint32_t bar = full0 + 8u * static_cast<uint32_t>(s);
-                    uint8_t* a = sA + s * C::A_BYTES;
-                    uint8_t* b = sB + s * C::B_BYTES;
-                    if constexpr (A_MN) {
 #pragma unroll
-                        for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a + j * (BK * 128), mA, bar, m0 + 64 * j, kb * BK);
-                    } else {
-                        tma_load_2d_pair(a, mA, bar, kb * BK, m0);
+                    for (int i = 0; i < C::NA; ++i) {
+                        const CUtensorMap* mA = i ? &tmA2 : &tmA;
+                        uint8_t* a = part_a(s, i);
+                        if constexpr (A_MN) {
+#pragma unroll
+                            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a + j * (BK * 128), mA, bar, m0 + 64 * j, kb * BK);
+                        } else {
+                            tma_load_2d_pair(a, mA, bar, kb * BK, m0);
+                        }
                     }
-                    if constexpr (B_MN) {
-                        for (int j = 0; j < bn / 64; ++j) tma_load_2d_pair(b + j * (BK * 128), mB, bar, n0 + 64 * j, kb * BK);
-                    } else {
-                        tma_load_2d_pair(b, mB, bar, kb * BK, n0);
+#pragma unroll
+                    for (int i = 0; i < C::NB; ++i) {
+                        const CUtensorMap* mB = i ? (w.wide || B_MN ? &tmB2 : &tmB2n) : (w.wide || B_MN ? &tmB : &tmBn);
+                        uint8_t* b = part_b(s, i);
+                        if constexpr (B_MN) {
+                            for (int j = 0; j < bn / 64; ++j) tma_load_2d_pair(b + j * (BK * 128), mB, bar, n0 + 64 * j, kb * BK);
+                        } else {
+                            tma_load_2d_pair(b, mB, bar, kb * BK, n0);
+                        }
                     }
                 }
             }
@@ -447,17 +458,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES>::THR
                 const int buf = ti & 1;
                 if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();
-                const int iters = w.nkb * p.splits;
-                for (int kb = 0; kb < iters; ++kb, ++g) {
+                for (int kb = 0; kb < w.nkb; ++kb, ++g) {
                     const int s = g % STAGES;
                     if (!mbar_wait(full + s, (g / STAGES) & 1, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a = smem_u32(sA + s * C::A_BYTES), b = smem_u32(sB + s * C::B_BYTES);
+                    const uint32_t a0 = smem_u32(part_a(s, 0)), a1 = smem_u32(part_a(s, C::NA - 1));
+                    const uint32_t b0 = smem_u32(part_b(s, 0)), b1 = smem_u32(part_b(s, C::NB - 1));
+                    auto desc_a = [&](uint32_t a, int kk) {
+                        return A_MN ? smem_desc_mn_sw128(a + kk * 2048, BK * 128) : smem_desc_sw128(a + kk * 32);
+                    };
+                    auto desc_b = [&](uint32_t b, int kk) {
+                        return B_MN ? smem_desc_mn_sw128(b + kk * 2048, BK * 128) : smem_desc_sw128(b + kk * 32);
+                    };
+                    const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t ad = A_MN ? smem_desc_mn_sw128(a + kk * 2048, BK * 128) : smem_desc_sw128(a + kk * 32);
-                        const uint64_t bd = B_MN ? smem_desc_mn_sw128(b + kk * 2048, BK * 128) : smem_desc_sw128(b + kk * 32);
-                        mma_f16_pair(tmem + static_cast<uint32_t>(buf * BN), ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        mma_f16_pair(d, desc_a(a0, kk), desc_b(b0, kk), idesc, (kb | kk) != 0 ? 1u : 0u);
+                        if constexpr (SPL >= 2) mma_f16_pair(d, desc_a(a1, kk), desc_b(b0, kk), idesc, 1u);
+                        if constexpr (SPL == 3) mma_f16_pair(d, desc_a(a0, kk), desc_b(b1, kk), idesc, 1u);
                     }
                     mma_commit_pair(smem_u32(empty + s));
                     mma_commit_pair(empty1 + 8u * static_cast<uint32_t>(s));
@@ -552,9 +570,9 @@ static int launch(const Args& a, cudaStream_t stream) {
 }
 
 // The pair kernel's launch: grid = 2 × (pairs resident at once, at most the work units), 74 pairs on 148 SMs.
-template <int STAGES, int A_MN, int B_MN, int EPI>
+template <int STAGES, int SPL, int A_MN, int B_MN, int EPI>
 static int launch_pair(const Args& a, cudaStream_t stream) {
-    using C = PairCfg<STAGES>;
+    using C = PairCfg<STAGES, SPL>;
     CUtensorMap tA, tB, tA2, tB2, tBn, tB2n, tO;
     const int splits = a.A2 ? (a.B2 ? 3 : 2) : 1;
     const bool split = splits > 1;
@@ -582,7 +600,7 @@ static int launch_pair(const Args& a, cudaStream_t stream) {
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
     }
     if (rc) return rc;
-    auto kern = gemm_bf16_pair_kernel<STAGES, A_MN, B_MN, EPI>;
+    auto kern = gemm_bf16_pair_kernel<STAGES, SPL, A_MN, B_MN, EPI>;
     int dev = 0;
     LAYA_CUDA(cudaGetDevice(&dev));
     static DeviceOnce attr;
@@ -616,12 +634,20 @@ static int launch_pair(const Args& a, cudaStream_t stream) {
     return OK;
 }
 
-template <int STAGES, int EPI>
+template <int STAGES, int SPL, int EPI>
+static int dispatch_pair_major(const Args& a, cudaStream_t s) {
+    if (!a.a_mn && !a.b_mn) return launch_pair<STAGES, SPL, 0, 0, EPI>(a, s);
+    if (!a.a_mn && a.b_mn) return launch_pair<STAGES, SPL, 0, 1, EPI>(a, s);
+    if (a.a_mn && a.b_mn) return launch_pair<STAGES, SPL, 1, 1, EPI>(a, s);
+    return launch_pair<STAGES, SPL, 1, 0, EPI>(a, s);
+}
+
+// stages per operand set: 6 × 32 KB plain, 4 × 48 KB with A's low part, 3 × 64 KB with both low parts
+template <int EPI>
 static int dispatch_pair(const Args& a, cudaStream_t s) {
-    if (!a.a_mn && !a.b_mn) return launch_pair<STAGES, 0, 0, EPI>(a, s);
-    if (!a.a_mn && a.b_mn) return launch_pair<STAGES, 0, 1, EPI>(a, s);
-    if (a.a_mn && a.b_mn) return launch_pair<STAGES, 1, 1, EPI>(a, s);
-    return launch_pair<STAGES, 1, 0, EPI>(a, s);
+    if (a.A2 && a.B2) return dispatch_pair_major<3, 3, EPI>(a, s);
+    if (a.A2) return dispatch_pair_major<4, 2, EPI>(a, s);
+    return dispatch_pair_major<6, 1, EPI>(a, s);
 }
 
 template <int BN, int STAGES, int EPI>
@@ -660,9 +686,9 @@ int gemm(const Args& a, cudaStream_t stream) {
         }
     } else if (a.M > BM && pair_enabled()) {
         switch (a.epi) {
-            case EPI_BF16: return dispatch_pair<6, EPI_BF16>(a, stream);
-            case EPI_F32: return dispatch_pair<6, EPI_F32>(a, stream);
-            case EPI_F32_ADD: return dispatch_pair<6, EPI_F32_ADD>(a, stream);
+            case EPI_BF16: return dispatch_pair<EPI_BF16>(a, stream);
+            case EPI_F32: return dispatch_pair<EPI_F32>(a, stream);
+            case EPI_F32_ADD: return dispatch_pair<EPI_F32_ADD>(a, stream);
         }
     } else {
         switch (a.epi) {
