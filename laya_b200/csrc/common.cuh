@@ -102,6 +102,19 @@ DEVI void tma_reduce_add_2d(const CUtensorMap* map, int x, int y, const void* sr
                  "r"(x), "r"(y), "r"(smem_u32(src))
                  : "memory");
 }
+// Untiled bulk copies (16-byte aligned addresses, size a multiple of 16): global → this CTA's shared memory completing
+// on an mbarrier, and shared → global tracked by the issuing thread's bulk groups.
+DEVI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+DEVI void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
 DEVI void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 DEVI void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 DEVI void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }

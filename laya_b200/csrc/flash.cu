@@ -661,19 +661,27 @@ static int launch_bwd(const fa::Args& a, int max_tiles, cudaStream_t s) {
     if (!rc) rc = set_smem(fa::bwd_dkdv_kernel<HD>, smem_kv);
     if (rc) return rc;
     dim3 grid(max_tiles, a.heads);
-    rc = HD == 64 ? flash_backward_dq_tc(a, s) : ERR_NOT_SUPPORTED;   // dQ on the tensor cores (flash_tc.cu)
+    if (HD == 64 && a.ds && (a.window < 0 || a.window % 64 == 0)) {
+        // dK, dV first, leaving every dS tile in the scratch; then dQ = dS·K streams them (flash_tc.cu)
+        rc = flash_backward_dkdv_tc(a, s);
+        if (rc == OK) return flash_backward_dq_ds(a, s);
+        if (rc != ERR_NOT_SUPPORTED) return rc;
+    }
+    fa::Args a0 = a;   // the kernels below recompute S and dP for dQ and store no dS
+    a0.ds = nullptr;
+    rc = HD == 64 ? flash_backward_dq_tc(a0, s) : ERR_NOT_SUPPORTED;   // dQ on the tensor cores (flash_tc.cu)
     if (rc == ERR_NOT_SUPPORTED) {
-        fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a);
+        fa::bwd_dq_kernel<HD><<<grid, 128, smem_dq, s>>>(a0);
         count_launch();
         LAYA_CUDA(cudaGetLastError());
     } else if (rc != OK) {
         return rc;
     }
     if (HD == 64) {   // dK, dV on the tensor cores (flash_tc.cu) when the batch carries its 128-row tile list
-        rc = flash_backward_dkdv_tc(a, s);
+        rc = flash_backward_dkdv_tc(a0, s);
         if (rc != ERR_NOT_SUPPORTED) return rc;
     }
-    fa::bwd_dkdv_kernel<HD><<<grid, 128, smem_kv, s>>>(a);
+    fa::bwd_dkdv_kernel<HD><<<grid, 128, smem_kv, s>>>(a0);
     count_launch();
     return OK;
 }

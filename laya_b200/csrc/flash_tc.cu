@@ -490,6 +490,7 @@ struct BwdParams {
     const float* cosv; const float* sinv;
     __nv_bfloat16* dqkv; int lddq;
     int* err;
+    uint8_t* ds; int ds_nq;   // the dS scratch (fa::Args) or null
 };
 constexpr int BQ2 = 64;                          // queries per tile of the dK/dV kernel
 constexpr int QTILE2 = BQ2 * 128;                // bytes of one 64-row × 64-column bf16 tile
@@ -624,9 +625,16 @@ __global__ void __launch_bounds__(320, 2)
                         mma_f16(tDK, smem_desc_sw128(ad + kk * 32), desc_mn_sw128(aq + kk * 2048, QTILE2), IDESC_G, acc);
                     }
                     mma_commit(empty + s);
+                    if (p.ds) {   // dSᵀ of tile i to the scratch for dQ = dS·K; its shared-memory read ends first
+                        const size_t idx = 1 + (static_cast<size_t>(tile) * p.ds_nq + i) * p.heads + head;
+                        bulk_store(p.ds + idx * TILE, sDS, TILE);
+                        bulk_commit();
+                        bulk_wait_read_all();
+                    }
                     mma_commit(pd_empty);
                 }
             }
+            if (p.ds) bulk_wait_all();
         }
     } else {
         // ---- softmax warps: thread (half, row) owns key row `row` and queries [32·half, 32·half + 32) of a tile
@@ -1035,6 +1043,170 @@ __global__ void __launch_bounds__(320, 2)
     }
 }
 
+// ------------------------------------------------------------------------------------------------ backward: dQ = dS·K
+// dQ from the dSᵀ tiles the dK/dV kernel left in the scratch (BwdParams::ds): for one 128-query tile of one head, over
+// every 128-key tile that sees it, dQ += dS·K with A = dS [128 queries × 128 keys] read M-contiguous from the two
+// 64-query dSᵀ tiles (a half the key tile does not see is the scratch's zero tile) and B = K read N-contiguous — one
+// tcgen05 product (M 128, N 64, K 128) per key tile, no recomputation of S, P or dP.  Persistent over (query tile,
+// head) items, query tiles fastest so consecutive items of a segment reuse its K tiles in L2; a two-stage ring of
+// 48 KB stages, two TMEM accumulators so one item's epilogue (dQ rotated back by −θ at the query position, bf16)
+// overlaps the next item's MMAs; two CTAs per SM.
+//   warp 0      producer: two bulk copies of dSᵀ halves and one TMA load of K per key tile
+//   warp 1      TMEM owner and MMA issuer
+//   warps 2-5   epilogue, one query row per thread
+constexpr int DQG_STAGE = 3 * TILE;
+constexpr int DQG_SMEM = 1024 + 2 * DQG_STAGE + 256;
+static_assert(2 * DQG_SMEM <= 232448, "two CTAs per SM");
+
+__global__ void __launch_bounds__(192, 2)
+    bwd_dq_ds_kernel(const __grid_constant__ CUtensorMap tmk, BwdParams p) {
+    constexpr uint32_t IDESC = make_idesc(1, 1, 1, BQ, HD) | (1u << 15) | (1u << 16);   // A (dS), B (K) MN-major
+    const int n_tq = *p.n_tq, n_items = n_tq * p.heads;
+    if (static_cast<int>(blockIdx.x) >= n_items) return;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * DQG_STAGE);
+    uint64_t* full = bars;            // [2]
+    uint64_t* empty = bars + 2;       // [2]
+    uint64_t* tfull = bars + 4;       // [2]
+    uint64_t* tempty = bars + 6;      // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = warp_id(), lane = lane_id();
+    const bool global = p.window < 0;
+    const int W = p.window;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(tfull + b, 1); mbar_init(tempty + b, 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, 128); tmem_relinquish(); }
+    if (warp == 0 && lane == 0) prefetch_tmap(&tmk);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // the key tiles [lo, hi) that see the item's query tile
+    struct Item { int head, g, item, q0, L, seg0, first, lo, hi; };
+    auto item_of = [&](int it) {
+        Item r;
+        r.head = it / n_tq;
+        r.g = it - r.head * n_tq;
+        r.item = p.tq_item[r.g];
+        r.q0 = p.tq_p0[r.g];
+        r.L = p.seg_len[r.item];
+        r.seg0 = p.seg_start[r.item];
+        r.first = r.g - r.q0 / BQ;                  // the item's first 128-row tile
+        r.lo = global ? 0 : max(0, r.q0 - W) / BK;
+        r.hi = global ? (r.L + BK - 1) / BK : (min(r.L, r.q0 + BQ + W) - 1) / BK + 1;
+        return r;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                const Item m = item_of(it);
+                for (int kt = m.lo; kt < m.hi; ++kt, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(empty + s, ((g >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full + s, DQG_STAGE);
+                    uint8_t* st = smem + s * DQG_STAGE;
+                    const int k0 = kt * BK;
+                    const int qb0 = global ? 0 : max(0, k0 - W), qe = global ? m.L : min(m.L, k0 + BK + W);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int q = m.q0 + h * BQ2;
+                        const size_t idx = (q >= qb0 && q < qe)
+                            ? 1 + (static_cast<size_t>(m.first + kt) * p.ds_nq + (q - qb0) / BQ2) * p.heads + m.head : 0;
+                        bulk_load(st + h * TILE, p.ds + idx * TILE, TILE, full + s);
+                    }
+                    tma_load_2d(st + 2 * TILE, &tmk, full + s, p.hidden + m.head * HD, m.seg0 + k0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t g = 0, ti = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ti) {
+                const Item m = item_of(it);
+                const int buf = ti & 1;
+                if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + static_cast<uint32_t>(buf * HD);
+                for (int kt = m.lo; kt < m.hi; ++kt, ++g) {
+                    const int s = g & 1;
+                    if (!mbar_wait(full + s, (g >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(smem + s * DQG_STAGE), b = a + 2 * TILE;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        mma_f16(d, desc_mn_sw128(a + kk * 2048, TILE), desc_mn_sw128(b + kk * 2048, TILE), IDESC,
+                                (kt > m.lo || kk > 0) ? 1u : 0u);
+                    mma_commit(empty + s);
+                }
+                mma_commit(tfull + buf);
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        uint32_t ti = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++ti) {
+            const Item m = item_of(it);
+            const int buf = ti & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err))) break;
+            tc_fence_after();
+            uint32_t x[32], y[32];
+            tmem_ld32(tmem + lane_off + static_cast<uint32_t>(buf * HD), x);
+            tmem_ld32(tmem + lane_off + static_cast<uint32_t>(buf * HD + 32), y);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty + buf);
+            const int q = m.q0 + row;
+            if (q < m.L) {
+                float a[32], b[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) { a[e] = __uint_as_float(x[e]); b[e] = __uint_as_float(y[e]); }
+                if (p.cosv) {   // pairs (i, i + 32) rotated back by −θ at the query's position
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
+                        const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
+                        const float u = a[i], v = b[i];
+                        a[i] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
+                        b[i] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                    }
+                }
+                __nv_bfloat16* out = p.dqkv + static_cast<size_t>(m.seg0 + q) * p.lddq + m.head * HD;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    *reinterpret_cast<uint4*>(out + 8 * t) =
+                        make_uint4(pack2(a[8 * t], a[8 * t + 1]), pack2(a[8 * t + 2], a[8 * t + 3]),
+                                   pack2(a[8 * t + 4], a[8 * t + 5]), pack2(a[8 * t + 6], a[8 * t + 7]));
+                    *reinterpret_cast<uint4*>(out + 32 + 8 * t) =
+                        make_uint4(pack2(b[8 * t], b[8 * t + 1]), pack2(b[8 * t + 2], b[8 * t + 3]),
+                                   pack2(b[8 * t + 4], b[8 * t + 5]), pack2(b[8 * t + 6], b[8 * t + 7]));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
 }  // namespace fat
 
 template <bool SPLIT, bool DROP>
@@ -1146,6 +1318,7 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
+    p.ds = a.ds; p.ds_nq = a.ds_nq;
     fat::bwd_dkdv_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::BWD_SMEM, s>>>(tk, tq, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
@@ -1187,8 +1360,44 @@ static int launch_dq_tc(const fa::Args& a, cudaStream_t s) {
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
+    p.ds = nullptr; p.ds_nq = 0;
     const int items = a.max_tq * a.heads, slots = 2 * nsm;   // 2 CTAs per SM
     fat::bwd_dq_tc_kernel<DROP><<<items < slots ? items : slots, 320, fat::DQ_SMEM, s>>>(tq, tkv, tdo, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// dQ = dS·K from the scratch the dK/dV kernel filled (run after it); ERR_NOT_SUPPORTED without a scratch or for
+// shapes it does not take.
+int flash_backward_dq_ds(const fa::Args& a, cudaStream_t s) {
+    if (!a.ds || a.ds_nq <= 0 || a.hidden / a.heads != fat::HD || !a.tq_item || a.max_tq <= 0 || a.T <= 0)
+        return ERR_NOT_SUPPORTED;
+    if ((a.window >= 0 && a.window % fat::BQ2) || (a.ld & 7) || (a.lddq & 7) ||
+        (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.ds) & 15))
+        return ERR_NOT_SUPPORTED;
+    CUtensorMap tk;
+    if (int rc = make_tmap_2d(&tk, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
+                              static_cast<uint64_t>(a.ld) * 2, fat::BK, fat::HD, true))
+        return rc;
+    static DeviceOnce attr;
+    int dev = 0, nsm = 0;
+    LAYA_CUDA(cudaGetDevice(&dev));
+    if (!attr.done(dev)) {
+        LAYA_CUDA(cudaFuncSetAttribute(fat::bwd_dq_ds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fat::DQG_SMEM));
+        attr.mark(dev);
+    }
+    if (int e = sm_count(dev, &nsm)) return e;
+    fat::BwdParams p{};
+    p.seg_start = a.seg_start; p.seg_len = a.seg_len;
+    p.tq_item = a.tq_item; p.tq_p0 = a.tq_p0; p.n_tq = a.n_tq;
+    p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
+    p.cosv = a.cosv; p.sinv = a.sinv;
+    p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
+    p.ds = a.ds; p.ds_nq = a.ds_nq;
+    const int items = a.max_tq * a.heads, slots = 2 * nsm;
+    fat::bwd_dq_ds_kernel<<<items < slots ? items : slots, 192, fat::DQG_SMEM, s>>>(tk, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;

@@ -43,6 +43,7 @@ namespace {
 constexpr size_t NONE = static_cast<size_t>(-1);
 constexpr size_t BUCKET_ELEMS = 25u * 1000u * 1000u / 4u;   // 25 MB of fp32 gradients per allreduce
 constexpr int MAX_GROUPS = 16;                               // noise groups a batch can carry
+constexpr size_t DS_SCRATCH_MAX = size_t(2) << 30;            // the attention backward's dS scratch, at most
 
 #define RC(x)                      \
     do {                           \
@@ -205,6 +206,8 @@ struct laya_trainer {
     float *smean = nullptr, *srstd = nullptr, *spre = nullptr, *logits = nullptr, *dlog = nullptr;
     // workspace
     float *R32 = nullptr, *dH = nullptr, *dN = nullptr, *dbig32 = nullptr, *dsum = nullptr, *dsn = nullptr;
+    uint8_t* ds = nullptr;   // the attention backward's dS scratch (null when it would exceed DS_SCRATCH_MAX)
+    int ds_nq = 0;
     float* ln_part = nullptr;                                // LayerNorm backward: per-CTA dγ/dβ partials
     bf16 *d16 = nullptr, *dctx16 = nullptr, *dqkv16 = nullptr, *dbig16 = nullptr, *dpre16 = nullptr;
     float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;
@@ -436,6 +439,7 @@ fa::Args attn_args(laya_trainer* t, const laya_batch* b, const bf16* qkv, const 
     a.tq_item = b->tq_item; a.tq_p0 = b->tq_p0; a.n_tq = b->n_tq; a.max_tq = b->tq; a.T = b->T;
     a.tp_item = b->tp_item; a.tp_p0 = b->tp_p0; a.n_tp = b->n_tp; a.max_tp = b->tp;
     a.err = t->err;
+    a.ds = t->ds; a.ds_nq = t->ds_nq;
     return a;
 }
 
@@ -858,6 +862,19 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
         return fail(rc);
     if ((rc = dalloc(t, reinterpret_cast<void**>(&t->rl_scratch), rlcd_scratch_bytes(MAX_GROUPS, t->Nc, t->Mc))))
         return fail(rc);
+    {   // the attention backward's dS scratch: per 128-row tile of the batch, ceil(max segment / 64) query tiles of
+        // 16 KB per head, after one zero tile; long-context geometries that would need more than DS_SCRATCH_MAX
+        // recompute S and dP in the dQ kernel instead
+        const int heads = std::max(t->heads, t->HH);
+        const size_t tiles = static_cast<size_t>(d.max_tokens + 127) / 128 + static_cast<size_t>(d.max_items);
+        const int nq = (t->maxpos + 63) / 64;
+        const size_t bytes = (1 + tiles * nq * heads) * 16384;
+        if (t->hd == 64 && bytes <= DS_SCRATCH_MAX) {
+            if ((rc = dalloc(t, reinterpret_cast<void**>(&t->ds), bytes))) return fail(rc);
+            if (cudaMemset(t->ds, 0, 16384) != cudaSuccess) return fail(cuda_fail(cudaGetLastError(), "dS zero tile"));
+            t->ds_nq = nq;
+        }
+    }
     {   // the LayerNorm backward's per-CTA dγ/dβ partials
         int nsm = 0;
         if ((rc = sm_count(t->device, &nsm))) return fail(rc);

@@ -55,6 +55,10 @@ struct Args {
     // the two-tile forward: 256-row pair tiles of every segment
     const int32_t* tp_item = nullptr; const int32_t* tp_p0 = nullptr; const int32_t* n_tp = nullptr; int max_tp = 0;
     int* err;
+    // the backward's dS scratch (flash_tc.cu): the dK/dV kernel leaves each 128-key × 64-query dSᵀ tile there and dQ
+    // = dS·K streams them back; tile (g, j, head) at 1 + (g·ds_nq + j)·heads + head (16 KB each, tile 0 zeros); null:
+    // dQ recomputes S and dP
+    uint8_t* ds = nullptr; int ds_nq = 0;
 };
 }  // namespace fa
 // q, k rotated at their segment positions (cosv null: no rotation), v copied, from fp32 or bf16 [T, lds] into bf16
@@ -67,6 +71,7 @@ int flash_forward_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: head_
 int flash_forward_pp(const fa::Args& a, cudaStream_t s);   // flash_pp.cu: head_dim 64, two query tiles per CTA
 int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s);   // flash_tc.cu: dK, dV for head_dim 64
 int flash_backward_dq_tc(const fa::Args& a, cudaStream_t s);     // flash_tc.cu: dQ for head_dim 64
+int flash_backward_dq_ds(const fa::Args& a, cudaStream_t s);     // flash_tc.cu: dQ = dS·K from the dS scratch
 // The decision forward's attention (inference) on the tensor cores: qkv16 [T, ld] fp16 = rotated q | k | v, 128-row
 // query tiles of every segment, context out as Q8_0 codes q [T, hidden] and scales d [hidden/32, ldd].
 struct InferAttn {
