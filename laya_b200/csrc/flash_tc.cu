@@ -618,6 +618,11 @@ __global__ void __launch_bounds__(320, 2)
                     tc_fence_after();
                     const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
                     const uint32_t ap = smem_u32(sP), ad = smem_u32(sDS);
+                    if (p.ds) {   // dSᵀ of tile i to the scratch for dQ = dS·K, its read overlapping the MMAs' issue
+                        const size_t idx = 1 + (static_cast<size_t>(tile) * p.ds_nq + i) * p.heads + head;
+                        bulk_store(p.ds + idx * TILE, sDS, TILE);
+                        bulk_commit();
+                    }
 #pragma unroll
                     for (int kk = 0; kk < BQ2 / 16; ++kk) {
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
@@ -625,12 +630,7 @@ __global__ void __launch_bounds__(320, 2)
                         mma_f16(tDK, smem_desc_sw128(ad + kk * 32), desc_mn_sw128(aq + kk * 2048, QTILE2), IDESC_G, acc);
                     }
                     mma_commit(empty + s);
-                    if (p.ds) {   // dSᵀ of tile i to the scratch for dQ = dS·K; its shared-memory read ends first
-                        const size_t idx = 1 + (static_cast<size_t>(tile) * p.ds_nq + i) * p.heads + head;
-                        bulk_store(p.ds + idx * TILE, sDS, TILE);
-                        bulk_commit();
-                        bulk_wait_read_all();
-                    }
+                    if (p.ds) bulk_wait_read_all();   // the tile's shared-memory read is done before it is rewritten
                     mma_commit(pd_empty);
                 }
             }
