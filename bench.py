@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--cpu-sample-rows", type=int, default=1, help="rows of 512 tokens in one Q8_0 CPU step")
     ap.add_argument("--cpu-train-tokens", type=int, default=256, help="tokens of the CPU fine-tune sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the nested config-4 (ModernBERT-large, 4 x 8192 tokens) measurement of the default run")
     ap.add_argument("--train-config", type=int, default=3, choices=[3, 4],
                     help="3: ModernBERT-base, 32 rows x U{256..1024}; 4: ModernBERT-large, 4 rows x 8192 tokens")
     ap.add_argument("--train-rows", type=int, default=None, help="rows per GPU of the fine-tune step")
@@ -883,6 +885,23 @@ def run_ours(args):
             if alt:
                 line["bf16_forward" if mode == 0 else "accurate_forward"] = {
                     "value": alt[1] / (alt[0] / 1e3), "unit": "tokens/s", "ms_per_step": alt[0]}
+        if args.workload == "all" and args.train_config == 3 and not args.no_config4 and world == 1:
+            # config 4 (ModernBERT-large, 4 rows of 8192 tokens) beside the headline on one GPU: a few timed steps
+            import copy
+            a4 = copy.copy(args)
+            a4.train_config, a4.train_layers, a4.train_rows = 4, None, None
+            a4.steps, a4.warmup = max(2, min(args.steps, 4)), 2
+            try:
+                r4 = train_measure(a4, d, mode, with_e2e=False, with_profile=False)
+                ms4 = d.reduce([r4["ms"]], MAX)[0]
+                tok4 = d.reduce([r4["tokens_per_step"]], SUM)[0]
+                c4 = {"metric": "fine-tune tokens/s (fwd+bwd+AdamW)", "value": tok4 / (ms4 / 1e3),
+                      "unit": "tokens/s", "ms_per_step": ms4, "steps": a4.steps, "warmup": a4.warmup,
+                      "config": train_config(world, r4["tokens_per_step"], fwd if rank == 0 else "", 4, 4, (8192, 8192))}
+            except Exception as e:   # reported, not fatal: the headline line stands on its own
+                c4 = {"error": f"{type(e).__name__}: {e}"}
+            if rank == 0 and line is not None:
+                line["config4_long_context"] = c4
             if not args.no_cpu_baseline and world == 1:   # the CPU sample: rank 0 at N = 1 only
                 line["cpu_baseline"] = train_cpu_baseline(args.cpu_train_tokens)
     if args.workload in ("all", "q8"):
