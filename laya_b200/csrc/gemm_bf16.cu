@@ -62,6 +62,8 @@ struct KParams {
     int ksplit;        // K chunks per output tile (accumulating outputs only: chunks reduce-add into the output)
     const float* bias;
     int* err;
+    // EPI_QKV: rotary tables [position, 32] (null: no rotation), each row's position, the rotated columns
+    const int32_t* tok_item; const int32_t* seg_start; const float* cosv; const float* sinv; int rot_cols;
 };
 
 // Drains one warp's share of an accumulator — 32 TMEM lanes (rows gr0..gr0+31) × cols columns from gc0, cols a
@@ -133,6 +135,70 @@ DEVI void drain_rows(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, c
                 else tma_store_2d(tmOut, gc0 + c * 32, gr0, stage);
                 bulk_commit();
             }
+        }
+    }
+}
+
+// The attention input's epilogue (EPI_QKV): 64-column chunks, each one head of q, k or v (chunks start on multiples of
+// 64 and the q | k | v boundaries are multiples of 64), so a thread holds both halves (i, i + 32) of its row's
+// rotation pairs: columns below rot_cols are rotated at the row's segment position in the reference's fp32 order
+// (Rotary.Apply, Ops.cs:490-503: x·c − y·s, y·c + x·s), then written as bf16 hi through tmOut and, with has_lo, the
+// bf16 remainder x − bf16(x) through tmOut2.
+DEVI void drain_qkv(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, const CUtensorMap* tmOut2, bool has_lo,
+                    const KParams& p, const float* bias, int gc0, int gr0, int lane, int cols) {
+    const int row = gr0 + lane;
+    const float* cr = nullptr;
+    const float* sr = nullptr;
+    if (p.cosv && row < p.M) {
+        const int pos = row - p.seg_start[p.tok_item[row]];
+        cr = p.cosv + static_cast<size_t>(pos) * 32;
+        sr = p.sinv + static_cast<size_t>(pos) * 32;
+    }
+#pragma unroll 1
+    for (int c = 0; c < cols / 64; ++c) {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tbase + c * 64, v0);
+        tmem_ld32(tbase + c * 64 + 32, v1);
+        tmem_ld_wait();
+        const int col0 = gc0 + c * 64;
+        float x[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            x[j] = __uint_as_float(v0[j]);
+            x[32 + j] = __uint_as_float(v1[j]);
+        }
+        if (bias) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) x[j] += col0 + j < p.N ? __ldg(bias + col0 + j) : 0.0f;
+        }
+        if (cr && col0 < p.rot_cols) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float cc = __ldg(cr + j), ss = __ldg(sr + j), u = x[j], v = x[32 + j];
+                x[j] = __fsub_rn(__fmul_rn(u, cc), __fmul_rn(v, ss));
+                x[32 + j] = __fadd_rn(__fmul_rn(v, cc), __fmul_rn(u, ss));
+            }
+        }
+#pragma unroll 1
+        for (int part = 0; part < (has_lo ? 2 : 1); ++part) {
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                uint32_t w[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float a = x[q * 8 + 2 * t], b = x[q * 8 + 2 * t + 1];
+                    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+                    if (part == 1)
+                        h = __floats2bfloat162_rn(a - __bfloat162float(h.x), b - __bfloat162float(h.y));
+                    w[t] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(stage + lane * 128 + ((q ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) { tma_store_2d(part ? tmOut2 : tmOut, col0, gr0, stage); bulk_commit(); }
         }
     }
 }
@@ -317,6 +383,7 @@ struct PairParams {
     KParams k;
     int units;        // work units walked by the pairs
     int split_from;   // units from here on are the halves of tiles split along N (split_from + 2·(tiles − split_from))
+    int has_lo;       // EPI_QKV: the low parts are written too
 };
 
 // One work unit of the pair kernel: output rows [m0, m0 + 256), columns [n0, n0 + (wide ? 256 : 128)), k-blocks
@@ -355,7 +422,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, SPL>
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                           const __grid_constant__ CUtensorMap tmBn, const __grid_constant__ CUtensorMap tmB2n,
-                          const __grid_constant__ CUtensorMap tmOut, PairParams pp) {
+                          const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
+                          PairParams pp) {
     using C = PairCfg<STAGES, SPL>;
     constexpr int BN = PAIR_BN;
     constexpr uint32_t IDESC_BASE = (static_cast<uint32_t>(A_MN) << 15) | (static_cast<uint32_t>(B_MN) << 16);
@@ -504,8 +572,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, SPL>
             if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
             const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * cols);
-            drain_rows<EPI>(tbase, stage, &tmOut, w.first ? p.bias : nullptr, p.N, w.n0 + half * cols, m0 + quarter * 32,
-                            lane, cols);
+            if constexpr (EPI == EPI_QKV)
+                drain_qkv(tbase, stage, &tmOut, &tmOut2, pp.has_lo != 0, p, w.first ? p.bias : nullptr, w.n0 + half * cols,
+                          m0 + quarter * 32, lane, cols);
+            else
+                drain_rows<EPI>(tbase, stage, &tmOut, w.first ? p.bias : nullptr, p.N, w.n0 + half * cols,
+                                m0 + quarter * 32, lane, cols);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * static_cast<uint32_t>(buf));
@@ -593,11 +665,18 @@ static int launch_pair(const Args& a, cudaStream_t stream) {
     if (!rc) rc = map_b(&tB2, b2, PAIR_BN / 2);
     if (!rc) rc = map_b(&tBn, a.B, PAIR_BN / 4);
     if (!rc) rc = map_b(&tB2n, b2, PAIR_BN / 4);
+    CUtensorMap tO2;
     if (!rc) {
-        if (EPI == EPI_BF16)
+        if (EPI == EPI_BF16 || EPI == EPI_QKV)
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
         else
             rc = make_tmap_2d(&tO, a.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.M, a.N, static_cast<uint64_t>(a.ldo) * 4, 32, 32, true);
+    }
+    if (!rc) {
+        if (EPI == EPI_QKV && a.out2)
+            rc = make_tmap_2d(&tO2, a.out2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.M, a.N, static_cast<uint64_t>(a.ldo) * 2, 32, 64, true);
+        else
+            tO2 = tO;
     }
     if (rc) return rc;
     auto kern = gemm_bf16_pair_kernel<STAGES, SPL, A_MN, B_MN, EPI>;
@@ -622,13 +701,15 @@ static int launch_pair(const Args& a, cudaStream_t stream) {
     }
     const int tiles = ((a.N + PAIR_BN - 1) / PAIR_BN) * ((a.M + 2 * BM - 1) / (2 * BM));
     const int ksplit = EPI == EPI_F32_ADD && a.ksplit_ok ? choose_ksplit(tiles, (a.K + BK - 1) / BK, pairs) : 1;
-    PairParams pp{KParams{a.M, a.N, a.K, splits, ksplit, a.bias, a.err}, tiles * ksplit, tiles * ksplit};
+    PairParams pp{KParams{a.M, a.N, a.K, splits, ksplit, a.bias, a.err, a.tok_item, a.seg_start, a.cosv, a.sinv,
+                          a.rot_cols},
+                  tiles * ksplit, tiles * ksplit, a.out2 ? 1 : 0};
     const int rem = tiles % pairs;
     if (ksplit == 1 && rem > 0 && 2 * rem <= pairs) {   // the last partial round, split along N
         pp.split_from = tiles - rem;
         pp.units = pp.split_from + 2 * rem;
     }
-    kern<<<2 * std::min(pp.units, pairs), C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tBn, tB2n, tO, pp);
+    kern<<<2 * std::min(pp.units, pairs), C::THREADS, C::SMEM, stream>>>(tA, tB, tA2, tB2, tBn, tB2n, tO, tO2, pp);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -674,9 +755,17 @@ int gemm(const Args& a, cudaStream_t stream) {
     if (a.B2 && !a.A2) { set_error("a split product with a low part of B needs the low part of A"); return ERR_ARGUMENT; }
     const uintptr_t al = reinterpret_cast<uintptr_t>(a.A) | reinterpret_cast<uintptr_t>(a.B) | reinterpret_cast<uintptr_t>(a.out) |
                          reinterpret_cast<uintptr_t>(a.A2) | reinterpret_cast<uintptr_t>(a.B2);
-    if ((al & 15) || (a.lda & 7) || (a.ldb & 7) || (a.epi == EPI_BF16 ? (a.ldo & 7) : (a.ldo & 3))) {
+    if ((al & 15) || (a.lda & 7) || (a.ldb & 7) || ((a.epi == EPI_BF16 || a.epi == EPI_QKV) ? (a.ldo & 7) : (a.ldo & 3))) {
         set_error("bf16 product operands need 16-byte aligned bases and row strides");
         return ERR_ARGUMENT;
+    }
+    if (a.epi == EPI_QKV) {   // CTA pairs only, operands K-major, 64-column heads; the caller falls back otherwise
+        if (a.N <= 128 || a.M <= BM || !pair_enabled() || a.a_mn || a.b_mn || (a.N % 64) || (a.rot_cols % 64) ||
+            (reinterpret_cast<uintptr_t>(a.out2) & 15) || (a.cosv && (!a.sinv || !a.tok_item || !a.seg_start)))
+            return ERR_NOT_SUPPORTED;
+        if (a.A2 && a.B2) return launch_pair<3, 3, 0, 0, EPI_QKV>(a, stream);
+        if (a.A2) return launch_pair<4, 2, 0, 0, EPI_QKV>(a, stream);
+        return launch_pair<6, 1, 0, 0, EPI_QKV>(a, stream);
     }
     if (a.N <= 128) {
         switch (a.epi) {

@@ -413,6 +413,22 @@ int lin_fwd(laya_trainer* t, int T, int N, int K, const bf16* x, const bf16* x_l
     if (x_lo) { a.A2 = x_lo; a.B2 = t->shadow_lo + w; }
     return timed(t, 0, 2.0 * T * N * K, [&] { return bf::gemm(a, t->stream); });
 }
+// The attention input in one product (EPI_QKV): q | k | v = x·Wᵀ (+ bias), q and k rotated at each row's segment
+// position (cosv null: none), bf16 hi into `hi` and, with x_lo, the low parts into `lo`.  ERR_NOT_SUPPORTED when the
+// product does not run on CTA pairs (then the caller writes fp32 and runs the prep pass).
+int lin_qkv(laya_trainer* t, const laya_batch* b, int T, int N, int K, const bf16* x, const bf16* x_lo, size_t w,
+            const float* bias, const float* cosv, const float* sinv, int rot_cols, bf16* hi, bf16* lo) {
+    if (T <= 128 || (cosv && t->hd != 64)) return ERR_NOT_SUPPORTED;   // one-CTA sizes; rotation pairs (i, i + 32)
+    bf::Args a{T, N, K, x, K, 0, t->shadow + w, K, 0, bias, bf::EPI_QKV, hi, N, t->err};
+    if (x_lo) { a.A2 = x_lo; a.B2 = t->shadow_lo + w; a.out2 = lo; }
+    a.tok_item = b->tok_item; a.seg_start = b->seg_start; a.cosv = cosv; a.sinv = sinv; a.rot_cols = rot_cols;
+    int rc = ERR_NOT_SUPPORTED;
+    const int t_rc = timed(t, 0, 2.0 * T * N * K, [&] {
+        rc = bf::gemm(a, t->stream);
+        return rc == ERR_NOT_SUPPORTED ? OK : rc;
+    });
+    return t_rc != OK ? t_rc : rc;
+}
 int lin_dx(laya_trainer* t, int T, int N, int K, const bf16* dy, size_t w, int epi, void* dx) {
     bf::Args a{T, K, N, dy, N, 0, t->shadow + w, K, 1, nullptr, epi, dx, K, t->err};
     return timed(t, 0, 2.0 * T * N * K, [&] { return bf::gemm(a, t->stream); });
@@ -487,7 +503,12 @@ int enc_forward(laya_trainer* t, const laya_batch* b, int l) {
     const bool g = t->global[l];
     const float* cosv = g ? t->cos_g : t->cos_l;
     const float* sinv = g ? t->sin_g : t->sin_l;
-    if (pr) {   // fp32 qkv → rotated bf16 hi (kept for the backward) and lo (this forward only)
+    // rotated bf16 hi (kept for the backward) and lo (accurate forward, this forward only) straight from the product
+    const int fused = lin_qkv(t, b, T, 3 * H, H, t->n1[l], n1lo, p.qkv, nullptr, cosv, sinv, 2 * H, t->qkv[l],
+                              pr ? t->ws_qkvlo : nullptr);
+    if (fused != OK && fused != ERR_NOT_SUPPORTED) return fused;
+    if (fused == OK) {
+    } else if (pr) {   // fp32 qkv → rotated bf16 hi and lo by the prep pass
         RC(lin_fwd(t, T, 3 * H, H, t->n1[l], n1lo, p.qkv, nullptr, bf::EPI_F32, t->ws_qkv32));
         RC(attn_prep(t->ws_qkv32, 1, 3 * H, T, H, t->heads, b->tok_item, b->seg_start, cosv, sinv, t->qkv[l],
                      t->ws_qkvlo, 3 * H, s));
@@ -525,9 +546,14 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
     bf16 *n1lo = at(t->hn1lo, l), *n2lo = at(t->hn2lo, l), *ctxlo = at(t->hctxlo, l), *actlo = at(t->hactlo, l);
     RC(ln_fwd(ln_args(t, T, t->HIN[l], p.n1w, p.n1b, 1e-5f, t->hn1[l], n1lo, nullptr, t->hm1[l], t->hr1[l]), s));
     if (pr) {   // no rotary in the head: the prep only splits fp32 qkv into hi and lo
-        RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, bf::EPI_F32, t->ws_qkv32));
-        RC(attn_prep(t->ws_qkv32, 1, 3 * H, T, H, t->HH, b->tok_item, b->seg_start, nullptr, nullptr, t->hqkv[l],
-                     t->ws_qkvlo, 3 * H, s));
+        const int fused = lin_qkv(t, b, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, nullptr, nullptr, 0,
+                                  t->hqkv[l], t->ws_qkvlo);
+        if (fused != OK && fused != ERR_NOT_SUPPORTED) return fused;
+        if (fused != OK) {
+            RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], n1lo, p.inw, t->master + p.inb, bf::EPI_F32, t->ws_qkv32));
+            RC(attn_prep(t->ws_qkv32, 1, 3 * H, T, H, t->HH, b->tok_item, b->seg_start, nullptr, nullptr, t->hqkv[l],
+                         t->ws_qkvlo, 3 * H, s));
+        }
     } else {
         RC(lin_fwd(t, T, 3 * H, H, t->hn1[l], nullptr, p.inw, t->master + p.inb, bf::EPI_BF16, t->hqkv[l]));
     }

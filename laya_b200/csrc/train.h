@@ -10,6 +10,8 @@ enum Epi : int {
     EPI_BF16 = 0,     // out bf16 = A·Bᵀ (+ bias)
     EPI_F32 = 1,      // out fp32 = A·Bᵀ (+ bias)
     EPI_F32_ADD = 2,  // out fp32 += A·Bᵀ (+ bias), by TMA reduce-add
+    EPI_QKV = 3,      // attention input: (A·Bᵀ + bias) with columns < rot_cols rotated at each row's segment position
+                      // (pairs (i, i + 32) of every 64-column head), out bf16 hi and out2 bf16 lo (or no lo)
 };
 // out[M, N] = A · Bᵀ with A [M, K] and B [N, K] in the logical view; a_mn / b_mn say the operand is stored with the
 // M (N) index contiguous instead of K: A as [K, lda] and B as [K, ldb].  Row strides in elements.
@@ -27,6 +29,11 @@ struct Args {
     const __nv_bfloat16* A2 = nullptr;
     const __nv_bfloat16* B2 = nullptr;
     int ksplit_ok = 0;   // EPI_F32_ADD only: K may be split into chunks that reduce-add (summation order varies)
+    // EPI_QKV (CTA-pair products only; ERR_NOT_SUPPORTED otherwise): the low parts, and the rotary tables
+    // [position, 32] with each row's position = row − seg_start[tok_item[row]]; cosv null: no rotation
+    void* out2 = nullptr;
+    const int32_t* tok_item = nullptr; const int32_t* seg_start = nullptr;
+    const float* cosv = nullptr; const float* sinv = nullptr; int rot_cols = 0;
 };
 int gemm(const Args& a, cudaStream_t stream);
 }  // namespace bf
