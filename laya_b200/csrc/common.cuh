@@ -44,14 +44,19 @@ DEVI void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 DEVI void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// A thread whose phase is not complete is suspended until it completes, or for at most LAYA_WAIT_SUSPEND_NS, so a
+// waiting warp takes no issue slots from the warps of its SM sub-partition that have work.
+#ifndef LAYA_WAIT_SUSPEND_NS
+#define LAYA_WAIT_SUSPEND_NS 20000u
+#endif
 DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(LAYA_WAIT_SUSPEND_NS)
         : "memory");
     return ok != 0;
 }

@@ -570,11 +570,21 @@ __global__ void __launch_bounds__(320, 2)
         }
         for (int j = 0; j < nq; ++j) {
             const int s = j & 1;
+            const int q0 = qb0 + j * BQ2;
+            // the tile's row statistics are read before the wait for its stage, so their latency overlaps it
+            float lv[BQ2 / 32], dv[BQ2 / 32];
+#pragma unroll
+            for (int i = 0; i < BQ2 / 32; ++i) {
+                const int r = lane + 32 * i;
+                const bool in = q0 + r < qe;
+                const size_t at = static_cast<size_t>(seg0 + (in ? q0 + r : 0)) * p.heads + head;
+                lv[i] = in ? __ldg(p.lse + at) : 0.f;
+                dv[i] = in ? __ldg(p.dsum + at) : 0.f;
+            }
             int got = 1;
             if (lane == 0) got = mbar_wait(empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err);
             if (!__shfl_sync(0xffffffffu, got, 0)) break;
             __syncwarp();
-            const int q0 = qb0 + j * BQ2;
             if (lane == 0) {
                 mbar_arrive_expect_tx(full + s, 2 * QTILE2);
                 tma_load_2d(sQO + s * 2 * QTILE2, &tmq, full + s, head * HD, seg0 + q0);
@@ -583,11 +593,8 @@ __global__ void __launch_bounds__(320, 2)
             float* rows = sRow + s * 2 * BQ2;
 #pragma unroll
             for (int i = 0; i < BQ2 / 32; ++i) {
-                const int r = lane + 32 * i;
-                const bool in = q0 + r < qe;
-                const size_t at = static_cast<size_t>(seg0 + (in ? q0 + r : 0)) * p.heads + head;
-                rows[r] = in ? __ldg(p.lse + at) : 0.f;
-                rows[BQ2 + r] = in ? __ldg(p.dsum + at) : 0.f;
+                rows[lane + 32 * i] = lv[i];
+                rows[BQ2 + lane + 32 * i] = dv[i];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(full + s);
@@ -723,15 +730,20 @@ __global__ void __launch_bounds__(320, 2)
                             a[e] = __uint_as_float(x[e]);
                             b[e] = __uint_as_float(y[e]);
                         }
-                        if (p.cosv) {
+                        if (p.cosv) {   // 16-byte aligned tables (checked at launch): four-wide loads
+                            const float4* c4 = reinterpret_cast<const float4*>(p.cosv + static_cast<size_t>(key) * (HD / 2) + pc * 16);
+                            const float4* s4 = reinterpret_cast<const float4*>(p.sinv + static_cast<size_t>(key) * (HD / 2) + pc * 16);
 #pragma unroll
-                            for (int e = 0; e < 16; ++e) {
-                                const int i = pc * 16 + e;
-                                const float c = p.cosv[static_cast<size_t>(key) * (HD / 2) + i];
-                                const float sn = p.sinv[static_cast<size_t>(key) * (HD / 2) + i];
-                                const float u = a[e], v = b[e];
-                                a[e] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
-                                b[e] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                            for (int t = 0; t < 4; ++t) {
+                                const float4 c = __ldg(c4 + t), sn = __ldg(s4 + t);
+                                const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+                                for (int u4 = 0; u4 < 4; ++u4) {
+                                    const int e = 4 * t + u4;
+                                    const float u = a[e], v = b[e];
+                                    a[e] = __fadd_rn(__fmul_rn(u, cc[u4]), __fmul_rn(v, ss[u4]));
+                                    b[e] = __fsub_rn(__fmul_rn(v, cc[u4]), __fmul_rn(u, ss[u4]));
+                                }
                             }
                         }
 #pragma unroll
@@ -1175,14 +1187,20 @@ __global__ void __launch_bounds__(192, 2)
                 float a[32], b[32];
 #pragma unroll
                 for (int e = 0; e < 32; ++e) { a[e] = __uint_as_float(x[e]); b[e] = __uint_as_float(y[e]); }
-                if (p.cosv) {   // pairs (i, i + 32) rotated back by −θ at the query's position
+                if (p.cosv) {   // pairs (i, i + 32) rotated back by −θ at the query's position (16-byte aligned tables)
+                    const float4* c4 = reinterpret_cast<const float4*>(p.cosv + static_cast<size_t>(q) * (HD / 2));
+                    const float4* s4 = reinterpret_cast<const float4*>(p.sinv + static_cast<size_t>(q) * (HD / 2));
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float c = p.cosv[static_cast<size_t>(q) * (HD / 2) + i];
-                        const float sn = p.sinv[static_cast<size_t>(q) * (HD / 2) + i];
-                        const float u = a[i], v = b[i];
-                        a[i] = __fadd_rn(__fmul_rn(u, c), __fmul_rn(v, sn));
-                        b[i] = __fsub_rn(__fmul_rn(v, c), __fmul_rn(u, sn));
+                    for (int t = 0; t < 8; ++t) {
+                        const float4 c = __ldg(c4 + t), sn = __ldg(s4 + t);
+                        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+                        for (int u4 = 0; u4 < 4; ++u4) {
+                            const int i = 4 * t + u4;
+                            const float u = a[i], v = b[i];
+                            a[i] = __fadd_rn(__fmul_rn(u, cc[u4]), __fmul_rn(v, ss[u4]));
+                            b[i] = __fsub_rn(__fmul_rn(v, cc[u4]), __fmul_rn(u, ss[u4]));
+                        }
                     }
                 }
                 __nv_bfloat16* out = p.dqkv + static_cast<size_t>(m.seg0 + q) * p.lddq + m.head * HD;
@@ -1329,7 +1347,8 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
 int flash_backward_dkdv_tc(const fa::Args& a, cudaStream_t s) {
     if (a.hidden / a.heads != fat::HD || !a.tq_item || a.max_tq <= 0 || a.T <= 0) return ERR_NOT_SUPPORTED;
     if ((a.ld & 7) || (a.ldo & 7) || (a.lddq & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15) ||
-        (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15))
+        (reinterpret_cast<uintptr_t>(a.dout) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.cosv) & 15) || (reinterpret_cast<uintptr_t>(a.sinv) & 15))
         return ERR_NOT_SUPPORTED;
     return a.dropout > 0.f ? launch_bwd_tc<true>(a, s) : launch_bwd_tc<false>(a, s);
 }
@@ -1375,7 +1394,8 @@ int flash_backward_dq_ds(const fa::Args& a, cudaStream_t s) {
         return ERR_NOT_SUPPORTED;
     if ((a.window >= 0 && a.window % fat::BQ2) || (a.ld & 7) || (a.lddq & 7) ||
         (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (reinterpret_cast<uintptr_t>(a.dqkv) & 15) ||
-        (reinterpret_cast<uintptr_t>(a.ds) & 15))
+        (reinterpret_cast<uintptr_t>(a.ds) & 15) || (reinterpret_cast<uintptr_t>(a.cosv) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.sinv) & 15))
         return ERR_NOT_SUPPORTED;
     CUtensorMap tk;
     if (int rc = make_tmap_2d(&tk, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, 3 * a.hidden,
