@@ -288,8 +288,11 @@ __global__ void __launch_bounds__(320, 1)
         if (lane == 0) {
             uint32_t base = 0, n = 0, pc[2] = {0, 0}, oc[2] = {0, 0};
             bool ok = true;
+            Span nx = span_of(p, blockIdx.x);
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n) {
-                const Span sp = span_of(p, item);
+                const Span sp = nx;
+                // the next item's geometry is read now, so its latency overlaps this item's MMAs
+                if (item + static_cast<int>(gridDim.x) < n_items) nx = span_of(p, item + gridDim.x);
                 if (!mbar_wait(q_full, n & 1, abort_flag, p.err)) break;
                 tc_fence_after();
                 int s_left = (sp.jhi[0] - sp.jlo[0]) + (sp.jhi[1] - sp.jlo[1]);

@@ -571,15 +571,16 @@ __global__ void __launch_bounds__(320, 2)
         for (int j = 0; j < nq; ++j) {
             const int s = j & 1;
             const int q0 = qb0 + j * BQ2;
-            // the tile's row statistics are read before the wait for its stage, so their latency overlaps it
+            // the tile's row statistics are read before the wait for its stage, so their latency overlaps it; they
+            // are staged as the softmax uses them: −lse·log2(e) and −scale·D
             float lv[BQ2 / 32], dv[BQ2 / 32];
 #pragma unroll
             for (int i = 0; i < BQ2 / 32; ++i) {
                 const int r = lane + 32 * i;
                 const bool in = q0 + r < qe;
                 const size_t at = static_cast<size_t>(seg0 + (in ? q0 + r : 0)) * p.heads + head;
-                lv[i] = in ? __ldg(p.lse + at) : 0.f;
-                dv[i] = in ? __ldg(p.dsum + at) : 0.f;
+                lv[i] = in ? -__ldg(p.lse + at) * LOG2E : 0.f;
+                dv[i] = in ? -p.scale * __ldg(p.dsum + at) : 0.f;
             }
             int got = 1;
             if (lane == 0) got = mbar_wait(empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err);
@@ -652,6 +653,11 @@ __global__ void __launch_bounds__(320, 2)
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         constexpr int HQ = BQ2 / 2;
         const float sl2 = p.scale * LOG2E;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), scale2 = f2_pack(p.scale, p.scale);
+        // the queries this key sees: [vlo, vhi] (within the tile's query range [qb0, qe) by construction)
+        const bool kin = key < L;
+        const int vlo = global ? 0 : key - W;
+        const int vhi = global ? L - 1 : min(L - 1, key + W);
         uint8_t* prow = sP + row * 128;
         uint8_t* drow = sDS + row * 128;
         bool ok = true;
@@ -678,15 +684,43 @@ __global__ void __launch_bounds__(320, 2)
                     if (lane == 0) mbar_arrive(st_free);
                 }
                 if (!ok) continue;
+                // P = 2^(S·scale·log2 e − lse·log2 e) (· dropout), dS = P ∘ (scale·dP·m − scale·D), two queries per
+                // .f32x2 instruction; a masked pair member gets the exponent −inf (P = 0).  The row statistics are
+                // the same for every thread (broadcast four-wide reads).
+                const int qp = q0 + pc * 16;
+                const bool whole = __all_sync(0xffffffffu, kin && qp >= vlo && qp + 15 <= vhi);
+                const float4* nl4 = reinterpret_cast<const float4*>(rows + half * HQ + pc * 16);
+                const float4* sd4 = reinterpret_cast<const float4*>(rows + BQ2 + half * HQ + pc * 16);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int qi = half * HQ + pc * 16 + e, q = q0 + pc * 16 + e;
-                    const float lse = rows[qi], dd = rows[BQ2 + qi];
-                    const bool vis = key < L && q < qe && (global || (key >= q - W && key <= q + W));
-                    const float pe = vis ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse * LOG2E)) : 0.f;
-                    const float m = DROP ? walk.next() : 1.0f;
-                    sv[e] = __float_as_uint(pe * m);
-                    dv[e] = __float_as_uint(p.scale * pe * (__uint_as_float(dv[e]) * m - dd));
+                for (int t = 0; t < 4; ++t) {
+                    const float4 nl = nl4[t], sd = sd4[t];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int e = 4 * t + 2 * u;
+                        float a0, a1;
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2x2,
+                                         u ? f2_pack(nl.z, nl.w) : f2_pack(nl.x, nl.y)),
+                                  a0, a1);
+                        if (!whole) {
+                            const int q = qp + e;
+                            if (!(kin && q >= vlo && q <= vhi)) a0 = -INFINITY;
+                            if (!(kin && q + 1 >= vlo && q + 1 <= vhi)) a1 = -INFINITY;
+                        }
+                        const float pe0 = ex2(a0), pe1 = ex2(a1);
+                        float d0 = __uint_as_float(dv[e]), d1 = __uint_as_float(dv[e + 1]);
+                        float p0 = pe0, p1 = pe1;
+                        if constexpr (DROP) {
+                            const float m0 = walk.next(), m1 = walk.next();
+                            p0 *= m0; p1 *= m1;
+                            d0 *= m0; d1 *= m1;
+                        }
+                        float g0, g1;
+                        f2_unpack(f2_mul(f2_pack(pe0, pe1),
+                                         f2_fma(scale2, f2_pack(d0, d1), u ? f2_pack(sd.z, sd.w) : f2_pack(sd.x, sd.y))),
+                                  g0, g1);
+                        sv[e] = __float_as_uint(p0); sv[e + 1] = __float_as_uint(p1);
+                        dv[e] = __float_as_uint(g0); dv[e + 1] = __float_as_uint(g1);
+                    }
                 }
                 // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
                 if (pc == 0 && j > 0) {
@@ -1121,8 +1155,11 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) {
             uint32_t g = 0;
             bool ok = true;
+            Item nx = item_of(blockIdx.x);
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                const Item m = item_of(it);
+                const Item m = nx;
+                // the next item's geometry is read now, so its latency overlaps this item's loads
+                if (it + static_cast<int>(gridDim.x) < n_items) nx = item_of(it + gridDim.x);
                 for (int kt = m.lo; kt < m.hi; ++kt, ++g) {
                     const int s = g & 1;
                     if (!mbar_wait(empty + s, ((g >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
@@ -1145,8 +1182,10 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) {
             uint32_t g = 0, ti = 0;
             bool ok = true;
+            Item nx = item_of(blockIdx.x);
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++ti) {
-                const Item m = item_of(it);
+                const Item m = nx;
+                if (it + static_cast<int>(gridDim.x) < n_items) nx = item_of(it + gridDim.x);
                 const int buf = ti & 1;
                 if (!mbar_wait(tempty + buf, ((ti >> 1) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();
