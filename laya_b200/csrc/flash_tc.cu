@@ -475,11 +475,17 @@ __global__ void __launch_bounds__(320, 1)
 // Same contract as fa::bwd_dkdv_kernel (flash.cu; Ops.AttentionBackward, Laya.Training/Ops.cs:368-470): for one
 // 128-key tile of one head, over every 64-query tile that sees it,
 //     Sᵀ = K·Qᵀ,  dPᵀ = V·dOᵀ  (M 128 keys, N 64 queries, K 64)            into TMEM columns [0, 64), [64, 128)
-//     Pᵀ = exp(scale·Sᵀ − lse) (· dropout),  dSᵀ = scale · P ∘ (dPᵀ·m − D)   by the softmax warps, bf16 into smem
+//     Pᵀ = exp(scale·Sᵀ − lse) (· dropout),  dSᵀ = P ∘ (scale·dPᵀ·m − scale·D)   by the softmax warps
 //     dV += Pᵀ·dO,  dK += dSᵀ·Q  (M 128 keys, N 64, K 64 queries; dO and Q read N-contiguous) into [128, 256)
-// then dK (rotated back by −θ at the key's position) and dV in bf16.  lse and D of the query tile are staged next to
-// its Q and dO tiles by the producer warp.  64-query tiles keep a CTA within 256 TMEM columns and ~98 KB of shared
-// memory, so two CTAs share an SM and one's MMA round trips overlap the other's softmax.
+// then dK (rotated back by −θ at the key's position) and dV in bf16.  Pᵀ goes back into the TMEM columns of dPᵀ it was
+// formed from (bf16 pairs, queries [0, 32) at [64, 80) and [32, 64) at [96, 112): each thread overwrites only columns
+// it has already read) and is the A operand of the dV MMA read from tensor memory; dSᵀ goes to shared memory (the A
+// operand of dK, and the tile the dQ kernel reads from the scratch).  With Pᵀ out of shared memory a CTA holds K, V,
+// three (Q, dO) stages and dSᵀ in ~99 KB, so two CTAs share an SM.  MMA order per tile j: Sᵀ(j) as soon as the
+// softmax has read Sᵀ(j − 1); then, once the softmax has finished tile j − 1, dV(j − 1), dK(j − 1) and dPᵀ(j) (dPᵀ(j)
+// overwrites Pᵀ(j − 1) after the dV MMA that reads it: MMAs of one thread run in order).  The softmax of tile j forms
+// P from Sᵀ(j) while dV/dK(j − 1) and dPᵀ(j) run.  lse and D of a query tile are staged next to its Q and dO tiles by
+// the producer warp, read from HBM before the producer waits for the stage.
 struct BwdParams {
     const int32_t* seg_start; const int32_t* seg_len;
     const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq;
@@ -494,8 +500,9 @@ struct BwdParams {
 };
 constexpr int BQ2 = 64;                          // queries per tile of the dK/dV kernel
 constexpr int QTILE2 = BQ2 * 128;                // bytes of one 64-row × 64-column bf16 tile
-constexpr int BWD_SMEM = 1024 + 2 * TILE + 4 * QTILE2 + 2 * TILE + 2 * 2 * BQ2 * 4 + 256;   // K, V, 2 × (Q, dO),
-                                                                                             // Pᵀ, dSᵀ; lse/D
+constexpr int BWD_ST = 3;                        // (Q, dO) stages
+constexpr int BWD_SMEM = 1024 + 2 * TILE + BWD_ST * 2 * QTILE2 + TILE + BWD_ST * 2 * BQ2 * 4 + 256;   // K, V, stages,
+                                                                                                   // dSᵀ; lse/D
 static_assert(2 * BWD_SMEM <= 232448, "two CTAs per SM");
 
 DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -505,6 +512,20 @@ DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr)
+        : "memory");
+}
+DEVI void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+// D[tmem] (+)= A[tmem] · B[smem] (kind::f16): A is M 128 rows in the TMEM lanes × K 16, two 16-bit values per column.
+DEVI void mma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -520,19 +541,19 @@ __global__ void __launch_bounds__(320, 2)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sK = smem;
     uint8_t* sV = smem + TILE;
-    uint8_t* sQO = smem + 2 * TILE;              // [2 stages][Q, dO], 64 rows each
-    uint8_t* sP = sQO + 4 * QTILE2;              // Pᵀ [128 keys × 64 queries]
-    uint8_t* sDS = sP + TILE;                    // dSᵀ
-    float* sRow = reinterpret_cast<float*>(sDS + TILE);   // [2 stages][lse 64 | D 64]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + 2 * 2 * BQ2);
+    uint8_t* sQO = smem + 2 * TILE;              // [BWD_ST stages][Q, dO], 64 rows each
+    uint8_t* sDS = sQO + BWD_ST * 2 * QTILE2;    // dSᵀ [128 keys × 64 queries]
+    float* sRow = reinterpret_cast<float*>(sDS + TILE);   // [BWD_ST stages][−lse·log2 e 64 | −scale·D 64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + BWD_ST * 2 * BQ2);
     uint64_t* kv_full = bars;
-    uint64_t* full = bars + 1;        // [2]
-    uint64_t* empty = bars + 3;       // [2]
-    uint64_t* st_full = bars + 5;
-    uint64_t* st_free = bars + 6;
-    uint64_t* pd_full = bars + 7;
-    uint64_t* pd_empty = bars + 8;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    uint64_t* full = bars + 1;                   // [BWD_ST]
+    uint64_t* empty = bars + 1 + BWD_ST;         // [BWD_ST]
+    uint64_t* s_full = bars + 1 + 2 * BWD_ST;    // Sᵀ(j) in TMEM
+    uint64_t* s_free = s_full + 1;               // Sᵀ(j) read by the softmax
+    uint64_t* dp_full = s_full + 2;              // dPᵀ(j) in TMEM
+    uint64_t* pd_full = s_full + 3;              // Pᵀ(j) in TMEM, dSᵀ(j) in smem
+    uint64_t* pd_empty = s_full + 4;             // dSᵀ(j) read by its dK MMA and its scratch copy
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 5);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int head = blockIdx.y, item = p.tq_item[tile], k0 = p.tq_p0[tile];
@@ -545,9 +566,10 @@ __global__ void __launch_bounds__(320, 2)
 
     if (threadIdx.x == 0) {
         mbar_init(kv_full, 1);
-        for (int s = 0; s < 2; ++s) { mbar_init(full + s, 2); mbar_init(empty + s, 1); }
-        mbar_init(st_full, 1);
-        mbar_init(st_free, 8);
+        for (int s = 0; s < BWD_ST; ++s) { mbar_init(full + s, 2); mbar_init(empty + s, 1); }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 8);
+        mbar_init(dp_full, 1);
         mbar_init(pd_full, 8);
         mbar_init(pd_empty, 1);
         *abort_flag = 0;
@@ -569,7 +591,7 @@ __global__ void __launch_bounds__(320, 2)
             tma_load_2d(sV, &tmk, kv_full, 2 * p.hidden + head * HD, seg0 + k0);
         }
         for (int j = 0; j < nq; ++j) {
-            const int s = j & 1;
+            const int s = j % BWD_ST;
             const int q0 = qb0 + j * BQ2;
             // the tile's row statistics are read before the wait for its stage, so their latency overlaps it; they
             // are staged as the softmax uses them: −lse·log2(e) and −scale·D
@@ -583,7 +605,7 @@ __global__ void __launch_bounds__(320, 2)
                 dv[i] = in ? -p.scale * __ldg(p.dsum + at) : 0.f;
             }
             int got = 1;
-            if (lane == 0) got = mbar_wait(empty + s, ((j >> 1) & 1) ^ 1, abort_flag, p.err);
+            if (lane == 0) got = mbar_wait(empty + s, ((j / BWD_ST) & 1) ^ 1, abort_flag, p.err);
             if (!__shfl_sync(0xffffffffu, got, 0)) break;
             __syncwarp();
             if (lane == 0) {
@@ -601,32 +623,35 @@ __global__ void __launch_bounds__(320, 2)
             if (lane == 0) mbar_arrive(full + s);
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: Sᵀ/dPᵀ of tile j are issued before dV/dK of tile j − 1
+        // ---- MMA issuer.  Iteration j: Sᵀ(j); the deferred release of dSᵀ(j − 2); dV/dK(j − 1); dPᵀ(j).
         if (lane == 0) {
             bool ok = mbar_wait(kv_full, 0, abort_flag, p.err);
             tc_fence_after();
-            const uint32_t ak = smem_u32(sK), av = smem_u32(sV);
+            const uint32_t ak = smem_u32(sK), av = smem_u32(sV), ad = smem_u32(sDS);
+            bool pend = false;   // a dSᵀ tile whose scratch copy and dK MMA must finish reading before pd_empty
             for (int j = 0; j <= nq && ok; ++j) {
+                const int s = j % BWD_ST;
+                const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
                 if (j < nq) {
-                    const int s = j & 1;
-                    if (!mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err)) break;
-                    if (j > 0 && !mbar_wait(st_free, (j - 1) & 1, abort_flag, p.err)) break;
+                    if (!mbar_wait(full + s, (j / BWD_ST) & 1, abort_flag, p.err)) { ok = false; break; }
+                    if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
+                    for (int kk = 0; kk < HD / 16; ++kk)
                         mma_f16(tS, smem_desc_sw128(ak + kk * 32), smem_desc_sw128(aq + kk * 32), IDESC_S, kk > 0);
-                        mma_f16(tDP, smem_desc_sw128(av + kk * 32), smem_desc_sw128(ado + kk * 32), IDESC_S, kk > 0);
-                    }
-                    mma_commit(st_full);
+                    mma_commit(s_full);
+                }
+                if (pend) {   // by now the copy has long read its tile: no wait in the common case
+                    if (p.ds) bulk_wait_read_all();
+                    mma_commit(pd_empty);
+                    pend = false;
                 }
                 if (j >= 1) {
-                    const int i = j - 1, s = i & 1;
-                    if (!mbar_wait(pd_full, i & 1, abort_flag, p.err)) break;
+                    const int i = j - 1, si = i % BWD_ST;
+                    if (!mbar_wait(pd_full, i & 1, abort_flag, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t aq = smem_u32(sQO + s * 2 * QTILE2), ado = aq + QTILE2;
-                    const uint32_t ap = smem_u32(sP), ad = smem_u32(sDS);
-                    if (p.ds) {   // dSᵀ of tile i to the scratch for dQ = dS·K, its read overlapping the MMAs' issue
+                    const uint32_t aqi = smem_u32(sQO + si * 2 * QTILE2), adoi = aqi + QTILE2;
+                    if (p.ds) {   // dSᵀ of tile i to the scratch for dQ = dS·K, its read overlapping the MMAs
                         const size_t idx = 1 + (static_cast<size_t>(tile) * p.ds_nq + i) * p.heads + head;
                         bulk_store(p.ds + idx * TILE, sDS, TILE);
                         bulk_commit();
@@ -634,13 +659,24 @@ __global__ void __launch_bounds__(320, 2)
 #pragma unroll
                     for (int kk = 0; kk < BQ2 / 16; ++kk) {
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                        mma_f16(tDV, smem_desc_sw128(ap + kk * 32), desc_mn_sw128(ado + kk * 2048, QTILE2), IDESC_G, acc);
-                        mma_f16(tDK, smem_desc_sw128(ad + kk * 32), desc_mn_sw128(aq + kk * 2048, QTILE2), IDESC_G, acc);
+                        // Pᵀ queries [16kk, 16kk + 16) sit at dPᵀ column 8kk, +16 for the second half-row
+                        mma_ts_f16(tDV, tDP + static_cast<uint32_t>(kk * 8 + (kk >= 2 ? 16 : 0)),
+                                   desc_mn_sw128(adoi + kk * 2048, QTILE2), IDESC_G, acc);
+                        mma_f16(tDK, smem_desc_sw128(ad + kk * 32), desc_mn_sw128(aqi + kk * 2048, QTILE2), IDESC_G, acc);
                     }
-                    mma_commit(empty + s);
-                    if (p.ds) bulk_wait_read_all();   // the tile's shared-memory read is done before it is rewritten
-                    mma_commit(pd_empty);
+                    mma_commit(empty + si);
+                    pend = true;
                 }
+                if (j < nq) {   // dPᵀ(j) over Pᵀ(j − 1): issued after the dV MMA that reads it
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        mma_f16(tDP, smem_desc_sw128(av + kk * 32), smem_desc_sw128(ado + kk * 32), IDESC_S, kk > 0);
+                    mma_commit(dp_full);
+                }
+            }
+            if (pend && ok) {
+                if (p.ds) bulk_wait_read_all();
+                mma_commit(pd_empty);
             }
             if (p.ds) bulk_wait_all();
         }
@@ -658,59 +694,87 @@ __global__ void __launch_bounds__(320, 2)
         const bool kin = key < L;
         const int vlo = global ? 0 : key - W;
         const int vhi = global ? L - 1 : min(L - 1, key + W);
-        uint8_t* prow = sP + row * 128;
         uint8_t* drow = sDS + row * 128;
+        const uint32_t tSh = tS + lane_off + half * HQ, tDPh = tDP + lane_off + half * HQ;
         bool ok = true;
         for (int j = 0; j < nq; ++j) {
-            const int s = j & 1;
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(st_full, j & 1, abort_flag, p.err) &&
-                                             mbar_wait(full + s, (j >> 1) & 1, abort_flag, p.err));
-            const float* rows = sRow + s * 2 * BQ2;
+            const int s = j % BWD_ST;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full, j & 1, abort_flag, p.err) &&
+                                             mbar_wait(full + s, (j / BWD_ST) & 1, abort_flag, p.err));
+            const float* rows = sRow + s * 2 * BQ2 + half * HQ;
             const int q0 = qb0 + j * BQ2 + half * HQ;
-            fat::DropWalk walk(p.seed, head, seg0 + q0, key, 1ull << 21, p.dropout, p.keep);
-            // the half-row's 32 queries in two 16-query pieces (fewer live registers)
+            // P = 2^(S·scale·log2 e − lse·log2 e) for the half-row's 32 queries, two per .f32x2 instruction; a masked
+            // pair member gets the exponent −inf (P = 0).  The row statistics are the same for every thread
+            // (broadcast four-wide reads).
+            uint32_t pv[32];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld16(tSh, *reinterpret_cast<uint32_t(*)[16]>(pv));
+                tmem_ld16(tSh + 16, *reinterpret_cast<uint32_t(*)[16]>(pv + 16));
+                tmem_ld_wait();
+            }
+            tc_fence_before();   // Sᵀ is in registers: release it to the next tile's MMA
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+            if (!ok) continue;
+            const bool whole = __all_sync(0xffffffffu, kin && q0 >= vlo && q0 + HQ - 1 <= vhi);
+            uint32_t kept = 0xffffffffu;   // dropout: which of the 32 probabilities are kept
+            {
+                fat::DropWalk walk(p.seed, head, seg0 + q0, key, 1ull << 21, p.dropout, p.keep);
+                const float4* nl4 = reinterpret_cast<const float4*>(rows);
 #pragma unroll
-            for (int pc = 0; pc < 2; ++pc) {
-                uint32_t sv[16], dv[16];
-                if (ok) {
-                    tc_fence_after();
-                    tmem_ld16(tS + lane_off + half * HQ + pc * 16, sv);
-                    tmem_ld16(tDP + lane_off + half * HQ + pc * 16, dv);
-                    tmem_ld_wait();
-                }
-                if (pc == 1) {   // Sᵀ and dPᵀ are in registers: release them to the next tile's MMAs
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(st_free);
-                }
-                if (!ok) continue;
-                // P = 2^(S·scale·log2 e − lse·log2 e) (· dropout), dS = P ∘ (scale·dP·m − scale·D), two queries per
-                // .f32x2 instruction; a masked pair member gets the exponent −inf (P = 0).  The row statistics are
-                // the same for every thread (broadcast four-wide reads).
-                const int qp = q0 + pc * 16;
-                const bool whole = __all_sync(0xffffffffu, kin && qp >= vlo && qp + 15 <= vhi);
-                const float4* nl4 = reinterpret_cast<const float4*>(rows + half * HQ + pc * 16);
-                const float4* sd4 = reinterpret_cast<const float4*>(rows + BQ2 + half * HQ + pc * 16);
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const float4 nl = nl4[t], sd = sd4[t];
+                for (int t = 0; t < HQ / 4; ++t) {
+                    const float4 nl = nl4[t];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
                         const int e = 4 * t + 2 * u;
                         float a0, a1;
-                        f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2x2,
+                        f2_unpack(f2_fma(f2_pack(__uint_as_float(pv[e]), __uint_as_float(pv[e + 1])), sl2x2,
                                          u ? f2_pack(nl.z, nl.w) : f2_pack(nl.x, nl.y)),
                                   a0, a1);
                         if (!whole) {
-                            const int q = qp + e;
+                            const int q = q0 + e;
                             if (!(kin && q >= vlo && q <= vhi)) a0 = -INFINITY;
                             if (!(kin && q + 1 >= vlo && q + 1 <= vhi)) a1 = -INFINITY;
                         }
-                        const float pe0 = ex2(a0), pe1 = ex2(a1);
+                        pv[e] = __float_as_uint(ex2(a0));
+                        pv[e + 1] = __float_as_uint(ex2(a1));
+                        if constexpr (DROP) {
+                            if (walk.next() == 0.f) kept &= ~(1u << e);
+                            if (walk.next() == 0.f) kept &= ~(1u << (e + 1));
+                        }
+                    }
+                }
+            }
+            // dSᵀ = P ∘ (scale·dPᵀ·m − scale·D) in 16-query pieces; Pᵀ·m back over the dPᵀ columns just read
+            ok = __all_sync(0xffffffffu, mbar_wait(dp_full, j & 1, abort_flag, p.err));
+            if (!ok) continue;
+            uint32_t dall[32];   // the half-row's dPᵀ in one TMEM round trip
+            tc_fence_after();
+            tmem_ld16(tDPh, *reinterpret_cast<uint32_t(*)[16]>(dall));
+            tmem_ld16(tDPh + 16, *reinterpret_cast<uint32_t(*)[16]>(dall + 16));
+            tmem_ld_wait();
+            // dSᵀ of the previous tile must have been read by its dK MMA and its scratch copy before it is rewritten
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
+                if (!ok) continue;
+            }
+#pragma unroll
+            for (int pc = 0; pc < 2; ++pc) {
+                uint32_t* dv = dall + pc * 16;
+                const float4* sd4 = reinterpret_cast<const float4*>(rows + BQ2 + pc * 16);
+                uint32_t pk[8];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float4 sd = sd4[t];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int e = 4 * t + 2 * u, ep = pc * 16 + e;
+                        const float pe0 = __uint_as_float(pv[ep]), pe1 = __uint_as_float(pv[ep + 1]);
                         float d0 = __uint_as_float(dv[e]), d1 = __uint_as_float(dv[e + 1]);
                         float p0 = pe0, p1 = pe1;
                         if constexpr (DROP) {
-                            const float m0 = walk.next(), m1 = walk.next();
+                            const float m0 = (kept >> ep) & 1u ? p.keep : 0.f, m1 = (kept >> (ep + 1)) & 1u ? p.keep : 0.f;
                             p0 *= m0; p1 *= m1;
                             d0 *= m0; d1 *= m1;
                         }
@@ -718,27 +782,21 @@ __global__ void __launch_bounds__(320, 2)
                         f2_unpack(f2_mul(f2_pack(pe0, pe1),
                                          f2_fma(scale2, f2_pack(d0, d1), u ? f2_pack(sd.z, sd.w) : f2_pack(sd.x, sd.y))),
                                   g0, g1);
-                        sv[e] = __float_as_uint(p0); sv[e + 1] = __float_as_uint(p1);
-                        dv[e] = __float_as_uint(g0); dv[e + 1] = __float_as_uint(g1);
+                        pk[e / 2] = pack2(p0, p1);
+                        dv[e] = __float_as_uint(g0);
+                        dv[e + 1] = __float_as_uint(g1);
                     }
                 }
-                // Pᵀ and dSᵀ of the previous tile must have been read by its dV/dK MMAs before they are rewritten
-                if (pc == 0 && j > 0) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (j - 1) & 1, abort_flag, p.err));
-                    if (!ok) continue;
-                }
+                tmem_st8(tDP + lane_off + static_cast<uint32_t>(half * HQ + pc * 8), pk);
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
-                    const float* f = reinterpret_cast<const float*>(sv + 8 * u);
                     const float* g = reinterpret_cast<const float*>(dv + 8 * u);
                     const int off = ((half * 4 + pc * 2 + u) ^ (row & 7)) << 4;
-                    *reinterpret_cast<uint4*>(prow + off) =
-                        make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
                     *reinterpret_cast<uint4*>(drow + off) =
                         make_uint4(pack2(g[0], g[1]), pack2(g[2], g[3]), pack2(g[4], g[5]), pack2(g[6], g[7]));
                 }
             }
-            if (!ok) continue;
+            tmem_st_wait();
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
