@@ -144,16 +144,18 @@ DEVI void drain_rows(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, c
 // rotation pairs: columns below rot_cols are rotated at the row's segment position in the reference's fp32 order
 // (Rotary.Apply, Ops.cs:490-503: x·c − y·s, y·c + x·s), then written as bf16 hi through tmOut and, with has_lo, the
 // bf16 remainder x − bf16(x) through tmOut2.
+// The row's position for the rotation (−1: the row is not rotated), found before the caller waits for the accumulator
+// and with the row's two 128-byte table lines (32 cosines, 32 sines) prefetched into L1, so these dependent loads
+// overlap the wait.
+DEVI int qkv_rot_pos(const KParams& p, int row, int gc0) {
+    if (!p.cosv || row >= p.M || gc0 >= p.rot_cols) return -1;
+    const int pos = row - p.seg_start[p.tok_item[row]];
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p.cosv + static_cast<size_t>(pos) * 32));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sinv + static_cast<size_t>(pos) * 32));
+    return pos;
+}
 DEVI void drain_qkv(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, const CUtensorMap* tmOut2, bool has_lo,
-                    const KParams& p, const float* bias, int gc0, int gr0, int lane, int cols) {
-    const int row = gr0 + lane;
-    const float* cr = nullptr;
-    const float* sr = nullptr;
-    if (p.cosv && row < p.M) {
-        const int pos = row - p.seg_start[p.tok_item[row]];
-        cr = p.cosv + static_cast<size_t>(pos) * 32;
-        sr = p.sinv + static_cast<size_t>(pos) * 32;
-    }
+                    const KParams& p, const float* bias, int gc0, int gr0, int lane, int cols, int pos) {
 #pragma unroll 1
     for (int c = 0; c < cols / 64; ++c) {
         uint32_t v0[32], v1[32];
@@ -171,12 +173,20 @@ DEVI void drain_qkv(uint32_t tbase, uint8_t* stage, const CUtensorMap* tmOut, co
 #pragma unroll
             for (int j = 0; j < 64; ++j) x[j] += col0 + j < p.N ? __ldg(bias + col0 + j) : 0.0f;
         }
-        if (cr && col0 < p.rot_cols) {
+        if (pos >= 0 && col0 < p.rot_cols) {   // 16-byte aligned tables (checked at launch): four-wide loads
+            const float4* c4 = reinterpret_cast<const float4*>(p.cosv + static_cast<size_t>(pos) * 32);
+            const float4* s4 = reinterpret_cast<const float4*>(p.sinv + static_cast<size_t>(pos) * 32);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float cc = __ldg(cr + j), ss = __ldg(sr + j), u = x[j], v = x[32 + j];
-                x[j] = __fsub_rn(__fmul_rn(u, cc), __fmul_rn(v, ss));
-                x[32 + j] = __fadd_rn(__fmul_rn(v, cc), __fmul_rn(u, ss));
+            for (int t = 0; t < 8; ++t) {
+                const float4 c = __ldg(c4 + t), sv = __ldg(s4 + t);
+                const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                for (int u4 = 0; u4 < 4; ++u4) {
+                    const int j = 4 * t + u4;
+                    const float u = x[j], v = x[32 + j];
+                    x[j] = __fsub_rn(__fmul_rn(u, cc[u4]), __fmul_rn(v, ss[u4]));
+                    x[32 + j] = __fadd_rn(__fmul_rn(v, cc[u4]), __fmul_rn(u, ss[u4]));
+                }
             }
         }
 #pragma unroll 1
@@ -569,12 +579,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, SPL>
             const int cols = w.wide ? BN / 2 : BN / 4;     // this warp's columns of the unit
             const int buf = ti & 1;
             const int m0 = w.m0 + static_cast<int>(rank) * BM;
+            int pos = -1;
+            if constexpr (EPI == EPI_QKV) pos = qkv_rot_pos(p, m0 + quarter * 32 + lane, w.n0 + half * cols);
             if (!mbar_wait(tfull + buf, (ti >> 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
             const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN + half * cols);
             if constexpr (EPI == EPI_QKV)
                 drain_qkv(tbase, stage, &tmOut, &tmOut2, pp.has_lo != 0, p, w.first ? p.bias : nullptr, w.n0 + half * cols,
-                          m0 + quarter * 32, lane, cols);
+                          m0 + quarter * 32, lane, cols, pos);
             else
                 drain_rows<EPI>(tbase, stage, &tmOut, w.first ? p.bias : nullptr, p.N, w.n0 + half * cols,
                                 m0 + quarter * 32, lane, cols);
@@ -761,7 +773,8 @@ int gemm(const Args& a, cudaStream_t stream) {
     }
     if (a.epi == EPI_QKV) {   // CTA pairs only, operands K-major, 64-column heads; the caller falls back otherwise
         if (a.N <= 128 || a.M <= BM || !pair_enabled() || a.a_mn || a.b_mn || (a.N % 64) || (a.rot_cols % 64) ||
-            (reinterpret_cast<uintptr_t>(a.out2) & 15) || (a.cosv && (!a.sinv || !a.tok_item || !a.seg_start)))
+            (reinterpret_cast<uintptr_t>(a.out2) & 15) || (a.cosv && (!a.sinv || !a.tok_item || !a.seg_start)) ||
+            (reinterpret_cast<uintptr_t>(a.cosv) & 15) || (reinterpret_cast<uintptr_t>(a.sinv) & 15))
             return ERR_NOT_SUPPORTED;
         if (a.A2 && a.B2) return launch_pair<3, 3, 0, 0, EPI_QKV>(a, stream);
         if (a.A2) return launch_pair<4, 2, 0, 0, EPI_QKV>(a, stream);
