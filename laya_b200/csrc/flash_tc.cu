@@ -497,6 +497,7 @@ struct BwdParams {
     __nv_bfloat16* dqkv; int lddq;
     int* err;
     uint8_t* ds; int ds_nq;   // the dS scratch (fa::Args) or null
+    int wave;                 // dK/dV: CTAs resident at once (two per SM)
 };
 constexpr int BQ2 = 64;                          // queries per tile of the dK/dV kernel
 constexpr int QTILE2 = BQ2 * 128;                // bytes of one 64-row × 64-column bf16 tile
@@ -535,8 +536,8 @@ __global__ void __launch_bounds__(320, 2)
                        const __grid_constant__ CUtensorMap tmdo, BwdParams p) {
     constexpr uint32_t IDESC_S = make_idesc(1, 1, 1, BK, BQ2);                    // M keys, N queries, K-major
     constexpr uint32_t IDESC_G = make_idesc(1, 1, 1, BK, HD) | (1u << 16);        // B (dO, Q) N-contiguous
-    const int tile = blockIdx.x;
-    if (tile >= *p.n_tq) return;
+    const int tile = blockIdx.x, n_tq = *p.n_tq;
+    if (tile >= n_tq) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sK = smem;
@@ -679,6 +680,16 @@ __global__ void __launch_bounds__(320, 2)
                 mma_commit(pd_empty);
             }
             if (p.ds) bulk_wait_all();
+        } else if (lane == 1 && p.wave > 0) {
+            // warm L2 with the K and V tiles of the CTA one resident wave ahead in launch order, whose first loads
+            // would otherwise come from DRAM after it starts
+            const long long lin = static_cast<long long>(blockIdx.y) * gridDim.x + blockIdx.x + p.wave;
+            const int t2 = static_cast<int>(lin % gridDim.x), h2 = static_cast<int>(lin / gridDim.x);
+            if (h2 < p.heads && t2 < n_tq) {
+                const int y2 = p.seg_start[p.tq_item[t2]] + p.tq_p0[t2];
+                tma_prefetch_2d(&tmk, p.hidden + h2 * HD, y2);
+                tma_prefetch_2d(&tmk, 2 * p.hidden + h2 * HD, y2);
+            }
         }
     } else {
         // ---- softmax warps: thread (half, row) owns key row `row` and queries [32·half, 32·half + 32) of a tile
@@ -1434,6 +1445,9 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
     p.ds = a.ds; p.ds_nq = a.ds_nq;
+    int nsm = 0;
+    if (int e = sm_count(dev, &nsm)) return e;
+    p.wave = 2 * nsm;
     fat::bwd_dkdv_tc_kernel<DROP><<<dim3(a.max_tq, a.heads), 320, fat::BWD_SMEM, s>>>(tk, tq, tdo, p);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
