@@ -56,6 +56,7 @@ struct Params {
     float* lse;
     int* err;
     __half* q8; float* q8d; int q8ldd;   // INFER 1: the context as Q8_0 codes [T, hidden] and scales [hidden/32, ldd]
+    const uint32_t* dmask; int dmask_w, dmask_rows;   // DROP 2: precomputed dropout decisions (fa::Args)
 };
 
 // MN-major operand, 128-byte swizzle (V as the N-contiguous B of P·V): 64-element atoms, 8-row K groups 1024 B apart.
@@ -181,7 +182,8 @@ DEVI Span span_of(const Params& p, int item) {
     return s;
 }
 
-template <bool SPLIT, bool DROP, int INFER = 0>
+// DROP: 0 no dropout, 1 the counter hash per probability, 2 the precomputed decisions (Params::dmask; global window).
+template <bool SPLIT, int DROP, int INFER = 0>
 __global__ void __launch_bounds__(320, 1)
     fwd_pp_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml, Params p) {
     static_assert(!INFER || (!SPLIT && !DROP), "the inference form is single-pass without dropout");
@@ -425,6 +427,13 @@ __global__ void __launch_bounds__(320, 1)
                 uint64_t rs2[2] = {0ull, 0ull};
                 const uint64_t c2x2 = f2_pack(c2, c2), nm2 = f2_pack(-msc, -msc);
                 DropWalk walk(p.seed, sp.head, sp.seg0 + q, k0, p.dropout, p.keep);
+                // precomputed decisions: the row's four words for the tile's 128 keys (k0 is a multiple of 128)
+                uint32_t dw[BK / 32] = {0u, 0u, 0u, 0u};
+                if (DROP == 2 && qin) {
+                    const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(
+                        p.dmask + (static_cast<size_t>(sp.head) * p.dmask_rows + sp.seg0 + q) * p.dmask_w + k0 / 32));
+                    dw[0] = w4.x; dw[1] = w4.y; dw[2] = w4.z; dw[3] = w4.w;
+                }
 #pragma unroll
                 for (int c = 0; c < BK / 32; ++c) {
                     uint32_t* f = v + 32 * c;   // the probabilities replace the scores
@@ -438,7 +447,13 @@ __global__ void __launch_bounds__(320, 1)
                         b = ex2(b);
                         const uint64_t pr = f2_pack(a, b);
                         rs2[e & 1] = f2_add(rs2[e & 1], pr);
-                        if constexpr (DROP) { a *= walk.next(); b *= walk.next(); }
+                        if constexpr (DROP == 2) {
+                            a = (dw[c] >> (2 * e)) & 1u ? a * p.keep : 0.f;
+                            b = (dw[c] >> (2 * e + 1)) & 1u ? b * p.keep : 0.f;
+                        } else if constexpr (DROP == 1) {
+                            a *= walk.next();
+                            b *= walk.next();
+                        }
                         ph[e] = INFER ? pack2h(a, b) : pack2(a, b);
                         if constexpr (SPLIT) {   // keep P for the lo remainder
                             f[2 * e] = __float_as_uint(a);
@@ -548,7 +563,7 @@ __global__ void __launch_bounds__(320, 1)
 
 }  // namespace fpp
 
-template <bool SPLIT, bool DROP>
+template <bool SPLIT, int DROP>
 static int launch_pp(const fa::Args& a, cudaStream_t s) {
     using C = fpp::Cfg<SPLIT>;
     CUtensorMap th, tl;
@@ -572,8 +587,40 @@ static int launch_pp(const fa::Args& a, cudaStream_t s) {
     p.window = a.window; p.hidden = a.hidden; p.heads = a.heads;
     p.scale = a.scale; p.dropout = a.dropout; p.keep = a.keep; p.seed = a.seed;
     p.out = a.out; p.out_lo = a.out_lo; p.ldo = a.ldo; p.lse = a.lse; p.err = a.err;
+    p.dmask = a.dmask; p.dmask_w = a.dmask_w; p.dmask_rows = a.dmask_rows;
     const int items = a.max_tp * a.heads;
     fpp::fwd_pp_kernel<SPLIT, DROP><<<items < nsm ? items : nsm, 320, C::SMEM, s>>>(th, tl, p);
+    count_launch();
+    LAYA_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// The dropout decisions of one layer (Ops.Dropout's counter hash, walked along keys as the forward walks them): one
+// warp per (head, row), each lane 32 keys of the row's segment at a time, one bit per key (1: kept).
+__global__ void __launch_bounds__(256) drop_mask_kernel(uint64_t seed, float dropout, float keep, int heads, int T,
+                                                        const int32_t* __restrict__ tok_item,
+                                                        const int32_t* __restrict__ seg_len, uint32_t* __restrict__ mask,
+                                                        int rows, int mw) {
+    const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= static_cast<long long>(heads) * T) return;
+    const int h = static_cast<int>(wid / T), t = static_cast<int>(wid % T);
+    const int nw = min((seg_len[tok_item[t]] + 31) / 32, mw);
+    for (int w = lane; w < nw; w += 32) {
+        fpp::DropWalk walk(seed, h, t, 32 * w, dropout, keep);
+        uint32_t bits = 0;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) bits |= (walk.next() != 0.f ? 1u : 0u) << i;
+        mask[(static_cast<size_t>(h) * rows + t) * mw + w] = bits;
+    }
+}
+
+int drop_mask(const fa::Args& a, const int32_t* tok_item, uint32_t* mask, cudaStream_t s) {
+    if (a.T <= 0 || a.dropout <= 0.f) return OK;
+    if (!mask || a.dmask_w <= 0 || (a.dmask_w & 3) || a.dmask_rows < a.T || !tok_item) return ERR_ARGUMENT;
+    const long long threads = static_cast<long long>(a.heads) * a.T * 32;
+    drop_mask_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
+        a.seed, a.dropout, a.keep, a.heads, a.T, tok_item, a.seg_len, mask, a.dmask_rows, a.dmask_w);
     count_launch();
     LAYA_CUDA(cudaGetLastError());
     return OK;
@@ -586,9 +633,9 @@ int flash_forward_pp(const fa::Args& a, cudaStream_t s) {
     if ((a.ld & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (a.qkv_lo && (reinterpret_cast<uintptr_t>(a.qkv_lo) & 15)))
         return ERR_NOT_SUPPORTED;
     if (a.qkv_lo && !a.out_lo) { set_error("accurate attention needs the context's low part"); return ERR_ARGUMENT; }
-    const bool drop = a.dropout > 0.f;
-    if (a.qkv_lo) return drop ? launch_pp<true, true>(a, s) : launch_pp<true, false>(a, s);
-    return drop ? launch_pp<false, true>(a, s) : launch_pp<false, false>(a, s);
+    const int drop = a.dropout <= 0.f ? 0 : (a.dmask && a.window < 0 ? 2 : 1);
+    if (a.qkv_lo) return drop == 2 ? launch_pp<true, 2>(a, s) : drop ? launch_pp<true, 1>(a, s) : launch_pp<true, 0>(a, s);
+    return drop == 2 ? launch_pp<false, 2>(a, s) : drop ? launch_pp<false, 1>(a, s) : launch_pp<false, 0>(a, s);
 }
 
 }  // namespace laya

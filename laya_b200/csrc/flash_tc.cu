@@ -498,12 +498,14 @@ struct BwdParams {
     int* err;
     uint8_t* ds; int ds_nq;   // the dS scratch (fa::Args) or null
     int wave;                 // dK/dV: CTAs resident at once (two per SM)
+    const uint32_t* dmask; int dmask_w, dmask_rows;   // precomputed dropout decisions (fa::Args), or null
 };
 constexpr int BQ2 = 64;                          // queries per tile of the dK/dV kernel
 constexpr int QTILE2 = BQ2 * 128;                // bytes of one 64-row × 64-column bf16 tile
 constexpr int BWD_ST = 3;                        // (Q, dO) stages
-constexpr int BWD_SMEM = 1024 + 2 * TILE + BWD_ST * 2 * QTILE2 + TILE + BWD_ST * 2 * BQ2 * 4 + 256;   // K, V, stages,
-                                                                                                   // dSᵀ; lse/D
+constexpr int BWD_MW = BK / 32;                  // dropout-decision words per query row of a key tile
+constexpr int BWD_SMEM = 1024 + 2 * TILE + BWD_ST * 2 * QTILE2 + TILE + BWD_ST * 2 * BQ2 * 4 +
+                         BWD_ST * BWD_MW * BQ2 * 4 + 256;   // K, V, stages, dSᵀ; lse/D; dropout words
 static_assert(2 * BWD_SMEM <= 232448, "two CTAs per SM");
 
 DEVI void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -545,7 +547,8 @@ __global__ void __launch_bounds__(320, 2)
     uint8_t* sQO = smem + 2 * TILE;              // [BWD_ST stages][Q, dO], 64 rows each
     uint8_t* sDS = sQO + BWD_ST * 2 * QTILE2;    // dSᵀ [128 keys × 64 queries]
     float* sRow = reinterpret_cast<float*>(sDS + TILE);   // [BWD_ST stages][−lse·log2 e 64 | −scale·D 64]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + BWD_ST * 2 * BQ2);
+    uint32_t* sMask = reinterpret_cast<uint32_t*>(sRow + BWD_ST * 2 * BQ2);   // [BWD_ST][word 4][query 64] (DROP)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sMask + BWD_ST * BWD_MW * BQ2);
     uint64_t* kv_full = bars;
     uint64_t* full = bars + 1;                   // [BWD_ST]
     uint64_t* empty = bars + 1 + BWD_ST;         // [BWD_ST]
@@ -605,6 +608,16 @@ __global__ void __launch_bounds__(320, 2)
                 lv[i] = in ? -__ldg(p.lse + at) * LOG2E : 0.f;
                 dv[i] = in ? -p.scale * __ldg(p.dsum + at) : 0.f;
             }
+            uint4 mw[BQ2 / 32];   // DROP with precomputed decisions: each of the lane's queries' 4 words of this key tile
+            if (DROP && p.dmask) {
+#pragma unroll
+                for (int i = 0; i < BQ2 / 32; ++i) {
+                    const int q = q0 + lane + 32 * i;
+                    mw[i] = q < qe ? __ldg(reinterpret_cast<const uint4*>(
+                                         p.dmask + (static_cast<size_t>(head) * p.dmask_rows + seg0 + q) * p.dmask_w + k0 / 32))
+                                   : make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
             int got = 1;
             if (lane == 0) got = mbar_wait(empty + s, ((j / BWD_ST) & 1) ^ 1, abort_flag, p.err);
             if (!__shfl_sync(0xffffffffu, got, 0)) break;
@@ -619,6 +632,17 @@ __global__ void __launch_bounds__(320, 2)
             for (int i = 0; i < BQ2 / 32; ++i) {
                 rows[lane + 32 * i] = lv[i];
                 rows[BQ2 + lane + 32 * i] = dv[i];
+            }
+            if (DROP && p.dmask) {
+                uint32_t* mrow = sMask + s * BWD_MW * BQ2;
+#pragma unroll
+                for (int i = 0; i < BQ2 / 32; ++i) {
+                    const int r = lane + 32 * i;
+                    mrow[0 * BQ2 + r] = mw[i].x;
+                    mrow[1 * BQ2 + r] = mw[i].y;
+                    mrow[2 * BQ2 + r] = mw[i].z;
+                    mrow[3 * BQ2 + r] = mw[i].w;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(full + s);
@@ -730,6 +754,16 @@ __global__ void __launch_bounds__(320, 2)
             if (!ok) continue;
             const bool whole = __all_sync(0xffffffffu, kin && q0 >= vlo && q0 + HQ - 1 <= vhi);
             uint32_t kept = 0xffffffffu;   // dropout: which of the 32 probabilities are kept
+            if (DROP && p.dmask) {   // this key's bit (lane) of the half-row's 32 queries' words (quarter)
+                const uint4* w4 = reinterpret_cast<const uint4*>(sMask + s * BWD_MW * BQ2 + quarter * BQ2 + half * HQ);
+                kept = 0u;
+#pragma unroll
+                for (int t = 0; t < HQ / 4; ++t) {
+                    const uint4 w = w4[t];
+                    kept |= (((w.x >> lane) & 1u) << (4 * t)) | (((w.y >> lane) & 1u) << (4 * t + 1)) |
+                            (((w.z >> lane) & 1u) << (4 * t + 2)) | (((w.w >> lane) & 1u) << (4 * t + 3));
+                }
+            }
             {
                 fat::DropWalk walk(p.seed, head, seg0 + q0, key, 1ull << 21, p.dropout, p.keep);
                 const float4* nl4 = reinterpret_cast<const float4*>(rows);
@@ -751,8 +785,10 @@ __global__ void __launch_bounds__(320, 2)
                         pv[e] = __float_as_uint(ex2(a0));
                         pv[e + 1] = __float_as_uint(ex2(a1));
                         if constexpr (DROP) {
-                            if (walk.next() == 0.f) kept &= ~(1u << e);
-                            if (walk.next() == 0.f) kept &= ~(1u << (e + 1));
+                            if (!p.dmask) {
+                                if (walk.next() == 0.f) kept &= ~(1u << e);
+                                if (walk.next() == 0.f) kept &= ~(1u << (e + 1));
+                            }
                         }
                     }
                 }
@@ -1445,6 +1481,7 @@ static int launch_bwd_tc(const fa::Args& a, cudaStream_t s) {
     p.lse = a.lse; p.dsum = a.dsum; p.cosv = a.cosv; p.sinv = a.sinv;
     p.dqkv = a.dqkv; p.lddq = a.lddq; p.err = a.err;
     p.ds = a.ds; p.ds_nq = a.ds_nq;
+    p.dmask = a.dmask; p.dmask_w = a.dmask_w; p.dmask_rows = a.dmask_rows;
     int nsm = 0;
     if (int e = sm_count(dev, &nsm)) return e;
     p.wave = 2 * nsm;

@@ -43,6 +43,7 @@ namespace {
 constexpr size_t NONE = static_cast<size_t>(-1);
 constexpr size_t BUCKET_ELEMS = 25u * 1000u * 1000u / 4u;   // 25 MB of fp32 gradients per allreduce
 constexpr int MAX_GROUPS = 16;                               // noise groups a batch can carry
+constexpr size_t DMASK_MAX = size_t(1) << 30;                  // the head layers' dropout decisions, at most
 constexpr size_t DS_SCRATCH_MAX = size_t(2) << 30;            // the attention backward's dS scratch, at most
 
 #define RC(x)                      \
@@ -208,6 +209,16 @@ struct laya_trainer {
     float *R32 = nullptr, *dH = nullptr, *dN = nullptr, *dbig32 = nullptr, *dsum = nullptr, *dsn = nullptr;
     uint8_t* ds = nullptr;   // the attention backward's dS scratch (null when it would exceed DS_SCRATCH_MAX)
     int ds_nq = 0;
+    // the head layers' attention dropout decisions, one bit per probability, drawn by each training forward for itself
+    // and its backward (null when they would exceed DMASK_MAX: the kernels then evaluate the hash per probability)
+    uint32_t* dmask = nullptr;
+    int dmask_w = 0, dmask_rows = 0;
+    size_t dmask_layer = 0;   // words per head layer
+    // the decisions are drawn on a second stream while the encoder layers run (whose kernels leave most issue slots
+    // idle); mask_begin orders them after the previous step's backward, mask_done before the head layers
+    cudaStream_t mask_stream = nullptr;
+    cudaEvent_t mask_begin = nullptr, mask_done = nullptr;
+    bool masks_pending = false;
     float* ln_part = nullptr;                                // LayerNorm backward: per-CTA dγ/dβ partials
     bf16 *d16 = nullptr, *dctx16 = nullptr, *dqkv16 = nullptr, *dbig16 = nullptr, *dpre16 = nullptr;
     float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;
@@ -560,6 +571,11 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
     const tr::Mask m0 = head_mask(t, l, 0);
     fa::Args att = attn_args(t, b, t->hqkv[l], pr ? t->ws_qkvlo : nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed,
                              t->hctx[l], ctxlo, t->hlse[l]);
+    if (t->masks_pending && m0.p > 0.f) {   // the layer's decisions, drawn at the start of the forward
+        LAYA_CUDA(cudaStreamWaitEvent(s, t->mask_done, 0));
+        att.dmask = t->dmask + static_cast<size_t>(l) * t->dmask_layer;
+        att.dmask_w = t->dmask_w; att.dmask_rows = t->dmask_rows;
+    }
     RC(timed(t, 1, 4.0 * H * b->pairs_global, [&] { return flash_forward(att, b->tiles, s); }));
     RC(lin_fwd(t, T, H, H, t->hctx[l], ctxlo, p.outw, t->master + p.outb, bf::EPI_F32, t->R32));
     RC(add_masked(t->HIN[l], t->R32, t->HX1[l], n, head_mask(t, l, 1), s));
@@ -580,6 +596,26 @@ int head_forward(laya_trainer* t, const laya_batch* b, int l) {
 int forward(laya_trainer* t, const laya_batch* b) {
     const int T = b->T, M = b->M, H = t->H;
     cudaStream_t s = t->stream;
+    t->masks_pending = false;
+    if (t->dmask && t->fwd_training && t->td.head_dropout > 0.f && t->HL > 0) {
+        if (!t->mask_stream) {
+            LAYA_CUDA(cudaStreamCreateWithFlags(&t->mask_stream, cudaStreamNonBlocking));
+            LAYA_CUDA(cudaEventCreateWithFlags(&t->mask_begin, cudaEventDisableTiming));
+            LAYA_CUDA(cudaEventCreateWithFlags(&t->mask_done, cudaEventDisableTiming));
+        }
+        LAYA_CUDA(cudaEventRecord(t->mask_begin, s));
+        LAYA_CUDA(cudaStreamWaitEvent(t->mask_stream, t->mask_begin, 0));
+        for (int l = 0; l < t->HL; ++l) {
+            const tr::Mask m0 = head_mask(t, l, 0);
+            fa::Args a = attn_args(t, b, t->hqkv[l], nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l],
+                                   nullptr, t->hlse[l]);
+            uint32_t* mk = t->dmask + static_cast<size_t>(l) * t->dmask_layer;
+            a.dmask = mk; a.dmask_w = t->dmask_w; a.dmask_rows = t->dmask_rows;
+            RC(drop_mask(a, b->tok_item, mk, t->mask_stream));
+        }
+        LAYA_CUDA(cudaEventRecord(t->mask_done, t->mask_stream));
+        t->masks_pending = true;
+    }
     tr::LnFwd e = ln_args(t, T, nullptr, t->emb_norm, NONE, t->eps, nullptr, nullptr, t->X[0], t->emb_mean, t->emb_rstd);
     e.ids = b->ids; e.table = t->master + t->tok_emb; e.vocab = t->V;
     RC(ln_fwd(e, s));
@@ -645,6 +681,10 @@ int head_backward(laya_trainer* t, const laya_batch* b, int l) {
     const tr::Mask m0 = head_mask(t, l, 0);
     fa::Args att = attn_args(t, b, t->hqkv[l], nullptr, t->HH, -1, nullptr, nullptr, m0.p, m0.seed, t->hctx[l],
                              nullptr, t->hlse[l]);
+    if (t->masks_pending && m0.p > 0.f) {   // the decisions the forward drew
+        att.dmask = t->dmask + static_cast<size_t>(l) * t->dmask_layer;
+        att.dmask_w = t->dmask_w; att.dmask_rows = t->dmask_rows;
+    }
     RC(timed(t, 2, 8.0 * H * b->pairs_global, [&] { return flash_backward(att, b->tiles, T, s); }));
     RC(lin_dw(t, T, 3 * H, H, t->dqkv16, t->hn1[l], p.inw));
     RC(colsum_bf16(t->dqkv16, T, 3 * H, G + p.inb, s));
@@ -901,6 +941,16 @@ int laya_trainer_create(const laya_model_desc* desc, const laya_train_desc* trai
             t->ds_nq = nq;
         }
     }
+    if (t->HL > 0) {   // the head layers' dropout decisions: [layer][head][row][4 words per 128 keys of the segment]
+        const int w = 4 * ((t->maxpos + 127) / 128);
+        const size_t words = static_cast<size_t>(t->HH) * static_cast<size_t>(d.max_tokens) * static_cast<size_t>(w);
+        if (words * t->HL * 4 <= DMASK_MAX) {
+            if ((rc = dalloc_t(t, &t->dmask, words * t->HL))) return fail(rc);
+            t->dmask_w = w;
+            t->dmask_rows = d.max_tokens;
+            t->dmask_layer = words;
+        }
+    }
     {   // the LayerNorm backward's per-CTA dγ/dβ partials
         int nsm = 0;
         if ((rc = sm_count(t->device, &nsm))) return fail(rc);
@@ -941,6 +991,9 @@ int laya_trainer_destroy(laya_trainer* t) {
     if (t->comm.ready) cudaEventDestroy(t->comm.ready);
     if (t->comm.done) cudaEventDestroy(t->comm.done);
     if (t->comm.stream) cudaStreamDestroy(t->comm.stream);
+    if (t->mask_stream) { cudaStreamSynchronize(t->mask_stream); cudaStreamDestroy(t->mask_stream); }
+    if (t->mask_begin) cudaEventDestroy(t->mask_begin);
+    if (t->mask_done) cudaEventDestroy(t->mask_done);
     for (void* p : t->allocs) cudaFree(p);
     for (auto& e : t->ev_pool) { cudaEventDestroy(e.first); cudaEventDestroy(e.second); }
     if (t->h_red) cudaFreeHost(t->h_red);

@@ -66,8 +66,16 @@ struct Args {
     // = dS·K streams them back; tile (g, j, head) at 1 + (g·ds_nq + j)·heads + head (16 KB each, tile 0 zeros); null:
     // dQ recomputes S and dP
     uint8_t* ds = nullptr; int ds_nq = 0;
+    // the dropout decisions of this layer's probabilities, precomputed by drop_mask (null: the kernels evaluate the
+    // counter hash per probability): word (head h, row t, w) at dmask[(h·dmask_rows + t)·dmask_w + w], bit i set when
+    // the probability of row t for key 32·w + i of its segment is kept; dmask_w is a multiple of 4 covering the
+    // longest segment rounded up to 128 keys
+    const uint32_t* dmask = nullptr; int dmask_w = 0; int dmask_rows = 0;
 };
 }  // namespace fa
+// Fills `mask` (a.dmask_w words per row, a.dmask_rows rows per head) for rows [0, a.T) with the decisions the counter
+// hash of Ops.Dropout makes for a.seed and a.dropout (flash_pp.cu).
+int drop_mask(const fa::Args& a, const int32_t* tok_item, uint32_t* mask, cudaStream_t s);
 // q, k rotated at their segment positions (cosv null: no rotation), v copied, from fp32 or bf16 [T, lds] into bf16
 // hi [T, ldd] (+ lo parts when lo is set); in place when src == hi (bf16).
 int attn_prep(const void* src, int src_f32, int lds, int T, int hidden, int heads, const int32_t* tok_item,

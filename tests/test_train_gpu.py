@@ -312,6 +312,42 @@ def test_large_geometry_matches_the_oracle(cuda):
     t.close()
 
 
+def test_head_dim_64_training_dropout_matches_the_oracle(cuda):
+    """Training-mode head dropout (p = 0.1) at head_dim 64, the geometry whose head layers run the tcgen05 attention:
+    the forward and the dK/dV kernel read decisions that a separate kernel draws with Ops.Uniform's counter hash, so
+    every kept or dropped probability must still be the oracle's; logits and every gradient against it, on two
+    steps in a row (the second one's decisions overwrite the first's)."""
+    import torch
+    import laya_b200
+    from laya_b200.workloads import training_batch, training_weights
+    from oracle.model import EncoderConfig
+    from oracle.train import TorchTrainModel, mix
+    cfg = EncoderConfig(hidden=1024, intermediate=2624, layers=2, heads=16, vocab=3000)
+    w = training_weights(hidden=1024, intermediate=2624, layers=2, vocab=3000, seed=5)
+    items, _ = training_batch(rows=3, min_len=150, max_len=400, vocab=3000, seed=8)
+    t = laya_b200.Trainer(desc_for(cfg, max_tokens=1280, max_items=4, max_markers=32),
+                          laya_b200.train_desc(max_segment=512))
+    t.load(w)
+    b = t.batch(items)
+    oi = [{"ids": it.token_ids, "markers": list(it.marker_positions), "qtype": it.question_type} for it in items]
+    coeff = [np.random.default_rng(12).standard_normal(it.options).astype(np.float32) for it in items]
+    for step in range(2):
+        seed = mix(42, 11 + step)
+        t.zero_grads()
+        logits = t.forward(b, training=True, seed=seed)
+        m = TorchTrainModel(cfg, w, head_dropout=0.1)
+        ref = m.forward(oi, training=True, seed=seed)
+        sum((r * torch.from_numpy(c)).sum() for r, c in zip(ref, coeff)).backward()
+        for l, r in zip(logits, ref):
+            assert max_rel(l, r.detach().numpy()) <= TOL
+        if step == 0:   # dropout is really on: the training logits differ from the evaluation ones
+            ev = m.forward(oi, training=False)
+            assert max(max_rel(r.detach().numpy(), e.detach().numpy()) for r, e in zip(ref, ev)) > 1e-3
+        t.backward(b, coeff)
+        check_grads(t, m.grads(), skip=[k for k in m.p if k.startswith("act_head.")], elementwise=False)
+    t.close()
+
+
 def test_errors_are_reported_like_the_reference(tiny_trainer):
     """Token ids outside the vocabulary and markers past their segment: ArgumentOutOfRangeException's code; a batch
     larger than the trainer, or an objective before any forward: ArgumentException's."""
