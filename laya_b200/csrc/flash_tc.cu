@@ -485,7 +485,8 @@ __global__ void __launch_bounds__(320, 1)
 // softmax has read Sᵀ(j − 1); then, once the softmax has finished tile j − 1, dV(j − 1), dK(j − 1) and dPᵀ(j) (dPᵀ(j)
 // overwrites Pᵀ(j − 1) after the dV MMA that reads it: MMAs of one thread run in order).  The softmax of tile j forms
 // P from Sᵀ(j) while dV/dK(j − 1) and dPᵀ(j) run.  lse and D of a query tile are staged next to its Q and dO tiles by
-// the producer warp, read from HBM before the producer waits for the stage.
+// the producer warp, read from HBM before the producer waits for the stage; with precomputed dropout decisions
+// (BwdParams::dmask) so are the tile's four words per query, from which each softmax thread takes its key's bits.
 struct BwdParams {
     const int32_t* seg_start; const int32_t* seg_len;
     const int32_t* tq_item; const int32_t* tq_p0; const int32_t* n_tq;
